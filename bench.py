@@ -1,0 +1,541 @@
+"""Benchmark of the SunnyNet token loop on B200s (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+Workloads (synthetic seeded inputs, random-init weights):
+  c1   gated scan, B=1 T=4096 C=1024 (one step = one full scan)
+  c2   SunnyNet small decode (L4 d512 i896 r320 V16384, fp32), B=256 per GPU
+  c2b1 the same model at B=1
+  c3   SunnyNet 100M-class (L12 d768 i1344 r480 V32000), INT8 per-row weights,
+       B=1024 split over the GPUs
+  c4   RWKV-7 191M shape, INT4 group-128 fp16 scales, B=64 per GPU (c4b1, c4b512)
+  c5   chunked prefill, SunnyNet 0.5B shape (L24 d1536 i2688 r960 V32000) fp32,
+       T=32768 in chunks of 256, 8 sequences per GPU
+
+A step is one pass of the hot path over one batch: one decode token for every
+sequence of the batch (or one full scan for c1, one 256-token chunk for c5).
+Sequences are independent and shard by batch over the ranks (no collective on
+the data path); timing is the max over ranks of CUDA-event time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+# ------------------------------------------------------------------ helpers
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "src": "fallback"}
+
+
+def profile_traffic(kernel_key: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    for f in sorted((REPO / "profiles").glob("*.md")):
+        for line in f.read_text().splitlines():
+            m = re.match(r"traffic_bytes_per_launch\[(.+?)\]:\s*([0-9.eE+]+)", line.strip())
+            if m and m.group(1) == kernel_key:
+                return float(m.group(2))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while running."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, torch):
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self, torch):
+        torch.cuda.synchronize()
+        if self.pg:
+            self.pg.barrier()
+        torch.cuda.synchronize()
+
+    def max(self, torch, v: float) -> float:
+        if not self.pg:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def timed_steps(torch, dist, step, K: int, W: int, flush=None):
+    """W warm-up steps, then K timed steps bracketed by barrier+sync; each step
+    is bracketed by CUDA events on the current stream, with an untimed L2
+    flush before it when `flush` is given. Returns (ms per step, max over ranks)."""
+    for _ in range(W):
+        if flush is not None:
+            flush()
+        step()
+    dist.barrier(torch)
+    st = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(K)]
+    for s, e in evs:
+        if flush is not None:
+            flush()
+        s.record(st)
+        step()
+        e.record(st)
+    dist.barrier(torch)
+    ms = sum(s.elapsed_time(e) for s, e in evs) / K
+    return dist.max(torch, ms)
+
+
+# ---------------------------------------------------------------- workloads
+def wl_c1(args, torch, dist, ours: bool):
+    """Gated scan, BASELINE config 1. One step = one scan of B*T*C elements."""
+    B, T, N = 1, 4096, 1024
+    rng = np.random.default_rng(0)
+    H = np.exp(np.linspace(np.log(2.0), np.log(8192.0), N))
+    a = rng.uniform(1.0 - 1.0 / H, 1.0, (B, T, N)).astype(np.float32)
+    u = rng.standard_normal((B, T, N)).astype(np.float32)
+    s0 = np.zeros((B, N), np.float32)
+    alg_bytes = 3 * B * T * N * 4  # read a, u; write out (+ B*N*8 for s0/send, negligible)
+    res = {"metric": "gated scan throughput (algorithmic bytes)", "unit": "GB/s",
+           "higher_is_better": True, "dtype": "f32",
+           "config": {"workload": "c1 gated scan B=1 T=4096 C=1024", "l2": "flushed between steps",
+                      "inputs": "a~U[1-1/H,1], H log-spaced [2,8192]; u~N(0,1); s0=0; seed 0"}}
+    if not ours:
+        return res, ref_scan(a, u, s0, alg_bytes)
+    from sunnynet_b200 import runtime
+    lib = runtime.load_runtime()
+    from sunnynet_b200._lib import check, ptr
+    da, du, ds = (torch.from_numpy(x).cuda() for x in (a, u, s0))
+    out = torch.empty_like(da)
+    send = torch.empty_like(ds)
+    check(lib.sn_abi_cuda_set_stream(torch.cuda.current_stream().cuda_stream))
+    check(lib.sn_abi_cuda_set_async(1))
+    flushbuf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    def step():
+        check(lib.sn_abi_recur_scan(ptr(da), ptr(du), ptr(ds), ptr(out), ptr(send), B, T, N, 1))
+
+    with ClockSampler(dist.local) as clk:
+        ms = timed_steps(torch, dist, step, args.steps, args.warmup, flush=flushbuf.zero_)
+        # keep the clock sampler busy on a longer loop of the same step
+        t_end = time.time() + 1.5
+        while time.time() < t_end:
+            for _ in range(200):
+                step()
+            torch.cuda.synchronize()
+    check(lib.sn_abi_cuda_set_async(0))
+    # end-to-end: the public call with pinned host buffers (H2D + kernel + D2H)
+    pa = torch.from_numpy(a).pin_memory()
+    pu = torch.from_numpy(u).pin_memory()
+    ps = torch.from_numpy(s0).pin_memory()
+    po = torch.empty_like(pa).pin_memory()
+    pe = torch.empty_like(ps).pin_memory()
+    for _ in range(3):
+        check(lib.sn_abi_recur_scan(ptr(pa), ptr(pu), ptr(ps), ptr(po), ptr(pe), B, T, N, 1))
+    reps = 20
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        check(lib.sn_abi_recur_scan(ptr(pa), ptr(pu), ptr(ps), ptr(po), ptr(pe), B, T, N, 1))
+    e2e_s = (time.perf_counter() - t0) / reps
+    e2e_s = dist.max(torch, e2e_s)
+    peaks = measured_peaks()
+    achieved = alg_bytes / (ms * 1e-3) / 1e9
+    res.update({
+        "ms_per_step": ms,
+        "value": achieved * dist.world,
+        "e2e": {"value": alg_bytes * dist.world / e2e_s / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": int(2 * B * T * N * 4 + B * N * 4),
+                "d2h_bytes_per_step": int(B * T * N * 4 + B * N * 4)},
+        "gpu_launches": args.steps,  # one scan kernel per step
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                     "peak_src": peaks["src"], "kernel": "scan_exact_kernel",
+                     "alg_bytes_per_launch": alg_bytes,
+                     "traffic": profile_traffic("scan_exact_kernel/c1")},
+        "clocks": clk.summary(),
+    })
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = ref_scan(a, u, s0, alg_bytes)
+    return res, None
+
+
+def ref_scan(a, u, s0, alg_bytes, budget_s=3.0):
+    """The reference AVX2 sn_recur_scan (oracle/_ref) on the host cores."""
+    import oracle
+    B, T, N = a.shape
+    out = np.empty_like(a)
+    se = np.empty((B, N), np.float32)
+    P = oracle.ptr
+    if oracle.ref_available():
+        L, kind = oracle.ref_abi(), "reference"
+        fn = lambda: L.sn_recur_scan(P(a), P(u), P(s0), P(out), P(se), B, T, N, 1)
+    else:
+        L, kind = oracle.lib(), "port"
+        fn = lambda: L.or_recur_scan(P(a), P(u), P(s0), P(out), P(se), B, T, N, 1)
+    fn()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        fn()
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": alg_bytes / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": kind,
+            "sample": f"{n} full C1 scans (B=1 T=4096 C=1024); the reference parallelises "
+                      f"over B only (recur.c:16), so B=1 runs on one thread"}
+
+
+def sunny_step_cost(S, B, wbytes, with_head=True):
+    """Algorithmic bytes and FLOPs of one decode step for B sequences (weights
+    read once, state s + 3-row history ring read, s + newest history row
+    written, embedding rows read, logits written)."""
+    D, I, R, V, L = S.dim, S.inner, S.rank, S.vocab, S.layers
+    mats = D * R + R * 2 * D + D * I + I * D + D * D
+    wts = L * mats * wbytes + (V * D * wbytes if with_head else 0)
+    if wbytes == 1:  # per-row fp32 scales
+        wts += 4 * (L * (R + 2 * D + I + D + D) + (V if with_head else 0))
+    state = B * L * (4 * D + 2 * D) * 4
+    io = B * D * 4 + (B * V * 4 if with_head else 0)
+    flops = 2 * B * (L * mats + (V * D if with_head else 0))
+    return wts + state + io, flops
+
+
+def family_cost(S, B, fam, wbytes):
+    """(bytes, flops) per launch of one kernel family of the SunnyNet step."""
+    D, I, R, V = S.dim, S.inner, S.rank, S.vocab
+    shapes = {"gemm_head": (V, D), "gemm_Wz": (I, D), "gemm_Wc": (D, I), "gemm_Ws": (D, D),
+              "gemm_V": (R, D), "gemm_U": (2 * D, R)}
+    if fam in shapes:
+        n, k = shapes[fam]
+        return n * k * wbytes + B * k * 4 + B * n * 4, 2 * B * n * k
+    return None, None
+
+
+def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
+    from sunnynet_b200 import formats
+    S = formats.SUNNY_PRESETS[preset]
+    B = B_total // dist.world if split else B_total
+    wbytes = 1 if quant else 4
+    step_bytes, step_flops = sunny_step_cost(S, B, wbytes)
+    res = {"metric": "decode tokens/s", "unit": "tokens/s", "higher_is_better": True,
+           "dtype": "i8w-f32" if quant else "f32",
+           "config": {"workload": f"{preset} SunnyNet decode L{S.layers} d{S.dim} i{S.inner} "
+                                  f"r{S.rank} V{S.vocab} {'INT8 per-row' if quant else 'fp32'}",
+                      "batch_per_gpu": B, "global_batch": B * dist.world,
+                      "prefill_tokens": prefill_T, "decode": "greedy, teacher-free",
+                      "l2": "flushed between steps" if step_bytes < 2 * (126 << 20) else
+                            "working set > L2"}}
+    td = tempfile.mkdtemp(prefix="snbench_")
+    path = Path(td) / ("m.usnq" if quant else "m.usnn")
+    w = formats.random_sunny(S, seed=0)
+    (formats.write_usnq if quant else formats.write_usnn)(path, w)
+    if not ours:
+        ref_path = Path(td) / "ref.usnn"
+        if quant:  # the reference has no INT8 SunnyNet: W8A32 = dequantised weights, fp32 blob
+            w = dequantised_weights(w)
+        formats.write_usnn(ref_path, w)
+        return res, ref_sunny(ref_path, S, B_total)
+    from sunnynet_b200 import _lib
+    from sunnynet_b200._lib import check
+    from sunnynet_b200.model import SunnyBatch
+    lib = _lib.load()
+    check(lib.sn_abi_cuda_set_stream(torch.cuda.current_stream().cuda_stream))
+    m = SunnyBatch(path, B)
+    g = torch.Generator(device="cuda").manual_seed(dist.rank)
+    logits = torch.empty(B, S.vocab, device="cuda")
+    check(lib.sn_abi_cuda_set_async(1))
+    prompt = torch.randint(0, S.vocab, (B, prefill_T), generator=g, device="cuda",
+                           dtype=torch.int32)
+    for t in range(prefill_T):
+        m.step(prompt[:, t].contiguous(), logits=logits)
+    cur = torch.argmax(logits, dim=1).to(torch.int32).contiguous()
+
+    def step():
+        m.step_argmax(cur, out=cur)
+
+    flushbuf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    flush = flushbuf.zero_ if step_bytes < 2 * (126 << 20) else None
+    with ClockSampler(dist.local) as clk:
+        ms = timed_steps(torch, dist, step, args.steps, args.warmup, flush=flush)
+        t_end = time.time() + 1.5
+        while time.time() < t_end:
+            for _ in range(20):
+                step()
+            torch.cuda.synchronize()
+    # live per-kernel timing (CUDA events around each kernel family, same step)
+    check(lib.sn_abi_cuda_profile(1))
+    for _ in range(3):
+        if flush:
+            flush()
+        step()
+    torch.cuda.synchronize()
+    check(lib.sn_abi_cuda_profile(0))
+    fams = _lib.profile_report()
+    check(lib.sn_abi_cuda_set_async(0))
+    dom = max(fams, key=lambda k: fams[k][1])
+    n_l, t_ms = fams[dom]
+    fb, ff = family_cost(S, B, dom, wbytes)
+    peaks = measured_peaks()
+    per_launch_s = t_ms / n_l * 1e-3
+    if B >= 64 and ff:
+        rl = {"bound": "tensor", "achieved": ff / per_launch_s / 1e12,
+              "peak": peaks["bf16_tflops"], "unit": "TFLOP/s"}
+    else:
+        rl = {"bound": "hbm", "achieved": (fb or 0) / per_launch_s / 1e9,
+              "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+    rl.update({"frac": rl["achieved"] / rl["peak"], "peak_src": peaks["src"], "kernel": dom,
+               "launches": n_l, "avg_launch_us": per_launch_s * 1e6,
+               "alg_bytes_per_launch": fb, "alg_flops_per_launch": ff,
+               "traffic": profile_traffic(f"{dom}/{preset}/B{B}"),
+               "step_alg_bytes": step_bytes, "step_alg_flops": step_flops,
+               "step_hbm_gbs": step_bytes / (ms * 1e-3) / 1e9,
+               "step_tflops": step_flops / (ms * 1e-3) / 1e12,
+               "families_ms_per_step": {k: v[1] / 3 for k, v in fams.items()}})
+    # end to end: the public call with pinned host tokens in, host logits out
+    ht = torch.randint(0, S.vocab, (B,), dtype=torch.int32).pin_memory()
+    hl = torch.empty(B, S.vocab).pin_memory()
+    for _ in range(3):
+        m.step(ht, logits=hl)
+    reps = max(5, min(50, int(2000 / max(ms, 0.05))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        m.step(ht, logits=hl)
+    e2e_s = dist.max(torch, (time.perf_counter() - t0) / reps)
+    launches = 8 * S.layers + 3  # per layer: prep, 5 GEMMs, gate, row stats; + stats, head, argmax
+    res.update({
+        "ms_per_step": ms,
+        "value": B * dist.world / (ms * 1e-3),
+        "e2e": {"value": B * dist.world / e2e_s, "unit": "tokens/s",
+                "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * S.vocab * 4,
+                "call": "sn_abi_sunny_step (host tokens, host logits)"},
+        "gpu_launches": launches * args.steps,
+        "roofline": rl,
+        "clocks": clk.summary(),
+    })
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        ref_path = Path(td) / "ref.usnn"
+        formats.write_usnn(ref_path, dequantised_weights(w) if quant else w)
+        res["cpu_baseline"] = ref_sunny(ref_path, S, B)
+    m.close()
+    return res, None
+
+
+def dequantised_weights(w):
+    """USNQ semantics as fp32 weights: per-row INT8 codes times the row scale."""
+    import copy
+    from sunnynet_b200 import formats
+    d = copy.deepcopy(w)
+
+    def dq(a):
+        q, sc = formats.quant_i8_rows(a)
+        return (q.astype(np.float32) * sc[:, None]).astype(np.float32)
+
+    for ly in d.layers:
+        for k in ("V", "U", "Wz", "Wc", "Ws_eff"):
+            ly[k] = dq(ly[k])
+    d.head = dq(d.embed)  # the USNQ head is INT8; the embedding lookup stays fp32
+    return d
+
+
+def ref_sunny(path, S, B, budget_s=10.0):
+    """Reference C runtime (oracle/_ref sn_step, B=1 per handle). B=1: one handle
+    with the reference's recommended (physical-core) thread count. B>1: one
+    single-threaded handle per physical core stepping concurrently (the C runtime
+    has no batched step); throughput = tokens of all handles / wall time."""
+    import ctypes
+    import threading
+    import oracle
+    if oracle.ref_available():
+        L, kind = oracle.ref_model(), "reference"
+        load = lambda: L.sn_load(str(path).encode(), S.vocab, S.dim, S.inner, S.rank, S.taps,
+                                 S.layers, S.group, 1)
+        stepf = lambda h, t, buf: L.sn_step(h, int(t), buf)
+        cores = max(1, int(L.sn_recommended_threads()))
+    else:
+        raise RuntimeError("oracle/_ref is not built; the CPU baseline needs the reference runtime")
+    rng = np.random.default_rng(0)
+    if B == 1:
+        L.sn_set_threads(cores)
+        h = load()
+        buf = np.empty(S.vocab, np.float32)
+        for t in rng.integers(0, S.vocab, 16):
+            stepf(h, t, oracle.ptr(buf))
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s:
+            stepf(h, int(buf.argmax()), oracle.ptr(buf))
+            n += 1
+        dt = time.perf_counter() - t0
+        L.sn_free(h)
+        return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": kind,
+                "sample": f"{n} greedy B=1 sn_step calls after a 16-token prefill, "
+                          f"{cores} OpenMP threads"}
+    K = min(cores, B, 32)
+    L.sn_set_threads(1)
+    handles = [load() for _ in range(K)]
+    counts = [0] * K
+    stop = time.perf_counter() + budget_s
+
+    def run(i):
+        buf = np.empty(S.vocab, np.float32)
+        p = oracle.ptr(buf)
+        r = np.random.default_rng(i)
+        for t in r.integers(0, S.vocab, 4):
+            stepf(handles[i], t, p)
+        while time.perf_counter() < stop:
+            stepf(handles[i], int(buf.argmax()), p)
+            counts[i] += 1
+
+    t0 = time.perf_counter()
+    ths = [threading.Thread(target=run, args=(i,)) for i in range(K)]
+    for th in ths:
+        th.start()
+    for th in ths:
+        th.join()
+    dt = time.perf_counter() - t0
+    for h in handles:
+        L.sn_free(h)
+    return {"value": sum(counts) / dt, "unit": "tokens/s", "cores": K, "kind": kind,
+            "sample": f"{sum(counts)} sn_step calls: {K} concurrent single-thread handles "
+                      f"(the reference C runtime decodes B=1 per handle), ~{budget_s:.0f} s"}
+
+
+def wl_c2(args, torch, dist, ours):
+    return wl_sunny(args, torch, dist, ours, "c2", 256, False, 256, split=False)
+
+
+def wl_c2b1(args, torch, dist, ours):
+    return wl_sunny(args, torch, dist, ours, "c2", 1, False, 256, split=False)
+
+
+def wl_c3(args, torch, dist, ours):
+    res, base = wl_sunny(args, torch, dist, ours, "c3", 1024, True, 64, split=True)
+    return res, base
+
+
+WORKLOADS = {"c1": wl_c1, "c2": wl_c2, "c2b1": wl_c2b1, "c3": wl_c3}
+SCALING = {"c3": "strong"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+    dist = Dist()
+    if args.impl == "reference":
+        if dist.rank != 0:
+            return 0
+        res, base = WORKLOADS[args.config](args, torch, dist, ours=False)
+        res.update({"impl": "reference", "value": base["value"], "n_gpus": args.gpus,
+                    "steps": args.steps, "warmup": args.warmup,
+                    "scaling": SCALING.get(args.config, "weak"),
+                    "vs_baseline": None, "data": "synthetic", "cpu_baseline": base,
+                    "e2e": {"value": base["value"], "unit": base["unit"],
+                            "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+        print(json.dumps(res))
+        return 0
+    dist.init(torch)
+    try:
+        res, _ = WORKLOADS[args.config](args, torch, dist, ours=True)
+        res.update({"n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+                    "scaling": SCALING.get(args.config, "weak"), "vs_baseline": None,
+                    "data": "synthetic (seeded random-init weights and token ids)"})
+        if dist.rank == 0:
+            print(json.dumps(res))
+    finally:
+        dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

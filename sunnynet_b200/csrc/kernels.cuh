@@ -1,0 +1,24 @@
+// Device-pointer launchers shared between translation units. All take device
+// pointers, enqueue on `st` and return an sn_status.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace sn {
+
+// W4A8 output epilogues
+enum W4Epi : int { kW4Store = 0, kW4Add = 1, kW4Relu2 = 2, kW4Tanh = 3, kW4Sigmoid = 4 };
+
+int launch_scan(const float* a, const float* b, const float* s0, float* out, float* send, int B,
+                int T, int N, int gated, cudaStream_t st);
+int launch_step(const float* a, const float* b, float* s, int B, int N, int gated,
+                cudaStream_t st);
+// Y (nseq,out) = W4A8(X (nseq,in)) with codes (out,in/2) and scales (out,in/block)
+int launch_w4a8(float* Y, const float* X, const uint8_t* Wq, const void* scale, int nseq, int in,
+                int out, int block, bool fp16, cudaStream_t st, int epi);
+int launch_gemv_f32(float* y, const float* x, const float* W, int in, int out, cudaStream_t st);
+int launch_quant_i4(const float* x, uint8_t* q, void* scale, int rows, int N, int block,
+                    bool fp16, cudaStream_t st);
+
+}  // namespace sn

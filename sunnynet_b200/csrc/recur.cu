@@ -1,0 +1,463 @@
+// Generic first-order recurrence and INT8 quantisation on sm_100a.
+//
+// Reference: sunnynet/runtime/recur.c (sn_recur_scan 13-48, sn_recur_step
+// 109-131, sn_quant_i8 134-161, sn_dequant_i8 163-178).
+//
+// Bit-exactness. The reference vectorises 8 channels with an FMA,
+// s = fma(a, s, b) with b = (1-a)*u rounded separately, and runs the N%8
+// remainder channels through scalar ISO-C code without contraction
+// (s = a*s + b, two roundings). The kernels below apply the same per-channel
+// rule with explicit __fmaf_rn / __fmul_rn / __fadd_rn, so every output is
+// bit-identical to the reference.
+//
+// Scan layout. One CTA owns CW adjacent channels of one sequence and walks T
+// in chunks of TC rows through an S-deep shared-memory ring:
+//   warp 0  loader   cp.async 16B (or 4B) copies of a and b/u rows -> ring
+//   warp 1  helper   gated form: b = (1-a)*u in place (same rounding as ref)
+//   warp 2  chain    lane = channel, s = fma(a,s,b) per row, result over b
+//   warp 3  storer   coalesced row stores of the results
+// Stages are handed on with mbarriers (full -> ready -> done -> empty); every
+// wait is bounded and records an error instead of hanging. The sequential
+// chain is the only serial part: ~one dependent FFMA per row.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+
+#include "kernels.cuh"
+#include "ptx.cuh"
+#include "recur.h"
+#include "runtime.cuh"
+
+namespace sn {
+namespace {
+
+constexpr int kTC = 128;  // rows per chunk
+
+template <int CW>
+struct ScanCfg {
+    static constexpr int S = CW == 8 ? 12 : (CW == 16 ? 7 : 4);  // ring depth (~100-128 KB)
+    static constexpr size_t smem = 2ull * S * kTC * CW * sizeof(float) + 4ull * S * 8;
+};
+
+__device__ __forceinline__ float rec_fused(float a, float s, float b) { return __fmaf_rn(a, s, b); }
+__device__ __forceinline__ float rec_split(float a, float s, float b) {
+    return __fadd_rn(__fmul_rn(a, s), b);
+}
+
+// The serial part: kTC rows of one channel (stride CW in shared memory),
+// s = fma(a, s, b), result written over b. The next 16 rows are loaded into
+// registers before the current 16 are chained, so the only dependency left
+// per row is the FMA itself (restrict: the a and b tiles never alias).
+template <int CW>
+__device__ __forceinline__ float chain_chunk(const float* __restrict__ pa, float* __restrict__ pb,
+                                             float s) {
+    constexpr int G = 16;
+    float ca[G], cb[G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+        ca[j] = pa[j * CW];
+        cb[j] = pb[j * CW];
+    }
+#pragma unroll
+    for (int g = 0; g < kTC / G; ++g) {
+        float na[G], nb[G];
+        if (g + 1 < kTC / G) {
+#pragma unroll
+            for (int j = 0; j < G; ++j) {
+                na[j] = pa[((g + 1) * G + j) * CW];
+                nb[j] = pb[((g + 1) * G + j) * CW];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < G; ++j) {
+            s = rec_fused(ca[j], s, cb[j]);
+            pb[(g * G + j) * CW] = s;
+        }
+        if (g + 1 < kTC / G) {
+#pragma unroll
+            for (int j = 0; j < G; ++j) {
+                ca[j] = na[j];
+                cb[j] = nb[j];
+            }
+        }
+    }
+    return s;
+}
+
+template <int CW>
+__global__ void __launch_bounds__(128)
+    scan_exact_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                      const float* __restrict__ s0, float* __restrict__ out,
+                      float* __restrict__ send, int T, int N, int nv, int gated, int vec,
+                      int* err) {
+    constexpr int S = ScanCfg<CW>::S;
+    constexpr int TILE = kTC * CW;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    float* sa = reinterpret_cast<float*>(smem_raw);
+    float* sb = sa + S * TILE;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sb + S * TILE);
+    uint64_t* ready = full + S;
+    uint64_t* done = ready + S;
+    uint64_t* empty = done + S;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bb = blockIdx.y;
+    const int d0 = blockIdx.x * CW;
+    const size_t base = (size_t)bb * T * N;
+    const int nch = (T + kTC - 1) / kTC;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 32);
+            mbar_init(&ready[i], 32);
+            mbar_init(&done[i], 32);
+            mbar_init(&empty[i], 32);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == 0) {  // ---------------------------------------------- loader
+        for (int c = 0; c < nch; ++c) {
+            const int st = c % S;
+            if (c >= S && !mbar_wait(&empty[st], ((c / S) - 1) & 1, err)) break;
+            const int t0 = c * kTC;
+            float* da = sa + st * TILE;
+            float* db = sb + st * TILE;
+            if (vec) {
+                constexpr int Q = CW / 4;
+#pragma unroll 4
+                for (int i = lane; i < kTC * Q; i += 32) {
+                    const int r = i / Q, q = i % Q;
+                    const int t = t0 + r, d = d0 + 4 * q;
+                    const bool ok = t < T && d < N;
+                    const size_t off = ok ? base + (size_t)t * N + d : 0;
+                    cp_async16(da + r * CW + 4 * q, a + off, ok ? 16u : 0u);
+                    cp_async16(db + r * CW + 4 * q, b + off, ok ? 16u : 0u);
+                }
+            } else {
+                for (int i = lane; i < TILE; i += 32) {
+                    const int r = i / CW, ch = i % CW;
+                    const int t = t0 + r, d = d0 + ch;
+                    const bool ok = t < T && d < N;
+                    const size_t off = ok ? base + (size_t)t * N + d : 0;
+                    cp_async4(da + i, a + off, ok ? 4u : 0u);
+                    cp_async4(db + i, b + off, ok ? 4u : 0u);
+                }
+            }
+            cp_async_arrive(&full[st]);
+        }
+        cp_async_wait_all();
+    } else if (warp == 1) {  // --------------------------------------- helper
+        for (int c = 0; c < nch; ++c) {
+            const int st = c % S;
+            if (!mbar_wait(&full[st], (c / S) & 1, err)) break;
+            if (gated) {
+                float4* da = reinterpret_cast<float4*>(sa + st * TILE);
+                float4* db = reinterpret_cast<float4*>(sb + st * TILE);
+#pragma unroll 4
+                for (int i = lane; i < TILE / 4; i += 32) {
+                    const float4 x = da[i];
+                    float4 u = db[i];
+                    u.x = __fmul_rn(__fsub_rn(1.0f, x.x), u.x);
+                    u.y = __fmul_rn(__fsub_rn(1.0f, x.y), u.y);
+                    u.z = __fmul_rn(__fsub_rn(1.0f, x.z), u.z);
+                    u.w = __fmul_rn(__fsub_rn(1.0f, x.w), u.w);
+                    db[i] = u;
+                }
+            }
+            mbar_arrive(&ready[st]);
+        }
+    } else if (warp == 2) {  // ---------------------------------------- chain
+        const int d = d0 + lane;
+        const bool live = lane < CW && d < N;
+        float s = live ? s0[(size_t)bb * N + d] : 0.0f;
+        const bool all_fused = d0 + CW <= nv;
+        const bool fused = d < nv;
+        for (int c = 0; c < nch; ++c) {
+            const int st = c % S;
+            if (!mbar_wait(&ready[st], (c / S) & 1, err)) break;
+            const int rows = min(kTC, T - c * kTC);
+            if (lane < CW) {
+                const float* pa = sa + st * TILE + lane;
+                float* pb = sb + st * TILE + lane;
+                if (all_fused && rows == kTC) {
+                    s = chain_chunk<CW>(pa, pb, s);
+                } else {
+                    for (int r = 0; r < rows; ++r) {
+                        const float av = pa[r * CW], bv = pb[r * CW];
+                        s = fused ? rec_fused(av, s, bv) : rec_split(av, s, bv);
+                        pb[r * CW] = s;
+                    }
+                }
+            }
+            mbar_arrive(&done[st]);
+        }
+        if (live) send[(size_t)bb * N + d] = s;
+    } else {  // ------------------------------------------------------ storer
+        for (int c = 0; c < nch; ++c) {
+            const int st = c % S;
+            if (!mbar_wait(&done[st], (c / S) & 1, err)) break;
+            const int t0 = c * kTC;
+            const int rows = min(kTC, T - t0);
+            const float* db = sb + st * TILE;
+            if (vec) {
+                constexpr int Q = CW / 4;
+                for (int i = lane; i < rows * Q; i += 32) {
+                    const int r = i / Q, q = i % Q;
+                    const int d = d0 + 4 * q;
+                    if (d < N)
+                        *reinterpret_cast<float4*>(out + base + (size_t)(t0 + r) * N + d) =
+                            *reinterpret_cast<const float4*>(db + r * CW + 4 * q);
+                }
+            } else {
+                for (int i = lane; i < rows * CW; i += 32) {
+                    const int r = i / CW, ch = i % CW;
+                    const int d = d0 + ch;
+                    if (d < N) out[base + (size_t)(t0 + r) * N + d] = db[i];
+                }
+            }
+            __syncwarp();
+            mbar_arrive(&empty[st]);
+        }
+    }
+}
+
+template <int CW>
+int launch_scan_cw(const float* a, const float* b, const float* s0, float* out, float* send,
+                   int B, int T, int N, int gated, int vec, cudaStream_t st) {
+    static bool attr = false;
+    const size_t smem = ScanCfg<CW>::smem;
+    if (!attr) {
+        SN_TRY(cuda_check(cudaFuncSetAttribute(scan_exact_kernel<CW>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem),
+                          "scan smem attr"));
+        attr = true;
+    }
+    dim3 grid((N + CW - 1) / CW, B);
+    scan_exact_kernel<CW><<<grid, 128, smem, st>>>(a, b, s0, out, send, T, N, N - N % 8, gated,
+                                                   vec, rt().d_err);
+    return cuda_check(cudaGetLastError(), "scan launch");
+}
+
+// Channels per CTA: enough CTAs to cover the SMs, wide rows when there are
+// plenty. SN_SCAN_CW (8/16/32) overrides, for tuning sweeps.
+int pick_cw(int B, int N) {
+    static int forced = -1;
+    if (forced < 0) {
+        const char* e = getenv("SN_SCAN_CW");
+        forced = e ? atoi(e) : 0;
+    }
+    if (forced == 8 || forced == 16 || forced == 32) return forced;
+    const long long sms = rt().num_sms;
+    if ((long long)B * ((N + 31) / 32) >= 2 * sms) return 32;
+    if ((long long)B * ((N + 15) / 16) >= sms) return 16;
+    return 8;
+}
+
+}  // namespace
+
+// Device-pointer scan used by the ABI entry points and by the model code.
+int launch_scan(const float* a, const float* b, const float* s0, float* out, float* send, int B,
+                int T, int N, int gated, cudaStream_t st) {
+    if (B > 65535) return fail(SN_E_INVAL, "recur_scan: B=%d exceeds 65535", B);
+    const bool vec = N % 4 == 0 && ((uintptr_t)a % 16 == 0) && ((uintptr_t)b % 16 == 0) &&
+                     ((uintptr_t)out % 16 == 0);
+    switch (pick_cw(B, N)) {
+        case 32: return launch_scan_cw<32>(a, b, s0, out, send, B, T, N, gated, vec, st);
+        case 16: return launch_scan_cw<16>(a, b, s0, out, send, B, T, N, gated, vec, st);
+        default: return launch_scan_cw<8>(a, b, s0, out, send, B, T, N, gated, vec, st);
+    }
+}
+
+// ------------------------------------------------------------------- step
+__global__ void step_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                            float* __restrict__ s, long long total, int N, int nv, int gated) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const float av = a[i];
+        const float bv = gated ? __fmul_rn(__fsub_rn(1.0f, av), b[i]) : b[i];
+        const int d = (int)(i % N);
+        s[i] = d < nv ? rec_fused(av, s[i], bv) : rec_split(av, s[i], bv);
+    }
+}
+
+int launch_step(const float* a, const float* b, float* s, int B, int N, int gated,
+                cudaStream_t st) {
+    const long long total = (long long)B * N;
+    const int blocks = grid_blocks(total);
+    step_kernel<<<blocks, 256, 0, st>>>(a, b, s, total, N, N - N % 8, gated);
+    return cuda_check(cudaGetLastError(), "step launch");
+}
+
+// ------------------------------------------------------------- INT8 quant
+// One CTA per (row, block): amax by max-reduction (exact), then the reference
+// arithmetic: sc = amax/127 (1 if amax == 0), inv = 1/sc, q = rint(x*inv).
+__global__ void quant_i8_kernel(const float* __restrict__ x, int8_t* __restrict__ q,
+                                float* __restrict__ scale, int N, int block, int nb) {
+    const int k = blockIdx.x, row = blockIdx.y;
+    const int lo = k * block, hi = min(N, lo + block);
+    const float* xr = x + (size_t)row * N;
+    float m = 0.0f;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) m = fmaxf(m, fabsf(xr[i]));
+    __shared__ float red[32];
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (threadIdx.x == 0) red[0] = m;
+    }
+    __syncthreads();
+    const float amax = red[0];
+    const float sc = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+    const float inv = __fdiv_rn(1.0f, sc);
+    if (threadIdx.x == 0) scale[(size_t)row * nb + k] = sc;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        float t = rintf(__fmul_rn(xr[i], inv));
+        t = fminf(fmaxf(t, -127.0f), 127.0f);
+        q[(size_t)row * N + i] = (int8_t)(int)t;
+    }
+}
+
+__global__ void dequant_i8_kernel(const int8_t* __restrict__ q, const float* __restrict__ scale,
+                                  float* __restrict__ x, long long total, int N, int block,
+                                  int nb) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long row = i / N;
+        const int col = (int)(i - row * N);
+        x[i] = __fmul_rn((float)q[i], scale[row * nb + col / block]);
+    }
+}
+
+}  // namespace sn
+
+using namespace sn;
+
+// ======================================================== C-ABI entry points
+namespace {
+
+int do_scan(const float* a, const float* b, const float* s0, float* out, float* send, int B,
+            int T, int N, int gated) {
+    if (!a || !b || !s0 || !out || !send || B <= 0 || T <= 0 || N <= 0)
+        return fail(SN_E_INVAL, "recur_scan: null pointer or non-positive dimension");
+    SN_TRY(ensure_init());
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    const size_t big = (size_t)B * T * N * sizeof(float), small = (size_t)B * N * sizeof(float);
+    Arr A, Bv, S0, O, SE;
+    SN_TRY(stage_in(a, big, 0, &A));
+    SN_TRY(stage_in(b, big, 1, &Bv));
+    SN_TRY(stage_in(s0, small, 2, &S0));
+    SN_TRY(stage_out(out, big, 3, &O));
+    SN_TRY(stage_out(send, small, 4, &SE));
+    SN_TRY(launch_scan((const float*)A.dev, (const float*)Bv.dev, (const float*)S0.dev,
+                       (float*)O.dev, (float*)SE.dev, B, T, N, gated ? 1 : 0, stream()));
+    SN_TRY(copy_back(O));
+    SN_TRY(copy_back(SE));
+    return finish(O.host || SE.host || A.dev != a || Bv.dev != b || S0.dev != s0);
+}
+
+int do_step(const float* a, const float* b, float* s, int B, int N, int gated) {
+    if (!a || !b || !s || B <= 0 || N <= 0)
+        return fail(SN_E_INVAL, "recur_step: null pointer or non-positive dimension");
+    SN_TRY(ensure_init());
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    const size_t n = (size_t)B * N * sizeof(float);
+    Arr A, Bv, Sx;
+    SN_TRY(stage_in(a, n, 0, &A));
+    SN_TRY(stage_in(b, n, 1, &Bv));
+    SN_TRY(stage_inout(s, n, 2, &Sx));
+    SN_TRY(launch_step((const float*)A.dev, (const float*)Bv.dev, (float*)Sx.dev, B, N,
+                       gated ? 1 : 0, stream()));
+    SN_TRY(copy_back(Sx));
+    return finish(Sx.host || A.dev != a || Bv.dev != b);
+}
+
+int do_quant_i8(const float* x, int8_t* q, float* scale, int B, int N, int block) {
+    if (!x || !q || !scale || B <= 0 || N <= 0)
+        return fail(SN_E_INVAL, "quant_i8: null pointer or non-positive dimension");
+    SN_TRY(ensure_init());
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    if (block <= 0) block = N;
+    const int nb = (N + block - 1) / block;
+    Arr X, Q, SC;
+    SN_TRY(stage_in(x, (size_t)B * N * 4, 0, &X));
+    SN_TRY(stage_out(q, (size_t)B * N, 1, &Q));
+    SN_TRY(stage_out(scale, (size_t)B * nb * 4, 2, &SC));
+    if (B > 65535) return fail(SN_E_INVAL, "quant_i8: B > 65535 rows");
+    quant_i8_kernel<<<dim3(nb, B), 256, 0, stream()>>>((const float*)X.dev, (int8_t*)Q.dev,
+                                                      (float*)SC.dev, N, block, nb);
+    SN_TRY(cuda_check(cudaGetLastError(), "quant_i8 launch"));
+    SN_TRY(copy_back(Q));
+    SN_TRY(copy_back(SC));
+    return finish(Q.host || SC.host || X.dev != x);
+}
+
+int do_dequant_i8(const int8_t* q, const float* scale, float* x, int B, int N, int block) {
+    if (!x || !q || !scale || B <= 0 || N <= 0)
+        return fail(SN_E_INVAL, "dequant_i8: null pointer or non-positive dimension");
+    SN_TRY(ensure_init());
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    if (block <= 0) block = N;
+    const int nb = (N + block - 1) / block;
+    Arr Q, SC, X;
+    SN_TRY(stage_in(q, (size_t)B * N, 0, &Q));
+    SN_TRY(stage_in(scale, (size_t)B * nb * 4, 1, &SC));
+    SN_TRY(stage_out(x, (size_t)B * N * 4, 2, &X));
+    const long long total = (long long)B * N;
+    const int blocks = grid_blocks(total);
+    dequant_i8_kernel<<<blocks, 256, 0, stream()>>>((const int8_t*)Q.dev, (const float*)SC.dev,
+                                                    (float*)X.dev, total, N, block, nb);
+    SN_TRY(cuda_check(cudaGetLastError(), "dequant_i8 launch"));
+    SN_TRY(copy_back(X));
+    return finish(X.host || Q.dev != q || SC.dev != scale);
+}
+
+}  // namespace
+
+extern "C" {
+
+sn_status sn_abi_recur_scan(const float* a, const float* b, const float* s0, float* out,
+                            float* send, int32_t B, int32_t T, int32_t N, int32_t gated) {
+    return do_scan(a, b, s0, out, send, B, T, N, gated);
+}
+
+sn_status sn_abi_recur_step(const float* a, const float* b, float* s, int32_t B, int32_t N,
+                            int32_t gated) {
+    return do_step(a, b, s, B, N, gated);
+}
+
+sn_status sn_abi_quant_i8(const float* x, int8_t* q, float* scale, int32_t B, int32_t N,
+                          int32_t block) {
+    return do_quant_i8(x, q, scale, B, N, block);
+}
+
+sn_status sn_abi_dequant_i8(const int8_t* q, const float* scale, float* x, int32_t B, int32_t N,
+                            int32_t block) {
+    return do_dequant_i8(q, scale, x, B, N, block);
+}
+
+// Internal symbol set (recur.h): same work, void returns like the reference;
+// failures are reported through sn_abi_last_error.
+void sn_recur_scan(const float* a, const float* b, const float* s0, float* out, float* send, int B,
+                   int T, int N, int gated) {
+    do_scan(a, b, s0, out, send, B, T, N, gated);
+}
+
+void sn_recur_step(const float* a, const float* b, float* s, int B, int N, int gated) {
+    do_step(a, b, s, B, N, gated);
+}
+
+void sn_quant_i8(const float* x, signed char* q, float* scale, int B, int N, int block) {
+    do_quant_i8(x, (int8_t*)q, scale, B, N, block);
+}
+
+void sn_dequant_i8(const signed char* q, const float* scale, float* x, int B, int N, int block) {
+    do_dequant_i8((const int8_t*)q, scale, x, B, N, block);
+}
+
+}  // extern "C"

@@ -1,0 +1,87 @@
+// Library runtime: one CUDA context per process, one stream, staging of host
+// arrays, error reporting. Every C-ABI entry point goes through here.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <mutex>
+
+#include "sn_abi.h"
+
+namespace sn {
+
+struct Runtime {
+    std::recursive_mutex mu;
+    bool inited = false;
+    int device = -1;
+    int num_sms = 148;
+    cudaStream_t own = nullptr;   // library-owned stream, used until a caller picks one
+    cudaStream_t user = nullptr;  // caller stream (sn_abi_cuda_set_stream; NULL = legacy default)
+    bool has_user = false;
+    bool async = false;
+    int threads = 1;
+    int scan_mode = 0;
+    volatile int* h_err = nullptr;  // mapped pinned word written by device waits
+    int* d_err = nullptr;           // device alias of h_err
+    void* slot[12] = {};
+    size_t cap[12] = {};
+};
+
+Runtime& rt();
+int ensure_init();                     // SN_OK or SN_E_DEVICE
+cudaStream_t stream();
+int fail(int code, const char* fmt, ...);
+int cuda_check(cudaError_t e, const char* where);
+bool is_device_ptr(const void* p);
+void* scratch(int slot, size_t bytes);  // device scratch, grows; nullptr on OOM
+int finish(bool host_involved);        // sync when needed, surface device errors
+
+// Device view of a caller array. Host arrays are copied into a scratch slot
+// (inputs) or computed there and copied back by finish_out (outputs).
+struct Arr {
+    void* dev = nullptr;
+    void* host = nullptr;  // non-null when the caller passed host memory
+    size_t bytes = 0;
+};
+int stage_in(const void* p, size_t bytes, int slot, Arr* a);
+int stage_out(void* p, size_t bytes, int slot, Arr* a);
+int stage_inout(void* p, size_t bytes, int slot, Arr* a);
+int copy_back(const Arr& a);
+
+// Blocks of `threads` covering `total` items, at most `per_sm` blocks per SM
+// (grid-stride kernels loop over the rest).
+inline int grid_blocks(long long total, int threads = 256, int per_sm = 8) {
+    const long long b = (total + threads - 1) / threads;
+    const long long cap = (long long)per_sm * rt().num_sms;
+    return (int)(b < 1 ? 1 : (b < cap ? b : cap));
+}
+
+// Kernel-family timing with CUDA events on the launching stream. Active only
+// between sn_abi_cuda_profile(1) and sn_abi_cuda_profile(0), and only for work
+// enqueued directly (model steps are then run without their CUDA graph).
+bool prof_on();
+void prof_begin(const char* family, cudaStream_t st);
+void prof_end(cudaStream_t st);
+
+struct ProfScope {
+    cudaStream_t st;
+    bool on;
+    ProfScope(const char* family, cudaStream_t s) : st(s), on(prof_on()) {
+        if (on) prof_begin(family, st);
+    }
+    ~ProfScope() {
+        if (on) prof_end(st);
+    }
+};
+
+// Error codes written into the device error word.
+enum DevErr : int { kErrNone = 0, kErrWaitTimeout = 1, kErrBadIndex = 2 };
+
+}  // namespace sn
+
+#define SN_TRY(expr)                 \
+    do {                             \
+        int _rc = (expr);            \
+        if (_rc != SN_OK) return _rc; \
+    } while (0)

@@ -1,0 +1,815 @@
+// RWKV-7 whole-model decode on sm_100a.
+//
+// Reference: sunnynet/runtime/rwkv7.c (head_step 143-189, rk_layer 191-320,
+// sn_rk_step 349-360, sn_rk_prefill 362-364, sn_rk_dbg 366-374, sn_rk_load
+// 415-508) and the numpy oracle RWKV7.step (runtime/rwkv7.py:123-211).
+//
+// Per layer and step, for B sequences:
+//   tmix_prep   xn = LN(x); d = shift0 - xn; six lerps; shift0 <- xn
+//   GEMVs       r, k, v, tanh(W1 xw), A1 xa, V1 xv, sigmoid(G1 xg)
+//   GEMVs       W2, A2, V2, G2 on the LoRA intermediates
+//   mix         w = exp(-sig(.)/sqrt(e)), v-first mix, a = sig(.), kk, k
+//   heads       per (sequence, head) CTA: the 64x64 state in place,
+//               S <- S*diag(w) - (S kk^)(kk^ a)^T + v k^T, y = S r, then the
+//               per-head group norm, the r.k bonus and the g gate
+//   GEMV        x += Wo y
+//   cmix_prep   xn2 = LN(x); xk = lerp(xn2, shift1); shift1 <- xn2
+//   GEMVs       relu(Wk xk)^2, then x += Wv (.)
+// then the final LN and the LM head. INT4 matrices run the W4A8 GEMV of
+// quant4.cu (bit-identical to the reference's sn_gemv_i4); fp32 matrices the
+// fp32 contraction of gemm.cu. The step is captured into a CUDA graph per B.
+//
+// HBM layout: INT4 codes (out,in/2) + scales (out,in/block) fp32 or fp16;
+// fp32 matrices transposed at load to (out,in); state S [seq][L][NH][HS][HS]
+// (row i = value dim), token shift [seq][L][2][D].
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <vector>
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+#include "runtime.cuh"
+#include "rwkv7.h"
+#include "sn_abi.h"
+
+namespace sn {
+namespace {
+
+constexpr int32_t kKRWK = 0x4B57524B;
+constexpr float kInvSqrtE = 0.6065306597126334f;  // rwkv7.c:33
+constexpr float kEpsGroup = 6.4e-4f;               // rwkv7.c:34
+
+__device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ float block_sum(float v, float* red) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    v = l < nw ? red[l] : 0.0f;
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// LN of one row held in `xr` (two-pass, as rwkv7.c:128-140); returns mean/rstd.
+__device__ void row_stats(const float* xr, int n, float eps, float* red, float* mean,
+                          float* rstd) {
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += xr[i];
+    const float m = block_sum(s, red) / (float)n;
+    float v = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float d = xr[i] - m;
+        v += d * d;
+    }
+    *mean = m;
+    *rstd = 1.0f / sqrtf(block_sum(v, red) / (float)n + eps);
+}
+
+// x = LN(embed[tok]) (rwkv7.c:352-353)
+__global__ void rk_embed_kernel(int D, const int32_t* __restrict__ tok, int vocab,
+                                int* __restrict__ err, const float* __restrict__ embed,
+                                const float* __restrict__ w, const float* __restrict__ b,
+                                float* __restrict__ x, float eps) {
+    __shared__ float red[32];
+    int t = tok[blockIdx.x];
+    if (t < 0 || t >= vocab) {  // never read outside the table; report instead
+        if (threadIdx.x == 0) atomicExch(err, kErrBadIndex);
+        t = 0;
+    }
+    const float* e = embed + (size_t)t * D;
+    float mean, rstd;
+    row_stats(e, D, eps, red, &mean, &rstd);
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+        x[(size_t)blockIdx.x * D + i] = (e[i] - mean) * rstd * w[i] + b[i];
+}
+
+// time-mix prologue (rwkv7.c:213-226); lerps written as 6 (B,D) planes
+__global__ void rk_tmix_prep_kernel(int D, int B, const float* __restrict__ x,
+                                    float* __restrict__ shift, long long shift_stride,
+                                    const float* __restrict__ w, const float* __restrict__ b,
+                                    const float* __restrict__ lerp, float* __restrict__ xn_out,
+                                    float* __restrict__ planes, float eps) {
+    __shared__ float red[32];
+    const int s = blockIdx.x;
+    const float* xr = x + (size_t)s * D;
+    float* sh = shift + s * shift_stride;
+    float mean, rstd;
+    row_stats(xr, D, eps, red, &mean, &rstd);
+    const size_t plane = (size_t)B * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        const float xn = (xr[i] - mean) * rstd * w[i] + b[i];
+        const float d = sh[i] - xn;
+        float* o = planes + (size_t)s * D + i;
+#pragma unroll
+        for (int j = 0; j < 6; ++j) o[j * plane] = xn + lerp[j * D + i] * d;
+        sh[i] = xn;
+        xn_out[(size_t)s * D + i] = xn;
+    }
+}
+
+// w, v-first mix, a, kk, k (rwkv7.c:232-264); one thread per (seq, channel)
+__global__ void rk_mix_kernel(int B, int D, int first, const float* __restrict__ dw,
+                              const float* __restrict__ w0, const float* __restrict__ dv,
+                              const float* __restrict__ v0, const float* __restrict__ da,
+                              const float* __restrict__ a0, const float* __restrict__ kkw,
+                              const float* __restrict__ kaw, float* __restrict__ ww,
+                              float* __restrict__ v, float* __restrict__ vfirst,
+                              float* __restrict__ a, float* __restrict__ k,
+                              float* __restrict__ kk) {
+    const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (idx >= (long long)B * D) return;
+    const int i = (int)(idx % D);
+    ww[idx] = expf(-sigm(dw[idx] + w0[i]) * kInvSqrtE);
+    if (first) {
+        vfirst[idx] = v[idx];
+    } else {
+        const float vv = v[idx];
+        v[idx] = vv + (vfirst[idx] - vv) * sigm(dv[idx] + v0[i]);
+    }
+    const float aa = sigm(da[idx] + a0[i]);
+    a[idx] = aa;
+    const float kv = k[idx];
+    kk[idx] = kv * kkw[i];
+    k[idx] = kv + kv * (aa - 1.0f) * kaw[i];
+}
+
+// One CTA (8 warps) per (sequence, head): the matrix-state update of
+// rwkv7.c:143-189 followed by group norm + bonus + gate (rwkv7.c:268-289).
+// A warp owns state rows i = warp, warp+8, ...; a lane owns VPL columns.
+template <int VPL>
+__global__ void __launch_bounds__(256)
+    rk_heads_kernel(int NH, int L, int layer, int D, float* __restrict__ S,
+                    const float* __restrict__ ww, const float* __restrict__ k,
+                    const float* __restrict__ v, const float* __restrict__ a,
+                    const float* __restrict__ kk, const float* __restrict__ r,
+                    const float* __restrict__ g, const float* __restrict__ rk,
+                    const float* __restrict__ lnw, const float* __restrict__ lnb,
+                    float* __restrict__ y) {
+    constexpr int HS = VPL * 32;
+    __shared__ float kn[HS], yv[HS], red[32];
+    const int h = blockIdx.x % NH, b = blockIdx.x / NH;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t o = (size_t)b * D + (size_t)h * HS;
+    float* Sh = S + (((size_t)b * L + layer) * NH + h) * HS * HS;
+    // kk normalised with floor 1e-12 (rwkv7.c:162-165)
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < HS; j += blockDim.x) ss += kk[o + j] * kk[o + j];
+    float nrm = sqrtf(block_sum(ss, red));
+    if (!(nrm > 1e-12f)) nrm = 1e-12f;
+    const float inv = 1.0f / nrm;
+    for (int j = threadIdx.x; j < HS; j += blockDim.x) kn[j] = kk[o + j] * inv;
+    __syncthreads();
+    float wj[VPL], kj[VPL], rj[VPL], knj[VPL], kaj[VPL];
+#pragma unroll
+    for (int t = 0; t < VPL; ++t) {
+        const int j = lane + 32 * t;
+        wj[t] = ww[o + j];
+        kj[t] = k[o + j];
+        rj[t] = r[o + j];
+        knj[t] = kn[j];
+        kaj[t] = __fmul_rn(kn[j], a[o + j]);
+    }
+    for (int i = warp; i < HS; i += 8) {
+        float* row = Sh + (size_t)i * HS;
+        float sv[VPL];
+        float p = 0.0f;
+#pragma unroll
+        for (int t = 0; t < VPL; ++t) {
+            sv[t] = row[lane + 32 * t];
+            p = fmaf(sv[t], knj[t], p);
+        }
+        for (int off = 16; off; off >>= 1) p += __shfl_xor_sync(0xffffffffu, p, off);
+        const float vi = v[o + i];
+        float yacc = 0.0f;
+#pragma unroll
+        for (int t = 0; t < VPL; ++t) {
+            const float ns =
+                __fmaf_rn(sv[t], wj[t], __fsub_rn(__fmul_rn(vi, kj[t]), __fmul_rn(p, kaj[t])));
+            row[lane + 32 * t] = ns;
+            yacc = fmaf(ns, rj[t], yacc);
+        }
+        for (int off = 16; off; off >>= 1) yacc += __shfl_xor_sync(0xffffffffu, yacc, off);
+        if (lane == 0) yv[i] = yacc;
+    }
+    __syncthreads();
+    // group norm over the head, r.k bonus, gate
+    float m = 0.0f;
+    for (int j = threadIdx.x; j < HS; j += blockDim.x) m += yv[j];
+    const float mean = block_sum(m, red) / (float)HS;
+    float var = 0.0f, dot = 0.0f;
+    for (int j = threadIdx.x; j < HS; j += blockDim.x) {
+        const float t = yv[j] - mean;
+        var += t * t;
+        dot += r[o + j] * k[o + j] * rk[h * HS + j];
+    }
+    const float rstd = 1.0f / sqrtf(block_sum(var, red) / (float)HS + kEpsGroup);
+    dot = block_sum(dot, red);
+    for (int j = threadIdx.x; j < HS; j += blockDim.x) {
+        const float nv = (yv[j] - mean) * rstd * lnw[h * HS + j] + lnb[h * HS + j];
+        y[o + j] = (nv + dot * v[o + j]) * g[o + j];
+    }
+}
+
+// channel-mix prologue (rwkv7.c:295-297)
+__global__ void rk_cmix_prep_kernel(int D, const float* __restrict__ x, float* __restrict__ shift,
+                                    long long shift_stride, const float* __restrict__ w,
+                                    const float* __restrict__ b, const float* __restrict__ lerp,
+                                    float* __restrict__ xk, float eps) {
+    __shared__ float red[32];
+    const int s = blockIdx.x;
+    const float* xr = x + (size_t)s * D;
+    float* sh = shift + s * shift_stride + D;
+    float mean, rstd;
+    row_stats(xr, D, eps, red, &mean, &rstd);
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        const float xn2 = (xr[i] - mean) * rstd * w[i] + b[i];
+        xk[(size_t)s * D + i] = xn2 + lerp[i] * (sh[i] - xn2);
+        sh[i] = xn2;
+    }
+}
+
+// y = LN(x) per row (final norm)
+__global__ void rk_ln_kernel(int D, const float* __restrict__ x, const float* __restrict__ w,
+                             const float* __restrict__ b, float* __restrict__ y, float eps) {
+    __shared__ float red[32];
+    const float* xr = x + (size_t)blockIdx.x * D;
+    float mean, rstd;
+    row_stats(xr, D, eps, red, &mean, &rstd);
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+        y[(size_t)blockIdx.x * D + i] = (xr[i] - mean) * rstd * w[i] + b[i];
+}
+
+__global__ void rk_argmax_kernel(int V, const float* __restrict__ lg, int32_t* __restrict__ out) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const float* r = lg + (size_t)blockIdx.x * V;
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = r[i];
+        if (v > best || (v == best && i < idx)) {
+            best = v;
+            idx = i;
+        }
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) {
+            best = ov;
+            idx = oi;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        bv[threadIdx.x >> 5] = best;
+        bi[threadIdx.x >> 5] = idx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+            if (bv[k] > best || (bv[k] == best && bi[k] < idx)) {
+                best = bv[k];
+                idx = bi[k];
+            }
+        out[blockIdx.x] = idx;
+    }
+}
+
+__global__ void rk_transpose_kernel(const float* __restrict__ src, float* __restrict__ dst, int in,
+                                    int out) {
+    __shared__ float t[32][33];
+    const int bx = blockIdx.x * 32, by = blockIdx.y * 32;
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int i = by + j, o = bx + threadIdx.x;
+        if (i < in && o < out) t[j][threadIdx.x] = src[(size_t)i * out + o];
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int o = bx + j, i = by + threadIdx.x;
+        if (i < in && o < out) dst[(size_t)o * in + i] = t[threadIdx.x][j];
+    }
+}
+
+}  // namespace
+
+struct RkMat {
+    int q4 = 0, in = 0, out = 0, block = 0;
+    bool fp16 = false;
+    float* w = nullptr;  // fp32 (out,in)
+    uint8_t* q = nullptr;
+    void* scale = nullptr;
+};
+
+struct RkLayer {
+    float *ln1w, *ln1b, *ln2w, *ln2b, *lerp;
+    RkMat rw, kw, vw, ow, w1, w2, a1, a2, v1, v2, g1, g2, cmk, cmv;
+    float *w0, *a0, *v0, *kkw, *kaw, *rkw, *lnxw, *lnxb, *cmk_lerp;
+    int Rw, Ra, Rv, Rg;
+};
+
+struct RwkvModel {
+    int vocab = 0, D = 0, HS = 0, NH = 0, F = 0, L = 0, nseq = 0, q4 = 0, group = 64;
+    float eps = 1e-5f;
+    std::vector<RkLayer> ly;
+    float *en_w = nullptr, *en_b = nullptr, *on_w = nullptr, *on_b = nullptr, *embed = nullptr;
+    RkMat head;
+    float *S = nullptr, *shift = nullptr;
+    int32_t *tok = nullptr, *next = nullptr;
+    float *x = nullptr, *xn = nullptr, *planes = nullptr, *r = nullptr, *k = nullptr, *v = nullptr;
+    float *a = nullptr, *g = nullptr, *kk = nullptr, *ww = nullptr, *y = nullptr, *xk2 = nullptr;
+    float *lo_w = nullptr, *lo_a = nullptr, *lo_v = nullptr, *lo_g = nullptr;
+    float *dw = nullptr, *da = nullptr, *dv = nullptr, *ck = nullptr, *vfirst = nullptr;
+    float *logits = nullptr, *xf = nullptr;
+    std::vector<void*> allocs;
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+    cudaStream_t cap = nullptr;
+    bool ready = false;
+
+    ~RwkvModel() {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        if (cap) cudaStreamDestroy(cap);
+        for (void* p : allocs) cudaFree(p);
+    }
+    template <class T>
+    T* dalloc(size_t n) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, (n ? n : 1) * sizeof(T)) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        allocs.push_back(p);
+        return (T*)p;
+    }
+};
+
+namespace {
+
+// Parses the tagged tensor stream of a KRWK file held in host memory.
+struct RkParser {
+    RwkvModel* m;
+    const unsigned char* p;
+    const unsigned char* end;
+    int version;
+    bool ok = true;
+    float* tmp = nullptr;
+    size_t tmp_n = 0;
+
+    const unsigned char* take(size_t n) {
+        if (!ok || (size_t)(end - p) < n) {
+            ok = false;
+            return nullptr;
+        }
+        const unsigned char* r = p;
+        p += n;
+        return r;
+    }
+    int i32() {
+        const unsigned char* q = take(4);
+        int v = 0;
+        if (q) memcpy(&v, q, 4);
+        return v;
+    }
+    template <class T>
+    T* upload(const void* src, size_t n) {
+        T* d = m->dalloc<T>(n);
+        if (!d || cudaMemcpy(d, src, n * sizeof(T), cudaMemcpyHostToDevice) != cudaSuccess) {
+            ok = false;
+            return nullptr;
+        }
+        return d;
+    }
+    float* vec(size_t n) {  // rwkv7.c:404-409
+        if (i32() != 0) ok = false;
+        const unsigned char* q = take(n * 4);
+        return q ? upload<float>(q, n) : nullptr;
+    }
+    void mat(RkMat* M, int in, int out) {  // rwkv7.c:380-402 (+ tag 2)
+        const int tag = i32();
+        M->in = in;
+        M->out = out;
+        if (!ok) return;
+        if (tag == 0) {
+            const size_t n = (size_t)in * out;
+            const unsigned char* q = take(n * 4);
+            if (!q) return;
+            if (tmp_n < n) {
+                if (tmp) cudaFree(tmp);
+                tmp = nullptr;
+                if (cudaMalloc(&tmp, n * 4) != cudaSuccess) {
+                    cudaGetLastError();
+                    ok = false;
+                    return;
+                }
+                tmp_n = n;
+            }
+            cudaMemcpy(tmp, q, n * 4, cudaMemcpyHostToDevice);
+            M->w = m->dalloc<float>(n);
+            if (!M->w) {
+                ok = false;
+                return;
+            }
+            dim3 grid((out + 31) / 32, (in + 31) / 32);
+            rk_transpose_kernel<<<grid, dim3(32, 8)>>>(tmp, M->w, in, out);
+        } else if (tag == 1 || (tag == 2 && version == 4)) {
+            const int blk = tag == 1 ? 64 : m->group;
+            if (blk <= 0 || in % blk) {
+                ok = false;
+                return;
+            }
+            const size_t qb = (size_t)out * (in / 2), ns = (size_t)out * (in / blk);
+            const unsigned char* q = take(qb);
+            const unsigned char* s = take(ns * (tag == 1 ? 4 : 2));
+            if (!q || !s) return;
+            M->q4 = 1;
+            M->block = blk;
+            M->fp16 = tag == 2;
+            M->q = upload<uint8_t>(q, qb);
+            M->scale = tag == 1 ? (void*)upload<float>(s, ns) : (void*)upload<__half>(s, ns);
+        } else {
+            ok = false;
+        }
+    }
+};
+
+int load_rwkv(RwkvModel* m, const char* path, int nseq) {
+    FILE* f = fopen(path, "rb");
+    if (!f) return fail(SN_E_IO, "cannot open %s", path);
+    fseek(f, 0, SEEK_END);
+    const long n = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    if (n < 48) {
+        fclose(f);
+        return fail(SN_E_FORMAT, "%s: truncated", path);
+    }
+    std::vector<unsigned char> buf((size_t)n);
+    const size_t got = fread(buf.data(), 1, (size_t)n, f);
+    fclose(f);
+    if (got != (size_t)n) return fail(SN_E_IO, "%s: short read", path);
+    int32_t h[10];
+    memcpy(h, buf.data(), 40);
+    if (h[0] != kKRWK || (h[1] != 3 && h[1] != 4))
+        return fail(SN_E_FORMAT, "%s: bad magic/version", path);
+    SN_TRY(ensure_init());
+    RkParser P{m, buf.data() + 40, buf.data() + buf.size(), h[1]};
+    m->L = h[2]; m->D = h[3]; m->HS = h[4]; m->NH = h[5]; m->F = h[6]; m->vocab = h[8];
+    m->q4 = h[9];
+    m->nseq = nseq;
+    const unsigned char* pe = P.take(4);
+    if (pe) memcpy(&m->eps, pe, 4);
+    if (h[1] == 4) m->group = P.i32();
+    const int L = m->L, D = m->D;
+    if (!P.ok || L <= 0 || D <= 0 || m->vocab <= 0 || m->F <= 0 || m->NH * m->HS != D ||
+        !(m->HS == 32 || m->HS == 64 || m->HS == 128 || m->HS == 256))
+        return fail(SN_E_FORMAT, "%s: unsupported dims", path);
+    m->ly.resize(L);
+    int rmax = 0;
+    for (int l = 0; l < L; ++l) {
+        RkLayer& A = m->ly[l];
+        A.Rw = P.i32(); A.Ra = P.i32(); A.Rv = P.i32(); A.Rg = P.i32();
+        rmax = std::max(std::max(rmax, std::max(A.Rw, A.Ra)), std::max(A.Rv, A.Rg));
+    }
+    for (int l = 0; l < L && P.ok; ++l) {
+        RkLayer& A = m->ly[l];
+        A.ln1w = P.vec(D); A.ln1b = P.vec(D); A.ln2w = P.vec(D); A.ln2b = P.vec(D);
+        A.lerp = P.vec((size_t)6 * D);
+        P.mat(&A.rw, D, D); P.mat(&A.kw, D, D); P.mat(&A.vw, D, D); P.mat(&A.ow, D, D);
+        P.mat(&A.w1, D, A.Rw); P.mat(&A.w2, A.Rw, D);
+        P.mat(&A.a1, D, A.Ra); P.mat(&A.a2, A.Ra, D);
+        P.mat(&A.v1, D, A.Rv); P.mat(&A.v2, A.Rv, D);
+        P.mat(&A.g1, D, A.Rg); P.mat(&A.g2, A.Rg, D);
+        A.w0 = P.vec(D); A.a0 = P.vec(D); A.v0 = P.vec(D);
+        A.kkw = P.vec(D); A.kaw = P.vec(D); A.rkw = P.vec(D);
+        A.lnxw = P.vec(D); A.lnxb = P.vec(D);
+        P.mat(&A.cmk, D, m->F); P.mat(&A.cmv, m->F, D);
+        A.cmk_lerp = P.vec(D);
+    }
+    if (P.ok) {
+        m->en_w = P.vec(D); m->en_b = P.vec(D); m->on_w = P.vec(D); m->on_b = P.vec(D);
+        m->embed = P.vec((size_t)m->vocab * D);
+        P.mat(&m->head, D, m->vocab);
+    }
+    if (P.tmp) cudaFree(P.tmp);
+    if (!P.ok) return fail(SN_E_FORMAT, "%s: malformed tensor stream", path);
+    const size_t B = (size_t)nseq;
+    m->S = m->dalloc<float>(B * L * m->NH * m->HS * m->HS);
+    m->shift = m->dalloc<float>(B * L * 2 * D);
+    m->tok = m->dalloc<int32_t>(B);
+    m->next = m->dalloc<int32_t>(B);
+    m->x = m->dalloc<float>(B * D); m->xn = m->dalloc<float>(B * D);
+    m->planes = m->dalloc<float>(6 * B * D);
+    m->r = m->dalloc<float>(B * D); m->k = m->dalloc<float>(B * D); m->v = m->dalloc<float>(B * D);
+    m->a = m->dalloc<float>(B * D); m->g = m->dalloc<float>(B * D); m->kk = m->dalloc<float>(B * D);
+    m->ww = m->dalloc<float>(B * D); m->y = m->dalloc<float>(B * D); m->xk2 = m->dalloc<float>(B * D);
+    m->lo_w = m->dalloc<float>(B * rmax); m->lo_a = m->dalloc<float>(B * rmax);
+    m->lo_v = m->dalloc<float>(B * rmax); m->lo_g = m->dalloc<float>(B * rmax);
+    m->dw = m->dalloc<float>(B * D); m->da = m->dalloc<float>(B * D); m->dv = m->dalloc<float>(B * D);
+    m->ck = m->dalloc<float>(B * m->F); m->vfirst = m->dalloc<float>(B * D);
+    m->xf = m->dalloc<float>(B * D);
+    m->logits = m->dalloc<float>(B * m->vocab);
+    if (!m->logits || !m->xf) return fail(SN_E_NOMEM, "device allocation failed");
+    cudaMemset(m->S, 0, B * L * m->NH * m->HS * m->HS * 4);
+    cudaMemset(m->shift, 0, B * L * 2 * D * 4);
+    SN_TRY(cuda_check(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking), "stream"));
+    SN_TRY(cuda_check(cudaDeviceSynchronize(), "rwkv load"));
+    m->ready = true;
+    return SN_OK;
+}
+
+// y (B,out) [epi]= M x (B,in)
+int mat_mul(const RkMat& M, float* y, const float* x, int B, int epi, cudaStream_t st) {
+    ProfScope ps(M.q4 ? "w4a8_gemv" : "gemm_f32", st);
+    if (M.q4) {
+        static const int map[] = {kW4Store, kW4Add, kW4Relu2, kW4Tanh, kW4Sigmoid};
+        return launch_w4a8(y, x, M.q, M.scale, B, M.in, M.out, M.block, M.fp16, st, map[epi]);
+    }
+    GemmArgs g;
+    g.M = B; g.N = M.out; g.K = M.in;
+    g.A = x; g.lda = M.in;
+    g.W = M.w; g.ldw = M.in;
+    g.C = y; g.ldc = M.out;
+    static const int emap[] = {kEpiNone, kEpiAdd, kEpiRelu2, kEpiTanh, kEpiSigmoid};
+    g.epi = emap[epi];
+    return launch_gemm(g, kWF32, st);
+}
+
+enum { E_STORE = 0, E_ADD = 1, E_RELU2 = 2, E_TANH = 3, E_SIG = 4 };
+
+int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer = -1) {
+    const int D = m->D;
+    const size_t plane = (size_t)B * D;
+    const long long sh_stride = (long long)m->L * 2 * D;
+    rk_embed_kernel<<<B, 256, 0, st>>>(D, m->tok, m->vocab, rt().d_err, m->embed, m->en_w,
+                                       m->en_b, m->x, m->eps);
+    const int nl = last_layer >= 0 ? last_layer + 1 : m->L;
+    const unsigned ew = (unsigned)((plane + 255) / 256);
+    for (int l = 0; l < nl; ++l) {
+        const RkLayer& A = m->ly[l];
+        float* sh = m->shift + (size_t)l * 2 * D;
+        rk_tmix_prep_kernel<<<B, 256, 0, st>>>(D, B, m->x, sh, sh_stride, A.ln1w, A.ln1b, A.lerp,
+                                               m->xn, m->planes, m->eps);
+        const float *xr = m->planes, *xw = xr + plane, *xk = xw + plane, *xv = xk + plane,
+                    *xa = xv + plane, *xg = xa + plane;
+        SN_TRY(mat_mul(A.rw, m->r, xr, B, E_STORE, st));
+        SN_TRY(mat_mul(A.kw, m->k, xk, B, E_STORE, st));
+        SN_TRY(mat_mul(A.vw, m->v, xv, B, E_STORE, st));
+        SN_TRY(mat_mul(A.w1, m->lo_w, xw, B, E_TANH, st));
+        SN_TRY(mat_mul(A.w2, m->dw, m->lo_w, B, E_STORE, st));
+        if (l > 0) {
+            SN_TRY(mat_mul(A.v1, m->lo_v, xv, B, E_STORE, st));
+            SN_TRY(mat_mul(A.v2, m->dv, m->lo_v, B, E_STORE, st));
+        }
+        SN_TRY(mat_mul(A.a1, m->lo_a, xa, B, E_STORE, st));
+        SN_TRY(mat_mul(A.a2, m->da, m->lo_a, B, E_STORE, st));
+        SN_TRY(mat_mul(A.g1, m->lo_g, xg, B, E_SIG, st));
+        SN_TRY(mat_mul(A.g2, m->g, m->lo_g, B, E_STORE, st));
+        rk_mix_kernel<<<ew, 256, 0, st>>>(B, D, l == 0 ? 1 : 0, m->dw, A.w0, m->dv, A.v0, m->da,
+                                         A.a0, A.kkw, A.kaw, m->ww, m->v, m->vfirst, m->a, m->k,
+                                         m->kk);
+        const int grid = B * m->NH;
+        ProfScope ps_heads("rk_heads", st);
+        switch (m->HS) {
+#define RK_HEADS(V)                                                                            \
+    rk_heads_kernel<V><<<grid, 256, 0, st>>>(m->NH, m->L, l, D, m->S, m->ww, m->k, m->v, m->a, \
+                                             m->kk, m->r, m->g, A.rkw, A.lnxw, A.lnxb, m->y);  \
+    break;
+            case 32: RK_HEADS(1)
+            case 64: RK_HEADS(2)
+            case 128: RK_HEADS(4)
+            default: RK_HEADS(8)
+#undef RK_HEADS
+        }
+        SN_TRY(mat_mul(A.ow, m->x, m->y, B, E_ADD, st));
+        rk_cmix_prep_kernel<<<B, 256, 0, st>>>(D, m->x, sh, sh_stride, A.ln2w, A.ln2b, A.cmk_lerp,
+                                               m->xk2, m->eps);
+        SN_TRY(mat_mul(A.cmk, m->ck, m->xk2, B, E_RELU2, st));
+        SN_TRY(mat_mul(A.cmv, m->x, m->ck, B, E_ADD, st));
+    }
+    if (last_layer < 0 && head) {
+        rk_ln_kernel<<<B, 256, 0, st>>>(D, m->x, m->on_w, m->on_b, m->xf, m->eps);
+        SN_TRY(mat_mul(m->head, m->logits, m->xf, B, E_STORE, st));
+    }
+    return cuda_check(cudaGetLastError(), "rwkv step launch");
+}
+
+int rk_run(RwkvModel* m, int B, bool head) {
+    if (prof_on()) return enqueue_rk(m, B, head, stream());  // bracket kernels, no graph
+    auto key = std::make_pair(B, head ? 1 : 0);
+    auto it = m->graphs.find(key);
+    if (it == m->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        SN_TRY(cuda_check(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeThreadLocal),
+                          "begin capture"));
+        const int rc = enqueue_rk(m, B, head, m->cap);
+        const cudaError_t e = cudaStreamEndCapture(m->cap, &g);
+        if (rc != SN_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        SN_TRY(cuda_check(e, "end capture"));
+        cudaGraphExec_t ex = nullptr;
+        const cudaError_t e2 = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        SN_TRY(cuda_check(e2, "graph instantiate"));
+        it = m->graphs.emplace(key, ex).first;
+    }
+    return cuda_check(cudaGraphLaunch(it->second, stream()), "graph launch");
+}
+
+int rk_step(RwkvModel* m, const int32_t* tokens, int B, float* logits, int32_t* next) {
+    if (!m || !m->ready || !tokens || B <= 0 || B > m->nseq)
+        return fail(SN_E_INVAL, "rwkv7_step: bad handle, tokens or B");
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaStream_t st = stream();
+    const bool tdev = is_device_ptr(tokens);
+    SN_TRY(cuda_check(cudaMemcpyAsync(m->tok, tokens, (size_t)B * 4,
+                                      tdev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st),
+                      "tokens"));
+    SN_TRY(rk_run(m, B, logits || next));
+    bool host = !tdev;
+    if (logits) {
+        const bool dev = is_device_ptr(logits);
+        host |= !dev;
+        SN_TRY(cuda_check(cudaMemcpyAsync(logits, m->logits, (size_t)B * m->vocab * 4,
+                                          dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                                          st),
+                          "logits"));
+    }
+    if (next) {
+        rk_argmax_kernel<<<B, 256, 0, st>>>(m->vocab, m->logits, m->next);
+        const bool dev = is_device_ptr(next);
+        host |= !dev;
+        SN_TRY(cuda_check(cudaMemcpyAsync(next, m->next, (size_t)B * 4,
+                                          dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                                          st),
+                          "next"));
+    }
+    return finish(host);
+}
+
+int rk_reset(RwkvModel* m) {
+    if (!m || !m->ready) return fail(SN_E_INVAL, "rwkv7_reset: bad handle");
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    const size_t B = (size_t)m->nseq;
+    cudaStream_t st = stream();
+    cudaMemsetAsync(m->S, 0, B * m->L * m->NH * m->HS * m->HS * 4, st);
+    cudaMemsetAsync(m->shift, 0, B * m->L * 2 * m->D * 4, st);
+    return finish(false);
+}
+
+}  // namespace
+}  // namespace sn
+
+using namespace sn;
+
+struct SnAbiRwkv7 {
+    std::unique_ptr<RwkvModel> m;
+};
+struct SnRWKV7 {
+    std::unique_ptr<RwkvModel> m;
+};
+
+namespace {
+std::unique_ptr<RwkvModel> open_rwkv(const char* path, int nseq) {
+    if (!path || nseq <= 0) {
+        fail(SN_E_INVAL, "rwkv7 load: null path or nseq <= 0");
+        return nullptr;
+    }
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    auto m = std::make_unique<RwkvModel>();
+    if (load_rwkv(m.get(), path, nseq) != SN_OK) return nullptr;
+    return m;
+}
+}  // namespace
+
+extern "C" {
+
+SnAbiRwkv7* sn_abi_rwkv7_load(const char* blob_path) {
+    auto m = open_rwkv(blob_path, 1);
+    return m ? new SnAbiRwkv7{std::move(m)} : nullptr;
+}
+
+SnAbiRwkv7* sn_abi_rwkv7_load_batch(const char* blob_path, int32_t nseq) {
+    auto m = open_rwkv(blob_path, nseq);
+    return m ? new SnAbiRwkv7{std::move(m)} : nullptr;
+}
+
+int32_t sn_abi_rwkv7_vocab(const SnAbiRwkv7* m) { return m ? m->m->vocab : 0; }
+
+sn_status sn_abi_rwkv7_step(SnAbiRwkv7* m, int32_t token, float* logits) {
+    if (!m || !logits || token < 0) return SN_E_INVAL;
+    if (token >= m->m->vocab) return fail(SN_E_INVAL, "token %d out of range", token);
+    return rk_step(m->m.get(), &token, 1, logits, nullptr);
+}
+
+sn_status sn_abi_rwkv7_prefill(SnAbiRwkv7* m, const int32_t* tokens, int32_t n, float* logits) {
+    if (!m || !tokens || !logits || n <= 0) return SN_E_INVAL;
+    for (int i = 0; i < n; ++i) {
+        if (tokens[i] < 0 || tokens[i] >= m->m->vocab) return SN_E_INVAL;
+        SN_TRY(rk_step(m->m.get(), tokens + i, 1, i == n - 1 ? logits : nullptr, nullptr));
+    }
+    return SN_OK;
+}
+
+sn_status sn_abi_rwkv7_reset(SnAbiRwkv7* m) { return m ? rk_reset(m->m.get()) : SN_E_INVAL; }
+
+void sn_abi_rwkv7_free(SnAbiRwkv7* m) {
+    if (!m) return;
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaDeviceSynchronize();
+    delete m;
+}
+
+sn_status sn_abi_rwkv7_step_batch(SnAbiRwkv7* m, const int32_t* tokens, int32_t B,
+                                  float* logits) {
+    return m ? rk_step(m->m.get(), tokens, B, logits, nullptr) : SN_E_INVAL;
+}
+
+sn_status sn_abi_rwkv7_step_argmax(SnAbiRwkv7* m, const int32_t* tokens, int32_t B,
+                                   int32_t* next) {
+    if (!m || !next) return SN_E_INVAL;
+    return rk_step(m->m.get(), tokens, B, nullptr, next);
+}
+
+sn_status sn_abi_rwkv7_get_state(SnAbiRwkv7* m, int32_t B, float* S, float* shift) {
+    if (!m || !S || !shift || B <= 0 || B > m->m->nseq) return SN_E_INVAL;
+    RwkvModel* r = m->m.get();
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    const size_t ns = (size_t)B * r->L * r->NH * r->HS * r->HS * 4;
+    const size_t nh = (size_t)B * r->L * 2 * r->D * 4;
+    const bool d1 = is_device_ptr(S), d2 = is_device_ptr(shift);
+    cudaStream_t st = stream();
+    SN_TRY(cuda_check(cudaMemcpyAsync(S, r->S, ns, d1 ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st), "S"));
+    SN_TRY(cuda_check(cudaMemcpyAsync(shift, r->shift, nh, d2 ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st), "shift"));
+    return finish(true);
+}
+
+int32_t sn_abi_rwkv7_dims(const SnAbiRwkv7* m, int32_t* d) {
+    if (!m || !d) return SN_E_INVAL;
+    const RwkvModel* r = m->m.get();
+    const int32_t v[8] = {r->vocab, r->D, r->HS, r->NH, r->F, r->L, r->q4, r->group};
+    memcpy(d, v, sizeof v);
+    return SN_OK;
+}
+
+// ---------------------------------------------------- reference rwkv7.h symbol set
+SnRWKV7* sn_rk_load(const char* path) {
+    auto m = open_rwkv(path, 1);
+    return m ? new SnRWKV7{std::move(m)} : nullptr;
+}
+
+void sn_rk_free(SnRWKV7* m) {
+    if (!m) return;
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaDeviceSynchronize();
+    delete m;
+}
+
+void sn_rk_reset(SnRWKV7* m) {
+    if (m) rk_reset(m->m.get());
+}
+
+void sn_rk_step(SnRWKV7* m, int token, float* logits) {
+    if (!m) return;
+    const int32_t t = token;
+    rk_step(m->m.get(), &t, 1, logits, nullptr);
+}
+
+void sn_rk_prefill(SnRWKV7* m, const int* tokens, int n, float* logits) {
+    if (!m || !tokens || n <= 0) return;
+    for (int i = 0; i < n; ++i) {
+        const int32_t t = tokens[i];
+        if (rk_step(m->m.get(), &t, 1, i == n - 1 ? logits : nullptr, nullptr) != SN_OK) return;
+    }
+}
+
+void sn_rk_dbg(SnRWKV7* m, int token, int layer, float* out) {
+    if (!m || !out || layer < 0 || layer >= m->m->L) return;
+    RwkvModel* r = m->m.get();
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaStream_t st = stream();
+    const int32_t t = token;
+    cudaMemcpyAsync(r->tok, &t, 4, cudaMemcpyHostToDevice, st);
+    if (enqueue_rk(r, 1, false, st, layer) != SN_OK) return;
+    // xn, r, k, v, a, g, ww, y, x (rwkv7.c:322-333)
+    const float* parts[9] = {r->xn, r->r, r->k, r->v, r->a, r->g, r->ww, r->y, r->x};
+    Arr o;
+    if (stage_out(out, (size_t)9 * r->D * 4, 7, &o) != SN_OK) return;
+    for (int i = 0; i < 9; ++i)
+        cudaMemcpyAsync((char*)o.dev + (size_t)i * r->D * 4, parts[i], (size_t)r->D * 4,
+                        cudaMemcpyDeviceToDevice, st);
+    copy_back(o);
+    finish(true);
+}
+
+int sn_rk_vocab(const SnRWKV7* m) { return m ? m->m->vocab : 0; }
+int sn_rk_ready(const SnRWKV7* m) { return m && m->m->ready ? 1 : 0; }
+
+}  // extern "C"

@@ -1,0 +1,838 @@
+// SunnyNet whole-model decode on sm_100a.
+//
+// Reference: sunnynet/runtime/sunnynet.c (sn_load 358-454, layer_step 212-291,
+// sn_step 321-334, sn_prefill 347-349, sn_reset 296-303, sn_dbg_layer 336-345)
+// and the batched oracle SunnyNet.forward_step (model.py:113-124,
+// layers.py:287-326).
+//
+// Per layer and step, for the B sequences of a batch (rows of every matrix
+// below are sequences):
+//   prep        raw = LN(x); at = raw + sum_k w_k*{raw, hist}; hist ring <- raw
+//   GEMM Ws     sfb = s_old Ws^T                    (reads the previous state)
+//   GEMM V      v = at V^T
+//   GEMM U      q = v U^T
+//   gate        u = q[:D]*sig(g_i-g_{i+1})*sig(g_i-g_{i+2}) in groups of G,
+//               p = 1 - delta(1-sig(g)), s = p*s + (1-p)*u   (state in place)
+//   GEMM Wz     z = u Wz^T, softwedge epilogue
+//   stats       per-row mean / rstd of z
+//   GEMM Wc     out = LN(z) Wc^T + (b_gain*s + sfb + x)   (LN applied on load)
+// then stats + LM head with the final LN applied on load. The whole step is
+// captured once per batch size into a CUDA graph and replayed.
+//
+// HBM layout: weights (out,in) row-major (fp32, fp16 or int8 + fp32 row
+// scale); state s [seq][L][D]; conv history as a ring [seq][L][K-1][D] with a
+// per-sequence write position (newest at slot (pos-1) mod (K-1)), so a step
+// writes one history row instead of shifting K-1 of them.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <vector>
+
+#include "gemm.cuh"
+#include "runtime.cuh"
+#include "sn_abi.h"
+#include "sunnynet.h"
+
+namespace sn {
+namespace {
+
+constexpr int32_t kUSNN = 0x4E4E5355;
+constexpr int32_t kUSNQ = 0x514E5355;
+
+__device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// Block-wide sum (blockDim.x multiple of 32, <= 1024).
+__device__ float block_sum(float v, float* red) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    v = l < nw ? red[l] : 0.0f;
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// One CTA per sequence: x (layer 0: embedding row), LN, causal taps, ring write.
+__global__ void prep_kernel(int D, int K, int KH, int layer, int L, const int32_t* __restrict__ tok,
+                            int vocab, int* __restrict__ err,
+                            const float* __restrict__ embed, float* __restrict__ x,
+                            float* __restrict__ raw_out, float* __restrict__ at,
+                            float* __restrict__ hist, int32_t* __restrict__ pos,
+                            const float* __restrict__ g, const float* __restrict__ c,
+                            const float* __restrict__ dw, float eps) {
+    __shared__ float red[32];
+    const int b = blockIdx.x;
+    // ring position of this (sequence, layer); every thread reads it before the
+    // block-wide barriers below, thread 0 advances it at the end
+    const int p = pos[b * L + layer];
+    float* xr = x + (size_t)b * D;
+    if (layer == 0) {
+        int t = tok[b];
+        if (t < 0 || t >= vocab) {  // never read outside the table; report instead
+            if (threadIdx.x == 0) atomicExch(err, kErrBadIndex);
+            t = 0;
+        }
+        const float* e = embed + (size_t)t * D;
+        for (int i = threadIdx.x; i < D; i += blockDim.x) xr[i] = e[i];
+        __syncthreads();
+    }
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) s += xr[i];
+    const float mean = block_sum(s, red) / (float)D;
+    float v = 0.0f;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        const float d = xr[i] - mean;
+        v += d * d;
+    }
+    const float rstd = 1.0f / sqrtf(block_sum(v, red) / (float)D + eps);
+    float* hb = hist + ((size_t)b * L + layer) * KH * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        const float r = (xr[i] - mean) * rstd * g[i] + c[i];
+        float a = r;
+        if (K > 1) {
+            float acc = r * dw[(size_t)(K - 1) * D + i];
+            for (int k = 0; k < K - 1; ++k) {
+                const int slot = ((p - 1 - k) % KH + KH) % KH;
+                acc += hb[(size_t)slot * D + i] * dw[(size_t)(K - 2 - k) * D + i];
+            }
+            a = r + acc;
+            hb[(size_t)(((p % KH) + KH) % KH) * D + i] = r;
+        }
+        at[(size_t)b * D + i] = a;
+        if (raw_out) raw_out[(size_t)b * D + i] = r;
+    }
+    if (threadIdx.x == 0) pos[b * L + layer] = p + 1;
+}
+
+// Gated competition + decay gate + state update, one thread per (seq, channel).
+__global__ void gate_kernel(int B, int D, int G, int L, int layer, const float* __restrict__ q,
+                            const float* __restrict__ delta, float* __restrict__ s,
+                            float* __restrict__ u, float* __restrict__ gate_out, int clamp,
+                            float p_floor) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= (long long)B * D) return;
+    const int b = (int)(i / D), d = (int)(i % D);
+    const float* qb = q + (size_t)b * 2 * D;
+    const int base = (d / G) * G, off = d - base;
+    const float g0 = qb[D + d];
+    const float g1 = qb[D + base + (off + 1) % G];
+    const float g2 = qb[D + base + (off + 2) % G];
+    const float uu = qb[d] * (sigm(g0 - g1) * sigm(g0 - g2));
+    float p = 1.0f - delta[d] * (1.0f - sigm(g0));
+    if (clamp && p < p_floor) p = p_floor;
+    float* sp = s + ((size_t)b * L + layer) * D + d;
+    *sp = p * *sp + (1.0f - p) * uu;
+    u[i] = uu;
+    if (gate_out) gate_out[i] = g0;
+}
+
+// Two-pass row mean / rstd.
+__global__ void rowstats_kernel(int n, const float* __restrict__ X, long long ldx,
+                                float* __restrict__ mu, float* __restrict__ rs, float eps) {
+    __shared__ float red[32];
+    const float* xr = X + blockIdx.x * ldx;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += xr[i];
+    const float mean = block_sum(s, red) / (float)n;
+    float v = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float d = xr[i] - mean;
+        v += d * d;
+    }
+    const float r = 1.0f / sqrtf(block_sum(v, red) / (float)n + eps);
+    if (threadIdx.x == 0) {
+        mu[blockIdx.x] = mean;
+        rs[blockIdx.x] = r;
+    }
+}
+
+// y = LN(z) materialised (debug dumps only).
+__global__ void apply_ln_kernel(int n, const float* __restrict__ z, const float* __restrict__ mu,
+                                const float* __restrict__ rs, const float* __restrict__ g,
+                                const float* __restrict__ c, float* __restrict__ y) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        y[(size_t)blockIdx.x * n + i] = (z[(size_t)blockIdx.x * n + i] - mu[blockIdx.x]) *
+                                            rs[blockIdx.x] * g[i] + c[i];
+}
+
+// Greedy next token: argmax of each logits row, lowest id on ties.
+__global__ void argmax_kernel(int V, const float* __restrict__ lg, int32_t* __restrict__ out) {
+    __shared__ float bv[32];
+    __shared__ int bi[32];
+    const float* r = lg + (size_t)blockIdx.x * V;
+    float best = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = r[i];
+        if (v > best || (v == best && i < idx)) {
+            best = v;
+            idx = i;
+        }
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > best || (ov == best && oi < idx)) {
+            best = ov;
+            idx = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        bv[w] = best;
+        bi[w] = idx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+            if (bv[k] > best || (bv[k] == best && bi[k] < idx)) {
+                best = bv[k];
+                idx = bi[k];
+            }
+        out[blockIdx.x] = idx;
+    }
+}
+
+// (in,out) -> (out,in)
+__global__ void transpose_kernel(const float* __restrict__ src, float* __restrict__ dst, int in,
+                                 int out) {
+    __shared__ float t[32][33];
+    const int bx = blockIdx.x * 32, by = blockIdx.y * 32;  // bx over out, by over in
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int i = by + j, o = bx + threadIdx.x;
+        if (i < in && o < out) t[j][threadIdx.x] = src[(size_t)i * out + o];
+    }
+    __syncthreads();
+    for (int j = threadIdx.y; j < 32; j += blockDim.y) {
+        const int o = bx + j, i = by + threadIdx.x;
+        if (i < in && o < out) dst[(size_t)o * in + i] = t[threadIdx.x][j];
+    }
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ s, __half* __restrict__ d, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        d[i] = __float2half_rn(s[i]);
+}
+
+// state export / import: ring <-> newest-first history
+__global__ void hist_io_kernel(int B, int L, int KH, int D, float* ring, float* flat,
+                               int32_t* pos, int to_flat) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const long long total = (long long)B * L * KH * D;
+    if (i >= total) return;
+    const int d = (int)(i % D);
+    const int k = (int)((i / D) % KH);
+    const long long bl = i / ((long long)KH * D);
+    const int p = to_flat ? pos[bl] : 0;  // pos is [seq][layer], bl = seq*L + layer
+    const int slot = ((p - 1 - k) % KH + KH) % KH;
+    float* r = ring + (bl * KH + slot) * D + d;
+    if (to_flat) flat[i] = *r;
+    else *r = flat[i];
+}
+
+}  // namespace
+
+struct SunnyLayer {
+    float *ni_g, *ni_c, *nm_g, *nm_c, *dw, *delta;
+    void *V, *U, *Wz, *Wc, *Ws;
+    float *sV, *sU, *sWz, *sWc, *sWs;  // int8 row scales
+    float a_tanh, b_gain;
+};
+
+struct SunnyModel {
+    int vocab = 0, D = 0, I = 0, R = 0, K = 0, L = 0, G = 0, clamp = 0, nseq = 0, KH = 1;
+    int wtype = kWF32;
+    float eps = 0, p_floor = 0;
+    std::vector<SunnyLayer> ly;
+    float *no_g = nullptr, *no_c = nullptr, *embed = nullptr;
+    void* head = nullptr;
+    float* shead = nullptr;
+    std::vector<void*> allocs;
+    // state
+    float* s = nullptr;
+    float* hist = nullptr;
+    int32_t* pos = nullptr;
+    // activations (nseq rows)
+    int32_t* tok = nullptr;
+    int32_t* next = nullptr;
+    float *x = nullptr, *at = nullptr, *raw = nullptr, *v = nullptr, *q = nullptr, *u = nullptr;
+    float *gate = nullptr, *sfb = nullptr, *z = nullptr, *mu = nullptr, *rs = nullptr;
+    float *logits = nullptr, *yn = nullptr;
+    std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (B, with head) -> graph
+    cudaStream_t cap = nullptr;
+    bool ready = false;
+
+    ~SunnyModel() {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        if (cap) cudaStreamDestroy(cap);
+        for (void* p : allocs) cudaFree(p);
+    }
+
+    template <class T>
+    T* dalloc(size_t n) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, (n ? n : 1) * sizeof(T)) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        allocs.push_back(p);
+        return (T*)p;
+    }
+};
+
+namespace {
+
+struct BlobReader {
+    FILE* f = nullptr;
+    bool ok = true;
+    explicit BlobReader(const char* path) : f(fopen(path, "rb")) { ok = f != nullptr; }
+    ~BlobReader() {
+        if (f) fclose(f);
+    }
+    bool read(void* dst, size_t n) {
+        if (ok && fread(dst, 1, n, f) != n) ok = false;
+        return ok;
+    }
+};
+
+// Upload helpers (host staging buffer reused).
+struct Uploader {
+    SunnyModel* m;
+    BlobReader* br;
+    std::vector<unsigned char> host;
+    float* tmp = nullptr;  // device scratch for transposes
+    size_t tmp_n = 0;
+    int rc = SN_OK;
+
+    float* vec(size_t n) {
+        float* d = m->dalloc<float>(n);
+        host.resize(n * 4);
+        if (!d) {
+            rc = SN_E_NOMEM;
+            return nullptr;
+        }
+        if (!br->read(host.data(), n * 4)) {
+            rc = SN_E_IO;
+            return nullptr;
+        }
+        if (cudaMemcpy(d, host.data(), n * 4, cudaMemcpyHostToDevice) != cudaSuccess) rc = SN_E_DEVICE;
+        return d;
+    }
+
+    // fp32 (in,out) block -> (out,in) fp32 or fp16 on device
+    void* mat_f32(int in, int out, bool half) {
+        const size_t n = (size_t)in * out;
+        if (tmp_n < n) {
+            if (tmp) cudaFree(tmp);
+            if (cudaMalloc(&tmp, n * 4) != cudaSuccess) {
+                cudaGetLastError();
+                rc = SN_E_NOMEM;
+                tmp = nullptr;
+                tmp_n = 0;
+                return nullptr;
+            }
+            tmp_n = n;
+        }
+        host.resize(n * 4);
+        if (!br->read(host.data(), n * 4)) {
+            rc = SN_E_IO;
+            return nullptr;
+        }
+        if (cudaMemcpy(tmp, host.data(), n * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+            rc = SN_E_DEVICE;
+            return nullptr;
+        }
+        float* d = m->dalloc<float>(n);
+        if (!d) {
+            rc = SN_E_NOMEM;
+            return nullptr;
+        }
+        dim3 grid((out + 31) / 32, (in + 31) / 32);
+        transpose_kernel<<<grid, dim3(32, 8)>>>(tmp, d, in, out);
+        if (!half) return d;
+        __half* h = m->dalloc<__half>(n);
+        if (!h) {
+            rc = SN_E_NOMEM;
+            return nullptr;
+        }
+        f32_to_f16_kernel<<<grid_blocks((long long)n), 256>>>(d, h, (long long)n);
+        return h;
+    }
+
+    // int8 (out,in) codes + fp32 row scales
+    void* mat_i8(int in, int out, float** scale) {
+        const size_t n = (size_t)in * out;
+        int8_t* d = m->dalloc<int8_t>(n);
+        if (!d) {
+            rc = SN_E_NOMEM;
+            return nullptr;
+        }
+        host.resize(n);
+        if (!br->read(host.data(), n)) {
+            rc = SN_E_IO;
+            return nullptr;
+        }
+        if (cudaMemcpy(d, host.data(), n, cudaMemcpyHostToDevice) != cudaSuccess) rc = SN_E_DEVICE;
+        *scale = vec((size_t)out);
+        return d;
+    }
+};
+
+int load_model(SunnyModel* m, const char* path, int nseq, bool half, const int* want) {
+    BlobReader br(path);
+    if (!br.ok) return fail(SN_E_IO, "cannot open %s", path);
+    int32_t h[12];
+    if (!br.read(h, 40)) return fail(SN_E_FORMAT, "%s: truncated header", path);
+    bool quant = false;
+    int vocab, D, I, R, K, L, G, tied, clamp;
+    if (h[0] == kUSNN) {
+        vocab = h[1]; D = h[2]; I = h[3]; R = h[4]; K = h[5]; L = h[6]; G = h[7]; tied = h[8];
+        clamp = h[9];
+    } else if (h[0] == kUSNQ) {
+        if (!br.read(h + 10, 8) || h[1] != 1 || h[11] != 8)
+            return fail(SN_E_FORMAT, "%s: unsupported USNQ version", path);
+        quant = true;
+        vocab = h[2]; D = h[3]; I = h[4]; R = h[5]; K = h[6]; L = h[7]; G = h[8]; tied = h[9];
+        clamp = h[10];
+    } else {
+        return fail(SN_E_FORMAT, "%s: bad magic 0x%08x", path, (unsigned)h[0]);
+    }
+    if (want) {  // sn_load: caller dims must match the header (sunnynet.c:363-368)
+        const int got[8] = {vocab, D, I, R, K, L, G, tied};
+        for (int i = 0; i < 8; ++i)
+            if (got[i] != want[i]) return fail(SN_E_FORMAT, "%s: header/dims mismatch", path);
+    }
+    if (vocab <= 0 || D <= 0 || I <= 0 || R <= 0 || K <= 0 || L <= 0 || G < 3 || D % G)
+        return fail(SN_E_FORMAT, "%s: invalid dims", path);
+    if (half && quant) return fail(SN_E_UNSUPPORTED, "fp16 load of an INT8 blob");
+    SN_TRY(ensure_init());
+    m->vocab = vocab; m->D = D; m->I = I; m->R = R; m->K = K; m->L = L; m->G = G;
+    m->clamp = clamp; m->nseq = nseq; m->KH = K > 1 ? K - 1 : 1;
+    m->wtype = quant ? kWI8 : (half ? kWF16 : kWF32);
+    Uploader up{m, &br};
+    m->ly.resize(L);
+    for (int l = 0; l < L && up.rc == SN_OK; ++l) {
+        SunnyLayer& y = m->ly[l];
+        memset(&y, 0, sizeof y);
+        y.ni_g = up.vec(D); y.ni_c = up.vec(D); y.nm_g = up.vec(I); y.nm_c = up.vec(I);
+        y.dw = up.vec((size_t)K * D);
+        if (quant) {
+            y.V = up.mat_i8(D, R, &y.sV);
+            y.U = up.mat_i8(R, 2 * D, &y.sU);
+            y.Wz = up.mat_i8(D, I, &y.sWz);
+            y.Wc = up.mat_i8(I, D, &y.sWc);
+            y.Ws = up.mat_i8(D, D, &y.sWs);
+        } else {
+            y.V = up.mat_f32(D, R, half);
+            y.U = up.mat_f32(R, 2 * D, half);
+            y.Wz = up.mat_f32(D, I, half);
+            y.Wc = up.mat_f32(I, D, half);
+            y.Ws = up.mat_f32(D, D, half);
+        }
+        y.delta = up.vec(D);
+        float sc2[2];
+        if (!br.read(sc2, 8)) up.rc = SN_E_IO;
+        y.a_tanh = sc2[0];
+        y.b_gain = sc2[1];
+    }
+    float ep[2] = {0, 0};
+    if (up.rc == SN_OK && !br.read(ep, 8)) up.rc = SN_E_IO;
+    if (up.rc == SN_OK) {
+        m->no_g = up.vec(D);
+        m->no_c = up.vec(D);
+        m->embed = up.vec((size_t)vocab * D);
+        m->head = quant ? up.mat_i8(D, vocab, &m->shead) : up.mat_f32(D, vocab, half);
+    }
+    if (up.tmp) cudaFree(up.tmp);
+    if (up.rc != SN_OK) return fail(up.rc == SN_E_IO ? SN_E_FORMAT : up.rc, "%s: load failed", path);
+    m->eps = ep[0];
+    m->p_floor = ep[1];
+    const size_t n = (size_t)nseq;
+    m->s = m->dalloc<float>(n * L * D);
+    m->hist = m->dalloc<float>(n * L * m->KH * D);
+    m->pos = m->dalloc<int32_t>(n * L);
+    m->tok = m->dalloc<int32_t>(n);
+    m->next = m->dalloc<int32_t>(n);
+    m->x = m->dalloc<float>(n * D);
+    m->at = m->dalloc<float>(n * D);
+    m->raw = m->dalloc<float>(n * D);
+    m->v = m->dalloc<float>(n * R);
+    m->q = m->dalloc<float>(n * 2 * D);
+    m->u = m->dalloc<float>(n * D);
+    m->gate = m->dalloc<float>(n * D);
+    m->sfb = m->dalloc<float>(n * D);
+    m->z = m->dalloc<float>(n * I);
+    m->yn = m->dalloc<float>(n * I);
+    m->mu = m->dalloc<float>(n);
+    m->rs = m->dalloc<float>(n);
+    m->logits = m->dalloc<float>(n * vocab);
+    if (!m->logits || !m->rs) return fail(SN_E_NOMEM, "device allocation failed");
+    SN_TRY(cuda_check(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking), "stream"));
+    cudaMemset(m->s, 0, n * L * D * 4);
+    cudaMemset(m->hist, 0, n * L * m->KH * D * 4);
+    cudaMemset(m->pos, 0, n * L * 4);
+    SN_TRY(cuda_check(cudaDeviceSynchronize(), "load"));
+    m->ready = true;
+    return SN_OK;
+}
+
+GemmArgs gemm(int M, int N, int K, const float* A, const void* W, const float* ws, float* C) {
+    GemmArgs g;
+    g.M = M; g.N = N; g.K = K;
+    g.A = A; g.lda = K;
+    g.W = W; g.ldw = K; g.wscale = ws;
+    g.C = C; g.ldc = N;
+    return g;
+}
+
+// Enqueue one decode step for sequences [0,B) (tokens already in m->tok).
+// last_layer >= 0 stops after that layer and fills the debug buffers.
+int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last_layer = -1) {
+    const int D = m->D, I = m->I, R = m->R;
+    const int nl = last_layer >= 0 ? last_layer + 1 : m->L;
+    const bool dbg = last_layer >= 0;
+    for (int l = 0; l < nl; ++l) {
+        const SunnyLayer& y = m->ly[l];
+        const bool this_dbg = dbg && l == last_layer;
+        {
+            ProfScope ps("prep_ln_taps", st);
+            prep_kernel<<<B, 256, 0, st>>>(D, m->K, m->KH, l, m->L, m->tok, m->vocab, rt().d_err,
+                                           m->embed, m->x, this_dbg ? m->raw : nullptr, m->at,
+                                           m->hist, m->pos, y.ni_g, y.ni_c, y.dw, m->eps);
+        }
+        // feedback reads the previous state: before the gate kernel updates it
+        GemmArgs gs = gemm(B, D, D, m->s + (size_t)l * D, y.Ws, y.sWs, m->sfb);
+        gs.lda = (long long)m->L * D;
+        {
+            ProfScope ps("gemm_Ws", st);
+            SN_TRY(launch_gemm(gs, m->wtype, st));
+        }
+        {
+            ProfScope ps("gemm_V", st);
+            SN_TRY(launch_gemm(gemm(B, R, D, m->at, y.V, y.sV, m->v), m->wtype, st));
+        }
+        {
+            ProfScope ps("gemm_U", st);
+            SN_TRY(launch_gemm(gemm(B, 2 * D, R, m->v, y.U, y.sU, m->q), m->wtype, st));
+        }
+        {
+            ProfScope ps("gate_state", st);
+            gate_kernel<<<(unsigned)(((long long)B * D + 255) / 256), 256, 0, st>>>(
+                B, D, m->G, m->L, l, m->q, y.delta, m->s, m->u, this_dbg ? m->gate : nullptr,
+                m->clamp, m->p_floor);
+        }
+        GemmArgs gz = gemm(B, I, D, m->u, y.Wz, y.sWz, m->z);
+        gz.epi = kEpiWedge;
+        gz.p = y.a_tanh;
+        {
+            ProfScope ps("gemm_Wz", st);
+            SN_TRY(launch_gemm(gz, m->wtype, st));
+        }
+        {
+            ProfScope ps("rowstats", st);
+            rowstats_kernel<<<B, 256, 0, st>>>(I, m->z, I, m->mu, m->rs, m->eps);
+        }
+        if (this_dbg)
+            apply_ln_kernel<<<B, 256, 0, st>>>(I, m->z, m->mu, m->rs, y.nm_g, y.nm_c, m->yn);
+        GemmArgs gc = gemm(B, D, I, m->z, y.Wc, y.sWc, m->x);
+        gc.mu = m->mu; gc.rs = m->rs; gc.g = y.nm_g; gc.c = y.nm_c;
+        gc.epi = kEpiResid;
+        gc.p = y.b_gain;
+        gc.S = m->s + (size_t)l * D;
+        gc.lds = (long long)m->L * D;
+        gc.F = m->sfb; gc.ldf = D;
+        gc.X = m->x; gc.ldx = D;
+        {
+            ProfScope ps("gemm_Wc", st);
+            SN_TRY(launch_gemm(gc, m->wtype, st));
+        }
+    }
+    if (dbg) return cuda_check(cudaGetLastError(), "dbg step");
+    if (with_head) {
+        {
+            ProfScope ps("rowstats", st);
+            rowstats_kernel<<<B, 256, 0, st>>>(D, m->x, D, m->mu, m->rs, m->eps);
+        }
+        GemmArgs gh = gemm(B, m->vocab, D, m->x, m->head, m->shead, m->logits);
+        gh.mu = m->mu; gh.rs = m->rs; gh.g = m->no_g; gh.c = m->no_c;
+        ProfScope ps("gemm_head", st);
+        SN_TRY(launch_gemm(gh, m->wtype, st));
+    }
+    return cuda_check(cudaGetLastError(), "step launch");
+}
+
+// Replay (capturing on first use) the graph of a B-sequence step.
+int run_step(SunnyModel* m, int B, bool with_head) {
+    cudaStream_t st = stream();
+    if (prof_on()) return enqueue_step(m, B, with_head, st);  // bracket kernels, no graph
+    auto key = std::make_pair(B, with_head ? 1 : 0);
+    auto it = m->graphs.find(key);
+    if (it == m->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        SN_TRY(cuda_check(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeThreadLocal),
+                          "begin capture"));
+        const int rc = enqueue_step(m, B, with_head, m->cap);
+        const cudaError_t e = cudaStreamEndCapture(m->cap, &g);
+        if (rc != SN_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        SN_TRY(cuda_check(e, "end capture"));
+        cudaGraphExec_t ex = nullptr;
+        const cudaError_t e2 = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        SN_TRY(cuda_check(e2, "graph instantiate"));
+        it = m->graphs.emplace(key, ex).first;
+    }
+    return cuda_check(cudaGraphLaunch(it->second, st), "graph launch");
+}
+
+int sunny_step(SunnyModel* m, const int32_t* tokens, int B, float* logits, int32_t* next) {
+    if (!m || !m->ready || !tokens || B <= 0 || B > m->nseq)
+        return fail(SN_E_INVAL, "sunny_step: bad handle, tokens or B");
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaStream_t st = stream();
+    const bool tok_dev = is_device_ptr(tokens);
+    SN_TRY(cuda_check(cudaMemcpyAsync(m->tok, tokens, (size_t)B * 4,
+                                      tok_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                      st),
+                      "tokens"));
+    const bool head = logits != nullptr || next != nullptr;
+    SN_TRY(run_step(m, B, head));
+    bool host = !tok_dev;
+    if (logits) {
+        const bool dev = is_device_ptr(logits);
+        host |= !dev;
+        SN_TRY(cuda_check(cudaMemcpyAsync(logits, m->logits, (size_t)B * m->vocab * 4,
+                                          dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                                          st),
+                          "logits"));
+    }
+    if (next) {
+        argmax_kernel<<<B, 256, 0, st>>>(m->vocab, m->logits, m->next);
+        const bool dev = is_device_ptr(next);
+        host |= !dev;
+        SN_TRY(cuda_check(cudaMemcpyAsync(next, m->next, (size_t)B * 4,
+                                          dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                                          st),
+                          "next"));
+    }
+    return finish(host);
+}
+
+int sunny_reset(SunnyModel* m) {
+    if (!m || !m->ready) return fail(SN_E_INVAL, "sunny_reset: bad handle");
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaStream_t st = stream();
+    const size_t n = (size_t)m->nseq;
+    cudaMemsetAsync(m->s, 0, n * m->L * m->D * 4, st);
+    cudaMemsetAsync(m->hist, 0, n * m->L * m->KH * m->D * 4, st);
+    cudaMemsetAsync(m->pos, 0, n * m->L * 4, st);
+    return finish(false);
+}
+
+int sunny_state_io(SunnyModel* m, int B, float* s, float* hist, bool get) {
+    if (!m || !m->ready || B <= 0 || B > m->nseq || !s || !hist)
+        return fail(SN_E_INVAL, "sunny state: bad arguments");
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaStream_t st = stream();
+    const size_t ns = (size_t)B * m->L * m->D * 4, nh = (size_t)B * m->L * m->KH * m->D * 4;
+    Arr S, H;
+    if (get) {
+        SN_TRY(stage_out(s, ns, 5, &S));
+        SN_TRY(stage_out(hist, nh, 6, &H));
+        SN_TRY(cuda_check(cudaMemcpyAsync(S.dev, m->s, ns, cudaMemcpyDeviceToDevice, st), "s"));
+    } else {
+        SN_TRY(stage_in(s, ns, 5, &S));
+        SN_TRY(stage_in(hist, nh, 6, &H));
+        SN_TRY(cuda_check(cudaMemcpyAsync(m->s, S.dev, ns, cudaMemcpyDeviceToDevice, st), "s"));
+        cudaMemsetAsync(m->pos, 0, (size_t)B * m->L * 4, st);
+    }
+    const long long total = (long long)B * m->L * m->KH * m->D;
+    hist_io_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+        B, m->L, m->KH, m->D, m->hist, (float*)H.dev, m->pos, get ? 1 : 0);
+    SN_TRY(cuda_check(cudaGetLastError(), "hist io"));
+    if (get) {
+        SN_TRY(copy_back(S));
+        SN_TRY(copy_back(H));
+    }
+    return finish(true);
+}
+
+}  // namespace
+}  // namespace sn
+
+using namespace sn;
+
+struct SnAbiSunny {
+    std::unique_ptr<SunnyModel> m;
+};
+struct SnModel {
+    std::unique_ptr<SunnyModel> m;
+};
+
+namespace {
+SnAbiSunny* open_sunny(const char* path, int nseq, bool half, const int* want) {
+    if (!path || nseq <= 0) {
+        fail(SN_E_INVAL, "sunny load: null path or nseq <= 0");
+        return nullptr;
+    }
+    auto h = new SnAbiSunny{std::make_unique<SunnyModel>()};
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    if (load_model(h->m.get(), path, nseq, half, want) != SN_OK) {
+        delete h;
+        return nullptr;
+    }
+    return h;
+}
+}  // namespace
+
+extern "C" {
+
+SnAbiSunny* sn_abi_sunny_load(const char* blob_path, int32_t nseq) {
+    return open_sunny(blob_path, nseq, false, nullptr);
+}
+
+void sn_abi_sunny_free(SnAbiSunny* m) {
+    if (!m) return;
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaDeviceSynchronize();
+    delete m;
+}
+
+sn_status sn_abi_sunny_reset(SnAbiSunny* m) { return m ? sunny_reset(m->m.get()) : SN_E_INVAL; }
+
+int32_t sn_abi_sunny_vocab(const SnAbiSunny* m) { return m ? m->m->vocab : 0; }
+
+int32_t sn_abi_sunny_dims(const SnAbiSunny* m, int32_t* d) {
+    if (!m || !d) return SN_E_INVAL;
+    const SunnyModel* s = m->m.get();
+    const int32_t v[8] = {s->vocab, s->D, s->I, s->R, s->K, s->L, s->G, s->wtype};
+    memcpy(d, v, sizeof v);
+    return SN_OK;
+}
+
+sn_status sn_abi_sunny_step(SnAbiSunny* m, const int32_t* tokens, int32_t B, float* logits) {
+    if (!m) return SN_E_INVAL;
+    return sunny_step(m->m.get(), tokens, B, logits, nullptr);
+}
+
+sn_status sn_abi_sunny_step_argmax(SnAbiSunny* m, const int32_t* tokens, int32_t B,
+                                   int32_t* next) {
+    if (!m || !next) return SN_E_INVAL;
+    return sunny_step(m->m.get(), tokens, B, nullptr, next);
+}
+
+sn_status sn_abi_sunny_prefill(SnAbiSunny* m, const int32_t* tokens, int32_t B, int32_t T,
+                               float* logits) {
+    if (!m || !tokens || B <= 0 || T <= 0 || B > m->m->nseq) return SN_E_INVAL;
+    // token rows are (B,T): feed column t of every sequence, head on the last only
+    std::vector<int32_t> col((size_t)B);
+    const bool dev = is_device_ptr(tokens);
+    std::vector<int32_t> host;
+    const int32_t* src = tokens;
+    if (dev) {
+        host.resize((size_t)B * T);
+        SN_TRY(cuda_check(cudaMemcpy(host.data(), tokens, host.size() * 4, cudaMemcpyDeviceToHost),
+                          "tokens"));
+        src = host.data();
+    }
+    for (int t = 0; t < T; ++t) {
+        for (int b = 0; b < B; ++b) col[b] = src[(size_t)b * T + t];
+        SN_TRY(sunny_step(m->m.get(), col.data(), B, t == T - 1 ? logits : nullptr, nullptr));
+    }
+    return SN_OK;
+}
+
+sn_status sn_abi_sunny_get_state(SnAbiSunny* m, int32_t B, float* s, float* hist) {
+    return m ? sunny_state_io(m->m.get(), B, s, hist, true) : SN_E_INVAL;
+}
+
+sn_status sn_abi_sunny_set_state(SnAbiSunny* m, int32_t B, const float* s, const float* hist) {
+    return m ? sunny_state_io(m->m.get(), B, (float*)s, (float*)hist, false) : SN_E_INVAL;
+}
+
+// ---------------------------------------------- reference sunnynet.h symbol set
+SnModel* sn_load(const char* path, int vocab, int dim, int inner, int rank, int taps, int layers,
+                 int group, int tied) {
+    const int want[8] = {vocab, dim, inner, rank, taps, layers, group, tied};
+    SnAbiSunny* h = open_sunny(path, 1, false, want);
+    if (!h) return nullptr;
+    SnModel* m = new SnModel{std::move(h->m)};
+    delete h;
+    return m;
+}
+
+SnModel* sn_load_h(const char* path, int vocab, int dim, int inner, int rank, int taps,
+                   int layers, int group, int tied) {
+    const int want[8] = {vocab, dim, inner, rank, taps, layers, group, tied};
+    SnAbiSunny* h = open_sunny(path, 1, true, want);
+    if (!h) return nullptr;
+    SnModel* m = new SnModel{std::move(h->m)};
+    delete h;
+    return m;
+}
+
+void sn_free(SnModel* m) {
+    if (!m) return;
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaDeviceSynchronize();
+    delete m;
+}
+
+void sn_reset(SnModel* m) {
+    if (m) sunny_reset(m->m.get());
+}
+
+void sn_step(SnModel* m, int token, float* logits) {
+    if (!m) return;
+    const int32_t t = token;
+    sunny_step(m->m.get(), &t, 1, logits, nullptr);
+}
+
+void sn_prefill(SnModel* m, const int* tokens, int n, float* logits) {
+    if (!m || !tokens || n <= 0) return;
+    for (int i = 0; i < n; ++i) {
+        const int32_t t = tokens[i];
+        if (sunny_step(m->m.get(), &t, 1, i == n - 1 ? logits : nullptr, nullptr) != SN_OK) return;
+    }
+}
+
+int sn_vocab(const SnModel* m) { return m ? m->m->vocab : 0; }
+
+int sn_ready(const SnModel* m) { return m && m->m->ready ? 1 : 0; }
+
+void sn_dbg_layer(SnModel* m, int token, int layer, float* dbg) {
+    if (!m || !dbg || layer < 0 || layer >= m->m->L) return;
+    SunnyModel* s = m->m.get();
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaStream_t st = stream();
+    const int32_t t = token;
+    cudaMemcpyAsync(s->tok, &t, 4, cudaMemcpyHostToDevice, st);
+    if (enqueue_step(s, 1, false, st, layer) != SN_OK) return;
+    const int D = s->D, I = s->I, R = s->R;
+    // raw, at, v, gate, u, s, zn, yn, sfb, out (sunnynet.c:278-290)
+    struct Part {
+        const float* p;
+        int n;
+    } parts[10] = {{s->raw, D}, {s->at, D}, {s->v, R}, {s->gate, D}, {s->u, D},
+                   {s->s + (size_t)layer * D, D}, {s->z, I}, {s->yn, I}, {s->sfb, D}, {s->x, D}};
+    Arr out;
+    const size_t total = (size_t)(7 * D + R + 2 * I) * 4;
+    if (stage_out(dbg, total, 7, &out) != SN_OK) return;
+    size_t off = 0;
+    for (auto& pt : parts) {
+        cudaMemcpyAsync((char*)out.dev + off, pt.p, (size_t)pt.n * 4, cudaMemcpyDeviceToDevice, st);
+        off += (size_t)pt.n * 4;
+    }
+    copy_back(out);
+    finish(true);
+}
+
+}  // extern "C"

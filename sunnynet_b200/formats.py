@@ -120,6 +120,7 @@ class SunnyWeights:
     no_g: np.ndarray | None = None
     no_c: np.ndarray | None = None
     embed: np.ndarray | None = None
+    head: np.ndarray | None = None   # (vocab, D); None = tied to embed (the reference's only mode)
     eps: float = 0.02 * 0.02 + 1e-5  # CenteredScaleNorm s_min^2 + eps (ops.py:38-47)
     clamp: int = 0
 
@@ -211,7 +212,8 @@ def write_usnn(path, w: SunnyWeights) -> int:
         put(ly["delta"])
         parts.append(struct.pack("<2f", ly["a_tanh"], ly["b_gain"]))
     parts.append(struct.pack("<2f", w.eps, 1.0 / S.h_max))
-    put(w.no_g); put(w.no_c); put(w.embed); put(w.embed.T)
+    put(w.no_g); put(w.no_c); put(w.embed)
+    put((w.embed if w.head is None else w.head).T)
     buf = b"".join(parts)
     Path(path).write_bytes(buf)
     return len(buf)
@@ -238,7 +240,7 @@ def write_usnq(path, w: SunnyWeights) -> int:
         parts.append(struct.pack("<2f", ly["a_tanh"], ly["b_gain"]))
     parts.append(struct.pack("<2f", w.eps, 1.0 / S.h_max))
     put(w.no_g); put(w.no_c); put(w.embed)
-    putq(w.embed)
+    putq(w.embed if w.head is None else w.head)
     buf = b"".join(parts)
     Path(path).write_bytes(buf)
     return len(buf)

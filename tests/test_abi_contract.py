@@ -1,0 +1,110 @@
+"""C-ABI contract checks that need no GPU: the library loads, exports every
+symbol include/*.h declares, and keeps the reference's version/caps/check/
+string/thread semantics (reference tests/test_abi.py:28-48, 86-95)."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+from sunnynet_b200 import _lib
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not _lib.LIB_PATH.exists():
+        from sunnynet_b200 import build
+        build.build()
+    return _lib.load()
+
+
+def _declared_functions():
+    names = set()
+    for h in (REPO / "include").glob("*.h"):
+        txt = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        txt = re.sub(r"#.*", "", txt)
+        for m in re.finditer(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(", txt):
+            n = m.group(1)
+            if n.startswith("sn_"):
+                names.add(n)
+    return names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    declared = _declared_functions()
+    assert len(declared) > 60
+    missing = [n for n in sorted(declared) if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(declared) <= set(_lib.SIGNATURES), set(declared) - set(_lib.SIGNATURES)
+
+
+def test_version_and_strings(lib):
+    assert lib.sn_abi_version() == 0x010100
+    n = lib.sn_abi_version_string(None, 0)
+    buf = ctypes.create_string_buffer(n)
+    assert lib.sn_abi_version_string(buf, n) == n == 6
+    assert buf.value == b"1.1.0"
+    n = lib.sn_abi_backend_string(None, 0)
+    buf = ctypes.create_string_buffer(n)
+    lib.sn_abi_backend_string(buf, n)
+    assert buf.value == b"cuda"
+    # too-small buffer: returns the needed length, copies nothing
+    small = ctypes.create_string_buffer(b"xx", 2)
+    assert lib.sn_abi_backend_string(small, 2) == 5 and small.raw == b"xx"
+
+
+def test_caps_superset_of_reference(lib):
+    caps = lib.sn_abi_caps()
+    for bit in range(5):  # RECUR_SCAN, RECUR_STEP, QUANT_I8, RWKV7, THREADS
+        assert caps & (1 << bit)
+    assert caps & (1 << 5)  # CUDA
+
+
+def test_major_version_check(lib):
+    assert lib.sn_abi_check(1) == 0
+    assert lib.sn_abi_check(2) == -5
+    assert lib.sn_abi_check(0) == -5
+
+
+def test_threads_contract(lib):
+    assert lib.sn_abi_set_threads(0) == -1
+    assert lib.sn_abi_set_threads(-3) == -1
+    assert lib.sn_abi_set_threads(6) == 0
+    assert lib.sn_abi_get_threads() == 6
+    assert lib.sn_recommended_threads() >= 1
+
+
+def test_null_and_negative_dims_are_einval_without_device(lib):
+    a = np.zeros((2, 8), np.float32)
+    pa = _lib.ptr(a)
+    assert lib.sn_abi_recur_step(None, pa, pa, 2, 8, 0) == -1
+    assert lib.sn_abi_recur_step(pa, pa, pa, 2, -8, 0) == -1
+    assert lib.sn_abi_recur_scan(pa, pa, pa, pa, pa, 2, -1, 8, 0) == -1
+    assert lib.sn_abi_quant_i8(None, pa, pa, 2, 8, 0) == -1
+    assert lib.sn_abi_dequant_i8(pa, pa, None, 2, 8, 0) == -1
+    assert lib.sn_abi_rwkv7_step(None, 0, pa) == -1
+    assert lib.sn_abi_rwkv7_prefill(None, pa, 1, pa) == -1
+    assert lib.sn_abi_rwkv7_reset(None) == -1
+    assert lib.sn_abi_rwkv7_vocab(None) == 0
+    assert lib.sn_abi_rwkv7_load(None) is None
+    assert lib.sn_abi_sunny_load(None, 1) is None
+    assert lib.sn_abi_sunny_step(None, pa, 1, pa) == -1
+    lib.sn_abi_rwkv7_free(None)
+    lib.sn_abi_sunny_free(None)
+
+
+def test_loaders_reject_bad_files_on_host(lib, tmp_path):
+    """Header validation happens before any device work (sunnynet.c:363-368,
+    rwkv7.c:419-422): missing file, wrong magic, truncated header."""
+    assert lib.sn_abi_rwkv7_load(str(tmp_path / "nope.bin").encode()) is None
+    bad = tmp_path / "bad.bin"
+    bad.write_bytes(b"\x00" * 64)
+    assert lib.sn_abi_rwkv7_load(str(bad).encode()) is None
+    assert lib.sn_abi_sunny_load(str(bad).encode(), 1) is None
+    assert lib.sn_load(str(bad).encode(), 16, 8, 8, 8, 4, 1, 8, 1) is None
+    short = tmp_path / "short.bin"
+    short.write_bytes(b"USNN")
+    assert lib.sn_abi_sunny_load(str(short).encode(), 1) is None

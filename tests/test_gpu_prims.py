@@ -1,0 +1,191 @@
+"""Parity of the CUDA primitives against the oracle, through the C ABI.
+
+Scan, step, INT8 and INT4 quantisation and the W4A8 GEMV are integer/bit
+work or fixed-order float work: they must be BIT-EXACT. Covers host-pointer
+calls (the reference's calling convention) and device-pointer calls, ragged
+sizes (N % 8 != 0, N % 4 != 0, T % 64 != 0), B > 1, zero blocks, and the
+BASELINE config-1 shape.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def rt():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from sunnynet_b200 import runtime
+    runtime.load_runtime()
+    return runtime
+
+
+def _scan_inputs(B, T, N, seed):
+    rng = np.random.default_rng(seed)
+    H = np.exp(np.linspace(np.log(2.0), np.log(8192.0), N))
+    a = rng.uniform(1.0 - 1.0 / H, 1.0, (B, T, N)).astype(np.float32)
+    u = rng.standard_normal((B, T, N)).astype(np.float32)
+    s0 = rng.standard_normal((B, N)).astype(np.float32)
+    return a, u, s0
+
+
+SCAN_SHAPES = [(1, 4096, 1024), (2, 130, 13), (3, 64, 40), (1, 777, 8), (4, 1, 96),
+               (1, 300, 77), (2, 1000, 36), (1, 65, 1)]
+
+
+@pytest.mark.parametrize("B,T,N", SCAN_SHAPES)
+@pytest.mark.parametrize("gated", [0, 1])
+def test_scan_bit_exact_host_pointers(rt, B, T, N, gated):
+    a, u, s0 = _scan_inputs(B, T, N, B * 7 + N)
+    out, send = rt.scan(a, u, s0, gated=bool(gated))
+    ro, rs = oracle.recur_scan(a, u, s0, gated)
+    assert np.array_equal(out, ro)
+    assert np.array_equal(send, rs)
+
+
+@pytest.mark.parametrize("B,T,N", [(1, 4096, 1024), (2, 130, 13), (8, 256, 512)])
+def test_scan_bit_exact_device_pointers(rt, B, T, N):
+    a, u, s0 = _scan_inputs(B, T, N, 3)
+    da, du, ds = (torch.from_numpy(x).cuda() for x in (a, u, s0))
+    out, send = rt.scan(da, du, ds, gated=True)
+    ro, rs = oracle.recur_scan(a, u, s0, 1)
+    assert np.array_equal(out.cpu().numpy(), ro)
+    assert np.array_equal(send.cpu().numpy(), rs)
+
+
+def test_scan_matches_golden(rt, golden):
+    g = golden("prims.npz")
+    for tag in ("a", "b", "c"):
+        a, u, s0 = g[f"scan_{tag}_a"], g[f"scan_{tag}_u"], g[f"scan_{tag}_s0"]
+        for gated in (0, 1):
+            out, send = rt.scan(a, u, s0, gated=bool(gated))
+            assert np.array_equal(out, g[f"scan_{tag}_g{gated}_out"])
+            assert np.array_equal(send, g[f"scan_{tag}_g{gated}_send"])
+
+
+@pytest.mark.parametrize("B,N", [(3, 16), (2, 13), (5, 1027), (1, 8)])
+@pytest.mark.parametrize("gated", [0, 1])
+def test_step_bit_exact_and_equals_scan(rt, B, N, gated):
+    rng = np.random.default_rng(N)
+    a = rng.uniform(0.1, 0.9, (B, N)).astype(np.float32)
+    b = rng.standard_normal((B, N)).astype(np.float32)
+    s0 = rng.standard_normal((B, N)).astype(np.float32)
+    s = s0.copy()
+    rt.step(a, b, s, gated=bool(gated))
+    assert np.array_equal(s, oracle.recur_step(a, b, s0, gated))
+    # stepwise == scan (reference test_runtime_step_equals_scan, tests/test_architecture.py:899)
+    T = 9
+    A = rng.uniform(0.3, 0.9, (B, T, N)).astype(np.float32)
+    U = rng.standard_normal((B, T, N)).astype(np.float32)
+    out, _ = rt.scan(A, U, s0, gated=bool(gated))
+    s = s0.copy()
+    for t in range(T):
+        rt.step(np.ascontiguousarray(A[:, t]), np.ascontiguousarray(U[:, t]), s, gated=bool(gated))
+        assert np.array_equal(s, out[:, t])
+
+
+@pytest.mark.parametrize("block", [16, 0, 64, 7])
+def test_quant_i8_bit_exact(rt, block):
+    rng = np.random.default_rng(block + 5)
+    x = (rng.standard_normal((6, 201)) * 3).astype(np.float32)
+    x[2, :40] = 0.0
+    q, sc = rt.quant_i8(x, block)
+    rq, rsc = oracle.quant_i8(x, block)
+    assert np.array_equal(q, rq) and np.array_equal(sc, rsc)
+    assert np.array_equal(rt.dequant_i8(q, sc, block), oracle.dequant_i8(rq, rsc, block))
+
+
+def test_quant_i8_golden(rt, golden):
+    g = golden("prims.npz")
+    for blk in (16, 0):
+        q, sc = rt.quant_i8(g["q8_x"], blk)
+        assert np.array_equal(q, g[f"q8_b{blk}_q"]) and np.array_equal(sc, g[f"q8_b{blk}_sc"])
+        assert np.array_equal(rt.dequant_i8(q, sc, blk), g[f"q8_b{blk}_xd"])
+
+
+@pytest.mark.parametrize("block,fp16", [(64, False), (128, False), (128, True), (32, True)])
+def test_quant_i4_bit_exact(rt, block, fp16):
+    rng = np.random.default_rng(block)
+    W = (rng.standard_normal((97, 768)) * 0.05).astype(np.float32)
+    W[5, :block] = 0.0
+    q, sc = rt.quant_i4(W, block, fp16_scale=fp16)
+    rq, rsc = oracle.quant_i4(W, block, fp16=fp16)
+    assert np.array_equal(q, rq)
+    assert np.array_equal(np.asarray(sc).view(np.uint8), rsc.view(np.uint8))
+    assert np.array_equal(rt.dequant_i4(q, sc, 768, block), oracle.dequant_i4(rq, rsc, 768, block))
+
+
+@pytest.mark.parametrize("out,n,block,fp16", [
+    (48, 256, 64, False), (768, 768, 64, False), (768, 768, 128, True),
+    (3072, 768, 128, True), (768, 3072, 128, True), (65536, 768, 128, True),
+    (100, 96, 32, False), (37, 192, 96, False), (64, 120, 24, False)])
+def test_w4a8_gemv_bit_exact(rt, out, n, block, fp16):
+    rng = np.random.default_rng(out + n)
+    W = (rng.standard_normal((out, n)) * 0.04).astype(np.float32)
+    x = rng.standard_normal(n).astype(np.float32)
+    x[:block] = 0.0  # a zero activation block (scale 1, codes 0)
+    q, sc = oracle.quant_i4(W, block, fp16=fp16)
+    y = rt.gemv_i4(x, q, sc, block)
+    assert np.array_equal(y, oracle.gemv_i4(x, q, sc, block))
+
+
+def test_w4a8_golden(rt, golden):
+    g = golden("prims.npz")
+    for blk in (64, 128):
+        y = rt.gemv_i4(g["q4_x"], g[f"q4_b{blk}_q"], g[f"q4_b{blk}_sc"], blk)
+        assert np.array_equal(y, g[f"q4_b{blk}_y"])
+
+
+@pytest.mark.parametrize("B", [1, 3, 8, 19])
+def test_w4a8_batched_bit_exact(rt, B):
+    rng = np.random.default_rng(B)
+    out, n, block = 300, 768, 128
+    W = (rng.standard_normal((out, n)) * 0.04).astype(np.float32)
+    X = rng.standard_normal((B, n)).astype(np.float32)
+    q, sc = oracle.quant_i4(W, block, fp16=True)
+    Y = rt.gemm_i4(X, q, sc, block)
+    for i in range(B):
+        assert np.array_equal(Y[i], oracle.gemv_i4(np.ascontiguousarray(X[i]), q, sc, block))
+
+
+def test_w4a8_device_pointers(rt):
+    rng = np.random.default_rng(11)
+    W = (rng.standard_normal((4096, 768)) * 0.04).astype(np.float32)
+    x = rng.standard_normal(768).astype(np.float32)
+    q, sc = oracle.quant_i4(W, 128, fp16=True)
+    y = rt.gemv_i4(torch.from_numpy(x).cuda(), torch.from_numpy(q).cuda(),
+                   torch.from_numpy(sc).cuda(), 128)
+    assert np.array_equal(y.cpu().numpy(), oracle.gemv_i4(x, q, sc, 128))
+
+
+def test_gemv_f32_tolerance(rt):
+    rng = np.random.default_rng(4)
+    W = rng.standard_normal((333, 515)).astype(np.float32)
+    x = rng.standard_normal(515).astype(np.float32)
+    y = rt.gemv_f32(x, W)
+    assert rel_err(y, (W.astype(np.float64) @ x)) < 1e-5
+
+
+def test_invalid_args_return_einval(rt):
+    """reference tests/test_abi.py:86-95"""
+    from sunnynet_b200 import _lib
+    lib = _lib.load()
+    a = np.zeros((2, 8), np.float32)
+    pa = _lib.ptr(a)
+    assert lib.sn_abi_recur_step(None, pa, pa, 2, 8, 0) == -1
+    assert lib.sn_abi_recur_step(pa, pa, pa, 2, -8, 0) == -1
+    assert lib.sn_abi_recur_scan(pa, pa, pa, pa, pa, 1, 0, 8, 0) == -1
+    w = np.zeros((4, 48), np.uint8)
+    s = np.ones((4, 1), np.float32)
+    y = np.zeros(4, np.float32)
+    x = np.zeros(96, np.float32)
+    # in % block != 0: the reference silently reinterprets bytes; here it is an error
+    assert lib.sn_abi_gemv_i4(_lib.ptr(y), _lib.ptr(x), _lib.ptr(w), _lib.ptr(s), 96, 4, 64, 0) == -1
