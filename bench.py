@@ -495,7 +495,114 @@ def wl_c3(args, torch, dist, ours):
     return res, base
 
 
-WORKLOADS = {"c1": wl_c1, "c2": wl_c2, "c2b1": wl_c2b1, "c3": wl_c3}
+def wl_c5(args, torch, dist, ours):
+    """Chunked prefill, BASELINE config 5 shape (L24 d1536 i2688 r960 V32000
+    fp32). One step = one 256-token chunk for each of 8 sequences per GPU,
+    continuing the same sequences (only the recurrent state is carried)."""
+    from sunnynet_b200 import formats
+    S = formats.SUNNY_PRESETS["c5"]
+    B, Tc = 8, 256
+    D, I, R, L = S.dim, S.inner, S.rank, S.layers
+    mats = D * R + R * 2 * D + D * I + I * D + D * D
+    flops = 2 * B * Tc * L * mats
+    res = {"metric": "prefill tokens/s", "unit": "tokens/s", "higher_is_better": True,
+           "dtype": "f32 (bf16x3 tensor-core split, fp32 accumulate)",
+           "config": {"workload": f"c5 chunked prefill L{L} d{D} i{I} r{R} V{S.vocab} fp32",
+                      "batch_per_gpu": B, "global_batch": B * dist.world, "chunk": Tc,
+                      "step": "one 256-token chunk of every sequence",
+                      "weights": "scaled-Gaussian random init (orthogonal QR at d2688 is "
+                                 "minutes of CPU; same scale)",
+                      "l2": "working set > L2"}}
+    td = tempfile.mkdtemp(prefix="snbench5_")
+    path = Path(td) / "m.usnn"
+    formats.write_usnn(path, formats.random_sunny(S, seed=0, fast=True))
+    if not ours:
+        return res, ref_prefill(path, S)
+    from sunnynet_b200 import _lib
+    from sunnynet_b200._lib import check
+    from sunnynet_b200.model import SunnyBatch
+    lib = _lib.load()
+    check(lib.sn_abi_cuda_set_stream(torch.cuda.current_stream().cuda_stream))
+    m = SunnyBatch(path, B)
+    check(lib.sn_abi_cuda_set_async(1))
+    g = torch.Generator(device="cuda").manual_seed(dist.rank)
+    toks = torch.randint(0, S.vocab, (B, Tc), generator=g, device="cuda", dtype=torch.int32)
+
+    def step():
+        m.prefill(toks, chunk=Tc, want_logits=False)
+
+    with ClockSampler(dist.local) as clk:
+        ms = timed_steps(torch, dist, step, args.steps, args.warmup)
+    check(lib.sn_abi_cuda_profile(1))
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    check(lib.sn_abi_cuda_profile(0))
+    fams = _lib.profile_report()
+    check(lib.sn_abi_cuda_set_async(0))
+    peaks = measured_peaks()
+    gemm_fams = {k: v for k, v in fams.items() if k.startswith("gemm_")}
+    dom = max(gemm_fams, key=lambda k: gemm_fams[k][1])
+    n_l, t_ms = fams[dom]
+    shapes = {"gemm_V": (R, D), "gemm_U": (2 * D, R), "gemm_Ws": (D, D), "gemm_Wz": (I, D),
+              "gemm_Wc": (D, I)}
+    n, k = shapes[dom]
+    ff = 2 * B * Tc * n * k
+    ach = ff / (t_ms / n_l * 1e-3) / 1e12
+    rl = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops_sustained"],
+          "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops_sustained"],
+          "peak_src": peaks["src"] + " (sustained bf16)", "kernel": dom, "launches": n_l,
+          "avg_launch_us": t_ms / n_l * 1e3, "alg_flops_per_launch": ff,
+          "note": "achieved counts the fp32 product once; the bf16x3 split issues 3 MMAs",
+          "traffic": profile_traffic(f"{dom}/c5"),
+          "step_tflops": flops / (ms * 1e-3) / 1e12,
+          "families_ms_per_step": {k: v[1] / 2 for k, v in fams.items()}}
+    # end to end: host token ids in (pinned), host logits of the last position out
+    ht = toks.cpu().pin_memory()
+    hl = torch.empty(B, S.vocab).pin_memory()
+    m.prefill(ht, chunk=Tc, logits=hl)
+    reps = 5
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        m.prefill(ht, chunk=Tc, logits=hl)
+    e2e_s = dist.max(torch, (time.perf_counter() - t0) / reps)
+    launches = 1 + L * 15 + 2
+    res.update({"ms_per_step": ms, "value": B * Tc * dist.world / (ms * 1e-3),
+                "e2e": {"value": B * Tc * dist.world / e2e_s, "unit": "tokens/s",
+                        "h2d_bytes_per_step": B * Tc * 4, "d2h_bytes_per_step": B * S.vocab * 4,
+                        "call": "sn_abi_sunny_prefill_chunked (host ids, host logits)"},
+                "gpu_launches": launches * args.steps, "roofline": rl, "clocks": clk.summary()})
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = ref_prefill(path, S)
+    m.close()
+    return res, None
+
+
+def ref_prefill(path, S, budget_s=15.0):
+    """Reference C runtime prefill (sn_prefill = token-by-token sn_step,
+    sunnynet.c:347-349) on one sequence, all physical cores."""
+    import oracle
+    if not oracle.ref_available():
+        raise RuntimeError("oracle/_ref is not built; the CPU baseline needs the reference runtime")
+    L = oracle.ref_model()
+    cores = max(1, int(L.sn_recommended_threads()))
+    L.sn_set_threads(cores)
+    h = L.sn_load(str(path).encode(), S.vocab, S.dim, S.inner, S.rank, S.taps, S.layers, S.group, 1)
+    buf = np.empty(S.vocab, np.float32)
+    rng = np.random.default_rng(0)
+    n, t0 = 0, time.perf_counter()
+    toks = rng.integers(0, S.vocab, 4096).astype(np.int32)
+    while time.perf_counter() - t0 < budget_s and n < len(toks):
+        L.sn_step(h, int(toks[n]), oracle.ptr(buf))
+        n += 1
+    dt = time.perf_counter() - t0
+    L.sn_free(h)
+    return {"value": n / dt, "unit": "tokens/s", "cores": cores, "kind": "reference",
+            "sample": f"{n} prompt tokens through sn_step (the reference prefill loop), "
+                      f"{cores} OpenMP threads"}
+
+
+WORKLOADS = {"c1": wl_c1, "c2": wl_c2, "c2b1": wl_c2b1, "c3": wl_c3, "c5": wl_c5}
 SCALING = {"c3": "strong"}
 
 

@@ -129,9 +129,13 @@ sn_status   sn_abi_sunny_step(SnAbiSunny* m, const int32_t* tokens, int32_t B, f
 /* greedy: next[B] = argmax of the step's logits (ties -> lowest id) */
 sn_status   sn_abi_sunny_step_argmax(SnAbiSunny* m, const int32_t* tokens, int32_t B,
                                      int32_t* next);
-/* feed tokens (B,T) row-major; logits of the last position -> logits[B][vocab] */
+/* feed tokens (B,T) row-major; logits of the last position -> logits[B][vocab]
+ * (NULL skips the head). Runs as 256-token chunks: the contractions over all
+ * B*chunk rows at once, the recurrence as a scan carrying only the state. */
 sn_status   sn_abi_sunny_prefill(SnAbiSunny* m, const int32_t* tokens, int32_t B, int32_t T,
                                  float* logits);
+sn_status   sn_abi_sunny_prefill_chunked(SnAbiSunny* m, const int32_t* tokens, int32_t B,
+                                         int32_t T, int32_t chunk, float* logits);
 /* state of sequences [0,B): s (B,L,D), hist (B,L,K-1,D), hist[.,.,0] newest */
 sn_status   sn_abi_sunny_get_state(SnAbiSunny* m, int32_t B, float* s, float* hist);
 sn_status   sn_abi_sunny_set_state(SnAbiSunny* m, int32_t B, const float* s, const float* hist);

@@ -54,6 +54,7 @@ SIGNATURES = {
     "sn_abi_sunny_step": (I32, [V, V, I32, V]),
     "sn_abi_sunny_step_argmax": (I32, [V, V, I32, V]),
     "sn_abi_sunny_prefill": (I32, [V, V, I32, I32, V]),
+    "sn_abi_sunny_prefill_chunked": (I32, [V, V, I32, I32, I32, V]),
     "sn_abi_sunny_get_state": (I32, [V, I32, V, V]),
     "sn_abi_sunny_set_state": (I32, [V, I32, V, V]),
     "sn_abi_rwkv7_load_batch": (V, [P, I32]),

@@ -1,6 +1,7 @@
 // SIMT implementations of the contractions declared in gemm.cuh.
 #include "gemm.cuh"
 #include "runtime.cuh"
+#include "tc_gemm.cuh"
 
 namespace sn {
 namespace {
@@ -13,27 +14,11 @@ __device__ __forceinline__ float wload(const void* W, long long i) {
 }
 
 __device__ __forceinline__ float a_eff(const GemmArgs& a, int m, int k, float v) {
-    if (a.mu) v = __fmul_rn(__fmul_rn(v - a.mu[m], a.rs[m]), a.g[k]) + a.c[k];
-    return v;
+    return gemm_a_eff(a, m, k, v);
 }
 
 __device__ __forceinline__ float epilogue(const GemmArgs& a, int m, int n, float acc) {
-    if (a.wscale) acc = acc * a.wscale[n];
-    if (a.epi == kEpiWedge) {
-        acc = acc * (1.0f + 0.5f * a.p / (1.0f + fabsf(acc)));
-    } else if (a.epi == kEpiResid) {
-        acc = acc + (a.p * a.S[m * a.lds + n] + a.F[m * a.ldf + n] + a.X[m * a.ldx + n]);
-    } else if (a.epi == kEpiAdd) {
-        acc = a.C[m * a.ldc + n] + acc;
-    } else if (a.epi == kEpiRelu2) {
-        const float t = acc > 0.0f ? acc : 0.0f;
-        acc = t * t;
-    } else if (a.epi == kEpiTanh) {
-        acc = tanhf(acc);
-    } else if (a.epi == kEpiSigmoid) {
-        acc = 1.0f / (1.0f + expf(-acc));
-    }
-    return acc;
+    return gemm_epilogue(a, m, n, acc);
 }
 
 // ---------------------------------------------------------------- GEMV (M <= 8)
@@ -197,8 +182,9 @@ int launch_wt(const GemmArgs& a, cudaStream_t st) {
 
 }  // namespace
 
-int launch_gemm(const GemmArgs& a, int wtype, cudaStream_t st) {
+int launch_gemm(const GemmArgs& a, int wtype, cudaStream_t st, const TcWeights* tc) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return SN_OK;
+    if (tc && tc_usable(a, tc)) return launch_tc_gemm(a, *tc, st);
     switch (wtype) {
         case kWI8: return launch_wt<kWI8>(a, st);
         case kWF16: return launch_wt<kWF16>(a, st);

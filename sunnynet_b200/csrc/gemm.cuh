@@ -56,6 +56,34 @@ struct GemmArgs {
     long long ldx = 0;
 };
 
-int launch_gemm(const GemmArgs& a, int wtype, cudaStream_t st);
+struct TcWeights;
+
+// Runs on the tensor cores when `tc` is given and the shape suits them
+// (tc_gemm.cu), else on the SIMT kernels.
+int launch_gemm(const GemmArgs& a, int wtype, cudaStream_t st, const TcWeights* tc = nullptr);
+
+// A' element (row-LN prologue when mu is set)
+__device__ __forceinline__ float gemm_a_eff(const GemmArgs& a, int m, int k, float v) {
+    if (a.mu) v = __fmul_rn(__fmul_rn(v - a.mu[m], a.rs[m]), a.g[k]) + a.c[k];
+    return v;
+}
+
+// epilogue of one output element
+__device__ __forceinline__ float gemm_epilogue(const GemmArgs& a, int m, int n, float acc) {
+    if (a.wscale) acc = acc * a.wscale[n];
+    switch (a.epi) {
+        case kEpiWedge: return acc * (1.0f + 0.5f * a.p / (1.0f + fabsf(acc)));
+        case kEpiResid:
+            return acc + (a.p * a.S[m * a.lds + n] + a.F[m * a.ldf + n] + a.X[m * a.ldx + n]);
+        case kEpiAdd: return a.C[m * a.ldc + n] + acc;
+        case kEpiRelu2: {
+            const float t = acc > 0.0f ? acc : 0.0f;
+            return t * t;
+        }
+        case kEpiTanh: return tanhf(acc);
+        case kEpiSigmoid: return 1.0f / (1.0f + expf(-acc));
+        default: return acc;
+    }
+}
 
 }  // namespace sn

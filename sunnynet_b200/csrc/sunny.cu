@@ -33,9 +33,11 @@
 #include <vector>
 
 #include "gemm.cuh"
+#include "kernels.cuh"
 #include "runtime.cuh"
 #include "sn_abi.h"
 #include "sunnynet.h"
+#include "tc_gemm.cuh"
 
 namespace sn {
 namespace {
@@ -220,6 +222,117 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ s, __half* __restric
         d[i] = __float2half_rn(s[i]);
 }
 
+// ---------------------------------------------------------- chunked prefill
+// x[m] = embed[tok[m]] for the M = B*Tc rows of a chunk.
+__global__ void gather_embed_kernel(int D, int vocab, int* __restrict__ err,
+                                    const int32_t* __restrict__ tok,
+                                    const float* __restrict__ embed, float* __restrict__ x) {
+    int t = tok[blockIdx.x];
+    if (t < 0 || t >= vocab) {
+        if (threadIdx.x == 0) atomicExch(err, kErrBadIndex);
+        t = 0;
+    }
+    const float* e = embed + (size_t)t * D;
+    float* xr = x + (size_t)blockIdx.x * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) xr[i] = e[i];
+}
+
+// Y[m] = LN(X[m]) per row
+__global__ void ln_rows_kernel(int n, const float* __restrict__ X, float* __restrict__ Y,
+                               const float* __restrict__ g, const float* __restrict__ c,
+                               float eps) {
+    __shared__ float red[32];
+    const float* xr = X + (size_t)blockIdx.x * n;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += xr[i];
+    const float mean = block_sum(s, red) / (float)n;
+    float v = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float d = xr[i] - mean;
+        v += d * d;
+    }
+    const float rstd = 1.0f / sqrtf(block_sum(v, red) / (float)n + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        Y[(size_t)blockIdx.x * n + i] = (xr[i] - mean) * rstd * g[i] + c[i];
+}
+
+// Causal taps over a chunk: position t of sequence b reads raw rows t-1..t-K+1
+// of the chunk, or the history ring for the ones before the chunk.
+__global__ void conv_chunk_kernel(int B, int Tc, int D, int K, int KH, int L, int layer,
+                                  const float* __restrict__ raw, const float* __restrict__ hist,
+                                  const int32_t* __restrict__ pos, const float* __restrict__ dw,
+                                  float* __restrict__ at) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= (long long)B * Tc * D) return;
+    const int d = (int)(i % D);
+    const long long m = i / D;
+    const int t = (int)(m % Tc), b = (int)(m / Tc);
+    const float r = raw[i];
+    float a = r;
+    if (K > 1) {
+        const int p = pos[b * L + layer];
+        const float* hb = hist + ((size_t)b * L + layer) * KH * D;
+        float acc = r * dw[(size_t)(K - 1) * D + d];
+        for (int k = 0; k < K - 1; ++k) {
+            const int tt = t - 1 - k;
+            const float hv = tt >= 0 ? raw[(m - 1 - k) * D + d]
+                                     : hb[(size_t)(((p + tt) % KH + KH) % KH) * D + d];
+            acc += hv * dw[(size_t)(K - 2 - k) * D + d];
+        }
+        a = r + acc;
+    }
+    at[i] = a;
+}
+
+// After the taps of a chunk: the last K-1 raw rows of each sequence enter the
+// ring and the position advances by Tc. One CTA per sequence.
+__global__ void ring_update_kernel(int Tc, int D, int KH, int L, int layer,
+                                   const float* __restrict__ raw, float* __restrict__ hist,
+                                   int32_t* __restrict__ pos) {
+    const int b = blockIdx.x;
+    const int p = pos[b * L + layer];
+    __syncthreads();
+    float* hb = hist + ((size_t)b * L + layer) * KH * D;
+    const int first = Tc > KH ? Tc - KH : 0;
+    for (int i = threadIdx.x; i < (Tc - first) * D; i += blockDim.x) {
+        const int t = first + i / D, d = i % D;
+        hb[(size_t)(((p + t) % KH + KH) % KH) * D + d] = raw[((size_t)b * Tc + t) * D + d];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) pos[b * L + layer] = p + Tc;
+}
+
+// u = compete(q), p = decay gate (the scan's a), one thread per (row, channel)
+__global__ void gate_chunk_kernel(long long M, int D, int G, const float* __restrict__ q,
+                                  const float* __restrict__ delta, float* __restrict__ u,
+                                  float* __restrict__ pa, int clamp, float p_floor) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= M * D) return;
+    const long long m = i / D;
+    const int d = (int)(i % D);
+    const float* qb = q + m * 2 * D;
+    const int base = (d / G) * G, off = d - base;
+    const float g0 = qb[D + d];
+    const float g1 = qb[D + base + (off + 1) % G];
+    const float g2 = qb[D + base + (off + 2) % G];
+    u[i] = qb[d] * (sigm(g0 - g1) * sigm(g0 - g2));
+    float p = 1.0f - delta[d] * (1.0f - sigm(g0));
+    if (clamp && p < p_floor) p = p_floor;
+    pa[i] = p;
+}
+
+// prev[b][t] = state before position t: s_in for t = 0, else states[b][t-1]
+__global__ void prev_kernel(int Tc, int D, long long total, const float* __restrict__ s0,
+                            const float* __restrict__ st, float* __restrict__ prev) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const int d = (int)(i % D);
+    const long long m = i / D;
+    const int t = (int)(m % Tc);
+    const long long b = m / Tc;
+    prev[i] = t == 0 ? s0[b * D + d] : st[i - D];
+}
+
 // state export / import: ring <-> newest-first history
 __global__ void hist_io_kernel(int B, int L, int KH, int D, float* ring, float* flat,
                                int32_t* pos, int to_flat) {
@@ -243,6 +356,7 @@ struct SunnyLayer {
     void *V, *U, *Wz, *Wc, *Ws;
     float *sV, *sU, *sWz, *sWc, *sWs;  // int8 row scales
     float a_tanh, b_gain;
+    TcWeights tV, tU, tWz, tWc, tWs;   // bf16 planes + TMA maps for the batched path
 };
 
 struct SunnyModel {
@@ -253,6 +367,7 @@ struct SunnyModel {
     float *no_g = nullptr, *no_c = nullptr, *embed = nullptr;
     void* head = nullptr;
     float* shead = nullptr;
+    TcWeights thead;
     std::vector<void*> allocs;
     // state
     float* s = nullptr;
@@ -265,11 +380,20 @@ struct SunnyModel {
     float *gate = nullptr, *sfb = nullptr, *z = nullptr, *mu = nullptr, *rs = nullptr;
     float *logits = nullptr, *yn = nullptr;
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (B, with head) -> graph
+    // chunked prefill: buffers of B*Tc rows, one graph per (B, Tc, head)
+    long long crows = 0;
+    int cseqs = 0;
+    int32_t* ctok = nullptr;
+    float *cx = nullptr, *craw = nullptr, *cat = nullptr, *cv = nullptr, *cq = nullptr;
+    float *cu = nullptr, *cp = nullptr, *cst = nullptr, *cprev = nullptr, *csfb = nullptr;
+    float *cz = nullptr, *cmu = nullptr, *crs = nullptr, *cs0 = nullptr, *csend = nullptr;
+    std::map<std::pair<long long, int>, cudaGraphExec_t> cgraphs;  // (B*65536+Tc, head)
     cudaStream_t cap = nullptr;
     bool ready = false;
 
     ~SunnyModel() {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        for (auto& kv : cgraphs) cudaGraphExecDestroy(kv.second);
         if (cap) cudaStreamDestroy(cap);
         for (void* p : allocs) cudaFree(p);
     }
@@ -451,6 +575,18 @@ int load_model(SunnyModel* m, const char* path, int nseq, bool half, const int* 
     }
     if (up.tmp) cudaFree(up.tmp);
     if (up.rc != SN_OK) return fail(up.rc == SN_E_IO ? SN_E_FORMAT : up.rc, "%s: load failed", path);
+    if (!getenv("SN_DISABLE_TC")) {  // bf16 hi/lo planes for the tensor-core path (B >= 16)
+        auto al = [](size_t n, void* o) -> void* { return ((SunnyModel*)o)->dalloc<uint8_t>(n); };
+        for (int l = 0; l < L; ++l) {
+            SunnyLayer& y = m->ly[l];
+            SN_TRY(tc_prepare(&y.tV, y.V, m->wtype, R, D, al, m));
+            SN_TRY(tc_prepare(&y.tU, y.U, m->wtype, 2 * D, R, al, m));
+            SN_TRY(tc_prepare(&y.tWz, y.Wz, m->wtype, I, D, al, m));
+            SN_TRY(tc_prepare(&y.tWc, y.Wc, m->wtype, D, I, al, m));
+            SN_TRY(tc_prepare(&y.tWs, y.Ws, m->wtype, D, D, al, m));
+        }
+        SN_TRY(tc_prepare(&m->thead, m->head, m->wtype, vocab, D, al, m));
+    }
     m->eps = ep[0];
     m->p_floor = ep[1];
     const size_t n = (size_t)nseq;
@@ -511,15 +647,15 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
         gs.lda = (long long)m->L * D;
         {
             ProfScope ps("gemm_Ws", st);
-            SN_TRY(launch_gemm(gs, m->wtype, st));
+            SN_TRY(launch_gemm(gs, m->wtype, st, &y.tWs));
         }
         {
             ProfScope ps("gemm_V", st);
-            SN_TRY(launch_gemm(gemm(B, R, D, m->at, y.V, y.sV, m->v), m->wtype, st));
+            SN_TRY(launch_gemm(gemm(B, R, D, m->at, y.V, y.sV, m->v), m->wtype, st, &y.tV));
         }
         {
             ProfScope ps("gemm_U", st);
-            SN_TRY(launch_gemm(gemm(B, 2 * D, R, m->v, y.U, y.sU, m->q), m->wtype, st));
+            SN_TRY(launch_gemm(gemm(B, 2 * D, R, m->v, y.U, y.sU, m->q), m->wtype, st, &y.tU));
         }
         {
             ProfScope ps("gate_state", st);
@@ -532,7 +668,7 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
         gz.p = y.a_tanh;
         {
             ProfScope ps("gemm_Wz", st);
-            SN_TRY(launch_gemm(gz, m->wtype, st));
+            SN_TRY(launch_gemm(gz, m->wtype, st, &y.tWz));
         }
         {
             ProfScope ps("rowstats", st);
@@ -550,7 +686,7 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
         gc.X = m->x; gc.ldx = D;
         {
             ProfScope ps("gemm_Wc", st);
-            SN_TRY(launch_gemm(gc, m->wtype, st));
+            SN_TRY(launch_gemm(gc, m->wtype, st, &y.tWc));
         }
     }
     if (dbg) return cuda_check(cudaGetLastError(), "dbg step");
@@ -562,7 +698,7 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
         GemmArgs gh = gemm(B, m->vocab, D, m->x, m->head, m->shead, m->logits);
         gh.mu = m->mu; gh.rs = m->rs; gh.g = m->no_g; gh.c = m->no_c;
         ProfScope ps("gemm_head", st);
-        SN_TRY(launch_gemm(gh, m->wtype, st));
+        SN_TRY(launch_gemm(gh, m->wtype, st, &m->thead));
     }
     return cuda_check(cudaGetLastError(), "step launch");
 }
@@ -591,6 +727,179 @@ int run_step(SunnyModel* m, int B, bool with_head) {
         it = m->graphs.emplace(key, ex).first;
     }
     return cuda_check(cudaGraphLaunch(it->second, st), "graph launch");
+}
+
+// ------------------------------------------------------------ chunked prefill
+int ensure_chunk_bufs(SunnyModel* m, int B, int Tc) {
+    const long long rows = (long long)B * Tc;
+    if (rows <= m->crows && B <= m->cseqs) return SN_OK;
+    const size_t D = m->D, I = m->I, R = m->R, n = (size_t)rows;
+    m->ctok = m->dalloc<int32_t>(n);
+    m->cx = m->dalloc<float>(n * D);
+    m->craw = m->dalloc<float>(n * D);
+    m->cat = m->dalloc<float>(n * D);
+    m->cv = m->dalloc<float>(n * R);
+    m->cq = m->dalloc<float>(n * 2 * D);
+    m->cu = m->dalloc<float>(n * D);
+    m->cp = m->dalloc<float>(n * D);
+    m->cst = m->dalloc<float>(n * D);
+    m->cprev = m->dalloc<float>(n * D);
+    m->csfb = m->dalloc<float>(n * D);
+    m->cz = m->dalloc<float>(n * I);
+    m->cmu = m->dalloc<float>(n);
+    m->crs = m->dalloc<float>(n);
+    m->cs0 = m->dalloc<float>((size_t)B * D);
+    m->csend = m->dalloc<float>((size_t)B * D);
+    if (!m->csend || !m->cs0 || !m->crs || !m->cz)
+        return fail(SN_E_NOMEM, "prefill buffers for %lld rows", rows);
+    m->crows = rows;
+    m->cseqs = B;
+    for (auto& kv : m->cgraphs) cudaGraphExecDestroy(kv.second);  // captured old pointers
+    m->cgraphs.clear();
+    return SN_OK;
+}
+
+// One chunk of Tc tokens for sequences [0,B) (ids already in m->ctok, row b*Tc+t):
+// every contraction runs over M = B*Tc rows, the recurrence as the scan.
+int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
+    const int D = m->D, I = m->I, R = m->R, L = m->L;
+    const long long M = (long long)B * Tc;
+    const unsigned eb = (unsigned)((M * D + 255) / 256);
+    {
+        ProfScope ps("prefill_rows", st);
+        gather_embed_kernel<<<(unsigned)M, 256, 0, st>>>(D, m->vocab, rt().d_err, m->ctok,
+                                                         m->embed, m->cx);
+    }
+    for (int l = 0; l < L; ++l) {
+        const SunnyLayer& y = m->ly[l];
+        {
+            ProfScope ps("prefill_rows", st);
+            ln_rows_kernel<<<(unsigned)M, 256, 0, st>>>(D, m->cx, m->craw, y.ni_g, y.ni_c, m->eps);
+            conv_chunk_kernel<<<eb, 256, 0, st>>>(B, Tc, D, m->K, m->KH, L, l, m->craw, m->hist,
+                                                 m->pos, y.dw, m->cat);
+            if (m->K > 1)
+                ring_update_kernel<<<B, 256, 0, st>>>(Tc, D, m->KH, L, l, m->craw, m->hist,
+                                                      m->pos);
+        }
+        {
+            ProfScope ps("gemm_V", st);
+            SN_TRY(launch_gemm(gemm((int)M, R, D, m->cat, y.V, y.sV, m->cv), m->wtype, st, &y.tV));
+        }
+        {
+            ProfScope ps("gemm_U", st);
+            SN_TRY(launch_gemm(gemm((int)M, 2 * D, R, m->cv, y.U, y.sU, m->cq), m->wtype, st,
+                               &y.tU));
+        }
+        {
+            ProfScope ps("prefill_scan", st);
+            gate_chunk_kernel<<<eb, 256, 0, st>>>(M, D, m->G, m->cq, y.delta, m->cu, m->cp,
+                                                  m->clamp, m->p_floor);
+            SN_TRY(cuda_check(cudaMemcpy2DAsync(m->cs0, (size_t)D * 4, m->s + (size_t)l * D,
+                                                (size_t)L * D * 4, (size_t)D * 4, B,
+                                                cudaMemcpyDeviceToDevice, st),
+                              "s0"));
+            SN_TRY(launch_scan(m->cp, m->cu, m->cs0, m->cst, m->csend, B, Tc, D, 1, st));
+            SN_TRY(cuda_check(cudaMemcpy2DAsync(m->s + (size_t)l * D, (size_t)L * D * 4, m->csend,
+                                                (size_t)D * 4, (size_t)D * 4, B,
+                                                cudaMemcpyDeviceToDevice, st),
+                              "send"));
+            prev_kernel<<<eb, 256, 0, st>>>(Tc, D, M * D, m->cs0, m->cst, m->cprev);
+        }
+        {
+            ProfScope ps("gemm_Ws", st);
+            SN_TRY(launch_gemm(gemm((int)M, D, D, m->cprev, y.Ws, y.sWs, m->csfb), m->wtype, st,
+                               &y.tWs));
+        }
+        GemmArgs gz = gemm((int)M, I, D, m->cu, y.Wz, y.sWz, m->cz);
+        gz.epi = kEpiWedge;
+        gz.p = y.a_tanh;
+        {
+            ProfScope ps("gemm_Wz", st);
+            SN_TRY(launch_gemm(gz, m->wtype, st, &y.tWz));
+        }
+        {
+            ProfScope ps("rowstats", st);
+            rowstats_kernel<<<(unsigned)M, 256, 0, st>>>(I, m->cz, I, m->cmu, m->crs, m->eps);
+        }
+        GemmArgs gc = gemm((int)M, D, I, m->cz, y.Wc, y.sWc, m->cx);
+        gc.mu = m->cmu; gc.rs = m->crs; gc.g = y.nm_g; gc.c = y.nm_c;
+        gc.epi = kEpiResid;
+        gc.p = y.b_gain;
+        gc.S = m->cst; gc.lds = D;
+        gc.F = m->csfb; gc.ldf = D;
+        gc.X = m->cx; gc.ldx = D;
+        {
+            ProfScope ps("gemm_Wc", st);
+            SN_TRY(launch_gemm(gc, m->wtype, st, &y.tWc));
+        }
+    }
+    if (head) {  // logits of each sequence's last position only
+        const float* last = m->cx + (size_t)(Tc - 1) * D;
+        rowstats_kernel<<<B, 256, 0, st>>>(D, last, (long long)Tc * D, m->cmu, m->crs, m->eps);
+        GemmArgs gh = gemm(B, m->vocab, D, last, m->head, m->shead, m->logits);
+        gh.lda = (long long)Tc * D;
+        gh.mu = m->cmu; gh.rs = m->crs; gh.g = m->no_g; gh.c = m->no_c;
+        ProfScope ps("gemm_head", st);
+        SN_TRY(launch_gemm(gh, m->wtype, st, &m->thead));
+    }
+    return cuda_check(cudaGetLastError(), "prefill chunk launch");
+}
+
+int run_chunk(SunnyModel* m, int B, int Tc, bool head) {
+    cudaStream_t st = stream();
+    if (prof_on()) return enqueue_chunk(m, B, Tc, head, st);
+    auto key = std::make_pair((long long)B * 65536 + Tc, head ? 1 : 0);
+    auto it = m->cgraphs.find(key);
+    if (it == m->cgraphs.end()) {
+        cudaGraph_t g = nullptr;
+        SN_TRY(cuda_check(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeThreadLocal),
+                          "begin capture"));
+        const int rc = enqueue_chunk(m, B, Tc, head, m->cap);
+        const cudaError_t e = cudaStreamEndCapture(m->cap, &g);
+        if (rc != SN_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        SN_TRY(cuda_check(e, "end capture"));
+        cudaGraphExec_t ex = nullptr;
+        const cudaError_t e2 = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        SN_TRY(cuda_check(e2, "graph instantiate"));
+        it = m->cgraphs.emplace(key, ex).first;
+    }
+    return cuda_check(cudaGraphLaunch(it->second, st), "graph launch");
+}
+
+// tokens (B,T) row-major; the carried state is the handle's own
+int sunny_prefill(SunnyModel* m, const int32_t* tokens, int B, int T, int chunk, float* logits) {
+    if (!m || !m->ready || !tokens || B <= 0 || T <= 0 || B > m->nseq || chunk <= 0)
+        return fail(SN_E_INVAL, "sunny_prefill: bad arguments");
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    const int Tc = chunk < T ? chunk : T;
+    SN_TRY(ensure_chunk_bufs(m, B, Tc));
+    cudaStream_t st = stream();
+    const bool tdev = is_device_ptr(tokens);
+    for (int c0 = 0; c0 < T; c0 += Tc) {
+        const int tc = Tc < T - c0 ? Tc : T - c0;
+        const bool last = c0 + tc >= T;
+        SN_TRY(cuda_check(cudaMemcpy2DAsync(m->ctok, (size_t)tc * 4, tokens + c0, (size_t)T * 4,
+                                            (size_t)tc * 4, B,
+                                            tdev ? cudaMemcpyDeviceToDevice
+                                                 : cudaMemcpyHostToDevice,
+                                            st),
+                          "prefill tokens"));
+        SN_TRY(run_chunk(m, B, tc, last && logits != nullptr));
+    }
+    bool host = !tdev;
+    if (logits) {
+        const bool dev = is_device_ptr(logits);
+        host |= !dev;
+        SN_TRY(cuda_check(cudaMemcpyAsync(logits, m->logits, (size_t)B * m->vocab * 4,
+                                          dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                                          st),
+                          "logits"));
+    }
+    return finish(host);
 }
 
 int sunny_step(SunnyModel* m, const int32_t* tokens, int B, float* logits, int32_t* next) {
@@ -731,23 +1040,14 @@ sn_status sn_abi_sunny_step_argmax(SnAbiSunny* m, const int32_t* tokens, int32_t
 
 sn_status sn_abi_sunny_prefill(SnAbiSunny* m, const int32_t* tokens, int32_t B, int32_t T,
                                float* logits) {
-    if (!m || !tokens || B <= 0 || T <= 0 || B > m->m->nseq) return SN_E_INVAL;
-    // token rows are (B,T): feed column t of every sequence, head on the last only
-    std::vector<int32_t> col((size_t)B);
-    const bool dev = is_device_ptr(tokens);
-    std::vector<int32_t> host;
-    const int32_t* src = tokens;
-    if (dev) {
-        host.resize((size_t)B * T);
-        SN_TRY(cuda_check(cudaMemcpy(host.data(), tokens, host.size() * 4, cudaMemcpyDeviceToHost),
-                          "tokens"));
-        src = host.data();
-    }
-    for (int t = 0; t < T; ++t) {
-        for (int b = 0; b < B; ++b) col[b] = src[(size_t)b * T + t];
-        SN_TRY(sunny_step(m->m.get(), col.data(), B, t == T - 1 ? logits : nullptr, nullptr));
-    }
-    return SN_OK;
+    if (!m) return SN_E_INVAL;
+    return sunny_prefill(m->m.get(), tokens, B, T, 256, logits);
+}
+
+sn_status sn_abi_sunny_prefill_chunked(SnAbiSunny* m, const int32_t* tokens, int32_t B, int32_t T,
+                                       int32_t chunk, float* logits) {
+    if (!m) return SN_E_INVAL;
+    return sunny_prefill(m->m.get(), tokens, B, T, chunk, logits);
 }
 
 sn_status sn_abi_sunny_get_state(SnAbiSunny* m, int32_t B, float* s, float* hist) {
@@ -796,12 +1096,11 @@ void sn_step(SnModel* m, int token, float* logits) {
     sunny_step(m->m.get(), &t, 1, logits, nullptr);
 }
 
+// sunnynet.c:347-349 feeds the tokens one by one; the result (state and the
+// last token's logits) is the same when the prompt runs as 256-token chunks.
 void sn_prefill(SnModel* m, const int* tokens, int n, float* logits) {
     if (!m || !tokens || n <= 0) return;
-    for (int i = 0; i < n; ++i) {
-        const int32_t t = tokens[i];
-        if (sunny_step(m->m.get(), &t, 1, i == n - 1 ? logits : nullptr, nullptr) != SN_OK) return;
-    }
+    sunny_prefill(m->m.get(), (const int32_t*)tokens, 1, n, 256, logits);
 }
 
 int sn_vocab(const SnModel* m) { return m ? m->m->vocab : 0; }

@@ -61,13 +61,22 @@ class SunnyBatch:
         check(self._lib.sn_abi_sunny_step_argmax(self._h, ptr(t), B, ptr(out)), "sunny_argmax")
         return out
 
-    def prefill(self, tokens):
-        """tokens (B, T) -> logits of the last position (B, vocab)."""
-        t = np.ascontiguousarray(np.asarray(tokens, np.int32))
+    def prefill(self, tokens, chunk: int = 256, logits=None, want_logits: bool = True):
+        """tokens (B, T) -> logits of the last position (B, vocab). Runs as
+        `chunk`-token chunks carrying only the recurrent state."""
+        if hasattr(tokens, "data_ptr"):
+            import torch
+            t = tokens.to(torch.int32).contiguous()
+        else:
+            t = np.ascontiguousarray(np.asarray(tokens, np.int32))
         B, T = t.shape
-        lg = np.empty((B, self.vocab), np.float32)
-        check(self._lib.sn_abi_sunny_prefill(self._h, ptr(t), B, T, ptr(lg)), "sunny_prefill")
-        return lg
+        if want_logits and logits is None:
+            logits = _out_like(t, (B, self.vocab), np.float32)
+        bind_stream(t, logits)
+        check(self._lib.sn_abi_sunny_prefill_chunked(self._h, ptr(t), B, T, int(chunk),
+                                                     ptr(logits) if want_logits else None),
+              "sunny_prefill")
+        return logits
 
     def reset(self):
         check(self._lib.sn_abi_sunny_reset(self._h), "sunny_reset")

@@ -150,20 +150,81 @@ def test_batched_vs_oracle(tiny, kind, B):
             assert np.linalg.norm(sh[i] - rsh) / np.linalg.norm(rsh) < L2_Q4
 
 
-@pytest.mark.parametrize("B", [1, 8])
-def test_config4_shape_int4_g128_vs_oracle(B):
-    """L12 D768 H12x64 F3072 V65536, INT4 group 128 fp16 scales."""
+@pytest.fixture(scope="module")
+def c4_blobs():
+    """BASELINE config 4 shape: L12 D768 H12x64 F3072 V65536, ranks 64/64/32/128."""
     from sunnynet_b200 import formats
-    from sunnynet_b200.rwkv7 import Rwkv7Batch
     shape = formats.RWKV_PRESETS["c4"]
-    with tempfile.TemporaryDirectory() as td:
-        p = Path(td) / "c4.bin"
-        formats.write_krwk(p, formats.random_rwkv(shape, 0), quant="q4g", group=128)
-        gm, om = Rwkv7Batch(p, B), oracle.Rwkv(p, B)
-        rng = np.random.default_rng(0)
-        for _ in range(3):
-            toks = rng.integers(0, shape.vocab, B).astype(np.int32)
-            check_q4(gm.step(toks), om.step(toks))
+    w = formats.random_rwkv(shape, 0)
+    td = tempfile.mkdtemp()
+    p32, p4 = Path(td) / "c4.f32.bin", Path(td) / "c4.q4g.bin"
+    formats.write_krwk(p32, w, quant="fp32")
+    formats.write_krwk(p4, w, quant="q4g", group=128)
+    return shape, p32, p4
+
+
+@pytest.mark.parametrize("B", [1, 4])
+def test_config4_shape_fp32_vs_oracle(c4_blobs, B):
+    """Every kernel of the full-shape model in fp32. Layer-0 intermediates at
+    1e-4; full-depth logits at 1e-4 relative L2 per row. This random-init
+    12-layer model amplifies rounding differences (a 1e-6 relative input
+    perturbation moves the oracle's own logits by ~3e-5), so the max-norm
+    bound at full depth is 3e-4."""
+    from sunnynet_b200.rwkv7 import Rwkv7Batch
+    from sunnynet_b200.runtime.rwkv7_c import SnRWKV7
+    shape, p32, _ = c4_blobs
+    g1, o1 = SnRWKV7(p32, shape.vocab), oracle.Rwkv(p32, 1)
+    g = np.array(g1.dbg(11, 0, shape.dim), np.float32)
+    r = o1.dbg(11, 0, shape.dim)
+    for j in range(9):
+        seg = slice(j * shape.dim, (j + 1) * shape.dim)
+        assert rel_err(g[seg], r[seg]) < TOL, j
+    gm, om = Rwkv7Batch(p32, B), oracle.Rwkv(p32, B)
+    rng = np.random.default_rng(B)
+    for _ in range(3):
+        toks = rng.integers(0, shape.vocab, B).astype(np.int32)
+        lg, ref = gm.step(toks), om.step(toks)
+        l2 = np.linalg.norm(lg - ref, axis=1) / np.linalg.norm(ref, axis=1)
+        assert l2.max() < TOL, l2
+        check_logits(lg, ref, 3e-4)
+
+
+def test_config4_shape_int4_layer0_vs_oracle(c4_blobs):
+    """INT4 group-128 kernels in context, before activation-code flips can
+    compound: every intermediate of layer 0 (sn_rk_dbg) within 5e-3."""
+    from sunnynet_b200.runtime.rwkv7_c import SnRWKV7
+    shape, _, p4 = c4_blobs
+    gm, om = SnRWKV7(p4, shape.vocab), oracle.Rwkv(p4, 1)
+    for tok in (7, 4242, 65000):
+        gm.reset()
+        om.reset()
+        g = np.array(gm.dbg(tok, 0, shape.dim), np.float32)
+        r = om.dbg(tok, 0, shape.dim)
+        for j in range(9):
+            seg = slice(j * shape.dim, (j + 1) * shape.dim)
+            assert rel_err(g[seg], r[seg]) < 5e-3, (tok, j)
+
+
+def test_config4_shape_int4_full_depth_statistics(c4_blobs):
+    """Full 12-layer INT4 logits. This random-init model amplifies a single
+    INT8 activation-code flip (INT4 vs fp32 relative L2 is ~0.7 here, and a
+    1e-6 input perturbation moves the INT4 oracle's logits by ~1%), so the
+    bound is statistical: median row relative L2 <= 5e-2, and every row well
+    inside the INT4 quantisation error itself."""
+    from sunnynet_b200.rwkv7 import Rwkv7Batch
+    shape, _, p4 = c4_blobs
+    B = 16
+    gm, om = Rwkv7Batch(p4, B), oracle.Rwkv(p4, B)
+    rng = np.random.default_rng(0)
+    rels = []
+    for _ in range(2):
+        toks = rng.integers(0, shape.vocab, B).astype(np.int32)
+        lg, ref = gm.step(toks), om.step(toks)
+        rels += list(np.linalg.norm(lg - ref, axis=1) / np.linalg.norm(ref, axis=1))
+    rels = np.array(rels)
+    print("INT4 full-depth row rel-L2: median %.3e max %.3e" % (np.median(rels), rels.max()))
+    assert np.median(rels) <= 5e-2
+    assert rels.max() <= 0.35
 
 
 def test_argmax_matches_logits(tiny):

@@ -62,7 +62,7 @@ def test_internal_abi_matches_reference_c_and_torch(golden):
 
 
 def test_prefill_equals_stepwise_and_reference(golden):
-    """reference tests/test_runtime_model.py:41-58; here exact (same kernels)."""
+    """reference tests/test_runtime_model.py:41-58 (chunked prefill vs steps)."""
     from sunnynet_b200.runtime.model import SnModel
     g = golden("sunny_tiny.npz")
     V, D, I, R, K, L = _golden_dims(g)
@@ -71,8 +71,50 @@ def test_prefill_equals_stepwise_and_reference(golden):
     b = SnModel(GOLDEN / "sunny_tiny.usnn", V, D, I, R, K, L, 8, 1)
     for t in g["tokens"]:
         last = np.array(b.step(int(t)), np.float32)
-    assert np.array_equal(lp, last)
+    check_logits(lp, last)
     check_logits(lp, g["prefill_logits_c"])
+    # the state after the prefill continues exactly like the stepped one
+    nxt = int(last.argmax())
+    check_logits(np.array(a.step(nxt)), np.array(b.step(nxt)))
+
+
+@pytest.mark.parametrize("chunk", [1, 7, 16, 40])
+def test_chunked_prefill_matches_forward(golden, chunk):
+    """Chunked prefill == SunnyNet.forward on the golden 2x40 prompt (final
+    logits and state), for any chunk length (tests/test_architecture.py:127-161)."""
+    from sunnynet_b200.model import SunnyBatch
+    g = golden("sunny_tiny.npz")
+    idx = g["fwd_idx"]
+    m = SunnyBatch(GOLDEN / "sunny_tiny.usnn", idx.shape[0])
+    lg = m.prefill(idx, chunk=chunk)
+    check_logits(lg, g["fwd_logits_last"])
+    s, h = m.get_state()
+    assert rel_err(s, g["fwd_s"]) < TOL
+    assert rel_err(h, g["fwd_hist"][:, :, ::-1]) < TOL
+
+
+@pytest.mark.parametrize("B,T,chunk", [(3, 300, 64), (8, 512, 256)])
+def test_chunked_prefill_vs_oracle_steps(B, T, chunk):
+    """Random model: chunked prefill (tensor-core GEMMs over B*chunk rows +
+    scan) vs the oracle stepping token by token; then decode continues."""
+    from sunnynet_b200 import formats
+    from sunnynet_b200.model import SunnyBatch
+    shape = formats.SunnyShape(2000, 128, 224, 80, 4, 3)
+    rng = np.random.default_rng(T)
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape, seed=2)
+        toks = rng.integers(0, shape.vocab, (B, T)).astype(np.int32)
+        gm, om = SunnyBatch(p, B), oracle.Sunny(p, B)
+        lg = gm.prefill(toks, chunk=chunk)
+        for t in range(T):
+            ref = om.step(toks[:, t], want_logits=(t == T - 1))
+        check_logits(lg, ref)
+        s, h = gm.get_state()
+        for i in range(B):
+            rs, rh = om.get_state(i, shape.layers, shape.dim, shape.kh)
+            assert rel_err(s[i], rs) < TOL and rel_err(h[i], rh) < TOL
+        nxt = ref.argmax(1).astype(np.int32)
+        check_logits(gm.step(nxt), om.step(nxt))
 
 
 def test_dbg_layer_matches_reference(golden):
@@ -166,6 +208,23 @@ def test_config2_shape_vs_oracle(B):
         p = _blob(td, shape, seed=0, fast=True)
         gm, om = SunnyBatch(p, B), oracle.Sunny(p, B)
         for _ in range(3 if B > 8 else 6):
+            toks = rng.integers(0, shape.vocab, B).astype(np.int32)
+            check_logits(gm.step(toks), om.step(toks))
+
+
+@pytest.mark.parametrize("B", [16, 64])
+def test_config3_shape_int8_vs_oracle(B):
+    """BASELINE config 3 (L12 d768 i1344 r480 V32000, INT8 per-row): the
+    tensor-core path with exact bf16 INT8 codes (two MMAs per K step); r=480
+    exercises a partial last K slab."""
+    from sunnynet_b200 import formats
+    from sunnynet_b200.model import SunnyBatch
+    shape = formats.SUNNY_PRESETS["c3"]
+    rng = np.random.default_rng(B)
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape, quant=True, seed=1, fast=True)
+        gm, om = SunnyBatch(p, B), oracle.Sunny(p, B)
+        for _ in range(2):
             toks = rng.integers(0, shape.vocab, B).astype(np.int32)
             check_logits(gm.step(toks), om.step(toks))
 
