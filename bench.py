@@ -602,7 +602,145 @@ def ref_prefill(path, S, budget_s=15.0):
                       f"{cores} OpenMP threads"}
 
 
-WORKLOADS = {"c1": wl_c1, "c2": wl_c2, "c2b1": wl_c2b1, "c3": wl_c3, "c5": wl_c5}
+def rwkv_step_cost(S, B, q4_bytes):
+    """Algorithmic bytes / FLOPs of one RWKV-7 decode step: weights once,
+    matrix state and token shift read+written, embedding rows, logits."""
+    D, F, V, L = S.dim, S.ffn, S.vocab, S.layers
+    Rw, Ra, Rv, Rg = S.ranks
+    mats = 4 * D * D + D * (Rw + Ra + Rv + Rg) * 2 + 2 * D * F
+    state = 2 * B * L * (S.n_head * S.head_size ** 2 + 2 * D) * 4
+    return q4_bytes + state + B * D * 4 + B * V * 4, 2 * B * (L * mats + V * D)
+
+
+def wl_rwkv(args, torch, dist, ours, B):
+    from sunnynet_b200 import formats
+    S = formats.RWKV_PRESETS["c4"]
+    td = tempfile.mkdtemp(prefix="snbench4_")
+    path = Path(td) / "c4.q4g.bin"
+    w = formats.random_rwkv(S, 0)
+    info = formats.write_krwk(path, w, quant="q4g", group=128)
+    step_bytes, step_flops = rwkv_step_cost(S, B, info["bytes"] - S.vocab * S.dim * 4)
+    res = {"metric": "decode tokens/s", "unit": "tokens/s", "higher_is_better": True,
+           "dtype": "int4w-a8 (W4A8) + f32",
+           "config": {"workload": f"c4 RWKV-7 L{S.layers} D{S.dim} H{S.n_head}x{S.head_size} "
+                                  f"F{S.ffn} V{S.vocab}, INT4 group 128 fp16 scales",
+                      "batch_per_gpu": B, "global_batch": B * dist.world,
+                      "decode": "greedy", "l2": "flushed between steps"
+                      if step_bytes < 2 * (126 << 20) else "working set > L2"}}
+    ref_blob = Path(td) / "c4.q4v3.bin"  # the reference's only INT4 format (block 64, fp32 scales)
+    if not ours:
+        formats.write_krwk(ref_blob, w, quant="q4")
+        return res, ref_rwkv(ref_blob, S, B)
+    from sunnynet_b200 import _lib
+    from sunnynet_b200._lib import check
+    from sunnynet_b200.rwkv7 import Rwkv7Batch
+    lib = _lib.load()
+    check(lib.sn_abi_cuda_set_stream(torch.cuda.current_stream().cuda_stream))
+    m = Rwkv7Batch(path, B)
+    check(lib.sn_abi_cuda_set_async(1))
+    g = torch.Generator(device="cuda").manual_seed(dist.rank)
+    cur = torch.randint(0, S.vocab, (B,), generator=g, device="cuda", dtype=torch.int32)
+    for _ in range(8):
+        m.step_argmax(cur, out=cur)
+
+    def step():
+        m.step_argmax(cur, out=cur)
+
+    flushbuf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    flush = flushbuf.zero_ if step_bytes < 2 * (126 << 20) else None
+    with ClockSampler(dist.local) as clk:
+        ms = timed_steps(torch, dist, step, args.steps, args.warmup, flush=flush)
+    check(lib.sn_abi_cuda_profile(1))
+    for _ in range(3):
+        if flush:
+            flush()
+        step()
+    torch.cuda.synchronize()
+    check(lib.sn_abi_cuda_profile(0))
+    fams = _lib.profile_report()
+    check(lib.sn_abi_cuda_set_async(0))
+    dom = max(fams, key=lambda k: fams[k][1])
+    n_l, t_ms = fams[dom]
+    peaks = measured_peaks()
+    step_gbs = step_bytes / (ms * 1e-3) / 1e9
+    if dom == "rk_heads":  # per launch: one layer's matrix states read + written
+        fb = 2 * B * S.n_head * S.head_size ** 2 * 4
+        ach = fb / (t_ms / n_l * 1e-3) / 1e9
+    else:
+        fb, ach = None, None
+    rl = {"bound": "hbm", "achieved": ach if ach else step_gbs, "peak": peaks["hbm_gbs"],
+          "unit": "GB/s", "peak_src": peaks["src"], "kernel": dom, "launches": n_l,
+          "avg_launch_us": t_ms / n_l * 1e3, "alg_bytes_per_launch": fb,
+          "achieved_is": "dominant kernel" if ach else "whole step (dominant is a GEMV family)",
+          "traffic": profile_traffic(f"{dom}/c4/B{B}"), "step_alg_bytes": step_bytes,
+          "step_alg_flops": step_flops, "step_hbm_gbs": step_gbs,
+          "families_ms_per_step": {k: v[1] / 3 for k, v in fams.items()}}
+    rl["frac"] = rl["achieved"] / rl["peak"]
+    ht = torch.randint(0, S.vocab, (B,), dtype=torch.int32).pin_memory()
+    hl = torch.empty(B, S.vocab).pin_memory()
+    for _ in range(2):
+        m.step(ht, logits=hl)
+    reps = max(5, min(40, int(2000 / max(ms, 0.05))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        m.step(ht, logits=hl)
+    e2e_s = dist.max(torch, (time.perf_counter() - t0) / reps)
+    res.update({"ms_per_step": ms, "value": B * dist.world / (ms * 1e-3),
+                "e2e": {"value": B * dist.world / e2e_s, "unit": "tokens/s",
+                        "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * S.vocab * 4,
+                        "call": "sn_abi_rwkv7_step_batch (host ids, host logits)"},
+                "gpu_launches": (S.layers * 20 + 4) * args.steps, "roofline": rl,
+                "clocks": clk.summary()})
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        formats.write_krwk(ref_blob, w, quant="q4")
+        res["cpu_baseline"] = ref_rwkv(ref_blob, S, B)
+    m.close()
+    return res, None
+
+
+def ref_rwkv(path, S, B, budget_s=10.0):
+    """Reference C runtime sn_rk_step on its INT4 blob (block 64, fp32 scales:
+    the only INT4 format rwkv7.c reads). B=1: one handle; B>1: one handle per
+    physical core stepping concurrently (the C runtime is B=1 per handle)."""
+    import threading
+    import oracle
+    if not oracle.ref_available():
+        raise RuntimeError("oracle/_ref is not built; the CPU baseline needs the reference runtime")
+    L = oracle.ref_abi()
+    cores = max(1, int(oracle.ref_model().sn_recommended_threads()))
+    K = 1 if B == 1 else min(cores, B, 32)
+    L.sn_set_threads(cores if B == 1 else 1)
+    hs = [L.sn_rk_load(str(path).encode()) for _ in range(K)]
+    counts = [0] * K
+    stop = time.perf_counter() + budget_s
+
+    def run(i):
+        buf = np.empty(S.vocab, np.float32)
+        p = oracle.ptr(buf)
+        L.sn_rk_step(hs[i], 1 + i, p)
+        while time.perf_counter() < stop:
+            L.sn_rk_step(hs[i], int(buf.argmax()), p)
+            counts[i] += 1
+
+    t0 = time.perf_counter()
+    ths = [threading.Thread(target=run, args=(i,)) for i in range(K)]
+    for th in ths:
+        th.start()
+    for th in ths:
+        th.join()
+    dt = time.perf_counter() - t0
+    for h in hs:
+        L.sn_rk_free(h)
+    return {"value": sum(counts) / dt, "unit": "tokens/s", "cores": cores if K == 1 else K,
+            "kind": "reference",
+            "sample": f"{sum(counts)} sn_rk_step calls on the reference INT4 blob (block 64), "
+                      f"{K} handle(s), ~{budget_s:.0f} s"}
+
+
+WORKLOADS = {"c1": wl_c1, "c2": wl_c2, "c2b1": wl_c2b1, "c3": wl_c3, "c5": wl_c5,
+             "c4": lambda a, t, d, ours: wl_rwkv(a, t, d, ours, 64),
+             "c4b1": lambda a, t, d, ours: wl_rwkv(a, t, d, ours, 1),
+             "c4b512": lambda a, t, d, ours: wl_rwkv(a, t, d, ours, 512)}
 SCALING = {"c3": "strong"}
 
 

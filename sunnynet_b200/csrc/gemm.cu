@@ -1,5 +1,6 @@
 // SIMT implementations of the contractions declared in gemm.cuh.
 #include "gemm.cuh"
+#include "ptx.cuh"
 #include "runtime.cuh"
 #include "tc_gemm.cuh"
 
@@ -26,15 +27,55 @@ constexpr int kGemvRows = 8;
 
 template <int WT>
 __global__ void __launch_bounds__(256) gemv_rows_kernel(GemmArgs a) {
-    extern __shared__ __align__(16) float sA[];  // [M][K]
+    extern __shared__ __align__(16) float sA[];  // [M][K], then mean[M], rstd[M]
     const int M = a.M, K = a.K;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    pdl_trigger();
+    {   // this warp's weight rows do not depend on the previous kernel: pull them
+        // into L2 while it finishes (launched with programmatic serialization)
+        const int wb = WT == kWF32 ? 4 : (WT == kWI8 ? 1 : 2);
+        const long long rowbytes = (long long)K * wb;
+        for (int n = blockIdx.x * (blockDim.x >> 5) + warp; n < a.N; n += nw) {
+            const char* row = reinterpret_cast<const char*>(a.W) + (long long)n * a.ldw * wb;
+            for (long long off = (long long)lane * 128; off < rowbytes; off += 32 * 128)
+                prefetch_l2(row + off);
+        }
+    }
+    pdl_wait();
+    float* st_mu = sA + M * K;
+    float* st_rs = st_mu + M;
     for (int i = threadIdx.x; i < M * K; i += blockDim.x) {
         const int m = i / K, k = i - m * K;
-        sA[i] = a_eff(a, m, k, a.A[m * a.lda + k]);
+        const float v = a.A[m * a.lda + k];
+        sA[i] = a.ln_inline ? v : a_eff(a, m, k, v);
     }
     __syncthreads();
-    const int lane = threadIdx.x & 31;
-    const int nw = gridDim.x * (blockDim.x >> 5);
+    if (a.ln_inline) {  // two-pass row statistics, one warp per row (M <= 8)
+        if (warp < M) {
+            const float* r = sA + warp * K;
+            float s = 0.0f;
+            for (int k = lane; k < K; k += 32) s += r[k];
+            for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            const float mean = s / (float)K;
+            float v = 0.0f;
+            for (int k = lane; k < K; k += 32) {
+                const float d = r[k] - mean;
+                v += d * d;
+            }
+            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) {
+                st_mu[warp] = mean;
+                st_rs[warp] = 1.0f / sqrtf(v / (float)K + a.ln_eps);
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < M * K; i += blockDim.x) {
+            const int m = i / K, k = i - m * K;
+            sA[i] = __fmul_rn(__fmul_rn(sA[i] - st_mu[m], st_rs[m]), a.g[k]) + a.c[k];
+        }
+        __syncthreads();
+    }
     const bool vec = (WT == kWF32 ? K % 4 == 0 : (WT == kWI8 ? K % 16 == 0 : K % 8 == 0)) &&
                      (a.ldw % (WT == kWF32 ? 4 : (WT == kWI8 ? 16 : 8)) == 0);
     for (int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); n < a.N; n += nw) {
@@ -159,7 +200,7 @@ __global__ void __launch_bounds__(256) gemm_tiled_kernel(GemmArgs a) {
 template <int WT>
 int launch_wt(const GemmArgs& a, cudaStream_t st) {
     if (a.M <= kGemvRows) {
-        const size_t smem = (size_t)a.M * a.K * sizeof(float);
+        const size_t smem = ((size_t)a.M * a.K + 2 * kGemvRows) * sizeof(float);
         if (smem > 200 * 1024) return fail(SN_E_INVAL, "gemm: K=%d too large for the row path", a.K);
         static int attr_set = 0;
         if (!attr_set) {
@@ -172,8 +213,10 @@ int launch_wt(const GemmArgs& a, cudaStream_t st) {
         int ctas = (a.N + 7) / 8;
         const int cap = 2 * rt().num_sms;
         if (ctas > cap) ctas = cap;
-        gemv_rows_kernel<WT><<<ctas, 256, smem, st>>>(a);
+        SN_TRY(cuda_check(launch_pdl(gemv_rows_kernel<WT>, dim3(ctas), dim3(256), smem, st, a),
+                          "gemv launch"));
     } else {
+        if (a.ln_inline) return fail(SN_E_INVAL, "gemm: in-kernel LN statistics need M <= 8");
         dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
         gemm_tiled_kernel<WT><<<grid, 256, 0, st>>>(a);
     }

@@ -40,11 +40,14 @@ struct GemmArgs {
     const float* wscale = nullptr;  // int8: per output row n
     float* C = nullptr;
     long long ldc = 0;
-    // optional row-LN prologue on A
+    // optional row-LN prologue on A: statistics given (mu, rs), or computed in
+    // the kernel from the staged rows (ln_inline, small-batch row path only)
     const float* mu = nullptr;
     const float* rs = nullptr;
     const float* g = nullptr;
     const float* c = nullptr;
+    int ln_inline = 0;
+    float ln_eps = 0.0f;
     // epilogue
     int epi = kEpiNone;
     float p = 0.0f;

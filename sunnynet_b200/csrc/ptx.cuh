@@ -76,4 +76,18 @@ __device__ __forceinline__ void cp_async_wait_all() {
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
+// Programmatic dependent launch: let the next kernel in the stream start
+// early (it must pdl_wait before reading this kernel's outputs) ...
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// ... and, in a kernel launched with programmatic serialization, wait until
+// the previous kernel has completed and its writes are visible. No-op when
+// the kernel was launched normally.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 }  // namespace sn

@@ -75,6 +75,24 @@ struct ProfScope {
     }
 };
 
+// Launch with programmatic stream serialization (the kernel may start while
+// the previous one finishes; it must call pdl_wait before reading its inputs).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Error codes written into the device error word.
 enum DevErr : int { kErrNone = 0, kErrWaitTimeout = 1, kErrBadIndex = 2 };
 

@@ -34,6 +34,7 @@
 
 #include "gemm.cuh"
 #include "kernels.cuh"
+#include "ptx.cuh"
 #include "runtime.cuh"
 #include "sn_abi.h"
 #include "sunnynet.h"
@@ -68,6 +69,7 @@ __global__ void prep_kernel(int D, int K, int KH, int layer, int L, const int32_
                             const float* __restrict__ g, const float* __restrict__ c,
                             const float* __restrict__ dw, float eps) {
     __shared__ float red[32];
+    pdl_trigger();  // the next GEMV may start prefetching its weights
     const int b = blockIdx.x;
     // ring position of this (sequence, layer); every thread reads it before the
     // block-wide barriers below, thread 0 advances it at the end
@@ -116,6 +118,7 @@ __global__ void gate_kernel(int B, int D, int G, int L, int layer, const float* 
                             const float* __restrict__ delta, float* __restrict__ s,
                             float* __restrict__ u, float* __restrict__ gate_out, int clamp,
                             float p_floor) {
+    pdl_trigger();
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (i >= (long long)B * D) return;
     const int b = (int)(i / D), d = (int)(i % D);
@@ -586,6 +589,11 @@ int load_model(SunnyModel* m, const char* path, int nseq, bool half, const int* 
             SN_TRY(tc_prepare(&y.tWs, y.Ws, m->wtype, D, D, al, m));
         }
         SN_TRY(tc_prepare(&m->thead, m->head, m->wtype, vocab, D, al, m));
+        if (nseq >= 16) {
+            SN_TRY(tc_reserve(D, nseq));
+            SN_TRY(tc_reserve(R, nseq));
+            SN_TRY(tc_reserve(I, nseq));
+        }
     }
     m->eps = ep[0];
     m->p_floor = ep[1];
@@ -670,14 +678,22 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
             ProfScope ps("gemm_Wz", st);
             SN_TRY(launch_gemm(gz, m->wtype, st, &y.tWz));
         }
-        {
+        // small batches compute the LN statistics inside the GEMV (one launch less)
+        const bool inline_ln = B <= 8 && !this_dbg;
+        if (!inline_ln) {
             ProfScope ps("rowstats", st);
             rowstats_kernel<<<B, 256, 0, st>>>(I, m->z, I, m->mu, m->rs, m->eps);
         }
         if (this_dbg)
             apply_ln_kernel<<<B, 256, 0, st>>>(I, m->z, m->mu, m->rs, y.nm_g, y.nm_c, m->yn);
         GemmArgs gc = gemm(B, D, I, m->z, y.Wc, y.sWc, m->x);
-        gc.mu = m->mu; gc.rs = m->rs; gc.g = y.nm_g; gc.c = y.nm_c;
+        gc.g = y.nm_g; gc.c = y.nm_c;
+        if (inline_ln) {
+            gc.ln_inline = 1;
+            gc.ln_eps = m->eps;
+        } else {
+            gc.mu = m->mu; gc.rs = m->rs;
+        }
         gc.epi = kEpiResid;
         gc.p = y.b_gain;
         gc.S = m->s + (size_t)l * D;
@@ -691,12 +707,18 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
     }
     if (dbg) return cuda_check(cudaGetLastError(), "dbg step");
     if (with_head) {
-        {
+        if (B > 8) {
             ProfScope ps("rowstats", st);
             rowstats_kernel<<<B, 256, 0, st>>>(D, m->x, D, m->mu, m->rs, m->eps);
         }
         GemmArgs gh = gemm(B, m->vocab, D, m->x, m->head, m->shead, m->logits);
-        gh.mu = m->mu; gh.rs = m->rs; gh.g = m->no_g; gh.c = m->no_c;
+        gh.g = m->no_g; gh.c = m->no_c;
+        if (B <= 8) {
+            gh.ln_inline = 1;
+            gh.ln_eps = m->eps;
+        } else {
+            gh.mu = m->mu; gh.rs = m->rs;
+        }
         ProfScope ps("gemm_head", st);
         SN_TRY(launch_gemm(gh, m->wtype, st, &m->thead));
     }
@@ -752,6 +774,11 @@ int ensure_chunk_bufs(SunnyModel* m, int B, int Tc) {
     m->csend = m->dalloc<float>((size_t)B * D);
     if (!m->csend || !m->cs0 || !m->crs || !m->cz)
         return fail(SN_E_NOMEM, "prefill buffers for %lld rows", rows);
+    if (!getenv("SN_DISABLE_TC") && rows >= 16) {
+        SN_TRY(tc_reserve(m->D, rows));
+        SN_TRY(tc_reserve(m->R, rows));
+        SN_TRY(tc_reserve(m->I, rows));
+    }
     m->crows = rows;
     m->cseqs = B;
     for (auto& kv : m->cgraphs) cudaGraphExecDestroy(kv.second);  // captured old pointers

@@ -1,27 +1,30 @@
 // tcgen05 / TMEM contraction for the batched token loop (see tc_gemm.cuh).
 //
-// One CTA computes a 128 x BN tile of C with the whole K loop, through an
-// S-deep shared-memory ring of K-slabs of 64 (one 128-byte swizzle row of bf16):
-//   warps 0-3  A producers: thread t owns row m0+t, loads 64 fp32 of it,
-//              applies the row-LN prologue, splits into bf16 hi/lo and stores
-//              both in the SWIZZLE_128B K-major layout the MMA descriptor
-//              expects (16-byte chunk c of row r at r*128 + ((c ^ r%8) * 16)
-//              inside its 1024-byte 8-row atom); then the epilogue
-//   warp 4     W producer: TMA 2-D tile loads of the hi/lo weight planes
-//              (SWIZZLE_128B, no multicast) signalled through complete_tx
-//   warp 5     TMEM allocation and the single MMA-issuing thread:
-//              tcgen05.mma.cta_group::1.kind::f16, M=128, N=BN, K=16, three
-//              products per K step (Ah*Wh, Ah*Wl, Al*Wh; two for INT8),
-//              tcgen05.commit frees a stage / signals the accumulator
-// Epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes 32w..32w+31 = its
-// rows) into registers, the shared gemm_epilogue, 16-byte global stores.
-// Every mbarrier wait is bounded; a role that gives up sets the error word,
-// drains its own in-flight TMA/MMA work and the CTA frees its TMEM.
+// Two launches per contraction:
+//   split_act_kernel  A' (fp32 activations, row-LN prologue applied) -> bf16
+//                     planes Ah, Al (M,K) with A' = Ah + Al to ~16 bits; once
+//                     per GEMM instead of once per N-tile
+//   tc_gemm_kernel    one CTA per 128 x BN tile of C, whole K loop through an
+//                     S-deep ring of 64-wide K slabs (one 128-byte swizzle row):
+//     warp 0  one thread issues the TMA 2-D tile loads of Ah, Al, Wh, Wl
+//             (SWIZZLE_128B, no multicast), one complete_tx barrier per stage
+//     warp 1  TMEM allocation; one thread issues tcgen05.mma.cta_group::1
+//             .kind::f16 (M=128, N=BN, K=16): Ah*Wh + Ah*Wl + Al*Wh per K step
+//             (two products for INT8 weights, exact in bf16), tcgen05.commit
+//             frees the stage / signals the accumulator
+//     warps 2-5 epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes of
+//             quarter w%4), 32x32 blocks staged through shared memory so each
+//             global access is one 128-byte row segment, shared gemm_epilogue
+// Every mbarrier wait is bounded; a role that gives up records the error,
+// drains its own in-flight TMA/MMA work, and the CTA frees its TMEM.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
+#include <map>
+#include <vector>
 
 #include "ptx.cuh"
 #include "runtime.cuh"
@@ -45,7 +48,7 @@ struct TcCfg {
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return (uint64_t)((saddr >> 4) & 0x3FFFu)  // start address
-           | ((uint64_t)1u << 16)               // leading byte offset (16 B, unused for SW128 K-major)
+           | ((uint64_t)1u << 16)               // leading byte offset (unused for SW128 K-major)
            | ((uint64_t)64u << 32)              // stride byte offset: 1024 B between 8-row atoms
            | ((uint64_t)1u << 46)               // descriptor version (sm_100)
            | ((uint64_t)2u << 61);              // SWIZZLE_128B
@@ -88,9 +91,6 @@ __device__ __forceinline__ void tc_fence_after() {
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     uint32_t r[32];
@@ -114,18 +114,46 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// A' -> (Ah, Al), 8 elements (one 16-byte chunk of each plane) per thread-step.
+__global__ void split_act_kernel(GemmArgs a, __nv_bfloat16* __restrict__ hi,
+                                 __nv_bfloat16* __restrict__ lo) {
+    const int cpr = a.K / 8;
+    const long long total = (long long)a.M * cpr;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int m = (int)(i / cpr), k = (int)(i % cpr) * 8;
+        const float* src = a.A + (long long)m * a.lda + k;
+        const float4 x0 = *reinterpret_cast<const float4*>(src);
+        const float4 x1 = *reinterpret_cast<const float4*>(src + 4);
+        float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        if (a.mu) {
+            const float mu = a.mu[m], rs = a.rs[m];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__fmul_rn(v[j] - mu, rs), a.g[k + j]) + a.c[k + j];
+        }
+        float l[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) l[j] = v[j] - __bfloat162float(__float2bfloat16_rn(v[j]));
+        const long long o = (long long)m * a.K + k;
+        *reinterpret_cast<uint4*>(hi + o) = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]),
+                                                       pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+        *reinterpret_cast<uint4*>(lo + o) = make_uint4(pack_bf16(l[0], l[1]), pack_bf16(l[2], l[3]),
+                                                       pack_bf16(l[4], l[5]), pack_bf16(l[6], l[7]));
+    }
+}
+
 template <int BN, bool I8>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmh, const __grid_constant__ CUtensorMap tml,
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
+                   const __grid_constant__ CUtensorMap twh, const __grid_constant__ CUtensorMap twl,
                    GemmArgs a, int* err) {
     using C = TcCfg<BN>;
     constexpr int S = C::S;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* sb = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // 1024-B aligned ring
-    uint64_t* a_full = reinterpret_cast<uint64_t*>(sb + S * C::STAGE);
-    uint64_t* w_full = a_full + S;
-    uint64_t* empty = w_full + S;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sb + S * C::STAGE);
+    uint64_t* empty = full + S;
     uint64_t* acc_full = empty + S;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(acc_full + 1);
     volatile int* give_up = reinterpret_cast<volatile int*>(acc_full + 2);
@@ -140,15 +168,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&a_full[s], 128);
-            mbar_init(&w_full[s], 1);
+            mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         mbar_init(acc_full, 1);
         *give_up = 0;
         fence_mbar_init();
     }
-    if (warp == 5) {  // TMEM accumulator: BN fp32 columns x 128 lanes
+    if (warp == 1) {  // TMEM accumulator: BN fp32 columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32((const void*)tmem_slot)),
                      "r"((uint32_t)BN)
@@ -160,75 +187,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < 4) {  // ------------------------------------------ A producers
-        const int t = threadIdx.x;
-        const int m = m0 + t;
-        const bool live = m < a.M;
-        const float mu = (live && a.mu) ? a.mu[m] : 0.0f;
-        const float rs = (live && a.mu) ? a.rs[m] : 0.0f;
-        const float* arow = a.A + (long long)(live ? m : 0) * a.lda;
-        const uint32_t r8 = t & 7;
-        const uint32_t row_off = (t >> 3) * 1024 + r8 * 128;
-        // the next slab's 64 values are loaded while this one is converted
-        float4 nx[16];
-        auto load_slab = [&](int kt) {
-#pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                const int k = kt * BK + 4 * q;
-                nx[q] = (live && k < a.K) ? *reinterpret_cast<const float4*>(arow + k)
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        };
-        load_slab(0);
-        for (int kt = 0; kt < nk; ++kt) {
-            const int s = kt % S;
-            float4 cur[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) cur[q] = nx[q];
-            if (kt + 1 < nk) load_slab(kt + 1);
-            if (kt >= S && !mbar_wait(&empty[s], ((kt / S) - 1) & 1, err)) {
-                *give_up = 1;
-                break;
-            }
-            const int k0 = kt * BK;
-            uint8_t* ah = stage_ptr(s, 0) + row_off;
-            uint8_t* al = stage_ptr(s, 1) + row_off;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {  // 8 values per 16-byte chunk
-                const int k = k0 + 8 * c;
-                float v[8] = {cur[2 * c].x,     cur[2 * c].y,     cur[2 * c].z,
-                              cur[2 * c].w,     cur[2 * c + 1].x, cur[2 * c + 1].y,
-                              cur[2 * c + 1].z, cur[2 * c + 1].w};
-                if (a.mu && live && k < a.K) {  // K % 8 == 0: a chunk is all in or all out
-                    const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.g + k));
-                    const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.g + k + 4));
-                    const float4 c0 = __ldg(reinterpret_cast<const float4*>(a.c + k));
-                    const float4 c1 = __ldg(reinterpret_cast<const float4*>(a.c + k + 4));
-                    const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-                    const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        v[j] = __fmul_rn(__fmul_rn(v[j] - mu, rs), gg[j]) + cc[j];
-                }
-                float lo[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float h = __bfloat162float(__float2bfloat16_rn(v[j]));
-                    lo[j] = v[j] - h;
-                }
-                const uint32_t sw = ((uint32_t)c ^ r8) * 16;
-                *reinterpret_cast<uint4*>(ah + sw) =
-                    make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]),
-                               pack_bf16(v[6], v[7]));
-                *reinterpret_cast<uint4*>(al + sw) =
-                    make_uint4(pack_bf16(lo[0], lo[1]), pack_bf16(lo[2], lo[3]),
-                               pack_bf16(lo[4], lo[5]), pack_bf16(lo[6], lo[7]));
-            }
-            fence_proxy_async();  // generic-proxy smem writes -> visible to the tensor core
-            mbar_arrive(&a_full[s]);
-        }
-    } else if (warp == 4) {  // ----------------------------------- W producer
+    if (warp == 0) {  // --------------------------------------------- TMA producer
         if (lane == 0) {
+            const uint32_t bytes = 2 * C::A_BYTES + (I8 ? 1 : 2) * C::W_BYTES;
             int issued = 0;
             for (int kt = 0; kt < nk; ++kt) {
                 const int s = kt % S;
@@ -237,25 +198,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *give_up = 1;
                     break;
                 }
-                mbar_expect_tx(&w_full[s], I8 ? C::W_BYTES : 2 * C::W_BYTES);
-                tma_load_2d(stage_ptr(s, 2), &tmh, kt * BK, n0, &w_full[s]);
-                if (!I8) tma_load_2d(stage_ptr(s, 3), &tml, kt * BK, n0, &w_full[s]);
+                mbar_expect_tx(&full[s], bytes);
+                tma_load_2d(stage_ptr(s, 0), &tah, kt * BK, m0, &full[s]);
+                tma_load_2d(stage_ptr(s, 1), &tal, kt * BK, m0, &full[s]);
+                tma_load_2d(stage_ptr(s, 2), &twh, kt * BK, n0, &full[s]);
+                if (!I8) tma_load_2d(stage_ptr(s, 3), &twl, kt * BK, n0, &full[s]);
                 issued = kt + 1;
             }
             // never leave with a tile load in flight: wait for the last use of each stage
             for (int kt = issued - S < 0 ? 0 : issued - S; kt < issued; ++kt)
-                mbar_wait(&w_full[kt % S], (kt / S) & 1, err);
+                mbar_wait(&full[kt % S], (kt / S) & 1, err);
         }
-    } else {  // ----------------------------------------------- MMA issuer
+    } else if (warp == 1) {  // ---------------------------------------- MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = (1u << 4)                    // D: f32
-                                   | (1u << 7) | (1u << 10)     // A, B: bf16
+            const uint32_t idesc = (1u << 4)                      // D: f32
+                                   | (1u << 7) | (1u << 10)       // A, B: bf16
                                    | ((uint32_t)(BN >> 3) << 17)  // N
-                                   | ((uint32_t)(BM >> 4) << 24);  // M
+                                   | ((uint32_t)(BM >> 4) << 24); // M
             for (int kt = 0; kt < nk; ++kt) {
                 const int s = kt % S;
-                if (!mbar_wait(&a_full[s], (kt / S) & 1, err) ||
-                    !mbar_wait(&w_full[s], (kt / S) & 1, err)) {
+                if (!mbar_wait(&full[s], (kt / S) & 1, err)) {
                     *give_up = 1;
                     break;
                 }
@@ -272,31 +234,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_commit(&empty[s]);  // stage reusable once these MMAs have read it
             }
-            tc_commit(acc_full);  // accumulator complete (or: no MMA left in flight)
+            tc_commit(acc_full);  // accumulator complete (or: nothing left in flight)
         }
-    }
-
-    // ------------------------------------------------------------- epilogue
-    if (warp < 4) {
+    } else {  // ------------------------------------------------ epilogue (warps 2-5)
+        const int q = warp & 3;  // TMEM lane quarter this warp may read
         const bool ok = mbar_wait(acc_full, 0, err);
         tc_fence_after();
         if (ok && !*give_up) {
-            // 32x32 blocks go through shared memory (the idle ring) so that a
+            // 32x32 blocks go through shared memory (the drained ring) so that a
             // warp touches one 128-byte row segment per global access
-            float* stg = reinterpret_cast<float*>(sb) + warp * (32 * 33);
+            float* stg = reinterpret_cast<float*>(sb) + (warp - 2) * (32 * 33);
 #pragma unroll 1
             for (int j0 = 0; j0 < BN; j0 += 32) {
                 float v[32];
-                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)j0, v);
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)j0, v);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = v[j];
                 __syncwarp();
                 const int n = n0 + j0 + lane;
 #pragma unroll 4
                 for (int r = 0; r < 32; ++r) {
-                    const int mm = m0 + warp * 32 + r;
+                    const int mm = m0 + q * 32 + r;
                     if (mm < a.M && n < a.N)
-                        a.C[(long long)mm * a.ldc + n] = gemm_epilogue(a, mm, n, stg[r * 33 + lane]);
+                        a.C[(long long)mm * a.ldc + n] =
+                            gemm_epilogue(a, mm, n, stg[r * 33 + lane]);
                 }
                 __syncwarp();
             }
@@ -304,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"((uint32_t)BN)
@@ -348,22 +309,36 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-int encode_map(CUtensorMap* tm, const void* base, int N, int K, int box_rows) {
-    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+// bf16 (rows, K) K-major plane, box = 64 x box_rows, SWIZZLE_128B
+int encode_map(CUtensorMap* tm, const void* base, long long rows, int K, int box_rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
     const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(SN_E_DEVICE, "cuTensorMapEncodeTiled entry point unavailable");
-    const CUresult r = enc(
-        tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? SN_OK : fail(SN_E_DEVICE, "cuTensorMapEncodeTiled failed (%d)", (int)r);
 }
 
+// Activation planes per K, reused by every contraction with that K (they run
+// in stream order). Grown only outside graph capture; superseded planes stay
+// allocated because captured graphs may still reference them.
+struct ActPlanes {
+    long long cap = 0;
+    __nv_bfloat16 *hi = nullptr, *lo = nullptr;
+    CUtensorMap tm_hi, tm_lo;
+};
+std::map<int, ActPlanes>& act_cache() {
+    static std::map<int, ActPlanes> c;
+    return c;
+}
+
 template <int BN, bool I8>
-int launch_bn(const GemmArgs& a, const TcWeights& tw, cudaStream_t st) {
+int launch_bn(const GemmArgs& a, const TcWeights& tw, const ActPlanes& ap, cudaStream_t st) {
     using C = TcCfg<BN>;
     static bool attr = false;
     auto k = tc_gemm_kernel<BN, I8>;
@@ -375,11 +350,35 @@ int launch_bn(const GemmArgs& a, const TcWeights& tw, cudaStream_t st) {
     }
     const int bi = BN == 32 ? 0 : (BN == 64 ? 1 : 2);
     dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
-    k<<<grid, kThreads, C::SMEM, st>>>(tw.tm_hi[bi], tw.tm_lo[bi], a, rt().d_err);
+    k<<<grid, kThreads, C::SMEM, st>>>(ap.tm_hi, ap.tm_lo, tw.tm_hi[bi], tw.tm_lo[bi], a,
+                                       rt().d_err);
     return cuda_check(cudaGetLastError(), "tc_gemm launch");
 }
 
 }  // namespace
+
+int tc_reserve(int K, long long rows) {
+    if (K % 8 != 0 || rows <= 0) return SN_OK;
+    ActPlanes& p = act_cache()[K];
+    if (p.cap >= rows) return SN_OK;
+    long long cap = 128;
+    while (cap < rows) cap *= 2;
+    void *hi = nullptr, *lo = nullptr;
+    if (cudaMalloc(&hi, (size_t)cap * K * 2) != cudaSuccess ||
+        cudaMalloc(&lo, (size_t)cap * K * 2) != cudaSuccess) {
+        cudaGetLastError();
+        if (hi) cudaFree(hi);
+        return fail(SN_E_NOMEM, "activation planes (%lld x %d)", cap, K);
+    }
+    ActPlanes np;
+    np.cap = cap;
+    np.hi = (__nv_bfloat16*)hi;
+    np.lo = (__nv_bfloat16*)lo;
+    SN_TRY(encode_map(&np.tm_hi, np.hi, cap, K, BM));
+    SN_TRY(encode_map(&np.tm_lo, np.lo, cap, K, BM));
+    p = np;  // the old planes (if any) stay allocated for graphs that captured them
+    return SN_OK;
+}
 
 int tc_prepare(TcWeights* tw, const void* W, int wtype, int N, int K,
                void* (*alloc)(size_t, void*), void* owner) {
@@ -409,11 +408,18 @@ bool tc_usable(const GemmArgs& a, const TcWeights* tw) {
         const char* e = getenv("SN_DISABLE_TC");
         disabled = e && atoi(e) ? 1 : 0;
     }
-    return !disabled && tw && tw->ready && a.M >= 16 && a.K == tw->K && a.N == tw->N &&
-           a.K % 8 == 0 && a.lda % 4 == 0 && ((uintptr_t)a.A % 16) == 0;
+    if (disabled || !tw || !tw->ready || a.M < 16 || a.K != tw->K || a.N != tw->N ||
+        a.K % 8 != 0 || a.lda % 4 != 0 || ((uintptr_t)a.A % 16) != 0)
+        return false;
+    auto it = act_cache().find(a.K);
+    return it != act_cache().end() && it->second.cap >= a.M;  // planes reserved up front
 }
 
 int launch_tc_gemm(const GemmArgs& a, const TcWeights& tw, cudaStream_t st) {
+    const ActPlanes& ap = act_cache()[a.K];
+    split_act_kernel<<<grid_blocks((long long)a.M * (a.K / 8), 256, 8), 256, 0, st>>>(a, ap.hi,
+                                                                                     ap.lo);
+    SN_TRY(cuda_check(cudaGetLastError(), "split_act launch"));
     // widest tile that still gives about a wave of CTAs
     const long long mt = (a.M + BM - 1) / BM;
     const long long sms = rt().num_sms;
@@ -421,13 +427,13 @@ int launch_tc_gemm(const GemmArgs& a, const TcWeights& tw, cudaStream_t st) {
     if (mt * ((a.N + 127) / 128) >= sms * 3 / 4) bn = 128;
     else if (mt * ((a.N + 63) / 64) >= sms * 3 / 4) bn = 64;
     if (tw.int8) {
-        if (bn == 128) return launch_bn<128, true>(a, tw, st);
-        if (bn == 64) return launch_bn<64, true>(a, tw, st);
-        return launch_bn<32, true>(a, tw, st);
+        if (bn == 128) return launch_bn<128, true>(a, tw, ap, st);
+        if (bn == 64) return launch_bn<64, true>(a, tw, ap, st);
+        return launch_bn<32, true>(a, tw, ap, st);
     }
-    if (bn == 128) return launch_bn<128, false>(a, tw, st);
-    if (bn == 64) return launch_bn<64, false>(a, tw, st);
-    return launch_bn<32, false>(a, tw, st);
+    if (bn == 128) return launch_bn<128, false>(a, tw, ap, st);
+    if (bn == 64) return launch_bn<64, false>(a, tw, ap, st);
+    return launch_bn<32, false>(a, tw, ap, st);
 }
 
 }  // namespace sn

@@ -33,7 +33,13 @@ struct TcWeights {
 int tc_prepare(TcWeights* tw, const void* W, int wtype, int N, int K, void* (*alloc)(size_t, void*),
                void* owner);
 
-// True when the tensor-core path supports this problem.
+// Reserve the bf16 activation planes the tensor-core path splits A into, for
+// every contraction with this K and up to `rows` rows. Must run outside CUDA
+// graph capture (it may allocate); the planes are shared by all contractions
+// with the same K, which run in stream order.
+int tc_reserve(int K, long long rows);
+
+// True when the tensor-core path supports this problem (planes reserved).
 bool tc_usable(const GemmArgs& a, const TcWeights* tw);
 
 int launch_tc_gemm(const GemmArgs& a, const TcWeights& tw, cudaStream_t st);
