@@ -14,6 +14,16 @@ int launch_scan(const float* a, const float* b, const float* s0, float* out, flo
                 int T, int N, int gated, cudaStream_t st);
 int launch_step(const float* a, const float* b, float* s, int B, int N, int gated,
                 cudaStream_t st);
+// Scan mode 1 (chunked in T): chunk length for the shape (0 when even one
+// chunk per sequence needs more than `max_records`; <= 0 means no limit),
+// the float2 records it needs, and the three-kernel scan itself. The records
+// need no initial contents: every record is written before it is read within
+// the same call. prof_scopes=false keeps the profiler's events out.
+int scan_chunk_rows(int B, int T, int N, int num_sms, long long max_records);
+long long scan_chunk_records(int B, int T, int N, int L);
+int launch_scan_chunked(const float* a, const float* b, const float* s0, float* out,
+                        float* send, int B, int T, int N, int gated, int L, float2* agg,
+                        cudaStream_t st, bool prof_scopes = true);
 // Y (nseq,out) = W4A8(X (nseq,in)) with codes (out,in/2) and scales (out,in/block)
 int launch_w4a8(float* Y, const float* X, const uint8_t* Wq, const void* scale, int nseq, int in,
                 int out, int block, bool fp16, cudaStream_t st, int epi);

@@ -272,6 +272,196 @@ int launch_scan(const float* a, const float* b, const float* s0, float* out, flo
     }
 }
 
+// ------------------------------------------------------- chunked scan (mode 1)
+// The recurrence is an affine map per row, s -> a*s + b, and affine maps
+// compose associatively: (A1,B1) then (A2,B2) is (A2*A1, A2*B1 + B2). Mode 1
+// cuts T into chunks of L rows and runs three kernels:
+//   agg    thread per (seq, chunk, channel): the chunk's composed map (A, B),
+//          B chained from 0 with the reference's per-row rule
+//   carry  per (seq, channel), over chunks: carry_c = A_c*carry_{c-1} + B_c,
+//          a two-level pass (8 warps split the chunks, a short serial combine
+//          of the 8 warp totals, then each warp re-applies its chunks); the
+//          state entering chunk c replaces A_c in the record
+//   apply  same threads as agg: re-run the chunk's rows from its carry with
+//          the reference rule, write every row; the last chunk writes send
+// Rows are read twice, the second time mostly from L2 (the agg pass just
+// pulled them in). Only the carry entering each chunk is composed, so the
+// outputs differ from the sequential scan by rounding of that composition
+// (a few ulp of the state per chunk boundary), not bit for bit.
+// Record layout: agg[(seq*nch + c)*N + n] = float2 (A or carry, B).
+namespace {
+
+constexpr int kAggRows = 8;  // rows loaded ahead per batch
+
+__device__ __forceinline__ float gate_b(float av, float uv, int gated) {
+    return gated ? __fmul_rn(__fsub_rn(1.0f, av), uv) : uv;
+}
+
+__global__ void __launch_bounds__(256)
+    scan_agg_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                    float2* __restrict__ agg, int T, int N, int nv, int L, int nch, int gated) {
+    pdl_trigger();
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int c = blockIdx.y, sq = blockIdx.z;
+    if (n >= N) return;
+    const int t0 = c * L, rows = min(L, T - t0);
+    const size_t off = ((size_t)sq * T + t0) * N + n;
+    const float* pa = a + off;
+    const float* pb = b + off;
+    const bool fused = n < nv;
+    float A = 1.0f, Bc = 0.0f;
+    int r = 0;
+    for (; r + kAggRows <= rows; r += kAggRows) {
+        float va[kAggRows], vb[kAggRows];
+#pragma unroll
+        for (int j = 0; j < kAggRows; ++j) {
+            va[j] = __ldg(pa + (size_t)(r + j) * N);
+            vb[j] = __ldg(pb + (size_t)(r + j) * N);
+        }
+#pragma unroll
+        for (int j = 0; j < kAggRows; ++j) {
+            const float bv = gate_b(va[j], vb[j], gated);
+            Bc = fused ? rec_fused(va[j], Bc, bv) : rec_split(va[j], Bc, bv);
+            A = __fmul_rn(A, va[j]);
+        }
+    }
+    for (; r < rows; ++r) {
+        const float av = __ldg(pa + (size_t)r * N);
+        const float bv = gate_b(av, __ldg(pb + (size_t)r * N), gated);
+        Bc = fused ? rec_fused(av, Bc, bv) : rec_split(av, Bc, bv);
+        A = __fmul_rn(A, av);
+    }
+    agg[((size_t)sq * nch + c) * N + n] = make_float2(A, Bc);
+}
+
+// Block: 32 channels x 8 warps; warp w owns chunks [w*per, (w+1)*per).
+__global__ void __launch_bounds__(256)
+    scan_carry_kernel(const float* __restrict__ s0, float2* __restrict__ agg, int N, int nch) {
+    __shared__ float2 wtot[8][32];
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int n = blockIdx.x * 32 + lane, sq = blockIdx.y;
+    const bool live = n < N;
+    const int per = (nch + 7) / 8;
+    const int c0 = min(nch, w * per), c1 = min(nch, c0 + per);
+    float2* rec = agg + (size_t)sq * nch * N + n;
+    float A = 1.0f, Bc = 0.0f;  // composition of this warp's chunks
+    if (live) {
+#pragma unroll 8
+        for (int c = c0; c < c1; ++c) {
+            const float2 m = __ldcg(rec + (size_t)c * N);
+            Bc = __fmaf_rn(m.x, Bc, m.y);
+            A = __fmul_rn(m.x, A);
+        }
+    }
+    wtot[w][lane] = make_float2(A, Bc);
+    __syncthreads();
+    float s = live ? s0[(size_t)sq * N + n] : 0.0f;
+    for (int v = 0; v < w; ++v) s = __fmaf_rn(wtot[v][lane].x, s, wtot[v][lane].y);
+    if (live) {
+#pragma unroll 8
+        for (int c = c0; c < c1; ++c) {
+            const float2 m = __ldcg(rec + (size_t)c * N);
+            rec[(size_t)c * N].x = s;
+            s = __fmaf_rn(m.x, s, m.y);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256)
+    scan_apply_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                      const float2* __restrict__ agg, float* __restrict__ out,
+                      float* __restrict__ send, int T, int N, int nv, int L, int nch, int gated) {
+    pdl_wait();
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int c = blockIdx.y, sq = blockIdx.z;
+    if (n >= N) return;
+    const int t0 = c * L, rows = min(L, T - t0);
+    const size_t off = ((size_t)sq * T + t0) * N + n;
+    const float* pa = a + off;
+    const float* pb = b + off;
+    float* po = out + off;
+    const bool fused = n < nv;
+    float s = __ldcg(&agg[((size_t)sq * nch + c) * N + n].x);
+    int r = 0;
+    for (; r + kAggRows <= rows; r += kAggRows) {
+        float va[kAggRows], vb[kAggRows];
+#pragma unroll
+        for (int j = 0; j < kAggRows; ++j) {
+            va[j] = __ldcs(pa + (size_t)(r + j) * N);
+            vb[j] = __ldcs(pb + (size_t)(r + j) * N);
+        }
+#pragma unroll
+        for (int j = 0; j < kAggRows; ++j) {
+            const float bv = gate_b(va[j], vb[j], gated);
+            s = fused ? rec_fused(va[j], s, bv) : rec_split(va[j], s, bv);
+            __stcs(po + (size_t)(r + j) * N, s);
+        }
+    }
+    for (; r < rows; ++r) {
+        const float av = __ldcs(pa + (size_t)r * N);
+        const float bv = gate_b(av, __ldcs(pb + (size_t)r * N), gated);
+        s = fused ? rec_fused(av, s, bv) : rec_split(av, s, bv);
+        __stcs(po + (size_t)r * N, s);
+    }
+    if (c == nch - 1) send[(size_t)sq * N + n] = s;
+}
+
+}  // namespace
+
+// Chunk length for mode 1: enough (seq, chunk, channel) threads to fill
+// `num_sms` SMs about once, between 16 and 256 rows, then longer until the
+// records fit in `max_records` (<= 0: no limit). Returns 0 when even one
+// chunk per sequence does not fit.
+int scan_chunk_rows(int B, int T, int N, int num_sms, long long max_records) {
+    const long long elems = (long long)B * T * N;
+    const long long want = (long long)num_sms * 1024;
+    int L = 16;
+    while (L < 256 && elems / L > want) L *= 2;
+    if (max_records > 0) {
+        while ((long long)B * N * ((T + L - 1) / L) > max_records) {
+            if (L >= T) return 0;
+            L = L > T / 2 ? T : 2 * L;
+        }
+    }
+    return L < T ? L : T;
+}
+
+long long scan_chunk_records(int B, int T, int N, int L) {
+    return (long long)B * N * ((T + L - 1) / L);
+}
+
+int launch_scan_chunked(const float* a, const float* b, const float* s0, float* out,
+                        float* send, int B, int T, int N, int gated, int L, float2* agg,
+                        cudaStream_t st, bool prof_scopes) {
+    if (B > 65535) return fail(SN_E_INVAL, "recur_scan: B=%d exceeds 65535", B);
+    if (L <= 0 || L > T) return fail(SN_E_INVAL, "recur_scan: bad chunk length %d", L);
+    const int nch = (T + L - 1) / L;
+    if (nch > 65535) return fail(SN_E_INVAL, "recur_scan: %d chunks exceed 65535", nch);
+    const int nv = N - N % 8;
+    const int tpb = N >= 256 ? 256 : ((N + 31) / 32) * 32;
+    const dim3 grid((N + tpb - 1) / tpb, nch, B);
+    {
+        ProfScope ps(prof_scopes ? "scan_agg" : nullptr, st);
+        scan_agg_kernel<<<grid, tpb, 0, st>>>(a, b, agg, T, N, nv, L, nch, gated);
+        SN_TRY(cuda_check(cudaGetLastError(), "scan agg launch"));
+    }
+    {
+        ProfScope ps(prof_scopes ? "scan_carry" : nullptr, st);
+        SN_TRY(cuda_check(launch_pdl(scan_carry_kernel, dim3((N + 31) / 32, B), dim3(256), 0, st,
+                                     s0, agg, N, nch),
+                          "scan carry launch"));
+    }
+    {
+        ProfScope ps(prof_scopes ? "scan_apply" : nullptr, st);
+        SN_TRY(cuda_check(launch_pdl(scan_apply_kernel, grid, dim3(tpb), 0, st, a, b,
+                                     (const float2*)agg, out, send, T, N, nv, L, nch, gated),
+                          "scan apply launch"));
+    }
+    return SN_OK;
+}
+
 // ------------------------------------------------------------------- step
 __global__ void step_kernel(const float* __restrict__ a, const float* __restrict__ b,
                             float* __restrict__ s, long long total, int N, int nv, int gated) {
@@ -354,8 +544,18 @@ int do_scan(const float* a, const float* b, const float* s0, float* out, float* 
     SN_TRY(stage_in(s0, small, 2, &S0));
     SN_TRY(stage_out(out, big, 3, &O));
     SN_TRY(stage_out(send, small, 4, &SE));
-    SN_TRY(launch_scan((const float*)A.dev, (const float*)Bv.dev, (const float*)S0.dev,
-                       (float*)O.dev, (float*)SE.dev, B, T, N, gated ? 1 : 0, stream()));
+    if (rt().scan_mode == 1) {
+        const int L = scan_chunk_rows(B, T, N, rt().num_sms, 0);
+        const size_t rb = (size_t)scan_chunk_records(B, T, N, L) * sizeof(float2);
+        void* agg = scratch(10, rb);
+        if (!agg) return fail(SN_E_NOMEM, "recur_scan: %zu bytes of chunk records", rb);
+        SN_TRY(launch_scan_chunked((const float*)A.dev, (const float*)Bv.dev,
+                                   (const float*)S0.dev, (float*)O.dev, (float*)SE.dev, B, T, N,
+                                   gated ? 1 : 0, L, (float2*)agg, stream()));
+    } else {
+        SN_TRY(launch_scan((const float*)A.dev, (const float*)Bv.dev, (const float*)S0.dev,
+                           (float*)O.dev, (float*)SE.dev, B, T, N, gated ? 1 : 0, stream()));
+    }
     SN_TRY(copy_back(O));
     SN_TRY(copy_back(SE));
     return finish(O.host || SE.host || A.dev != a || Bv.dev != b || S0.dev != s0);

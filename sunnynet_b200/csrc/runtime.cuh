@@ -67,7 +67,8 @@ void prof_end(cudaStream_t st);
 struct ProfScope {
     cudaStream_t st;
     bool on;
-    ProfScope(const char* family, cudaStream_t s) : st(s), on(prof_on()) {
+    // family == nullptr: no scope
+    ProfScope(const char* family, cudaStream_t s) : st(s), on(family && prof_on()) {
         if (on) prof_begin(family, st);
     }
     ~ProfScope() {

@@ -19,7 +19,7 @@ from .._lib import check, ptr
 
 __all__ = ["runtime_available", "load_runtime", "FMA", "GATED", "scan", "step", "quant_i8",
            "dequant_i8", "quant_i4", "dequant_i4", "gemv_i4", "gemm_i4", "gemv_f32",
-           "bind_stream"]
+           "bind_stream", "set_scan_mode"]
 
 FMA = 0
 GATED = 1
@@ -58,6 +58,17 @@ def _empty(like, shape, dtype):
                np.float16: torch.float16}[dtype]
         return torch.empty(shape, dtype=tdt, device=like.device)
     return np.empty(shape, dtype)
+
+
+def set_scan_mode(mode: int) -> int:
+    """Select the scan algorithm of ``scan``; returns the previous mode.
+
+    0 (default): sequential in T per channel, bit-identical to the reference.
+    1: chunked in T (per-chunk affine maps composed into the carry entering
+    each chunk), many times more parallel; outputs within a few ulp of the
+    state per chunk boundary of mode 0 instead of bit-identical.
+    """
+    return int(load_runtime().sn_abi_cuda_scan_mode(int(mode)))
 
 
 def scan(a, b, s0, gated=False):
