@@ -71,6 +71,23 @@ sn_status sn_abi_recur_step(const float* a, const float* b, float* s,
 sn_status sn_abi_recur_scan(const float* a, const float* b, const float* s0,
                             float* out, float* send,
                             int32_t B, int32_t T, int32_t N, int32_t gated);
+/* No counterpart in the reference. The chunked scan (the arithmetic of scan
+ * mode 1, within a few ulp per chunk boundary of the bit-exact scan) for
+ * callers that cannot allocate device memory: a process whose device memory
+ * belongs to its own pool allocator, a loop that must not stall on the
+ * device synchronisation cudaMalloc/cudaFree imply, a fixed memory budget.
+ * It calls no allocator: its temporary records live in a fixed 2 MiB array
+ * of the library's device image, held by every GPU that loads the library
+ * until exit. Every array must be device memory; the work is enqueued on
+ * `cuda_stream` (NULL = legacy default stream) and the call returns without
+ * synchronising. Rejects B*N > 262144 with SN_E_INVAL. The first call on a
+ * device looks up the array's device address (make it before any stream
+ * capture). Calls that overlap on the GPU share the array and race: order
+ * them on one stream. Nothing in the array needs to start at zero. */
+sn_status sn_abi_recur_scan_noalloc(const float* a, const float* b, const float* s0,
+                                    float* out, float* send,
+                                    int32_t B, int32_t T, int32_t N, int32_t gated,
+                                    void* cuda_stream);
 /* symmetric per-block INT8; block <= 0 means one block per row. sn_abi.h:83-86 */
 sn_status sn_abi_quant_i8(const float* x, int8_t* q, float* scale,
                           int32_t B, int32_t N, int32_t block);

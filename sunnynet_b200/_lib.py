@@ -26,6 +26,7 @@ SIGNATURES = {
     "sn_abi_get_threads": (I32, []),
     "sn_abi_recur_step": (I32, [V, V, V, I32, I32, I32]),
     "sn_abi_recur_scan": (I32, [V, V, V, V, V, I32, I32, I32, I32]),
+    "sn_abi_recur_scan_noalloc": (I32, [V, V, V, V, V, I32, I32, I32, I32, V]),
     "sn_abi_quant_i8": (I32, [V, V, V, I32, I32, I32]),
     "sn_abi_dequant_i8": (I32, [V, V, V, I32, I32, I32]),
     "sn_abi_rwkv7_load": (V, [P]),
