@@ -316,6 +316,8 @@ def family_cost(S, B, fam, wbytes):
     if fam in shapes:
         n, k = shapes[fam]
         return n * k * wbytes + B * k * 4 + B * n * 4, 2 * B * n * k
+    if fam == "fused_step":  # the whole step in one kernel (B <= 8)
+        return sunny_step_cost(S, B, wbytes, with_head=True)
     return None, None
 
 
@@ -409,7 +411,12 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
     for _ in range(reps):
         m.step(ht, logits=hl)
     e2e_s = dist.max(torch, (time.perf_counter() - t0) / reps)
-    launches = 8 * S.layers + 3  # per layer: prep, 5 GEMMs, gate, row stats; + stats, head, argmax
+    if B <= 8:  # fused step kernel + argmax
+        launches = 2
+    elif B >= 16:  # per layer: prep, 5 x (split + tcgen05 GEMM), gate, row stats; + head, argmax
+        launches = 13 * S.layers + 4
+    else:  # per layer: prep, 5 SIMT GEMMs, gate, row stats; + stats, head, argmax
+        launches = 8 * S.layers + 3
     res.update({
         "ms_per_step": ms,
         "value": B * dist.world / (ms * 1e-3),

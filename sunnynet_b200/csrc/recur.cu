@@ -289,82 +289,121 @@ int launch_scan(const float* a, const float* b, const float* s0, float* out, flo
 // outputs differ from the sequential scan by rounding of that composition
 // (a few ulp of the state per chunk boundary), not bit for bit.
 // Record layout: agg[(seq*nch + c)*N + n] = float2 (A or carry, B).
+// The agg and apply kernels stage their tile (up to kSub rows of the CTA's
+// channels, a and b) in shared memory with cp.async, so a CTA has its whole
+// tile in flight at once instead of a few rows per thread.
 namespace {
 
-constexpr int kAggRows = 8;  // rows loaded ahead per batch
+constexpr int kSub = 32;        // rows staged per round
+constexpr int kScanTile = 128;  // channels per CTA: a 32 KB tile, 7 CTAs per SM
 
 __device__ __forceinline__ float gate_b(float av, float uv, int gated) {
     return gated ? __fmul_rn(__fsub_rn(1.0f, av), uv) : uv;
 }
 
-__global__ void __launch_bounds__(256)
-    scan_agg_kernel(const float* __restrict__ a, const float* __restrict__ b,
-                    float2* __restrict__ agg, int T, int N, int nv, int L, int nch, int gated) {
-    pdl_trigger();
-    const int n = blockIdx.x * blockDim.x + threadIdx.x;
-    const int c = blockIdx.y, sq = blockIdx.z;
-    if (n >= N) return;
-    const int t0 = c * L, rows = min(L, T - t0);
-    const size_t off = ((size_t)sq * T + t0) * N + n;
-    const float* pa = a + off;
-    const float* pb = b + off;
-    const bool fused = n < nv;
-    float A = 1.0f, Bc = 0.0f;
-    int r = 0;
-    for (; r + kAggRows <= rows; r += kAggRows) {
-        float va[kAggRows], vb[kAggRows];
-#pragma unroll
-        for (int j = 0; j < kAggRows; ++j) {
-            va[j] = __ldg(pa + (size_t)(r + j) * N);
-            vb[j] = __ldg(pb + (size_t)(r + j) * N);
+// rows x tpb floats of a and b, starting at element off0 (row stride N,
+// channel n0 of the tile at column 0) -> sa, sb (row stride tpb). Channels
+// >= N are zero-filled. vec: 16-byte copies (N % 4 == 0, 16-byte bases).
+__device__ __forceinline__ void stage_rows(float* sa, float* sb, const float* a, const float* b,
+                                           size_t off0, int rows, int N, int n0, int tpb,
+                                           bool vec) {
+    if (vec) {
+        const int q4 = tpb >> 2;
+        for (int i = threadIdx.x; i < rows * q4; i += blockDim.x) {
+            const int r = i / q4, q = i - r * q4;
+            const bool ok = n0 + 4 * q < N;
+            const size_t g = ok ? off0 + (size_t)r * N + 4 * q : 0;
+            cp_async16(sa + r * tpb + 4 * q, a + g, ok ? 16u : 0u);
+            cp_async16(sb + r * tpb + 4 * q, b + g, ok ? 16u : 0u);
         }
-#pragma unroll
-        for (int j = 0; j < kAggRows; ++j) {
-            const float bv = gate_b(va[j], vb[j], gated);
-            Bc = fused ? rec_fused(va[j], Bc, bv) : rec_split(va[j], Bc, bv);
-            A = __fmul_rn(A, va[j]);
+    } else {
+        for (int i = threadIdx.x; i < rows * tpb; i += blockDim.x) {
+            const int r = i / tpb, ch = i - r * tpb;
+            const bool ok = n0 + ch < N;
+            const size_t g = ok ? off0 + (size_t)r * N + ch : 0;
+            cp_async4(sa + i, a + g, ok ? 4u : 0u);
+            cp_async4(sb + i, b + g, ok ? 4u : 0u);
         }
     }
-    for (; r < rows; ++r) {
-        const float av = __ldg(pa + (size_t)r * N);
-        const float bv = gate_b(av, __ldg(pb + (size_t)r * N), gated);
-        Bc = fused ? rec_fused(av, Bc, bv) : rec_split(av, Bc, bv);
-        A = __fmul_rn(A, av);
-    }
-    agg[((size_t)sq * nch + c) * N + n] = make_float2(A, Bc);
+    cp_async_wait_all();
+    __syncthreads();
 }
 
-// Block: 32 channels x 8 warps; warp w owns chunks [w*per, (w+1)*per).
 __global__ void __launch_bounds__(256)
+    scan_agg_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                    float2* __restrict__ agg, int T, int N, int nv, int L, int nch, int gated,
+                    int vec) {
+    extern __shared__ __align__(16) float stile[];
+    pdl_trigger();
+    const int tpb = blockDim.x;
+    float* sa = stile;
+    float* sb = stile + kSub * tpb;
+    const int n0 = blockIdx.x * tpb, n = n0 + threadIdx.x;
+    const int c = blockIdx.y, sq = blockIdx.z;
+    const int t0 = c * L, rows = min(L, T - t0);
+    const bool fused = n < nv;
+    float A = 1.0f, Bc = 0.0f;
+    for (int r0 = 0; r0 < rows; r0 += kSub) {
+        const int rs = min(kSub, rows - r0);
+        if (r0) __syncthreads();  // the previous round is consumed
+        stage_rows(sa, sb, a, b, ((size_t)sq * T + t0 + r0) * N + n0, rs, N, n0, tpb, vec != 0);
+        for (int r = 0; r < rs; ++r) {
+            const float av = sa[r * tpb + threadIdx.x];
+            const float bv = gate_b(av, sb[r * tpb + threadIdx.x], gated);
+            Bc = fused ? rec_fused(av, Bc, bv) : rec_split(av, Bc, bv);
+            A = __fmul_rn(A, av);
+        }
+    }
+    if (n < N) agg[((size_t)sq * nch + c) * N + n] = make_float2(A, Bc);
+}
+
+// Block: 32 channels x kCarryWarps warps; warp w owns chunks
+// [w*per, (w+1)*per). Records are read kCarryBatch at a time into registers
+// before any of them is used or overwritten, so each batch costs one L2
+// round trip rather than one per chunk.
+constexpr int kCarryWarps = 32;
+constexpr int kCarryBatch = 8;
+
+__global__ void __launch_bounds__(kCarryWarps * 32)
     scan_carry_kernel(const float* __restrict__ s0, float2* __restrict__ agg, int N, int nch) {
-    __shared__ float2 wtot[8][32];
+    __shared__ float2 wtot[kCarryWarps][32];
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int n = blockIdx.x * 32 + lane, sq = blockIdx.y;
     const bool live = n < N;
-    const int per = (nch + 7) / 8;
+    const int per = (nch + kCarryWarps - 1) / kCarryWarps;
     const int c0 = min(nch, w * per), c1 = min(nch, c0 + per);
     float2* rec = agg + (size_t)sq * nch * N + n;
     float A = 1.0f, Bc = 0.0f;  // composition of this warp's chunks
-    if (live) {
-#pragma unroll 8
-        for (int c = c0; c < c1; ++c) {
-            const float2 m = __ldcg(rec + (size_t)c * N);
-            Bc = __fmaf_rn(m.x, Bc, m.y);
-            A = __fmul_rn(m.x, A);
+    for (int cb = c0; cb < c1; cb += kCarryBatch) {
+        float2 m[kCarryBatch];
+#pragma unroll
+        for (int j = 0; j < kCarryBatch; ++j)
+            if (live && cb + j < c1) m[j] = __ldcg(rec + (size_t)(cb + j) * N);
+#pragma unroll
+        for (int j = 0; j < kCarryBatch; ++j) {
+            if (live && cb + j < c1) {
+                Bc = __fmaf_rn(m[j].x, Bc, m[j].y);
+                A = __fmul_rn(m[j].x, A);
+            }
         }
     }
     wtot[w][lane] = make_float2(A, Bc);
     __syncthreads();
     float s = live ? s0[(size_t)sq * N + n] : 0.0f;
     for (int v = 0; v < w; ++v) s = __fmaf_rn(wtot[v][lane].x, s, wtot[v][lane].y);
-    if (live) {
-#pragma unroll 8
-        for (int c = c0; c < c1; ++c) {
-            const float2 m = __ldcg(rec + (size_t)c * N);
-            rec[(size_t)c * N].x = s;
-            s = __fmaf_rn(m.x, s, m.y);
+    for (int cb = c0; cb < c1; cb += kCarryBatch) {
+        float2 m[kCarryBatch];
+#pragma unroll
+        for (int j = 0; j < kCarryBatch; ++j)
+            if (live && cb + j < c1) m[j] = __ldcg(rec + (size_t)(cb + j) * N);
+#pragma unroll
+        for (int j = 0; j < kCarryBatch; ++j) {
+            if (live && cb + j < c1) {
+                rec[(size_t)(cb + j) * N].x = s;
+                s = __fmaf_rn(m[j].x, s, m[j].y);
+            }
         }
     }
 }
@@ -372,51 +411,47 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     scan_apply_kernel(const float* __restrict__ a, const float* __restrict__ b,
                       const float2* __restrict__ agg, float* __restrict__ out,
-                      float* __restrict__ send, int T, int N, int nv, int L, int nch, int gated) {
-    pdl_wait();
-    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+                      float* __restrict__ send, int T, int N, int nv, int L, int nch, int gated,
+                      int vec) {
+    extern __shared__ __align__(16) float stile[];
+    const int tpb = blockDim.x;
+    float* sa = stile;
+    float* sb = stile + kSub * tpb;
+    const int n0 = blockIdx.x * tpb, n = n0 + threadIdx.x;
     const int c = blockIdx.y, sq = blockIdx.z;
-    if (n >= N) return;
     const int t0 = c * L, rows = min(L, T - t0);
-    const size_t off = ((size_t)sq * T + t0) * N + n;
-    const float* pa = a + off;
-    const float* pb = b + off;
-    float* po = out + off;
     const bool fused = n < nv;
-    float s = __ldcg(&agg[((size_t)sq * nch + c) * N + n].x);
-    int r = 0;
-    for (; r + kAggRows <= rows; r += kAggRows) {
-        float va[kAggRows], vb[kAggRows];
-#pragma unroll
-        for (int j = 0; j < kAggRows; ++j) {
-            va[j] = __ldcs(pa + (size_t)(r + j) * N);
-            vb[j] = __ldcs(pb + (size_t)(r + j) * N);
+    const size_t base = ((size_t)sq * T + t0) * N;
+    // a and b were complete before the agg kernel started: stage the first
+    // round while the carry kernel still runs, then wait for the carries
+    stage_rows(sa, sb, a, b, base + n0, min(kSub, rows), N, n0, tpb, vec != 0);
+    pdl_wait();
+    float s = n < N ? __ldcg(&agg[((size_t)sq * nch + c) * N + n].x) : 0.0f;
+    for (int r0 = 0; r0 < rows; r0 += kSub) {
+        const int rs = min(kSub, rows - r0);
+        if (r0) {
+            __syncthreads();
+            stage_rows(sa, sb, a, b, base + (size_t)r0 * N + n0, rs, N, n0, tpb, vec != 0);
         }
-#pragma unroll
-        for (int j = 0; j < kAggRows; ++j) {
-            const float bv = gate_b(va[j], vb[j], gated);
-            s = fused ? rec_fused(va[j], s, bv) : rec_split(va[j], s, bv);
-            __stcs(po + (size_t)(r + j) * N, s);
+        for (int r = 0; r < rs; ++r) {
+            const float av = sa[r * tpb + threadIdx.x];
+            const float bv = gate_b(av, sb[r * tpb + threadIdx.x], gated);
+            s = fused ? rec_fused(av, s, bv) : rec_split(av, s, bv);
+            if (n < N) __stcs(out + base + (size_t)(r0 + r) * N + n, s);
         }
     }
-    for (; r < rows; ++r) {
-        const float av = __ldcs(pa + (size_t)r * N);
-        const float bv = gate_b(av, __ldcs(pb + (size_t)r * N), gated);
-        s = fused ? rec_fused(av, s, bv) : rec_split(av, s, bv);
-        __stcs(po + (size_t)r * N, s);
-    }
-    if (c == nch - 1) send[(size_t)sq * N + n] = s;
+    if (c == nch - 1 && n < N) send[(size_t)sq * N + n] = s;
 }
 
 }  // namespace
 
-// Chunk length for mode 1: enough (seq, chunk, channel) threads to fill
-// `num_sms` SMs about once, between 16 and 256 rows, then longer until the
-// records fit in `max_records` (<= 0: no limit). Returns 0 when even one
-// chunk per sequence does not fit.
+// Chunk length for mode 1: the shortest (16..256 rows) whose (seq, chunk,
+// channel) threads fit in one wave of 128-thread CTAs at 7 per SM, then
+// longer until the records fit in `max_records` (<= 0: no limit). Returns 0
+// when even one chunk per sequence does not fit.
 int scan_chunk_rows(int B, int T, int N, int num_sms, long long max_records) {
     const long long elems = (long long)B * T * N;
-    const long long want = (long long)num_sms * 1024;
+    const long long want = (long long)num_sms * 7 * 128;
     int L = 16;
     while (L < 256 && elems / L > want) L *= 2;
     if (max_records > 0) {
@@ -440,23 +475,36 @@ int launch_scan_chunked(const float* a, const float* b, const float* s0, float* 
     const int nch = (T + L - 1) / L;
     if (nch > 65535) return fail(SN_E_INVAL, "recur_scan: %d chunks exceed 65535", nch);
     const int nv = N - N % 8;
-    const int tpb = N >= 256 ? 256 : ((N + 31) / 32) * 32;
+    const int tpb = N >= kScanTile ? kScanTile : ((N + 31) / 32) * 32;
     const dim3 grid((N + tpb - 1) / tpb, nch, B);
+    const size_t smem = 2ull * kSub * tpb * sizeof(float);
+    const int vec = N % 4 == 0 && (uintptr_t)a % 16 == 0 && (uintptr_t)b % 16 == 0;
+    static const cudaError_t attr_rc = [] {  // once per process (thread-safe init)
+        const int mx = (int)(2ull * kSub * kScanTile * sizeof(float));
+        cudaError_t e = cudaFuncSetAttribute(scan_agg_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(scan_apply_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
+        return e;
+    }();
+    SN_TRY(cuda_check(attr_rc, "scan smem attribute"));
     {
         ProfScope ps(prof_scopes ? "scan_agg" : nullptr, st);
-        scan_agg_kernel<<<grid, tpb, 0, st>>>(a, b, agg, T, N, nv, L, nch, gated);
+        scan_agg_kernel<<<grid, tpb, smem, st>>>(a, b, agg, T, N, nv, L, nch, gated, vec);
         SN_TRY(cuda_check(cudaGetLastError(), "scan agg launch"));
     }
     {
         ProfScope ps(prof_scopes ? "scan_carry" : nullptr, st);
-        SN_TRY(cuda_check(launch_pdl(scan_carry_kernel, dim3((N + 31) / 32, B), dim3(256), 0, st,
-                                     s0, agg, N, nch),
+        SN_TRY(cuda_check(launch_pdl(scan_carry_kernel, dim3((N + 31) / 32, B),
+                                     dim3(kCarryWarps * 32), 0, st, s0, agg, N, nch),
                           "scan carry launch"));
     }
     {
         ProfScope ps(prof_scopes ? "scan_apply" : nullptr, st);
-        SN_TRY(cuda_check(launch_pdl(scan_apply_kernel, grid, dim3(tpb), 0, st, a, b,
-                                     (const float2*)agg, out, send, T, N, nv, L, nch, gated),
+        SN_TRY(cuda_check(launch_pdl(scan_apply_kernel, grid, dim3(tpb), smem, st, a, b,
+                                     (const float2*)agg, out, send, T, N, nv, L, nch, gated,
+                                     vec),
                           "scan apply launch"));
     }
     return SN_OK;

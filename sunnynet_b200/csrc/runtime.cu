@@ -160,6 +160,7 @@ struct Prof {
     std::vector<cudaEvent_t> pool;
     std::string open;
     cudaEvent_t open_ev = nullptr;
+    std::map<std::string, std::pair<int, double>> extra;  // prof_add (device timestamps)
 };
 Prof& prof() {
     static Prof p;
@@ -199,6 +200,12 @@ void prof_end(cudaStream_t st) {
     p.recs.push_back({p.open, p.open_ev, e});
 }
 
+void prof_add(const char* family, int launches, double ms) {
+    auto& a = prof().extra[family];
+    a.first += launches;
+    a.second += ms;
+}
+
 }  // namespace sn
 
 using namespace sn;
@@ -215,6 +222,7 @@ sn_status sn_abi_cuda_profile(int32_t on) {
             p.pool.push_back(r.b);
         }
         p.recs.clear();
+        p.extra.clear();
     }
     p.on = on != 0;
     return SN_OK;
@@ -231,6 +239,11 @@ int32_t sn_abi_cuda_profile_report(char* buf, int32_t buflen) {
         auto& a = agg[r.family];
         a.first += 1;
         a.second += ms;
+    }
+    for (auto& kv : p.extra) {
+        auto& a = agg[kv.first];
+        a.first += kv.second.first;
+        a.second += kv.second.second;
     }
     std::string s = "{";
     for (auto& kv : agg) {

@@ -63,6 +63,8 @@ inline int grid_blocks(long long total, int threads = 256, int per_sm = 8) {
 bool prof_on();
 void prof_begin(const char* family, cudaStream_t st);
 void prof_end(cudaStream_t st);
+// Add a family measured another way (e.g. device timestamps) to the report.
+void prof_add(const char* family, int launches, double ms);
 
 struct ProfScope {
     cudaStream_t st;

@@ -37,6 +37,7 @@
 #include "ptx.cuh"
 #include "runtime.cuh"
 #include "sn_abi.h"
+#include "sunny_fused.cuh"
 #include "sunnynet.h"
 #include "tc_gemm.cuh"
 
@@ -392,6 +393,12 @@ struct SunnyModel {
     float *cz = nullptr, *cmu = nullptr, *crs = nullptr, *cs0 = nullptr, *csend = nullptr;
     std::map<std::pair<long long, int>, cudaGraphExec_t> cgraphs;  // (B*65536+Tc, head)
     cudaStream_t cap = nullptr;
+    // fused small-batch step (sunny_fused.cu): per-layer descriptors on the
+    // device, barrier words, and the arguments common to every launch
+    FusedLayer* dlayers = nullptr;
+    unsigned* fbar = nullptr;
+    unsigned long long* ftrace = nullptr;  // profile mode: phase timestamps
+    FusedArgs fbase;
     bool ready = false;
 
     ~SunnyModel() {
@@ -621,6 +628,36 @@ int load_model(SunnyModel* m, const char* path, int nseq, bool half, const int* 
     cudaMemset(m->s, 0, n * L * D * 4);
     cudaMemset(m->hist, 0, n * L * m->KH * D * 4);
     cudaMemset(m->pos, 0, n * L * 4);
+    {   // fused small-batch step: layer descriptors and barrier words
+        std::vector<FusedLayer> fl(L);
+        for (int l = 0; l < L; ++l) {
+            const SunnyLayer& y = m->ly[l];
+            fl[l] = FusedLayer{y.ni_g, y.ni_c, y.nm_g, y.nm_c, y.dw, y.delta, y.V, y.U, y.Wz,
+                               y.Wc, y.Ws, y.sV, y.sU, y.sWz, y.sWc, y.sWs, y.a_tanh, y.b_gain};
+        }
+        m->dlayers = m->dalloc<FusedLayer>(L);
+        m->fbar = m->dalloc<unsigned>(kBarWords);
+        m->ftrace = m->dalloc<unsigned long long>((size_t)rt().num_sms * (8 * L + 2));
+        if (!m->dlayers || !m->fbar || !m->ftrace)
+            return fail(SN_E_NOMEM, "device allocation failed");
+        SN_TRY(cuda_check(cudaMemcpy(m->dlayers, fl.data(), L * sizeof(FusedLayer),
+                                     cudaMemcpyHostToDevice),
+                          "layer descriptors"));
+        FusedArgs& f = m->fbase;
+        f.D = D; f.I = I; f.R = R; f.K = m->K; f.KH = m->KH; f.L = L; f.G = m->G;
+        f.vocab = vocab; f.clamp = m->clamp; f.wtype = m->wtype;
+        f.ctas = rt().num_sms;
+        f.bulk_prefetch = getenv("SN_FUSED_NO_PREFETCH") ? 0 : 1;
+        f.eps = m->eps; f.p_floor = m->p_floor;
+        f.layers = m->dlayers;
+        f.no_g = m->no_g; f.no_c = m->no_c; f.embed = m->embed;
+        f.head = m->head; f.shead = m->shead;
+        f.s = m->s; f.hist = m->hist; f.pos = m->pos; f.tok = m->tok;
+        f.x = m->x; f.v = m->v; f.u = m->u; f.sfb = m->sfb; f.z = m->z;
+        f.logits = m->logits;
+        f.bar = m->fbar;
+        f.err = rt().d_err;
+    }
     SN_TRY(cuda_check(cudaDeviceSynchronize(), "load"));
     m->ready = true;
     return SN_OK;
@@ -725,9 +762,65 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
     return cuda_check(cudaGetLastError(), "step launch");
 }
 
+// Profile mode: per-phase times of one fused step from its device timestamps
+// (%globaltimer, ns). A phase's time is the slowest CTA's (phase end - its own
+// start); a barrier's is (last CTA out) - (last CTA in).
+int fused_trace_report(SunnyModel* m, const FusedArgs& fa, cudaStream_t st) {
+    const int n = rt().num_sms, S = fa.trace_slots, L = m->L;
+    std::vector<unsigned long long> t((size_t)n * S);
+    SN_TRY(cuda_check(cudaMemcpyAsync(t.data(), fa.trace, t.size() * sizeof(t[0]),
+                                      cudaMemcpyDeviceToHost, st),
+                      "fused trace"));
+    SN_TRY(cuda_check(cudaStreamSynchronize(st), "fused trace"));
+    auto last = [&](int e) {
+        unsigned long long v = 0;
+        for (int c = 0; c < n; ++c) v = t[(size_t)c * S + e] > v ? t[(size_t)c * S + e] : v;
+        return v;
+    };
+    auto span = [&](int e0, int e1) {
+        long long w = 0;
+        for (int c = 0; c < n; ++c) {
+            const long long d = (long long)(t[(size_t)c * S + e1] - t[(size_t)c * S + e0]);
+            w = d > w ? d : w;
+        }
+        return w;
+    };
+    static const char* names[4] = {"fused:P1_ln_taps_V_Ws", "fused:P2_U_gate_state",
+                                   "fused:P3_Wz", "fused:P4_lnz_Wc_resid"};
+    double bar_ns = 0.0;
+    int nbar = 0;
+    for (int l = 0; l < L; ++l)
+        for (int k = 0; k < 4; ++k) {
+            const int e = 1 + 8 * l + 2 * k;
+            prof_add(names[k], 1, span(e - 1, e) * 1e-6);
+            if (l + 1 < L || k < 3 || fa.with_head) {
+                bar_ns += (double)(last(e + 1) - last(e));
+                ++nbar;
+            }
+        }
+    if (fa.with_head) prof_add("fused:head", 1, span(8 * L, 8 * L + 1) * 1e-6);
+    prof_add("fused:barriers", nbar, bar_ns * 1e-6);
+    return SN_OK;
+}
+
 // Replay (capturing on first use) the graph of a B-sequence step.
 int run_step(SunnyModel* m, int B, bool with_head) {
     cudaStream_t st = stream();
+    if (B <= kFusedMaxB && !getenv("SN_DISABLE_FUSED")) {  // one persistent kernel per step
+        FusedArgs fa = m->fbase;
+        fa.B = B;
+        fa.with_head = with_head ? 1 : 0;
+        if (fused_smem_bytes(fa)) {
+            if (!prof_on()) return launch_sunny_fused(fa, st);
+            fa.trace = m->ftrace;
+            fa.trace_slots = 8 * m->L + 2;
+            {
+                ProfScope ps("fused_step", st);
+                SN_TRY(launch_sunny_fused(fa, st));
+            }
+            return fused_trace_report(m, fa, st);
+        }
+    }
     if (prof_on()) return enqueue_step(m, B, with_head, st);  // bracket kernels, no graph
     auto key = std::make_pair(B, with_head ? 1 : 0);
     auto it = m->graphs.find(key);

@@ -276,3 +276,83 @@ def test_half_weights_track_fp32(golden):
         worst = max(worst, float(np.abs(la - lb).max()))
         assert np.isfinite(lb).all()
     assert worst < 2e-2
+
+
+# --------------------------------------------- fused small-batch step (B <= 8)
+def _steps(blob, B, toks_seq, fused):
+    """Logits of each step and the final state, with the fused persistent step
+    or the multi-kernel step (the fused one is taken for B <= 8 unless
+    SN_DISABLE_FUSED is set; the library reads it at every step)."""
+    import os
+    from sunnynet_b200.model import SunnyBatch
+    m = SunnyBatch(blob, B)
+    old = os.environ.pop("SN_DISABLE_FUSED", None)
+    try:
+        if not fused:
+            os.environ["SN_DISABLE_FUSED"] = "1"
+        lgs = [m.step(t).copy() for t in toks_seq]
+        s, h = m.get_state()
+    finally:
+        os.environ.pop("SN_DISABLE_FUSED", None)
+        if old is not None:
+            os.environ["SN_DISABLE_FUSED"] = old
+    return lgs, s, h
+
+
+@pytest.mark.parametrize("B", [1, 8])
+@pytest.mark.parametrize("preset,quant", [("c2", False), ("mid", True), ("mid", False)])
+def test_fused_step_matches_multi_kernel_step(B, preset, quant):
+    """The one-kernel step (grid barriers between phases) against the
+    multi-kernel step on the same tokens: logits and states within 1e-4."""
+    from sunnynet_b200 import formats
+    shape = (formats.SUNNY_PRESETS["c2"] if preset == "c2"
+             else formats.SunnyShape(2000, 128, 224, 80, 4, 3))
+    rng = np.random.default_rng(B + 10 * quant)
+    toks = [rng.integers(0, shape.vocab, B).astype(np.int32) for _ in range(5)]
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape, quant=quant, seed=2, fast=True)
+        lf, sf, hf = _steps(p, B, toks, fused=True)
+        lm, sm, hm = _steps(p, B, toks, fused=False)
+    for a, b in zip(lf, lm):
+        check_logits(a, b)
+    assert rel_err(sf, sm) < TOL and rel_err(hf, hm) < TOL
+
+
+def test_config3_shape_int8_fused_vs_oracle():
+    """BASELINE config 3 shape (INT8 per-row) at B=2: the fused step's int8
+    weight rows against the oracle."""
+    from sunnynet_b200 import formats
+    from sunnynet_b200.model import SunnyBatch
+    shape = formats.SUNNY_PRESETS["c3"]
+    rng = np.random.default_rng(7)
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape, quant=True, seed=1, fast=True)
+        gm, om = SunnyBatch(p, 2), oracle.Sunny(p, 2)
+        for _ in range(3):
+            toks = rng.integers(0, shape.vocab, 2).astype(np.int32)
+            check_logits(gm.step(toks), om.step(toks))
+
+
+@pytest.mark.parametrize("B", [2, 16])
+def test_bad_token_id_is_reported_and_handle_stays_usable(B):
+    """A token id outside the vocabulary is never read from the table: the
+    step reports SN_E_DEVICE (the device-side index check) and the next step
+    with valid ids runs normally (fused path at B=2, multi-kernel at B=16)."""
+    from sunnynet_b200 import formats
+    from sunnynet_b200._lib import SnError
+    from sunnynet_b200.model import SunnyBatch
+    shape = formats.SunnyShape(512, 64, 96, 32, 4, 2)
+    rng = np.random.default_rng(5)
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape)
+        m = SunnyBatch(p, B)
+        bad = rng.integers(0, 512, B).astype(np.int32)
+        bad[B // 2] = 512 + 7
+        with pytest.raises(SnError) as ei:
+            m.step(bad)
+        assert ei.value.code == -6
+        m.reset()
+        om = oracle.Sunny(p, B)
+        for _ in range(3):
+            toks = rng.integers(0, 512, B).astype(np.int32)
+            check_logits(m.step(toks), om.step(toks))
