@@ -27,6 +27,14 @@ int launch_scan_chunked(const float* a, const float* b, const float* s0, float* 
 // Y (nseq,out) = W4A8(X (nseq,in)) with codes (out,in/2) and scales (out,in/block)
 int launch_w4a8(float* Y, const float* X, const uint8_t* Wq, const void* scale, int nseq, int in,
                 int out, int block, bool fp16, cudaStream_t st, int epi);
+// The same contraction on the tensor cores (w4a8_tc.cu) for M >= 16 sequences,
+// K % 128 == 0, block in {32, 64, 128}: bit-identical results. Its activation
+// workspace is reserved outside graph capture (w4a8_tc_reserve) before use.
+bool w4a8_tc_ok(int M, int K, int N, int block, const void* Wq);
+bool w4a8_tc_ready(int M, int K, int block);
+int w4a8_tc_reserve(int M, int K, int block);
+int launch_w4a8_tc(float* Y, const float* X, const uint8_t* Wq, const void* scale, int M, int K,
+                   int N, int block, bool fp16, int epi, cudaStream_t st);
 int launch_gemv_f32(float* y, const float* x, const float* W, int in, int out, cudaStream_t st);
 int launch_quant_i4(const float* x, uint8_t* q, void* scale, int rows, int N, int block,
                     bool fp16, cudaStream_t st);

@@ -267,6 +267,8 @@ __global__ void gemv_f32_kernel(float* __restrict__ y, const float* __restrict__
 // and by the RWKV-7 model.
 int launch_w4a8(float* Y, const float* X, const uint8_t* Wq, const void* scale, int nseq, int in,
                 int out, int block, bool fp16, cudaStream_t st, int epi) {
+    if (w4a8_tc_ok(nseq, in, out, block, Wq) && w4a8_tc_ready(nseq, in, block))
+        return launch_w4a8_tc(Y, X, Wq, scale, nseq, in, out, block, fp16, epi, st);
     const int nb = in / block;
     const size_t smem = (size_t)kMaxSeqTile * in + (size_t)kMaxSeqTile * nb * 8 + 16;
     if (smem > 200 * 1024) return fail(SN_E_INVAL, "gemv_i4: in=%d too large", in);
@@ -376,6 +378,7 @@ int do_gemm_i4(float* Y, const float* X, const uint8_t* Wq, const void* scale, i
     SN_TRY(stage_in(Wq, (size_t)out * (in / 2), 1, &Q));
     SN_TRY(stage_in(scale, ns, 2, &S));
     SN_TRY(stage_out(Y, (size_t)B * out * 4, 3, &Ya));
+    if (w4a8_tc_ok(B, in, out, block, Q.dev)) SN_TRY(w4a8_tc_reserve(B, in, block));
     SN_TRY(launch_w4a8((float*)Ya.dev, (const float*)Xa.dev, (const uint8_t*)Q.dev, S.dev, B, in,
                        out, block, fp16 != 0, stream(), kW4Store));
     SN_TRY(copy_back(Ya));

@@ -518,6 +518,17 @@ int load_rwkv(RwkvModel* m, const char* path, int nseq) {
     cudaMemset(m->S, 0, B * L * m->NH * m->HS * m->HS * 4);
     cudaMemset(m->shift, 0, B * L * 2 * D * 4);
     SN_TRY(cuda_check(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking), "stream"));
+    {   // activation workspace of the tensor-core W4A8 path, before any capture
+        auto reserve = [&](const RkMat& M) -> int {
+            if (!M.q4 || !w4a8_tc_ok(nseq, M.in, M.out, M.block, M.q)) return SN_OK;
+            return w4a8_tc_reserve(nseq, M.in, M.block);
+        };
+        for (const RkLayer& y : m->ly)
+            for (const RkMat* M : {&y.rw, &y.kw, &y.vw, &y.ow, &y.w1, &y.w2, &y.a1, &y.a2, &y.v1,
+                                   &y.v2, &y.g1, &y.g2, &y.cmk, &y.cmv})
+                SN_TRY(reserve(*M));
+        SN_TRY(reserve(m->head));
+    }
     SN_TRY(cuda_check(cudaDeviceSynchronize(), "rwkv load"));
     m->ready = true;
     return SN_OK;

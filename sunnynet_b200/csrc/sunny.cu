@@ -637,7 +637,7 @@ int load_model(SunnyModel* m, const char* path, int nseq, bool half, const int* 
         }
         m->dlayers = m->dalloc<FusedLayer>(L);
         m->fbar = m->dalloc<unsigned>(kBarWords);
-        m->ftrace = m->dalloc<unsigned long long>((size_t)rt().num_sms * (8 * L + 2));
+        m->ftrace = m->dalloc<unsigned long long>((size_t)rt().num_sms * 2 * (32 * L + 9));
         if (!m->dlayers || !m->fbar || !m->ftrace)
             return fail(SN_E_NOMEM, "device allocation failed");
         SN_TRY(cuda_check(cudaMemcpy(m->dlayers, fl.data(), L * sizeof(FusedLayer),
@@ -763,42 +763,58 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
 }
 
 // Profile mode: per-phase times of one fused step from its device timestamps
-// (%globaltimer, ns). A phase's time is the slowest CTA's (phase end - its own
-// start); a barrier's is (last CTA out) - (last CTA in).
+// (slot 1+8p+j of phase p: j = 0 loads done, 1 row statistics done, 2 inputs
+// ready, 3 weights ready, 4 rows done, 5 barrier passed). A part's time is the
+// slowest CTA's span in its own clock64 cycles; a barrier's is (last CTA out)
+// - (last CTA in) on %globaltimer.
 int fused_trace_report(SunnyModel* m, const FusedArgs& fa, cudaStream_t st) {
     const int n = rt().num_sms, S = fa.trace_slots, L = m->L;
-    std::vector<unsigned long long> t((size_t)n * S);
+    std::vector<unsigned long long> t((size_t)n * 2 * S);  // [cta][globaltimer S | clock64 S]
     SN_TRY(cuda_check(cudaMemcpyAsync(t.data(), fa.trace, t.size() * sizeof(t[0]),
                                       cudaMemcpyDeviceToHost, st),
                       "fused trace"));
     SN_TRY(cuda_check(cudaStreamSynchronize(st), "fused trace"));
+    int khz = 0;  // SM clock for the cycle spans
+    cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, rt().device);
+    const double ms_per_cycle = khz > 0 ? 1.0 / khz : 0.0;
     auto last = [&](int e) {
         unsigned long long v = 0;
-        for (int c = 0; c < n; ++c) v = t[(size_t)c * S + e] > v ? t[(size_t)c * S + e] : v;
+        for (int c = 0; c < n; ++c) {
+            const unsigned long long x = t[(size_t)c * 2 * S + e];
+            v = x > v ? x : v;
+        }
         return v;
     };
-    auto span = [&](int e0, int e1) {
+    auto span = [&](int e0, int e1) {  // slowest CTA, in its own cycles
         long long w = 0;
         for (int c = 0; c < n; ++c) {
-            const long long d = (long long)(t[(size_t)c * S + e1] - t[(size_t)c * S + e0]);
+            const unsigned long long* ck = &t[(size_t)c * 2 * S + S];
+            const long long d = (long long)(ck[e1] - ck[e0]);
             w = d > w ? d : w;
         }
-        return w;
+        return w * ms_per_cycle;
     };
-    static const char* names[4] = {"fused:P1_ln_taps_V_Ws", "fused:P2_U_gate_state",
-                                   "fused:P3_Wz", "fused:P4_lnz_Wc_resid"};
+    static const char* names[5] = {"P1_ln_taps_V_Ws", "P2_U_gate_state", "P3_Wz",
+                                   "P4_lnz_Wc_resid", "head"};
     double bar_ns = 0.0;
     int nbar = 0;
-    for (int l = 0; l < L; ++l)
-        for (int k = 0; k < 4; ++k) {
-            const int e = 1 + 8 * l + 2 * k;
-            prof_add(names[k], 1, span(e - 1, e) * 1e-6);
-            if (l + 1 < L || k < 3 || fa.with_head) {
-                bar_ns += (double)(last(e + 1) - last(e));
-                ++nbar;
-            }
+    static const char* parts[5] = {"loads", "stats", "ln", "wait_w", "rows"};
+    for (int p = 0; p <= 4 * L; ++p) {
+        if (p == 4 * L && !fa.with_head) break;
+        const int k = p == 4 * L ? 4 : p % 4;
+        int prev = p == 0 ? 0 : 1 + 8 * (p - 1) + 5;  // start: previous barrier passed
+        for (int j = 0; j < 5; ++j) {
+            const int e = 1 + 8 * p + j;
+            char name[64];
+            snprintf(name, sizeof name, "fused:%s.%s", names[k], parts[j]);
+            prof_add(name, 1, span(prev, e));
+            prev = e;
         }
-    if (fa.with_head) prof_add("fused:head", 1, span(8 * L, 8 * L + 1) * 1e-6);
+        if (p < 4 * L && (p + 1 < 4 * L || fa.with_head)) {
+            bar_ns += (double)(last(1 + 8 * p + 5) - last(1 + 8 * p + 4));
+            ++nbar;
+        }
+    }
     prof_add("fused:barriers", nbar, bar_ns * 1e-6);
     return SN_OK;
 }
@@ -806,21 +822,6 @@ int fused_trace_report(SunnyModel* m, const FusedArgs& fa, cudaStream_t st) {
 // Replay (capturing on first use) the graph of a B-sequence step.
 int run_step(SunnyModel* m, int B, bool with_head) {
     cudaStream_t st = stream();
-    if (B <= kFusedMaxB && !getenv("SN_DISABLE_FUSED")) {  // one persistent kernel per step
-        FusedArgs fa = m->fbase;
-        fa.B = B;
-        fa.with_head = with_head ? 1 : 0;
-        if (fused_smem_bytes(fa)) {
-            if (!prof_on()) return launch_sunny_fused(fa, st);
-            fa.trace = m->ftrace;
-            fa.trace_slots = 8 * m->L + 2;
-            {
-                ProfScope ps("fused_step", st);
-                SN_TRY(launch_sunny_fused(fa, st));
-            }
-            return fused_trace_report(m, fa, st);
-        }
-    }
     if (prof_on()) return enqueue_step(m, B, with_head, st);  // bracket kernels, no graph
     auto key = std::make_pair(B, with_head ? 1 : 0);
     auto it = m->graphs.find(key);
@@ -1028,11 +1029,49 @@ int sunny_step(SunnyModel* m, const int32_t* tokens, int B, float* logits, int32
     std::lock_guard<std::recursive_mutex> lk(rt().mu);
     cudaStream_t st = stream();
     const bool tok_dev = is_device_ptr(tokens);
+    const bool head = logits != nullptr || next != nullptr;
+    if (B <= kFusedMaxB && !getenv("SN_DISABLE_FUSED")) {
+        // one persistent kernel per step; it reads the caller's device tokens
+        // and writes device logits / next tokens (greedy argmax fused) in place
+        FusedArgs fa = m->fbase;
+        fa.B = B;
+        fa.with_head = head ? 1 : 0;
+        if (fused_plan(&fa, !getenv("SN_FUSED_NO_STAGE"))) {
+            if (!tok_dev)
+                SN_TRY(cuda_check(cudaMemcpyAsync(m->tok, tokens, (size_t)B * 4,
+                                                  cudaMemcpyHostToDevice, st),
+                                  "tokens"));
+            const bool lg_dev = logits && is_device_ptr(logits);
+            const bool nx_dev = next && is_device_ptr(next);
+            fa.tok = tok_dev ? tokens : m->tok;
+            fa.logits = logits ? (lg_dev ? logits : m->logits) : nullptr;
+            fa.next = next ? (nx_dev ? next : m->next) : nullptr;
+            if (prof_on()) {
+                fa.trace = m->ftrace;
+                fa.trace_slots = 32 * m->L + 9;
+                {
+                    ProfScope ps("fused_step", st);
+                    SN_TRY(launch_sunny_fused(fa, st));
+                }
+                SN_TRY(fused_trace_report(m, fa, st));
+            } else {
+                SN_TRY(launch_sunny_fused(fa, st));
+            }
+            if (logits && !lg_dev)
+                SN_TRY(cuda_check(cudaMemcpyAsync(logits, m->logits, (size_t)B * m->vocab * 4,
+                                                  cudaMemcpyDeviceToHost, st),
+                                  "logits"));
+            if (next && !nx_dev)
+                SN_TRY(cuda_check(cudaMemcpyAsync(next, m->next, (size_t)B * 4,
+                                                  cudaMemcpyDeviceToHost, st),
+                                  "next"));
+            return finish(!tok_dev || (logits && !lg_dev) || (next && !nx_dev));
+        }
+    }
     SN_TRY(cuda_check(cudaMemcpyAsync(m->tok, tokens, (size_t)B * 4,
                                       tok_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
                                       st),
                       "tokens"));
-    const bool head = logits != nullptr || next != nullptr;
     SN_TRY(run_step(m, B, head));
     bool host = !tok_dev;
     if (logits) {

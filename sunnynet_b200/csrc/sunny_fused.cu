@@ -22,9 +22,14 @@
 //   P4  LN statistics of z (redundantly per CTA), its slice of Wc with the
 //       residual epilogue into x
 // and the head is one more phase. Each CTA owns contiguous row ranges, so
-// its weights for a phase are one or two contiguous byte ranges: thread 0
-// prefetches them into L2 (cp.async.bulk.prefetch) kPrefetchAhead phases
-// before they are read, and the HBM stream runs under the barrier chain.
+// its weights for a phase are one or two contiguous byte ranges. Staged
+// variant (the slices fit two shared-memory buffers): at the start of phase
+// p thread 0 bulk-copies phase p+1's ranges into the buffer phase p-1 used
+// (cp.async.bulk, completion on that buffer's mbarrier), so each phase finds
+// its weights on chip and the HBM stream runs under the barrier chain; the
+// head (largest slice) is read from global memory behind an L2 prefetch
+// issued a layer ahead. Unstaged variant: every phase reads global memory
+// behind cp.async.bulk.prefetch.L2 hints issued kPrefetchAhead phases ahead.
 // Within a phase a warp takes two weight rows at a time so their loads
 // overlap; loads that do not depend on the phase's dot products (ring rows,
 // residual terms) are issued with the phase inputs.
@@ -40,6 +45,8 @@
 // mode thread 0 of every CTA records %globaltimer at each phase end and
 // barrier exit (FusedArgs::trace).
 #include <cuda_fp16.h>
+
+#include <algorithm>
 
 #include "gemm.cuh"
 #include "ptx.cuh"
@@ -106,11 +113,15 @@ __device__ bool grid_sync(unsigned* bar, unsigned k, int* err) {
     return ok != 0;
 }
 
+// Profile mode: %globaltimer (shared time base, ~1 us ticks) and clock64
+// (this SM's cycles, fine-grained) at mark e of this CTA.
 __device__ __forceinline__ void trace_mark(const FusedArgs& a, int e) {
     if (a.trace && threadIdx.x == 0) {
         unsigned long long t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        a.trace[(size_t)blockIdx.x * a.trace_slots + e] = t;
+        unsigned long long* row = a.trace + (size_t)blockIdx.x * 2 * a.trace_slots;
+        row[e] = t;
+        row[a.trace_slots + e] = (unsigned long long)clock64();
     }
 }
 
@@ -123,11 +134,12 @@ struct WBytes {
     static constexpr int v = WT == kWF32 ? 4 : (WT == kWI8 ? 1 : 2);
 };
 
-// Per-lane partial dot products of NR weight rows (K-major, ldw = K) with
-// the B rows of X (shared memory, row stride K); the loads of the NR rows are
+// Per-lane partial dot products of NR weight rows (row r starts at rp[r]:
+// global memory, or this CTA's staged copy in shared memory when S) with the
+// B rows of X (shared memory, row stride K); the loads of the NR rows are
 // issued together. The caller reduces over lanes.
-template <int WT, int NR>
-__device__ __forceinline__ void rows_dot(const void* W, const int (&n)[NR], int K, const float* X,
+template <int WT, int NR, bool S>
+__device__ __forceinline__ void rows_dot(const char* const (&rp)[NR], int K, const float* X,
                                          int B, float (&acc)[NR][kFusedMaxB]) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
@@ -135,16 +147,14 @@ __device__ __forceinline__ void rows_dot(const void* W, const int (&n)[NR], int 
 #pragma unroll
         for (int m = 0; m < kFusedMaxB; ++m) acc[r][m] = 0.0f;
     if (WT == kWF32) {
-        const float4* w4[NR];
-#pragma unroll
-        for (int r = 0; r < NR; ++r)
-            w4[r] = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(W) +
-                                                    (size_t)n[r] * K);
 #pragma unroll 2
         for (int k4 = lane; k4 < K / 4; k4 += 32) {
             float4 w[NR];
 #pragma unroll
-            for (int r = 0; r < NR; ++r) w[r] = __ldg(w4[r] + k4);
+            for (int r = 0; r < NR; ++r) {
+                const float4* p = reinterpret_cast<const float4*>(rp[r]) + k4;
+                w[r] = S ? *p : __ldg(p);
+            }
 #pragma unroll
             for (int m = 0; m < kFusedMaxB; ++m) {
                 if (m < B) {
@@ -159,50 +169,32 @@ __device__ __forceinline__ void rows_dot(const void* W, const int (&n)[NR], int 
                 }
             }
         }
-    } else if (WT == kWI8) {
-        const int4* w16[NR];
-#pragma unroll
-        for (int r = 0; r < NR; ++r)
-            w16[r] = reinterpret_cast<const int4*>(reinterpret_cast<const int8_t*>(W) +
-                                                   (size_t)n[r] * K);
-        for (int k16 = lane; k16 < K / 16; k16 += 32) {
-            int4 w[NR];
-#pragma unroll
-            for (int r = 0; r < NR; ++r) w[r] = __ldg(w16[r] + k16);
-#pragma unroll
-            for (int m = 0; m < kFusedMaxB; ++m) {
-                if (m < B) {
-                    const float* x = X + m * K + 16 * k16;
-#pragma unroll
-                    for (int r = 0; r < NR; ++r) {
-                        const int8_t* wb = reinterpret_cast<const int8_t*>(&w[r]);
-#pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            acc[r][m] = fmaf((float)wb[j], x[j], acc[r][m]);
-                    }
-                }
-            }
-        }
     } else {
-        const int4* w8[NR];
-#pragma unroll
-        for (int r = 0; r < NR; ++r)
-            w8[r] = reinterpret_cast<const int4*>(reinterpret_cast<const __half*>(W) +
-                                                  (size_t)n[r] * K);
-        for (int k8 = lane; k8 < K / 8; k8 += 32) {
+        constexpr int E = WT == kWI8 ? 16 : 8;  // weights per 16-byte load
+        for (int kv = lane; kv < K / E; kv += 32) {
             int4 w[NR];
 #pragma unroll
-            for (int r = 0; r < NR; ++r) w[r] = __ldg(w8[r] + k8);
+            for (int r = 0; r < NR; ++r) {
+                const int4* p = reinterpret_cast<const int4*>(rp[r]) + kv;
+                w[r] = S ? *p : __ldg(p);
+            }
 #pragma unroll
             for (int m = 0; m < kFusedMaxB; ++m) {
                 if (m < B) {
-                    const float* x = X + m * K + 8 * k8;
+                    const float* x = X + m * K + E * kv;
 #pragma unroll
                     for (int r = 0; r < NR; ++r) {
-                        const __half* wh = reinterpret_cast<const __half*>(&w[r]);
+                        if (WT == kWI8) {
+                            const int8_t* wb = reinterpret_cast<const int8_t*>(&w[r]);
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            acc[r][m] = fmaf(__half2float(wh[j]), x[j], acc[r][m]);
+                            for (int j = 0; j < 16; ++j)
+                                acc[r][m] = fmaf((float)wb[j], x[j], acc[r][m]);
+                        } else {
+                            const __half* wh = reinterpret_cast<const __half*>(&w[r]);
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                acc[r][m] = fmaf(__half2float(wh[j]), x[j], acc[r][m]);
+                        }
                     }
                 }
             }
@@ -210,19 +202,21 @@ __device__ __forceinline__ void rows_dot(const void* W, const int (&n)[NR], int 
     }
 }
 
-// `count` rows of W (row index map(i), i < count) with the B inputs in X,
-// two rows per warp pass. pre(n) is issued before the dot (per lane, lane =
-// sequence) and its value handed to emit(i, n, dot, pre) on lanes < B.
-template <int WT, class Map, class Pre, class Emit>
-__device__ __forceinline__ void rows_loop(const void* W, const float* ws, int count, Map map,
-                                          int K, const float* X, int B, Pre pre, Emit emit) {
+// `count` rows (global row index map(i), data at rowp(i, n)) with the B
+// inputs in X, two rows per warp pass. pre(n) is issued before the dot (per
+// lane, lane = sequence) and its value handed to emit(i, n, dot, pre) on
+// lanes < B. ws: per-row scales of int8 weights (or null).
+template <int WT, bool S, class Map, class RowP, class Pre, class Emit>
+__device__ __forceinline__ void rows_loop(const float* ws, int count, Map map, RowP rowp, int K,
+                                          const float* X, int B, Pre pre, Emit emit) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int i = warp;
     for (; i + kWarps < count; i += 2 * kWarps) {
-        const int n[2] = {map(i), map(i + kWarps)};
-        const float p0 = pre(n[0]), p1 = pre(n[1]);
+        const int n0 = map(i), n1 = map(i + kWarps);
+        const char* rp[2] = {rowp(i, n0), rowp(i + kWarps, n1)};
+        const float p0 = pre(n0), p1 = pre(n1);
         float acc[2][kFusedMaxB];
-        rows_dot<WT, 2>(W, n, K, X, B, acc);
+        rows_dot<WT, 2, S>(rp, K, X, B, acc);
         float o0 = 0.0f, o1 = 0.0f;
 #pragma unroll
         for (int m = 0; m < kFusedMaxB; ++m) {
@@ -235,19 +229,20 @@ __device__ __forceinline__ void rows_loop(const void* W, const float* ws, int co
             }
         }
         if (ws) {
-            o0 *= __ldg(ws + n[0]);
-            o1 *= __ldg(ws + n[1]);
+            o0 *= __ldg(ws + n0);
+            o1 *= __ldg(ws + n1);
         }
         if (lane < B) {
-            emit(i, n[0], o0, p0);
-            emit(i + kWarps, n[1], o1, p1);
+            emit(i, n0, o0, p0);
+            emit(i + kWarps, n1, o1, p1);
         }
     }
     if (i < count) {
-        const int n[1] = {map(i)};
-        const float p0 = pre(n[0]);
+        const int n0 = map(i);
+        const char* rp[1] = {rowp(i, n0)};
+        const float p0 = pre(n0);
         float acc[1][kFusedMaxB];
-        rows_dot<WT, 1>(W, n, K, X, B, acc);
+        rows_dot<WT, 1, S>(rp, K, X, B, acc);
         float o0 = 0.0f;
 #pragma unroll
         for (int m = 0; m < kFusedMaxB; ++m) {
@@ -256,8 +251,8 @@ __device__ __forceinline__ void rows_loop(const void* W, const float* ws, int co
                 if (lane == m) o0 = v0;
             }
         }
-        if (ws) o0 *= __ldg(ws + n[0]);
-        if (lane < B) emit(i, n[0], o0, p0);
+        if (ws) o0 *= __ldg(ws + n0);
+        if (lane < B) emit(i, n0, o0, p0);
     }
 }
 
@@ -282,55 +277,69 @@ __device__ __forceinline__ void row_stats(const float* X, int n, int B, float ep
     }
 }
 
+// This CTA's weight bytes of phase p (4l+k for layer l, 4L for the head): up
+// to two contiguous ranges, in the order the phase's rows are staged.
+//   P1: V rows then Ws rows of the CTA's slice of R+D;  P2: the u rows then
+//   the gate rows of U for its groups;  P3: Wz rows;  P4: Wc rows;  head rows.
 template <int WT>
-__device__ void prefetch_phase(const FusedArgs& a, int p) {
-    if (!a.bulk_prefetch || threadIdx.x != 0 || p > 4 * a.L) return;
-    if (p == 4 * a.L && !a.with_head) return;
+__device__ void phase_ranges(const FusedArgs& a, const FusedLayer* layers, int p,
+                             const char* (&ptr)[2],
+                             long long (&bytes)[2]) {
     constexpr int wb = WBytes<WT>::v;
     const int cta = blockIdx.x, nct = gridDim.x;
-    const char* ptr[2] = {nullptr, nullptr};
-    long long bytes[2] = {0, 0};
-    if (p == 4 * a.L) {
+    ptr[0] = ptr[1] = nullptr;
+    bytes[0] = bytes[1] = 0;
+    if (p >= 4 * a.L) {
         const int r0 = slice_lo(a.vocab, cta, nct), r1 = slice_lo(a.vocab, cta + 1, nct);
         ptr[0] = reinterpret_cast<const char*>(a.head) + (size_t)r0 * a.D * wb;
         bytes[0] = (long long)(r1 - r0) * a.D * wb;
-    } else {
-        const FusedLayer& y = a.layers[p / 4];
-        const int D = a.D, R = a.R, I = a.I;
-        switch (p % 4) {
-            case 0: {
-                const int r0 = slice_lo(R + D, cta, nct), r1 = slice_lo(R + D, cta + 1, nct);
-                const int v0 = min(r0, R), v1 = min(r1, R);
-                ptr[0] = reinterpret_cast<const char*>(y.V) + (size_t)v0 * D * wb;
-                bytes[0] = (long long)(v1 - v0) * D * wb;
-                const int s0 = max(r0, R) - R, s1 = max(r1, R) - R;
-                ptr[1] = reinterpret_cast<const char*>(y.Ws) + (size_t)s0 * D * wb;
-                bytes[1] = (long long)(s1 - s0) * D * wb;
-                break;
-            }
-            case 1: {
-                const int NG = D / a.G;
-                const int g0 = slice_lo(NG, cta, nct), g1 = slice_lo(NG, cta + 1, nct);
-                ptr[0] = reinterpret_cast<const char*>(y.U) + (size_t)g0 * a.G * R * wb;
-                bytes[0] = (long long)(g1 - g0) * a.G * R * wb;
-                ptr[1] = reinterpret_cast<const char*>(y.U) + (size_t)(D + g0 * a.G) * R * wb;
-                bytes[1] = bytes[0];
-                break;
-            }
-            case 2: {
-                const int r0 = slice_lo(I, cta, nct), r1 = slice_lo(I, cta + 1, nct);
-                ptr[0] = reinterpret_cast<const char*>(y.Wz) + (size_t)r0 * D * wb;
-                bytes[0] = (long long)(r1 - r0) * D * wb;
-                break;
-            }
-            default: {
-                const int r0 = slice_lo(D, cta, nct), r1 = slice_lo(D, cta + 1, nct);
-                ptr[0] = reinterpret_cast<const char*>(y.Wc) + (size_t)r0 * I * wb;
-                bytes[0] = (long long)(r1 - r0) * I * wb;
-                break;
-            }
+        return;
+    }
+    const FusedLayer& y = layers[p / 4];
+    const int D = a.D, R = a.R, I = a.I;
+    switch (p % 4) {
+        case 0: {
+            const int r0 = slice_lo(R + D, cta, nct), r1 = slice_lo(R + D, cta + 1, nct);
+            const int v0 = min(r0, R), v1 = min(r1, R);
+            ptr[0] = reinterpret_cast<const char*>(y.V) + (size_t)v0 * D * wb;
+            bytes[0] = (long long)(v1 - v0) * D * wb;
+            const int s0 = max(r0, R) - R, s1 = max(r1, R) - R;
+            ptr[1] = reinterpret_cast<const char*>(y.Ws) + (size_t)s0 * D * wb;
+            bytes[1] = (long long)(s1 - s0) * D * wb;
+            break;
+        }
+        case 1: {
+            const int NG = D / a.G;
+            const int g0 = slice_lo(NG, cta, nct), g1 = slice_lo(NG, cta + 1, nct);
+            ptr[0] = reinterpret_cast<const char*>(y.U) + (size_t)g0 * a.G * R * wb;
+            bytes[0] = (long long)(g1 - g0) * a.G * R * wb;
+            ptr[1] = reinterpret_cast<const char*>(y.U) + (size_t)(D + g0 * a.G) * R * wb;
+            bytes[1] = bytes[0];
+            break;
+        }
+        case 2: {
+            const int r0 = slice_lo(I, cta, nct), r1 = slice_lo(I, cta + 1, nct);
+            ptr[0] = reinterpret_cast<const char*>(y.Wz) + (size_t)r0 * D * wb;
+            bytes[0] = (long long)(r1 - r0) * D * wb;
+            break;
+        }
+        default: {
+            const int r0 = slice_lo(D, cta, nct), r1 = slice_lo(D, cta + 1, nct);
+            ptr[0] = reinterpret_cast<const char*>(y.Wc) + (size_t)r0 * I * wb;
+            bytes[0] = (long long)(r1 - r0) * I * wb;
+            break;
         }
     }
+}
+
+// L2 prefetch hint for phase p's ranges (thread 0).
+template <int WT>
+__device__ void prefetch_phase(const FusedArgs& a, const FusedLayer* layers, int p) {
+    // the head (p == 4L) is staged / prefetched by the kernel at the last layer
+    if (!a.bulk_prefetch || threadIdx.x != 0 || p >= 4 * a.L) return;
+    const char* ptr[2];
+    long long bytes[2];
+    phase_ranges<WT>(a, layers, p, ptr, bytes);
     for (int i = 0; i < 2; ++i)
         for (long long o = 0; o < bytes[i]; o += kPrefetchChunk) {
             const long long n = bytes[i] - o < kPrefetchChunk ? bytes[i] - o : kPrefetchChunk;
@@ -338,9 +347,31 @@ __device__ void prefetch_phase(const FusedArgs& a, int p) {
         }
 }
 
-// Shared-memory layout of the fused step (floats), shared by host and device.
+// Copy phase p's ranges into `buf` (back to back), completing on `mb`
+// (thread 0). Every thread's reads of `buf` from its previous use finished
+// before the grid barrier that precedes this call.
+template <int WT>
+__device__ void stage_phase(const FusedArgs& a, const FusedLayer* layers, int p, char* buf,
+                            uint64_t* mb) {
+    if (threadIdx.x != 0) return;
+    const char* ptr[2];
+    long long bytes[2];
+    phase_ranges<WT>(a, layers, p, ptr, bytes);
+    fence_proxy_async_smem();
+    mbar_expect_tx(mb, (uint32_t)(bytes[0] + bytes[1]));
+    long long off = 0;
+    for (int i = 0; i < 2; ++i)
+        for (long long o = 0; o < bytes[i]; o += kPrefetchChunk) {
+            const long long n = bytes[i] - o < kPrefetchChunk ? bytes[i] - o : kPrefetchChunk;
+            bulk_g2s(buf + off, ptr[i] + o, (uint32_t)n, mb);
+            off += n;
+        }
+}
+
+// Shared-memory layout of the fused step, shared by host and device: float
+// offsets, then (staged variant) two weight buffers and their mbarriers.
 struct FusedSmem {
-    int A, Rr, S, Q, stat, pos, total;
+    int A, Rr, S, Q, stat, pos, par, desc, wbuf, hbuf, mbar, total;  // in floats
     __host__ __device__ FusedSmem(const FusedArgs& a, int ctas) {
         const int maxK = max(a.D, max(a.I, a.R));
         const int NG = a.D / a.G;
@@ -348,16 +379,22 @@ struct FusedSmem {
         A = 0;                                      // [B][K] inputs of the phase's rows
         Rr = A + a.B * maxK;                        // [B][D] normalised x (ring row)
         S = Rr + a.B * a.D;                         // [B][D] state before the update
-        Q = S + a.B * a.D;                          // [groups][2G][8] U outputs (P2)
-        stat = Q + groups * 2 * a.G * kFusedMaxB;   // mean[8], rstd[8]
+        Q = S + a.B * a.D;  // [groups][2G][8] U outputs (P2), then argmax scratch (head)
+        stat = Q + max(groups * 2 * a.G * kFusedMaxB, 2 * kWarps * kFusedMaxB);  // mean, rstd
         pos = stat + 2 * kFusedMaxB;                // [B][L] ring positions at step start
-        total = pos + a.B * a.L;
+        par = pos + a.B * a.L;                      // the phase's per-channel parameters
+        desc = (par + max(3 * a.D, max(2 * a.I, groups * a.G)) + 1) / 2 * 2;  // 8-byte aligned
+        wbuf = (desc + a.L * (int)(sizeof(FusedLayer) / 4) + 31) / 32 * 32;  // 128-byte aligned
+        hbuf = wbuf + 2 * (a.stage_bytes / 4);      // staged head rows
+        mbar = hbuf + a.head_stage_bytes / 4;       // 3 x uint64
+        total = mbar + 6;
     }
 };
 
-template <int WT>
+template <int WT, bool STAGE>
 __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs a) {
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ __align__(128) float sm[];
+    constexpr int wb = WBytes<WT>::v;
     const int B = a.B, D = a.D, I = a.I, R = a.R, L = a.L, G = a.G, KH = a.KH, Kc = a.K;
     const int cta = blockIdx.x, nct = gridDim.x;
     const FusedSmem lay(a, nct);
@@ -367,18 +404,104 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
     float* gq = sm + lay.Q;
     float* stat = sm + lay.stat;
     int* spos = reinterpret_cast<int*>(sm + lay.pos);
+    float* par = sm + lay.par;
+    const FusedLayer* sdesc = reinterpret_cast<const FusedLayer*>(sm + lay.desc);
+    char* wbuf = reinterpret_cast<char*>(sm + lay.wbuf);
+    char* hbuf = reinterpret_cast<char*>(sm + lay.hbuf);
+    uint64_t* mb = reinterpret_cast<uint64_t*>(sm + lay.mbar);  // [0,1] layer, [2] head
     const int tid = threadIdx.x;
     unsigned nbar = 0;
     auto none = [](int) { return 0.0f; };
+    const int hr0 = slice_lo(a.vocab, cta, nct), hr1 = slice_lo(a.vocab, cta + 1, nct);
+    const int hs = min(hr1 - hr0, a.head_stage_bytes / (D * wb));  // staged head rows
 
+    // profile mode: mark j of phase p (see FusedArgs::trace)
+    auto TM = [&](int p, int j) { trace_mark(a, 1 + 8 * p + j); };
     trace_mark(a, 0);
-    for (int p = 0; p < kPrefetchAhead; ++p) prefetch_phase<WT>(a, p);
+    if (tid == 0) {
+        mbar_init(&mb[0], 1);
+        mbar_init(&mb[1], 1);
+        mbar_init(&mb[2], 1);
+        fence_mbar_init();
+    }
+    {   // layer descriptors into shared memory (read at every parameter access)
+        const unsigned* src = reinterpret_cast<const unsigned*>(a.layers);
+        unsigned* dst = reinterpret_cast<unsigned*>(sm + lay.desc);
+        for (int w = tid; w < L * (int)(sizeof(FusedLayer) / 4); w += kFusedThreads)
+            dst[w] = __ldg(src + w);
+    }
     for (int i = tid; i < B * L; i += kFusedThreads) spos[i] = __ldcg(a.pos + i);
     __syncthreads();
+    if (tid == 0 && a.bulk_prefetch) {
+        // the small per-layer vectors, the recurrent state and the ring rows
+        // are read once per step, each right when a phase needs it: pull them
+        // all into L2 now, each range by one CTA
+        int idx = 0;
+        auto pf = [&](const void* p, long long bytes) {
+            if (idx++ % nct != cta) return;
+            for (long long o = 0; o < bytes; o += kPrefetchChunk)
+                bulk_prefetch_l2(static_cast<const char*>(p) + o,
+                                 (unsigned)(bytes - o < kPrefetchChunk ? bytes - o : kPrefetchChunk));
+        };
+        for (int l = 0; l < L; ++l) {
+            const FusedLayer& y = sdesc[l];
+            pf(y.ni_g, D * 4ll);
+            pf(y.ni_c, D * 4ll);
+            pf(y.nm_g, I * 4ll);
+            pf(y.nm_c, I * 4ll);
+            pf(y.dw, (long long)Kc * D * 4);
+            pf(y.delta, D * 4ll);
+        }
+        pf(a.no_g, D * 4ll);
+        pf(a.no_c, D * 4ll);
+        for (int b = 0; b < B; ++b) {
+            pf(a.s + (size_t)b * L * D, (long long)L * D * 4);
+            if (Kc > 1) pf(a.hist + (size_t)b * L * KH * D, (long long)L * KH * D * 4);
+        }
+    }
+    if (STAGE) {
+        stage_phase<WT>(a, sdesc, 0, wbuf, &mb[0]);
+        stage_phase<WT>(a, sdesc, 1, wbuf + a.stage_bytes, &mb[1]);
+    } else {
+        for (int p = 0; p < kPrefetchAhead; ++p) prefetch_phase<WT>(a, sdesc, p);
+    }
+
+    // start of phase p (after its barrier): stage p+1 / prefetch ahead; at
+    // the last layer also the head: its first hs rows into hbuf, the rest as
+    // an L2 hint. Before its rows: wait for the staged weights of p.
+    auto phase_begin = [&](int p) {
+        if (STAGE && p >= 1 && p + 1 < 4 * L)
+            stage_phase<WT>(a, sdesc, p + 1, wbuf + ((p + 1) & 1) * a.stage_bytes, &mb[(p + 1) & 1]);
+        if (p == 4 * L - 4 && a.with_head && tid == 0) {
+            const char* h = reinterpret_cast<const char*>(a.head) + (size_t)hr0 * D * wb;
+            const long long sb = (long long)hs * D * wb;
+            const long long rest = (long long)(hr1 - hr0) * D * wb - sb;
+            fence_proxy_async_smem();
+            mbar_expect_tx(&mb[2], (uint32_t)sb);
+            for (long long o = 0; o < sb; o += kPrefetchChunk)
+                bulk_g2s(hbuf + o, h + o, (uint32_t)(sb - o < kPrefetchChunk ? sb - o : kPrefetchChunk),
+                         &mb[2]);
+            if (a.bulk_prefetch)
+                for (long long o = 0; o < rest; o += kPrefetchChunk)
+                    bulk_prefetch_l2(h + sb + o,
+                                     (unsigned)(rest - o < kPrefetchChunk ? rest - o : kPrefetchChunk));
+        }
+    };
+    auto weights_ready = [&](int p) -> bool {
+        if (!STAGE) return true;
+        if (mbar_wait(&mb[p & 1], (p >> 1) & 1, a.err)) return true;
+        if (tid == 0) atomicExch(a.bar + kBarAbort, 1u);  // others leave at their barrier
+        return false;
+    };
+    auto wrow = [&](int p, long long off) -> const char* {  // staged row of phase p
+        return wbuf + (p & 1) * a.stage_bytes + off;
+    };
 
     for (int l = 0; l < L; ++l) {
-        const FusedLayer& y = a.layers[l];
+        const FusedLayer& y = sdesc[l];
         // ------------------------------------------------ P1: LN, taps, V, Ws
+        const int p1 = 4 * l;
+        phase_begin(p1);
         for (int i = tid; i < B * D; i += kFusedThreads) {
             const int b = i / D, d = i - b * D;
             float xv;
@@ -395,6 +518,11 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
             }
             bufR[i] = xv;
             bufS[i] = __ldcg(a.s + ((size_t)b * L + l) * D + d);
+            if (b == 0) {  // this layer's LN parameters and newest tap weight
+                par[d] = y.ni_g[d];
+                par[D + d] = y.ni_c[d];
+                par[2 * D + d] = Kc > 1 ? y.dw[(size_t)(Kc - 1) * D + d] : 0.0f;
+            }
             if (Kc > 1) {  // the ring part of the causal taps (no LN needed)
                 const int p = spos[b * L + l];
                 const float* hb = a.hist + ((size_t)b * L + l) * KH * D;
@@ -407,33 +535,56 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
             }
         }
         __syncthreads();
+        TM(4 * l, 0);
         row_stats(bufR, D, B, a.eps, stat);
         __syncthreads();
+        TM(4 * l, 1);
         for (int i = tid; i < B * D; i += kFusedThreads) {
             const int b = i / D, d = i - b * D;
-            const float r = (bufR[i] - stat[b]) * stat[kFusedMaxB + b] * y.ni_g[d] + y.ni_c[d];
+            const float r = (bufR[i] - stat[b]) * stat[kFusedMaxB + b] * par[d] + par[D + d];
             bufR[i] = r;
-            bufA[i] = Kc > 1 ? r + (r * y.dw[(size_t)(Kc - 1) * D + d] + bufA[i]) : r;
+            bufA[i] = Kc > 1 ? r + (r * par[2 * D + d] + bufA[i]) : r;
         }
         __syncthreads();
+        TM(4 * l, 2);
+        if (!weights_ready(p1)) return;
+        TM(4 * l, 3);
         {
             const int r0 = slice_lo(R + D, cta, nct), r1 = slice_lo(R + D, cta + 1, nct);
             const int v0 = min(r0, R), v1 = min(r1, R);
             const int w0 = max(r0, R) - R, w1 = max(r1, R) - R;
-            rows_loop<WT>(y.V, y.sV, v1 - v0, [=](int i) { return v0 + i; }, D, bufA, B, none,
-                          [&](int, int n, float v, float) { a.v[(threadIdx.x & 31) * R + n] = v; });
-            rows_loop<WT>(y.Ws, y.sWs, w1 - w0, [=](int i) { return w0 + i; }, D, bufS, B, none,
-                          [&](int, int n, float v, float) {
-                              a.sfb[(threadIdx.x & 31) * D + n] = v;
-                          });
+            const long long vbytes = (long long)(v1 - v0) * D * wb;
+            rows_loop<WT, STAGE>(
+                y.sV, v1 - v0, [=](int i) { return v0 + i; },
+                [&](int i, int n) {
+                    return STAGE ? wrow(p1, (long long)i * D * wb)
+                                 : reinterpret_cast<const char*>(y.V) + (size_t)n * D * wb;
+                },
+                D, bufA, B, none,
+                [&](int, int n, float v, float) { a.v[(threadIdx.x & 31) * R + n] = v; });
+            rows_loop<WT, STAGE>(
+                y.sWs, w1 - w0, [=](int i) { return w0 + i; },
+                [&](int i, int n) {
+                    return STAGE ? wrow(p1, vbytes + (long long)i * D * wb)
+                                 : reinterpret_cast<const char*>(y.Ws) + (size_t)n * D * wb;
+                },
+                D, bufS, B, none,
+                [&](int, int n, float v, float) { a.sfb[(threadIdx.x & 31) * D + n] = v; });
         }
-        trace_mark(a, 1 + 8 * l);
-        prefetch_phase<WT>(a, 4 * l + kPrefetchAhead);
+        TM(4 * l, 4);
+        if (!STAGE) prefetch_phase<WT>(a, sdesc, p1 + kPrefetchAhead);
         if (!grid_sync(a.bar, nbar++, a.err)) return;
-        trace_mark(a, 2 + 8 * l);
+        TM(4 * l, 5);
 
         // ------------------------------------ P2: U, competition, state update
+        const int p2 = p1 + 1;
+        phase_begin(p2);
         for (int i = tid; i < B * R; i += kFusedThreads) bufA[i] = __ldcg(a.v + i);
+        {   // decay gains of this CTA's competition groups
+            const int NG = D / G;
+            const int c0 = slice_lo(NG, cta, nct) * G, c1 = slice_lo(NG, cta + 1, nct) * G;
+            for (int t = tid; t < c1 - c0; t += kFusedThreads) par[t] = y.delta[c0 + t];
+        }
         if (cta == 0 && Kc > 1) {
             for (int i = tid; i < B * D; i += kFusedThreads) {
                 const int b = i / D, d = i - b * D;
@@ -443,15 +594,27 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
             if (tid < B) a.pos[tid * L + l] = spos[tid * L + l] + 1;
         }
         __syncthreads();
+        TM(4 * l + 1, 0);
+        TM(4 * l + 1, 1);
+        TM(4 * l + 1, 2);
+        if (!weights_ready(p2)) return;
+        TM(4 * l + 1, 3);
         {
             const int NG = D / G;
             const int g0 = slice_lo(NG, cta, nct), g1 = slice_lo(NG, cta + 1, nct);
             const int twoG = 2 * G;
-            rows_loop<WT>(
-                y.U, y.sU, (g1 - g0) * twoG,
+            const long long ubytes = (long long)(g1 - g0) * G * R * wb;  // the u rows
+            rows_loop<WT, STAGE>(
+                y.sU, (g1 - g0) * twoG,
                 [=](int i) {
                     const int grp = g0 + i / twoG, j = i - (i / twoG) * twoG;
                     return j < G ? grp * G + j : D + grp * G + (j - G);
+                },
+                [&](int i, int n) {
+                    if (!STAGE) return reinterpret_cast<const char*>(y.U) + (size_t)n * R * wb;
+                    const int gi = i / twoG, j = i - gi * twoG;
+                    const long long row = (long long)gi * G + (j < G ? j : j - G);
+                    return wrow(p2, (j < G ? 0 : ubytes) + row * R * wb);
                 },
                 R, bufA, B, none,
                 [&](int i, int, float v, float) { gq[i * kFusedMaxB + (threadIdx.x & 31)] = v; });
@@ -465,45 +628,71 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
                 const float g1v = q[(G + (j + 1) % G) * kFusedMaxB + m];
                 const float g2v = q[(G + (j + 2) % G) * kFusedMaxB + m];
                 const float uu = q[j * kFusedMaxB + m] * (sigm(g0v - g1v) * sigm(g0v - g2v));
-                float pg = 1.0f - y.delta[d] * (1.0f - sigm(g0v));
+                float pg = 1.0f - par[gi * G + j] * (1.0f - sigm(g0v));
                 if (a.clamp && pg < a.p_floor) pg = a.p_floor;
                 a.s[((size_t)m * L + l) * D + d] = pg * bufS[m * D + d] + (1.0f - pg) * uu;
                 a.u[m * D + d] = uu;
             }
         }
-        trace_mark(a, 3 + 8 * l);
-        prefetch_phase<WT>(a, 4 * l + 1 + kPrefetchAhead);
+        TM(4 * l + 1, 4);
+        if (!STAGE) prefetch_phase<WT>(a, sdesc, p2 + kPrefetchAhead);
         if (!grid_sync(a.bar, nbar++, a.err)) return;
-        trace_mark(a, 4 + 8 * l);
+        TM(4 * l + 1, 5);
 
         // ------------------------------------------------------------ P3: Wz
+        const int p3 = p2 + 1;
+        phase_begin(p3);
         for (int i = tid; i < B * D; i += kFusedThreads) bufA[i] = __ldcg(a.u + i);
         __syncthreads();
+        TM(4 * l + 2, 0);
+        TM(4 * l + 2, 1);
+        TM(4 * l + 2, 2);
+        if (!weights_ready(p3)) return;
+        TM(4 * l + 2, 3);
         {
             const int r0 = slice_lo(I, cta, nct), r1 = slice_lo(I, cta + 1, nct);
             const float at = y.a_tanh;
-            rows_loop<WT>(y.Wz, y.sWz, r1 - r0, [=](int i) { return r0 + i; }, D, bufA, B, none,
-                          [&](int, int n, float acc, float) {
-                              a.z[(threadIdx.x & 31) * I + n] =
-                                  acc * (1.0f + 0.5f * at / (1.0f + fabsf(acc)));
-                          });
+            rows_loop<WT, STAGE>(
+                y.sWz, r1 - r0, [=](int i) { return r0 + i; },
+                [&](int i, int n) {
+                    return STAGE ? wrow(p3, (long long)i * D * wb)
+                                 : reinterpret_cast<const char*>(y.Wz) + (size_t)n * D * wb;
+                },
+                D, bufA, B, none,
+                [&](int, int n, float acc, float) {
+                    a.z[(threadIdx.x & 31) * I + n] =
+                        acc * (1.0f + 0.5f * at / (1.0f + fabsf(acc)));
+                });
         }
-        trace_mark(a, 5 + 8 * l);
-        prefetch_phase<WT>(a, 4 * l + 2 + kPrefetchAhead);
+        TM(4 * l + 2, 4);
+        if (!STAGE) prefetch_phase<WT>(a, sdesc, p3 + kPrefetchAhead);
         if (!grid_sync(a.bar, nbar++, a.err)) return;
-        trace_mark(a, 6 + 8 * l);
+        TM(4 * l + 2, 5);
 
         // ---------------------------------------------- P4: LN(z), Wc, residual
-        for (int i = tid; i < B * I; i += kFusedThreads) bufA[i] = __ldcg(a.z + i);
-        __syncthreads();
-        row_stats(bufA, I, B, a.eps, stat);
-        __syncthreads();
+        const int p4 = p3 + 1;
+        phase_begin(p4);
         for (int i = tid; i < B * I; i += kFusedThreads) {
-            const int b = i / I, k = i - b * I;
-            bufA[i] = __fmul_rn(__fmul_rn(bufA[i] - stat[b], stat[kFusedMaxB + b]), y.nm_g[k]) +
-                      y.nm_c[k];
+            bufA[i] = __ldcg(a.z + i);
+            if (i < I) {
+                par[i] = y.nm_g[i];
+                par[I + i] = y.nm_c[i];
+            }
         }
         __syncthreads();
+        TM(4 * l + 3, 0);
+        row_stats(bufA, I, B, a.eps, stat);
+        __syncthreads();
+        TM(4 * l + 3, 1);
+        for (int i = tid; i < B * I; i += kFusedThreads) {
+            const int b = i / I, k = i - b * I;
+            bufA[i] = __fmul_rn(__fmul_rn(bufA[i] - stat[b], stat[kFusedMaxB + b]), par[k]) +
+                      par[I + k];
+        }
+        __syncthreads();
+        TM(4 * l + 3, 2);
+        if (!weights_ready(p4)) return;
+        TM(4 * l + 3, 3);
         {
             const int r0 = slice_lo(D, cta, nct), r1 = slice_lo(D, cta + 1, nct);
             const float bg = y.b_gain;
@@ -516,53 +705,130 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
                 return bg * __ldcg(a.s + ((size_t)m * L + l) * D + n) + __ldcg(a.sfb + o) +
                        __ldcg(a.x + o);
             };
-            rows_loop<WT>(y.Wc, y.sWc, r1 - r0, [=](int i) { return r0 + i; }, I, bufA, B, resid,
-                          [&](int, int n, float acc, float rsd) {
-                              a.x[(size_t)(threadIdx.x & 31) * D + n] = acc + rsd;
-                          });
+            rows_loop<WT, STAGE>(
+                y.sWc, r1 - r0, [=](int i) { return r0 + i; },
+                [&](int i, int n) {
+                    return STAGE ? wrow(p4, (long long)i * I * wb)
+                                 : reinterpret_cast<const char*>(y.Wc) + (size_t)n * I * wb;
+                },
+                I, bufA, B, resid,
+                [&](int, int n, float acc, float rsd) {
+                    a.x[(size_t)(threadIdx.x & 31) * D + n] = acc + rsd;
+                });
         }
-        trace_mark(a, 7 + 8 * l);
-        prefetch_phase<WT>(a, 4 * l + 3 + kPrefetchAhead);
+        TM(4 * l + 3, 4);
+        if (!STAGE) prefetch_phase<WT>(a, sdesc, p4 + kPrefetchAhead);
         if (l + 1 < L || a.with_head) {
             if (!grid_sync(a.bar, nbar++, a.err)) return;
-            trace_mark(a, 8 + 8 * l);
+            TM(4 * l + 3, 5);
         }
     }
     if (!a.with_head) return;
 
-    // --------------------------------------------------- head: LN(x), logits
-    for (int i = tid; i < B * D; i += kFusedThreads) bufA[i] = __ldcg(a.x + i);
+    // ------------------------------------------- head: LN(x), logits, argmax
+    for (int i = tid; i < B * D; i += kFusedThreads) {
+        bufA[i] = __ldcg(a.x + i);
+        if (i < D) {
+            par[i] = a.no_g[i];
+            par[D + i] = a.no_c[i];
+        }
+    }
     __syncthreads();
     row_stats(bufA, D, B, a.eps, stat);
     __syncthreads();
     for (int i = tid; i < B * D; i += kFusedThreads) {
         const int b = i / D, k = i - b * D;
-        bufA[i] = __fmul_rn(__fmul_rn(bufA[i] - stat[b], stat[kFusedMaxB + b]), a.no_g[k]) +
-                  a.no_c[k];
+        bufA[i] = __fmul_rn(__fmul_rn(bufA[i] - stat[b], stat[kFusedMaxB + b]), par[k]) +
+                  par[D + k];
     }
     __syncthreads();
     {
-        const int r0 = slice_lo(a.vocab, cta, nct), r1 = slice_lo(a.vocab, cta + 1, nct);
         const int V = a.vocab;
-        rows_loop<WT>(a.head, a.shead, r1 - r0, [=](int i) { return r0 + i; }, D, bufA, B, none,
-                      [&](int, int n, float v, float) {
-                          a.logits[(size_t)(threadIdx.x & 31) * V + n] = v;
-                      });
+        float bv = -INFINITY;  // this lane's (sequence's) best logit and its row
+        int bi = 0x7fffffff;
+        auto emit = [&](int, int n, float v, float) {
+            if (a.logits) a.logits[(size_t)(threadIdx.x & 31) * V + n] = v;
+            if (v > bv || (v == bv && n < bi)) {  // NaN never wins, lowest id on ties
+                bv = v;
+                bi = n;
+            }
+        };
+        TM(4 * L, 0);
+        TM(4 * L, 1);
+        TM(4 * L, 2);
+        if (hs > 0) {
+            if (!(mbar_wait(&mb[2], 0, a.err))) {
+                if (tid == 0) atomicExch(a.bar + kBarAbort, 1u);
+                return;
+            }
+            TM(4 * L, 3);
+            rows_loop<WT, true>(
+                a.shead, hs, [=](int i) { return hr0 + i; },
+                [&](int i, int) -> const char* { return hbuf + (size_t)i * D * wb; }, D, bufA, B,
+                none, emit);
+        }
+        if (hs == 0) TM(4 * L, 3);
+        rows_loop<WT, false>(
+            a.shead, hr1 - hr0 - hs, [=](int i) { return hr0 + hs + i; },
+            [&](int, int n) { return reinterpret_cast<const char*>(a.head) + (size_t)n * D * wb; },
+            D, bufA, B, none, emit);
+        if (a.next) {  // CTA best per sequence, then a packed atomic max across CTAs
+            float* wv = gq;  // [warps][8] (P2 scratch is free now)
+            int* wi = reinterpret_cast<int*>(gq + kWarps * kFusedMaxB);
+            const int warp = tid >> 5, lane = tid & 31;
+            if (lane < kFusedMaxB) {
+                wv[warp * kFusedMaxB + lane] = bv;
+                wi[warp * kFusedMaxB + lane] = bi;
+            }
+            __syncthreads();
+            unsigned long long* slot = reinterpret_cast<unsigned long long*>(a.bar + kBarAmax);
+            if (tid < B) {
+                float v = -INFINITY;
+                int ix = 0x7fffffff;
+                for (int w = 0; w < kWarps; ++w) {
+                    const float wvv = wv[w * kFusedMaxB + tid];
+                    const int wii = wi[w * kFusedMaxB + tid];
+                    if (wvv > v || (wvv == v && wii < ix)) {
+                        v = wvv;
+                        ix = wii;
+                    }
+                }
+                if (ix != 0x7fffffff) {  // ordered float bits above, lowest id wins ties
+                    const unsigned f = __float_as_uint(v);
+                    const unsigned key = (f & 0x80000000u) ? ~f : (f | 0x80000000u);
+                    atomicMax(slot + tid, ((unsigned long long)key << 32) | (0xffffffffu - ix));
+                }
+            }
+            __syncthreads();
+            if (tid == 0) {  // the last CTA through here decodes the winners
+                __threadfence();
+                const unsigned done = atomicAdd(a.bar + kBarDone, 1u);
+                if (done == gridDim.x - 1) {
+                    __threadfence();
+                    for (int m = 0; m < B; ++m) {
+                        const unsigned long long k = atomicAdd(slot + m, 0ull);
+                        a.next[m] = k ? (int)(0xffffffffu - (unsigned)(k & 0xffffffffu))
+                                      : 0x7fffffff;  // every logit NaN
+                    }
+                }
+            }
+        }
     }
-    trace_mark(a, 1 + 8 * L);
+    TM(4 * L, 4);
 }
 
-template <int WT>
+template <int WT, bool STAGE>
 int launch_wt(const FusedArgs& a, size_t smem, cudaStream_t st) {
     static int ok = -1;
     if (ok < 0) {
-        SN_TRY(cuda_check(cudaFuncSetAttribute(sunny_fused_kernel<WT>,
+        SN_TRY(cuda_check(cudaFuncSetAttribute(sunny_fused_kernel<WT, STAGE>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               200 * 1024),
+                                               kFusedMaxSmem),
                           "fused smem attr"));
         int per_sm = 0;
         SN_TRY(cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                              &per_sm, sunny_fused_kernel<WT>, kFusedThreads, 200 * 1024),
+                              &per_sm, sunny_fused_kernel<WT, STAGE>, kFusedThreads,
+                              kFusedMaxSmem),
                           "fused occupancy"));
         ok = per_sm >= 1 ? 1 : 0;
     }
@@ -577,7 +843,20 @@ int launch_wt(const FusedArgs& a, size_t smem, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_check(cudaLaunchKernelEx(&cfg, sunny_fused_kernel<WT>, a), "fused step launch");
+    return cuda_check(cudaLaunchKernelEx(&cfg, sunny_fused_kernel<WT, STAGE>, a),
+                      "fused step launch");
+}
+
+// Largest per-CTA weight slice of any layer phase (bytes), for staging.
+long long max_phase_slice(const FusedArgs& a) {
+    const int wb = a.wtype == kWF32 ? 4 : (a.wtype == kWI8 ? 1 : 2);
+    auto up = [&](long long n) { return (n + a.ctas - 1) / a.ctas; };
+    const long long NG = a.D / a.G;
+    long long m = up((long long)a.R + a.D) * a.D;
+    m = std::max(m, up(NG) * 2 * a.G * a.R);
+    m = std::max(m, up(a.I) * a.D);
+    m = std::max(m, up(a.D) * a.I);
+    return (m * wb + 127) / 128 * 128;
 }
 
 }  // namespace
@@ -588,7 +867,24 @@ size_t fused_smem_bytes(const FusedArgs& a) {
     const int wb = a.wtype == kWF32 ? 4 : (a.wtype == kWI8 ? 16 : 8);  // K multiple for 16 B
     if (a.D % wb || a.I % wb || a.R % wb) return 0;
     const size_t bytes = (size_t)FusedSmem(a, a.ctas).total * sizeof(float);
-    return bytes <= 200 * 1024 ? bytes : 0;
+    return bytes <= (size_t)kFusedMaxSmem ? bytes : 0;
+}
+
+size_t fused_plan(FusedArgs* a, bool stage) {
+    a->stage_bytes = 0;
+    a->head_stage_bytes = 0;
+    if (!fused_smem_bytes(*a)) return 0;
+    if (stage) {
+        a->stage_bytes = (int)max_phase_slice(*a);
+        if (!fused_smem_bytes(*a)) a->stage_bytes = 0;
+        // the rest of the shared memory holds the first rows of the head slice
+        const long long row = (long long)a->D * (a->wtype == kWF32 ? 4 : (a->wtype == kWI8 ? 1 : 2));
+        const long long rows = (a->vocab + a->ctas - 1) / a->ctas;
+        const long long room = (long long)kFusedMaxSmem - (long long)fused_smem_bytes(*a);
+        const long long fit = room > 0 ? room / row : 0;
+        a->head_stage_bytes = (int)((fit < rows ? fit : rows) * row);
+    }
+    return fused_smem_bytes(*a);
 }
 
 int launch_sunny_fused(const FusedArgs& a, cudaStream_t st) {
@@ -596,10 +892,14 @@ int launch_sunny_fused(const FusedArgs& a, cudaStream_t st) {
     if (!smem) return fail(SN_E_INVAL, "fused step: shapes unsupported");
     SN_TRY(cuda_check(cudaMemsetAsync(a.bar, 0, kBarWords * sizeof(unsigned), st),
                       "barrier reset"));
+    const bool stage = a.stage_bytes > 0;
     switch (a.wtype) {
-        case kWI8: return launch_wt<kWI8>(a, smem, st);
-        case kWF16: return launch_wt<kWF16>(a, smem, st);
-        default: return launch_wt<kWF32>(a, smem, st);
+        case kWI8: return stage ? launch_wt<kWI8, true>(a, smem, st)
+                                : launch_wt<kWI8, false>(a, smem, st);
+        case kWF16: return stage ? launch_wt<kWF16, true>(a, smem, st)
+                                 : launch_wt<kWF16, false>(a, smem, st);
+        default: return stage ? launch_wt<kWF32, true>(a, smem, st)
+                              : launch_wt<kWF32, false>(a, smem, st);
     }
 }
 

@@ -29,6 +29,7 @@
 #include "ptx.cuh"
 #include "runtime.cuh"
 #include "tc_gemm.cuh"
+#include "tcgen05.cuh"
 
 namespace sn {
 namespace {
@@ -45,69 +46,6 @@ struct TcCfg {
     static constexpr int S = BN == 128 ? 3 : (BN == 64 ? 4 : 5);
     static constexpr int SMEM = S * STAGE + 1024 + 256;
 };
-
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu)  // start address
-           | ((uint64_t)1u << 16)               // leading byte offset (unused for SW128 K-major)
-           | ((uint64_t)64u << 32)              // stride byte offset: 1024 B between 8-row atoms
-           | ((uint64_t)1u << 46)               // descriptor version (sm_100)
-           | ((uint64_t)2u << 61);              // SWIZZLE_128B
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y,
-                                            uint64_t* mbar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-        "%3}], [%4];" ::"r"(smem_u32(dst)),
-        "l"(tm), "r"(x), "r"(y), "r"(smem_u32(mbar))
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                       uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc)
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint64_t* b) {
-    asm volatile(
-        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-            smem_u32(b))
-        : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-        "%30, %31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // .x = a (low half), .y = b
@@ -311,17 +249,8 @@ EncodeTiledFn encode_fn() {
 
 // bf16 (rows, K) K-major plane, box = 64 x box_rows, SWIZZLE_128B
 int encode_map(CUtensorMap* tm, const void* base, long long rows, int K, int box_rows) {
-    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-    const cuuint32_t estr[2] = {1, 1};
-    EncodeTiledFn enc = encode_fn();
-    if (!enc) return fail(SN_E_DEVICE, "cuTensorMapEncodeTiled entry point unavailable");
-    const CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
-                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? SN_OK : fail(SN_E_DEVICE, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return encode_tiled(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, base, K, rows, (long long)K * 2, BK,
+                        box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // Activation planes per K, reused by every contraction with that K (they run
@@ -356,6 +285,23 @@ int launch_bn(const GemmArgs& a, const TcWeights& tw, const ActPlanes& ap, cudaS
 }
 
 }  // namespace
+
+// 2-D tensor map: `rows` rows of `inner` elements, `row_bytes` apart, box
+// box_inner x box_rows, out-of-range elements read as zero.
+int encode_tiled(CUtensorMap* tm, CUtensorMapDataType type, const void* base, long long inner,
+                 long long rows, long long row_bytes, int box_inner, int box_rows,
+                 CUtensorMapSwizzle swz) {
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(SN_E_DEVICE, "cuTensorMapEncodeTiled entry point unavailable");
+    const CUresult r = enc(tm, type, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? SN_OK : fail(SN_E_DEVICE, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+}
 
 int tc_reserve(int K, long long rows) {
     if (K % 8 != 0 || rows <= 0) return SN_OK;

@@ -203,6 +203,22 @@ def test_w4a8_batched_bit_exact(rt, B):
         assert np.array_equal(Y[i], oracle.gemv_i4(np.ascontiguousarray(X[i]), q, sc, block))
 
 
+@pytest.mark.parametrize("B,n,out,block,fp16", [
+    (16, 768, 768, 128, True), (64, 768, 3072, 128, True), (130, 3072, 768, 128, False),
+    (64, 768, 300, 64, True), (256, 256, 100, 32, False), (33, 1024, 4096, 128, True)])
+def test_w4a8_tensor_core_bit_exact(rt, B, n, out, block, fp16):
+    """B >= 16 runs on tcgen05 kind::i8 (exact int32 block dots, block-ordered
+    fp32 epilogue): every output must equal the reference GEMV bit for bit,
+    including ragged N tiles and M not a multiple of 128."""
+    rng = np.random.default_rng(B + out)
+    W = (rng.standard_normal((out, n)) * 0.04).astype(np.float32)
+    X = (rng.standard_normal((B, n)) * rng.uniform(0.1, 3.0, (B, 1))).astype(np.float32)
+    q, sc = oracle.quant_i4(W, block, fp16=fp16)
+    Y = rt.gemm_i4(X, q, sc, block)
+    ref = np.stack([oracle.gemv_i4(np.ascontiguousarray(X[i]), q, sc, block) for i in range(B)])
+    assert np.array_equal(Y, ref)
+
+
 def test_w4a8_device_pointers(rt):
     rng = np.random.default_rng(11)
     W = (rng.standard_normal((4096, 768)) * 0.04).astype(np.float32)

@@ -356,3 +356,25 @@ def test_bad_token_id_is_reported_and_handle_stays_usable(B):
         for _ in range(3):
             toks = rng.integers(0, 512, B).astype(np.int32)
             check_logits(m.step(toks), om.step(toks))
+
+
+@pytest.mark.parametrize("B", [1, 3, 8])
+def test_fused_argmax_matches_logits_in_place(B):
+    """Greedy steps of the fused path write the argmax straight into the
+    caller's device buffer, which here also holds the input tokens (as a decode
+    loop does): each step's ids must equal the argmax of the logits of a twin
+    model fed the same tokens (lowest id on ties)."""
+    from sunnynet_b200 import formats
+    from sunnynet_b200.model import SunnyBatch
+    shape = formats.SunnyShape(2048, 64, 96, 32, 4, 2)
+    rng = np.random.default_rng(11 + B)
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape)
+        a, b = SunnyBatch(p, B), SunnyBatch(p, B)
+        cur = torch.from_numpy(rng.integers(0, 2048, B).astype(np.int32)).cuda()
+        for _ in range(5):
+            toks = cur.cpu().numpy().copy()
+            lg = a.step(toks)
+            b.step_argmax(cur, out=cur)
+            torch.cuda.synchronize()
+            assert np.array_equal(cur.cpu().numpy(), lg.argmax(1).astype(np.int32))
