@@ -36,6 +36,10 @@ int w4a8_tc_reserve(int M, int K, int block);
 int launch_w4a8_tc(float* Y, const float* X, const uint8_t* Wq, const void* scale, int M, int K,
                    int N, int block, bool fp16, int epi, cudaStream_t st);
 int launch_gemv_f32(float* y, const float* x, const float* W, int in, int out, cudaStream_t st);
+// out[b] = argmax of logits row b (lowest id on ties, NaN never chosen);
+// part holds B * kArgChunks float2 of scratch (argmax.cu).
+constexpr int kArgChunks = 32;
+int launch_argmax(const float* lg, int B, int V, float2* part, int32_t* out, cudaStream_t st);
 int launch_quant_i4(const float* x, uint8_t* q, void* scale, int rows, int N, int block,
                     bool fp16, cudaStream_t st);
 

@@ -247,41 +247,6 @@ __global__ void rk_ln_kernel(int D, const float* __restrict__ x, const float* __
         y[(size_t)blockIdx.x * D + i] = (xr[i] - mean) * rstd * w[i] + b[i];
 }
 
-__global__ void rk_argmax_kernel(int V, const float* __restrict__ lg, int32_t* __restrict__ out) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
-    const float* r = lg + (size_t)blockIdx.x * V;
-    float best = -INFINITY;
-    int idx = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = r[i];
-        if (v > best || (v == best && i < idx)) {
-            best = v;
-            idx = i;
-        }
-    }
-    for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ov > best || (ov == best && oi < idx)) {
-            best = ov;
-            idx = oi;
-        }
-    }
-    if ((threadIdx.x & 31) == 0) {
-        bv[threadIdx.x >> 5] = best;
-        bi[threadIdx.x >> 5] = idx;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
-            if (bv[k] > best || (bv[k] == best && bi[k] < idx)) {
-                best = bv[k];
-                idx = bi[k];
-            }
-        out[blockIdx.x] = idx;
-    }
-}
 
 __global__ void rk_transpose_kernel(const float* __restrict__ src, float* __restrict__ dst, int in,
                                     int out) {
@@ -328,6 +293,7 @@ struct RwkvModel {
     float *lo_w = nullptr, *lo_a = nullptr, *lo_v = nullptr, *lo_g = nullptr;
     float *dw = nullptr, *da = nullptr, *dv = nullptr, *ck = nullptr, *vfirst = nullptr;
     float *logits = nullptr, *xf = nullptr;
+    float2* apart = nullptr;  // argmax partials (B x kArgChunks)
     std::vector<void*> allocs;
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
     cudaStream_t cap = nullptr;
@@ -514,7 +480,8 @@ int load_rwkv(RwkvModel* m, const char* path, int nseq) {
     m->ck = m->dalloc<float>(B * m->F); m->vfirst = m->dalloc<float>(B * D);
     m->xf = m->dalloc<float>(B * D);
     m->logits = m->dalloc<float>(B * m->vocab);
-    if (!m->logits || !m->xf) return fail(SN_E_NOMEM, "device allocation failed");
+    m->apart = m->dalloc<float2>(B * kArgChunks);
+    if (!m->logits || !m->xf || !m->apart) return fail(SN_E_NOMEM, "device allocation failed");
     cudaMemset(m->S, 0, B * L * m->NH * m->HS * m->HS * 4);
     cudaMemset(m->shift, 0, B * L * 2 * D * 4);
     SN_TRY(cuda_check(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking), "stream"));
@@ -654,7 +621,7 @@ int rk_step(RwkvModel* m, const int32_t* tokens, int B, float* logits, int32_t* 
                           "logits"));
     }
     if (next) {
-        rk_argmax_kernel<<<B, 256, 0, st>>>(m->vocab, m->logits, m->next);
+        SN_TRY(launch_argmax(m->logits, B, m->vocab, m->apart, m->next, st));
         const bool dev = is_device_ptr(next);
         host |= !dev;
         SN_TRY(cuda_check(cudaMemcpyAsync(next, m->next, (size_t)B * 4,

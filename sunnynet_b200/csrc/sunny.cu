@@ -166,43 +166,6 @@ __global__ void apply_ln_kernel(int n, const float* __restrict__ z, const float*
                                             rs[blockIdx.x] * g[i] + c[i];
 }
 
-// Greedy next token: argmax of each logits row, lowest id on ties.
-__global__ void argmax_kernel(int V, const float* __restrict__ lg, int32_t* __restrict__ out) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
-    const float* r = lg + (size_t)blockIdx.x * V;
-    float best = -INFINITY;
-    int idx = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = r[i];
-        if (v > best || (v == best && i < idx)) {
-            best = v;
-            idx = i;
-        }
-    }
-    for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ov > best || (ov == best && oi < idx)) {
-            best = ov;
-            idx = oi;
-        }
-    }
-    const int w = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) {
-        bv[w] = best;
-        bi[w] = idx;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
-            if (bv[k] > best || (bv[k] == best && bi[k] < idx)) {
-                best = bv[k];
-                idx = bi[k];
-            }
-        out[blockIdx.x] = idx;
-    }
-}
 
 // (in,out) -> (out,in)
 __global__ void transpose_kernel(const float* __restrict__ src, float* __restrict__ dst, int in,
@@ -383,6 +346,7 @@ struct SunnyModel {
     float *x = nullptr, *at = nullptr, *raw = nullptr, *v = nullptr, *q = nullptr, *u = nullptr;
     float *gate = nullptr, *sfb = nullptr, *z = nullptr, *mu = nullptr, *rs = nullptr;
     float *logits = nullptr, *yn = nullptr;
+    float2* apart = nullptr;  // argmax partials (B x kArgChunks)
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (B, with head) -> graph
     // chunked prefill: buffers of B*Tc rows, one graph per (B, Tc, head)
     long long crows = 0;
@@ -623,7 +587,8 @@ int load_model(SunnyModel* m, const char* path, int nseq, bool half, const int* 
     m->mu = m->dalloc<float>(n);
     m->rs = m->dalloc<float>(n);
     m->logits = m->dalloc<float>(n * vocab);
-    if (!m->logits || !m->rs) return fail(SN_E_NOMEM, "device allocation failed");
+    m->apart = m->dalloc<float2>(n * kArgChunks);
+    if (!m->logits || !m->rs || !m->apart) return fail(SN_E_NOMEM, "device allocation failed");
     SN_TRY(cuda_check(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking), "stream"));
     cudaMemset(m->s, 0, n * L * D * 4);
     cudaMemset(m->hist, 0, n * L * m->KH * D * 4);
@@ -1083,7 +1048,7 @@ int sunny_step(SunnyModel* m, const int32_t* tokens, int B, float* logits, int32
                           "logits"));
     }
     if (next) {
-        argmax_kernel<<<B, 256, 0, st>>>(m->vocab, m->logits, m->next);
+        SN_TRY(launch_argmax(m->logits, B, m->vocab, m->apart, m->next, st));
         const bool dev = is_device_ptr(next);
         host |= !dev;
         SN_TRY(cuda_check(cudaMemcpyAsync(next, m->next, (size_t)B * 4,

@@ -138,14 +138,14 @@ struct WBytes {
 // global memory, or this CTA's staged copy in shared memory when S) with the
 // B rows of X (shared memory, row stride K); the loads of the NR rows are
 // issued together. The caller reduces over lanes.
-template <int WT, int NR, bool S>
+template <int WT, int NR, bool S, int MB>
 __device__ __forceinline__ void rows_dot(const char* const (&rp)[NR], int K, const float* X,
-                                         int B, float (&acc)[NR][kFusedMaxB]) {
+                                         int B, float (&acc)[NR][MB]) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int r = 0; r < NR; ++r)
 #pragma unroll
-        for (int m = 0; m < kFusedMaxB; ++m) acc[r][m] = 0.0f;
+        for (int m = 0; m < MB; ++m) acc[r][m] = 0.0f;
     if (WT == kWF32) {
 #pragma unroll 2
         for (int k4 = lane; k4 < K / 4; k4 += 32) {
@@ -156,7 +156,7 @@ __device__ __forceinline__ void rows_dot(const char* const (&rp)[NR], int K, con
                 w[r] = S ? *p : __ldg(p);
             }
 #pragma unroll
-            for (int m = 0; m < kFusedMaxB; ++m) {
+            for (int m = 0; m < MB; ++m) {
                 if (m < B) {
                     const float4 x = *reinterpret_cast<const float4*>(X + m * K + 4 * k4);
 #pragma unroll
@@ -179,7 +179,7 @@ __device__ __forceinline__ void rows_dot(const char* const (&rp)[NR], int K, con
                 w[r] = S ? *p : __ldg(p);
             }
 #pragma unroll
-            for (int m = 0; m < kFusedMaxB; ++m) {
+            for (int m = 0; m < MB; ++m) {
                 if (m < B) {
                     const float* x = X + m * K + E * kv;
 #pragma unroll
@@ -206,7 +206,7 @@ __device__ __forceinline__ void rows_dot(const char* const (&rp)[NR], int K, con
 // inputs in X, two rows per warp pass. pre(n) is issued before the dot (per
 // lane, lane = sequence) and its value handed to emit(i, n, dot, pre) on
 // lanes < B. ws: per-row scales of int8 weights (or null).
-template <int WT, bool S, class Map, class RowP, class Pre, class Emit>
+template <int WT, bool S, int MB, class Map, class RowP, class Pre, class Emit>
 __device__ __forceinline__ void rows_loop(const float* ws, int count, Map map, RowP rowp, int K,
                                           const float* X, int B, Pre pre, Emit emit) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -215,11 +215,11 @@ __device__ __forceinline__ void rows_loop(const float* ws, int count, Map map, R
         const int n0 = map(i), n1 = map(i + kWarps);
         const char* rp[2] = {rowp(i, n0), rowp(i + kWarps, n1)};
         const float p0 = pre(n0), p1 = pre(n1);
-        float acc[2][kFusedMaxB];
-        rows_dot<WT, 2, S>(rp, K, X, B, acc);
+        float acc[2][MB];
+        rows_dot<WT, 2, S, MB>(rp, K, X, B, acc);
         float o0 = 0.0f, o1 = 0.0f;
 #pragma unroll
-        for (int m = 0; m < kFusedMaxB; ++m) {
+        for (int m = 0; m < MB; ++m) {
             if (m < B) {
                 const float v0 = warp_sum(acc[0][m]), v1 = warp_sum(acc[1][m]);
                 if (lane == m) {
@@ -241,11 +241,11 @@ __device__ __forceinline__ void rows_loop(const float* ws, int count, Map map, R
         const int n0 = map(i);
         const char* rp[1] = {rowp(i, n0)};
         const float p0 = pre(n0);
-        float acc[1][kFusedMaxB];
-        rows_dot<WT, 1, S>(rp, K, X, B, acc);
+        float acc[1][MB];
+        rows_dot<WT, 1, S, MB>(rp, K, X, B, acc);
         float o0 = 0.0f;
 #pragma unroll
-        for (int m = 0; m < kFusedMaxB; ++m) {
+        for (int m = 0; m < MB; ++m) {
             if (m < B) {
                 const float v0 = warp_sum(acc[0][m]);
                 if (lane == m) o0 = v0;
@@ -381,8 +381,8 @@ struct FusedSmem {
         S = Rr + a.B * a.D;                         // [B][D] state before the update
         Q = S + a.B * a.D;  // [groups][2G][8] U outputs (P2), then argmax scratch (head)
         stat = Q + max(groups * 2 * a.G * kFusedMaxB, 2 * kWarps * kFusedMaxB);  // mean, rstd
-        pos = stat + 2 * kFusedMaxB;                // [B][L] ring positions at step start
-        par = pos + a.B * a.L;                      // the phase's per-channel parameters
+        pos = stat + 2 * kFusedMaxB;                // [B][L] ring positions, [8] tokens
+        par = pos + a.B * a.L + kFusedMaxB;         // the phase's per-channel parameters
         desc = (par + max(3 * a.D, max(2 * a.I, groups * a.G)) + 1) / 2 * 2;  // 8-byte aligned
         wbuf = (desc + a.L * (int)(sizeof(FusedLayer) / 4) + 31) / 32 * 32;  // 128-byte aligned
         hbuf = wbuf + 2 * (a.stage_bytes / 4);      // staged head rows
@@ -391,11 +391,13 @@ struct FusedSmem {
     }
 };
 
-template <int WT, bool STAGE>
+template <int WT, bool STAGE, int MB>
 __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs a) {
     extern __shared__ __align__(128) float sm[];
     constexpr int wb = WBytes<WT>::v;
-    const int B = a.B, D = a.D, I = a.I, R = a.R, L = a.L, G = a.G, KH = a.KH, Kc = a.K;
+    // MB: compile-time bound of the batch (1: the single-sequence variant)
+    const int B = MB == 1 ? 1 : a.B, D = a.D, I = a.I, R = a.R, L = a.L, G = a.G, KH = a.KH,
+              Kc = a.K;
     const int cta = blockIdx.x, nct = gridDim.x;
     const FusedSmem lay(a, nct);
     float* bufA = sm + lay.A;
@@ -404,6 +406,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
     float* gq = sm + lay.Q;
     float* stat = sm + lay.stat;
     int* spos = reinterpret_cast<int*>(sm + lay.pos);
+    int* stok = spos + B * L;
     float* par = sm + lay.par;
     const FusedLayer* sdesc = reinterpret_cast<const FusedLayer*>(sm + lay.desc);
     char* wbuf = reinterpret_cast<char*>(sm + lay.wbuf);
@@ -431,6 +434,14 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
             dst[w] = __ldg(src + w);
     }
     for (int i = tid; i < B * L; i += kFusedThreads) spos[i] = __ldcg(a.pos + i);
+    if (tid < B) {
+        int t = a.tok[tid];
+        if (t < 0 || t >= a.vocab) {  // never read outside the table; report instead
+            atomicExch(a.err, kErrBadIndex);
+            t = 0;
+        }
+        stok[tid] = t;
+    }
     __syncthreads();
     if (tid == 0 && a.bulk_prefetch) {
         // the small per-layer vectors, the recurrent state and the ring rows
@@ -503,36 +514,42 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
         const int p1 = 4 * l;
         phase_begin(p1);
         for (int i = tid; i < B * D; i += kFusedThreads) {
+            // every global load of the element first, then the shared stores:
+            // a load placed after a store through a generic pointer waits for
+            // it, which would serialise the round trips
             const int b = i / D, d = i - b * D;
-            float xv;
-            if (l == 0) {
-                int t = a.tok[b];
-                if (t < 0 || t >= a.vocab) {  // never read outside the table; report instead
-                    if (d == 0) atomicExch(a.err, kErrBadIndex);
-                    t = 0;
-                }
-                xv = a.embed[(size_t)t * D + d];
-                if (cta == 0) a.x[i] = xv;
-            } else {
-                xv = __ldcg(a.x + i);
-            }
-            bufR[i] = xv;
-            bufS[i] = __ldcg(a.s + ((size_t)b * L + l) * D + d);
+            const float xv = l == 0 ? a.embed[(size_t)stok[b] * D + d] : __ldcg(a.x + i);
+            const float sv = __ldcg(a.s + ((size_t)b * L + l) * D + d);
+            float g = 0.0f, c = 0.0f, wl = 0.0f;
             if (b == 0) {  // this layer's LN parameters and newest tap weight
-                par[d] = y.ni_g[d];
-                par[D + d] = y.ni_c[d];
-                par[2 * D + d] = Kc > 1 ? y.dw[(size_t)(Kc - 1) * D + d] : 0.0f;
+                g = y.ni_g[d];
+                c = y.ni_c[d];
+                wl = Kc > 1 ? y.dw[(size_t)(Kc - 1) * D + d] : 0.0f;
             }
-            if (Kc > 1) {  // the ring part of the causal taps (no LN needed)
-                const int p = spos[b * L + l];
-                const float* hb = a.hist + ((size_t)b * L + l) * KH * D;
-                float part = 0.0f;
-                for (int k = 0; k < Kc - 1; ++k) {
+            float hv[kFusedMaxTaps], wv[kFusedMaxTaps];  // the ring part of the taps
+            const int p = spos[b * L + l];
+            const float* hb = a.hist + ((size_t)b * L + l) * KH * D;
+#pragma unroll
+            for (int k = 0; k < kFusedMaxTaps; ++k) {
+                if (k < Kc - 1) {
                     const int slot = ((p - 1 - k) % KH + KH) % KH;
-                    part += __ldcg(hb + (size_t)slot * D + d) * y.dw[(size_t)(Kc - 2 - k) * D + d];
+                    hv[k] = __ldcg(hb + (size_t)slot * D + d);
+                    wv[k] = y.dw[(size_t)(Kc - 2 - k) * D + d];
                 }
-                bufA[i] = part;
             }
+            float part = 0.0f;
+#pragma unroll
+            for (int k = 0; k < kFusedMaxTaps; ++k)
+                if (k < Kc - 1) part += hv[k] * wv[k];
+            if (l == 0 && cta == 0) a.x[i] = xv;
+            bufR[i] = xv;
+            bufS[i] = sv;
+            if (b == 0) {
+                par[d] = g;
+                par[D + d] = c;
+                par[2 * D + d] = wl;
+            }
+            bufA[i] = part;
         }
         __syncthreads();
         TM(4 * l, 0);
@@ -554,7 +571,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
             const int v0 = min(r0, R), v1 = min(r1, R);
             const int w0 = max(r0, R) - R, w1 = max(r1, R) - R;
             const long long vbytes = (long long)(v1 - v0) * D * wb;
-            rows_loop<WT, STAGE>(
+            rows_loop<WT, STAGE, MB>(
                 y.sV, v1 - v0, [=](int i) { return v0 + i; },
                 [&](int i, int n) {
                     return STAGE ? wrow(p1, (long long)i * D * wb)
@@ -562,7 +579,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
                 },
                 D, bufA, B, none,
                 [&](int, int n, float v, float) { a.v[(threadIdx.x & 31) * R + n] = v; });
-            rows_loop<WT, STAGE>(
+            rows_loop<WT, STAGE, MB>(
                 y.sWs, w1 - w0, [=](int i) { return w0 + i; },
                 [&](int i, int n) {
                     return STAGE ? wrow(p1, vbytes + (long long)i * D * wb)
@@ -579,11 +596,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
         // ------------------------------------ P2: U, competition, state update
         const int p2 = p1 + 1;
         phase_begin(p2);
-        for (int i = tid; i < B * R; i += kFusedThreads) bufA[i] = __ldcg(a.v + i);
-        {   // decay gains of this CTA's competition groups
+        {   // v, and the decay gains of this CTA's competition groups
             const int NG = D / G;
             const int c0 = slice_lo(NG, cta, nct) * G, c1 = slice_lo(NG, cta + 1, nct) * G;
-            for (int t = tid; t < c1 - c0; t += kFusedThreads) par[t] = y.delta[c0 + t];
+            const int n = max(B * R, c1 - c0);
+            for (int i = tid; i < n; i += kFusedThreads) {
+                const float vv = i < B * R ? __ldcg(a.v + i) : 0.0f;
+                const float dl = i < c1 - c0 ? y.delta[c0 + i] : 0.0f;
+                if (i < B * R) bufA[i] = vv;
+                if (i < c1 - c0) par[i] = dl;
+            }
         }
         if (cta == 0 && Kc > 1) {
             for (int i = tid; i < B * D; i += kFusedThreads) {
@@ -604,7 +626,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
             const int g0 = slice_lo(NG, cta, nct), g1 = slice_lo(NG, cta + 1, nct);
             const int twoG = 2 * G;
             const long long ubytes = (long long)(g1 - g0) * G * R * wb;  // the u rows
-            rows_loop<WT, STAGE>(
+            rows_loop<WT, STAGE, MB>(
                 y.sU, (g1 - g0) * twoG,
                 [=](int i) {
                     const int grp = g0 + i / twoG, j = i - (i / twoG) * twoG;
@@ -652,7 +674,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
         {
             const int r0 = slice_lo(I, cta, nct), r1 = slice_lo(I, cta + 1, nct);
             const float at = y.a_tanh;
-            rows_loop<WT, STAGE>(
+            rows_loop<WT, STAGE, MB>(
                 y.sWz, r1 - r0, [=](int i) { return r0 + i; },
                 [&](int i, int n) {
                     return STAGE ? wrow(p3, (long long)i * D * wb)
@@ -673,10 +695,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
         const int p4 = p3 + 1;
         phase_begin(p4);
         for (int i = tid; i < B * I; i += kFusedThreads) {
-            bufA[i] = __ldcg(a.z + i);
+            const float zv = __ldcg(a.z + i);
+            float g = 0.0f, c = 0.0f;
             if (i < I) {
-                par[i] = y.nm_g[i];
-                par[I + i] = y.nm_c[i];
+                g = y.nm_g[i];
+                c = y.nm_c[i];
+            }
+            bufA[i] = zv;
+            if (i < I) {
+                par[i] = g;
+                par[I + i] = c;
             }
         }
         __syncthreads();
@@ -705,7 +733,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
                 return bg * __ldcg(a.s + ((size_t)m * L + l) * D + n) + __ldcg(a.sfb + o) +
                        __ldcg(a.x + o);
             };
-            rows_loop<WT, STAGE>(
+            rows_loop<WT, STAGE, MB>(
                 y.sWc, r1 - r0, [=](int i) { return r0 + i; },
                 [&](int i, int n) {
                     return STAGE ? wrow(p4, (long long)i * I * wb)
@@ -727,10 +755,16 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
 
     // ------------------------------------------- head: LN(x), logits, argmax
     for (int i = tid; i < B * D; i += kFusedThreads) {
-        bufA[i] = __ldcg(a.x + i);
+        const float xv = __ldcg(a.x + i);
+        float g = 0.0f, c = 0.0f;
         if (i < D) {
-            par[i] = a.no_g[i];
-            par[D + i] = a.no_c[i];
+            g = a.no_g[i];
+            c = a.no_c[i];
+        }
+        bufA[i] = xv;
+        if (i < D) {
+            par[i] = g;
+            par[D + i] = c;
         }
     }
     __syncthreads();
@@ -762,13 +796,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
                 return;
             }
             TM(4 * L, 3);
-            rows_loop<WT, true>(
+            rows_loop<WT, true, MB>(
                 a.shead, hs, [=](int i) { return hr0 + i; },
                 [&](int i, int) -> const char* { return hbuf + (size_t)i * D * wb; }, D, bufA, B,
                 none, emit);
         }
         if (hs == 0) TM(4 * L, 3);
-        rows_loop<WT, false>(
+        rows_loop<WT, false, MB>(
             a.shead, hr1 - hr0 - hs, [=](int i) { return hr0 + hs + i; },
             [&](int, int n) { return reinterpret_cast<const char*>(a.head) + (size_t)n * D * wb; },
             D, bufA, B, none, emit);
@@ -817,17 +851,17 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
     TM(4 * L, 4);
 }
 
-template <int WT, bool STAGE>
+template <int WT, bool STAGE, int MB>
 int launch_wt(const FusedArgs& a, size_t smem, cudaStream_t st) {
     static int ok = -1;
     if (ok < 0) {
-        SN_TRY(cuda_check(cudaFuncSetAttribute(sunny_fused_kernel<WT, STAGE>,
+        SN_TRY(cuda_check(cudaFuncSetAttribute(sunny_fused_kernel<WT, STAGE, MB>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                kFusedMaxSmem),
                           "fused smem attr"));
         int per_sm = 0;
         SN_TRY(cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                              &per_sm, sunny_fused_kernel<WT, STAGE>, kFusedThreads,
+                              &per_sm, sunny_fused_kernel<WT, STAGE, MB>, kFusedThreads,
                               kFusedMaxSmem),
                           "fused occupancy"));
         ok = per_sm >= 1 ? 1 : 0;
@@ -843,7 +877,7 @@ int launch_wt(const FusedArgs& a, size_t smem, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cuda_check(cudaLaunchKernelEx(&cfg, sunny_fused_kernel<WT, STAGE>, a),
+    return cuda_check(cudaLaunchKernelEx(&cfg, sunny_fused_kernel<WT, STAGE, MB>, a),
                       "fused step launch");
 }
 
@@ -863,6 +897,7 @@ long long max_phase_slice(const FusedArgs& a) {
 
 size_t fused_smem_bytes(const FusedArgs& a) {
     if (a.B < 1 || a.B > kFusedMaxB || a.G < 1 || a.G > kFusedMaxG || a.D % a.G) return 0;
+    if (a.K < 1 || a.K - 1 > kFusedMaxTaps) return 0;
     if (a.ctas < 1) return 0;
     const int wb = a.wtype == kWF32 ? 4 : (a.wtype == kWI8 ? 16 : 8);  // K multiple for 16 B
     if (a.D % wb || a.I % wb || a.R % wb) return 0;
@@ -892,15 +927,18 @@ int launch_sunny_fused(const FusedArgs& a, cudaStream_t st) {
     if (!smem) return fail(SN_E_INVAL, "fused step: shapes unsupported");
     SN_TRY(cuda_check(cudaMemsetAsync(a.bar, 0, kBarWords * sizeof(unsigned), st),
                       "barrier reset"));
-    const bool stage = a.stage_bytes > 0;
+    const bool stage = a.stage_bytes > 0, one = a.B == 1;
+#define SN_FUSED_LAUNCH(WT)                                                    \
+    return stage ? (one ? launch_wt<WT, true, 1>(a, smem, st)                  \
+                        : launch_wt<WT, true, kFusedMaxB>(a, smem, st))        \
+                 : (one ? launch_wt<WT, false, 1>(a, smem, st)                 \
+                        : launch_wt<WT, false, kFusedMaxB>(a, smem, st))
     switch (a.wtype) {
-        case kWI8: return stage ? launch_wt<kWI8, true>(a, smem, st)
-                                : launch_wt<kWI8, false>(a, smem, st);
-        case kWF16: return stage ? launch_wt<kWF16, true>(a, smem, st)
-                                 : launch_wt<kWF16, false>(a, smem, st);
-        default: return stage ? launch_wt<kWF32, true>(a, smem, st)
-                              : launch_wt<kWF32, false>(a, smem, st);
+        case kWI8: SN_FUSED_LAUNCH(kWI8);
+        case kWF16: SN_FUSED_LAUNCH(kWF16);
+        default: SN_FUSED_LAUNCH(kWF32);
     }
+#undef SN_FUSED_LAUNCH
 }
 
 }  // namespace sn

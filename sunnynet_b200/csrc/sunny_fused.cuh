@@ -11,6 +11,7 @@ namespace sn {
 constexpr int kFusedMaxB = 8;
 constexpr int kFusedThreads = 512;
 constexpr int kFusedMaxG = 16;
+constexpr int kFusedMaxTaps = 8;  // ring taps (conv kernel - 1)
 constexpr int kFusedMaxSmem = 200 * 1024;  // dynamic shared memory cap
 
 // Per-layer weights (device pointers), copied to device memory once at load.

@@ -80,7 +80,9 @@ __global__ void split_act_kernel(GemmArgs a, __nv_bfloat16* __restrict__ hi,
     }
 }
 
-template <int BN, bool I8>
+// LOADS: the epilogue reads more than the accumulator (residual / accumulate
+// kinds); those operands are then all loaded before any result is stored.
+template <int BN, bool I8, bool LOADS>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
                    const __grid_constant__ CUtensorMap twh, const __grid_constant__ CUtensorMap twl,
@@ -190,12 +192,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = v[j];
                 __syncwarp();
                 const int n = n0 + j0 + lane;
+                const bool nok = n < a.N;
+                if (!LOADS) {
 #pragma unroll 4
-                for (int r = 0; r < 32; ++r) {
-                    const int mm = m0 + q * 32 + r;
-                    if (mm < a.M && n < a.N)
-                        a.C[(long long)mm * a.ldc + n] =
-                            gemm_epilogue(a, mm, n, stg[r * 33 + lane]);
+                    for (int r = 0; r < 32; ++r) {
+                        const int mm = m0 + q * 32 + r;
+                        if (mm < a.M && nok)
+                            a.C[(long long)mm * a.ldc + n] =
+                                gemm_epilogue(a, mm, n, stg[r * 33 + lane]);
+                    }
+                } else {
+                    // the epilogue's other operands for all 32 rows are loaded
+                    // before any of them is used or any result stored, so the
+                    // loads overlap (one round trip per block, not per row)
+                    float pre[32];
+#pragma unroll
+                    for (int r = 0; r < 32; ++r) {
+                        const long long mm = m0 + q * 32 + r;
+                        pre[r] = 0.0f;
+                        if (mm < a.M && nok) {
+                            if (a.epi == kEpiResid)
+                                pre[r] = a.p * a.S[mm * a.lds + n] + a.F[mm * a.ldf + n] +
+                                         a.X[mm * a.ldx + n];
+                            else
+                                pre[r] = a.C[mm * a.ldc + n];
+                        }
+                    }
+                    const float ws = a.wscale && nok ? a.wscale[n] : 1.0f;
+#pragma unroll 4
+                    for (int r = 0; r < 32; ++r) {
+                        const long long mm = m0 + q * 32 + r;
+                        if (mm < a.M && nok) {
+                            float acc = stg[r * 33 + lane];
+                            if (a.wscale) acc = acc * ws;
+                            a.C[mm * a.ldc + n] =
+                                a.epi == kEpiResid ? acc + pre[r] : pre[r] + acc;
+                        }
+                    }
                 }
                 __syncwarp();
             }
@@ -266,11 +299,11 @@ std::map<int, ActPlanes>& act_cache() {
     return c;
 }
 
-template <int BN, bool I8>
+template <int BN, bool I8, bool LOADS>
 int launch_bn(const GemmArgs& a, const TcWeights& tw, const ActPlanes& ap, cudaStream_t st) {
     using C = TcCfg<BN>;
     static bool attr = false;
-    auto k = tc_gemm_kernel<BN, I8>;
+    auto k = tc_gemm_kernel<BN, I8, LOADS>;
     if (!attr) {
         SN_TRY(cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                C::SMEM),
@@ -372,14 +405,25 @@ int launch_tc_gemm(const GemmArgs& a, const TcWeights& tw, cudaStream_t st) {
     int bn = 32;
     if (mt * ((a.N + 127) / 128) >= sms * 3 / 4) bn = 128;
     else if (mt * ((a.N + 63) / 64) >= sms * 3 / 4) bn = 64;
+    const bool ld = a.epi == kEpiResid || a.epi == kEpiAdd;
     if (tw.int8) {
-        if (bn == 128) return launch_bn<128, true>(a, tw, ap, st);
-        if (bn == 64) return launch_bn<64, true>(a, tw, ap, st);
-        return launch_bn<32, true>(a, tw, ap, st);
+        if (ld) {
+            if (bn == 128) return launch_bn<128, true, true>(a, tw, ap, st);
+            if (bn == 64) return launch_bn<64, true, true>(a, tw, ap, st);
+            return launch_bn<32, true, true>(a, tw, ap, st);
+        }
+        if (bn == 128) return launch_bn<128, true, false>(a, tw, ap, st);
+        if (bn == 64) return launch_bn<64, true, false>(a, tw, ap, st);
+        return launch_bn<32, true, false>(a, tw, ap, st);
     }
-    if (bn == 128) return launch_bn<128, false>(a, tw, ap, st);
-    if (bn == 64) return launch_bn<64, false>(a, tw, ap, st);
-    return launch_bn<32, false>(a, tw, ap, st);
+    if (ld) {
+        if (bn == 128) return launch_bn<128, false, true>(a, tw, ap, st);
+        if (bn == 64) return launch_bn<64, false, true>(a, tw, ap, st);
+        return launch_bn<32, false, true>(a, tw, ap, st);
+    }
+    if (bn == 128) return launch_bn<128, false, false>(a, tw, ap, st);
+    if (bn == 64) return launch_bn<64, false, false>(a, tw, ap, st);
+    return launch_bn<32, false, false>(a, tw, ap, st);
 }
 
 }  // namespace sn
