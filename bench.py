@@ -413,8 +413,9 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
     e2e_s = dist.max(torch, (time.perf_counter() - t0) / reps)
     if B <= 8:  # fused step kernel + argmax
         launches = 2
-    elif B >= 16:  # per layer: prep, 5 x (split + tcgen05 GEMM), gate, row stats; + head, argmax
-        launches = 13 * S.layers + 4
+    elif B >= 16:  # state split; per layer: Ws (side stream), prep, V, U, gate, Wz, LN planes,
+        # Wc (tcgen05 GEMMs fed by planes their producers write); LN planes, head, 2 argmax
+        launches = 8 * S.layers + 5
     else:  # per layer: prep, 5 SIMT GEMMs, gate, row stats; + stats, head, argmax
         launches = 8 * S.layers + 3
     res.update({
@@ -644,6 +645,30 @@ def rwkv_step_cost(S, B, q4_bytes):
     return q4_bytes + state + B * D * 4 + B * V * 4, 2 * B * (L * mats + V * D)
 
 
+def rwkv_launches(S, B, block=128):
+    """Kernels one greedy RWKV-7 step launches (rwkv7.cu enqueue_rk + argmax):
+    a W4A8 matrix is one weight-streaming launch below 16 sequences, or a
+    quantise + tensor-core launch when its shape suits the tensor cores; the
+    first-stage projections of a layer share one such pair when all suit."""
+    D, F = S.dim, S.ffn
+    Rw, Ra, Rv, Rg = S.ranks
+
+    def tc(K, N):
+        return B >= 16 and N >= 32 and K % 128 == 0 and block in (32, 64, 128)
+
+    def mm(K, N):
+        return 2 if tc(K, N) else 1
+
+    n = 1  # embed + LN0
+    for l in range(S.layers):
+        first = [(D, D)] * 3 + [(D, Rw), (D, Ra), (D, Rg)] + ([(D, Rv)] if l > 0 else [])
+        grouped = all(tc(K, N) for K, N in first)
+        n += 1 + (2 if grouped else sum(mm(K, N) for K, N in first))  # prep + first stage
+        n += mm(Rw, D) + mm(Ra, D) + mm(Rg, D) + (mm(Rv, D) if l > 0 else 0)
+        n += 2 + mm(D, D) + 1 + mm(D, F) + mm(F, D)  # mix, heads, out, cmix prep, ffn
+    return n + 2 + 2  # final LN + head (fp32), argmax partials + final
+
+
 def wl_rwkv(args, torch, dist, ours, B):
     from sunnynet_b200 import formats
     S = formats.RWKV_PRESETS["c4"]
@@ -721,7 +746,7 @@ def wl_rwkv(args, torch, dist, ours, B):
                 "e2e": {"value": B * dist.world / e2e_s, "unit": "tokens/s",
                         "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * S.vocab * 4,
                         "call": "sn_abi_rwkv7_step_batch (host ids, host logits)"},
-                "gpu_launches": (S.layers * 20 + 4) * args.steps, "roofline": rl,
+                "gpu_launches": rwkv_launches(S, B) * args.steps, "roofline": rl,
                 "clocks": clk.summary()})
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         formats.write_krwk(ref_blob, w, quant="q4")

@@ -57,6 +57,10 @@ struct GemmArgs {
     long long ldf = 0;
     const float* X = nullptr;
     long long ldx = 0;
+    // tensor-core path only: also store the result as bf16 hi/lo planes
+    // (ld = ldc), the input format of a following tensor-core contraction
+    void* Ch = nullptr;
+    void* Cl = nullptr;
 };
 
 struct TcWeights;

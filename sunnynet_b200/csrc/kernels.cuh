@@ -30,11 +30,24 @@ int launch_w4a8(float* Y, const float* X, const uint8_t* Wq, const void* scale, 
 // The same contraction on the tensor cores (w4a8_tc.cu) for M >= 16 sequences,
 // K % 128 == 0, block in {32, 64, 128}: bit-identical results. Its activation
 // workspace is reserved outside graph capture (w4a8_tc_reserve) before use.
+// `planes`: distinct activation inputs one launch quantises (a group).
 bool w4a8_tc_ok(int M, int K, int N, int block, const void* Wq);
-bool w4a8_tc_ready(int M, int K, int block);
-int w4a8_tc_reserve(int M, int K, int block);
+bool w4a8_tc_ready(int M, int K, int block, int planes = 1);
+int w4a8_tc_reserve(int M, int K, int block, int planes = 1);
 int launch_w4a8_tc(float* Y, const float* X, const uint8_t* Wq, const void* scale, int M, int K,
                    int N, int block, bool fp16, int epi, cudaStream_t st);
+// Up to 8 such contractions sharing M, K, block and scale type in one launch
+// (plus one quantisation launch over their distinct inputs).
+struct W4Problem {
+    float* Y;
+    const float* X;
+    const uint8_t* Wq;
+    const void* scale;
+    int N;
+    int epi;
+};
+int launch_w4a8_tc_group(const W4Problem* pr, int np, int M, int K, int block, bool fp16,
+                         cudaStream_t st);
 int launch_gemv_f32(float* y, const float* x, const float* W, int in, int out, cudaStream_t st);
 // out[b] = argmax of logits row b (lowest id on ties, NaN never chosen);
 // part holds B * kArgChunks float2 of scratch (argmax.cu).

@@ -96,6 +96,23 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// launch_pdl when `pdl`, else a plain launch of the same kernel.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_if(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Error codes written into the device error word.
 enum DevErr : int { kErrNone = 0, kErrWaitTimeout = 1, kErrBadIndex = 2 };
 

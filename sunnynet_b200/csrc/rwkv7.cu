@@ -495,6 +495,11 @@ int load_rwkv(RwkvModel* m, const char* path, int nseq) {
                                    &y.v2, &y.g1, &y.g2, &y.cmk, &y.cmv})
                 SN_TRY(reserve(*M));
         SN_TRY(reserve(m->head));
+        if (!m->ly.empty()) {  // the grouped first-stage projections: six input planes
+            const RkMat& r0 = m->ly[0].rw;
+            if (r0.q4 && w4a8_tc_ok(nseq, r0.in, r0.out, r0.block, r0.q))
+                SN_TRY(w4a8_tc_reserve(nseq, r0.in, r0.block, 6));
+        }
     }
     SN_TRY(cuda_check(cudaDeviceSynchronize(), "rwkv load"));
     m->ready = true;
@@ -535,18 +540,32 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
                                                m->xn, m->planes, m->eps);
         const float *xr = m->planes, *xw = xr + plane, *xk = xw + plane, *xv = xk + plane,
                     *xa = xv + plane, *xg = xa + plane;
-        SN_TRY(mat_mul(A.rw, m->r, xr, B, E_STORE, st));
-        SN_TRY(mat_mul(A.kw, m->k, xk, B, E_STORE, st));
-        SN_TRY(mat_mul(A.vw, m->v, xv, B, E_STORE, st));
-        SN_TRY(mat_mul(A.w1, m->lo_w, xw, B, E_TANH, st));
-        SN_TRY(mat_mul(A.w2, m->dw, m->lo_w, B, E_STORE, st));
-        if (l > 0) {
-            SN_TRY(mat_mul(A.v1, m->lo_v, xv, B, E_STORE, st));
-            SN_TRY(mat_mul(A.v2, m->dv, m->lo_v, B, E_STORE, st));
+        {   // first-stage projections of the input mixes (v1 from layer 1 on):
+            // one grouped tensor-core launch when every matrix qualifies
+            const RkMat* gm[7] = {&A.rw, &A.kw, &A.vw, &A.w1, &A.a1, &A.g1, &A.v1};
+            float* gy[7] = {m->r, m->k, m->v, m->lo_w, m->lo_a, m->lo_g, m->lo_v};
+            const float* gx[7] = {xr, xk, xv, xw, xa, xg, xv};
+            const int ge[7] = {E_STORE, E_STORE, E_STORE, E_TANH, E_STORE, E_SIG, E_STORE};
+            const int ng = l > 0 ? 7 : 6;
+            bool grouped = gm[0]->q4 && w4a8_tc_ready(B, D, gm[0]->block, 6);
+            for (int i = 0; i < ng && grouped; ++i)
+                grouped = gm[i]->q4 && gm[i]->in == D && gm[i]->block == gm[0]->block &&
+                          gm[i]->fp16 == gm[0]->fp16 &&
+                          w4a8_tc_ok(B, gm[i]->in, gm[i]->out, gm[i]->block, gm[i]->q);
+            if (grouped) {
+                static const int map[] = {kW4Store, kW4Add, kW4Relu2, kW4Tanh, kW4Sigmoid};
+                W4Problem pr[7];
+                for (int i = 0; i < ng; ++i)
+                    pr[i] = W4Problem{gy[i], gx[i], gm[i]->q, gm[i]->scale, gm[i]->out, map[ge[i]]};
+                ProfScope ps("w4a8_group", st);
+                SN_TRY(launch_w4a8_tc_group(pr, ng, B, D, gm[0]->block, gm[0]->fp16, st));
+            } else {
+                for (int i = 0; i < ng; ++i) SN_TRY(mat_mul(*gm[i], gy[i], gx[i], B, ge[i], st));
+            }
         }
-        SN_TRY(mat_mul(A.a1, m->lo_a, xa, B, E_STORE, st));
+        SN_TRY(mat_mul(A.w2, m->dw, m->lo_w, B, E_STORE, st));
+        if (l > 0) SN_TRY(mat_mul(A.v2, m->dv, m->lo_v, B, E_STORE, st));
         SN_TRY(mat_mul(A.a2, m->da, m->lo_a, B, E_STORE, st));
-        SN_TRY(mat_mul(A.g1, m->lo_g, xg, B, E_SIG, st));
         SN_TRY(mat_mul(A.g2, m->g, m->lo_g, B, E_STORE, st));
         rk_mix_kernel<<<ew, 256, 0, st>>>(B, D, l == 0 ? 1 : 0, m->dw, A.w0, m->dv, A.v0, m->da,
                                          A.a0, A.kkw, A.kaw, m->ww, m->v, m->vfirst, m->a, m->k,

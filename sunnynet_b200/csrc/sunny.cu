@@ -68,9 +68,12 @@ __global__ void prep_kernel(int D, int K, int KH, int layer, int L, const int32_
                             float* __restrict__ raw_out, float* __restrict__ at,
                             float* __restrict__ hist, int32_t* __restrict__ pos,
                             const float* __restrict__ g, const float* __restrict__ c,
-                            const float* __restrict__ dw, float eps) {
+                            const float* __restrict__ dw, float eps,
+                            __nv_bfloat16* __restrict__ ath = nullptr,
+                            __nv_bfloat16* __restrict__ atl = nullptr) {
     __shared__ float red[32];
     pdl_trigger();  // the next GEMV may start prefetching its weights
+    pdl_wait();     // no-op unless launched with programmatic serialization
     const int b = blockIdx.x;
     // ring position of this (sequence, layer); every thread reads it before the
     // block-wide barriers below, thread 0 advances it at the end
@@ -109,6 +112,7 @@ __global__ void prep_kernel(int D, int K, int KH, int layer, int L, const int32_
             hb[(size_t)(((p % KH) + KH) % KH) * D + i] = r;
         }
         at[(size_t)b * D + i] = a;
+        if (ath) store_split(ath, atl, (long long)b * D + i, a);
         if (raw_out) raw_out[(size_t)b * D + i] = r;
     }
     if (threadIdx.x == 0) pos[b * L + layer] = p + 1;
@@ -118,8 +122,10 @@ __global__ void prep_kernel(int D, int K, int KH, int layer, int L, const int32_
 __global__ void gate_kernel(int B, int D, int G, int L, int layer, const float* __restrict__ q,
                             const float* __restrict__ delta, float* __restrict__ s,
                             float* __restrict__ u, float* __restrict__ gate_out, int clamp,
-                            float p_floor) {
+                            float p_floor, __nv_bfloat16* __restrict__ uh = nullptr,
+                            __nv_bfloat16* __restrict__ ul = nullptr) {
     pdl_trigger();
+    pdl_wait();
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (i >= (long long)B * D) return;
     const int b = (int)(i / D), d = (int)(i % D);
@@ -134,6 +140,7 @@ __global__ void gate_kernel(int B, int D, int G, int L, int layer, const float* 
     float* sp = s + ((size_t)b * L + layer) * D + d;
     *sp = p * *sp + (1.0f - p) * uu;
     u[i] = uu;
+    if (uh) store_split(uh, ul, i, uu);
     if (gate_out) gate_out[i] = g0;
 }
 
@@ -155,6 +162,31 @@ __global__ void rowstats_kernel(int n, const float* __restrict__ X, long long ld
         mu[blockIdx.x] = mean;
         rs[blockIdx.x] = r;
     }
+}
+
+// Row LN written straight into bf16 planes: the statistics as rowstats_kernel
+// computes them, then ((x - mu) * rs) * g + c per element (the order the
+// contraction prologue uses), one CTA per row.
+__global__ void ln_split_kernel(int n, const float* __restrict__ X, long long ldx,
+                                const float* __restrict__ g, const float* __restrict__ c,
+                                __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo,
+                                float eps) {
+    __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();
+    const float* xr = X + blockIdx.x * ldx;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s += xr[i];
+    const float mean = block_sum(s, red) / (float)n;
+    float v = 0.0f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float d = xr[i] - mean;
+        v += d * d;
+    }
+    const float r = 1.0f / sqrtf(block_sum(v, red) / (float)n + eps);
+    const long long o = (long long)blockIdx.x * n;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        store_split(hi, lo, o + i, __fmul_rn(__fmul_rn(xr[i] - mean, r), g[i]) + c[i]);
 }
 
 // y = LN(z) materialised (debug dumps only).
@@ -347,6 +379,16 @@ struct SunnyModel {
     float *gate = nullptr, *sfb = nullptr, *z = nullptr, *mu = nullptr, *rs = nullptr;
     float *logits = nullptr, *yn = nullptr;
     float2* apart = nullptr;  // argmax partials (B x kArgChunks)
+    // tensor-core step (B >= 16): bf16 planes of each contraction's input,
+    // the per-layer state feedback sfb of all layers, and the side stream the
+    // feedback contractions run on (with its fork / join events)
+    bool tc_step = false;
+    TcAct p_at, p_v, p_u, p_z, p_x, p_s;
+    std::vector<TcAct> p_sl;  // layer l's rows of p_s
+    float* sfb_all = nullptr;  // [L][nseq][D]
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_split = nullptr;
+    std::vector<cudaEvent_t> ev_ws;
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;  // (B, with head) -> graph
     // chunked prefill: buffers of B*Tc rows, one graph per (B, Tc, head)
     long long crows = 0;
@@ -369,6 +411,10 @@ struct SunnyModel {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
         for (auto& kv : cgraphs) cudaGraphExecDestroy(kv.second);
         if (cap) cudaStreamDestroy(cap);
+        if (side) cudaStreamDestroy(side);
+        if (ev_fork) cudaEventDestroy(ev_fork);
+        if (ev_split) cudaEventDestroy(ev_split);
+        for (cudaEvent_t e : ev_ws) cudaEventDestroy(e);
         for (void* p : allocs) cudaFree(p);
     }
 
@@ -590,6 +636,33 @@ int load_model(SunnyModel* m, const char* path, int nseq, bool half, const int* 
     m->apart = m->dalloc<float2>(n * kArgChunks);
     if (!m->logits || !m->rs || !m->apart) return fail(SN_E_NOMEM, "device allocation failed");
     SN_TRY(cuda_check(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking), "stream"));
+    bool tc_all = nseq >= 16 && m->thead.ready && D % 8 == 0 && R % 8 == 0 && I % 8 == 0;
+    for (int l = 0; l < L && tc_all; ++l) {
+        const SunnyLayer& y = m->ly[l];
+        tc_all = y.tV.ready && y.tU.ready && y.tWz.ready && y.tWc.ready && y.tWs.ready;
+    }
+    if (tc_all) {
+        auto al = [](size_t nb, void* o) -> void* { return ((SunnyModel*)o)->dalloc<uint8_t>(nb); };
+        SN_TRY(tc_act_alloc(&m->p_at, D, nseq, al, m));
+        SN_TRY(tc_act_alloc(&m->p_v, R, nseq, al, m));
+        SN_TRY(tc_act_alloc(&m->p_u, D, nseq, al, m));
+        SN_TRY(tc_act_alloc(&m->p_z, I, nseq, al, m));
+        SN_TRY(tc_act_alloc(&m->p_x, D, nseq, al, m));
+        SN_TRY(tc_act_alloc(&m->p_s, D, n * L, al, m));
+        m->p_sl.resize(L);
+        for (int l = 0; l < L; ++l)
+            SN_TRY(tc_act_view(&m->p_sl[l], m->p_s, (long long)l * D, nseq, (long long)L * D, D));
+        m->sfb_all = m->dalloc<float>(n * L * D);
+        if (!m->sfb_all) return fail(SN_E_NOMEM, "device allocation failed");
+        SN_TRY(cuda_check(cudaStreamCreateWithFlags(&m->side, cudaStreamNonBlocking), "stream"));
+        SN_TRY(cuda_check(cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming), "event"));
+        SN_TRY(cuda_check(cudaEventCreateWithFlags(&m->ev_split, cudaEventDisableTiming), "event"));
+        m->ev_ws.assign(L, nullptr);
+        for (int l = 0; l < L; ++l)
+            SN_TRY(cuda_check(cudaEventCreateWithFlags(&m->ev_ws[l], cudaEventDisableTiming),
+                              "event"));
+        m->tc_step = !getenv("SN_TC_SPLIT_STEP");
+    }
     cudaMemset(m->s, 0, n * L * D * 4);
     cudaMemset(m->hist, 0, n * L * m->KH * D * 4);
     cudaMemset(m->pos, 0, n * L * 4);
@@ -727,6 +800,125 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
     return cuda_check(cudaGetLastError(), "step launch");
 }
 
+// The batched step on the tensor cores (B >= 16, model->tc_step). Same
+// arithmetic as enqueue_step, arranged for the tensor-core contractions:
+//  - each contraction's input is written as bf16 planes by the kernel that
+//    produces it (prep: at; V epilogue: v; gate: u; ln_split: LN(z) and the
+//    final LN(x)), so no contraction needs a split launch of its own;
+//  - the feedback contractions sfb_l = s_l(old) Ws_l^T read only the state
+//    left by the previous step, so all L of them run on a side stream (after
+//    one split of the whole state) while the layer chain runs; gate_0 waits
+//    for that split (the gates overwrite the state) and Wc_l for sfb_l.
+// With side == st (profile mode) everything runs in order on one stream.
+int enqueue_step_tc(SunnyModel* m, int B, bool with_head, cudaStream_t st, cudaStream_t side) {
+    const int D = m->D, I = m->I, R = m->R, L = m->L;
+    const size_t n = (size_t)m->nseq;
+    const bool fork = side != st;
+    if (fork) {
+        SN_TRY(cuda_check(cudaEventRecord(m->ev_fork, st), "fork"));
+        SN_TRY(cuda_check(cudaStreamWaitEvent(side, m->ev_fork, 0), "fork"));
+    }
+    {
+        ProfScope ps("split_state", side);
+        SN_TRY(launch_split_rows(m->s, (long long)B * L, D, D, m->p_s, side));
+    }
+    if (fork) SN_TRY(cuda_check(cudaEventRecord(m->ev_split, side), "split event"));
+    for (int l = 0; l < L; ++l) {
+        const SunnyLayer& y = m->ly[l];
+        GemmArgs gs = gemm(B, D, D, m->s + (size_t)l * D, y.Ws, y.sWs, m->sfb_all + l * n * D);
+        gs.lda = (long long)L * D;
+        {
+            ProfScope ps("gemm_Ws", side);
+            SN_TRY(launch_tc_gemm_act(gs, y.tWs, m->p_sl[l], side));
+        }
+        if (fork) SN_TRY(cuda_check(cudaEventRecord(m->ev_ws[l], side), "Ws event"));
+    }
+    for (int l = 0; l < L; ++l) {
+        const SunnyLayer& y = m->ly[l];
+        {
+            ProfScope ps("prep_ln_taps", st);
+            const dim3 g1(B), t256(256);
+            if (l > 0)  // follows Wc of the previous layer on this stream
+                SN_TRY(cuda_check(
+                    launch_pdl(prep_kernel, g1, t256, 0, st, D, m->K, m->KH, l, L,
+                               (const int32_t*)m->tok, m->vocab, rt().d_err,
+                               (const float*)m->embed, m->x, (float*)nullptr, m->at, m->hist,
+                               m->pos, (const float*)y.ni_g, (const float*)y.ni_c,
+                               (const float*)y.dw, m->eps, m->p_at.hi, m->p_at.lo),
+                    "prep launch"));
+            else
+                prep_kernel<<<g1, t256, 0, st>>>(D, m->K, m->KH, l, L, m->tok, m->vocab,
+                                                 rt().d_err, m->embed, m->x, nullptr, m->at,
+                                                 m->hist, m->pos, y.ni_g, y.ni_c, y.dw, m->eps,
+                                                 m->p_at.hi, m->p_at.lo);
+        }
+        {
+            GemmArgs gv = gemm(B, R, D, m->at, y.V, y.sV, m->v);
+            gv.Ch = m->p_v.hi;
+            gv.Cl = m->p_v.lo;
+            ProfScope ps("gemm_V", st);
+            SN_TRY(launch_tc_gemm_act(gv, y.tV, m->p_at, st, true));
+        }
+        {
+            ProfScope ps("gemm_U", st);
+            SN_TRY(launch_tc_gemm_act(gemm(B, 2 * D, R, m->v, y.U, y.sU, m->q), y.tU, m->p_v, st,
+                                      true));
+        }
+        if (l == 0 && fork) SN_TRY(cuda_check(cudaStreamWaitEvent(st, m->ev_split, 0), "join"));
+        {
+            ProfScope ps("gate_state", st);
+            // after the join (layer 0) a plain launch; later layers follow U directly
+            SN_TRY(cuda_check(
+                launch_pdl_if(l > 0 || !fork, gate_kernel,
+                              dim3((unsigned)(((long long)B * D + 255) / 256)), dim3(256), 0, st,
+                              B, D, m->G, L, l, (const float*)m->q, (const float*)y.delta, m->s,
+                              m->u, (float*)nullptr, m->clamp, m->p_floor, m->p_u.hi, m->p_u.lo),
+                "gate launch"));
+        }
+        {
+            GemmArgs gz = gemm(B, I, D, m->u, y.Wz, y.sWz, m->z);
+            gz.epi = kEpiWedge;
+            gz.p = y.a_tanh;
+            ProfScope ps("gemm_Wz", st);
+            SN_TRY(launch_tc_gemm_act(gz, y.tWz, m->p_u, st, true));
+        }
+        {
+            ProfScope ps("rowstats", st);
+            SN_TRY(cuda_check(launch_pdl(ln_split_kernel, dim3(B), dim3(256), 0, st, I,
+                                         (const float*)m->z, (long long)I, (const float*)y.nm_g,
+                                         (const float*)y.nm_c, m->p_z.hi, m->p_z.lo, m->eps),
+                              "ln_split launch"));
+        }
+        if (fork) SN_TRY(cuda_check(cudaStreamWaitEvent(st, m->ev_ws[l], 0), "join"));
+        GemmArgs gc = gemm(B, D, I, m->z, y.Wc, y.sWc, m->x);
+        gc.epi = kEpiResid;
+        gc.p = y.b_gain;
+        gc.S = m->s + (size_t)l * D;
+        gc.lds = (long long)L * D;
+        gc.F = m->sfb_all + l * n * D;
+        gc.ldf = D;
+        gc.X = m->x;
+        gc.ldx = D;
+        {
+            ProfScope ps("gemm_Wc", st);  // after the join with sfb_l: a plain launch
+            SN_TRY(launch_tc_gemm_act(gc, y.tWc, m->p_z, st, !fork));
+        }
+    }
+    if (with_head) {
+        {
+            ProfScope ps("rowstats", st);
+            SN_TRY(cuda_check(launch_pdl(ln_split_kernel, dim3(B), dim3(256), 0, st, D,
+                                         (const float*)m->x, (long long)D, (const float*)m->no_g,
+                                         (const float*)m->no_c, m->p_x.hi, m->p_x.lo, m->eps),
+                              "ln_split launch"));
+        }
+        ProfScope ps("gemm_head", st);
+        SN_TRY(launch_tc_gemm_act(gemm(B, m->vocab, D, m->x, m->head, m->shead, m->logits),
+                                  m->thead, m->p_x, st, true));
+    }
+    return cuda_check(cudaGetLastError(), "tc step launch");
+}
+
 // Profile mode: per-phase times of one fused step from its device timestamps
 // (slot 1+8p+j of phase p: j = 0 loads done, 1 row statistics done, 2 inputs
 // ready, 3 weights ready, 4 rows done, 5 barrier passed). A part's time is the
@@ -787,14 +979,17 @@ int fused_trace_report(SunnyModel* m, const FusedArgs& fa, cudaStream_t st) {
 // Replay (capturing on first use) the graph of a B-sequence step.
 int run_step(SunnyModel* m, int B, bool with_head) {
     cudaStream_t st = stream();
-    if (prof_on()) return enqueue_step(m, B, with_head, st);  // bracket kernels, no graph
+    const bool tc = m->tc_step && B >= 16;
+    if (prof_on())  // bracket kernels, no graph
+        return tc ? enqueue_step_tc(m, B, with_head, st, st) : enqueue_step(m, B, with_head, st);
     auto key = std::make_pair(B, with_head ? 1 : 0);
     auto it = m->graphs.find(key);
     if (it == m->graphs.end()) {
         cudaGraph_t g = nullptr;
         SN_TRY(cuda_check(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeThreadLocal),
                           "begin capture"));
-        const int rc = enqueue_step(m, B, with_head, m->cap);
+        const int rc = tc ? enqueue_step_tc(m, B, with_head, m->cap, m->side)
+                          : enqueue_step(m, B, with_head, m->cap);
         const cudaError_t e = cudaStreamEndCapture(m->cap, &g);
         if (rc != SN_OK) {
             if (g) cudaGraphDestroy(g);

@@ -101,6 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const int nk = (a.K + BK - 1) / BK;
+    pdl_trigger();  // the next kernel may start its own prologue
     auto stage_ptr = [&](int s, int part) -> uint8_t* {  // 0 Ah, 1 Al, 2 Wh, 3 Wl
         return sb + s * C::STAGE +
                (part < 2 ? part * C::A_BYTES : 2 * C::A_BYTES + (part - 2) * C::W_BYTES);
@@ -130,19 +131,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {  // --------------------------------------------- TMA producer
         if (lane == 0) {
             const uint32_t bytes = 2 * C::A_BYTES + (I8 ? 1 : 2) * C::W_BYTES;
+            // the weight tiles of the first S stages do not depend on the
+            // previous kernel: in flight before waiting for it (programmatic
+            // launch; pdl_wait is a no-op otherwise)
+            const int pre = nk < S ? nk : S;
+            for (int kt = 0; kt < pre; ++kt) {
+                mbar_expect_tx(&full[kt], bytes);
+                tma_load_2d(stage_ptr(kt, 2), &twh, kt * BK, n0, &full[kt]);
+                if (!I8) tma_load_2d(stage_ptr(kt, 3), &twl, kt * BK, n0, &full[kt]);
+            }
+            pdl_wait();
             int issued = 0;
             for (int kt = 0; kt < nk; ++kt) {
                 const int s = kt % S;
-                if (*give_up) break;
-                if (kt >= S && !mbar_wait(&empty[s], ((kt / S) - 1) & 1, err)) {
-                    *give_up = 1;
-                    break;
+                if (kt >= pre) {  // stages of the first round are never abandoned half-loaded
+                    if (*give_up) break;
+                    if (!mbar_wait(&empty[s], ((kt / S) - 1) & 1, err)) {
+                        *give_up = 1;
+                        break;
+                    }
+                    mbar_expect_tx(&full[s], bytes);
+                    tma_load_2d(stage_ptr(s, 2), &twh, kt * BK, n0, &full[s]);
+                    if (!I8) tma_load_2d(stage_ptr(s, 3), &twl, kt * BK, n0, &full[s]);
                 }
-                mbar_expect_tx(&full[s], bytes);
                 tma_load_2d(stage_ptr(s, 0), &tah, kt * BK, m0, &full[s]);
                 tma_load_2d(stage_ptr(s, 1), &tal, kt * BK, m0, &full[s]);
-                tma_load_2d(stage_ptr(s, 2), &twh, kt * BK, n0, &full[s]);
-                if (!I8) tma_load_2d(stage_ptr(s, 3), &twl, kt * BK, n0, &full[s]);
                 issued = kt + 1;
             }
             // never leave with a tile load in flight: wait for the last use of each stage
@@ -178,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {  // ------------------------------------------------ epilogue (warps 2-5)
         const int q = warp & 3;  // TMEM lane quarter this warp may read
+        pdl_wait();  // the epilogue reads (and overwrites) the previous kernels' outputs
         const bool ok = mbar_wait(acc_full, 0, err);
         tc_fence_after();
         if (ok && !*give_up) {
@@ -197,9 +211,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 4
                     for (int r = 0; r < 32; ++r) {
                         const int mm = m0 + q * 32 + r;
-                        if (mm < a.M && nok)
-                            a.C[(long long)mm * a.ldc + n] =
-                                gemm_epilogue(a, mm, n, stg[r * 33 + lane]);
+                        if (mm < a.M && nok) {
+                            const long long o = (long long)mm * a.ldc + n;
+                            const float y = gemm_epilogue(a, mm, n, stg[r * 33 + lane]);
+                            a.C[o] = y;
+                            if (a.Ch)
+                                store_split((__nv_bfloat16*)a.Ch, (__nv_bfloat16*)a.Cl, o, y);
+                        }
                     }
                 } else {
                     // the epilogue's other operands for all 32 rows are loaded
@@ -225,8 +243,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (mm < a.M && nok) {
                             float acc = stg[r * 33 + lane];
                             if (a.wscale) acc = acc * ws;
-                            a.C[mm * a.ldc + n] =
-                                a.epi == kEpiResid ? acc + pre[r] : pre[r] + acc;
+                            const float y = a.epi == kEpiResid ? acc + pre[r] : pre[r] + acc;
+                            a.C[mm * a.ldc + n] = y;
+                            if (a.Ch)
+                                store_split((__nv_bfloat16*)a.Ch, (__nv_bfloat16*)a.Cl,
+                                            mm * a.ldc + n, y);
                         }
                     }
                 }
@@ -300,7 +321,8 @@ std::map<int, ActPlanes>& act_cache() {
 }
 
 template <int BN, bool I8, bool LOADS>
-int launch_bn(const GemmArgs& a, const TcWeights& tw, const ActPlanes& ap, cudaStream_t st) {
+int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
+              const CUtensorMap& tal, cudaStream_t st, bool pdl) {
     using C = TcCfg<BN>;
     static bool attr = false;
     auto k = tc_gemm_kernel<BN, I8, LOADS>;
@@ -312,8 +334,11 @@ int launch_bn(const GemmArgs& a, const TcWeights& tw, const ActPlanes& ap, cudaS
     }
     const int bi = BN == 32 ? 0 : (BN == 64 ? 1 : 2);
     dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
-    k<<<grid, kThreads, C::SMEM, st>>>(ap.tm_hi, ap.tm_lo, tw.tm_hi[bi], tw.tm_lo[bi], a,
-                                       rt().d_err);
+    if (pdl)
+        return cuda_check(launch_pdl(k, grid, dim3(kThreads), C::SMEM, st, tah, tal, tw.tm_hi[bi],
+                                     tw.tm_lo[bi], a, rt().d_err),
+                          "tc_gemm launch");
+    k<<<grid, kThreads, C::SMEM, st>>>(tah, tal, tw.tm_hi[bi], tw.tm_lo[bi], a, rt().d_err);
     return cuda_check(cudaGetLastError(), "tc_gemm launch");
 }
 
@@ -394,36 +419,86 @@ bool tc_usable(const GemmArgs& a, const TcWeights* tw) {
     return it != act_cache().end() && it->second.cap >= a.M;  // planes reserved up front
 }
 
-int launch_tc_gemm(const GemmArgs& a, const TcWeights& tw, cudaStream_t st) {
-    const ActPlanes& ap = act_cache()[a.K];
-    split_act_kernel<<<grid_blocks((long long)a.M * (a.K / 8), 256, 8), 256, 0, st>>>(a, ap.hi,
-                                                                                     ap.lo);
-    SN_TRY(cuda_check(cudaGetLastError(), "split_act launch"));
-    // widest tile that still gives about a wave of CTAs
+namespace {
+
+// widest tile that still gives about a wave of CTAs
+int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
+                 const CUtensorMap& tal, cudaStream_t st, bool pdl) {
     const long long mt = (a.M + BM - 1) / BM;
     const long long sms = rt().num_sms;
     int bn = 32;
     if (mt * ((a.N + 127) / 128) >= sms * 3 / 4) bn = 128;
     else if (mt * ((a.N + 63) / 64) >= sms * 3 / 4) bn = 64;
     const bool ld = a.epi == kEpiResid || a.epi == kEpiAdd;
+#define SN_TC_BN(I8, LD)                                                          \
+    return bn == 128 ? launch_bn<128, I8, LD>(a, tw, tah, tal, st, pdl)            \
+                     : (bn == 64 ? launch_bn<64, I8, LD>(a, tw, tah, tal, st, pdl) \
+                                 : launch_bn<32, I8, LD>(a, tw, tah, tal, st, pdl))
     if (tw.int8) {
-        if (ld) {
-            if (bn == 128) return launch_bn<128, true, true>(a, tw, ap, st);
-            if (bn == 64) return launch_bn<64, true, true>(a, tw, ap, st);
-            return launch_bn<32, true, true>(a, tw, ap, st);
-        }
-        if (bn == 128) return launch_bn<128, true, false>(a, tw, ap, st);
-        if (bn == 64) return launch_bn<64, true, false>(a, tw, ap, st);
-        return launch_bn<32, true, false>(a, tw, ap, st);
+        if (ld) SN_TC_BN(true, true);
+        SN_TC_BN(true, false);
     }
-    if (ld) {
-        if (bn == 128) return launch_bn<128, false, true>(a, tw, ap, st);
-        if (bn == 64) return launch_bn<64, false, true>(a, tw, ap, st);
-        return launch_bn<32, false, true>(a, tw, ap, st);
-    }
-    if (bn == 128) return launch_bn<128, false, false>(a, tw, ap, st);
-    if (bn == 64) return launch_bn<64, false, false>(a, tw, ap, st);
-    return launch_bn<32, false, false>(a, tw, ap, st);
+    if (ld) SN_TC_BN(false, true);
+    SN_TC_BN(false, false);
+#undef SN_TC_BN
+}
+
+}  // namespace
+
+int launch_tc_gemm(const GemmArgs& a, const TcWeights& tw, cudaStream_t st) {
+    const ActPlanes& ap = act_cache()[a.K];
+    split_act_kernel<<<grid_blocks((long long)a.M * (a.K / 8), 256, 8), 256, 0, st>>>(a, ap.hi,
+                                                                                     ap.lo);
+    SN_TRY(cuda_check(cudaGetLastError(), "split_act launch"));
+    return launch_tiles(a, tw, ap.tm_hi, ap.tm_lo, st, false);
+}
+
+int tc_act_alloc(TcAct* p, int K, long long rows, void* (*alloc)(size_t, void*), void* owner) {
+    *p = TcAct{};
+    if (K % 8 != 0 || rows <= 0) return fail(SN_E_INVAL, "tc planes: K %% 8 or rows");
+    p->hi = (__nv_bfloat16*)alloc((size_t)rows * K * 2, owner);
+    p->lo = (__nv_bfloat16*)alloc((size_t)rows * K * 2, owner);
+    if (!p->hi || !p->lo) return fail(SN_E_NOMEM, "tc planes (%lld x %d)", rows, K);
+    return tc_act_view(p, *p, 0, rows, K, K);
+}
+
+int tc_act_view(TcAct* v, const TcAct& base, long long off, long long rows, long long ld, int K) {
+    if (off % 8 || ld % 8 || K % 8 || rows <= 0) return fail(SN_E_INVAL, "tc plane view");
+    TcAct t;
+    t.K = K;
+    t.rows = rows;
+    t.ld = ld;
+    t.hi = base.hi + off;
+    t.lo = base.lo + off;
+    SN_TRY(encode_tiled(&t.tm_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, t.hi, K, rows, ld * 2, BK, BM,
+                        CU_TENSOR_MAP_SWIZZLE_128B));
+    SN_TRY(encode_tiled(&t.tm_lo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, t.lo, K, rows, ld * 2, BK, BM,
+                        CU_TENSOR_MAP_SWIZZLE_128B));
+    t.ready = true;
+    *v = t;
+    return SN_OK;
+}
+
+int launch_split_rows(const float* A, long long rows, int K, long long lda, const TcAct& dst,
+                      cudaStream_t st) {
+    if (!dst.ready || dst.K != K || dst.ld != K || rows > dst.rows || K % 8 || lda % 4 ||
+        (uintptr_t)A % 16)
+        return fail(SN_E_INVAL, "split_rows: planes do not fit");
+    GemmArgs g;
+    g.M = (int)rows;
+    g.K = K;
+    g.A = A;
+    g.lda = lda;
+    split_act_kernel<<<grid_blocks(rows * (K / 8), 256, 8), 256, 0, st>>>(g, dst.hi, dst.lo);
+    return cuda_check(cudaGetLastError(), "split_rows launch");
+}
+
+int launch_tc_gemm_act(const GemmArgs& a, const TcWeights& tw, const TcAct& act, cudaStream_t st,
+                       bool pdl) {
+    if (!tw.ready || !act.ready || a.K != tw.K || a.N != tw.N || a.K != act.K || a.M > act.rows ||
+        a.M <= 0)
+        return fail(SN_E_INVAL, "tc_gemm_act: shape does not match the planes / weights");
+    return launch_tiles(a, tw, act.tm_hi, act.tm_lo, st, pdl);
 }
 
 }  // namespace sn

@@ -44,4 +44,40 @@ bool tc_usable(const GemmArgs& a, const TcWeights* tw);
 
 int launch_tc_gemm(const GemmArgs& a, const TcWeights& tw, cudaStream_t st);
 
+// bf16 activation planes A' = hi + lo, (rows, K) with rows `ld` elements
+// apart, and their TMA maps (box 64 x 128, SWIZZLE_128B). The kernel that
+// produces a contraction's input writes them directly (store_split), so the
+// contraction needs no split launch of its own.
+struct TcAct {
+    int K = 0;
+    long long rows = 0, ld = 0;
+    __nv_bfloat16* hi = nullptr;
+    __nv_bfloat16* lo = nullptr;
+    CUtensorMap tm_hi, tm_lo;
+    bool ready = false;
+};
+
+// Allocate (rows, K) planes, ld = K. K % 8 == 0 (16-byte TMA row stride).
+int tc_act_alloc(TcAct* p, int K, long long rows, void* (*alloc)(size_t, void*), void* owner);
+// View of `rows` rows of K elements starting `off` elements into base's
+// planes, `ld` elements apart (off and ld multiples of 8).
+int tc_act_view(TcAct* v, const TcAct& base, long long off, long long rows, long long ld, int K);
+// Split fp32 rows (rows, K) with row stride lda into dst's planes (ld = K).
+int launch_split_rows(const float* A, long long rows, int K, long long lda, const TcAct& dst,
+                      cudaStream_t st);
+// The contraction with A' read from planes already written (a.A, a.mu are not
+// read; the epilogue operands and a.Ch / a.Cl are as for launch_tc_gemm).
+// pdl: launched with programmatic serialization: its barrier setup, TMEM
+// allocation and first weight tiles overlap the previous kernel's tail.
+int launch_tc_gemm_act(const GemmArgs& a, const TcWeights& tw, const TcAct& act, cudaStream_t st,
+                       bool pdl = false);
+
+// hi = bf16(v), lo = bf16(v - hi): the split every plane writer uses
+__device__ __forceinline__ void store_split(__nv_bfloat16* hi, __nv_bfloat16* lo, long long i,
+                                            float v) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = h;
+    lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+}
+
 }  // namespace sn

@@ -12,12 +12,17 @@
 // accumulation stays in the epilogue with round-to-nearest mul/add, so every
 // output equals the SIMT GEMV's (and the reference's) bit for bit.
 //
-// Two launches per contraction:
+// Two launches per group of contractions (up to kW4MaxGroup problems sharing
+// M, K, the block size and the scale type, e.g. the seven projections of an
+// RWKV-7 layer's input mixes):
 //   quant_rows_kernel  activation rows -> codes (M,K) int8 + per-block scale
-//                      and code sum (a warp per (row, block), the reference's
-//                      arithmetic), once per contraction
-//   w4a8_tc_kernel     one CTA per 128 sequences x BN output rows; K walks in
-//                      128-byte slabs through an S-deep shared-memory ring
+//                      and code sum (a warp per (input, row, block), the
+//                      reference's arithmetic), once per distinct input
+//   w4a8_tc_kernel     persistent, one CTA per SM over the tiles (problem,
+//                      128 sequences, BN output rows), the problem found from
+//                      a prefix of tile counts; K walks in 128-byte slabs
+//                      through an S-deep shared-memory ring that, like the two
+//                      accumulator slots, carries over from tile to tile
 //     warp 0     TMA: activation codes (SWIZZLE_128B box 128x128) and the
 //                packed nibble rows (box 64 B x BN), one complete_tx barrier
 //     warps 6-9  dequant in the mainloop: unpack each slab's nibbles to u8
@@ -29,7 +34,8 @@
 //                into one of two accumulator slots, commits the slot
 //     warps 2-5  per block: tcgen05.ld the slot (warp w reads TMEM lanes of
 //                quarter w%4 = its 32 sequences), release it, accumulate in
-//                block order in registers; finally the epilogue and stores
+//                block order in registers; per tile the epilogue, rows staged
+//                in shared memory so each store is one coalesced row segment
 // Every wait is bounded; a role that gives up records the error and leaves
 // its loop, the MMA issuer waits for its own MMAs, the TMA issuer for its own
 // loads, and the CTA frees its TMEM.
@@ -57,6 +63,29 @@ struct W4Cfg {
     static constexpr int STAGE = A_BYTES + U_BYTES + P_BYTES;  // multiple of 1024
 };
 
+constexpr int kW4MaxGroup = 8;
+
+// One launch's problems: tensor maps of each problem's activation codes and
+// packed weights, outputs, scales, activation block scales and code sums.
+struct W4Group {
+    CUtensorMap ta[kW4MaxGroup];
+    CUtensorMap tw[kW4MaxGroup];
+    float* Y[kW4MaxGroup];
+    const void* scale[kW4MaxGroup];
+    const float* sx[kW4MaxGroup];
+    const int* xs[kW4MaxGroup];
+    int N[kW4MaxGroup];
+    int epi[kW4MaxGroup];
+    int tile0[kW4MaxGroup + 1];  // first CTA of each problem; tile0[np] = grid size
+    int np;
+};
+
+// The distinct inputs of a group, quantised into consecutive planes.
+struct W4QGroup {
+    const float* X[kW4MaxGroup];
+    int n;
+};
+
 __device__ __forceinline__ float load_scale_w(const void* s, size_t i, bool fp16) {
     return fp16 ? __half2float(reinterpret_cast<const __half*>(s)[i])
                 : reinterpret_cast<const float*>(s)[i];
@@ -75,16 +104,20 @@ __device__ __forceinline__ void w4_apply(float* y, float v, int epi) {
     }
 }
 
-// Warp per (row, block): the reference's activation quantisation.
-__global__ void quant_rows_kernel(const float* __restrict__ X, int M, int K, int block,
+// Warp per (input, row, block): the reference's activation quantisation.
+// Input u's codes go to plane u of codes / sx / xsum.
+__global__ void quant_rows_kernel(const __grid_constant__ W4QGroup q, int M, int K, int block,
                                   int8_t* __restrict__ codes, float* __restrict__ sx,
                                   int* __restrict__ xsum) {
     const int nb = K / block;
     const int lane = threadIdx.x & 31;
     const long long w = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (w >= (long long)M * nb) return;
-    const int m = (int)(w / nb), b = (int)(w % nb);
-    const float* xb = X + (size_t)m * K + (size_t)b * block;
+    if (w >= (long long)q.n * M * nb) return;
+    const int u = (int)(w / ((long long)M * nb));
+    const long long wr = w - (long long)u * M * nb;
+    const int m0 = (int)(wr / nb), b = (int)(wr % nb);
+    const int m = u * M + m0;  // row of the plane-stacked outputs
+    const float* xb = q.X[u] + (size_t)m0 * K + (size_t)b * block;
     float mx = 0.0f;
     for (int i = lane; i < block; i += 32) mx = fmaxf(mx, fabsf(xb[i]));
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -104,22 +137,32 @@ __global__ void quant_rows_kernel(const float* __restrict__ X, int M, int K, int
     }
 }
 
+// Problem, first sequence and first output row of tile t of a group.
+template <int BN>
+__device__ __forceinline__ void w4_tile(const W4Group& g, int t, int& pi, int& m0, int& n0) {
+    pi = 0;
+    while (pi + 1 < g.np && t >= g.tile0[pi + 1]) ++pi;
+    const int ntn = (g.N[pi] + BN - 1) / BN, local = t - g.tile0[pi];
+    m0 = (local / ntn) * kBM;
+    n0 = (local % ntn) * BN;
+}
+
+// Persistent: CTA c takes tiles c, c + gridDim.x, ... and every role walks
+// the same sequence of (tile, slab) and (tile, block) steps, so the ring and
+// the two accumulator slots carry over tile boundaries (the loads and MMAs
+// of the next tile overlap the epilogue of the last).
 template <int BN, bool FP16S>
 __global__ void __launch_bounds__(kW4Threads, 1)
-    w4a8_tc_kernel(const __grid_constant__ CUtensorMap tma, const __grid_constant__ CUtensorMap tmw,
-                   float* __restrict__ Y, const void* __restrict__ scale,
-                   const float* __restrict__ sxg, const int* __restrict__ xsg, int M, int N, int K,
-                   int block, int epi, int* err) {
+    w4a8_tc_kernel(const __grid_constant__ W4Group g, int M, int K, int block, int* err) {
     using C = W4Cfg<BN>;
     constexpr int S = kW4Stages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* ring = smem_raw + (((raw + 1023u) & ~1023u) - raw);
     const int nb = K / block, nslab = K / kSlab, bps = kSlab / block, mpb = block / 32;
-    float* sw_s = reinterpret_cast<float*>(ring + S * C::STAGE);  // [BN][nb]
-    float* sx_s = sw_s + BN * nb;                                 // [128][nb]
-    int* xs_s = reinterpret_cast<int*>(sx_s + kBM * nb);          // [128][nb]
-    uint64_t* full = reinterpret_cast<uint64_t*>(xs_s + kBM * nb + ((BN * nb) & 1));
+    const int ntiles = g.tile0[g.np];
+    float* stg_all = reinterpret_cast<float*>(ring + S * C::STAGE);  // [4][32][BN+1]
+    uint64_t* full = reinterpret_cast<uint64_t*>(stg_all + 4 * 32 * (BN + 1));
     uint64_t* wready = full + S;
     uint64_t* empty = wready + S;
     uint64_t* accf = empty + S;  // [2]
@@ -132,7 +175,6 @@ __global__ void __launch_bounds__(kW4Threads, 1)
     auto sP = [&](int s) { return ring + s * C::STAGE + C::A_BYTES + C::U_BYTES; };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -148,15 +190,6 @@ __global__ void __launch_bounds__(kW4Threads, 1)
         fence_mbar_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
-    for (int i = tid; i < BN * nb; i += kW4Threads) {
-        const int j = i / nb, b = i - j * nb, n = n0 + j;
-        sw_s[i] = n < N ? load_scale_w(scale, (size_t)n * nb + b, FP16S) : 0.0f;
-    }
-    for (int i = tid; i < kBM * nb; i += kW4Threads) {
-        const int r = i / nb, m = m0 + r;
-        sx_s[i] = m < M ? sxg[(size_t)m0 * nb + i] : 0.0f;
-        xs_s[i] = m < M ? xsg[(size_t)m0 * nb + i] : 0;
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -164,28 +197,34 @@ __global__ void __launch_bounds__(kW4Threads, 1)
 
     if (warp == 0) {  // --------------------------------------------------- TMA
         if (lane == 0) {
-            int issued = 0;
-            for (int s = 0; s < nslab; ++s) {
-                const int st = s % S;
-                if (*give_up) break;
-                if (s >= S && !mbar_wait(&empty[st], ((s / S) - 1) & 1, err)) {
-                    *give_up = 1;
-                    break;
+            int gs = 0, issued = 0;
+            bool run = true;
+            for (int t = blockIdx.x; t < ntiles && run; t += gridDim.x) {
+                int pi, m0, n0;
+                w4_tile<BN>(g, t, pi, m0, n0);
+                for (int s = 0; s < nslab; ++s, ++gs) {
+                    const int st = gs % S;
+                    if (*give_up || (gs >= S && !mbar_wait(&empty[st], ((gs / S) - 1) & 1, err))) {
+                        *give_up = 1;
+                        run = false;
+                        break;
+                    }
+                    mbar_expect_tx(&full[st], C::A_BYTES + C::P_BYTES);
+                    tma_load_2d(sA(st), &g.ta[pi], s * kSlab, m0, &full[st]);
+                    tma_load_2d(sP(st), &g.tw[pi], s * (kSlab / 2), n0, &full[st]);
+                    issued = gs + 1;
                 }
-                mbar_expect_tx(&full[st], C::A_BYTES + C::P_BYTES);
-                tma_load_2d(sA(st), &tma, s * kSlab, m0, &full[st]);
-                tma_load_2d(sP(st), &tmw, s * (kSlab / 2), n0, &full[st]);
-                issued = s + 1;
             }
-            for (int s = issued - S < 0 ? 0 : issued - S; s < issued; ++s)
-                mbar_wait(&full[s % S], (s / S) & 1, err);  // no load left in flight
+            for (int x = issued - S < 0 ? 0 : issued - S; x < issued; ++x)
+                mbar_wait(&full[x % S], (x / S) & 1, err);  // no load left in flight
         }
     } else if (warp >= 6) {  // ----------------------------------- unpack nibbles
         const int ut = tid - 192, half = block / 2;
-        for (int s = 0; s < nslab; ++s) {
-            const int st = s % S;
+        const int total = ((ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * nslab;
+        for (int gs = 0; gs < total; ++gs) {
+            const int st = gs % S;
             if (*give_up) break;
-            if (!mbar_wait(&full[st], (s / S) & 1, err)) {
+            if (!mbar_wait(&full[st], (gs / S) & 1, err)) {
                 *give_up = 1;
                 break;
             }
@@ -213,11 +252,13 @@ __global__ void __launch_bounds__(kW4Threads, 1)
                                    | (0u << 10)                     // B: u8
                                    | ((uint32_t)(BN >> 3) << 17)    // N
                                    | ((uint32_t)(kBM >> 4) << 24);  // M
+            const int total =
+                ((ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * nslab;
             int b = 0;
             bool ok = true;
-            for (int s = 0; s < nslab && ok; ++s) {
-                const int st = s % S;
-                if (!mbar_wait(&wready[st], (s / S) & 1, err)) {
+            for (int gs = 0; gs < total && ok; ++gs) {
+                const int st = gs % S;
+                if (!mbar_wait(&wready[st], (gs / S) & 1, err)) {
                     *give_up = 1;
                     break;
                 }
@@ -244,40 +285,83 @@ __global__ void __launch_bounds__(kW4Threads, 1)
             mbar_wait(done, 0, err);  // every MMA issued here has completed
         }
     } else {  // ----------------------------------------------- epilogue, warps 2-5
-        const int q = warp & 3, r = q * 32 + lane, m = m0 + r;
-        float acc[BN];
+        // warp w reads TMEM lanes of quarter w%4: sequences m0 + 32*(w%4) + lane.
+        // The weight scales of a block reach every lane by shuffle (lane j holds
+        // output row n0 + j's), the activation scale and code sum are the
+        // lane's own; the next block's are loaded while this one is applied.
+        const int q = warp & 3;
+        float* stg = stg_all + (warp - 2) * 32 * (BN + 1);
+        int b = 0;  // block counter across tiles (accumulator slot b & 1)
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+            int pi, m0, n0;
+            w4_tile<BN>(g, t, pi, m0, n0);
+            const int N = g.N[pi], m = m0 + q * 32 + lane;
+            const bool mok = m < M;
+            const float* sxr = g.sx[pi] + (size_t)(mok ? m : 0) * nb;
+            const int* xsr = g.xs[pi] + (size_t)(mok ? m : 0) * nb;
+            const void* scale = g.scale[pi];
+            const int na = n0 + lane, nc = n0 + 32 + lane;
+            float acc[BN];
 #pragma unroll
-        for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
-        bool ok = true;
-        for (int b = 0; b < nb; ++b) {
-            const int slot = b & 1;
-            if (*give_up || !mbar_wait(&accf[slot], (b >> 1) & 1, err)) {
-                *give_up = 1;
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const float xs = sx_s[r * nb + b];
-            const int x8 = 8 * xs_s[r * nb + b];
-#pragma unroll
-            for (int j0 = 0; j0 < BN; j0 += 32) {
-                uint32_t d[32];
-                tmem_ld32_u(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * BN + j0), d);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float f = (float)((int)d[j] - x8);
-                    acc[j0 + j] = __fadd_rn(acc[j0 + j],
-                                            __fmul_rn(__fmul_rn(sw_s[(j0 + j) * nb + b], xs), f));
+            for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
+            float xs_c = mok ? sxr[0] : 0.0f;
+            int x8_c = mok ? 8 * xsr[0] : 0;
+            float wa_c = na < N ? load_scale_w(scale, (size_t)na * nb, FP16S) : 0.0f;
+            float wc_c = BN > 32 && nc < N ? load_scale_w(scale, (size_t)nc * nb, FP16S) : 0.0f;
+            bool ok = true;
+            for (int k = 0; k < nb; ++k, ++b) {
+                float xs_n = 0.0f, wa_n = 0.0f, wc_n = 0.0f;
+                int x8_n = 0;
+                if (k + 1 < nb) {
+                    if (mok) {
+                        xs_n = sxr[k + 1];
+                        x8_n = 8 * xsr[k + 1];
+                    }
+                    if (na < N) wa_n = load_scale_w(scale, (size_t)na * nb + k + 1, FP16S);
+                    if (BN > 32 && nc < N) wc_n = load_scale_w(scale, (size_t)nc * nb + k + 1, FP16S);
                 }
-            }
-            tc_fence_before();
-            mbar_arrive(&acce[slot]);
-        }
-        if (ok && m < M) {
-            float* yr = Y + (size_t)m * N;
+                const int slot = b & 1;
+                ok = !*give_up && mbar_wait(&accf[slot], (b >> 1) & 1, err);
+                ok = __all_sync(0xffffffffu, ok);  // one decision per warp
+                if (!ok) {
+                    *give_up = 1;
+                    break;
+                }
+                tc_fence_after();
 #pragma unroll
-            for (int j = 0; j < BN; ++j)
-                if (n0 + j < N) w4_apply(yr + n0 + j, acc[j], epi);
+                for (int j0 = 0; j0 < BN; j0 += 32) {
+                    uint32_t d[32];
+                    tmem_ld32_u(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * BN + j0), d);
+                    const float wl = j0 == 0 ? wa_c : wc_c;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float w = __shfl_sync(0xffffffffu, wl, j);
+                        const float f = (float)((int)d[j] - x8_c);
+                        acc[j0 + j] = __fadd_rn(acc[j0 + j], __fmul_rn(__fmul_rn(w, xs_c), f));
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&acce[slot]);
+                xs_c = xs_n;
+                x8_c = x8_n;
+                wa_c = wa_n;
+                wc_c = wc_n;
+            }
+            if (!ok) break;
+            // rows through shared memory: one coalesced segment per stored row
+#pragma unroll
+            for (int j = 0; j < BN; ++j) stg[lane * (BN + 1) + j] = acc[j];
+            __syncwarp();
+            float* __restrict__ Y = g.Y[pi];
+            const int epi = g.epi[pi];
+            for (int rr = 0; rr < 32; ++rr) {
+                const int mm = m0 + q * 32 + rr;
+                if (mm >= M) break;
+#pragma unroll
+                for (int j = lane; j < BN; j += 32)
+                    if (n0 + j < N) w4_apply(Y + (size_t)mm * N + n0 + j, stg[rr * (BN + 1) + j], epi);
+            }
+            __syncwarp();
         }
     }
     tc_fence_before();
@@ -288,9 +372,9 @@ __global__ void __launch_bounds__(kW4Threads, 1)
     }
 }
 
-// Workspace for the activation codes of one contraction (reused in stream
-// order). Grown outside graph capture only; a superseded buffer stays
-// allocated because captured graphs may still reference it.
+// Workspace for the activation codes of one launch (reused in stream order).
+// Grown outside graph capture only; a superseded buffer stays allocated
+// because captured graphs may still reference it.
 struct W4Work {
     void* p = nullptr;
     size_t cap = 0;
@@ -300,19 +384,18 @@ W4Work& w4_work() {
     return w;
 }
 
-size_t w4_work_bytes(int M, int K, int block) {
-    const size_t nb = (size_t)(K / block);
-    return (((size_t)M * K + 255) / 256) * 256 + (size_t)M * nb * 8;
+size_t w4_codes_bytes(int planes, int M, int K) {
+    return (((size_t)planes * M * K + 255) / 256) * 256;
+}
+size_t w4_work_bytes(int M, int K, int block, int planes) {
+    return w4_codes_bytes(planes, M, K) + (size_t)planes * M * (K / block) * 8;
 }
 
 template <int BN, bool FP16S>
-int launch_bn(const CUtensorMap& ta, const CUtensorMap& tw, float* Y, const void* scale,
-              const float* sx, const int* xs, int M, int N, int K, int block, int epi,
-              cudaStream_t st) {
+int launch_bn(const W4Group& g, int M, int K, int block, cudaStream_t st) {
     using C = W4Cfg<BN>;
-    const int nb = K / block;
-    const size_t smem = 1024 + (size_t)kW4Stages * C::STAGE + 4ull * (BN * nb + 2 * kBM * nb) +
-                        8 + 8ull * (3 * kW4Stages + 5) + 16;
+    const size_t smem = 1024 + (size_t)kW4Stages * C::STAGE + 4ull * 4 * 32 * (BN + 1) +
+                        8ull * (3 * kW4Stages + 5) + 16;
     static int attr = 0;
     if (!attr) {
         SN_TRY(cuda_check(cudaFuncSetAttribute(w4a8_tc_kernel<BN, FP16S>,
@@ -321,10 +404,9 @@ int launch_bn(const CUtensorMap& ta, const CUtensorMap& tw, float* Y, const void
                           "w4a8_tc smem attr"));
         attr = 1;
     }
-    if (smem > 200 * 1024) return fail(SN_E_INVAL, "w4a8_tc: K=%d needs too much shared memory", K);
-    const dim3 grid((N + BN - 1) / BN, (M + kBM - 1) / kBM);
-    w4a8_tc_kernel<BN, FP16S><<<grid, kW4Threads, smem, st>>>(ta, tw, Y, scale, sx, xs, M, N, K,
-                                                              block, epi, rt().d_err);
+    if (smem > 200 * 1024) return fail(SN_E_INVAL, "w4a8_tc: BN=%d needs too much shared memory", BN);
+    const int ctas = g.tile0[g.np] < rt().num_sms ? g.tile0[g.np] : rt().num_sms;  // persistent
+    w4a8_tc_kernel<BN, FP16S><<<ctas, kW4Threads, smem, st>>>(g, M, K, block, rt().d_err);
     return cuda_check(cudaGetLastError(), "w4a8_tc launch");
 }
 
@@ -335,13 +417,15 @@ bool w4a8_tc_ok(int M, int K, int N, int block, const void* Wq) {
            (uintptr_t)Wq % 16 == 0 && !getenv("SN_DISABLE_TC");
 }
 
-bool w4a8_tc_ready(int M, int K, int block) {
-    return w4_work().cap >= w4_work_bytes(M, K, block);
+bool w4a8_tc_ready(int M, int K, int block, int planes) {
+    if (block <= 0 || M <= 0 || planes <= 0) return false;
+    return w4_work().cap >= w4_work_bytes(M, K, block, planes);
 }
 
-int w4a8_tc_reserve(int M, int K, int block) {
+int w4a8_tc_reserve(int M, int K, int block, int planes) {
+    if (block <= 0 || M <= 0 || planes <= 0) return fail(SN_E_INVAL, "w4a8_tc: bad reserve shape");
     W4Work& w = w4_work();
-    const size_t need = w4_work_bytes(M, K, block);
+    const size_t need = w4_work_bytes(M, K, block, planes);
     if (w.cap >= need) return SN_OK;
     void* p = nullptr;
     if (cudaMalloc(&p, need) != cudaSuccess) {
@@ -353,32 +437,62 @@ int w4a8_tc_reserve(int M, int K, int block) {
     return SN_OK;
 }
 
-int launch_w4a8_tc(float* Y, const float* X, const uint8_t* Wq, const void* scale, int M, int K,
-                   int N, int block, bool fp16, int epi, cudaStream_t st) {
+int launch_w4a8_tc_group(const W4Problem* pr, int np, int M, int K, int block, bool fp16,
+                         cudaStream_t st) {
+    if (np < 1 || np > kW4MaxGroup) return fail(SN_E_INVAL, "w4a8_tc: %d problems in a group", np);
+    // distinct inputs, each quantised once
+    W4QGroup q;
+    q.n = 0;
+    int plane[kW4MaxGroup];
+    for (int i = 0; i < np; ++i) {
+        int u = 0;
+        while (u < q.n && q.X[u] != pr[i].X) ++u;
+        if (u == q.n) q.X[q.n++] = pr[i].X;
+        plane[i] = u;
+    }
     W4Work& w = w4_work();
-    if (w.cap < w4_work_bytes(M, K, block))
+    if (w.cap < w4_work_bytes(M, K, block, q.n))
         return fail(SN_E_INVAL, "w4a8_tc: activation workspace not reserved");
     const int nb = K / block;
     int8_t* codes = static_cast<int8_t*>(w.p);
-    float* sx = reinterpret_cast<float*>(static_cast<char*>(w.p) + (((size_t)M * K + 255) / 256) * 256);
-    int* xs = reinterpret_cast<int*>(sx + (size_t)M * nb);
+    float* sx = reinterpret_cast<float*>(static_cast<char*>(w.p) + w4_codes_bytes(q.n, M, K));
+    int* xs = reinterpret_cast<int*>(sx + (size_t)q.n * M * nb);
     {
-        const long long warps = (long long)M * nb;
-        quant_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(X, M, K, block, codes, sx, xs);
+        const long long warps = (long long)q.n * M * nb;
+        quant_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(q, M, K, block, codes, sx,
+                                                                       xs);
         SN_TRY(cuda_check(cudaGetLastError(), "w4a8_tc quant launch"));
     }
     const int mt = (M + kBM - 1) / kBM;
-    const int BN = (long long)((N + 63) / 64) * mt >= rt().num_sms ? 64 : 32;
-    CUtensorMap ta, tw;
-    SN_TRY(encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, codes, K, M, K, kSlab, kBM,
-                        CU_TENSOR_MAP_SWIZZLE_128B));
-    SN_TRY(encode_tiled(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, Wq, K / 2, N, K / 2, kSlab / 2, BN,
-                        CU_TENSOR_MAP_SWIZZLE_NONE));
+    long long tiles64 = 0;
+    for (int i = 0; i < np; ++i) tiles64 += (long long)((pr[i].N + 63) / 64) * mt;
+    const int BN = tiles64 >= rt().num_sms ? 64 : 32;
+    W4Group g;
+    g.np = np;
+    g.tile0[0] = 0;
+    for (int i = 0; i < np; ++i) {
+        const int u = plane[i];
+        SN_TRY(encode_tiled(&g.ta[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, codes + (size_t)u * M * K, K,
+                            M, K, kSlab, kBM, CU_TENSOR_MAP_SWIZZLE_128B));
+        SN_TRY(encode_tiled(&g.tw[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, pr[i].Wq, K / 2, pr[i].N,
+                            K / 2, kSlab / 2, BN, CU_TENSOR_MAP_SWIZZLE_NONE));
+        g.Y[i] = pr[i].Y;
+        g.scale[i] = pr[i].scale;
+        g.sx[i] = sx + (size_t)u * M * nb;
+        g.xs[i] = xs + (size_t)u * M * nb;
+        g.N[i] = pr[i].N;
+        g.epi[i] = pr[i].epi;
+        g.tile0[i + 1] = g.tile0[i] + ((pr[i].N + BN - 1) / BN) * mt;
+    }
     if (BN == 64)
-        return fp16 ? launch_bn<64, true>(ta, tw, Y, scale, sx, xs, M, N, K, block, epi, st)
-                    : launch_bn<64, false>(ta, tw, Y, scale, sx, xs, M, N, K, block, epi, st);
-    return fp16 ? launch_bn<32, true>(ta, tw, Y, scale, sx, xs, M, N, K, block, epi, st)
-                : launch_bn<32, false>(ta, tw, Y, scale, sx, xs, M, N, K, block, epi, st);
+        return fp16 ? launch_bn<64, true>(g, M, K, block, st) : launch_bn<64, false>(g, M, K, block, st);
+    return fp16 ? launch_bn<32, true>(g, M, K, block, st) : launch_bn<32, false>(g, M, K, block, st);
+}
+
+int launch_w4a8_tc(float* Y, const float* X, const uint8_t* Wq, const void* scale, int M, int K,
+                   int N, int block, bool fp16, int epi, cudaStream_t st) {
+    const W4Problem p{Y, X, Wq, scale, N, epi};
+    return launch_w4a8_tc_group(&p, 1, M, K, block, fp16, st);
 }
 
 }  // namespace sn

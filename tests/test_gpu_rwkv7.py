@@ -128,8 +128,11 @@ def test_stable_abi_equals_internal_bitwise(tiny):
 
 
 @pytest.mark.parametrize("kind", ["fp32", "q4", "q4g"])
-@pytest.mark.parametrize("B", [1, 3, 11])
+@pytest.mark.parametrize("B", [1, 3, 11, 20])
 def test_batched_vs_oracle(tiny, kind, B):
+    """B >= 16 with INT4 weights runs the tensor-core W4A8 contractions: the
+    grouped launch of a layer's first-stage projections where every matrix
+    qualifies (layer 0 here) and one launch per matrix otherwise."""
     from sunnynet_b200.rwkv7 import Rwkv7Batch
     g, shape, paths = tiny
     gm, om = Rwkv7Batch(paths[kind], B), oracle.Rwkv(paths[kind], B)

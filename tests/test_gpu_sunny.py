@@ -378,3 +378,35 @@ def test_fused_argmax_matches_logits_in_place(B):
             b.step_argmax(cur, out=cur)
             torch.cuda.synchronize()
             assert np.array_equal(cur.cpu().numpy(), lg.argmax(1).astype(np.int32))
+
+
+# ------------------------------- batched tensor-core step: planes + side stream
+@pytest.mark.parametrize("B", [16, 40, 130])
+@pytest.mark.parametrize("quant", [False, True])
+def test_tc_step_planes_equal_split_step(B, quant):
+    """The tensor-core step whose producers write the bf16 input planes (and
+    whose feedback contractions run on a side stream) against the same
+    contractions fed by a split launch each (SN_TC_SPLIT_STEP, read at load):
+    the planes hold the same values, so logits and states are bit-identical."""
+    import os
+    from sunnynet_b200 import formats
+    from sunnynet_b200.model import SunnyBatch
+    shape = formats.SunnyShape(2000, 128, 224, 80, 4, 3)
+    rng = np.random.default_rng(B)
+    toks = [rng.integers(0, shape.vocab, B).astype(np.int32) for _ in range(4)]
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape, quant=quant, seed=5, fast=True)
+        a = SunnyBatch(p, B)
+        os.environ["SN_TC_SPLIT_STEP"] = "1"
+        try:
+            b = SunnyBatch(p, B)
+        finally:
+            os.environ.pop("SN_TC_SPLIT_STEP", None)
+        om = oracle.Sunny(p, B)
+        for t in toks:
+            la, lb = a.step(t), b.step(t)
+            assert np.array_equal(la, lb)
+            check_logits(la, om.step(t))
+        sa, ha = a.get_state()
+        sb, hb = b.get_state()
+        assert np.array_equal(sa, sb) and np.array_equal(ha, hb)
