@@ -80,6 +80,71 @@ __global__ void split_act_kernel(GemmArgs a, __nv_bfloat16* __restrict__ hi,
     }
 }
 
+// 32 rows [mr0, mr0 + 32) of output column n from a staged 32x32 block
+// (row r at stg[r * 33 + lane]) with the element-wise epilogue EPI (the
+// kinds that read nothing but the accumulator), same arithmetic as
+// gemm_epilogue; optionally also the bf16 planes of the result.
+template <int EPI>
+__device__ __forceinline__ void tc_rows(const GemmArgs& a, int mr0, int n, bool nok, float ws,
+                                        const float* stg, int lane) {
+    if (!nok) return;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+        const int mm = mr0 + r;
+        if (mm >= a.M) continue;
+        float acc = stg[r * 33 + lane];
+        if (a.wscale) acc = acc * ws;
+        float y;
+        if (EPI == kEpiWedge) y = acc * (1.0f + 0.5f * a.p / (1.0f + fabsf(acc)));
+        else if (EPI == kEpiRelu2) {
+            const float t = acc > 0.0f ? acc : 0.0f;
+            y = t * t;
+        } else if (EPI == kEpiTanh) y = tanhf(acc);
+        else if (EPI == kEpiSigmoid) y = 1.0f / (1.0f + expf(-acc));
+        else y = acc;
+        const long long o = (long long)mm * a.ldc + n;
+        a.C[o] = y;
+        if (a.Ch) store_split((__nv_bfloat16*)a.Ch, (__nv_bfloat16*)a.Cl, o, y);
+    }
+}
+
+// gemm_epilogue with the kind fixed at compile time (same arithmetic).
+template <int EPI>
+__device__ __forceinline__ float epi_elem(const GemmArgs& a, int m, int n, float acc) {
+    if (a.wscale) acc = acc * a.wscale[n];
+    if (EPI == kEpiWedge) return acc * (1.0f + 0.5f * a.p / (1.0f + fabsf(acc)));
+    if (EPI == kEpiResid)
+        return acc + (a.p * a.S[m * a.lds + n] + a.F[m * a.ldf + n] + a.X[m * a.ldx + n]);
+    if (EPI == kEpiAdd) return a.C[m * a.ldc + n] + acc;
+    if (EPI == kEpiRelu2) {
+        const float t = acc > 0.0f ? acc : 0.0f;
+        return t * t;
+    }
+    if (EPI == kEpiTanh) return tanhf(acc);
+    if (EPI == kEpiSigmoid) return 1.0f / (1.0f + expf(-acc));
+    return acc;
+}
+
+// Split K: rows [r0, r0 + rows) of the tile, each element the sum of the
+// cluster's partials (rank 0 first, then 1, ...), then the epilogue.
+template <int EPI, int BN>
+__device__ __forceinline__ void tc_reduce(const GemmArgs& a, const float* part, int ks, int r0,
+                                          int rows, int m0, int n0) {
+    for (int i = threadIdx.x; i < rows * BN; i += kThreads) {
+        const int r = r0 + i / BN, j = i % BN;
+        const int mm = m0 + r, n = n0 + j;
+        const float* src = part + r * (BN + 1) + j;
+        float acc = ld_dsmem_f32(src, 0);
+        for (int p = 1; p < ks; ++p) acc += ld_dsmem_f32(src, (uint32_t)p);
+        if (mm < a.M && n < a.N) {
+            const long long o = (long long)mm * a.ldc + n;
+            const float y = epi_elem<EPI>(a, mm, n, acc);
+            a.C[o] = y;
+            if (a.Ch) store_split((__nv_bfloat16*)a.Ch, (__nv_bfloat16*)a.Cl, o, y);
+        }
+    }
+}
+
 // LOADS: the epilogue reads more than the accumulator (residual / accumulate
 // kinds); those operands are then all loaded before any result is stored.
 template <int BN, bool I8, bool LOADS>
@@ -99,8 +164,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* give_up = reinterpret_cast<volatile int*>(acc_full + 2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    const int nk = (a.K + BK - 1) / BK;
+    // split K: a cluster of ks CTAs along x shares one output tile, CTA kz of
+    // it takes K slabs [k0, k0 + nk) (ks = 1 without a cluster launch)
+    const int ks = (int)cluster_size(), kz = (int)cluster_rank();
+    const int m0 = blockIdx.y * BM, n0 = (blockIdx.x / ks) * BN;
+    const int nkt = (a.K + BK - 1) / BK;
+    const int k0 = kz * nkt / ks, nk = (kz + 1) * nkt / ks - k0;
     pdl_trigger();  // the next kernel may start its own prologue
     auto stage_ptr = [&](int s, int part) -> uint8_t* {  // 0 Ah, 1 Al, 2 Wh, 3 Wl
         return sb + s * C::STAGE +
@@ -137,8 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int pre = nk < S ? nk : S;
             for (int kt = 0; kt < pre; ++kt) {
                 mbar_expect_tx(&full[kt], bytes);
-                tma_load_2d(stage_ptr(kt, 2), &twh, kt * BK, n0, &full[kt]);
-                if (!I8) tma_load_2d(stage_ptr(kt, 3), &twl, kt * BK, n0, &full[kt]);
+                tma_load_2d(stage_ptr(kt, 2), &twh, (k0 + kt) * BK, n0, &full[kt]);
+                if (!I8) tma_load_2d(stage_ptr(kt, 3), &twl, (k0 + kt) * BK, n0, &full[kt]);
             }
             pdl_wait();
             int issued = 0;
@@ -151,11 +220,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     mbar_expect_tx(&full[s], bytes);
-                    tma_load_2d(stage_ptr(s, 2), &twh, kt * BK, n0, &full[s]);
-                    if (!I8) tma_load_2d(stage_ptr(s, 3), &twl, kt * BK, n0, &full[s]);
+                    tma_load_2d(stage_ptr(s, 2), &twh, (k0 + kt) * BK, n0, &full[s]);
+                    if (!I8) tma_load_2d(stage_ptr(s, 3), &twl, (k0 + kt) * BK, n0, &full[s]);
                 }
-                tma_load_2d(stage_ptr(s, 0), &tah, kt * BK, m0, &full[s]);
-                tma_load_2d(stage_ptr(s, 1), &tal, kt * BK, m0, &full[s]);
+                tma_load_2d(stage_ptr(s, 0), &tah, (k0 + kt) * BK, m0, &full[s]);
+                tma_load_2d(stage_ptr(s, 1), &tal, (k0 + kt) * BK, m0, &full[s]);
                 issued = kt + 1;
             }
             // never leave with a tile load in flight: wait for the last use of each stage
@@ -194,7 +263,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         pdl_wait();  // the epilogue reads (and overwrites) the previous kernels' outputs
         const bool ok = mbar_wait(acc_full, 0, err);
         tc_fence_after();
-        if (ok && !*give_up) {
+        if (ks > 1) {
+            // split K: this CTA's partial rows into its shared memory (the
+            // drained ring), [128][BN+1]; reduced across the cluster below
+            if (ok && !*give_up) {
+                float* part = reinterpret_cast<float*>(sb) + (q * 32 + lane) * (BN + 1);
+#pragma unroll 1
+                for (int j0 = 0; j0 < BN; j0 += 32) {
+                    float v[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)j0, v);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) part[j0 + j] = v[j];
+                }
+            }
+        } else if (ok && !*give_up) {
             // 32x32 blocks go through shared memory (the drained ring) so that a
             // warp touches one 128-byte row segment per global access
             float* stg = reinterpret_cast<float*>(sb) + (warp - 2) * (32 * 33);
@@ -208,16 +290,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int n = n0 + j0 + lane;
                 const bool nok = n < a.N;
                 if (!LOADS) {
-#pragma unroll 4
-                    for (int r = 0; r < 32; ++r) {
-                        const int mm = m0 + q * 32 + r;
-                        if (mm < a.M && nok) {
-                            const long long o = (long long)mm * a.ldc + n;
-                            const float y = gemm_epilogue(a, mm, n, stg[r * 33 + lane]);
-                            a.C[o] = y;
-                            if (a.Ch)
-                                store_split((__nv_bfloat16*)a.Ch, (__nv_bfloat16*)a.Cl, o, y);
-                        }
+                    // the epilogue kind is chosen once per block, not per element
+                    const float ws = a.wscale && nok ? a.wscale[n] : 1.0f;
+                    const int mr0 = m0 + q * 32;
+                    switch (a.epi) {
+                        case kEpiWedge: tc_rows<kEpiWedge>(a, mr0, n, nok, ws, stg, lane); break;
+                        case kEpiRelu2: tc_rows<kEpiRelu2>(a, mr0, n, nok, ws, stg, lane); break;
+                        case kEpiTanh: tc_rows<kEpiTanh>(a, mr0, n, nok, ws, stg, lane); break;
+                        case kEpiSigmoid: tc_rows<kEpiSigmoid>(a, mr0, n, nok, ws, stg, lane); break;
+                        default: tc_rows<kEpiNone>(a, mr0, n, nok, ws, stg, lane);
                     }
                 } else {
                     // the epilogue's other operands for all 32 rows are loaded
@@ -237,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                     const float ws = a.wscale && nok ? a.wscale[n] : 1.0f;
-#pragma unroll 4
+#pragma unroll  // pre[] stays in registers
                     for (int r = 0; r < 32; ++r) {
                         const long long mm = m0 + q * 32 + r;
                         if (mm < a.M && nok) {
@@ -262,6 +343,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                      "r"((uint32_t)BN)
                      : "memory");
+    }
+    if (ks > 1) {
+        // every CTA of the cluster reaches both barriers (all waits above are
+        // bounded); CTA kz finishes rows [kz*128/ks, (kz+1)*128/ks) of the
+        // tile, summing the partials in rank order, so results do not depend
+        // on timing
+        cluster_sync();
+        const float* part = reinterpret_cast<const float*>(sb);
+        const int rows = BM / ks, r0 = kz * rows;
+        switch (a.epi) {
+            case kEpiWedge: tc_reduce<kEpiWedge, BN>(a, part, ks, r0, rows, m0, n0); break;
+            case kEpiResid: tc_reduce<kEpiResid, BN>(a, part, ks, r0, rows, m0, n0); break;
+            case kEpiAdd: tc_reduce<kEpiAdd, BN>(a, part, ks, r0, rows, m0, n0); break;
+            case kEpiRelu2: tc_reduce<kEpiRelu2, BN>(a, part, ks, r0, rows, m0, n0); break;
+            case kEpiTanh: tc_reduce<kEpiTanh, BN>(a, part, ks, r0, rows, m0, n0); break;
+            case kEpiSigmoid: tc_reduce<kEpiSigmoid, BN>(a, part, ks, r0, rows, m0, n0); break;
+            default: tc_reduce<kEpiNone, BN>(a, part, ks, r0, rows, m0, n0);
+        }
+        cluster_sync();  // no CTA leaves while its partials may still be read
     }
 }
 
@@ -322,7 +422,7 @@ std::map<int, ActPlanes>& act_cache() {
 
 template <int BN, bool I8, bool LOADS>
 int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
-              const CUtensorMap& tal, cudaStream_t st, bool pdl) {
+              const CUtensorMap& tal, cudaStream_t st, bool pdl, int ks) {
     using C = TcCfg<BN>;
     static bool attr = false;
     auto k = tc_gemm_kernel<BN, I8, LOADS>;
@@ -333,13 +433,30 @@ int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
         attr = true;
     }
     const int bi = BN == 32 ? 0 : (BN == 64 ? 1 : 2);
-    dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
-    if (pdl)
-        return cuda_check(launch_pdl(k, grid, dim3(kThreads), C::SMEM, st, tah, tal, tw.tm_hi[bi],
-                                     tw.tm_lo[bi], a, rt().d_err),
-                          "tc_gemm launch");
-    k<<<grid, kThreads, C::SMEM, st>>>(tah, tal, tw.tm_hi[bi], tw.tm_lo[bi], a, rt().d_err);
-    return cuda_check(cudaGetLastError(), "tc_gemm launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(((a.N + BN - 1) / BN) * ks), (unsigned)((a.M + BM - 1) / BM));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute la[2];
+    int na = 0;
+    if (pdl) {
+        la[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        la[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (ks > 1) {  // split K over a cluster of ks CTAs along x
+        la[na].id = cudaLaunchAttributeClusterDimension;
+        la[na].val.clusterDim.x = (unsigned)ks;
+        la[na].val.clusterDim.y = 1;
+        la[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = la;
+    cfg.numAttrs = na;
+    return cuda_check(cudaLaunchKernelEx(&cfg, k, tah, tal, tw.tm_hi[bi], tw.tm_lo[bi], a,
+                                         rt().d_err),
+                      "tc_gemm launch");
 }
 
 }  // namespace
@@ -429,11 +546,18 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
     int bn = 32;
     if (mt * ((a.N + 127) / 128) >= sms * 3 / 4) bn = 128;
     else if (mt * ((a.N + 63) / 64) >= sms * 3 / 4) bn = 64;
+    // split K over a cluster while that still fits in one wave and leaves
+    // each CTA at least two slabs (few-tile contractions of batched decode)
+    const long long tiles = mt * ((a.N + bn - 1) / bn);
+    const int nkt = (a.K + BK - 1) / BK;
+    int ks = 1;
+    if (!getenv("SN_TC_NO_SPLITK"))
+        while (ks < 8 && tiles * ks * 2 <= sms && nkt >= ks * 4) ks *= 2;
     const bool ld = a.epi == kEpiResid || a.epi == kEpiAdd;
-#define SN_TC_BN(I8, LD)                                                          \
-    return bn == 128 ? launch_bn<128, I8, LD>(a, tw, tah, tal, st, pdl)            \
-                     : (bn == 64 ? launch_bn<64, I8, LD>(a, tw, tah, tal, st, pdl) \
-                                 : launch_bn<32, I8, LD>(a, tw, tah, tal, st, pdl))
+#define SN_TC_BN(I8, LD)                                                              \
+    return bn == 128 ? launch_bn<128, I8, LD>(a, tw, tah, tal, st, pdl, ks)            \
+                     : (bn == 64 ? launch_bn<64, I8, LD>(a, tw, tah, tal, st, pdl, ks) \
+                                 : launch_bn<32, I8, LD>(a, tw, tah, tal, st, pdl, ks))
     if (tw.int8) {
         if (ld) SN_TC_BN(true, true);
         SN_TC_BN(true, false);

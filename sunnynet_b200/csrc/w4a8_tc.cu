@@ -34,8 +34,10 @@
 //                into one of two accumulator slots, commits the slot
 //     warps 2-5  per block: tcgen05.ld the slot (warp w reads TMEM lanes of
 //                quarter w%4 = its 32 sequences), release it, accumulate in
-//                block order in registers; per tile the epilogue, rows staged
-//                in shared memory so each store is one coalesced row segment
+//                block order in registers (the block's scales brought in by
+//                cp.async a few blocks ahead); per tile the epilogue, rows
+//                staged in shared memory so each store is one coalesced row
+//                segment
 // Every wait is bounded; a role that gives up records the error and leaves
 // its loop, the MMA issuer waits for its own MMAs, the TMA issuer for its own
 // loads, and the CTA frees its TMEM.
@@ -64,6 +66,7 @@ struct W4Cfg {
 };
 
 constexpr int kW4MaxGroup = 8;
+constexpr int kScD = 4;  // blocks of scales in flight ahead of the epilogue
 
 // One launch's problems: tensor maps of each problem's activation codes and
 // packed weights, outputs, scales, activation block scales and code sums.
@@ -91,16 +94,41 @@ __device__ __forceinline__ float load_scale_w(const void* s, size_t i, bool fp16
                 : reinterpret_cast<const float*>(s)[i];
 }
 
-__device__ __forceinline__ void w4_apply(float* y, float v, int epi) {
-    switch (epi) {
-        case kW4Add: *y = *y + v; break;
-        case kW4Relu2: {
-            const float t = v > 0.0f ? v : 0.0f;
-            *y = t * t;
-        } break;
-        case kW4Tanh: *y = tanhf(v); break;
-        case kW4Sigmoid: *y = 1.0f / (1.0f + expf(-v)); break;
-        default: *y = v;
+// Rows [mrow0, mrow0 + 32) x columns [n0, n0 + BN) of one tile from the
+// warp's staging area to Y with epilogue EPI; lane j stores columns j, j+32,
+// so each row is one coalesced segment. kW4Add loads all its old values
+// before any store.
+template <int BN, int EPI>
+__device__ __forceinline__ void w4_store_rows(float* __restrict__ Y, int N, int M, int mrow0,
+                                              int n0, const float* stg, int lane) {
+#pragma unroll
+    for (int jj = 0; jj < BN / 32; ++jj) {
+        const int j = jj * 32 + lane, n = n0 + j;
+        if (n >= N) continue;
+        float old[32];
+        if (EPI == kW4Add) {
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr)
+                old[rr] = mrow0 + rr < M ? Y[(size_t)(mrow0 + rr) * N + n] : 0.0f;
+        }
+#pragma unroll
+        for (int rr = 0; rr < 32; ++rr) {
+            if (mrow0 + rr >= M) continue;
+            const float v = stg[rr * (BN + 1) + j];
+            float* y = Y + (size_t)(mrow0 + rr) * N + n;
+            if (EPI == kW4Add) {
+                *y = old[rr] + v;
+            } else if (EPI == kW4Relu2) {
+                const float t = v > 0.0f ? v : 0.0f;
+                *y = t * t;
+            } else if (EPI == kW4Tanh) {
+                *y = tanhf(v);
+            } else if (EPI == kW4Sigmoid) {
+                *y = 1.0f / (1.0f + expf(-v));
+            } else {
+                *y = v;
+            }
+        }
     }
 }
 
@@ -137,9 +165,23 @@ __global__ void quant_rows_kernel(const __grid_constant__ W4QGroup q, int M, int
     }
 }
 
+// Per-problem tables of a launch, copied from the parameters into shared
+// memory once (indexing the parameter arrays by a run-time problem number
+// costs a memory round trip each time).
+struct W4Tables {
+    int tile0[kW4MaxGroup + 1];
+    int N[kW4MaxGroup];
+    int epi[kW4MaxGroup];
+    float* Y[kW4MaxGroup];
+    const void* scale[kW4MaxGroup];
+    const float* sx[kW4MaxGroup];
+    const int* xs[kW4MaxGroup];
+    int np;
+};
+
 // Problem, first sequence and first output row of tile t of a group.
 template <int BN>
-__device__ __forceinline__ void w4_tile(const W4Group& g, int t, int& pi, int& m0, int& n0) {
+__device__ __forceinline__ void w4_tile(const W4Tables& g, int t, int& pi, int& m0, int& n0) {
     pi = 0;
     while (pi + 1 < g.np && t >= g.tile0[pi + 1]) ++pi;
     const int ntn = (g.N[pi] + BN - 1) / BN, local = t - g.tile0[pi];
@@ -162,7 +204,9 @@ __global__ void __launch_bounds__(kW4Threads, 1)
     const int nb = K / block, nslab = K / kSlab, bps = kSlab / block, mpb = block / 32;
     const int ntiles = g.tile0[g.np];
     float* stg_all = reinterpret_cast<float*>(ring + S * C::STAGE);  // [4][32][BN+1]
-    uint64_t* full = reinterpret_cast<uint64_t*>(stg_all + 4 * 32 * (BN + 1));
+    // per epilogue warp: kScD slots of [32 sx][32 xsum][BN weight-scale words]
+    uint32_t* scr_all = reinterpret_cast<uint32_t*>(stg_all + 4 * 32 * (BN + 1));
+    uint64_t* full = reinterpret_cast<uint64_t*>(scr_all + 4 * kScD * (64 + BN));
     uint64_t* wready = full + S;
     uint64_t* empty = wready + S;
     uint64_t* accf = empty + S;  // [2]
@@ -175,6 +219,23 @@ __global__ void __launch_bounds__(kW4Threads, 1)
     auto sP = [&](int s) { return ring + s * C::STAGE + C::A_BYTES + C::U_BYTES; };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ W4Tables gt;
+#pragma unroll
+    for (int i = 0; i < kW4MaxGroup; ++i) {  // constant indices: parameter-bank loads
+        if (tid == i) {
+            gt.tile0[i] = g.tile0[i];
+            gt.N[i] = g.N[i];
+            gt.epi[i] = g.epi[i];
+            gt.Y[i] = g.Y[i];
+            gt.scale[i] = g.scale[i];
+            gt.sx[i] = g.sx[i];
+            gt.xs[i] = g.xs[i];
+        }
+    }
+    if (tid == kW4MaxGroup) {
+        gt.tile0[kW4MaxGroup] = g.tile0[kW4MaxGroup];
+        gt.np = g.np;
+    }
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
@@ -201,7 +262,7 @@ __global__ void __launch_bounds__(kW4Threads, 1)
             bool run = true;
             for (int t = blockIdx.x; t < ntiles && run; t += gridDim.x) {
                 int pi, m0, n0;
-                w4_tile<BN>(g, t, pi, m0, n0);
+                w4_tile<BN>(gt, t, pi, m0, n0);
                 for (int s = 0; s < nslab; ++s, ++gs) {
                     const int st = gs % S;
                     if (*give_up || (gs >= S && !mbar_wait(&empty[st], ((gs / S) - 1) & 1, err))) {
@@ -286,40 +347,51 @@ __global__ void __launch_bounds__(kW4Threads, 1)
         }
     } else {  // ----------------------------------------------- epilogue, warps 2-5
         // warp w reads TMEM lanes of quarter w%4: sequences m0 + 32*(w%4) + lane.
-        // The weight scales of a block reach every lane by shuffle (lane j holds
-        // output row n0 + j's), the activation scale and code sum are the
-        // lane's own; the next block's are loaded while this one is applied.
-        const int q = warp & 3;
-        float* stg = stg_all + (warp - 2) * 32 * (BN + 1);
+        // The scales of block k (activation scale and code sum of the lane's
+        // row, weight scale of each output row of the tile) arrive by cp.async
+        // in a ring of kScD blocks, issued kScD blocks ahead of their use.
+        const int q = warp & 3, wi = warp - 2;
+        float* stg = stg_all + wi * 32 * (BN + 1);
+        uint32_t* scr = scr_all + wi * kScD * (64 + BN);
         int b = 0;  // block counter across tiles (accumulator slot b & 1)
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
             int pi, m0, n0;
-            w4_tile<BN>(g, t, pi, m0, n0);
-            const int N = g.N[pi], m = m0 + q * 32 + lane;
+            w4_tile<BN>(gt, t, pi, m0, n0);
+            const int N = gt.N[pi], mrow0 = m0 + q * 32, m = mrow0 + lane;
             const bool mok = m < M;
-            const float* sxr = g.sx[pi] + (size_t)(mok ? m : 0) * nb;
-            const int* xsr = g.xs[pi] + (size_t)(mok ? m : 0) * nb;
-            const void* scale = g.scale[pi];
-            const int na = n0 + lane, nc = n0 + 32 + lane;
+            const float* sxr = gt.sx[pi] + (size_t)(mok ? m : 0) * nb;
+            const int* xsr = gt.xs[pi] + (size_t)(mok ? m : 0) * nb;
+            const char* scale = static_cast<const char*>(gt.scale[pi]);
+            auto issue = [&](int k) {  // block k's scales into slot k % kScD
+                uint32_t* sl = scr + (k % kScD) * (64 + BN);
+                cp_async4(sl + lane, sxr + k, mok ? 4u : 0u);
+                cp_async4(sl + 32 + lane, xsr + k, mok ? 4u : 0u);
+#pragma unroll
+                for (int jj = 0; jj < BN / 32; ++jj) {
+                    const int n = n0 + jj * 32 + lane;
+                    const size_t e = (size_t)(n < N ? n : 0) * nb + k;
+                    // fp16: the aligned 4-byte word holding the element
+                    const char* src = FP16S ? reinterpret_cast<const char*>(
+                                                  reinterpret_cast<uintptr_t>(scale + 2 * e) & ~(uintptr_t)3)
+                                            : scale + 4 * e;
+                    cp_async4(sl + 64 + jj * 32 + lane, src, n < N ? 4u : 0u);
+                }
+            };
+#pragma unroll
+            for (int p = 0; p < kScD; ++p) {
+                if (p < nb) issue(p);
+                cp_async_commit();
+            }
             float acc[BN];
 #pragma unroll
             for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
-            float xs_c = mok ? sxr[0] : 0.0f;
-            int x8_c = mok ? 8 * xsr[0] : 0;
-            float wa_c = na < N ? load_scale_w(scale, (size_t)na * nb, FP16S) : 0.0f;
-            float wc_c = BN > 32 && nc < N ? load_scale_w(scale, (size_t)nc * nb, FP16S) : 0.0f;
             bool ok = true;
             for (int k = 0; k < nb; ++k, ++b) {
-                float xs_n = 0.0f, wa_n = 0.0f, wc_n = 0.0f;
-                int x8_n = 0;
-                if (k + 1 < nb) {
-                    if (mok) {
-                        xs_n = sxr[k + 1];
-                        x8_n = 8 * xsr[k + 1];
-                    }
-                    if (na < N) wa_n = load_scale_w(scale, (size_t)na * nb + k + 1, FP16S);
-                    if (BN > 32 && nc < N) wc_n = load_scale_w(scale, (size_t)nc * nb + k + 1, FP16S);
-                }
+                cp_async_wait_group<kScD - 1>();  // block k's group has landed
+                __syncwarp();
+                const uint32_t* sl = scr + (k % kScD) * (64 + BN);
+                const float xs = __uint_as_float(sl[lane]);
+                const int x8 = 8 * (int)sl[32 + lane];
                 const int slot = b & 1;
                 ok = !*give_up && mbar_wait(&accf[slot], (b >> 1) & 1, err);
                 ok = __all_sync(0xffffffffu, ok);  // one decision per warp
@@ -332,34 +404,41 @@ __global__ void __launch_bounds__(kW4Threads, 1)
                 for (int j0 = 0; j0 < BN; j0 += 32) {
                     uint32_t d[32];
                     tmem_ld32_u(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * BN + j0), d);
-                    const float wl = j0 == 0 ? wa_c : wc_c;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        const float w = __shfl_sync(0xffffffffu, wl, j);
-                        const float f = (float)((int)d[j] - x8_c);
-                        acc[j0 + j] = __fadd_rn(acc[j0 + j], __fmul_rn(__fmul_rn(w, xs_c), f));
+                        const uint32_t wd = sl[64 + j0 + j];  // same address in every lane
+                        float w;
+                        if (FP16S) {
+                            const uintptr_t ea = reinterpret_cast<uintptr_t>(
+                                scale + 2 * ((size_t)(n0 + j0 + j) * nb + k));
+                            w = __half2float(__ushort_as_half(
+                                (unsigned short)((ea & 2) ? (wd >> 16) : (wd & 0xFFFFu))));
+                        } else {
+                            w = __uint_as_float(wd);
+                        }
+                        const float f = (float)((int)d[j] - x8);
+                        acc[j0 + j] = __fadd_rn(acc[j0 + j], __fmul_rn(__fmul_rn(w, xs), f));
                     }
                 }
                 tc_fence_before();
                 mbar_arrive(&acce[slot]);
-                xs_c = xs_n;
-                x8_c = x8_n;
-                wa_c = wa_n;
-                wc_c = wc_n;
+                __syncwarp();  // every lane is done with the slot before it is refilled
+                if (k + kScD < nb) issue(k + kScD);
+                cp_async_commit();
             }
+            cp_async_wait_all();
             if (!ok) break;
             // rows through shared memory: one coalesced segment per stored row
 #pragma unroll
             for (int j = 0; j < BN; ++j) stg[lane * (BN + 1) + j] = acc[j];
             __syncwarp();
-            float* __restrict__ Y = g.Y[pi];
-            const int epi = g.epi[pi];
-            for (int rr = 0; rr < 32; ++rr) {
-                const int mm = m0 + q * 32 + rr;
-                if (mm >= M) break;
-#pragma unroll
-                for (int j = lane; j < BN; j += 32)
-                    if (n0 + j < N) w4_apply(Y + (size_t)mm * N + n0 + j, stg[rr * (BN + 1) + j], epi);
+            float* __restrict__ Y = gt.Y[pi];
+            switch (gt.epi[pi]) {
+                case kW4Add: w4_store_rows<BN, kW4Add>(Y, N, M, mrow0, n0, stg, lane); break;
+                case kW4Relu2: w4_store_rows<BN, kW4Relu2>(Y, N, M, mrow0, n0, stg, lane); break;
+                case kW4Tanh: w4_store_rows<BN, kW4Tanh>(Y, N, M, mrow0, n0, stg, lane); break;
+                case kW4Sigmoid: w4_store_rows<BN, kW4Sigmoid>(Y, N, M, mrow0, n0, stg, lane); break;
+                default: w4_store_rows<BN, kW4Store>(Y, N, M, mrow0, n0, stg, lane);
             }
             __syncwarp();
         }
@@ -395,7 +474,7 @@ template <int BN, bool FP16S>
 int launch_bn(const W4Group& g, int M, int K, int block, cudaStream_t st) {
     using C = W4Cfg<BN>;
     const size_t smem = 1024 + (size_t)kW4Stages * C::STAGE + 4ull * 4 * 32 * (BN + 1) +
-                        8ull * (3 * kW4Stages + 5) + 16;
+                        4ull * 4 * kScD * (64 + BN) + 8ull * (3 * kW4Stages + 5) + 16;
     static int attr = 0;
     if (!attr) {
         SN_TRY(cuda_check(cudaFuncSetAttribute(w4a8_tc_kernel<BN, FP16S>,

@@ -410,3 +410,35 @@ def test_tc_step_planes_equal_split_step(B, quant):
         sa, ha = a.get_state()
         sb, hb = b.get_state()
         assert np.array_equal(sa, sb) and np.array_equal(ha, hb)
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_split_k_cluster_matches_unsplit_and_oracle(quant):
+    """Few-tile contractions split K over a thread-block cluster (partials
+    summed across the cluster's shared memory in rank order). Against the
+    same model with the split off (SN_TC_NO_SPLITK, read when a step is
+    captured) and against the oracle: both within the fp32 tolerance, and the
+    split path is deterministic (two models, identical logits)."""
+    import os
+    from sunnynet_b200 import formats
+    from sunnynet_b200.model import SunnyBatch
+    shape = formats.SunnyShape(3000, 256, 448, 160, 4, 2)  # K up to 448: 7 slabs
+    B = 48
+    rng = np.random.default_rng(7 + quant)
+    toks = [rng.integers(0, shape.vocab, B).astype(np.int32) for _ in range(3)]
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape, quant=quant, seed=8, fast=True)
+        a, a2 = SunnyBatch(p, B), SunnyBatch(p, B)
+        os.environ["SN_TC_NO_SPLITK"] = "1"
+        try:
+            b = SunnyBatch(p, B)
+            lb = [b.step(t) for t in toks]
+        finally:
+            os.environ.pop("SN_TC_NO_SPLITK", None)
+        om = oracle.Sunny(p, B)
+        for t, l_b in zip(toks, lb):
+            la = a.step(t)
+            assert np.array_equal(la, a2.step(t))
+            ref = om.step(t)
+            check_logits(la, ref)
+            check_logits(l_b, ref)
