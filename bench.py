@@ -664,8 +664,14 @@ def rwkv_launches(S, B, block=128):
         first = [(D, D)] * 3 + [(D, Rw), (D, Ra), (D, Rg)] + ([(D, Rv)] if l > 0 else [])
         grouped = all(tc(K, N) for K, N in first)
         n += 1 + (2 if grouped else sum(mm(K, N) for K, N in first))  # prep + first stage
-        n += mm(Rw, D) + mm(Ra, D) + mm(Rg, D) + (mm(Rv, D) if l > 0 else 0)
-        n += 2 + mm(D, D) + 1 + mm(D, F) + mm(F, D)  # mix, heads, out, cmix prep, ffn
+        # LoRA second stages: ranks below a quantisation block stay fp32 and are
+        # folded into the mix kernel; g2 (and any quantised one) is a contraction
+        fp32 = [r % block != 0 for r in (Rw, Ra, Rv)]
+        if all(fp32):
+            n += mm(Rg, D) + 1  # g2, fused LoRA + mix
+        else:
+            n += mm(Rw, D) + mm(Ra, D) + mm(Rg, D) + (mm(Rv, D) if l > 0 else 0) + 1
+        n += 1 + mm(D, D) + 1 + mm(D, F) + mm(F, D)  # heads, out, cmix prep, ffn
     return n + 2 + 2  # final LN + head (fp32), argmax partials + final
 
 

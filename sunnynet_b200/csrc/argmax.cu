@@ -11,6 +11,7 @@
 #include <cmath>
 
 #include "kernels.cuh"
+#include "ptx.cuh"
 #include "runtime.cuh"
 
 namespace sn {
@@ -28,6 +29,7 @@ __global__ void __launch_bounds__(256)
     __shared__ float sv[8];
     __shared__ int si[8];
     const int c = blockIdx.x, row = blockIdx.y;
+    pdl_trigger();
     const long long lo = (long long)V * c / kArgChunks, hi = (long long)V * (c + 1) / kArgChunks;
     const float* r = lg + (size_t)row * V;
     float bv = -INFINITY;
@@ -49,6 +51,7 @@ __global__ void __launch_bounds__(256)
 
 __global__ void argmax_final_kernel(const float2* __restrict__ part, int32_t* __restrict__ out) {
     const int row = blockIdx.x, lane = threadIdx.x;
+    pdl_wait();  // the partials of argmax_part_kernel (programmatic launch)
     float bv = -INFINITY;
     int bi = 0x7fffffff;
     for (int c = lane; c < kArgChunks; c += 32) {
@@ -67,8 +70,9 @@ int launch_argmax(const float* lg, int B, int V, float2* part, int32_t* out, cud
     if (B > 65535) return fail(SN_E_INVAL, "argmax: %d rows exceed 65535", B);
     argmax_part_kernel<<<dim3(kArgChunks, B), 256, 0, st>>>(V, lg, part);
     SN_TRY(cuda_check(cudaGetLastError(), "argmax launch"));
-    argmax_final_kernel<<<B, 32, 0, st>>>(part, out);
-    return cuda_check(cudaGetLastError(), "argmax launch");
+    return cuda_check(launch_pdl(argmax_final_kernel, dim3(B), dim3(32), 0, st,
+                                 (const float2*)part, out),
+                      "argmax launch");
 }
 
 }  // namespace sn

@@ -142,6 +142,8 @@ __global__ void __launch_bounds__(256) gemm_tiled_kernel(GemmArgs a) {
     const int tid = threadIdx.x;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const int tx = tid % 16, ty = tid / 16;
+    pdl_trigger();
+    pdl_wait();  // no-op unless launched with programmatic serialization
     float acc[4][4] = {};
     // staging: each thread loads 4 A and 4 W elements per BK slab
     float ra[4], rw[4];
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(256) gemm_tiled_kernel(GemmArgs a) {
 }
 
 template <int WT>
-int launch_wt(const GemmArgs& a, cudaStream_t st) {
+int launch_wt(const GemmArgs& a, cudaStream_t st, bool pdl) {
     if (a.M <= kGemvRows) {
         const size_t smem = ((size_t)a.M * a.K + 2 * kGemvRows) * sizeof(float);
         if (smem > 200 * 1024) return fail(SN_E_INVAL, "gemm: K=%d too large for the row path", a.K);
@@ -218,20 +220,21 @@ int launch_wt(const GemmArgs& a, cudaStream_t st) {
     } else {
         if (a.ln_inline) return fail(SN_E_INVAL, "gemm: in-kernel LN statistics need M <= 8");
         dim3 grid((a.N + BN - 1) / BN, (a.M + BM - 1) / BM);
-        gemm_tiled_kernel<WT><<<grid, 256, 0, st>>>(a);
+        SN_TRY(cuda_check(launch_pdl_if(pdl, gemm_tiled_kernel<WT>, grid, dim3(256), 0, st, a),
+                          "gemm launch"));
     }
     return cuda_check(cudaGetLastError(), "gemm launch");
 }
 
 }  // namespace
 
-int launch_gemm(const GemmArgs& a, int wtype, cudaStream_t st, const TcWeights* tc) {
+int launch_gemm(const GemmArgs& a, int wtype, cudaStream_t st, const TcWeights* tc, bool pdl) {
     if (a.M <= 0 || a.N <= 0 || a.K <= 0) return SN_OK;
     if (tc && tc_usable(a, tc)) return launch_tc_gemm(a, *tc, st);
     switch (wtype) {
-        case kWI8: return launch_wt<kWI8>(a, st);
-        case kWF16: return launch_wt<kWF16>(a, st);
-        default: return launch_wt<kWF32>(a, st);
+        case kWI8: return launch_wt<kWI8>(a, st, pdl);
+        case kWF16: return launch_wt<kWF16>(a, st, pdl);
+        default: return launch_wt<kWF32>(a, st, pdl);
     }
 }
 

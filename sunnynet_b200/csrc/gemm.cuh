@@ -66,8 +66,11 @@ struct GemmArgs {
 struct TcWeights;
 
 // Runs on the tensor cores when `tc` is given and the shape suits them
-// (tc_gemm.cu), else on the SIMT kernels.
-int launch_gemm(const GemmArgs& a, int wtype, cudaStream_t st, const TcWeights* tc = nullptr);
+// (tc_gemm.cu), else on the SIMT kernels. pdl: the SIMT tiled kernel is
+// launched with programmatic serialization (the small-batch row kernel
+// always is).
+int launch_gemm(const GemmArgs& a, int wtype, cudaStream_t st, const TcWeights* tc = nullptr,
+                bool pdl = false);
 
 // A' element (row-LN prologue when mu is set)
 __device__ __forceinline__ float gemm_a_eff(const GemmArgs& a, int m, int k, float v) {

@@ -24,9 +24,11 @@ long long scan_chunk_records(int B, int T, int N, int L);
 int launch_scan_chunked(const float* a, const float* b, const float* s0, float* out,
                         float* send, int B, int T, int N, int gated, int L, float2* agg,
                         cudaStream_t st, bool prof_scopes = true);
-// Y (nseq,out) = W4A8(X (nseq,in)) with codes (out,in/2) and scales (out,in/block)
+// Y (nseq,out) = W4A8(X (nseq,in)) with codes (out,in/2) and scales (out,in/block).
+// pdl: launched with programmatic serialization (the kernels wait for the
+// previous one before reading their input; weights may be fetched earlier).
 int launch_w4a8(float* Y, const float* X, const uint8_t* Wq, const void* scale, int nseq, int in,
-                int out, int block, bool fp16, cudaStream_t st, int epi);
+                int out, int block, bool fp16, cudaStream_t st, int epi, bool pdl = false);
 // The same contraction on the tensor cores (w4a8_tc.cu) for M >= 16 sequences,
 // K % 128 == 0, block in {32, 64, 128}: bit-identical results. Its activation
 // workspace is reserved outside graph capture (w4a8_tc_reserve) before use.
@@ -35,7 +37,7 @@ bool w4a8_tc_ok(int M, int K, int N, int block, const void* Wq);
 bool w4a8_tc_ready(int M, int K, int block, int planes = 1);
 int w4a8_tc_reserve(int M, int K, int block, int planes = 1);
 int launch_w4a8_tc(float* Y, const float* X, const uint8_t* Wq, const void* scale, int M, int K,
-                   int N, int block, bool fp16, int epi, cudaStream_t st);
+                   int N, int block, bool fp16, int epi, cudaStream_t st, bool pdl = false);
 // Up to 8 such contractions sharing M, K, block and scale type in one launch
 // (plus one quantisation launch over their distinct inputs).
 struct W4Problem {
@@ -47,7 +49,7 @@ struct W4Problem {
     int epi;
 };
 int launch_w4a8_tc_group(const W4Problem* pr, int np, int M, int K, int block, bool fp16,
-                         cudaStream_t st);
+                         cudaStream_t st, bool pdl = false);
 int launch_gemv_f32(float* y, const float* x, const float* W, int in, int out, cudaStream_t st);
 // out[b] = argmax of logits row b (lowest id on ties, NaN never chosen);
 // part holds B * kArgChunks float2 of scratch (argmax.cu).

@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include "kernels.cuh"
+#include "ptx.cuh"
 #include "quant.h"
 #include "runtime.cuh"
 
@@ -153,12 +154,18 @@ __global__ void __launch_bounds__(256)
     int8_t* xq = reinterpret_cast<int8_t*>(smem);
     float* xs = reinterpret_cast<float*>(smem + (size_t)kMaxSeqTile * in);
     int* xsum = reinterpret_cast<int*>(xs + kMaxSeqTile * nb);
-    quant_act_smem(X + (size_t)seq0 * in, ns, in, block, nb, xq, xs, xsum);
-    __syncthreads();
-
     const int lane = threadIdx.x & 31;
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int nw = gridDim.x * (blockDim.x >> 5);
+    pdl_trigger();
+    if (gw < out) {  // the warp's first weight row toward L2 while the previous kernel ends
+        const char* wr0 = reinterpret_cast<const char*>(Wq) + (size_t)gw * (in / 2);
+        for (int off = lane * 128; off < in / 2; off += 32 * 128) prefetch_l2(wr0 + off);
+    }
+    pdl_wait();  // no-op unless launched with programmatic serialization
+    quant_act_smem(X + (size_t)seq0 * in, ns, in, block, nb, xq, xs, xsum);
+    __syncthreads();
+
     for (int row = gw; row < out; row += nw) {
         const uint8_t* wr = Wq + (size_t)row * (in / 2);
         float acc[kMaxSeqTile];
@@ -213,6 +220,8 @@ __global__ void w4a8_generic_kernel(float* __restrict__ Y, const float* __restri
     int8_t* xq = reinterpret_cast<int8_t*>(smem);
     float* xs = reinterpret_cast<float*>(smem + (size_t)kMaxSeqTile * in);
     int* xsum = reinterpret_cast<int*>(xs + kMaxSeqTile * nb);
+    pdl_trigger();
+    pdl_wait();
     quant_act_smem(X + (size_t)seq0 * in, ns, in, block, nb, xq, xs, xsum);
     __syncthreads();
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < out * ns;
@@ -266,9 +275,9 @@ __global__ void gemv_f32_kernel(float* __restrict__ y, const float* __restrict__
 // Device-pointer W4A8 GEMV/GEMM (Y (nseq,out), X (nseq,in)), used by the ABI
 // and by the RWKV-7 model.
 int launch_w4a8(float* Y, const float* X, const uint8_t* Wq, const void* scale, int nseq, int in,
-                int out, int block, bool fp16, cudaStream_t st, int epi) {
+                int out, int block, bool fp16, cudaStream_t st, int epi, bool pdl) {
     if (w4a8_tc_ok(nseq, in, out, block, Wq) && w4a8_tc_ready(nseq, in, block))
-        return launch_w4a8_tc(Y, X, Wq, scale, nseq, in, out, block, fp16, epi, st);
+        return launch_w4a8_tc(Y, X, Wq, scale, nseq, in, out, block, fp16, epi, st, pdl);
     const int nb = in / block;
     const size_t smem = (size_t)kMaxSeqTile * in + (size_t)kMaxSeqTile * nb * 8 + 16;
     if (smem > 200 * 1024) return fail(SN_E_INVAL, "gemv_i4: in=%d too large", in);
@@ -286,15 +295,18 @@ int launch_w4a8(float* Y, const float* X, const uint8_t* Wq, const void* scale, 
         if (smem > 48 * 1024)
             SN_TRY(cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    (int)smem), "w4a8 smem"));
-        k<<<grid, 256, smem, st>>>(Y, X, Wq, scale, nseq, in, out, block, epi);
+        return cuda_check(launch_pdl_if(pdl, k, grid, dim3(256), smem, st, Y, X, Wq, scale, nseq,
+                                        in, out, block, epi),
+                          "w4a8 launch");
     } else {
         auto k = fp16 ? w4a8_generic_kernel<true> : w4a8_generic_kernel<false>;
         if (smem > 48 * 1024)
             SN_TRY(cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    (int)smem), "w4a8 smem"));
-        k<<<grid, 256, smem, st>>>(Y, X, Wq, scale, nseq, in, out, block, epi);
+        return cuda_check(launch_pdl_if(pdl, k, grid, dim3(256), smem, st, Y, X, Wq, scale, nseq,
+                                        in, out, block, epi),
+                          "w4a8 launch");
     }
-    return cuda_check(cudaGetLastError(), "w4a8 launch");
 }
 
 int launch_gemv_f32(float* y, const float* x, const float* W, int in, int out, cudaStream_t st) {

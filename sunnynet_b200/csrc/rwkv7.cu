@@ -34,6 +34,7 @@
 
 #include "gemm.cuh"
 #include "kernels.cuh"
+#include "ptx.cuh"
 #include "runtime.cuh"
 #include "rwkv7.h"
 #include "sn_abi.h"
@@ -79,6 +80,7 @@ __global__ void rk_embed_kernel(int D, const int32_t* __restrict__ tok, int voca
                                 const float* __restrict__ w, const float* __restrict__ b,
                                 float* __restrict__ x, float eps) {
     __shared__ float red[32];
+    pdl_trigger();
     int t = tok[blockIdx.x];
     if (t < 0 || t >= vocab) {  // never read outside the table; report instead
         if (threadIdx.x == 0) atomicExch(err, kErrBadIndex);
@@ -98,6 +100,8 @@ __global__ void rk_tmix_prep_kernel(int D, int B, const float* __restrict__ x,
                                     const float* __restrict__ lerp, float* __restrict__ xn_out,
                                     float* __restrict__ planes, float eps) {
     __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();  // no-op unless launched with programmatic serialization
     const int s = blockIdx.x;
     const float* xr = x + (size_t)s * D;
     float* sh = shift + s * shift_stride;
@@ -124,6 +128,8 @@ __global__ void rk_mix_kernel(int B, int D, int first, const float* __restrict__
                               float* __restrict__ v, float* __restrict__ vfirst,
                               float* __restrict__ a, float* __restrict__ k,
                               float* __restrict__ kk) {
+    pdl_trigger();
+    pdl_wait();  // no-op unless launched with programmatic serialization
     const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (idx >= (long long)B * D) return;
     const int i = (int)(idx % D);
@@ -135,6 +141,72 @@ __global__ void rk_mix_kernel(int B, int D, int first, const float* __restrict__
         v[idx] = vv + (vfirst[idx] - vv) * sigm(dv[idx] + v0[i]);
     }
     const float aa = sigm(da[idx] + a0[i]);
+    a[idx] = aa;
+    const float kv = k[idx];
+    kk[idx] = kv * kkw[i];
+    k[idx] = kv + kv * (aa - 1.0f) * kaw[i];
+}
+
+// rk_mix_kernel with the LoRA second stages folded in, for fp32 w2 / a2 / v2
+// (rank Rw, Ra, Rv <= kLoraMax): dw = w2 lo_w, da = a2 lo_a, dv = v2 lo_v
+// (first: no dv) per (sequence, channel), each a sequential fmaf over the
+// rank, then the mix. CTA = 32 channels x 8 sequences (warp w: sequence
+// by*8 + w, lane: channel bx*32 + lane); the 32 channels' weight rows are
+// staged transposed in shared memory ([k][33]), the 8 sequences' LoRA
+// vectors after them.
+constexpr int kLoraMax = 128;
+__global__ void __launch_bounds__(256)
+    rk_lora_mix_kernel(int B, int D, int first, int Rw, int Ra, int Rv,
+                       const float* __restrict__ w2, const float* __restrict__ a2,
+                       const float* __restrict__ v2, const float* __restrict__ lo_w,
+                       const float* __restrict__ lo_a, const float* __restrict__ lo_v,
+                       const float* __restrict__ w0, const float* __restrict__ v0,
+                       const float* __restrict__ a0, const float* __restrict__ kkw,
+                       const float* __restrict__ kaw, float* __restrict__ ww,
+                       float* __restrict__ v, float* __restrict__ vfirst, float* __restrict__ a,
+                       float* __restrict__ k, float* __restrict__ kk) {
+    extern __shared__ float sm[];
+    pdl_trigger();
+    pdl_wait();  // no-op unless launched with programmatic serialization
+    const int rv = first ? 0 : Rv, R = Rw + Ra + rv;
+    float* wt = sm;                 // [R][33]: rows of w2, then a2, then v2
+    float* lo = sm + R * 33;        // [8][R]
+    const int d0 = blockIdx.x * 32, b0 = blockIdx.y * 8;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // staged with cp.async: every thread's copies are in flight at once (a
+    // load-then-store loop would wait a memory round trip per element)
+    for (int i = tid; i < 32 * R; i += 256) {
+        const int c = i / R, kk_ = i % R, d = d0 + c < D ? d0 + c : 0;
+        const float* src = kk_ < Rw        ? w2 + (size_t)d * Rw + kk_
+                           : kk_ < Rw + Ra ? a2 + (size_t)d * Ra + (kk_ - Rw)
+                                           : v2 + (size_t)d * Rv + (kk_ - Rw - Ra);
+        cp_async4(wt + kk_ * 33 + c, src, d0 + c < D ? 4u : 0u);
+    }
+    for (int i = tid; i < 8 * R; i += 256) {
+        const int j = i / R, kk_ = i % R, b = b0 + j < B ? b0 + j : 0;
+        const float* src = kk_ < Rw        ? lo_w + (size_t)b * Rw + kk_
+                           : kk_ < Rw + Ra ? lo_a + (size_t)b * Ra + (kk_ - Rw)
+                                           : lo_v + (size_t)b * Rv + (kk_ - Rw - Ra);
+        cp_async4(lo + j * R + kk_, src, b0 + j < B ? 4u : 0u);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const int b = b0 + warp, i = d0 + lane;
+    if (b >= B || i >= D) return;
+    const float* lb = lo + warp * R;
+    float dw = 0.0f, da = 0.0f, dv = 0.0f;
+    for (int q = 0; q < Rw; ++q) dw = fmaf(lb[q], wt[q * 33 + lane], dw);
+    for (int q = Rw; q < Rw + Ra; ++q) da = fmaf(lb[q], wt[q * 33 + lane], da);
+    for (int q = Rw + Ra; q < R; ++q) dv = fmaf(lb[q], wt[q * 33 + lane], dv);
+    const size_t idx = (size_t)b * D + i;
+    ww[idx] = expf(-sigm(dw + w0[i]) * kInvSqrtE);
+    if (first) {
+        vfirst[idx] = v[idx];
+    } else {
+        const float vv = v[idx];
+        v[idx] = vv + (vfirst[idx] - vv) * sigm(dv + v0[i]);
+    }
+    const float aa = sigm(da + a0[i]);
     a[idx] = aa;
     const float kv = k[idx];
     kk[idx] = kv * kkw[i];
@@ -155,6 +227,8 @@ __global__ void __launch_bounds__(256)
                     float* __restrict__ y) {
     constexpr int HS = VPL * 32;
     __shared__ float kn[HS], yv[HS], red[32];
+    pdl_trigger();
+    pdl_wait();  // no-op unless launched with programmatic serialization
     const int h = blockIdx.x % NH, b = blockIdx.x / NH;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t o = (size_t)b * D + (size_t)h * HS;
@@ -224,6 +298,8 @@ __global__ void rk_cmix_prep_kernel(int D, const float* __restrict__ x, float* _
                                     const float* __restrict__ b, const float* __restrict__ lerp,
                                     float* __restrict__ xk, float eps) {
     __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();  // no-op unless launched with programmatic serialization
     const int s = blockIdx.x;
     const float* xr = x + (size_t)s * D;
     float* sh = shift + s * shift_stride + D;
@@ -240,6 +316,8 @@ __global__ void rk_cmix_prep_kernel(int D, const float* __restrict__ x, float* _
 __global__ void rk_ln_kernel(int D, const float* __restrict__ x, const float* __restrict__ w,
                              const float* __restrict__ b, float* __restrict__ y, float eps) {
     __shared__ float red[32];
+    pdl_trigger();
+    pdl_wait();  // no-op unless launched with programmatic serialization
     const float* xr = x + (size_t)blockIdx.x * D;
     float mean, rstd;
     row_stats(xr, D, eps, red, &mean, &rstd);
@@ -507,11 +585,14 @@ int load_rwkv(RwkvModel* m, const char* path, int nseq) {
 }
 
 // y (B,out) [epi]= M x (B,in)
+// Launched with programmatic serialization: inside the step every contraction
+// follows another kernel of the same stream.
 int mat_mul(const RkMat& M, float* y, const float* x, int B, int epi, cudaStream_t st) {
     ProfScope ps(M.q4 ? "w4a8_gemv" : "gemm_f32", st);
     if (M.q4) {
         static const int map[] = {kW4Store, kW4Add, kW4Relu2, kW4Tanh, kW4Sigmoid};
-        return launch_w4a8(y, x, M.q, M.scale, B, M.in, M.out, M.block, M.fp16, st, map[epi]);
+        return launch_w4a8(y, x, M.q, M.scale, B, M.in, M.out, M.block, M.fp16, st, map[epi],
+                           true);
     }
     GemmArgs g;
     g.M = B; g.N = M.out; g.K = M.in;
@@ -520,7 +601,7 @@ int mat_mul(const RkMat& M, float* y, const float* x, int B, int epi, cudaStream
     g.C = y; g.ldc = M.out;
     static const int emap[] = {kEpiNone, kEpiAdd, kEpiRelu2, kEpiTanh, kEpiSigmoid};
     g.epi = emap[epi];
-    return launch_gemm(g, kWF32, st);
+    return launch_gemm(g, kWF32, st, nullptr, true);
 }
 
 enum { E_STORE = 0, E_ADD = 1, E_RELU2 = 2, E_TANH = 3, E_SIG = 4 };
@@ -536,8 +617,13 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
     for (int l = 0; l < nl; ++l) {
         const RkLayer& A = m->ly[l];
         float* sh = m->shift + (size_t)l * 2 * D;
-        rk_tmix_prep_kernel<<<B, 256, 0, st>>>(D, B, m->x, sh, sh_stride, A.ln1w, A.ln1b, A.lerp,
-                                               m->xn, m->planes, m->eps);
+        // every kernel after the embedding follows another one on this stream:
+        // programmatic launches (each waits before touching its inputs)
+        SN_TRY(cuda_check(launch_pdl(rk_tmix_prep_kernel, dim3(B), dim3(256), 0, st, D, B,
+                                     (const float*)m->x, sh, sh_stride, (const float*)A.ln1w,
+                                     (const float*)A.ln1b, (const float*)A.lerp, m->xn, m->planes,
+                                     m->eps),
+                          "tmix launch"));
         const float *xr = m->planes, *xw = xr + plane, *xk = xw + plane, *xv = xk + plane,
                     *xa = xv + plane, *xg = xa + plane;
         {   // first-stage projections of the input mixes (v1 from layer 1 on):
@@ -558,39 +644,73 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
                 for (int i = 0; i < ng; ++i)
                     pr[i] = W4Problem{gy[i], gx[i], gm[i]->q, gm[i]->scale, gm[i]->out, map[ge[i]]};
                 ProfScope ps("w4a8_group", st);
-                SN_TRY(launch_w4a8_tc_group(pr, ng, B, D, gm[0]->block, gm[0]->fp16, st));
+                SN_TRY(launch_w4a8_tc_group(pr, ng, B, D, gm[0]->block, gm[0]->fp16, st, true));
             } else {
                 for (int i = 0; i < ng; ++i) SN_TRY(mat_mul(*gm[i], gy[i], gx[i], B, ge[i], st));
             }
         }
-        SN_TRY(mat_mul(A.w2, m->dw, m->lo_w, B, E_STORE, st));
-        if (l > 0) SN_TRY(mat_mul(A.v2, m->dv, m->lo_v, B, E_STORE, st));
-        SN_TRY(mat_mul(A.a2, m->da, m->lo_a, B, E_STORE, st));
         SN_TRY(mat_mul(A.g2, m->g, m->lo_g, B, E_STORE, st));
-        rk_mix_kernel<<<ew, 256, 0, st>>>(B, D, l == 0 ? 1 : 0, m->dw, A.w0, m->dv, A.v0, m->da,
-                                         A.a0, A.kkw, A.kaw, m->ww, m->v, m->vfirst, m->a, m->k,
-                                         m->kk);
-        const int grid = B * m->NH;
-        ProfScope ps_heads("rk_heads", st);
-        switch (m->HS) {
-#define RK_HEADS(V)                                                                            \
-    rk_heads_kernel<V><<<grid, 256, 0, st>>>(m->NH, m->L, l, D, m->S, m->ww, m->k, m->v, m->a, \
-                                             m->kk, m->r, m->g, A.rkw, A.lnxw, A.lnxb, m->y);  \
+        // fp32 LoRA second stages (ranks below a quantisation block stay fp32)
+        // are folded into the mix kernel
+        const int R = A.w2.in + A.a2.in + (l > 0 ? A.v2.in : 0);
+        const size_t smem = ((size_t)R * 33 + 8 * R) * 4;
+        const bool fold = !A.w2.q4 && !A.a2.q4 && (l == 0 || !A.v2.q4) && A.w2.in <= kLoraMax &&
+                          A.a2.in <= kLoraMax && A.v2.in <= kLoraMax && smem <= 48 * 1024;
+        if (fold) {
+            ProfScope ps("rk_lora_mix", st);
+            SN_TRY(cuda_check(
+                launch_pdl(rk_lora_mix_kernel, dim3((unsigned)((D + 31) / 32), (unsigned)((B + 7) / 8)),
+                           dim3(256), smem, st, B, D, l == 0 ? 1 : 0, A.w2.in, A.a2.in, A.v2.in,
+                           (const float*)A.w2.w, (const float*)A.a2.w, (const float*)A.v2.w,
+                           (const float*)m->lo_w, (const float*)m->lo_a, (const float*)m->lo_v,
+                           (const float*)A.w0, (const float*)A.v0, (const float*)A.a0,
+                           (const float*)A.kkw, (const float*)A.kaw, m->ww, m->v, m->vfirst, m->a,
+                           m->k, m->kk),
+                "lora mix launch"));
+        } else {
+            SN_TRY(mat_mul(A.w2, m->dw, m->lo_w, B, E_STORE, st));
+            if (l > 0) SN_TRY(mat_mul(A.v2, m->dv, m->lo_v, B, E_STORE, st));
+            SN_TRY(mat_mul(A.a2, m->da, m->lo_a, B, E_STORE, st));
+            SN_TRY(cuda_check(launch_pdl(rk_mix_kernel, dim3(ew), dim3(256), 0, st, B, D,
+                                         l == 0 ? 1 : 0, (const float*)m->dw, (const float*)A.w0,
+                                         (const float*)m->dv, (const float*)A.v0,
+                                         (const float*)m->da, (const float*)A.a0,
+                                         (const float*)A.kkw, (const float*)A.kaw, m->ww, m->v,
+                                         m->vfirst, m->a, m->k, m->kk),
+                              "mix launch"));
+        }
+        {
+            const dim3 grid((unsigned)(B * m->NH));
+            ProfScope ps_heads("rk_heads", st);
+            cudaError_t e;
+            switch (m->HS) {
+#define RK_HEADS(V)                                                                                \
+    e = launch_pdl(rk_heads_kernel<V>, grid, dim3(256), 0, st, m->NH, m->L, l, D, m->S,            \
+                   (const float*)m->ww, (const float*)m->k, (const float*)m->v, (const float*)m->a, \
+                   (const float*)m->kk, (const float*)m->r, (const float*)m->g,                    \
+                   (const float*)A.rkw, (const float*)A.lnxw, (const float*)A.lnxb, m->y);         \
     break;
-            case 32: RK_HEADS(1)
-            case 64: RK_HEADS(2)
-            case 128: RK_HEADS(4)
-            default: RK_HEADS(8)
+                case 32: RK_HEADS(1)
+                case 64: RK_HEADS(2)
+                case 128: RK_HEADS(4)
+                default: RK_HEADS(8)
 #undef RK_HEADS
+            }
+            SN_TRY(cuda_check(e, "heads launch"));
         }
         SN_TRY(mat_mul(A.ow, m->x, m->y, B, E_ADD, st));
-        rk_cmix_prep_kernel<<<B, 256, 0, st>>>(D, m->x, sh, sh_stride, A.ln2w, A.ln2b, A.cmk_lerp,
-                                               m->xk2, m->eps);
+        SN_TRY(cuda_check(launch_pdl(rk_cmix_prep_kernel, dim3(B), dim3(256), 0, st, D,
+                                     (const float*)m->x, sh, sh_stride, (const float*)A.ln2w,
+                                     (const float*)A.ln2b, (const float*)A.cmk_lerp, m->xk2,
+                                     m->eps),
+                          "cmix launch"));
         SN_TRY(mat_mul(A.cmk, m->ck, m->xk2, B, E_RELU2, st));
         SN_TRY(mat_mul(A.cmv, m->x, m->ck, B, E_ADD, st));
     }
     if (last_layer < 0 && head) {
-        rk_ln_kernel<<<B, 256, 0, st>>>(D, m->x, m->on_w, m->on_b, m->xf, m->eps);
+        SN_TRY(cuda_check(launch_pdl(rk_ln_kernel, dim3(B), dim3(256), 0, st, D, (const float*)m->x,
+                                     (const float*)m->on_w, (const float*)m->on_b, m->xf, m->eps),
+                          "ln launch"));
         SN_TRY(mat_mul(m->head, m->logits, m->xf, B, E_STORE, st));
     }
     return cuda_check(cudaGetLastError(), "rwkv step launch");

@@ -44,7 +44,9 @@ struct TcCfg {
     static constexpr int W_BYTES = BN * 128;
     static constexpr int STAGE = 2 * A_BYTES + 2 * W_BYTES;
     static constexpr int S = BN == 128 ? 3 : (BN == 64 ? 4 : 5);
-    static constexpr int SMEM = S * STAGE + 1024 + 256;
+    // epilogue operands loaded under the main loop: [4 warps][32][33] floats
+    static constexpr int PRE = 4 * 32 * 33 * 4;
+    static constexpr int SMEM = S * STAGE + PRE + 1024 + 256;
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -88,7 +90,7 @@ template <int EPI>
 __device__ __forceinline__ void tc_rows(const GemmArgs& a, int mr0, int n, bool nok, float ws,
                                         const float* stg, int lane) {
     if (!nok) return;
-#pragma unroll
+#pragma unroll 4  // compact: this runs once per launch, from a cold instruction cache
     for (int r = 0; r < 32; ++r) {
         const int mm = mr0 + r;
         if (mm >= a.M) continue;
@@ -125,22 +127,89 @@ __device__ __forceinline__ float epi_elem(const GemmArgs& a, int m, int n, float
     return acc;
 }
 
-// Split K: rows [r0, r0 + rows) of the tile, each element the sum of the
-// cluster's partials (rank 0 first, then 1, ...), then the epilogue.
+// The residual (p*S + F + X) or accumulate (C) operand of output (mm, n),
+// 0 outside the matrix.
+__device__ __forceinline__ float tc_operand(const GemmArgs& a, long long mm, int n) {
+    if (mm >= a.M || n >= a.N) return 0.0f;
+    return a.epi == kEpiResid ? a.p * a.S[mm * a.lds + n] + a.F[mm * a.ldf + n] + a.X[mm * a.ldx + n]
+                              : a.C[mm * a.ldc + n];
+}
+
+// Epilogue code runs once per launch, mostly from a cold instruction cache:
+// its loops keep small bodies (a few elements per iteration, enough loads in
+// flight) instead of being unrolled whole.
+//
+// Split K, owner side, in groups of 4 consecutive outputs of a row (16-byte
+// loads and stores; the host splits K only when every operand allows that).
+// The owner's ng = rows * BN / 4 groups are spread over the 128 epilogue
+// threads: group g = u * 128 + et, row-major. tc_own_operands stages each
+// group's residual / accumulate operands in shared memory before the
+// accumulator is ready; tc_reduce sums the ks partial rows of the cluster in
+// rank order (partials at [row][BN+4] in each CTA), then applies the epilogue.
+template <int BN>
+__device__ __forceinline__ void tc_own_operands(const GemmArgs& a, int mr0, int n0, int ng, int et,
+                                                float4* pre) {
+#pragma unroll 2
+    for (int u = 0; u * 128 < ng; ++u) {
+        const int g = u * 128 + et;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const long long mm = mr0 + (4 * g) / BN;
+        const int n = n0 + (4 * g) % BN;
+        if (g < ng && mm < a.M && n < a.N) {
+            if (a.epi == kEpiResid) {
+                const float4 sv = *reinterpret_cast<const float4*>(a.S + mm * a.lds + n);
+                const float4 fv = *reinterpret_cast<const float4*>(a.F + mm * a.ldf + n);
+                const float4 xv = *reinterpret_cast<const float4*>(a.X + mm * a.ldx + n);
+                v = make_float4(a.p * sv.x + fv.x + xv.x, a.p * sv.y + fv.y + xv.y,
+                                a.p * sv.z + fv.z + xv.z, a.p * sv.w + fv.w + xv.w);
+            } else {
+                v = *reinterpret_cast<const float4*>(a.C + mm * a.ldc + n);
+            }
+        }
+        pre[g] = v;
+    }
+}
+
 template <int EPI, int BN>
-__device__ __forceinline__ void tc_reduce(const GemmArgs& a, const float* part, int ks, int r0,
-                                          int rows, int m0, int n0) {
-    for (int i = threadIdx.x; i < rows * BN; i += kThreads) {
-        const int r = r0 + i / BN, j = i % BN;
-        const int mm = m0 + r, n = n0 + j;
-        const float* src = part + r * (BN + 1) + j;
-        float acc = ld_dsmem_f32(src, 0);
-        for (int p = 1; p < ks; ++p) acc += ld_dsmem_f32(src, (uint32_t)p);
-        if (mm < a.M && n < a.N) {
-            const long long o = (long long)mm * a.ldc + n;
-            const float y = epi_elem<EPI>(a, mm, n, acc);
-            a.C[o] = y;
-            if (a.Ch) store_split((__nv_bfloat16*)a.Ch, (__nv_bfloat16*)a.Cl, o, y);
+__device__ __forceinline__ void tc_reduce(const GemmArgs& a, const float* part, int ks, int rows,
+                                          int r0, int m0, int n0, int et, const float4* pre) {
+    const int ng = rows * BN / 4;
+#pragma unroll 2
+    for (int u = 0; u * 128 < ng; ++u) {
+        const int g = u * 128 + et;
+        if (g >= ng) continue;
+        const int r = (4 * g) / BN, c = (4 * g) % BN;
+        const float* src = part + (r0 + r) * (BN + 4) + c;
+        float4 x = ld_dsmem_f32x4(src, 0);
+        for (int p = 1; p < ks; ++p) {
+            const float4 t = ld_dsmem_f32x4(src, (uint32_t)p);
+            x.x += t.x;
+            x.y += t.y;
+            x.z += t.z;
+            x.w += t.w;
+        }
+        const long long mm = m0 + r0 + r;
+        const int n = n0 + c;
+        if (mm >= a.M || n >= a.N) continue;  // N % 4 == 0: a group is all in or all out
+        float y[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (EPI == kEpiResid || EPI == kEpiAdd) {
+                const float4 pv = pre[g];
+                const float pi = i == 0 ? pv.x : (i == 1 ? pv.y : (i == 2 ? pv.z : pv.w));
+                float xi = y[i];
+                if (a.wscale) xi = xi * a.wscale[n + i];
+                y[i] = EPI == kEpiResid ? xi + pi : pi + xi;
+            } else {
+                y[i] = epi_elem<EPI>(a, (int)mm, n + i, y[i]);
+            }
+        }
+        const long long o = mm * a.ldc + n;
+        *reinterpret_cast<float4*>(a.C + o) = make_float4(y[0], y[1], y[2], y[3]);
+        if (a.Ch) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                store_split((__nv_bfloat16*)a.Ch, (__nv_bfloat16*)a.Cl, o + i, y[i]);
         }
     }
 }
@@ -157,7 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* sb = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // 1024-B aligned ring
-    uint64_t* full = reinterpret_cast<uint64_t*>(sb + S * C::STAGE);
+    float* pre_all = reinterpret_cast<float*>(sb + S * C::STAGE);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sb + S * C::STAGE + C::PRE);
     uint64_t* empty = full + S;
     uint64_t* acc_full = empty + S;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(acc_full + 1);
@@ -260,79 +330,89 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {  // ------------------------------------------------ epilogue (warps 2-5)
         const int q = warp & 3;  // TMEM lane quarter this warp may read
+        const int et = threadIdx.x - 64;
         pdl_wait();  // the epilogue reads (and overwrites) the previous kernels' outputs
-        const bool ok = mbar_wait(acc_full, 0, err);
-        tc_fence_after();
         if (ks > 1) {
-            // split K: this CTA's partial rows into its shared memory (the
-            // drained ring), [128][BN+1]; reduced across the cluster below
+            // split K: CTA kz owns rows [kz*rows, (kz+1)*rows) of the tile; its
+            // residual / accumulate operands are loaded now, under the main loop
+            const int rows = BM / ks;
+            if (LOADS)
+                tc_own_operands<BN>(a, m0 + kz * rows, n0, rows * BN / 4, et,
+                                    reinterpret_cast<float4*>(pre_all));
+            const bool ok = mbar_wait(acc_full, 0, err);
+            tc_fence_after();
             if (ok && !*give_up) {
-                float* part = reinterpret_cast<float*>(sb) + (q * 32 + lane) * (BN + 1);
+                // this CTA's partial rows into its own shared memory (the
+                // drained ring), [128][BN+4]; the owners read them below
+                float4* part = reinterpret_cast<float4*>(reinterpret_cast<float*>(sb) +
+                                                         (q * 32 + lane) * (BN + 4));
 #pragma unroll 1
                 for (int j0 = 0; j0 < BN; j0 += 32) {
                     float v[32];
                     tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)j0, v);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) part[j0 + j] = v[j];
+                    for (int j = 0; j < 32; j += 4)
+                        part[(j0 + j) / 4] = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
                 }
             }
-        } else if (ok && !*give_up) {
-            // 32x32 blocks go through shared memory (the drained ring) so that a
-            // warp touches one 128-byte row segment per global access
-            float* stg = reinterpret_cast<float*>(sb) + (warp - 2) * (32 * 33);
+        } else {
+            // this warp's operands of a 32x32 block, [row][33] in shared memory
+            float* pre_w = pre_all + (warp - 2) * (32 * 33);
+            if (LOADS && BN == 32) {  // the only block's operands, under the main loop
+#pragma unroll 8
+                for (int r = 0; r < 32; ++r)
+                    pre_w[r * 33 + lane] = tc_operand(a, m0 + q * 32 + r, n0 + lane);
+            }
+            const bool ok = mbar_wait(acc_full, 0, err);
+            tc_fence_after();
+            if (ok && !*give_up) {
+                // 32x32 blocks go through shared memory (the drained ring) so that a
+                // warp touches one 128-byte row segment per global access
+                float* stg = reinterpret_cast<float*>(sb) + (warp - 2) * (32 * 33);
 #pragma unroll 1
-            for (int j0 = 0; j0 < BN; j0 += 32) {
-                float v[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)j0, v);
+                for (int j0 = 0; j0 < BN; j0 += 32) {
+                    float v[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)j0, v);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = v[j];
-                __syncwarp();
-                const int n = n0 + j0 + lane;
-                const bool nok = n < a.N;
-                if (!LOADS) {
-                    // the epilogue kind is chosen once per block, not per element
-                    const float ws = a.wscale && nok ? a.wscale[n] : 1.0f;
-                    const int mr0 = m0 + q * 32;
-                    switch (a.epi) {
-                        case kEpiWedge: tc_rows<kEpiWedge>(a, mr0, n, nok, ws, stg, lane); break;
-                        case kEpiRelu2: tc_rows<kEpiRelu2>(a, mr0, n, nok, ws, stg, lane); break;
-                        case kEpiTanh: tc_rows<kEpiTanh>(a, mr0, n, nok, ws, stg, lane); break;
-                        case kEpiSigmoid: tc_rows<kEpiSigmoid>(a, mr0, n, nok, ws, stg, lane); break;
-                        default: tc_rows<kEpiNone>(a, mr0, n, nok, ws, stg, lane);
-                    }
-                } else {
-                    // the epilogue's other operands for all 32 rows are loaded
-                    // before any of them is used or any result stored, so the
-                    // loads overlap (one round trip per block, not per row)
-                    float pre[32];
-#pragma unroll
-                    for (int r = 0; r < 32; ++r) {
-                        const long long mm = m0 + q * 32 + r;
-                        pre[r] = 0.0f;
-                        if (mm < a.M && nok) {
-                            if (a.epi == kEpiResid)
-                                pre[r] = a.p * a.S[mm * a.lds + n] + a.F[mm * a.ldf + n] +
-                                         a.X[mm * a.ldx + n];
-                            else
-                                pre[r] = a.C[mm * a.ldc + n];
+                    for (int j = 0; j < 32; ++j) stg[lane * 33 + j] = v[j];
+                    __syncwarp();
+                    const int n = n0 + j0 + lane;
+                    const bool nok = n < a.N;
+                    if (!LOADS) {
+                        // the epilogue kind is chosen once per block, not per element
+                        const float ws = a.wscale && nok ? a.wscale[n] : 1.0f;
+                        const int mr0 = m0 + q * 32;
+                        switch (a.epi) {
+                            case kEpiWedge: tc_rows<kEpiWedge>(a, mr0, n, nok, ws, stg, lane); break;
+                            case kEpiRelu2: tc_rows<kEpiRelu2>(a, mr0, n, nok, ws, stg, lane); break;
+                            case kEpiTanh: tc_rows<kEpiTanh>(a, mr0, n, nok, ws, stg, lane); break;
+                            case kEpiSigmoid: tc_rows<kEpiSigmoid>(a, mr0, n, nok, ws, stg, lane); break;
+                            default: tc_rows<kEpiNone>(a, mr0, n, nok, ws, stg, lane);
+                        }
+                    } else {
+                        if (BN > 32) {  // wider tiles: this block's operands now
+#pragma unroll 8
+                            for (int r = 0; r < 32; ++r)
+                                pre_w[r * 33 + lane] = tc_operand(a, m0 + q * 32 + r, n);
+                        }
+                        const float ws = a.wscale && nok ? a.wscale[n] : 1.0f;
+#pragma unroll 4
+                        for (int r = 0; r < 32; ++r) {
+                            const long long mm = m0 + q * 32 + r;
+                            if (mm < a.M && nok) {
+                                float acc = stg[r * 33 + lane];
+                                if (a.wscale) acc = acc * ws;
+                                const float pr = pre_w[r * 33 + lane];
+                                const float y = a.epi == kEpiResid ? acc + pr : pr + acc;
+                                a.C[mm * a.ldc + n] = y;
+                                if (a.Ch)
+                                    store_split((__nv_bfloat16*)a.Ch, (__nv_bfloat16*)a.Cl,
+                                                mm * a.ldc + n, y);
+                            }
                         }
                     }
-                    const float ws = a.wscale && nok ? a.wscale[n] : 1.0f;
-#pragma unroll  // pre[] stays in registers
-                    for (int r = 0; r < 32; ++r) {
-                        const long long mm = m0 + q * 32 + r;
-                        if (mm < a.M && nok) {
-                            float acc = stg[r * 33 + lane];
-                            if (a.wscale) acc = acc * ws;
-                            const float y = a.epi == kEpiResid ? acc + pre[r] : pre[r] + acc;
-                            a.C[mm * a.ldc + n] = y;
-                            if (a.Ch)
-                                store_split((__nv_bfloat16*)a.Ch, (__nv_bfloat16*)a.Cl,
-                                            mm * a.ldc + n, y);
-                        }
-                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
         }
     }
@@ -345,23 +425,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                      : "memory");
     }
     if (ks > 1) {
-        // every CTA of the cluster reaches both barriers (all waits above are
-        // bounded); CTA kz finishes rows [kz*128/ks, (kz+1)*128/ks) of the
-        // tile, summing the partials in rank order, so results do not depend
-        // on timing
+        // every thread of the cluster reaches both barriers (all waits above
+        // are bounded). CTA kz finishes rows [kz*rows, (kz+1)*rows) of the
+        // tile, summing the cluster's partials in rank order (results do not
+        // depend on timing); no CTA leaves while its partials may be read.
         cluster_sync();
-        const float* part = reinterpret_cast<const float*>(sb);
-        const int rows = BM / ks, r0 = kz * rows;
-        switch (a.epi) {
-            case kEpiWedge: tc_reduce<kEpiWedge, BN>(a, part, ks, r0, rows, m0, n0); break;
-            case kEpiResid: tc_reduce<kEpiResid, BN>(a, part, ks, r0, rows, m0, n0); break;
-            case kEpiAdd: tc_reduce<kEpiAdd, BN>(a, part, ks, r0, rows, m0, n0); break;
-            case kEpiRelu2: tc_reduce<kEpiRelu2, BN>(a, part, ks, r0, rows, m0, n0); break;
-            case kEpiTanh: tc_reduce<kEpiTanh, BN>(a, part, ks, r0, rows, m0, n0); break;
-            case kEpiSigmoid: tc_reduce<kEpiSigmoid, BN>(a, part, ks, r0, rows, m0, n0); break;
-            default: tc_reduce<kEpiNone, BN>(a, part, ks, r0, rows, m0, n0);
+        if (warp >= 2) {
+            const int et = threadIdx.x - 64, rows = BM / ks, r0 = kz * rows;
+            const float* part = reinterpret_cast<const float*>(sb);
+            switch (a.epi) {
+                case kEpiWedge: tc_reduce<kEpiWedge, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
+                case kEpiResid: tc_reduce<kEpiResid, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
+                case kEpiAdd: tc_reduce<kEpiAdd, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
+                case kEpiRelu2: tc_reduce<kEpiRelu2, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
+                case kEpiTanh: tc_reduce<kEpiTanh, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
+                case kEpiSigmoid: tc_reduce<kEpiSigmoid, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
+                default: tc_reduce<kEpiNone, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all));
+            }
         }
-        cluster_sync();  // no CTA leaves while its partials may still be read
+        cluster_sync();
     }
 }
 
@@ -550,8 +632,17 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
     // each CTA at least two slabs (few-tile contractions of batched decode)
     const long long tiles = mt * ((a.N + bn - 1) / bn);
     const int nkt = (a.K + BK - 1) / BK;
+    // Split K pays for its cross-CTA reduction only with a long enough K loop
+    // (>= 8 slabs); the reduction works on 16-byte groups, so every operand
+    // it touches must allow that.
+    auto al16 = [](const void* p, long long ld) {
+        return p == nullptr || ((uintptr_t)p % 16 == 0 && ld % 4 == 0);
+    };
+    bool vec = a.N % 4 == 0 && al16(a.C, a.ldc) &&
+               (a.Ch == nullptr || ((uintptr_t)a.Ch % 8 == 0 && (uintptr_t)a.Cl % 8 == 0));
+    if (a.epi == kEpiResid) vec = vec && al16(a.S, a.lds) && al16(a.F, a.ldf) && al16(a.X, a.ldx);
     int ks = 1;
-    if (!getenv("SN_TC_NO_SPLITK"))
+    if (!getenv("SN_TC_NO_SPLITK") && bn <= 64 && vec && nkt >= 8)
         while (ks < 8 && tiles * ks * 2 <= sms && nkt >= ks * 4) ks *= 2;
     const bool ld = a.epi == kEpiResid || a.epi == kEpiAdd;
 #define SN_TC_BN(I8, LD)                                                              \

@@ -139,6 +139,8 @@ __global__ void quant_rows_kernel(const __grid_constant__ W4QGroup q, int M, int
                                   int* __restrict__ xsum) {
     const int nb = K / block;
     const int lane = threadIdx.x & 31;
+    pdl_trigger();
+    pdl_wait();  // no-op unless launched with programmatic serialization
     const long long w = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5);
     if (w >= (long long)q.n * M * nb) return;
     const int u = (int)(w / ((long long)M * nb));
@@ -219,6 +221,7 @@ __global__ void __launch_bounds__(kW4Threads, 1)
     auto sP = [&](int s) { return ring + s * C::STAGE + C::A_BYTES + C::U_BYTES; };
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_trigger();  // the next kernel may start its own prologue
     __shared__ W4Tables gt;
 #pragma unroll
     for (int i = 0; i < kW4MaxGroup; ++i) {  // constant indices: parameter-bank loads
@@ -258,6 +261,19 @@ __global__ void __launch_bounds__(kW4Threads, 1)
 
     if (warp == 0) {  // --------------------------------------------------- TMA
         if (lane == 0) {
+            // the packed weights of the first tile's first S slabs do not depend
+            // on the previous kernel (the activation quantisation): in flight
+            // before waiting for it
+            const int pre = nslab < S ? nslab : S;
+            if ((int)blockIdx.x < ntiles) {
+                int pi, m0, n0;
+                w4_tile<BN>(gt, blockIdx.x, pi, m0, n0);
+                for (int s = 0; s < pre; ++s) {
+                    mbar_expect_tx(&full[s], C::A_BYTES + C::P_BYTES);
+                    tma_load_2d(sP(s), &g.tw[pi], s * (kSlab / 2), n0, &full[s]);
+                }
+            }
+            pdl_wait();
             int gs = 0, issued = 0;
             bool run = true;
             for (int t = blockIdx.x; t < ntiles && run; t += gridDim.x) {
@@ -265,14 +281,16 @@ __global__ void __launch_bounds__(kW4Threads, 1)
                 w4_tile<BN>(gt, t, pi, m0, n0);
                 for (int s = 0; s < nslab; ++s, ++gs) {
                     const int st = gs % S;
-                    if (*give_up || (gs >= S && !mbar_wait(&empty[st], ((gs / S) - 1) & 1, err))) {
-                        *give_up = 1;
-                        run = false;
-                        break;
+                    if (gs >= pre) {  // first-round stages are never abandoned half-loaded
+                        if (*give_up || !mbar_wait(&empty[st], ((gs / S) - 1) & 1, err)) {
+                            *give_up = 1;
+                            run = false;
+                            break;
+                        }
+                        mbar_expect_tx(&full[st], C::A_BYTES + C::P_BYTES);
+                        tma_load_2d(sP(st), &g.tw[pi], s * (kSlab / 2), n0, &full[st]);
                     }
-                    mbar_expect_tx(&full[st], C::A_BYTES + C::P_BYTES);
                     tma_load_2d(sA(st), &g.ta[pi], s * kSlab, m0, &full[st]);
-                    tma_load_2d(sP(st), &g.tw[pi], s * (kSlab / 2), n0, &full[st]);
                     issued = gs + 1;
                 }
             }
@@ -351,6 +369,7 @@ __global__ void __launch_bounds__(kW4Threads, 1)
         // row, weight scale of each output row of the tile) arrive by cp.async
         // in a ring of kScD blocks, issued kScD blocks ahead of their use.
         const int q = warp & 3, wi = warp - 2;
+        pdl_wait();  // scales and (kW4Add) outputs come from earlier kernels
         float* stg = stg_all + wi * 32 * (BN + 1);
         uint32_t* scr = scr_all + wi * kScD * (64 + BN);
         int b = 0;  // block counter across tiles (accumulator slot b & 1)
@@ -472,6 +491,7 @@ size_t w4_work_bytes(int M, int K, int block, int planes) {
 
 template <int BN, bool FP16S>
 int launch_bn(const W4Group& g, int M, int K, int block, cudaStream_t st) {
+    // always a programmatic launch: it follows its own quantisation kernel
     using C = W4Cfg<BN>;
     const size_t smem = 1024 + (size_t)kW4Stages * C::STAGE + 4ull * 4 * 32 * (BN + 1) +
                         4ull * 4 * kScD * (64 + BN) + 8ull * (3 * kW4Stages + 5) + 16;
@@ -485,8 +505,9 @@ int launch_bn(const W4Group& g, int M, int K, int block, cudaStream_t st) {
     }
     if (smem > 200 * 1024) return fail(SN_E_INVAL, "w4a8_tc: BN=%d needs too much shared memory", BN);
     const int ctas = g.tile0[g.np] < rt().num_sms ? g.tile0[g.np] : rt().num_sms;  // persistent
-    w4a8_tc_kernel<BN, FP16S><<<ctas, kW4Threads, smem, st>>>(g, M, K, block, rt().d_err);
-    return cuda_check(cudaGetLastError(), "w4a8_tc launch");
+    return cuda_check(launch_pdl(w4a8_tc_kernel<BN, FP16S>, dim3(ctas), dim3(kW4Threads), smem, st,
+                                 g, M, K, block, rt().d_err),
+                      "w4a8_tc launch");
 }
 
 }  // namespace
@@ -517,7 +538,7 @@ int w4a8_tc_reserve(int M, int K, int block, int planes) {
 }
 
 int launch_w4a8_tc_group(const W4Problem* pr, int np, int M, int K, int block, bool fp16,
-                         cudaStream_t st) {
+                         cudaStream_t st, bool pdl) {
     if (np < 1 || np > kW4MaxGroup) return fail(SN_E_INVAL, "w4a8_tc: %d problems in a group", np);
     // distinct inputs, each quantised once
     W4QGroup q;
@@ -538,9 +559,9 @@ int launch_w4a8_tc_group(const W4Problem* pr, int np, int M, int K, int block, b
     int* xs = reinterpret_cast<int*>(sx + (size_t)q.n * M * nb);
     {
         const long long warps = (long long)q.n * M * nb;
-        quant_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(q, M, K, block, codes, sx,
-                                                                       xs);
-        SN_TRY(cuda_check(cudaGetLastError(), "w4a8_tc quant launch"));
+        SN_TRY(cuda_check(launch_pdl_if(pdl, quant_rows_kernel, dim3((unsigned)((warps + 7) / 8)),
+                                        dim3(256), 0, st, q, M, K, block, codes, sx, xs),
+                          "w4a8_tc quant launch"));
     }
     const int mt = (M + kBM - 1) / kBM;
     long long tiles64 = 0;
@@ -569,9 +590,9 @@ int launch_w4a8_tc_group(const W4Problem* pr, int np, int M, int K, int block, b
 }
 
 int launch_w4a8_tc(float* Y, const float* X, const uint8_t* Wq, const void* scale, int M, int K,
-                   int N, int block, bool fp16, int epi, cudaStream_t st) {
+                   int N, int block, bool fp16, int epi, cudaStream_t st, bool pdl) {
     const W4Problem p{Y, X, Wq, scale, N, epi};
-    return launch_w4a8_tc_group(&p, 1, M, K, block, fp16, st);
+    return launch_w4a8_tc_group(&p, 1, M, K, block, fp16, st, pdl);
 }
 
 }  // namespace sn

@@ -422,7 +422,8 @@ def test_split_k_cluster_matches_unsplit_and_oracle(quant):
     import os
     from sunnynet_b200 import formats
     from sunnynet_b200.model import SunnyBatch
-    shape = formats.SunnyShape(3000, 256, 448, 160, 4, 2)  # K up to 448: 7 slabs
+    # K = 512 / 640: 8 and 10 slabs, enough for the split (Ws, V, Wz, Wc)
+    shape = formats.SunnyShape(3000, 512, 640, 160, 4, 2)
     B = 48
     rng = np.random.default_rng(7 + quant)
     toks = [rng.integers(0, shape.vocab, B).astype(np.int32) for _ in range(3)]
