@@ -663,7 +663,8 @@ def rwkv_launches(S, B, block=128):
     for l in range(S.layers):
         first = [(D, D)] * 3 + [(D, Rw), (D, Ra), (D, Rg)] + ([(D, Rv)] if l > 0 else [])
         grouped = all(tc(K, N) for K, N in first)
-        n += 1 + (2 if grouped else sum(mm(K, N) for K, N in first))  # prep + first stage
+        small = B <= 8 and all(K % block == 0 for K, N in first)  # one SIMT group launch
+        n += 1 + (2 if grouped else 1 if small else sum(mm(K, N) for K, N in first))  # prep + stage 1
         # LoRA second stages: ranks below a quantisation block stay fp32 and are
         # folded into the mix kernel; g2 (and any quantised one) is a contraction
         fp32 = [r % block != 0 for r in (Rw, Ra, Rv)]

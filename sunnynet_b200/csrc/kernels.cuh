@@ -50,6 +50,10 @@ struct W4Problem {
 };
 int launch_w4a8_tc_group(const W4Problem* pr, int np, int M, int K, int block, bool fp16,
                          cudaStream_t st, bool pdl = false);
+// The same group on the SIMT W4A8 kernel, for nseq <= 8 (quant4.cu): one
+// launch, each CTA on one problem's rows.
+int launch_w4a8_group(const W4Problem* pr, int np, int nseq, int in, int block, bool fp16,
+                      cudaStream_t st, bool pdl = false);
 int launch_gemv_f32(float* y, const float* x, const float* W, int in, int out, cudaStream_t st);
 // out[b] = argmax of logits row b (lowest id on ties, NaN never chosen);
 // part holds B * kArgChunks float2 of scratch (argmax.cu).

@@ -14,6 +14,8 @@
 // (low nibble) | value k+block/2 (high nibble); scales (out, in/block) fp32
 // or fp16. A warp owns one output row per pass and streams it with 16-byte
 // loads; 16 code bytes = 32 weights = one dp4a pair per 4 bytes.
+#include <algorithm>
+
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -141,70 +143,130 @@ __device__ __forceinline__ void w4_store(float* y, float v, int epi) {
     }
 }
 
-// Fast path: block % 32 == 0 (whole 16-byte chunks per block half), in % 32 == 0.
-// Each warp takes one output row at a time; NS sequences share each weight load.
-template <bool FP16S>
-__global__ void __launch_bounds__(256)
-    w4a8_kernel(float* __restrict__ Y, const float* __restrict__ X, const uint8_t* __restrict__ Wq,
-                const void* __restrict__ scale, int nseq, int in, int out, int block, int epi) {
+// Fast path: block % 32 == 0 (whole 16-byte chunks per block half), in % 32 == 0,
+// in <= 1024 * NCH (a 16-byte chunk holds 32 codes; NCH chunk passes of 32
+// lanes per row). A warp takes kW4Rows output rows at a time
+// (rows gw, gw + nw, ...): the 16-byte weight chunks and block scales of all
+// of them are loaded before any is used, and the first group's before the
+// activations are quantised (they do not depend on the previous kernel), so
+// the weight stream has several rows in flight per warp. NS sequences share
+// each weight load. The per-row arithmetic is the reference's, in its order.
+constexpr int kW4Rows = 4;
+constexpr int kW4MaxProblems = 8;
+template <bool FP16S, int NCH>
+__device__ __forceinline__ void w4a8_rows(float* __restrict__ Y, const float* __restrict__ X,
+                                          const uint8_t* __restrict__ Wq,
+                                          const void* __restrict__ scale, int nseq, int in,
+                                          int out, int block, int epi, int gw, int nw) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int nb = in / block, half = block / 2, cpb = half / 16, cpr = in / 32;
+    const int nch = (cpr + 31) / 32;  // chunk passes per row (<= NCH)
     const int seq0 = blockIdx.y * kMaxSeqTile;
     const int ns = min(kMaxSeqTile, nseq - seq0);
     int8_t* xq = reinterpret_cast<int8_t*>(smem);
     float* xs = reinterpret_cast<float*>(smem + (size_t)kMaxSeqTile * in);
     int* xsum = reinterpret_cast<int*>(xs + kMaxSeqTile * nb);
     const int lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int nw = gridDim.x * (blockDim.x >> 5);
+    uint4 wr[kW4Rows][NCH];
+    float sw[kW4Rows][NCH];
+    auto load_rows = [&](int row0) {  // rows row0 + i*nw, i < kW4Rows
+#pragma unroll
+        for (int i = 0; i < kW4Rows; ++i) {
+            const int row = row0 + i * nw;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                const int ci = c * 32 + lane;
+                const bool live = c < nch && ci < cpr && row < out;
+                wr[i][c] = live ? __ldg(reinterpret_cast<const uint4*>(Wq + (size_t)row * (in / 2)) + ci)
+                                : make_uint4(0, 0, 0, 0);
+                sw[i][c] = live ? load_scale(scale, (size_t)row * nb + ci / cpb, FP16S) : 0.0f;
+            }
+        }
+    };
     pdl_trigger();
-    if (gw < out) {  // the warp's first weight row toward L2 while the previous kernel ends
-        const char* wr0 = reinterpret_cast<const char*>(Wq) + (size_t)gw * (in / 2);
-        for (int off = lane * 128; off < in / 2; off += 32 * 128) prefetch_l2(wr0 + off);
-    }
+    load_rows(gw);
     pdl_wait();  // no-op unless launched with programmatic serialization
     quant_act_smem(X + (size_t)seq0 * in, ns, in, block, nb, xq, xs, xsum);
     __syncthreads();
 
-    for (int row = gw; row < out; row += nw) {
-        const uint8_t* wr = Wq + (size_t)row * (in / 2);
-        float acc[kMaxSeqTile];
+    for (int row0 = gw; row0 < out; row0 += kW4Rows * nw) {
 #pragma unroll
-        for (int s = 0; s < kMaxSeqTile; ++s) acc[s] = 0.0f;
-        for (int c0 = 0; c0 < cpr; c0 += 32) {
-            const int ci = c0 + lane;
-            const bool live = ci < cpr;
-            const uint4 w = live ? __ldg(reinterpret_cast<const uint4*>(wr) + ci) : make_uint4(0, 0, 0, 0);
-            const int b = live ? ci / cpb : 0;
-            const int j = (ci % cpb) * 16;
-            const float sw = live ? load_scale(scale, (size_t)row * nb + b, FP16S) : 0.0f;
-            const int nblk = min(32, cpr - c0) / cpb;  // whole blocks in this pass
-            const int bfirst = c0 / cpb;
+        for (int i = 0; i < kW4Rows; ++i) {
+            const int row = row0 + i * nw;
+            if (row >= out) break;
+            float acc[kMaxSeqTile];
 #pragma unroll
-            for (int s = 0; s < kMaxSeqTile; ++s) {
-                if (s >= ns) break;
-                int d = live ? dot16(w, xq + (size_t)s * in + b * block + j,
-                                     xq + (size_t)s * in + b * block + half + j)
-                             : 0;
-                for (int o = 1; o < cpb; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                // sequential block-order accumulation (same value in every lane)
-                for (int k = 0; k < nblk; ++k) {
-                    const int dk = __shfl_sync(0xffffffffu, d, k * cpb);
-                    const float swk = __shfl_sync(0xffffffffu, sw, k * cpb);
-                    const int bk = bfirst + k;
-                    const float f = (float)(dk - 8 * xsum[s * nb + bk]);
-                    acc[s] = __fadd_rn(acc[s], __fmul_rn(__fmul_rn(swk, xs[s * nb + bk]), f));
+            for (int s = 0; s < kMaxSeqTile; ++s) acc[s] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < NCH; ++c) {
+                if (c >= nch) break;
+                const int c0 = c * 32, ci = c0 + lane;
+                const bool live = ci < cpr;
+                const uint4 w = wr[i][c];
+                const int b = live ? ci / cpb : 0;
+                const int j = (ci % cpb) * 16;
+                const int nblk = min(32, cpr - c0) / cpb;  // whole blocks in this pass
+                const int bfirst = c0 / cpb;
+#pragma unroll
+                for (int s = 0; s < kMaxSeqTile; ++s) {
+                    if (s >= ns) break;
+                    int d = live ? dot16(w, xq + (size_t)s * in + b * block + j,
+                                         xq + (size_t)s * in + b * block + half + j)
+                                 : 0;
+                    for (int o = 1; o < cpb; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                    // sequential block-order accumulation (same value in every lane)
+                    for (int k = 0; k < nblk; ++k) {
+                        const int dk = __shfl_sync(0xffffffffu, d, k * cpb);
+                        const float swk = __shfl_sync(0xffffffffu, sw[i][c], k * cpb);
+                        const int bk = bfirst + k;
+                        const float f = (float)(dk - 8 * xsum[s * nb + bk]);
+                        acc[s] = __fadd_rn(acc[s], __fmul_rn(__fmul_rn(swk, xs[s * nb + bk]), f));
+                    }
                 }
             }
-        }
-        if (lane < ns) {
-            float v = acc[0];
+            if (lane < ns) {
+                float v = acc[0];
 #pragma unroll
-            for (int s = 1; s < kMaxSeqTile; ++s)
-                if (lane == s) v = acc[s];
-            w4_store(Y + (size_t)(seq0 + lane) * out + row, v, epi);
+                for (int s = 1; s < kMaxSeqTile; ++s)
+                    if (lane == s) v = acc[s];
+                w4_store(Y + (size_t)(seq0 + lane) * out + row, v, epi);
+            }
         }
+        if (row0 + kW4Rows * nw < out) load_rows(row0 + kW4Rows * nw);
     }
+}
+
+template <bool FP16S, int NCH>
+__global__ void __launch_bounds__(256, NCH == 1 ? 4 : 2)
+    w4a8_kernel(float* __restrict__ Y, const float* __restrict__ X, const uint8_t* __restrict__ Wq,
+                const void* __restrict__ scale, int nseq, int in, int out, int block, int epi) {
+    w4a8_rows<FP16S, NCH>(Y, X, Wq, scale, nseq, in, out, block, epi,
+                          blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5),
+                          gridDim.x * (blockDim.x >> 5));
+}
+
+// Up to 8 contractions sharing the input width, block and scale type in one
+// launch (the first-stage projections of an RWKV-7 layer at small batch):
+// CTAs [cta0[p], cta0[p+1]) take problem p's rows, quantising only its input.
+struct W4SimtGroup {
+    float* Y[kW4MaxProblems];
+    const float* X[kW4MaxProblems];
+    const uint8_t* Wq[kW4MaxProblems];
+    const void* scale[kW4MaxProblems];
+    int N[kW4MaxProblems];
+    int epi[kW4MaxProblems];
+    int cta0[kW4MaxProblems + 1];
+    int np;
+};
+
+template <bool FP16S, int NCH>
+__global__ void __launch_bounds__(256, NCH == 1 ? 4 : 2)
+    w4a8_group_kernel(const __grid_constant__ W4SimtGroup g, int nseq, int in, int block) {
+    int p = 0;
+    while (p + 1 < g.np && (int)blockIdx.x >= g.cta0[p + 1]) ++p;
+    const int local = (int)blockIdx.x - g.cta0[p], nct = g.cta0[p + 1] - g.cta0[p];
+    w4a8_rows<FP16S, NCH>(g.Y[p], g.X[p], g.Wq[p], g.scale[p], nseq, in, g.N[p], block, g.epi[p],
+                          local * (blockDim.x >> 5) + (threadIdx.x >> 5), nct * (blockDim.x >> 5));
 }
 
 // General path (any even block dividing in): one lane per (row, block) dot,
@@ -283,15 +345,18 @@ int launch_w4a8(float* Y, const float* X, const uint8_t* Wq, const void* scale, 
     if (smem > 200 * 1024) return fail(SN_E_INVAL, "gemv_i4: in=%d too large", in);
     // whole 16-byte chunks per block half, and chunk groups that tile a warp
     const bool pow2 = block == 32 || block == 64 || block == 128 || block == 256;
-    const bool fast = pow2 && in % 32 == 0 && ((uintptr_t)Wq % 16 == 0);
+    const bool fast = pow2 && in % 32 == 0 && in <= 4096 && ((uintptr_t)Wq % 16 == 0);
+    const int nch = in <= 1024 ? 1 : (in <= 2048 ? 2 : 4);
     const int seq_tiles = (nseq + kMaxSeqTile - 1) / kMaxSeqTile;
     const int warps_needed = out;
     int ctas = (warps_needed + 7) / 8;
-    const int cap = 4 * rt().num_sms;
+    const int cap = 8 * rt().num_sms;  // 8 CTAs of 256 threads fit on an SM
     if (ctas > cap) ctas = cap;
     dim3 grid(ctas, seq_tiles);
     if (fast) {
-        auto k = fp16 ? w4a8_kernel<true> : w4a8_kernel<false>;
+        auto k = nch == 1 ? (fp16 ? w4a8_kernel<true, 1> : w4a8_kernel<false, 1>)
+                 : nch == 2 ? (fp16 ? w4a8_kernel<true, 2> : w4a8_kernel<false, 2>)
+                            : (fp16 ? w4a8_kernel<true, 4> : w4a8_kernel<false, 4>);
         if (smem > 48 * 1024)
             SN_TRY(cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    (int)smem), "w4a8 smem"));
@@ -307,6 +372,47 @@ int launch_w4a8(float* Y, const float* X, const uint8_t* Wq, const void* scale, 
                                         in, out, block, epi),
                           "w4a8 launch");
     }
+}
+
+int launch_w4a8_group(const W4Problem* pr, int np, int nseq, int in, int block, bool fp16,
+                      cudaStream_t st, bool pdl) {
+    if (np < 1 || np > kW4MaxProblems) return fail(SN_E_INVAL, "w4a8 group: %d problems", np);
+    if (nseq > kMaxSeqTile)  // one sequence tile per CTA in the grouped form
+        return fail(SN_E_INVAL, "w4a8 group: %d sequences (at most %d)", nseq, kMaxSeqTile);
+    const bool pow2 = block == 32 || block == 64 || block == 128 || block == 256;
+    if (!pow2 || in % 32 != 0 || in > 4096 || in % block != 0)
+        return fail(SN_E_INVAL, "w4a8 group: unsupported in=%d block=%d", in, block);
+    W4SimtGroup g;
+    g.np = np;
+    g.cta0[0] = 0;
+    long long rows = 0;
+    for (int i = 0; i < np; ++i) rows += pr[i].N;
+    const int budget = 8 * rt().num_sms;  // CTAs, shared out by rows
+    for (int i = 0; i < np; ++i) {
+        if ((uintptr_t)pr[i].Wq % 16) return fail(SN_E_INVAL, "w4a8 group: unaligned codes");
+        g.Y[i] = pr[i].Y;
+        g.X[i] = pr[i].X;
+        g.Wq[i] = pr[i].Wq;
+        g.scale[i] = pr[i].scale;
+        g.N[i] = pr[i].N;
+        g.epi[i] = pr[i].epi;
+        int c = (int)((long long)budget * pr[i].N / rows);
+        c = std::max(1, std::min(c, (pr[i].N + 7) / 8));
+        g.cta0[i + 1] = g.cta0[i] + c;
+    }
+    const int nb = in / block;
+    const size_t smem = (size_t)kMaxSeqTile * in + (size_t)kMaxSeqTile * nb * 8 + 16;
+    const int nch = in <= 1024 ? 1 : (in <= 2048 ? 2 : 4);
+    auto k = nch == 1 ? (fp16 ? w4a8_group_kernel<true, 1> : w4a8_group_kernel<false, 1>)
+             : nch == 2 ? (fp16 ? w4a8_group_kernel<true, 2> : w4a8_group_kernel<false, 2>)
+                        : (fp16 ? w4a8_group_kernel<true, 4> : w4a8_group_kernel<false, 4>);
+    if (smem > 48 * 1024)
+        SN_TRY(cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem),
+                          "w4a8 group smem"));
+    return cuda_check(launch_pdl_if(pdl, k, dim3(g.cta0[np]), dim3(256), smem, st, g, nseq, in,
+                                    block),
+                      "w4a8 group launch");
 }
 
 int launch_gemv_f32(float* y, const float* x, const float* W, int in, int out, cudaStream_t st) {

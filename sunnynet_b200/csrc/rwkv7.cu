@@ -638,13 +638,24 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
                 grouped = gm[i]->q4 && gm[i]->in == D && gm[i]->block == gm[0]->block &&
                           gm[i]->fp16 == gm[0]->fp16 &&
                           w4a8_tc_ok(B, gm[i]->in, gm[i]->out, gm[i]->block, gm[i]->q);
-            if (grouped) {
+            // small batches: the same group on the SIMT kernel
+            bool small = !grouped && B <= 8 && gm[0]->q4;
+            for (int i = 0; i < ng && small; ++i)
+                small = gm[i]->q4 && gm[i]->in == D && gm[i]->block == gm[0]->block &&
+                        gm[i]->fp16 == gm[0]->fp16 && (uintptr_t)gm[i]->q % 16 == 0;
+            small = small && D % 32 == 0 && D <= 4096 &&
+                    (gm[0]->block == 32 || gm[0]->block == 64 || gm[0]->block == 128 ||
+                     gm[0]->block == 256);
+            if (grouped || small) {
                 static const int map[] = {kW4Store, kW4Add, kW4Relu2, kW4Tanh, kW4Sigmoid};
                 W4Problem pr[7];
                 for (int i = 0; i < ng; ++i)
                     pr[i] = W4Problem{gy[i], gx[i], gm[i]->q, gm[i]->scale, gm[i]->out, map[ge[i]]};
                 ProfScope ps("w4a8_group", st);
-                SN_TRY(launch_w4a8_tc_group(pr, ng, B, D, gm[0]->block, gm[0]->fp16, st, true));
+                if (grouped)
+                    SN_TRY(launch_w4a8_tc_group(pr, ng, B, D, gm[0]->block, gm[0]->fp16, st, true));
+                else
+                    SN_TRY(launch_w4a8_group(pr, ng, B, D, gm[0]->block, gm[0]->fp16, st, true));
             } else {
                 for (int i = 0; i < ng; ++i) SN_TRY(mat_mul(*gm[i], gy[i], gx[i], B, ge[i], st));
             }

@@ -620,31 +620,50 @@ bool tc_usable(const GemmArgs& a, const TcWeights* tw) {
 
 namespace {
 
-// widest tile that still gives about a wave of CTAs
+// Tile width BN and K split ks from a cost model of this kernel, per CTA in
+// SM cycles (measured on B200 decode and prefill shapes): ~2400 to the first
+// K slab, then the slab bytes at ~45 B/cycle (the TMA rate of one SM:
+// 2 x 128 x 128 B of A planes + 128 B per weight row and plane), ~900 per 32
+// output columns of epilogue, ~4000 for a split's cluster reduction; times
+// the number of waves. Split K needs a 16-byte-friendly epilogue, BN <= 64
+// and >= 8 K slabs (two per CTA at least).
 int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
                  const CUtensorMap& tal, cudaStream_t st, bool pdl) {
     const long long mt = (a.M + BM - 1) / BM;
     const long long sms = rt().num_sms;
-    int bn = 32;
-    if (mt * ((a.N + 127) / 128) >= sms * 3 / 4) bn = 128;
-    else if (mt * ((a.N + 63) / 64) >= sms * 3 / 4) bn = 64;
-    // split K over a cluster while that still fits in one wave and leaves
-    // each CTA at least two slabs (few-tile contractions of batched decode)
-    const long long tiles = mt * ((a.N + bn - 1) / bn);
     const int nkt = (a.K + BK - 1) / BK;
-    // Split K pays for its cross-CTA reduction only with a long enough K loop
-    // (>= 8 slabs); the reduction works on 16-byte groups, so every operand
-    // it touches must allow that.
     auto al16 = [](const void* p, long long ld) {
         return p == nullptr || ((uintptr_t)p % 16 == 0 && ld % 4 == 0);
     };
     bool vec = a.N % 4 == 0 && al16(a.C, a.ldc) &&
                (a.Ch == nullptr || ((uintptr_t)a.Ch % 8 == 0 && (uintptr_t)a.Cl % 8 == 0));
     if (a.epi == kEpiResid) vec = vec && al16(a.S, a.lds) && al16(a.F, a.ldf) && al16(a.X, a.ldx);
-    int ks = 1;
-    if (!getenv("SN_TC_NO_SPLITK") && bn <= 64 && vec && nkt >= 8)
-        while (ks < 8 && tiles * ks * 2 <= sms && nkt >= ks * 4) ks *= 2;
+    const bool may_split = vec && nkt >= 8 && !getenv("SN_TC_NO_SPLITK");
     const bool ld = a.epi == kEpiResid || a.epi == kEpiAdd;
+    int bn = 32, ks = 1;
+    double best = 1e300;
+    // residual / accumulate epilogues stage only their first 32 columns of
+    // operands under the main loop (the rest load after it), which the model
+    // does not see: they keep BN = 32 unless that leaves most SMs idle
+    const int bld = mt * ((a.N + 127) / 128) >= sms * 3 / 4   ? 128
+                    : mt * ((a.N + 63) / 64) >= sms * 3 / 4 ? 64
+                                                            : 32;
+    for (int b : {32, 64, 128}) {
+        if (ld && b != bld) continue;
+        const long long tiles = mt * ((a.N + b - 1) / b);
+        const double slab = 2.0 * BM * 128 + (tw.int8 ? 1.0 : 2.0) * b * 128;
+        for (int k = 1; k <= 8; k *= 2) {
+            if (k > 1 && (!may_split || b > 64 || nkt < 2 * k || tiles * k > sms)) continue;
+            const long long waves = (tiles * k + sms - 1) / sms;
+            const double t = (double)waves * (2400.0 + ((nkt + k - 1) / k) * slab / 45.0 +
+                                              900.0 * b / 32 + (k > 1 ? 4000.0 : 0.0));
+            if (t < best * 0.98) {  // a wider or more split choice must win clearly
+                best = t;
+                bn = b;
+                ks = k;
+            }
+        }
+    }
 #define SN_TC_BN(I8, LD)                                                              \
     return bn == 128 ? launch_bn<128, I8, LD>(a, tw, tah, tal, st, pdl, ks)            \
                      : (bn == 64 ? launch_bn<64, I8, LD>(a, tw, tah, tal, st, pdl, ks) \
