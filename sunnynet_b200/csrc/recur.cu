@@ -23,11 +23,13 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 
 #include "kernels.cuh"
 #include "ptx.cuh"
 #include "recur.h"
 #include "runtime.cuh"
+#include "tcgen05.cuh"
 
 namespace sn {
 namespace {
@@ -329,24 +331,62 @@ __device__ __forceinline__ void stage_rows(float* sa, float* sb, const float* a,
     __syncthreads();
 }
 
+// The same staging by TMA, for full 128-channel tiles: boxes of 8 rows x 128
+// channels of a and b (tensor maps over the (B*T, N) arrays; rows or channels
+// past the end read as zero), issued by one thread, completing on `bar`.
+// Rows past the chunk's end (up to 7) are loaded and not used.
+constexpr int kBoxRows = 8;
+__device__ __forceinline__ void stage_rows_tma(float* sa, float* sb, const CUtensorMap* ta,
+                                               const CUtensorMap* tb, int row0, int rows, int n0,
+                                               uint64_t* bar, uint32_t& phase, int* err) {
+    if (threadIdx.x == 0) {
+        fence_proxy_async_smem();  // the generic reads of the last round come first
+        const int nbox = (rows + kBoxRows - 1) / kBoxRows;
+        mbar_expect_tx(bar, (uint32_t)(2 * nbox * kBoxRows * kScanTile * sizeof(float)));
+        for (int i = 0; i < nbox; ++i) {
+            tma_load_2d(sa + i * kBoxRows * kScanTile, ta, n0, row0 + i * kBoxRows, bar);
+            tma_load_2d(sb + i * kBoxRows * kScanTile, tb, n0, row0 + i * kBoxRows, bar);
+        }
+    }
+    mbar_wait(bar, phase, err);
+    phase ^= 1u;
+}
+
 __global__ void __launch_bounds__(256)
     scan_agg_kernel(const float* __restrict__ a, const float* __restrict__ b,
                     float2* __restrict__ agg, int T, int N, int nv, int L, int nch, int gated,
-                    int vec) {
-    extern __shared__ __align__(16) float stile[];
+                    int vec, const __grid_constant__ CUtensorMap ta,
+                    const __grid_constant__ CUtensorMap tb, int tma, int* err) {
+    extern __shared__ __align__(16) unsigned char stile_raw[];
+    __shared__ __align__(8) uint64_t bar;
     pdl_trigger();
     const int tpb = blockDim.x;
+    // 128-byte aligned staging area (TMA destinations)
+    float* stile = reinterpret_cast<float*>(
+        stile_raw + (((smem_u32(stile_raw) + 127u) & ~127u) - smem_u32(stile_raw)));
     float* sa = stile;
     float* sb = stile + kSub * tpb;
     const int n0 = blockIdx.x * tpb, n = n0 + threadIdx.x;
     const int c = blockIdx.y, sq = blockIdx.z;
     const int t0 = c * L, rows = min(L, T - t0);
     const bool fused = n < nv;
+    uint32_t phase = 0;
+    if (tma) {
+        if (threadIdx.x == 0) {
+            mbar_init(&bar, 1);
+            fence_mbar_init();
+        }
+        __syncthreads();
+    }
     float A = 1.0f, Bc = 0.0f;
     for (int r0 = 0; r0 < rows; r0 += kSub) {
         const int rs = min(kSub, rows - r0);
         if (r0) __syncthreads();  // the previous round is consumed
-        stage_rows(sa, sb, a, b, ((size_t)sq * T + t0 + r0) * N + n0, rs, N, n0, tpb, vec != 0);
+        if (tma)
+            stage_rows_tma(sa, sb, &ta, &tb, sq * T + t0 + r0, rs, n0, &bar, phase, err);
+        else
+            stage_rows(sa, sb, a, b, ((size_t)sq * T + t0 + r0) * N + n0, rs, N, n0, tpb,
+                       vec != 0);
         for (int r = 0; r < rs; ++r) {
             const float av = sa[r * tpb + threadIdx.x];
             const float bv = gate_b(av, sb[r * tpb + threadIdx.x], gated);
@@ -412,9 +452,14 @@ __global__ void __launch_bounds__(256)
     scan_apply_kernel(const float* __restrict__ a, const float* __restrict__ b,
                       const float2* __restrict__ agg, float* __restrict__ out,
                       float* __restrict__ send, int T, int N, int nv, int L, int nch, int gated,
-                      int vec) {
-    extern __shared__ __align__(16) float stile[];
+                      int vec, const __grid_constant__ CUtensorMap ta,
+                      const __grid_constant__ CUtensorMap tb, int tma, int* err) {
+    extern __shared__ __align__(16) unsigned char stile_raw[];
+    __shared__ __align__(8) uint64_t bar;
     const int tpb = blockDim.x;
+    // 128-byte aligned staging area (TMA destinations)
+    float* stile = reinterpret_cast<float*>(
+        stile_raw + (((smem_u32(stile_raw) + 127u) & ~127u) - smem_u32(stile_raw)));
     float* sa = stile;
     float* sb = stile + kSub * tpb;
     const int n0 = blockIdx.x * tpb, n = n0 + threadIdx.x;
@@ -422,16 +467,30 @@ __global__ void __launch_bounds__(256)
     const int t0 = c * L, rows = min(L, T - t0);
     const bool fused = n < nv;
     const size_t base = ((size_t)sq * T + t0) * N;
+    uint32_t phase = 0;
+    if (tma) {
+        if (threadIdx.x == 0) {
+            mbar_init(&bar, 1);
+            fence_mbar_init();
+        }
+        __syncthreads();
+    }
     // a and b were complete before the agg kernel started: stage the first
     // round while the carry kernel still runs, then wait for the carries
-    stage_rows(sa, sb, a, b, base + n0, min(kSub, rows), N, n0, tpb, vec != 0);
+    if (tma)
+        stage_rows_tma(sa, sb, &ta, &tb, sq * T + t0, min(kSub, rows), n0, &bar, phase, err);
+    else
+        stage_rows(sa, sb, a, b, base + n0, min(kSub, rows), N, n0, tpb, vec != 0);
     pdl_wait();
     float s = n < N ? __ldcg(&agg[((size_t)sq * nch + c) * N + n].x) : 0.0f;
     for (int r0 = 0; r0 < rows; r0 += kSub) {
         const int rs = min(kSub, rows - r0);
         if (r0) {
             __syncthreads();
-            stage_rows(sa, sb, a, b, base + (size_t)r0 * N + n0, rs, N, n0, tpb, vec != 0);
+            if (tma)
+                stage_rows_tma(sa, sb, &ta, &tb, sq * T + t0 + r0, rs, n0, &bar, phase, err);
+            else
+                stage_rows(sa, sb, a, b, base + (size_t)r0 * N + n0, rs, N, n0, tpb, vec != 0);
         }
         for (int r = 0; r < rs; ++r) {
             const float av = sa[r * tpb + threadIdx.x];
@@ -445,22 +504,33 @@ __global__ void __launch_bounds__(256)
 
 }  // namespace
 
-// Chunk length for mode 1: the shortest (16..256 rows) whose (seq, chunk,
-// channel) threads fit in one wave of 128-thread CTAs at 7 per SM, then
+// Chunk length for mode 1: the shortest (>= 16 rows) whose (seq, chunk,
+// channel tile) CTAs all fit in one wave at the agg / apply kernels' real
+// occupancy (a second, partial wave would cost as much as the first), then
 // longer until the records fit in `max_records` (<= 0: no limit). Returns 0
 // when even one chunk per sequence does not fit.
 int scan_chunk_rows(int B, int T, int N, int num_sms, long long max_records) {
-    const long long elems = (long long)B * T * N;
-    const long long want = (long long)num_sms * 7 * 128;
-    int L = 16;
-    while (L < 256 && elems / L > want) L *= 2;
+    const int tpb = N >= kScanTile ? kScanTile : ((N + 31) / 32) * 32;
+    const long long tiles = (long long)B * ((N + tpb - 1) / tpb);
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, scan_agg_kernel, tpb,
+                                                      2ull * kSub * tpb * sizeof(float) + 128) !=
+            cudaSuccess ||
+        occ < 1) {
+        cudaGetLastError();
+        occ = 6;
+    }
+    const long long slots = (long long)num_sms * occ;
+    long long L = ((long long)T * tiles + slots - 1) / slots;
+    L = (L + kBoxRows - 1) / kBoxRows * kBoxRows;  // whole TMA boxes
+    if (L < 16) L = 16;
     if (max_records > 0) {
         while ((long long)B * N * ((T + L - 1) / L) > max_records) {
             if (L >= T) return 0;
             L = L > T / 2 ? T : 2 * L;
         }
     }
-    return L < T ? L : T;
+    return (int)(L < T ? L : T);
 }
 
 long long scan_chunk_records(int B, int T, int N, int L) {
@@ -477,10 +547,23 @@ int launch_scan_chunked(const float* a, const float* b, const float* s0, float* 
     const int nv = N - N % 8;
     const int tpb = N >= kScanTile ? kScanTile : ((N + 31) / 32) * 32;
     const dim3 grid((N + tpb - 1) / tpb, nch, B);
-    const size_t smem = 2ull * kSub * tpb * sizeof(float);
+    const size_t smem = 2ull * kSub * tpb * sizeof(float) + 128;  // + alignment slack
     const int vec = N % 4 == 0 && (uintptr_t)a % 16 == 0 && (uintptr_t)b % 16 == 0;
+    // TMA staging for full 128-channel tiles (16-byte rows and bases)
+    CUtensorMap ta, tb;
+    memset(&ta, 0, sizeof ta);
+    memset(&tb, 0, sizeof tb);
+    int tma = vec && tpb == kScanTile && !getenv("SN_SCAN_NO_TMA");
+    if (tma) {
+        tma = encode_tiled(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a, N, (long long)B * T,
+                           (long long)N * 4, kScanTile, kBoxRows, CU_TENSOR_MAP_SWIZZLE_NONE) ==
+                  SN_OK &&
+              encode_tiled(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, b, N, (long long)B * T,
+                           (long long)N * 4, kScanTile, kBoxRows, CU_TENSOR_MAP_SWIZZLE_NONE) ==
+                  SN_OK;
+    }
     static const cudaError_t attr_rc = [] {  // once per process (thread-safe init)
-        const int mx = (int)(2ull * kSub * kScanTile * sizeof(float));
+        const int mx = (int)(2ull * kSub * kScanTile * sizeof(float) + 128);
         cudaError_t e = cudaFuncSetAttribute(scan_agg_kernel,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
         if (e == cudaSuccess)
@@ -491,7 +574,8 @@ int launch_scan_chunked(const float* a, const float* b, const float* s0, float* 
     SN_TRY(cuda_check(attr_rc, "scan smem attribute"));
     {
         ProfScope ps(prof_scopes ? "scan_agg" : nullptr, st);
-        scan_agg_kernel<<<grid, tpb, smem, st>>>(a, b, agg, T, N, nv, L, nch, gated, vec);
+        scan_agg_kernel<<<grid, tpb, smem, st>>>(a, b, agg, T, N, nv, L, nch, gated, vec, ta, tb,
+                                                 tma, rt().d_err);
         SN_TRY(cuda_check(cudaGetLastError(), "scan agg launch"));
     }
     {
@@ -504,7 +588,7 @@ int launch_scan_chunked(const float* a, const float* b, const float* s0, float* 
         ProfScope ps(prof_scopes ? "scan_apply" : nullptr, st);
         SN_TRY(cuda_check(launch_pdl(scan_apply_kernel, grid, dim3(tpb), smem, st, a, b,
                                      (const float2*)agg, out, send, T, N, nv, L, nch, gated,
-                                     vec),
+                                     vec, ta, tb, tma, rt().d_err),
                           "scan apply launch"));
     }
     return SN_OK;
