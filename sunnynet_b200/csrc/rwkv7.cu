@@ -226,6 +226,11 @@ __global__ void __launch_bounds__(256)
                     const float* __restrict__ lnw, const float* __restrict__ lnb,
                     float* __restrict__ y) {
     constexpr int HS = VPL * 32;
+    // warp w owns state rows w, w+8, ...; for heads up to 128 wide all of
+    // them are loaded at once, before anything else, so the state costs one
+    // memory round trip per warp instead of one per row
+    constexpr int RPW = HS / 8;
+    constexpr bool PRE = VPL <= 4;
     __shared__ float kn[HS], yv[HS], red[32];
     pdl_trigger();
     pdl_wait();  // no-op unless launched with programmatic serialization
@@ -233,6 +238,13 @@ __global__ void __launch_bounds__(256)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t o = (size_t)b * D + (size_t)h * HS;
     float* Sh = S + (((size_t)b * L + layer) * NH + h) * HS * HS;
+    float spre[PRE ? RPW : 1][VPL];
+    if (PRE) {
+#pragma unroll
+        for (int q = 0; q < (PRE ? RPW : 1); ++q)
+#pragma unroll
+            for (int t = 0; t < VPL; ++t) spre[q][t] = Sh[(size_t)(warp + 8 * q) * HS + lane + 32 * t];
+    }
     // kk normalised with floor 1e-12 (rwkv7.c:162-165)
     float ss = 0.0f;
     for (int j = threadIdx.x; j < HS; j += blockDim.x) ss += kk[o + j] * kk[o + j];
@@ -251,13 +263,15 @@ __global__ void __launch_bounds__(256)
         knj[t] = kn[j];
         kaj[t] = __fmul_rn(kn[j], a[o + j]);
     }
-    for (int i = warp; i < HS; i += 8) {
+#pragma unroll(PRE ? RPW : 1)
+    for (int q = 0; q < RPW; ++q) {
+        const int i = warp + 8 * q;
         float* row = Sh + (size_t)i * HS;
         float sv[VPL];
         float p = 0.0f;
 #pragma unroll
         for (int t = 0; t < VPL; ++t) {
-            sv[t] = row[lane + 32 * t];
+            sv[t] = PRE ? spre[PRE ? q : 0][t] : row[lane + 32 * t];
             p = fmaf(sv[t], knj[t], p);
         }
         for (int off = 16; off; off >>= 1) p += __shfl_xor_sync(0xffffffffu, p, off);
