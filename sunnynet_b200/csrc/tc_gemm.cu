@@ -43,7 +43,7 @@ struct TcCfg {
     static constexpr int A_BYTES = BM * 128;
     static constexpr int W_BYTES = BN * 128;
     static constexpr int STAGE = 2 * A_BYTES + 2 * W_BYTES;
-    static constexpr int S = BN == 128 ? 3 : (BN == 64 ? 4 : 5);
+    static constexpr int S = BN == 256 ? 2 : (BN == 128 ? 3 : (BN == 64 ? 4 : 5));
     // epilogue operands loaded under the main loop: [4 warps][32][33] floats
     static constexpr int PRE = 4 * 32 * 33 * 4;
     static constexpr int SMEM = S * STAGE + PRE + 1024 + 256;
@@ -514,7 +514,7 @@ int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
                           "tc smem"));
         attr = true;
     }
-    const int bi = BN == 32 ? 0 : (BN == 64 ? 1 : 2);
+    const int bi = BN == 32 ? 0 : (BN == 64 ? 1 : (BN == 128 ? 2 : 3));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(((a.N + BN - 1) / BN) * ks), (unsigned)((a.M + BM - 1) / BM));
     cfg.blockDim = dim3(kThreads);
@@ -596,8 +596,8 @@ int tc_prepare(TcWeights* tw, const void* W, int wtype, int N, int K,
     if (!tw->hi || (!tw->int8 && !tw->lo)) return fail(SN_E_NOMEM, "tc weight planes");
     split_bf16_kernel<<<grid_blocks((long long)n), 256>>>(W, wtype, (long long)n, tw->hi, tw->lo);
     SN_TRY(cuda_check(cudaGetLastError(), "split launch"));
-    const int rows[3] = {32, 64, 128};
-    for (int i = 0; i < 3; ++i) {
+    const int rows[4] = {32, 64, 128, 256};
+    for (int i = 0; i < 4; ++i) {
         SN_TRY(encode_map(&tw->tm_hi[i], tw->hi, N, K, rows[i]));
         SN_TRY(encode_map(&tw->tm_lo[i], tw->int8 ? tw->hi : tw->lo, N, K, rows[i]));
     }
@@ -645,10 +645,11 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
     // residual / accumulate epilogues stage only their first 32 columns of
     // operands under the main loop (the rest load after it), which the model
     // does not see: they keep BN = 32 unless that leaves most SMs idle
-    const int bld = mt * ((a.N + 127) / 128) >= sms * 3 / 4   ? 128
-                    : mt * ((a.N + 63) / 64) >= sms * 3 / 4 ? 64
-                                                            : 32;
-    for (int b : {32, 64, 128}) {
+    const int bld = mt * ((a.N + 255) / 256) >= sms * 3 / 4   ? 256
+                    : mt * ((a.N + 127) / 128) >= sms * 3 / 4 ? 128
+                    : mt * ((a.N + 63) / 64) >= sms * 3 / 4   ? 64
+                                                              : 32;
+    for (int b : {32, 64, 128, 256}) {
         if (ld && b != bld) continue;
         const long long tiles = mt * ((a.N + b - 1) / b);
         const double slab = 2.0 * BM * 128 + (tw.int8 ? 1.0 : 2.0) * b * 128;
@@ -664,10 +665,11 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
             }
         }
     }
-#define SN_TC_BN(I8, LD)                                                              \
-    return bn == 128 ? launch_bn<128, I8, LD>(a, tw, tah, tal, st, pdl, ks)            \
-                     : (bn == 64 ? launch_bn<64, I8, LD>(a, tw, tah, tal, st, pdl, ks) \
-                                 : launch_bn<32, I8, LD>(a, tw, tah, tal, st, pdl, ks))
+#define SN_TC_BN(I8, LD)                                                                  \
+    return bn == 256   ? launch_bn<256, I8, LD>(a, tw, tah, tal, st, pdl, ks)              \
+           : bn == 128 ? launch_bn<128, I8, LD>(a, tw, tah, tal, st, pdl, ks)              \
+                       : (bn == 64 ? launch_bn<64, I8, LD>(a, tw, tah, tal, st, pdl, ks)   \
+                                   : launch_bn<32, I8, LD>(a, tw, tah, tal, st, pdl, ks))
     if (tw.int8) {
         if (ld) SN_TC_BN(true, true);
         SN_TC_BN(true, false);

@@ -22,8 +22,8 @@ struct TcWeights {
     bool int8 = false;                 // hi holds the exact int8 codes; no lo plane
     __nv_bfloat16* hi = nullptr;
     __nv_bfloat16* lo = nullptr;
-    CUtensorMap tm_hi[3];              // box rows 32 / 64 / 128
-    CUtensorMap tm_lo[3];
+    CUtensorMap tm_hi[4];              // box rows 32 / 64 / 128 / 256
+    CUtensorMap tm_lo[4];
     bool ready = false;
 };
 

@@ -96,8 +96,7 @@ __device__ __forceinline__ float load_scale_w(const void* s, size_t i, bool fp16
 
 // Rows [mrow0, mrow0 + 32) x columns [n0, n0 + BN) of one tile from the
 // warp's staging area to Y with epilogue EPI; lane j stores columns j, j+32,
-// so each row is one coalesced segment. kW4Add loads all its old values
-// before any store.
+// so each row is one coalesced segment.
 template <int BN, int EPI>
 __device__ __forceinline__ void w4_store_rows(float* __restrict__ Y, int N, int M, int mrow0,
                                               int n0, const float* stg, int lane) {
@@ -105,28 +104,34 @@ __device__ __forceinline__ void w4_store_rows(float* __restrict__ Y, int N, int 
     for (int jj = 0; jj < BN / 32; ++jj) {
         const int j = jj * 32 + lane, n = n0 + j;
         if (n >= N) continue;
-        float old[32];
-        if (EPI == kW4Add) {
-#pragma unroll
-            for (int rr = 0; rr < 32; ++rr)
-                old[rr] = mrow0 + rr < M ? Y[(size_t)(mrow0 + rr) * N + n] : 0.0f;
-        }
-#pragma unroll
-        for (int rr = 0; rr < 32; ++rr) {
-            if (mrow0 + rr >= M) continue;
-            const float v = stg[rr * (BN + 1) + j];
-            float* y = Y + (size_t)(mrow0 + rr) * N + n;
+        // compact loop (runs once per tile, from a cold instruction cache);
+        // kW4Add reads 8 rows' old values before storing any of them
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 8) {
+            float old[8];
             if (EPI == kW4Add) {
-                *y = old[rr] + v;
-            } else if (EPI == kW4Relu2) {
-                const float t = v > 0.0f ? v : 0.0f;
-                *y = t * t;
-            } else if (EPI == kW4Tanh) {
-                *y = tanhf(v);
-            } else if (EPI == kW4Sigmoid) {
-                *y = 1.0f / (1.0f + expf(-v));
-            } else {
-                *y = v;
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    old[q] = mrow0 + r0 + q < M ? Y[(size_t)(mrow0 + r0 + q) * N + n] : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int rr = r0 + q;
+                if (mrow0 + rr >= M) continue;
+                const float v = stg[rr * (BN + 1) + j];
+                float* y = Y + (size_t)(mrow0 + rr) * N + n;
+                if (EPI == kW4Add) {
+                    *y = old[q] + v;
+                    } else if (EPI == kW4Relu2) {
+                    const float t = v > 0.0f ? v : 0.0f;
+                    *y = t * t;
+                } else if (EPI == kW4Tanh) {
+                    *y = tanhf(v);
+                } else if (EPI == kW4Sigmoid) {
+                    *y = 1.0f / (1.0f + expf(-v));
+                } else {
+                    *y = v;
+                }
             }
         }
     }
@@ -405,45 +410,115 @@ __global__ void __launch_bounds__(kW4Threads, 1)
 #pragma unroll
             for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
             bool ok = true;
-            for (int k = 0; k < nb; ++k, ++b) {
-                cp_async_wait_group<kScD - 1>();  // block k's group has landed
+            // block k of the tile from TMEM values d (block counter bb): the
+            // reference's ordered accumulation, then the slot is released
+            // block k's weight scales, as they arrived (fp16 in the aligned
+            // word that holds it, or fp32) -> fp32 in place: lane j converts
+            // column j once, instead of every lane converting every column
+            auto decode = [&](int k) {
+                uint32_t* sl = scr + (k % kScD) * (64 + BN);
+#pragma unroll
+                for (int jj = 0; jj < BN / 32; ++jj) {
+                    const int j = jj * 32 + lane;
+                    if (FP16S) {
+                        const uint32_t wd = sl[64 + j];
+                        const uintptr_t ea =
+                            reinterpret_cast<uintptr_t>(scale + 2 * ((size_t)(n0 + j) * nb + k));
+                        sl[64 + j] = __float_as_uint(__half2float(__ushort_as_half(
+                            (unsigned short)((ea & 2) ? (wd >> 16) : (wd & 0xFFFFu)))));
+                    }
+                }
                 __syncwarp();
+            };
+            auto consume = [&](const uint32_t* d, int k, int bb, int j0) {
                 const uint32_t* sl = scr + (k % kScD) * (64 + BN);
                 const float xs = __uint_as_float(sl[lane]);
                 const int x8 = 8 * (int)sl[32 + lane];
-                const int slot = b & 1;
-                ok = !*give_up && mbar_wait(&accf[slot], (b >> 1) & 1, err);
-                ok = __all_sync(0xffffffffu, ok);  // one decision per warp
-                if (!ok) {
-                    *give_up = 1;
-                    break;
-                }
-                tc_fence_after();
 #pragma unroll
-                for (int j0 = 0; j0 < BN; j0 += 32) {
-                    uint32_t d[32];
-                    tmem_ld32_u(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * BN + j0), d);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const uint32_t wd = sl[64 + j0 + j];  // same address in every lane
-                        float w;
-                        if (FP16S) {
-                            const uintptr_t ea = reinterpret_cast<uintptr_t>(
-                                scale + 2 * ((size_t)(n0 + j0 + j) * nb + k));
-                            w = __half2float(__ushort_as_half(
-                                (unsigned short)((ea & 2) ? (wd >> 16) : (wd & 0xFFFFu))));
-                        } else {
-                            w = __uint_as_float(wd);
-                        }
-                        const float f = (float)((int)d[j] - x8);
-                        acc[j0 + j] = __fadd_rn(acc[j0 + j], __fmul_rn(__fmul_rn(w, xs), f));
-                    }
+                for (int j = 0; j < 32; ++j) {
+                    const float w = __uint_as_float(sl[64 + j0 + j]);  // same address in every lane
+                    const float f = (float)((int)d[j] - x8);
+                    acc[j0 + j] = __fadd_rn(acc[j0 + j], __fmul_rn(__fmul_rn(w, xs), f));
                 }
+            };
+            auto wait_acc = [&](int bb) -> bool {  // one decision per warp
+                bool w = !*give_up && mbar_wait(&accf[bb & 1], (bb >> 1) & 1, err);
+                w = __all_sync(0xffffffffu, w);
+                if (!w) *give_up = 1;
+                return w;
+            };
+            auto release = [&](int k, int bb) {  // slot and scale ring entry done
                 tc_fence_before();
-                mbar_arrive(&acce[slot]);
-                __syncwarp();  // every lane is done with the slot before it is refilled
+                mbar_arrive(&acce[bb & 1]);
+                __syncwarp();  // every lane is done with the ring slot before it is refilled
                 if (k + kScD < nb) issue(k + kScD);
                 cp_async_commit();
+            };
+            const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+            if (BN == 32) {
+                // pipelined: block k+1's TMEM load is in flight while block k
+                // is applied (two register buffers, alternating)
+                uint32_t dA[32], dB[32];
+                int k = 0;
+                ok = wait_acc(b);
+                if (ok) {
+                    tc_fence_after();
+                    tmem_ld32_issue(trow + (uint32_t)((b & 1) * BN), dA);
+                    tmem_wait32(dA);
+                }
+                while (ok && k < nb) {
+                    bool more = k + 1 < nb;
+                    if (more) {
+                        ok = wait_acc(b + 1);
+                        if (ok) {
+                            tc_fence_after();
+                            tmem_ld32_issue(trow + (uint32_t)(((b + 1) & 1) * BN), dB);
+                        }
+                    }
+                    cp_async_wait_group<kScD - 1>();  // block k's scales have landed
+                    __syncwarp();
+                    decode(k);
+                    consume(dA, k, b, 0);
+                    release(k, b);
+                    ++k;
+                    ++b;
+                    if (!ok || !more) break;
+                    tmem_wait32(dB);
+                    more = k + 1 < nb;
+                    if (more) {
+                        ok = wait_acc(b + 1);
+                        if (ok) {
+                            tc_fence_after();
+                            tmem_ld32_issue(trow + (uint32_t)(((b + 1) & 1) * BN), dA);
+                        }
+                    }
+                    cp_async_wait_group<kScD - 1>();
+                    __syncwarp();
+                    decode(k);
+                    consume(dB, k, b, 0);
+                    release(k, b);
+                    ++k;
+                    ++b;
+                    if (!ok || !more) break;
+                    tmem_wait32(dA);
+                }
+                if (!ok) b += nb - k;  // keep the slot counter in step with the MMA side
+            } else {
+                for (int k = 0; k < nb; ++k, ++b) {
+                    cp_async_wait_group<kScD - 1>();  // block k's group has landed
+                    __syncwarp();
+                    decode(k);
+                    ok = wait_acc(b);
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int j0 = 0; j0 < BN; j0 += 32) {
+                        uint32_t d[32];
+                        tmem_ld32_u(trow + (uint32_t)((b & 1) * BN + j0), d);
+                        consume(d, k, b, j0);
+                    }
+                    release(k, b);
+                }
             }
             cp_async_wait_all();
             if (!ok) break;
