@@ -155,6 +155,16 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+// Barrier `id` (1..15) among `n` threads of the CTA (whole warps).
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// L2 prefetch of [p, p + bytes): p 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Arrive on `b` and add `bytes` to the transaction count its phase waits for.
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
@@ -170,6 +180,19 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
             "r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(b))
         : "memory");
+}
+
+// 1-D bulk copy of this CTA's shared memory -> global, in the thread's bulk
+// async-group; src, dst 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                 "r"(smem_u32(src)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk store of this thread has read its source.
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 // Order this thread's earlier generic-proxy shared-memory accesses (made

@@ -12,9 +12,13 @@
 //             .kind::f16 (M=128, N=BN, K=16): Ah*Wh + Ah*Wl + Al*Wh per K step
 //             (two products for INT8 weights, exact in bf16), tcgen05.commit
 //             frees the stage / signals the accumulator
-//     warps 2-5 epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes of
-//             quarter w%4), 32x32 blocks staged through shared memory so each
-//             global access is one 128-byte row segment, shared gemm_epilogue
+//     warps 2.. epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes of
+//             quarter w%4), each thread finishing its own output row (wide
+//             tiles: four warp groups share the 32-column blocks): rows
+//             staged in the drained ring (residual operands fetched there by
+//             bulk copies) and stored by one bulk copy per row; unaligned
+//             shapes stage 32x32 blocks so each global access is one 128-byte
+//             row segment; same arithmetic as gemm_epilogue
 // Every mbarrier wait is bounded; a role that gives up records the error,
 // drains its own in-flight TMA/MMA work, and the CTA frees its TMEM.
 #include <cuda.h>
@@ -36,7 +40,12 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // bf16 per slab row = 128 bytes
-constexpr int kThreads = 192;
+// Epilogue warps: group 0 (warps 2-5, one per TMEM lane quarter) runs every
+// epilogue; in the thread-per-row epilogues of wide tiles kEpiGroups groups
+// share the 32-column blocks, so the latency chains of several warps (IEEE
+// divides, tanh, exp) interleave on each scheduler.
+constexpr int kEpiGroups = 4;
+constexpr int kThreads = 64 + 128 * kEpiGroups;
 
 template <int BN>
 struct TcCfg {
@@ -46,7 +55,8 @@ struct TcCfg {
     static constexpr int S = BN == 256 ? 2 : (BN == 128 ? 3 : (BN == 64 ? 4 : 5));
     // epilogue operands loaded under the main loop: [4 warps][32][33] floats
     static constexpr int PRE = 4 * 32 * 33 * 4;
-    static constexpr int SMEM = S * STAGE + PRE + 1024 + 256;
+    // after the 256 bytes of barriers: the tile's per-column weight scales
+    static constexpr int SMEM = S * STAGE + PRE + 1024 + 256 + BN * 4;
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -133,6 +143,101 @@ __device__ __forceinline__ float tc_operand(const GemmArgs& a, long long mm, int
     if (mm >= a.M || n >= a.N) return 0.0f;
     return a.epi == kEpiResid ? a.p * a.S[mm * a.lds + n] + a.F[mm * a.ldf + n] + a.X[mm * a.ldx + n]
                               : a.C[mm * a.ldc + n];
+}
+
+// Rows [mr0, mr0 + 32) of column n's operand into pre_w[r * 33 + lane]. Loads
+// through GemmArgs' pointers may alias the generic shared-memory pointer, so
+// the compiler keeps each load after the previous store; sixteen rows are
+// loaded into registers before any is stored, so their round trips overlap.
+__device__ __forceinline__ void tc_block_operands(const GemmArgs& a, long long mr0, int n,
+                                                  float* pre_w, int lane) {
+#pragma unroll 1
+    for (int r0 = 0; r0 < 32; r0 += 16) {
+        float t[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) t[i] = tc_operand(a, mr0 + r0 + i, n);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pre_w[(r0 + i) * 33 + lane] = t[i];
+    }
+}
+
+// L2 prefetch hints for row mm's operand segment [n0, min(n0 + BN, N)): one
+// bulk prefetch per segment when rows are 16-byte aligned, else one hint per
+// 128-byte line, every address inside the matrix. Issued by the idle epilogue
+// threads under the main loop, so the epilogue's reads hit L2.
+template <int BN>
+__device__ __forceinline__ void tc_prefetch_row(const GemmArgs& a, long long mm, int n0, bool bulk) {
+    if (mm >= a.M || n0 >= a.N) return;
+    const int nl = (a.N - n0 < BN ? a.N - n0 : BN) - 1;  // last column offset
+    const float* rows[3];
+    int nr = 0;
+    if (a.epi == kEpiResid) {
+        rows[nr++] = a.S + mm * a.lds + n0;
+        rows[nr++] = a.F + mm * a.ldf + n0;
+        rows[nr++] = a.X + mm * a.ldx + n0;
+    } else {
+        rows[nr++] = a.C + mm * a.ldc + n0;
+    }
+    for (int i = 0; i < nr; ++i) {
+        if (bulk) {
+            bulk_prefetch_l2(rows[i], (uint32_t)(nl + 1) * 4u);
+        } else {
+            for (int c = 0; c < nl; c += 32) prefetch_l2(rows[i] + c);
+            prefetch_l2(rows[i] + nl);
+        }
+    }
+}
+
+// True when every operand row segment of the epilogue can move as one bulk
+// copy: 16-byte aligned bases, leading dimensions and widths (N % 4 == 0).
+__device__ __forceinline__ bool tc_rows_aligned(const GemmArgs& a) {
+    auto al = [](const float* p, long long ld) {
+        return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (ld & 3) == 0;
+    };
+    if ((a.N & 3) != 0) return false;
+    return a.epi == kEpiResid ? al(a.S, a.lds) && al(a.F, a.ldf) && al(a.X, a.ldx) : al(a.C, a.ldc);
+}
+
+// Thread-per-row epilogue of the accumulator-only kinds, one 32-column
+// block: v = 32 accumulator columns of this thread's row (as tcgen05.ld
+// hands them), ws = their weight scales (shared memory), the result into the
+// staged fp32 row `out` (16-byte aligned) and, with planes, the bf16 rows
+// hi / lo. Same arithmetic as tc_rows.
+template <int EPI>
+__device__ __forceinline__ void tc_row_block(const GemmArgs& a, const float* v, const float* ws,
+                                             float* out, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        float y[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float acc = v[j + i];
+            if (a.wscale) acc = acc * ws[j + i];
+            if (EPI == kEpiWedge) {
+                y[i] = acc * (1.0f + 0.5f * a.p / (1.0f + fabsf(acc)));
+            } else if (EPI == kEpiRelu2) {
+                const float t = acc > 0.0f ? acc : 0.0f;
+                y[i] = t * t;
+            } else if (EPI == kEpiTanh) {
+                y[i] = tanhf(acc);
+            } else if (EPI == kEpiSigmoid) {
+                y[i] = 1.0f / (1.0f + expf(-acc));
+            } else {
+                y[i] = acc;
+            }
+        }
+        *reinterpret_cast<float4*>(out + j) = make_float4(y[0], y[1], y[2], y[3]);
+        if (hi) {
+            __nv_bfloat16 h[4], l[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {  // store_split's rounding
+                h[i] = __float2bfloat16_rn(y[i]);
+                l[i] = __float2bfloat16_rn(y[i] - __bfloat162float(h[i]));
+            }
+            *reinterpret_cast<uint2*>(hi + j) = *reinterpret_cast<const uint2*>(h);
+            *reinterpret_cast<uint2*>(lo + j) = *reinterpret_cast<const uint2*>(l);
+        }
+    }
 }
 
 // Epilogue code runs once per launch, mostly from a cold instruction cache:
@@ -232,6 +337,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* acc_full = empty + S;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(acc_full + 1);
     volatile int* give_up = reinterpret_cast<volatile int*>(acc_full + 2);
+    uint64_t* op_full = acc_full + 3;  // [4]: a warp's epilogue operands landed
+    uint64_t* row_done = op_full + 4;  // [4]: the other groups' columns of a quarter's rows
+    float* wsc = reinterpret_cast<float*>(sb + S * C::STAGE + C::PRE + 256);  // [BN]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // split K: a cluster of ks CTAs along x shares one output tile, CTA kz of
@@ -252,6 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&empty[s], 1);
         }
         mbar_init(acc_full, 1);
+        for (int q = 0; q < 4; ++q) {
+            mbar_init(&op_full[q], 1);
+            mbar_init(&row_done[q], 32 * (kEpiGroups - 1));
+        }
         *give_up = 0;
         fence_mbar_init();
     }
@@ -328,11 +440,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc_commit(acc_full);  // accumulator complete (or: nothing left in flight)
         }
-    } else {  // ------------------------------------------------ epilogue (warps 2-5)
-        const int q = warp & 3;  // TMEM lane quarter this warp may read
+    } else {  // ------------------------------------------------ epilogue (warps 2..)
+        const int q = warp & 3;         // TMEM lane quarter this warp may read
+        const int g = (warp - 2) >> 2;  // column group
         const int et = threadIdx.x - 64;
         pdl_wait();  // the epilogue reads (and overwrites) the previous kernels' outputs
-        if (ks > 1) {
+        if (ks > 1 && g > 0) {
+            // split K: group 0 alone
+        } else if (ks > 1) {
             // split K: CTA kz owns rows [kz*rows, (kz+1)*rows) of the tile; its
             // residual / accumulate operands are loaded now, under the main loop
             const int rows = BM / ks;
@@ -357,15 +472,142 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         } else {
             // this warp's operands of a 32x32 block, [row][33] in shared memory
-            float* pre_w = pre_all + (warp - 2) * (32 * 33);
-            if (LOADS && BN == 32) {  // the only block's operands, under the main loop
-#pragma unroll 8
-                for (int r = 0; r < 32; ++r)
-                    pre_w[r * 33 + lane] = tc_operand(a, m0 + q * 32 + r, n0 + lane);
+            // (group 0)
+            float* pre_w = pre_all + ((warp - 2) & 3) * (32 * 33);
+            // Wide residual / accumulate tiles whose operand rows fit the drained
+            // ring (plus the operand area after it) go through it whole: rows
+            // [array][row][BN + 4] floats, fetched by bulk copies once the last
+            // MMA has completed; each thread then finishes its own row (the 32
+            // accumulator columns tcgen05.ld hands it) with conflict-free float4
+            // accesses and stores the row back by one bulk copy.
+            constexpr int RS = BN + 4;  // padded row stride: 16-byte bank groups differ per row
+            constexpr bool kRing = LOADS && BN > 32 && 3 * BM * RS * 4 <= S * C::STAGE + C::PRE;
+            const bool out_al = (reinterpret_cast<uintptr_t>(a.C) & 15) == 0 && (a.ldc & 3) == 0 &&
+                                (a.N & 3) == 0;
+            const bool ring = kRing && tc_rows_aligned(a) && a.Ch == nullptr && out_al;
+            // Other wide tiles finish rows the same way when their results can
+            // leave by bulk copies: fp32 rows [128][RS] at the ring start, the
+            // bf16 planes' rows [2][128][RSH] after them. 32-column tiles keep
+            // the staged blocks: rows of 128 bytes (64 for a plane) are too short
+            // for one bulk copy each to beat coalesced warp stores.
+            constexpr int RSH = BN + 8;
+            constexpr bool kPlanesFit = BM * RS * 4 + 2 * BM * RSH * 2 <= S * C::STAGE;
+            const bool planes_al = a.Ch != nullptr && kPlanesFit &&
+                                   (reinterpret_cast<uintptr_t>(a.Ch) & 15) == 0 &&
+                                   (reinterpret_cast<uintptr_t>(a.Cl) & 15) == 0 &&
+                                   (a.ldc & 7) == 0 && (a.N & 7) == 0;
+            const bool rows = !LOADS && BN > 32 && out_al && (a.Ch == nullptr || planes_al);
+            if (LOADS && BN == 32 && g == 0)  // the only block's operands, under the main loop
+                tc_block_operands(a, m0 + q * 32, n0 + lane, pre_w, lane);
+            if (LOADS && BN > 32 && g == 0)  // the other blocks' operands into L2 meanwhile
+                tc_prefetch_row<BN>(a, m0 + et, n0, ring);
+            if (a.wscale) {  // the tile's column scales, read from shared memory below
+                for (int c = et; c < BN; c += 128 * kEpiGroups)
+                    wsc[c] = n0 + c < a.N ? a.wscale[n0 + c] : 1.0f;
+                named_bar_sync(1, 128 * kEpiGroups);  // every epilogue warp
             }
-            const bool ok = mbar_wait(acc_full, 0, err);
+            bool ok = mbar_wait(acc_full, 0, err);
             tc_fence_after();
-            if (ok && !*give_up) {
+            const int row = q * 32 + lane;  // TMEM lane = tile row of this thread
+            const long long mm = m0 + row;
+            const int nc = a.N - n0 < BN ? a.N - n0 : BN;
+            float* orow = reinterpret_cast<float*>(sb) + row * RS;
+            // Rows are finished by all groups, one 32-column block in kEpiGroups
+            // each; group 0 then stores them once every group has arrived on
+            // the quarter's row_done barrier (after its proxy fence).
+            auto rows_finished = [&]() -> bool {
+                fence_proxy_async_smem();
+                if (kEpiGroups == 1) return true;
+                if (g > 0) {
+                    mbar_arrive(&row_done[q]);
+                    return false;
+                }
+                return mbar_wait(&row_done[q], 0, err);
+            };
+            if (kRing && ring) {
+                const bool resid = a.epi == kEpiResid;
+                if (g == 0 && ok && !*give_up) {
+                    // every MMA has completed, so no stage of the ring is still read
+                    const int left = a.M - (m0 + q * 32);  // this warp's rows inside the matrix
+                    const int nr = left < 0 ? 0 : (left < 32 ? left : 32);
+                    if (lane == 0)
+                        mbar_expect_tx(&op_full[q], (uint32_t)(nr * nc * 4 * (resid ? 3 : 1)));
+                    __syncwarp();
+                    if (mm < a.M) {
+                        if (resid) {
+                            bulk_g2s(orow, a.S + mm * a.lds + n0, nc * 4, &op_full[q]);
+                            bulk_g2s(orow + BM * RS, a.F + mm * a.ldf + n0, nc * 4, &op_full[q]);
+                            bulk_g2s(orow + 2 * BM * RS, a.X + mm * a.ldx + n0, nc * 4, &op_full[q]);
+                        } else {
+                            bulk_g2s(orow, a.C + mm * a.ldc + n0, nc * 4, &op_full[q]);
+                        }
+                    }
+                }
+                if (ok && !*give_up) ok = mbar_wait(&op_full[q], 0, err);
+                if (ok && !*give_up) {
+#pragma unroll 1
+                    for (int j0 = g * 32; j0 < BN; j0 += 32 * kEpiGroups) {
+                        float v[32];
+                        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)j0, v);
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4* o = reinterpret_cast<float4*>(orow + j0 + j);
+                            const float4 s4 = o[0];
+                            float y[4] = {v[j], v[j + 1], v[j + 2], v[j + 3]};
+                            float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+                            float fv[4] = {0.0f, 0.0f, 0.0f, 0.0f}, xv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                            if (resid) {
+                                const float4 f4 = o[BM * RS / 4], x4 = o[2 * BM * RS / 4];
+                                fv[0] = f4.x, fv[1] = f4.y, fv[2] = f4.z, fv[3] = f4.w;
+                                xv[0] = x4.x, xv[1] = x4.y, xv[2] = x4.z, xv[3] = x4.w;
+                            }
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                if (a.wscale) y[i] = y[i] * wsc[j0 + j + i];
+                                // same arithmetic as tc_operand and the staged path
+                                if (resid) y[i] = y[i] + (a.p * sv[i] + fv[i] + xv[i]);
+                                else y[i] = sv[i] + y[i];
+                            }
+                            o[0] = make_float4(y[0], y[1], y[2], y[3]);
+                        }
+                    }
+                }
+                if (rows_finished() && ok && !*give_up && mm < a.M) {
+                    bulk_s2g(a.C + mm * a.ldc + n0, orow, nc * 4);  // the finished row
+                    bulk_commit();
+                    bulk_wait_read_all();  // the ring stays valid until read
+                }
+            } else if (rows) {
+                __nv_bfloat16* hrow =
+                    a.Ch ? reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<float*>(sb) + BM * RS) +
+                               row * RSH
+                         : nullptr;
+                __nv_bfloat16* lrow = a.Ch ? hrow + BM * RSH : nullptr;
+#pragma unroll 1
+                for (int j0 = g * 32; ok && !*give_up && j0 < BN; j0 += 32 * kEpiGroups) {
+                    float v[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)j0, v);
+                    __nv_bfloat16* h = hrow ? hrow + j0 : nullptr;
+                    __nv_bfloat16* l = lrow ? lrow + j0 : nullptr;
+                    float* out = orow + j0;
+                    switch (a.epi) {
+                        case kEpiWedge: tc_row_block<kEpiWedge>(a, v, wsc + j0, out, h, l); break;
+                        case kEpiRelu2: tc_row_block<kEpiRelu2>(a, v, wsc + j0, out, h, l); break;
+                        case kEpiTanh: tc_row_block<kEpiTanh>(a, v, wsc + j0, out, h, l); break;
+                        case kEpiSigmoid: tc_row_block<kEpiSigmoid>(a, v, wsc + j0, out, h, l); break;
+                        default: tc_row_block<kEpiNone>(a, v, wsc + j0, out, h, l);
+                    }
+                }
+                if (rows_finished() && ok && !*give_up && mm < a.M) {  // the finished row
+                    bulk_s2g(a.C + mm * a.ldc + n0, orow, nc * 4);
+                    if (a.Ch) {
+                        bulk_s2g(reinterpret_cast<__nv_bfloat16*>(a.Ch) + mm * a.ldc + n0, hrow, nc * 2);
+                        bulk_s2g(reinterpret_cast<__nv_bfloat16*>(a.Cl) + mm * a.ldc + n0, lrow, nc * 2);
+                    }
+                    bulk_commit();
+                    bulk_wait_read_all();  // the ring stays valid until read
+                }
+            } else if (g == 0 && ok && !*give_up) {
                 // 32x32 blocks go through shared memory (the drained ring) so that a
                 // warp touches one 128-byte row segment per global access
                 float* stg = reinterpret_cast<float*>(sb) + (warp - 2) * (32 * 33);
@@ -390,24 +632,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                             default: tc_rows<kEpiNone>(a, mr0, n, nok, ws, stg, lane);
                         }
                     } else {
-                        if (BN > 32) {  // wider tiles: this block's operands now
-#pragma unroll 8
-                            for (int r = 0; r < 32; ++r)
-                                pre_w[r * 33 + lane] = tc_operand(a, m0 + q * 32 + r, n);
-                        }
+                        if (BN > 32)  // wider tiles: this block's operands now
+                            tc_block_operands(a, m0 + q * 32, n, pre_w, lane);
                         const float ws = a.wscale && nok ? a.wscale[n] : 1.0f;
 #pragma unroll 4
                         for (int r = 0; r < 32; ++r) {
-                            const long long mm = m0 + q * 32 + r;
-                            if (mm < a.M && nok) {
+                            const long long mr = m0 + q * 32 + r;
+                            if (mr < a.M && nok) {
                                 float acc = stg[r * 33 + lane];
                                 if (a.wscale) acc = acc * ws;
                                 const float pr = pre_w[r * 33 + lane];
                                 const float y = a.epi == kEpiResid ? acc + pr : pr + acc;
-                                a.C[mm * a.ldc + n] = y;
+                                a.C[mr * a.ldc + n] = y;
                                 if (a.Ch)
                                     store_split((__nv_bfloat16*)a.Ch, (__nv_bfloat16*)a.Cl,
-                                                mm * a.ldc + n, y);
+                                                mr * a.ldc + n, y);
                             }
                         }
                     }
@@ -430,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // tile, summing the cluster's partials in rank order (results do not
         // depend on timing); no CTA leaves while its partials may be read.
         cluster_sync();
-        if (warp >= 2) {
+        if (warp >= 2 && warp < 6) {  // epilogue group 0
             const int et = threadIdx.x - 64, rows = BM / ks, r0 = kz * rows;
             const float* part = reinterpret_cast<const float*>(sb);
             switch (a.epi) {
@@ -640,24 +879,30 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
     if (a.epi == kEpiResid) vec = vec && al16(a.S, a.lds) && al16(a.F, a.ldf) && al16(a.X, a.ldx);
     const bool may_split = vec && nkt >= 8 && !getenv("SN_TC_NO_SPLITK");
     const bool ld = a.epi == kEpiResid || a.epi == kEpiAdd;
-    int bn = 32, ks = 1;
-    double best = 1e300;
-    // residual / accumulate epilogues stage only their first 32 columns of
-    // operands under the main loop (the rest load after it), which the model
-    // does not see: they keep BN = 32 unless that leaves most SMs idle
+    // residual / accumulate tiles of 64 or 128 columns fetch their operand
+    // rows into the drained ring by bulk copies (all of a tile's at once,
+    // ~48 B/cycle) when rows are 16-byte aligned and no bf16 planes are
+    // written; otherwise wide tiles load them block by block after the main
+    // loop, which the model does not see: those keep BN = 32 unless that
+    // leaves most SMs idle
+    const bool ring = ld && vec && a.Ch == nullptr;
+    const int narr = a.epi == kEpiResid ? 3 : 1;
     const int bld = mt * ((a.N + 255) / 256) >= sms * 3 / 4   ? 256
                     : mt * ((a.N + 127) / 128) >= sms * 3 / 4 ? 128
                     : mt * ((a.N + 63) / 64) >= sms * 3 / 4   ? 64
                                                               : 32;
+    int bn = 32, ks = 1;
+    double best = 1e300;
     for (int b : {32, 64, 128, 256}) {
-        if (ld && b != bld) continue;
+        if (ld && (ring ? b > 128 : b != bld)) continue;
         const long long tiles = mt * ((a.N + b - 1) / b);
         const double slab = 2.0 * BM * 128 + (tw.int8 ? 1.0 : 2.0) * b * 128;
+        const double fetch = ring && b > 32 ? narr * BM * b * 4.0 / 48.0 : 0.0;
         for (int k = 1; k <= 8; k *= 2) {
             if (k > 1 && (!may_split || b > 64 || nkt < 2 * k || tiles * k > sms)) continue;
             const long long waves = (tiles * k + sms - 1) / sms;
             const double t = (double)waves * (2400.0 + ((nkt + k - 1) / k) * slab / 45.0 +
-                                              900.0 * b / 32 + (k > 1 ? 4000.0 : 0.0));
+                                              900.0 * b / 32 + (k > 1 ? 4000.0 : fetch));
             if (t < best * 0.98) {  // a wider or more split choice must win clearly
                 best = t;
                 bn = b;
