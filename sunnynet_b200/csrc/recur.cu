@@ -291,9 +291,10 @@ int launch_scan(const float* a, const float* b, const float* s0, float* out, flo
 // outputs differ from the sequential scan by rounding of that composition
 // (a few ulp of the state per chunk boundary), not bit for bit.
 // Record layout: agg[(seq*nch + c)*N + n] = float2 (A or carry, B).
-// The agg and apply kernels stage their tile (up to kSub rows of the CTA's
-// channels, a and b) in shared memory with cp.async, so a CTA has its whole
-// tile in flight at once instead of a few rows per thread.
+// The agg and apply kernels stage their tile (rows of the CTA's channels, a
+// and b) in shared memory, by TMA for full 128-channel tiles (two buffers in
+// flight, results stored back by bulk copies) and by cp.async otherwise, so
+// a CTA has whole rounds of rows in flight instead of a few rows per thread.
 namespace {
 
 constexpr int kSub = 32;        // rows staged per round
@@ -331,25 +332,34 @@ __device__ __forceinline__ void stage_rows(float* sa, float* sb, const float* a,
     __syncthreads();
 }
 
-// The same staging by TMA, for full 128-channel tiles: boxes of 8 rows x 128
-// channels of a and b (tensor maps over the (B*T, N) arrays; rows or channels
-// past the end read as zero), issued by one thread, completing on `bar`.
-// Rows past the chunk's end (up to 7) are loaded and not used.
+// Full 128-channel tiles are staged by TMA instead: boxes of 8 rows x 128
+// channels of a and b (tensor maps over the (B*T, N) arrays; rows or
+// channels past the end read as zero), issued by one thread. Rows past the
+// chunk's end (up to 7) are loaded and not used.
 constexpr int kBoxRows = 8;
-__device__ __forceinline__ void stage_rows_tma(float* sa, float* sb, const CUtensorMap* ta,
-                                               const CUtensorMap* tb, int row0, int rows, int n0,
-                                               uint64_t* bar, uint32_t& phase, int* err) {
-    if (threadIdx.x == 0) {
-        fence_proxy_async_smem();  // the generic reads of the last round come first
-        const int nbox = (rows + kBoxRows - 1) / kBoxRows;
-        mbar_expect_tx(bar, (uint32_t)(2 * nbox * kBoxRows * kScanTile * sizeof(float)));
-        for (int i = 0; i < nbox; ++i) {
-            tma_load_2d(sa + i * kBoxRows * kScanTile, ta, n0, row0 + i * kBoxRows, bar);
-            tma_load_2d(sb + i * kBoxRows * kScanTile, tb, n0, row0 + i * kBoxRows, bar);
-        }
+
+// Full 128-channel tiles by TMA run as a two-buffer pipeline: rounds of
+// kRound rows (a then b), round k in buffer k & 1 with its own mbarrier, so
+// round k + 1 lands while round k is consumed; the apply kernel writes its
+// results over the consumed a rows and stores each row by one bulk copy.
+// Both buffers together take the same 32 KB as the kSub staging area.
+constexpr int kRound = 16;
+constexpr int kBufF = 2 * kRound * kScanTile;  // floats per buffer
+static_assert(2 * kBufF == 2 * kSub * kScanTile, "pipeline buffers share the staging area");
+
+// One thread: issue round rows [row0, row0 + min(kRound, left)) of tile n0
+// into buffer `buf`, completing on `bar`.
+__device__ __forceinline__ void issue_round(float* buf, const CUtensorMap* ta,
+                                            const CUtensorMap* tb, int row0, int left, int n0,
+                                            uint64_t* bar) {
+    fence_proxy_async_smem();  // the generic accesses of the buffer's last round come first
+    const int nbox = ((left < kRound ? left : kRound) + kBoxRows - 1) / kBoxRows;
+    mbar_expect_tx(bar, (uint32_t)(2 * nbox * kBoxRows * kScanTile * sizeof(float)));
+    for (int i = 0; i < nbox; ++i) {
+        tma_load_2d(buf + i * kBoxRows * kScanTile, ta, n0, row0 + i * kBoxRows, bar);
+        tma_load_2d(buf + kRound * kScanTile + i * kBoxRows * kScanTile, tb, n0,
+                    row0 + i * kBoxRows, bar);
     }
-    mbar_wait(bar, phase, err);
-    phase ^= 1u;
 }
 
 __global__ void __launch_bounds__(256)
@@ -358,7 +368,7 @@ __global__ void __launch_bounds__(256)
                     int vec, const __grid_constant__ CUtensorMap ta,
                     const __grid_constant__ CUtensorMap tb, int tma, int* err) {
     extern __shared__ __align__(16) unsigned char stile_raw[];
-    __shared__ __align__(8) uint64_t bar;
+    __shared__ __align__(8) uint64_t bars[2];
     pdl_trigger();
     const int tpb = blockDim.x;
     // 128-byte aligned staging area (TMA destinations)
@@ -370,28 +380,47 @@ __global__ void __launch_bounds__(256)
     const int c = blockIdx.y, sq = blockIdx.z;
     const int t0 = c * L, rows = min(L, T - t0);
     const bool fused = n < nv;
-    uint32_t phase = 0;
-    if (tma) {
-        if (threadIdx.x == 0) {
-            mbar_init(&bar, 1);
-            fence_mbar_init();
-        }
-        __syncthreads();
-    }
     float A = 1.0f, Bc = 0.0f;
-    for (int r0 = 0; r0 < rows; r0 += kSub) {
-        const int rs = min(kSub, rows - r0);
-        if (r0) __syncthreads();  // the previous round is consumed
-        if (tma)
-            stage_rows_tma(sa, sb, &ta, &tb, sq * T + t0 + r0, rs, n0, &bar, phase, err);
-        else
+    if (tma) {
+        const int nr = (rows + kRound - 1) / kRound;
+        if (threadIdx.x == 0) {
+            mbar_init(&bars[0], 1);
+            mbar_init(&bars[1], 1);
+            fence_mbar_init();
+            for (int k = 0; k < 2 && k < nr; ++k)
+                issue_round(stile + k * kBufF, &ta, &tb, sq * T + t0 + k * kRound,
+                            rows - k * kRound, n0, &bars[k]);
+        }
+        __syncthreads();  // barriers initialised before anyone waits
+        for (int k = 0; k < nr; ++k) {
+            const int j = k & 1;
+            mbar_wait(&bars[j], (uint32_t)((k >> 1) & 1), err);
+            const float* ra = stile + j * kBufF;
+            const float* rb = ra + kRound * kScanTile;
+            const int rs = min(kRound, rows - k * kRound);
+            for (int r = 0; r < rs; ++r) {
+                const float av = ra[r * kScanTile + threadIdx.x];
+                const float bv = gate_b(av, rb[r * kScanTile + threadIdx.x], gated);
+                Bc = fused ? rec_fused(av, Bc, bv) : rec_split(av, Bc, bv);
+                A = __fmul_rn(A, av);
+            }
+            __syncthreads();  // buffer j consumed
+            if (threadIdx.x == 0 && k + 2 < nr)
+                issue_round(stile + j * kBufF, &ta, &tb, sq * T + t0 + (k + 2) * kRound,
+                            rows - (k + 2) * kRound, n0, &bars[j]);
+        }
+    } else {
+        for (int r0 = 0; r0 < rows; r0 += kSub) {
+            const int rs = min(kSub, rows - r0);
+            if (r0) __syncthreads();  // the previous round is consumed
             stage_rows(sa, sb, a, b, ((size_t)sq * T + t0 + r0) * N + n0, rs, N, n0, tpb,
                        vec != 0);
-        for (int r = 0; r < rs; ++r) {
-            const float av = sa[r * tpb + threadIdx.x];
-            const float bv = gate_b(av, sb[r * tpb + threadIdx.x], gated);
-            Bc = fused ? rec_fused(av, Bc, bv) : rec_split(av, Bc, bv);
-            A = __fmul_rn(A, av);
+            for (int r = 0; r < rs; ++r) {
+                const float av = sa[r * tpb + threadIdx.x];
+                const float bv = gate_b(av, sb[r * tpb + threadIdx.x], gated);
+                Bc = fused ? rec_fused(av, Bc, bv) : rec_split(av, Bc, bv);
+                A = __fmul_rn(A, av);
+            }
         }
     }
     if (n < N) agg[((size_t)sq * nch + c) * N + n] = make_float2(A, Bc);
@@ -455,7 +484,7 @@ __global__ void __launch_bounds__(256)
                       int vec, const __grid_constant__ CUtensorMap ta,
                       const __grid_constant__ CUtensorMap tb, int tma, int* err) {
     extern __shared__ __align__(16) unsigned char stile_raw[];
-    __shared__ __align__(8) uint64_t bar;
+    __shared__ __align__(8) uint64_t bars[2];
     const int tpb = blockDim.x;
     // 128-byte aligned staging area (TMA destinations)
     float* stile = reinterpret_cast<float*>(
@@ -467,36 +496,70 @@ __global__ void __launch_bounds__(256)
     const int t0 = c * L, rows = min(L, T - t0);
     const bool fused = n < nv;
     const size_t base = ((size_t)sq * T + t0) * N;
-    uint32_t phase = 0;
+    float s = 0.0f;
     if (tma) {
+        const int nr = (rows + kRound - 1) / kRound;
+        // results go back over the consumed a rows, out by one bulk copy per row
+        const bool bulk_out = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+        const int nval = N - n0 < kScanTile ? N - n0 : kScanTile;  // channels of this tile
+        // a and b were complete before the agg kernel started: stage the first
+        // rounds while the carry kernel still runs, then wait for the carries
         if (threadIdx.x == 0) {
-            mbar_init(&bar, 1);
+            mbar_init(&bars[0], 1);
+            mbar_init(&bars[1], 1);
             fence_mbar_init();
+            for (int k = 0; k < 2 && k < nr; ++k)
+                issue_round(stile + k * kBufF, &ta, &tb, sq * T + t0 + k * kRound,
+                            rows - k * kRound, n0, &bars[k]);
         }
-        __syncthreads();
-    }
-    // a and b were complete before the agg kernel started: stage the first
-    // round while the carry kernel still runs, then wait for the carries
-    if (tma)
-        stage_rows_tma(sa, sb, &ta, &tb, sq * T + t0, min(kSub, rows), n0, &bar, phase, err);
-    else
+        __syncthreads();  // barriers initialised before anyone waits
+        pdl_wait();
+        s = n < N ? __ldcg(&agg[((size_t)sq * nch + c) * N + n].x) : 0.0f;
+        for (int k = 0; k < nr; ++k) {
+            const int j = k & 1;
+            mbar_wait(&bars[j], (uint32_t)((k >> 1) & 1), err);
+            float* ra = stile + j * kBufF;
+            const float* rb = ra + kRound * kScanTile;
+            const int rs = min(kRound, rows - k * kRound);
+            const size_t rbase = base + (size_t)(k * kRound) * N;
+            for (int r = 0; r < rs; ++r) {
+                const float av = ra[r * kScanTile + threadIdx.x];
+                const float bv = gate_b(av, rb[r * kScanTile + threadIdx.x], gated);
+                s = fused ? rec_fused(av, s, bv) : rec_split(av, s, bv);
+                if (bulk_out) ra[r * kScanTile + threadIdx.x] = s;
+                else if (n < N) __stcs(out + rbase + (size_t)r * N + n, s);
+            }
+            if (bulk_out) {
+                fence_proxy_async_smem();
+                __syncthreads();  // the round's rows are complete
+                if (threadIdx.x < rs) {
+                    bulk_s2g(out + rbase + (size_t)threadIdx.x * N + n0,
+                             ra + threadIdx.x * kScanTile, (uint32_t)nval * 4u);
+                    bulk_commit();
+                    bulk_wait_read_all();  // the buffer is reloaded below
+                }
+            }
+            __syncthreads();  // buffer j consumed
+            if (threadIdx.x == 0 && k + 2 < nr)
+                issue_round(stile + j * kBufF, &ta, &tb, sq * T + t0 + (k + 2) * kRound,
+                            rows - (k + 2) * kRound, n0, &bars[j]);
+        }
+    } else {
         stage_rows(sa, sb, a, b, base + n0, min(kSub, rows), N, n0, tpb, vec != 0);
-    pdl_wait();
-    float s = n < N ? __ldcg(&agg[((size_t)sq * nch + c) * N + n].x) : 0.0f;
-    for (int r0 = 0; r0 < rows; r0 += kSub) {
-        const int rs = min(kSub, rows - r0);
-        if (r0) {
-            __syncthreads();
-            if (tma)
-                stage_rows_tma(sa, sb, &ta, &tb, sq * T + t0 + r0, rs, n0, &bar, phase, err);
-            else
+        pdl_wait();
+        s = n < N ? __ldcg(&agg[((size_t)sq * nch + c) * N + n].x) : 0.0f;
+        for (int r0 = 0; r0 < rows; r0 += kSub) {
+            const int rs = min(kSub, rows - r0);
+            if (r0) {
+                __syncthreads();
                 stage_rows(sa, sb, a, b, base + (size_t)r0 * N + n0, rs, N, n0, tpb, vec != 0);
-        }
-        for (int r = 0; r < rs; ++r) {
-            const float av = sa[r * tpb + threadIdx.x];
-            const float bv = gate_b(av, sb[r * tpb + threadIdx.x], gated);
-            s = fused ? rec_fused(av, s, bv) : rec_split(av, s, bv);
-            if (n < N) __stcs(out + base + (size_t)(r0 + r) * N + n, s);
+            }
+            for (int r = 0; r < rs; ++r) {
+                const float av = sa[r * tpb + threadIdx.x];
+                const float bv = gate_b(av, sb[r * tpb + threadIdx.x], gated);
+                s = fused ? rec_fused(av, s, bv) : rec_split(av, s, bv);
+                if (n < N) __stcs(out + base + (size_t)(r0 + r) * N + n, s);
+            }
         }
     }
     if (c == nch - 1 && n < N) send[(size_t)sq * N + n] = s;

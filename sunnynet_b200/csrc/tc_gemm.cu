@@ -47,14 +47,18 @@ constexpr int BK = 64;  // bf16 per slab row = 128 bytes
 constexpr int kEpiGroups = 4;
 constexpr int kThreads = 64 + 128 * kEpiGroups;
 
-template <int BN>
+template <int BN, bool I8>
 struct TcCfg {
     static constexpr int A_BYTES = BM * 128;
     static constexpr int W_BYTES = BN * 128;
-    static constexpr int STAGE = 2 * A_BYTES + 2 * W_BYTES;
-    static constexpr int S = BN == 256 ? 2 : (BN == 128 ? 3 : (BN == 64 ? 4 : 5));
+    // a stage: the A hi / lo slabs and the weight hi (and, bf16 weights, lo) slab
+    static constexpr int STAGE = 2 * A_BYTES + (I8 ? 1 : 2) * W_BYTES;
     // epilogue operands loaded under the main loop: [4 warps][32][33] floats
     static constexpr int PRE = 4 * 32 * 33 * 4;
+    // as many stages as fit the 227 KB of shared memory next to the operand
+    // area, 1 KB of alignment slack, 256 B of barriers and BN column scales
+    static constexpr int S_FIT = (227 * 1024 - PRE - 1024 - 256 - BN * 4) / STAGE;
+    static constexpr int S = S_FIT > 6 ? 6 : S_FIT;
     // after the 256 bytes of barriers: the tile's per-column weight scales
     static constexpr int SMEM = S * STAGE + PRE + 1024 + 256 + BN * 4;
 };
@@ -326,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
                    const __grid_constant__ CUtensorMap twh, const __grid_constant__ CUtensorMap twl,
                    GemmArgs a, int* err) {
-    using C = TcCfg<BN>;
+    using C = TcCfg<BN, I8>;
     constexpr int S = C::S;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -744,7 +748,7 @@ std::map<int, ActPlanes>& act_cache() {
 template <int BN, bool I8, bool LOADS>
 int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
               const CUtensorMap& tal, cudaStream_t st, bool pdl, int ks) {
-    using C = TcCfg<BN>;
+    using C = TcCfg<BN, I8>;
     static bool attr = false;
     auto k = tc_gemm_kernel<BN, I8, LOADS>;
     if (!attr) {
