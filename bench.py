@@ -252,13 +252,15 @@ def wl_c1(args, torch, dist, ours: bool):
         "e2e": {"value": alg_bytes * dist.world / e2e_s / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": int(2 * B * T * N * 4 + B * N * 4),
                 "d2h_bytes_per_step": int(B * T * N * 4 + B * N * 4)},
-        "gpu_launches": 3 * args.steps,  # agg, carry, apply per step
+        # one cooperative launch per step, or agg + carry + apply
+        "gpu_launches": (1 if "scan_onepass" in kern else 3) * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "peak_src": peaks["src"],
-                     "kernel": "scan_agg+scan_carry+scan_apply (one mode-1 scan)",
+                     "kernel": "+".join(kern) + " (one mode-1 scan)",
                      "alg_bytes_per_launch": alg_bytes, "kernels": kern,
-                     "traffic": profile_traffic("scan_chunked/c1")},
+                     "traffic": profile_traffic("scan_onepass/c1" if "scan_onepass" in kern
+                                                else "scan_chunked/c1")},
         "exact_mode": {"ms_per_step": ms_exact, "value": ach_exact * dist.world,
                        "kernel": "scan_exact_kernel", "frac": ach_exact / peaks["hbm_gbs"],
                        "traffic": profile_traffic("scan_exact_kernel/c1")},

@@ -155,6 +155,26 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+// L2 loads (ld.global.cg) of data that other CTAs, or the kernel before a
+// programmatic wait, wrote: volatile asm with a memory clobber, so each load
+// stays after the flag wait, barrier or griddepcontrol.wait that made its
+// data visible (a load asm without them may be hoisted above it).
+__device__ __forceinline__ float ld_cg(const float* p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ float2 ld_cg(const float2* p) {
+    float2 v;
+    asm volatile("ld.global.cg.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_cg(const int* p) {
+    int v;
+    asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // Barrier `id` (1..15) among `n` threads of the CTA (whole warps).
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");

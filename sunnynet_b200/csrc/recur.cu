@@ -449,7 +449,7 @@ __global__ void __launch_bounds__(kCarryWarps * 32)
         float2 m[kCarryBatch];
 #pragma unroll
         for (int j = 0; j < kCarryBatch; ++j)
-            if (live && cb + j < c1) m[j] = __ldcg(rec + (size_t)(cb + j) * N);
+            if (live && cb + j < c1) m[j] = ld_cg(rec + (size_t)(cb + j) * N);
 #pragma unroll
         for (int j = 0; j < kCarryBatch; ++j) {
             if (live && cb + j < c1) {
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(kCarryWarps * 32)
         float2 m[kCarryBatch];
 #pragma unroll
         for (int j = 0; j < kCarryBatch; ++j)
-            if (live && cb + j < c1) m[j] = __ldcg(rec + (size_t)(cb + j) * N);
+            if (live && cb + j < c1) m[j] = ld_cg(rec + (size_t)(cb + j) * N);
 #pragma unroll
         for (int j = 0; j < kCarryBatch; ++j) {
             if (live && cb + j < c1) {
@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(256)
         }
         __syncthreads();  // barriers initialised before anyone waits
         pdl_wait();
-        s = n < N ? __ldcg(&agg[((size_t)sq * nch + c) * N + n].x) : 0.0f;
+        s = n < N ? ld_cg(&agg[((size_t)sq * nch + c) * N + n]).x : 0.0f;
         for (int k = 0; k < nr; ++k) {
             const int j = k & 1;
             mbar_wait(&bars[j], (uint32_t)((k >> 1) & 1), err);
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(256)
     } else {
         stage_rows(sa, sb, a, b, base + n0, min(kSub, rows), N, n0, tpb, vec != 0);
         pdl_wait();
-        s = n < N ? __ldcg(&agg[((size_t)sq * nch + c) * N + n].x) : 0.0f;
+        s = n < N ? ld_cg(&agg[((size_t)sq * nch + c) * N + n]).x : 0.0f;
         for (int r0 = 0; r0 < rows; r0 += kSub) {
             const int rs = min(kSub, rows - r0);
             if (r0) {

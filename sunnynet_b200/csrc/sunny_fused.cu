@@ -433,7 +433,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
         for (int w = tid; w < L * (int)(sizeof(FusedLayer) / 4); w += kFusedThreads)
             dst[w] = __ldg(src + w);
     }
-    for (int i = tid; i < B * L; i += kFusedThreads) spos[i] = __ldcg(a.pos + i);
+    for (int i = tid; i < B * L; i += kFusedThreads) spos[i] = ld_cg(a.pos + i);
     if (tid < B) {
         int t = a.tok[tid];
         if (t < 0 || t >= a.vocab) {  // never read outside the table; report instead
@@ -518,8 +518,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
             // a load placed after a store through a generic pointer waits for
             // it, which would serialise the round trips
             const int b = i / D, d = i - b * D;
-            const float xv = l == 0 ? a.embed[(size_t)stok[b] * D + d] : __ldcg(a.x + i);
-            const float sv = __ldcg(a.s + ((size_t)b * L + l) * D + d);
+            const float xv = l == 0 ? a.embed[(size_t)stok[b] * D + d] : ld_cg(a.x + i);
+            const float sv = ld_cg(a.s + ((size_t)b * L + l) * D + d);
             float g = 0.0f, c = 0.0f, wl = 0.0f;
             if (b == 0) {  // this layer's LN parameters and newest tap weight
                 g = y.ni_g[d];
@@ -533,7 +533,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
             for (int k = 0; k < kFusedMaxTaps; ++k) {
                 if (k < Kc - 1) {
                     const int slot = ((p - 1 - k) % KH + KH) % KH;
-                    hv[k] = __ldcg(hb + (size_t)slot * D + d);
+                    hv[k] = ld_cg(hb + (size_t)slot * D + d);
                     wv[k] = y.dw[(size_t)(Kc - 2 - k) * D + d];
                 }
             }
@@ -601,7 +601,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
             const int c0 = slice_lo(NG, cta, nct) * G, c1 = slice_lo(NG, cta + 1, nct) * G;
             const int n = max(B * R, c1 - c0);
             for (int i = tid; i < n; i += kFusedThreads) {
-                const float vv = i < B * R ? __ldcg(a.v + i) : 0.0f;
+                const float vv = i < B * R ? ld_cg(a.v + i) : 0.0f;
                 const float dl = i < c1 - c0 ? y.delta[c0 + i] : 0.0f;
                 if (i < B * R) bufA[i] = vv;
                 if (i < c1 - c0) par[i] = dl;
@@ -664,7 +664,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
         // ------------------------------------------------------------ P3: Wz
         const int p3 = p2 + 1;
         phase_begin(p3);
-        for (int i = tid; i < B * D; i += kFusedThreads) bufA[i] = __ldcg(a.u + i);
+        for (int i = tid; i < B * D; i += kFusedThreads) bufA[i] = ld_cg(a.u + i);
         __syncthreads();
         TM(4 * l + 2, 0);
         TM(4 * l + 2, 1);
@@ -695,7 +695,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
         const int p4 = p3 + 1;
         phase_begin(p4);
         for (int i = tid; i < B * I; i += kFusedThreads) {
-            const float zv = __ldcg(a.z + i);
+            const float zv = ld_cg(a.z + i);
             float g = 0.0f, c = 0.0f;
             if (i < I) {
                 g = y.nm_g[i];
@@ -730,8 +730,8 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
                 const int m = threadIdx.x & 31;
                 if (m >= Bq) return 0.0f;
                 const size_t o = (size_t)m * D + n;
-                return bg * __ldcg(a.s + ((size_t)m * L + l) * D + n) + __ldcg(a.sfb + o) +
-                       __ldcg(a.x + o);
+                return bg * ld_cg(a.s + ((size_t)m * L + l) * D + n) + ld_cg(a.sfb + o) +
+                       ld_cg(a.x + o);
             };
             rows_loop<WT, STAGE, MB>(
                 y.sWc, r1 - r0, [=](int i) { return r0 + i; },
@@ -755,7 +755,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) sunny_fused_kernel(FusedArgs
 
     // ------------------------------------------- head: LN(x), logits, argmax
     for (int i = tid; i < B * D; i += kFusedThreads) {
-        const float xv = __ldcg(a.x + i);
+        const float xv = ld_cg(a.x + i);
         float g = 0.0f, c = 0.0f;
         if (i < D) {
             g = a.no_g[i];
