@@ -41,11 +41,15 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;  // bf16 per slab row = 128 bytes
 // Epilogue warps: group 0 (warps 2-5, one per TMEM lane quarter) runs every
-// epilogue; in the thread-per-row epilogues of wide tiles kEpiGroups groups
-// share the 32-column blocks, so the latency chains of several warps (IEEE
-// divides, tanh, exp) interleave on each scheduler.
-constexpr int kEpiGroups = 4;
-constexpr int kThreads = 64 + 128 * kEpiGroups;
+// epilogue; in the thread-per-row epilogues of wide tiles (BN > 32) four
+// groups share the 32-column blocks, so the latency chains of several warps
+// (IEEE divides, tanh, exp) interleave on each scheduler. 32-column tiles
+// launch group 0 alone.
+template <int BN>
+struct TcEpi {
+    static constexpr int GROUPS = BN > 32 ? 4 : 1;
+    static constexpr int THREADS = 64 + 128 * GROUPS;
+};
 
 template <int BN, bool I8>
 struct TcCfg {
@@ -326,12 +330,13 @@ __device__ __forceinline__ void tc_reduce(const GemmArgs& a, const float* part, 
 // LOADS: the epilogue reads more than the accumulator (residual / accumulate
 // kinds); those operands are then all loaded before any result is stored.
 template <int BN, bool I8, bool LOADS>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
                    const __grid_constant__ CUtensorMap twh, const __grid_constant__ CUtensorMap twl,
                    GemmArgs a, int* err) {
     using C = TcCfg<BN, I8>;
     constexpr int S = C::S;
+    constexpr int kEpiGroups = TcEpi<BN>::GROUPS;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* sb = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // 1024-B aligned ring
@@ -366,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(acc_full, 1);
         for (int q = 0; q < 4; ++q) {
             mbar_init(&op_full[q], 1);
-            mbar_init(&row_done[q], 32 * (kEpiGroups - 1));
+            if (kEpiGroups > 1) mbar_init(&row_done[q], 32 * (kEpiGroups - 1));
         }
         *give_up = 0;
         fence_mbar_init();
@@ -760,7 +765,7 @@ int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
     const int bi = BN == 32 ? 0 : (BN == 64 ? 1 : (BN == 128 ? 2 : 3));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(((a.N + BN - 1) / BN) * ks), (unsigned)((a.M + BM - 1) / BM));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(TcEpi<BN>::THREADS);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute la[2];
