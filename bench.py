@@ -601,7 +601,11 @@ def wl_c5(args, torch, dist, ours):
     for _ in range(reps):
         m.prefill(ht, chunk=Tc, logits=hl)
     e2e_s = dist.max(torch, (time.perf_counter() - t0) / reps)
-    launches = 1 + L * 15 + 2
+    # embedding gather; per layer LN rows, taps (writing V's input planes),
+    # ring update, V (writing U's planes), U, gate (writing Wz's planes),
+    # scan, state shift (writing Ws's planes), Ws, Wz, LN of z into Wc's
+    # planes, Wc; the head's row statistics, input split and contraction
+    launches = 1 + L * 12 + 3
     res.update({"ms_per_step": ms, "value": B * Tc * dist.world / (ms * 1e-3),
                 "e2e": {"value": B * Tc * dist.world / e2e_s, "unit": "tokens/s",
                         "h2d_bytes_per_step": B * Tc * 4, "d2h_bytes_per_step": B * S.vocab * 4,

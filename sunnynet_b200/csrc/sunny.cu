@@ -257,10 +257,13 @@ __global__ void ln_rows_kernel(int n, const float* __restrict__ X, float* __rest
 
 // Causal taps over a chunk: position t of sequence b reads raw rows t-1..t-K+1
 // of the chunk, or the history ring for the ones before the chunk.
+// With hi / lo, the taps are written only as the bf16 planes of the next
+// contraction's input (the values split_act_kernel would make from at).
 __global__ void conv_chunk_kernel(int B, int Tc, int D, int K, int KH, int L, int layer,
                                   const float* __restrict__ raw, const float* __restrict__ hist,
                                   const int32_t* __restrict__ pos, const float* __restrict__ dw,
-                                  float* __restrict__ at) {
+                                  float* __restrict__ at, __nv_bfloat16* __restrict__ hi = nullptr,
+                                  __nv_bfloat16* __restrict__ lo = nullptr) {
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (i >= (long long)B * Tc * D) return;
     const int d = (int)(i % D);
@@ -280,7 +283,8 @@ __global__ void conv_chunk_kernel(int B, int Tc, int D, int K, int KH, int L, in
         }
         a = r + acc;
     }
-    at[i] = a;
+    if (hi) store_split(hi, lo, i, a);
+    else at[i] = a;
 }
 
 // After the taps of a chunk: the last K-1 raw rows of each sequence enter the
@@ -302,9 +306,12 @@ __global__ void ring_update_kernel(int Tc, int D, int KH, int L, int layer,
 }
 
 // u = compete(q), p = decay gate (the scan's a), one thread per (row, channel)
+// (with uh / ul also the bf16 planes of u, the input of the Wz contraction)
 __global__ void gate_chunk_kernel(long long M, int D, int G, const float* __restrict__ q,
                                   const float* __restrict__ delta, float* __restrict__ u,
-                                  float* __restrict__ pa, int clamp, float p_floor) {
+                                  float* __restrict__ pa, int clamp, float p_floor,
+                                  __nv_bfloat16* __restrict__ uh = nullptr,
+                                  __nv_bfloat16* __restrict__ ul = nullptr) {
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (i >= M * D) return;
     const long long m = i / D;
@@ -314,22 +321,29 @@ __global__ void gate_chunk_kernel(long long M, int D, int G, const float* __rest
     const float g0 = qb[D + d];
     const float g1 = qb[D + base + (off + 1) % G];
     const float g2 = qb[D + base + (off + 2) % G];
-    u[i] = qb[d] * (sigm(g0 - g1) * sigm(g0 - g2));
+    const float uu = qb[d] * (sigm(g0 - g1) * sigm(g0 - g2));
+    u[i] = uu;
+    if (uh) store_split(uh, ul, i, uu);
     float p = 1.0f - delta[d] * (1.0f - sigm(g0));
     if (clamp && p < p_floor) p = p_floor;
     pa[i] = p;
 }
 
 // prev[b][t] = state before position t: s_in for t = 0, else states[b][t-1]
+// (with hi / lo written only as the bf16 planes of the Ws contraction's input)
 __global__ void prev_kernel(int Tc, int D, long long total, const float* __restrict__ s0,
-                            const float* __restrict__ st, float* __restrict__ prev) {
+                            const float* __restrict__ st, float* __restrict__ prev,
+                            __nv_bfloat16* __restrict__ hi = nullptr,
+                            __nv_bfloat16* __restrict__ lo = nullptr) {
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (i >= total) return;
     const int d = (int)(i % D);
     const long long m = i / D;
     const int t = (int)(m % Tc);
     const long long b = m / Tc;
-    prev[i] = t == 0 ? s0[b * D + d] : st[i - D];
+    const float v = t == 0 ? s0[b * D + d] : st[i - D];
+    if (hi) store_split(hi, lo, i, v);
+    else prev[i] = v;
 }
 
 // state export / import: ring <-> newest-first history
@@ -397,6 +411,10 @@ struct SunnyModel {
     float *cx = nullptr, *craw = nullptr, *cat = nullptr, *cv = nullptr, *cq = nullptr;
     float *cu = nullptr, *cp = nullptr, *cst = nullptr, *cprev = nullptr, *csfb = nullptr;
     float *cz = nullptr, *cmu = nullptr, *crs = nullptr, *cs0 = nullptr, *csend = nullptr;
+    // tensor-core prefill: each contraction's input written as bf16 planes by
+    // its producer (taps, V's epilogue, the gate, the state shift, the LN of z)
+    bool c_tc = false;
+    TcAct c_at, c_v, c_u, c_prev, c_z;
     std::map<std::pair<long long, int>, cudaGraphExec_t> cgraphs;  // (B*65536+Tc, head)
     cudaStream_t cap = nullptr;
     // fused small-batch step (sunny_fused.cu): per-layer descriptors on the
@@ -1033,6 +1051,21 @@ int ensure_chunk_bufs(SunnyModel* m, int B, int Tc) {
         SN_TRY(tc_reserve(m->R, rows));
         SN_TRY(tc_reserve(m->I, rows));
     }
+    bool tc = !getenv("SN_DISABLE_TC") && rows >= 16 && D % 8 == 0 && R % 8 == 0 && I % 8 == 0;
+    for (int l = 0; l < m->L && tc; ++l) {
+        const SunnyLayer& y = m->ly[l];
+        tc = y.tV.ready && y.tU.ready && y.tWz.ready && y.tWc.ready && y.tWs.ready;
+    }
+    m->c_tc = false;
+    if (tc) {
+        auto al = [](size_t nb, void* o) -> void* { return ((SunnyModel*)o)->dalloc<uint8_t>(nb); };
+        SN_TRY(tc_act_alloc(&m->c_at, (int)D, rows, al, m));
+        SN_TRY(tc_act_alloc(&m->c_v, (int)R, rows, al, m));
+        SN_TRY(tc_act_alloc(&m->c_u, (int)D, rows, al, m));
+        SN_TRY(tc_act_alloc(&m->c_prev, (int)D, rows, al, m));
+        SN_TRY(tc_act_alloc(&m->c_z, (int)I, rows, al, m));
+        m->c_tc = true;
+    }
     m->crows = rows;
     m->cseqs = B;
     for (auto& kv : m->cgraphs) cudaGraphExecDestroy(kv.second);  // captured old pointers
@@ -1046,6 +1079,8 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
     const int D = m->D, I = m->I, R = m->R, L = m->L;
     const long long M = (long long)B * Tc;
     const unsigned eb = (unsigned)((M * D + 255) / 256);
+    // producer-written planes (the contraction dispatch uses SIMT below 16 rows)
+    const bool ctc = m->c_tc && M >= 16;
     {
         ProfScope ps("prefill_rows", st);
         gather_embed_kernel<<<(unsigned)M, 256, 0, st>>>(D, m->vocab, rt().d_err, m->ctok,
@@ -1057,16 +1092,30 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
             ProfScope ps("prefill_rows", st);
             ln_rows_kernel<<<(unsigned)M, 256, 0, st>>>(D, m->cx, m->craw, y.ni_g, y.ni_c, m->eps);
             conv_chunk_kernel<<<eb, 256, 0, st>>>(B, Tc, D, m->K, m->KH, L, l, m->craw, m->hist,
-                                                 m->pos, y.dw, m->cat);
+                                                 m->pos, y.dw, m->cat,
+                                                 ctc ? m->c_at.hi : nullptr,
+                                                 ctc ? m->c_at.lo : nullptr);
             if (m->K > 1)
                 ring_update_kernel<<<B, 256, 0, st>>>(Tc, D, m->KH, L, l, m->craw, m->hist,
                                                       m->pos);
         }
-        {
-            ProfScope ps("gemm_V", st);
-            SN_TRY(launch_gemm(gemm((int)M, R, D, m->cat, y.V, y.sV, m->cv), m->wtype, st, &y.tV));
-        }
-        {
+        if (ctc) {  // inputs as producer-written planes; V writes U's
+            GemmArgs gv = gemm((int)M, R, D, m->cat, y.V, y.sV, m->cv);
+            gv.Ch = m->c_v.hi;
+            gv.Cl = m->c_v.lo;
+            {
+                ProfScope ps("gemm_V", st);
+                SN_TRY(launch_tc_gemm_act(gv, y.tV, m->c_at, st));
+            }
+            ProfScope ps("gemm_U", st);
+            SN_TRY(launch_tc_gemm_act(gemm((int)M, 2 * D, R, m->cv, y.U, y.sU, m->cq), y.tU,
+                                      m->c_v, st));
+        } else {
+            {
+                ProfScope ps("gemm_V", st);
+                SN_TRY(launch_gemm(gemm((int)M, R, D, m->cat, y.V, y.sV, m->cv), m->wtype, st,
+                                   &y.tV));
+            }
             ProfScope ps("gemm_U", st);
             SN_TRY(launch_gemm(gemm((int)M, 2 * D, R, m->cv, y.U, y.sU, m->cq), m->wtype, st,
                                &y.tU));
@@ -1074,7 +1123,9 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
         {
             ProfScope ps("prefill_scan", st);
             gate_chunk_kernel<<<eb, 256, 0, st>>>(M, D, m->G, m->cq, y.delta, m->cu, m->cp,
-                                                  m->clamp, m->p_floor);
+                                                  m->clamp, m->p_floor,
+                                                  ctc ? m->c_u.hi : nullptr,
+                                                  ctc ? m->c_u.lo : nullptr);
             SN_TRY(cuda_check(cudaMemcpy2DAsync(m->cs0, (size_t)D * 4, m->s + (size_t)l * D,
                                                 (size_t)L * D * 4, (size_t)D * 4, B,
                                                 cudaMemcpyDeviceToDevice, st),
@@ -1084,26 +1135,36 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
                                                 (size_t)D * 4, (size_t)D * 4, B,
                                                 cudaMemcpyDeviceToDevice, st),
                               "send"));
-            prev_kernel<<<eb, 256, 0, st>>>(Tc, D, M * D, m->cs0, m->cst, m->cprev);
+            prev_kernel<<<eb, 256, 0, st>>>(Tc, D, M * D, m->cs0, m->cst, m->cprev,
+                                            ctc ? m->c_prev.hi : nullptr,
+                                            ctc ? m->c_prev.lo : nullptr);
         }
         {
             ProfScope ps("gemm_Ws", st);
-            SN_TRY(launch_gemm(gemm((int)M, D, D, m->cprev, y.Ws, y.sWs, m->csfb), m->wtype, st,
-                               &y.tWs));
+            const GemmArgs gs = gemm((int)M, D, D, m->cprev, y.Ws, y.sWs, m->csfb);
+            if (ctc) SN_TRY(launch_tc_gemm_act(gs, y.tWs, m->c_prev, st));
+            else SN_TRY(launch_gemm(gs, m->wtype, st, &y.tWs));
         }
         GemmArgs gz = gemm((int)M, I, D, m->cu, y.Wz, y.sWz, m->cz);
         gz.epi = kEpiWedge;
         gz.p = y.a_tanh;
         {
             ProfScope ps("gemm_Wz", st);
-            SN_TRY(launch_gemm(gz, m->wtype, st, &y.tWz));
+            if (ctc) SN_TRY(launch_tc_gemm_act(gz, y.tWz, m->c_u, st));
+            else SN_TRY(launch_gemm(gz, m->wtype, st, &y.tWz));
         }
-        {
+        if (ctc) {  // LN(z) straight into Wc's input planes
+            ProfScope ps("rowstats", st);
+            ln_split_kernel<<<(unsigned)M, 256, 0, st>>>(I, m->cz, I, y.nm_g, y.nm_c, m->c_z.hi,
+                                                         m->c_z.lo, m->eps);
+        } else {
             ProfScope ps("rowstats", st);
             rowstats_kernel<<<(unsigned)M, 256, 0, st>>>(I, m->cz, I, m->cmu, m->crs, m->eps);
         }
         GemmArgs gc = gemm((int)M, D, I, m->cz, y.Wc, y.sWc, m->cx);
-        gc.mu = m->cmu; gc.rs = m->crs; gc.g = y.nm_g; gc.c = y.nm_c;
+        if (!ctc) {
+            gc.mu = m->cmu; gc.rs = m->crs; gc.g = y.nm_g; gc.c = y.nm_c;
+        }
         gc.epi = kEpiResid;
         gc.p = y.b_gain;
         gc.S = m->cst; gc.lds = D;
@@ -1111,7 +1172,8 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
         gc.X = m->cx; gc.ldx = D;
         {
             ProfScope ps("gemm_Wc", st);
-            SN_TRY(launch_gemm(gc, m->wtype, st, &y.tWc));
+            if (ctc) SN_TRY(launch_tc_gemm_act(gc, y.tWc, m->c_z, st));
+            else SN_TRY(launch_gemm(gc, m->wtype, st, &y.tWc));
         }
     }
     if (head) {  // logits of each sequence's last position only
