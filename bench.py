@@ -603,9 +603,10 @@ def wl_c5(args, torch, dist, ours):
     e2e_s = dist.max(torch, (time.perf_counter() - t0) / reps)
     # embedding gather; per layer LN rows, taps (writing V's input planes),
     # ring update, V (writing U's planes), U, gate (writing Wz's planes),
-    # scan, state shift (writing Ws's planes), Ws, Wz, LN of z into Wc's
-    # planes, Wc; the head's row statistics, input split and contraction
-    launches = 1 + L * 12 + 3
+    # scan (writing Ws's input planes, the state entering each position), Ws,
+    # Wz, LN of z into Wc's planes, Wc; the head's row statistics, input split
+    # and contraction
+    launches = 1 + L * 11 + 3
     res.update({"ms_per_step": ms, "value": B * Tc * dist.world / (ms * 1e-3),
                 "e2e": {"value": B * Tc * dist.world / e2e_s, "unit": "tokens/s",
                         "h2d_bytes_per_step": B * Tc * 4, "d2h_bytes_per_step": B * S.vocab * 4,

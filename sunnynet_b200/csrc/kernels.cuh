@@ -1,6 +1,7 @@
 // Device-pointer launchers shared between translation units. All take device
 // pointers, enqueue on `st` and return an sn_status.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -12,6 +13,13 @@ enum W4Epi : int { kW4Store = 0, kW4Add = 1, kW4Relu2 = 2, kW4Tanh = 3, kW4Sigmo
 
 int launch_scan(const float* a, const float* b, const float* s0, float* out, float* send, int B,
                 int T, int N, int gated, cudaStream_t st);
+// The same scan with the entering / leaving states at row strides s0_ld /
+// send_ld (a layer's rows of a [seq][layer][N] state array), optionally also
+// writing the state entering each position as bf16 planes ph / pl (row t:
+// s0 for t = 0, out row t - 1 after), the input of a following contraction.
+int launch_scan_strided(const float* a, const float* b, const float* s0, long long s0_ld,
+                        float* out, float* send, long long send_ld, int B, int T, int N,
+                        int gated, __nv_bfloat16* ph, __nv_bfloat16* pl, cudaStream_t st);
 int launch_step(const float* a, const float* b, float* s, int B, int N, int gated,
                 cudaStream_t st);
 // Scan mode 1 (chunked in T): chunk length for the shape (0 when even one

@@ -19,6 +19,7 @@
 // Stages are handed on with mbarriers (full -> ready -> done -> empty); every
 // wait is bounded and records an error instead of hanging. The sequential
 // chain is the only serial part: ~one dependent FFMA per row.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -29,6 +30,7 @@
 #include "ptx.cuh"
 #include "recur.h"
 #include "runtime.cuh"
+#include "tc_gemm.cuh"
 #include "tcgen05.cuh"
 
 namespace sn {
@@ -90,8 +92,9 @@ __device__ __forceinline__ float chain_chunk(const float* __restrict__ pa, float
 template <int CW>
 __global__ void __launch_bounds__(128)
     scan_exact_kernel(const float* __restrict__ a, const float* __restrict__ b,
-                      const float* __restrict__ s0, float* __restrict__ out,
-                      float* __restrict__ send, int T, int N, int nv, int gated, int vec,
+                      const float* s0, float* __restrict__ out, float* send, int T, int N,
+                      int nv, int gated, int vec, long long s0_ld, long long send_ld,
+                      __nv_bfloat16* __restrict__ ph, __nv_bfloat16* __restrict__ pl,
                       int* err) {
     constexpr int S = ScanCfg<CW>::S;
     constexpr int TILE = kTC * CW;
@@ -174,7 +177,10 @@ __global__ void __launch_bounds__(128)
     } else if (warp == 2) {  // ---------------------------------------- chain
         const int d = d0 + lane;
         const bool live = lane < CW && d < N;
-        float s = live ? s0[(size_t)bb * N + d] : 0.0f;
+        float s = live ? s0[(size_t)bb * s0_ld + d] : 0.0f;
+        // the state entering each position, as bf16 planes: row 0 is s0 (rows
+        // t >= 1 are out row t - 1, written by the storer)
+        if (ph && live) store_split(ph, pl, base + d, s);
         const bool all_fused = d0 + CW <= nv;
         const bool fused = d < nv;
         for (int c = 0; c < nch; ++c) {
@@ -196,7 +202,7 @@ __global__ void __launch_bounds__(128)
             }
             mbar_arrive(&done[st]);
         }
-        if (live) send[(size_t)bb * N + d] = s;
+        if (live) send[(size_t)bb * send_ld + d] = s;
     } else {  // ------------------------------------------------------ storer
         for (int c = 0; c < nch; ++c) {
             const int st = c % S;
@@ -209,15 +215,32 @@ __global__ void __launch_bounds__(128)
                 for (int i = lane; i < rows * Q; i += 32) {
                     const int r = i / Q, q = i % Q;
                     const int d = d0 + 4 * q;
-                    if (d < N)
-                        *reinterpret_cast<float4*>(out + base + (size_t)(t0 + r) * N + d) =
-                            *reinterpret_cast<const float4*>(db + r * CW + 4 * q);
+                    if (d < N) {
+                        const float4 v = *reinterpret_cast<const float4*>(db + r * CW + 4 * q);
+                        const size_t o = base + (size_t)(t0 + r) * N + d;
+                        *reinterpret_cast<float4*>(out + o) = v;
+                        if (ph && t0 + r + 1 < T) {  // the state entering position t + 1
+                            const float x[4] = {v.x, v.y, v.z, v.w};
+                            __nv_bfloat16 h[4], l[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {  // store_split's rounding
+                                h[j] = __float2bfloat16_rn(x[j]);
+                                l[j] = __float2bfloat16_rn(x[j] - __bfloat162float(h[j]));
+                            }
+                            *reinterpret_cast<uint2*>(ph + o + N) = *reinterpret_cast<const uint2*>(h);
+                            *reinterpret_cast<uint2*>(pl + o + N) = *reinterpret_cast<const uint2*>(l);
+                        }
+                    }
                 }
             } else {
                 for (int i = lane; i < rows * CW; i += 32) {
                     const int r = i / CW, ch = i % CW;
                     const int d = d0 + ch;
-                    if (d < N) out[base + (size_t)(t0 + r) * N + d] = db[i];
+                    if (d < N) {
+                        const size_t o = base + (size_t)(t0 + r) * N + d;
+                        out[o] = db[i];
+                        if (ph && t0 + r + 1 < T) store_split(ph, pl, o + N, db[i]);
+                    }
                 }
             }
             __syncwarp();
@@ -228,7 +251,8 @@ __global__ void __launch_bounds__(128)
 
 template <int CW>
 int launch_scan_cw(const float* a, const float* b, const float* s0, float* out, float* send,
-                   int B, int T, int N, int gated, int vec, cudaStream_t st) {
+                   int B, int T, int N, int gated, int vec, long long s0_ld, long long send_ld,
+                   __nv_bfloat16* ph, __nv_bfloat16* pl, cudaStream_t st) {
     static bool attr = false;
     const size_t smem = ScanCfg<CW>::smem;
     if (!attr) {
@@ -240,7 +264,7 @@ int launch_scan_cw(const float* a, const float* b, const float* s0, float* out, 
     }
     dim3 grid((N + CW - 1) / CW, B);
     scan_exact_kernel<CW><<<grid, 128, smem, st>>>(a, b, s0, out, send, T, N, N - N % 8, gated,
-                                                   vec, rt().d_err);
+                                                   vec, s0_ld, send_ld, ph, pl, rt().d_err);
     return cuda_check(cudaGetLastError(), "scan launch");
 }
 
@@ -264,13 +288,21 @@ int pick_cw(int B, int N) {
 // Device-pointer scan used by the ABI entry points and by the model code.
 int launch_scan(const float* a, const float* b, const float* s0, float* out, float* send, int B,
                 int T, int N, int gated, cudaStream_t st) {
+    return launch_scan_strided(a, b, s0, N, out, send, N, B, T, N, gated, nullptr, nullptr, st);
+}
+
+int launch_scan_strided(const float* a, const float* b, const float* s0, long long s0_ld,
+                        float* out, float* send, long long send_ld, int B, int T, int N,
+                        int gated, __nv_bfloat16* ph, __nv_bfloat16* pl, cudaStream_t st) {
     if (B > 65535) return fail(SN_E_INVAL, "recur_scan: B=%d exceeds 65535", B);
+    // (plane stores are 8-byte vectors of four channels on the vector path)
     const bool vec = N % 4 == 0 && ((uintptr_t)a % 16 == 0) && ((uintptr_t)b % 16 == 0) &&
-                     ((uintptr_t)out % 16 == 0);
+                     ((uintptr_t)out % 16 == 0) &&
+                     (!ph || ((uintptr_t)ph % 8 == 0 && (uintptr_t)pl % 8 == 0));
     switch (pick_cw(B, N)) {
-        case 32: return launch_scan_cw<32>(a, b, s0, out, send, B, T, N, gated, vec, st);
-        case 16: return launch_scan_cw<16>(a, b, s0, out, send, B, T, N, gated, vec, st);
-        default: return launch_scan_cw<8>(a, b, s0, out, send, B, T, N, gated, vec, st);
+        case 32: return launch_scan_cw<32>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st);
+        case 16: return launch_scan_cw<16>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st);
+        default: return launch_scan_cw<8>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st);
     }
 }
 

@@ -330,20 +330,15 @@ __global__ void gate_chunk_kernel(long long M, int D, int G, const float* __rest
 }
 
 // prev[b][t] = state before position t: s_in for t = 0, else states[b][t-1]
-// (with hi / lo written only as the bf16 planes of the Ws contraction's input)
 __global__ void prev_kernel(int Tc, int D, long long total, const float* __restrict__ s0,
-                            const float* __restrict__ st, float* __restrict__ prev,
-                            __nv_bfloat16* __restrict__ hi = nullptr,
-                            __nv_bfloat16* __restrict__ lo = nullptr) {
+                            const float* __restrict__ st, float* __restrict__ prev) {
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (i >= total) return;
     const int d = (int)(i % D);
     const long long m = i / D;
     const int t = (int)(m % Tc);
     const long long b = m / Tc;
-    const float v = t == 0 ? s0[b * D + d] : st[i - D];
-    if (hi) store_split(hi, lo, i, v);
-    else prev[i] = v;
+    prev[i] = t == 0 ? s0[b * D + d] : st[i - D];
 }
 
 // state export / import: ring <-> newest-first history
@@ -1126,18 +1121,25 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
                                                   m->clamp, m->p_floor,
                                                   ctc ? m->c_u.hi : nullptr,
                                                   ctc ? m->c_u.lo : nullptr);
-            SN_TRY(cuda_check(cudaMemcpy2DAsync(m->cs0, (size_t)D * 4, m->s + (size_t)l * D,
-                                                (size_t)L * D * 4, (size_t)D * 4, B,
-                                                cudaMemcpyDeviceToDevice, st),
-                              "s0"));
-            SN_TRY(launch_scan(m->cp, m->cu, m->cs0, m->cst, m->csend, B, Tc, D, 1, st));
-            SN_TRY(cuda_check(cudaMemcpy2DAsync(m->s + (size_t)l * D, (size_t)L * D * 4, m->csend,
-                                                (size_t)D * 4, (size_t)D * 4, B,
-                                                cudaMemcpyDeviceToDevice, st),
-                              "send"));
-            prev_kernel<<<eb, 256, 0, st>>>(Tc, D, M * D, m->cs0, m->cst, m->cprev,
-                                            ctc ? m->c_prev.hi : nullptr,
-                                            ctc ? m->c_prev.lo : nullptr);
+            if (ctc) {
+                // the layer's state rows read and written in place, the state
+                // entering each position written as Ws's input planes
+                float* sl = m->s + (size_t)l * D;
+                SN_TRY(launch_scan_strided(m->cp, m->cu, sl, (long long)L * D, m->cst, sl,
+                                           (long long)L * D, B, Tc, D, 1, m->c_prev.hi,
+                                           m->c_prev.lo, st));
+            } else {
+                SN_TRY(cuda_check(cudaMemcpy2DAsync(m->cs0, (size_t)D * 4, m->s + (size_t)l * D,
+                                                    (size_t)L * D * 4, (size_t)D * 4, B,
+                                                    cudaMemcpyDeviceToDevice, st),
+                                  "s0"));
+                SN_TRY(launch_scan(m->cp, m->cu, m->cs0, m->cst, m->csend, B, Tc, D, 1, st));
+                SN_TRY(cuda_check(cudaMemcpy2DAsync(m->s + (size_t)l * D, (size_t)L * D * 4,
+                                                    m->csend, (size_t)D * 4, (size_t)D * 4, B,
+                                                    cudaMemcpyDeviceToDevice, st),
+                                  "send"));
+                prev_kernel<<<eb, 256, 0, st>>>(Tc, D, M * D, m->cs0, m->cst, m->cprev);
+            }
         }
         {
             ProfScope ps("gemm_Ws", st);
