@@ -287,6 +287,53 @@ __global__ void conv_chunk_kernel(int B, int Tc, int D, int K, int KH, int L, in
     else at[i] = a;
 }
 
+// conv_chunk_kernel for four consecutive channels per thread (D % 4 == 0,
+// 16-byte aligned rows), writing the taps only as bf16 planes; the same
+// arithmetic per channel.
+__global__ void conv_chunk4_kernel(int B, int Tc, int D, int K, int KH, int L, int layer,
+                                   const float* __restrict__ raw, const float* __restrict__ hist,
+                                   const int32_t* __restrict__ pos, const float* __restrict__ dw,
+                                   __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+    const int D4 = D >> 2;
+    const long long i4 = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i4 >= (long long)B * Tc * D4) return;
+    const int d = (int)(i4 % D4) * 4;
+    const long long m = i4 / D4;
+    const int t = (int)(m % Tc), b = (int)(m / Tc);
+    const float4 r4 = *reinterpret_cast<const float4*>(raw + m * D + d);
+    const float r[4] = {r4.x, r4.y, r4.z, r4.w};
+    float a[4] = {r[0], r[1], r[2], r[3]};
+    if (K > 1) {
+        const int p = pos[b * L + layer];
+        const float* hb = hist + ((size_t)b * L + layer) * KH * D;
+        const float4 w4 = *reinterpret_cast<const float4*>(dw + (size_t)(K - 1) * D + d);
+        const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+        float acc[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[j] = r[j] * w[j];
+        for (int k = 0; k < K - 1; ++k) {
+            const int tt = t - 1 - k;
+            const float* src = tt >= 0 ? raw + (m - 1 - k) * D + d
+                                       : hb + (size_t)(((p + tt) % KH + KH) % KH) * D + d;
+            const float4 h4 = *reinterpret_cast<const float4*>(src);
+            const float4 k4 = *reinterpret_cast<const float4*>(dw + (size_t)(K - 2 - k) * D + d);
+            const float hv[4] = {h4.x, h4.y, h4.z, h4.w}, wk[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) acc[j] += hv[j] * wk[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) a[j] = r[j] + acc[j];
+    }
+    __nv_bfloat16 h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {  // store_split's rounding
+        h[j] = __float2bfloat16_rn(a[j]);
+        l[j] = __float2bfloat16_rn(a[j] - __bfloat162float(h[j]));
+    }
+    *reinterpret_cast<uint2*>(hi + m * D + d) = *reinterpret_cast<const uint2*>(h);
+    *reinterpret_cast<uint2*>(lo + m * D + d) = *reinterpret_cast<const uint2*>(l);
+}
+
 // After the taps of a chunk: the last K-1 raw rows of each sequence enter the
 // ring and the position advances by Tc. One CTA per sequence.
 __global__ void ring_update_kernel(int Tc, int D, int KH, int L, int layer,
@@ -1086,10 +1133,17 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
         {
             ProfScope ps("prefill_rows", st);
             ln_rows_kernel<<<(unsigned)M, 256, 0, st>>>(D, m->cx, m->craw, y.ni_g, y.ni_c, m->eps);
-            conv_chunk_kernel<<<eb, 256, 0, st>>>(B, Tc, D, m->K, m->KH, L, l, m->craw, m->hist,
-                                                 m->pos, y.dw, m->cat,
-                                                 ctc ? m->c_at.hi : nullptr,
-                                                 ctc ? m->c_at.lo : nullptr);
+            const bool al16 = (uintptr_t)y.dw % 16 == 0 && (uintptr_t)m->hist % 16 == 0 &&
+                              (uintptr_t)m->craw % 16 == 0;
+            if (ctc && al16)  // four channels per thread (planes: D % 8 == 0)
+                conv_chunk4_kernel<<<(unsigned)((M * D / 4 + 255) / 256), 256, 0, st>>>(
+                    B, Tc, D, m->K, m->KH, L, l, m->craw, m->hist, m->pos, y.dw, m->c_at.hi,
+                    m->c_at.lo);
+            else
+                conv_chunk_kernel<<<eb, 256, 0, st>>>(B, Tc, D, m->K, m->KH, L, l, m->craw,
+                                                     m->hist, m->pos, y.dw, m->cat,
+                                                     ctc ? m->c_at.hi : nullptr,
+                                                     ctc ? m->c_at.lo : nullptr);
             if (m->K > 1)
                 ring_update_kernel<<<B, 256, 0, st>>>(Tc, D, m->KH, L, l, m->craw, m->hist,
                                                       m->pos);
