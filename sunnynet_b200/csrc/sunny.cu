@@ -376,6 +376,61 @@ __global__ void gate_chunk_kernel(long long M, int D, int G, const float* __rest
     pa[i] = p;
 }
 
+// gate_chunk_kernel with one thread per competition group of G channels
+// (G = 4 or 8, D % G == 0, 16-byte aligned rows): the group's u and gate
+// inputs read as float4s, u, p and u's bf16 planes written as vectors; the
+// same arithmetic per channel.
+template <int G>
+__global__ void gate_group_kernel(long long M, int D, const float* __restrict__ q,
+                                  const float* __restrict__ delta, float* __restrict__ u,
+                                  float* __restrict__ pa, int clamp, float p_floor,
+                                  __nv_bfloat16* __restrict__ uh, __nv_bfloat16* __restrict__ ul) {
+    const int ng = D / G;
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= M * ng) return;
+    const long long m = i / ng;
+    const int base = (int)(i % ng) * G;
+    const float* qb = q + m * 2 * D;
+    float qv[G], gq[G], dl[G];
+#pragma unroll
+    for (int j = 0; j < G; j += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(qb + base + j);
+        const float4 g = *reinterpret_cast<const float4*>(qb + D + base + j);
+        const float4 e = *reinterpret_cast<const float4*>(delta + base + j);
+        qv[j] = a.x, qv[j + 1] = a.y, qv[j + 2] = a.z, qv[j + 3] = a.w;
+        gq[j] = g.x, gq[j + 1] = g.y, gq[j + 2] = g.z, gq[j + 3] = g.w;
+        dl[j] = e.x, dl[j + 1] = e.y, dl[j + 2] = e.z, dl[j + 3] = e.w;
+    }
+    float uu[G], pp[G];
+#pragma unroll
+    for (int off = 0; off < G; ++off) {
+        const float g0 = gq[off], g1 = gq[(off + 1) % G], g2 = gq[(off + 2) % G];
+        uu[off] = qv[off] * (sigm(g0 - g1) * sigm(g0 - g2));
+        float p = 1.0f - dl[off] * (1.0f - sigm(g0));
+        if (clamp && p < p_floor) p = p_floor;
+        pp[off] = p;
+    }
+    const long long o = m * D + base;
+#pragma unroll
+    for (int j = 0; j < G; j += 4) {
+        *reinterpret_cast<float4*>(u + o + j) = make_float4(uu[j], uu[j + 1], uu[j + 2], uu[j + 3]);
+        *reinterpret_cast<float4*>(pa + o + j) = make_float4(pp[j], pp[j + 1], pp[j + 2], pp[j + 3]);
+    }
+    if (uh) {
+        __nv_bfloat16 h[G], l[G];
+#pragma unroll
+        for (int j = 0; j < G; ++j) {  // store_split's rounding
+            h[j] = __float2bfloat16_rn(uu[j]);
+            l[j] = __float2bfloat16_rn(uu[j] - __bfloat162float(h[j]));
+        }
+#pragma unroll
+        for (int j = 0; j < G; j += 4) {
+            *reinterpret_cast<uint2*>(uh + o + j) = *reinterpret_cast<const uint2*>(h + j);
+            *reinterpret_cast<uint2*>(ul + o + j) = *reinterpret_cast<const uint2*>(l + j);
+        }
+    }
+}
+
 // prev[b][t] = state before position t: s_in for t = 0, else states[b][t-1]
 __global__ void prev_kernel(int Tc, int D, long long total, const float* __restrict__ s0,
                             const float* __restrict__ st, float* __restrict__ prev) {
@@ -1171,10 +1226,21 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
         }
         {
             ProfScope ps("prefill_scan", st);
-            gate_chunk_kernel<<<eb, 256, 0, st>>>(M, D, m->G, m->cq, y.delta, m->cu, m->cp,
-                                                  m->clamp, m->p_floor,
-                                                  ctc ? m->c_u.hi : nullptr,
-                                                  ctc ? m->c_u.lo : nullptr);
+            __nv_bfloat16* uh = ctc ? m->c_u.hi : nullptr;
+            __nv_bfloat16* ul = ctc ? m->c_u.lo : nullptr;
+            const bool gvec = D % 8 == 0 && (uintptr_t)y.delta % 16 == 0 &&
+                              (uintptr_t)m->cq % 16 == 0 && (uintptr_t)m->cu % 16 == 0 &&
+                              (uintptr_t)m->cp % 16 == 0;
+            const unsigned gb = (unsigned)((M * D / 8 + 255) / 256);
+            if (gvec && m->G == 8)
+                gate_group_kernel<8><<<gb, 256, 0, st>>>(M, D, m->cq, y.delta, m->cu, m->cp,
+                                                         m->clamp, m->p_floor, uh, ul);
+            else if (gvec && m->G == 4)
+                gate_group_kernel<4><<<2 * gb, 256, 0, st>>>(M, D, m->cq, y.delta, m->cu, m->cp,
+                                                             m->clamp, m->p_floor, uh, ul);
+            else
+                gate_chunk_kernel<<<eb, 256, 0, st>>>(M, D, m->G, m->cq, y.delta, m->cu, m->cp,
+                                                      m->clamp, m->p_floor, uh, ul);
             if (ctc) {
                 // the layer's state rows read and written in place, the state
                 // entering each position written as Ws's input planes
