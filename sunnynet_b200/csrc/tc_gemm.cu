@@ -390,6 +390,12 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
 
     if (warp == 0) {  // --------------------------------------------- TMA producer
         if (lane == 0) {
+            // descriptors into the cache before the first copies (the A maps'
+            // first use comes after the wait for the previous kernel)
+            prefetch_tmap(&tah);
+            prefetch_tmap(&tal);
+            prefetch_tmap(&twh);
+            if (!I8) prefetch_tmap(&twl);
             const uint32_t bytes = 2 * C::A_BYTES + (I8 ? 1 : 2) * C::W_BYTES;
             // the weight tiles of the first S stages do not depend on the
             // previous kernel: in flight before waiting for it (programmatic

@@ -20,6 +20,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 }
 
 // 2-D tiled TMA load (no multicast) completing on `mbar`.
+// Fetch a tensor map (a kernel parameter or global memory) into the
+// descriptor cache ahead of its first TMA copy.
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* tm) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y,
                                             uint64_t* mbar) {
     asm volatile(

@@ -273,6 +273,8 @@ __global__ void __launch_bounds__(kW4Threads, 1)
             if ((int)blockIdx.x < ntiles) {
                 int pi, m0, n0;
                 w4_tile<BN>(gt, blockIdx.x, pi, m0, n0);
+                prefetch_tmap(&g.ta[pi]);  // first used after the wait below
+                prefetch_tmap(&g.tw[pi]);
                 for (int s = 0; s < pre; ++s) {
                     mbar_expect_tx(&full[s], C::A_BYTES + C::P_BYTES);
                     tma_load_2d(sP(s), &g.tw[pi], s * (kSlab / 2), n0, &full[s]);
