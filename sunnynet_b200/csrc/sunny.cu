@@ -287,6 +287,25 @@ __global__ void conv_chunk_kernel(int B, int Tc, int D, int K, int KH, int L, in
     else at[i] = a;
 }
 
+// ring_update_kernel with float4 copies (D % 4 == 0, 16-byte aligned rows),
+// launched with enough threads that each copies about one vector.
+__global__ void ring_update4_kernel(int Tc, int D, int KH, int L, int layer,
+                                    const float* __restrict__ raw, float* __restrict__ hist,
+                                    int32_t* __restrict__ pos) {
+    const int b = blockIdx.x;
+    const int p = pos[b * L + layer];
+    __syncthreads();
+    float* hb = hist + ((size_t)b * L + layer) * KH * D;
+    const int first = Tc > KH ? Tc - KH : 0, D4 = D >> 2;
+    for (int i = threadIdx.x; i < (Tc - first) * D4; i += blockDim.x) {
+        const int t = first + i / D4, d = (i % D4) * 4;
+        *reinterpret_cast<float4*>(hb + (size_t)(((p + t) % KH + KH) % KH) * D + d) =
+            *reinterpret_cast<const float4*>(raw + ((size_t)b * Tc + t) * D + d);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) pos[b * L + layer] = p + Tc;
+}
+
 // conv_chunk_kernel for four consecutive channels per thread (D % 4 == 0,
 // 16-byte aligned rows), writing the taps only as bf16 planes; the same
 // arithmetic per channel.
@@ -1199,9 +1218,15 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
                                                      m->hist, m->pos, y.dw, m->cat,
                                                      ctc ? m->c_at.hi : nullptr,
                                                      ctc ? m->c_at.lo : nullptr);
-            if (m->K > 1)
+            if (m->K > 1 && al16 && D % 4 == 0) {
+                const int v = (Tc < m->KH ? Tc : m->KH) * D / 4;
+                const int th = v < 1024 ? (v + 31) / 32 * 32 : 1024;
+                ring_update4_kernel<<<B, th, 0, st>>>(Tc, D, m->KH, L, l, m->craw, m->hist,
+                                                      m->pos);
+            } else if (m->K > 1) {
                 ring_update_kernel<<<B, 256, 0, st>>>(Tc, D, m->KH, L, l, m->craw, m->hist,
                                                       m->pos);
+            }
         }
         if (ctc) {  // inputs as producer-written planes; V writes U's
             GemmArgs gv = gemm((int)M, R, D, m->cat, y.V, y.sV, m->cv);
