@@ -41,7 +41,10 @@ constexpr int kTC = 128;  // rows per chunk
 template <int CW>
 struct ScanCfg {
     static constexpr int S = CW == 8 ? 12 : (CW == 16 ? 7 : 4);  // ring depth (~100-128 KB)
-    static constexpr size_t smem = 2ull * S * kTC * CW * sizeof(float) + 4ull * S * 8;
+    // a launch uses min(S, chunks) stages: short sequences keep more CTAs per SM
+    static size_t smem(int stages) {
+        return 2ull * stages * kTC * CW * sizeof(float) + 4ull * stages * 8;
+    }
 };
 
 __device__ __forceinline__ float rec_fused(float a, float s, float b) { return __fmaf_rn(a, s, b); }
@@ -96,8 +99,8 @@ __global__ void __launch_bounds__(128)
                       int nv, int gated, int vec, long long s0_ld, long long send_ld,
                       __nv_bfloat16* __restrict__ ph, __nv_bfloat16* __restrict__ pl,
                       int* err) {
-    constexpr int S = ScanCfg<CW>::S;
     constexpr int TILE = kTC * CW;
+    const int S = min(ScanCfg<CW>::S, (T + kTC - 1) / kTC);  // stages of this launch
     extern __shared__ __align__(128) unsigned char smem_raw[];
     float* sa = reinterpret_cast<float*>(smem_raw);
     float* sb = sa + S * TILE;
@@ -254,11 +257,12 @@ int launch_scan_cw(const float* a, const float* b, const float* s0, float* out, 
                    int B, int T, int N, int gated, int vec, long long s0_ld, long long send_ld,
                    __nv_bfloat16* ph, __nv_bfloat16* pl, cudaStream_t st) {
     static bool attr = false;
-    const size_t smem = ScanCfg<CW>::smem;
-    if (!attr) {
+    const int nch = (T + kTC - 1) / kTC;
+    const size_t smem = ScanCfg<CW>::smem(nch < ScanCfg<CW>::S ? nch : ScanCfg<CW>::S);
+    if (!attr) {  // the largest ring this kernel can take
         SN_TRY(cuda_check(cudaFuncSetAttribute(scan_exact_kernel<CW>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)smem),
+                                               (int)ScanCfg<CW>::smem(ScanCfg<CW>::S)),
                           "scan smem attr"));
         attr = true;
     }
