@@ -337,6 +337,8 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
     using C = TcCfg<BN, I8>;
     constexpr int S = C::S;
     constexpr int kEpiGroups = TcEpi<BN>::GROUPS;
+    // TMEM is allocated in powers of two columns (a 192-wide tile takes 256)
+    constexpr uint32_t kTmemCols = BN <= 32 ? 32u : (BN <= 64 ? 64u : (BN <= 128 ? 128u : 256u));
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     uint8_t* sb = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // 1024-B aligned ring
@@ -379,7 +381,7 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
     if (warp == 1) {  // TMEM accumulator: BN fp32 columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32((const void*)tmem_slot)),
-                     "r"((uint32_t)BN)
+                     "r"(kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -675,7 +677,7 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"((uint32_t)BN)
+                     "r"(kTmemCols)
                      : "memory");
     }
     if (ks > 1) {
@@ -768,7 +770,7 @@ int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
                           "tc smem"));
         attr = true;
     }
-    const int bi = BN == 32 ? 0 : (BN == 64 ? 1 : (BN == 128 ? 2 : 3));
+    const int bi = BN == 32 ? 0 : (BN == 64 ? 1 : (BN == 128 ? 2 : (BN == 256 ? 3 : 4)));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(((a.N + BN - 1) / BN) * ks), (unsigned)((a.M + BM - 1) / BM));
     cfg.blockDim = dim3(TcEpi<BN>::THREADS);
@@ -850,8 +852,8 @@ int tc_prepare(TcWeights* tw, const void* W, int wtype, int N, int K,
     if (!tw->hi || (!tw->int8 && !tw->lo)) return fail(SN_E_NOMEM, "tc weight planes");
     split_bf16_kernel<<<grid_blocks((long long)n), 256>>>(W, wtype, (long long)n, tw->hi, tw->lo);
     SN_TRY(cuda_check(cudaGetLastError(), "split launch"));
-    const int rows[4] = {32, 64, 128, 256};
-    for (int i = 0; i < 4; ++i) {
+    const int rows[5] = {32, 64, 128, 256, 192};  // weight tile heights (BN)
+    for (int i = 0; i < 5; ++i) {
         SN_TRY(encode_map(&tw->tm_hi[i], tw->hi, N, K, rows[i]));
         SN_TRY(encode_map(&tw->tm_lo[i], tw->int8 ? tw->hi : tw->lo, N, K, rows[i]));
     }
@@ -908,8 +910,11 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
                                                               : 32;
     int bn = 32, ks = 1;
     double best = 1e300;
-    for (int b : {32, 64, 128, 256}) {
+    for (int b : {32, 64, 128, 192, 256}) {
         if (ld && (ring ? b > 128 : b != bld)) continue;
+        // 192-wide tiles: two ring stages, and neither residual operands nor
+        // the bf16 planes of the result fit the drained ring for their epilogue
+        if (b == 192 && (ld || a.Ch != nullptr || tw.int8)) continue;
         const long long tiles = mt * ((a.N + b - 1) / b);
         const double slab = 2.0 * BM * 128 + (tw.int8 ? 1.0 : 2.0) * b * 128;
         const double fetch = ring && b > 32 ? narr * BM * b * 4.0 / 48.0 : 0.0;
@@ -927,6 +932,7 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
     }
 #define SN_TC_BN(I8, LD)                                                                  \
     return bn == 256   ? launch_bn<256, I8, LD>(a, tw, tah, tal, st, pdl, ks)              \
+           : bn == 192 ? launch_bn<192, I8, LD>(a, tw, tah, tal, st, pdl, ks)              \
            : bn == 128 ? launch_bn<128, I8, LD>(a, tw, tah, tal, st, pdl, ks)              \
                        : (bn == 64 ? launch_bn<64, I8, LD>(a, tw, tah, tal, st, pdl, ks)   \
                                    : launch_bn<32, I8, LD>(a, tw, tah, tal, st, pdl, ks))

@@ -22,8 +22,8 @@ struct TcWeights {
     bool int8 = false;                 // hi holds the exact int8 codes; no lo plane
     __nv_bfloat16* hi = nullptr;
     __nv_bfloat16* lo = nullptr;
-    CUtensorMap tm_hi[4];              // box rows 32 / 64 / 128 / 256
-    CUtensorMap tm_lo[4];
+    CUtensorMap tm_hi[5];              // box rows 32 / 64 / 128 / 256 / 192
+    CUtensorMap tm_lo[5];
     bool ready = false;
 };
 
