@@ -5,7 +5,7 @@ package and loads the reference C runtime built by oracle/Makefile into
 oracle/_ref). Outputs small files into tests/golden/; the tests then need
 neither the reference tree nor oracle/_ref.
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference checkout>
 
 What is pinned:
 * prims.npz      -- sn_recur_scan/step, sn_quant_i8/dequant_i8, sn_quant_i4/
@@ -318,7 +318,7 @@ def make_rwkv(out: Path, ref_root: Path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="root of the reference checkout")
     args = ap.parse_args()
     oracle.build()
     if not oracle.ref_available():
