@@ -21,6 +21,14 @@ int  sn_threads(void);                      /* recur.h:22 */
 /* recur.h:26-27; a, b, out (B,T,N); s0, send (B,N). Bit-identical to the reference. */
 void sn_recur_scan(const float* a, const float* b, const float* s0,
                    float* out, float* send, int B, int T, int N, int gated);
+/* recur.h:27-30: reverse pass over the scan's outputs. a, b, out, dout, da,
+ * db (B,T,N); s0, ds0 (B,N). With gated == 1, b holds u and da/db are the
+ * gradients w.r.t. a and u: da = ds*(s_prev - u), db = ds*(1 - a).
+ * Bit-identical to the reference (recur.c:51-107). */
+void sn_recur_bwd(const float* a, const float* b, const float* s0,
+                  const float* out, const float* dout,
+                  float* da, float* db, float* ds0,
+                  int B, int T, int N, int gated);
 /* recur.h:36: one step, s updated in place. */
 void sn_recur_step(const float* a, const float* b, float* s, int B, int N, int gated);
 /* recur.h:40-43: symmetric per-block INT8, block <= 0 = whole row. */

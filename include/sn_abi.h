@@ -42,6 +42,7 @@ extern "C" {
 #define SN_CAP_QUANT_I4     (1u << 6)  /* sn_abi_quant_i4 / dequant_i4 / gemv_i4 */
 #define SN_CAP_SUNNY        (1u << 7)  /* sn_abi_sunny_* whole-model handle */
 #define SN_CAP_BATCH        (1u << 8)  /* batched steps + state export/import */
+#define SN_CAP_RECUR_BWD    (1u << 9)  /* sn_abi_recur_bwd */
 
 /* Status codes (reference sn_abi.h:41-46, docs/ABI.md:55-68) */
 #define SN_OK              0
@@ -78,16 +79,28 @@ sn_status sn_abi_recur_scan(const float* a, const float* b, const float* s0,
  * device synchronisation cudaMalloc/cudaFree imply, a fixed memory budget.
  * It calls no allocator: its temporary records live in a fixed 2 MiB array
  * of the library's device image, held by every GPU that loads the library
- * until exit. Every array must be device memory; the work is enqueued on
- * `cuda_stream` (NULL = legacy default stream) and the call returns without
- * synchronising. Rejects B*N > 262144 with SN_E_INVAL. The first call on a
- * device looks up the array's device address (make it before any stream
- * capture). Calls that overlap on the GPU share the array and race: order
- * them on one stream. Nothing in the array needs to start at zero. */
+ * until exit. Every array must be memory of the current device (or managed
+ * memory); the work is enqueued on `cuda_stream` (NULL = legacy default
+ * stream) and the call returns without synchronising. Rejects B*N > 262144
+ * with SN_E_INVAL. The first call on a device looks up the array's device
+ * address (make it before any stream capture). Calls that overlap on the GPU
+ * share the array and race: order them on one stream. Nothing in the array
+ * needs to start at zero. A device wait that gives up (a GPU stalled for
+ * about a second) cannot change the returned status; it leaves the affected
+ * rows and final states NaN instead, so check `send` when that matters. */
 sn_status sn_abi_recur_scan_noalloc(const float* a, const float* b, const float* s0,
                                     float* out, float* send,
                                     int32_t B, int32_t T, int32_t N, int32_t gated,
                                     void* cuda_stream);
+/* ABI 1.1 (SN_CAP_RECUR_BWD): the stable, status-returning face of the
+ * reference's internal sn_recur_bwd (recur.h:27-30, recur.c:51-107), the
+ * reverse pass over the scan's outputs. a, b, out, dout, da, db (B,T,N); s0,
+ * ds0 (B,N); gated == 1: b holds u, da = ds*(s_prev - u), db = ds*(1 - a).
+ * Bit-identical to the reference. */
+sn_status sn_abi_recur_bwd(const float* a, const float* b, const float* s0,
+                           const float* out, const float* dout,
+                           float* da, float* db, float* ds0,
+                           int32_t B, int32_t T, int32_t N, int32_t gated);
 /* symmetric per-block INT8; block <= 0 means one block per row. sn_abi.h:83-86 */
 sn_status sn_abi_quant_i8(const float* x, int8_t* q, float* scale,
                           int32_t B, int32_t N, int32_t block);
@@ -117,6 +130,14 @@ int32_t   sn_abi_cuda_scan_mode(int32_t mode);        /* 0 exact (default), 1 ch
 sn_status sn_abi_cuda_profile(int32_t on);
 /* JSON {"family": [launches, total_ms], ...}; returns the length incl. NUL. */
 int32_t   sn_abi_cuda_profile_report(char* buf, int32_t buflen);
+/* Failure-path test hook (no reference counterpart). Runs one CTA that waits,
+ * through the library's bounded device waits, on something that never
+ * completes: kind 0 an mbarrier phase, kind 1 a grid barrier like the fused
+ * decode step's. After `cycles` SM cycles (1 .. 2^31; the step kernels use
+ * 2^31) the wait gives up and the kernel returns. Returns SN_E_DEVICE when
+ * the give-up was reported, as every model call does after a device wait
+ * times out; the library stays usable afterwards. */
+sn_status sn_abi_cuda_wait_selftest(int32_t kind, int64_t cycles);
 
 /* INT4 (SN_CAP_QUANT_I4), the stable-ABI face of the reference's internal
  * quant.h:20-27. scale_fp16 != 0 selects fp16 scales (group formats). */

@@ -29,9 +29,13 @@ _F = ctypes.POINTER(ctypes.c_float)
 _V, _I, _P = ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p
 
 
-def build(quiet: bool = True) -> None:
-    """Compile the restatement (and oracle/_ref when the reference is present)."""
-    r = subprocess.run(["make", "-C", str(HERE), "all"], capture_output=True, text=True)
+def build(quiet: bool = True, ref_root=None) -> None:
+    """Compile the restatement, and oracle/_ref from the reference's own runtime
+    sources when `ref_root` (the reference checkout) is given and present."""
+    cmd = ["make", "-C", str(HERE), "all"]
+    if ref_root is not None and (Path(ref_root) / "sunnynet" / "runtime").is_dir():
+        cmd.append(f"REF={Path(ref_root) / 'sunnynet' / 'runtime'}")
+    r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("oracle build failed:\n" + (r.stderr or r.stdout)[-2000:])
     if not quiet:
@@ -60,6 +64,7 @@ def lib():
     L = ctypes.CDLL(str(ORACLE_SO))
     L.or_recur_scan.argtypes = [_V, _V, _V, _V, _V, _I, _I, _I, _I]
     L.or_recur_step.argtypes = [_V, _V, _V, _I, _I, _I]
+    L.or_recur_bwd.argtypes = [_V, _V, _V, _V, _V, _V, _V, _V, _I, _I, _I, _I]
     L.or_quant_i8.argtypes = [_V, _V, _V, _I, _I, _I]
     L.or_dequant_i8.argtypes = [_V, _V, _V, _I, _I, _I]
     L.or_quant_i4.argtypes = [_V, _V, _V, _I, _I, _I, _I]
@@ -104,6 +109,7 @@ def ref_abi():
         L = ctypes.CDLL(str(REF_ABI_SO))
         L.sn_recur_scan.argtypes = [_V, _V, _V, _V, _V, _I, _I, _I, _I]
         L.sn_recur_step.argtypes = [_V, _V, _V, _I, _I, _I]
+        L.sn_recur_bwd.argtypes = [_V, _V, _V, _V, _V, _V, _V, _V, _I, _I, _I, _I]
         L.sn_quant_i8.argtypes = [_V, _V, _V, _I, _I, _I]
         L.sn_dequant_i8.argtypes = [_V, _V, _V, _I, _I, _I]
         L.sn_quant_i4.argtypes = [_V, _V, _V, _I, _I, _I]
@@ -160,6 +166,17 @@ def recur_scan(a, b, s0, gated):
     send = np.empty((B, N), np.float32)
     lib().or_recur_scan(ptr(a), ptr(b), ptr(s0), ptr(out), ptr(send), B, T, N, int(gated))
     return out, send
+
+
+def recur_bwd(a, b, s0, out, dout, gated):
+    """Reverse pass of the scan (reference recur.c:51-107) -> (da, db, ds0)."""
+    B, T, N = a.shape
+    da = np.empty_like(a)
+    db = np.empty_like(a)
+    ds0 = np.empty((B, N), np.float32)
+    lib().or_recur_bwd(ptr(a), ptr(b), ptr(s0), ptr(out), ptr(dout), ptr(da), ptr(db), ptr(ds0),
+                       B, T, N, int(gated))
+    return da, db, ds0
 
 
 def recur_step(a, b, s, gated):

@@ -119,6 +119,41 @@ void or_recur_scan(const float* a, const float* b, const float* s0, float* out,
     }
 }
 
+/* recur.c:51-107: reverse-time pass of the scan. Per channel, from t = T-1
+ * down to 0: g = dout_t + g (one rounding), da_t = g*(s_{t-1} - u_t) and
+ * db_t = g*(1 - a_t) for the gated form (da_t = g*s_{t-1}, db_t = g for the
+ * FMA form), then g = g*a_t. s_{-1} = s0; ds0 = g after t = 0. No FMA appears
+ * in either of the reference's paths (AVX2 lanes and the N%8 tail), so one
+ * rule serves every channel. */
+void or_recur_bwd(const float* a, const float* b, const float* s0, const float* out,
+                  const float* dout, float* da, float* db, float* ds0, int B, int T, int N,
+                  int gated) {
+#pragma omp parallel for schedule(static)
+    for (int bb = 0; bb < B; ++bb) {
+        const size_t base = (size_t)bb * T * N;
+        for (int d = 0; d < N; ++d) {
+            float g = 0.0f;
+            for (int t = T - 1; t >= 0; --t) {
+                const size_t o = base + (size_t)t * N + d;
+                g = dout[o] + g;
+                const float av = a[o];
+                const float sp = t > 0 ? out[o - N] : s0[(size_t)bb * N + d];
+                if (gated) {
+                    const float diff = sp - b[o];
+                    const float oma = 1.0f - av;
+                    da[o] = g * diff;
+                    db[o] = g * oma;
+                } else {
+                    da[o] = g * sp;
+                    db[o] = g;
+                }
+                g = g * av;
+            }
+            ds0[(size_t)bb * N + d] = g;
+        }
+    }
+}
+
 /* recur.c:109-131, same fused/unfused split as the scan. */
 void or_recur_step(const float* a, const float* b, float* s, int B, int N, int gated) {
     const int nv = N - N % 8;

@@ -21,6 +21,10 @@ extern "C" {
 /* ---- generic recurrence (reference sunnynet/runtime/recur.c) ---- */
 void or_recur_scan(const float* a, const float* b, const float* s0, float* out,
                    float* send, int B, int T, int N, int gated);
+/* reverse pass: a, b/u, out, dout, da, db (B,T,N); s0, ds0 (B,N) */
+void or_recur_bwd(const float* a, const float* b, const float* s0, const float* out,
+                  const float* dout, float* da, float* db, float* ds0, int B, int T, int N,
+                  int gated);
 void or_recur_step(const float* a, const float* b, float* s, int B, int N, int gated);
 void or_quant_i8(const float* x, int8_t* q, float* scale, int B, int N, int block);
 void or_dequant_i8(const int8_t* q, const float* scale, float* x, int B, int N, int block);

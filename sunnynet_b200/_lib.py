@@ -27,6 +27,7 @@ SIGNATURES = {
     "sn_abi_recur_step": (I32, [V, V, V, I32, I32, I32]),
     "sn_abi_recur_scan": (I32, [V, V, V, V, V, I32, I32, I32, I32]),
     "sn_abi_recur_scan_noalloc": (I32, [V, V, V, V, V, I32, I32, I32, I32, V]),
+    "sn_abi_recur_bwd": (I32, [V, V, V, V, V, V, V, V, I32, I32, I32, I32]),
     "sn_abi_quant_i8": (I32, [V, V, V, I32, I32, I32]),
     "sn_abi_dequant_i8": (I32, [V, V, V, I32, I32, I32]),
     "sn_abi_rwkv7_load": (V, [P]),
@@ -43,6 +44,7 @@ SIGNATURES = {
     "sn_abi_cuda_scan_mode": (I32, [I32]),
     "sn_abi_cuda_profile": (I32, [I32]),
     "sn_abi_cuda_profile_report": (I32, [P, I32]),
+    "sn_abi_cuda_wait_selftest": (I32, [I32, ctypes.c_int64]),
     "sn_abi_quant_i4": (I32, [V, V, V, I32, I32, I32, I32]),
     "sn_abi_dequant_i4": (I32, [V, V, V, I32, I32, I32, I32]),
     "sn_abi_gemv_i4": (I32, [V, V, V, V, I32, I32, I32, I32]),
@@ -68,6 +70,7 @@ SIGNATURES = {
     "sn_threads": (CI, []),
     "sn_recur_scan": (None, [V, V, V, V, V, CI, CI, CI, CI]),
     "sn_recur_step": (None, [V, V, V, CI, CI, CI]),
+    "sn_recur_bwd": (None, [V, V, V, V, V, V, V, V, CI, CI, CI, CI]),
     "sn_quant_i8": (None, [V, V, V, CI, CI, CI]),
     "sn_dequant_i8": (None, [V, V, V, CI, CI, CI]),
     # quant.h

@@ -28,7 +28,8 @@ int32_t sn_abi_version(void) { return SN_ABI_VERSION; }
 
 uint32_t sn_abi_caps(void) {
     return SN_CAP_RECUR_SCAN | SN_CAP_RECUR_STEP | SN_CAP_QUANT_I8 | SN_CAP_RWKV7 |
-           SN_CAP_THREADS | SN_CAP_CUDA | SN_CAP_QUANT_I4 | SN_CAP_SUNNY | SN_CAP_BATCH;
+           SN_CAP_THREADS | SN_CAP_CUDA | SN_CAP_QUANT_I4 | SN_CAP_SUNNY | SN_CAP_BATCH |
+           SN_CAP_RECUR_BWD;
 }
 
 sn_status sn_abi_check(int32_t caller_major) {

@@ -26,12 +26,16 @@ int launch_step(const float* a, const float* b, float* s, int B, int N, int gate
 // chunk per sequence needs more than `max_records`; <= 0 means no limit),
 // the float2 records it needs, and the three-kernel scan itself. The records
 // need no initial contents: every record is written before it is read within
-// the same call. prof_scopes=false keeps the profiler's events out.
+// the same call. prof_scopes=false keeps the profiler's events out. `err`:
+// the device error word a bounded wait that gives up sets (nullptr: the
+// runtime's mapped word). A CTA whose wait gave up leaves its uncomputed
+// outputs NaN (its chunk record, or its chunk's rows and final state), so the
+// failure also shows in the results.
 int scan_chunk_rows(int B, int T, int N, int num_sms, long long max_records);
 long long scan_chunk_records(int B, int T, int N, int L);
 int launch_scan_chunked(const float* a, const float* b, const float* s0, float* out,
                         float* send, int B, int T, int N, int gated, int L, float2* agg,
-                        cudaStream_t st, bool prof_scopes = true);
+                        cudaStream_t st, bool prof_scopes = true, int* err = nullptr);
 // Y (nseq,out) = W4A8(X (nseq,in)) with codes (out,in/2) and scales (out,in/block).
 // pdl: launched with programmatic serialization (the kernels wait for the
 // previous one before reading their input; weights may be fetched earlier).

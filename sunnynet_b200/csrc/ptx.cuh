@@ -35,19 +35,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for phase `parity` of an mbarrier, giving up after ~2^31 SM cycles
-// (about a second). On give-up the error word is set and false is returned;
-// callers then leave their loops so the kernel always terminates.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err) {
+// Default bound of every device wait: 2^31 SM cycles (about a second).
+constexpr long long kWaitCycles = 1ll << 31;
+
+// Wait for phase `parity` of an mbarrier, giving up after `limit` SM cycles.
+// On give-up the error word is set and false is returned; callers then leave
+// their loops so the kernel always terminates.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* b, uint32_t parity, int* err,
+                                              long long limit) {
     if (mbar_try_wait(b, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(b, parity)) {
-        if (clock64() - t0 > (1ll << 31)) {
+        if (clock64() - t0 > limit) {
             if (err) atomicExch(err, 1);
             return false;
         }
     }
     return true;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* err) {
+    return mbar_wait_for(b, parity, err, kWaitCycles);
 }
 
 // 16-byte async global->shared copy; src_bytes < 16 zero-fills the rest.

@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(128)
     if (warp == 0) {  // ---------------------------------------------- loader
         for (int c = 0; c < nch; ++c) {
             const int st = c % S;
-            if (c >= S && !mbar_wait(&empty[st], ((c / S) - 1) & 1, err)) break;
+            if (c >= S && !__all_sync(~0u, mbar_wait(&empty[st], ((c / S) - 1) & 1, err))) break;
             const int t0 = c * kTC;
             float* da = sa + st * TILE;
             float* db = sb + st * TILE;
@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(128)
     } else if (warp == 1) {  // --------------------------------------- helper
         for (int c = 0; c < nch; ++c) {
             const int st = c % S;
-            if (!mbar_wait(&full[st], (c / S) & 1, err)) break;
+            if (!__all_sync(~0u, mbar_wait(&full[st], (c / S) & 1, err))) break;
             if (gated) {
                 float4* da = reinterpret_cast<float4*>(sa + st * TILE);
                 float4* db = reinterpret_cast<float4*>(sb + st * TILE);
@@ -188,7 +188,10 @@ __global__ void __launch_bounds__(128)
         const bool fused = d < nv;
         for (int c = 0; c < nch; ++c) {
             const int st = c % S;
-            if (!mbar_wait(&ready[st], (c / S) & 1, err)) break;
+            if (!__all_sync(~0u, mbar_wait(&ready[st], (c / S) & 1, err))) {
+                s = __int_as_float(0x7fc00000);  // the final state is unknown
+                break;
+            }
             const int rows = min(kTC, T - c * kTC);
             if (lane < CW) {
                 const float* pa = sa + st * TILE + lane;
@@ -209,7 +212,7 @@ __global__ void __launch_bounds__(128)
     } else {  // ------------------------------------------------------ storer
         for (int c = 0; c < nch; ++c) {
             const int st = c % S;
-            if (!mbar_wait(&done[st], (c / S) & 1, err)) break;
+            if (!__all_sync(~0u, mbar_wait(&done[st], (c / S) & 1, err))) break;
             const int t0 = c * kTC;
             const int rows = min(kTC, T - t0);
             const float* db = sb + st * TILE;
@@ -287,6 +290,251 @@ int pick_cw(int B, int N) {
     return 8;
 }
 
+// ------------------------------------------------------- reverse pass (bwd)
+// sn_recur_bwd (reference recur.c:51-107). Per channel, from t = T-1 down to
+// 0: g = dout_t + g, then da_t = g*(s_{t-1} - u_t) and db_t = g*(1 - a_t) for
+// the gated form (da_t = g*s_{t-1}, db_t = g for the FMA form), then
+// g = g*a_t; s_{-1} = s0 and ds0 = g after t = 0. The reference rounds every
+// operation separately, in its AVX2 lanes and in its N%8 scalar tail alike,
+// so one rule with explicit round-to-nearest operations is bit-exact for
+// every channel.
+//
+// Layout: one CTA owns CW adjacent channels of one sequence and walks T
+// backwards in chunks of kBT rows through an S-deep ring of four row tiles
+// (a, b/u, the state entering each row, dout):
+//   warp 0     loader    cp.async of the four tiles; the state entering row t
+//                        is out row t-1, or s0 for t = 0
+//   warp 1     chain     lane = channel: g = dout + g, written over dout; g *= a
+//   warps 2-3  epilogue  da, db from g, a, b and the entering state; row stores
+// Stages are handed on with mbarriers (full: loader -> chain, done: chain ->
+// epilogue, empty: epilogue -> loader); every wait is bounded and a warp that
+// gives up leaves its loop (the chain then reports ds0 as NaN).
+constexpr int kBT = 64;  // rows per chunk of the reverse walk
+
+template <int CW>
+struct BwdCfg {
+    static constexpr int S = CW == 8 ? 12 : (CW == 16 ? 6 : 4);  // ring depth (~96-128 KB)
+    static size_t smem(int stages) {
+        return 4ull * stages * kBT * CW * sizeof(float) + 3ull * stages * 8;
+    }
+};
+
+// kBT rows of one channel (stride CW), walked from the last row down: g =
+// dout + g written over dout, g *= a. The next 16 rows are read into
+// registers before the current 16 are chained.
+template <int CW>
+__device__ __forceinline__ float bwd_chain(const float* __restrict__ pa, float* __restrict__ pg,
+                                           float g) {
+    constexpr int G = 16, NG = kBT / G;
+    float ca[G], cg[G];
+#pragma unroll
+    for (int j = 0; j < G; ++j) {
+        ca[j] = pa[((NG - 1) * G + j) * CW];
+        cg[j] = pg[((NG - 1) * G + j) * CW];
+    }
+#pragma unroll
+    for (int gi = NG - 1; gi >= 0; --gi) {
+        float na[G], ng[G];
+        if (gi > 0) {
+#pragma unroll
+            for (int j = 0; j < G; ++j) {
+                na[j] = pa[((gi - 1) * G + j) * CW];
+                ng[j] = pg[((gi - 1) * G + j) * CW];
+            }
+        }
+#pragma unroll
+        for (int j = G - 1; j >= 0; --j) {
+            g = __fadd_rn(cg[j], g);
+            pg[(gi * G + j) * CW] = g;
+            g = __fmul_rn(g, ca[j]);
+        }
+        if (gi > 0) {
+#pragma unroll
+            for (int j = 0; j < G; ++j) {
+                ca[j] = na[j];
+                cg[j] = ng[j];
+            }
+        }
+    }
+    return g;
+}
+
+__device__ __forceinline__ void bwd_grads(float g, float av, float bv, float sp, int gated,
+                                          float* x, float* y) {
+    if (gated) {
+        *x = __fmul_rn(g, __fsub_rn(sp, bv));
+        *y = __fmul_rn(g, __fsub_rn(1.0f, av));
+    } else {
+        *x = __fmul_rn(g, sp);
+        *y = g;
+    }
+}
+
+template <int CW>
+__global__ void __launch_bounds__(128)
+    scan_bwd_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                    const float* __restrict__ s0, const float* __restrict__ out,
+                    const float* __restrict__ dout, float* __restrict__ da,
+                    float* __restrict__ db, float* __restrict__ ds0, int T, int N, int gated,
+                    int vec, int* err) {
+    constexpr int TILE = kBT * CW;
+    const int nch = (T + kBT - 1) / kBT;
+    const int S = min(BwdCfg<CW>::S, nch);  // stages of this launch
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    float* ta = reinterpret_cast<float*>(smem_raw);  // [S][TILE] a
+    float* tb = ta + S * TILE;                       // b (u when gated)
+    float* tp = tb + S * TILE;                       // the state entering each row
+    float* tg = tp + S * TILE;                       // dout, then g
+    uint64_t* full = reinterpret_cast<uint64_t*>(tg + S * TILE);
+    uint64_t* done = full + S;
+    uint64_t* empty = done + S;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bb = blockIdx.y, d0 = blockIdx.x * CW;
+    const size_t base = (size_t)bb * T * N;
+    const float* s0b = s0 + (size_t)bb * N;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 32);
+            mbar_init(&done[i], 32);
+            mbar_init(&empty[i], 64);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    // step k of the walk handles chunk nch-1-k of the sequence, in stage k % S
+    if (warp == 0) {  // ---------------------------------------------- loader
+        for (int k = 0; k < nch; ++k) {
+            const int st = k % S;
+            if (k >= S && !__all_sync(~0u, mbar_wait(&empty[st], ((k / S) - 1) & 1, err))) break;
+            const int t0 = (nch - 1 - k) * kBT;
+            float* pa = ta + st * TILE;
+            float* pb = tb + st * TILE;
+            float* pp = tp + st * TILE;
+            float* pg = tg + st * TILE;
+            if (vec) {
+                constexpr int Q = CW / 4;
+#pragma unroll 2
+                for (int i = lane; i < kBT * Q; i += 32) {
+                    const int r = i / Q, q = i % Q;
+                    const int t = t0 + r, d = d0 + 4 * q;
+                    const bool ok = t < T && d < N;
+                    const size_t off = ok ? base + (size_t)t * N + d : 0;
+                    const float* ps = !ok ? a : (t > 0 ? out + off - N : s0b + d);
+                    const uint32_t n = ok ? 16u : 0u;
+                    cp_async16(pa + r * CW + 4 * q, a + off, n);
+                    cp_async16(pb + r * CW + 4 * q, b + off, n);
+                    cp_async16(pp + r * CW + 4 * q, ps, n);
+                    cp_async16(pg + r * CW + 4 * q, dout + off, n);
+                }
+            } else {
+                for (int i = lane; i < TILE; i += 32) {
+                    const int r = i / CW, ch = i % CW;
+                    const int t = t0 + r, d = d0 + ch;
+                    const bool ok = t < T && d < N;
+                    const size_t off = ok ? base + (size_t)t * N + d : 0;
+                    const float* ps = !ok ? a : (t > 0 ? out + off - N : s0b + d);
+                    const uint32_t n = ok ? 4u : 0u;
+                    cp_async4(pa + i, a + off, n);
+                    cp_async4(pb + i, b + off, n);
+                    cp_async4(pp + i, ps, n);
+                    cp_async4(pg + i, dout + off, n);
+                }
+            }
+            cp_async_arrive(&full[st]);
+        }
+        cp_async_wait_all();
+    } else if (warp == 1) {  // ---------------------------------------- chain
+        const int d = d0 + lane;
+        float g = 0.0f;
+        for (int k = 0; k < nch; ++k) {
+            const int st = k % S;
+            if (!__all_sync(~0u, mbar_wait(&full[st], (k / S) & 1, err))) {
+                g = __int_as_float(0x7fc00000);  // the gradient of s0 is unknown
+                break;
+            }
+            const int rows = min(kBT, T - (nch - 1 - k) * kBT);
+            if (lane < CW) {
+                const float* pa = ta + st * TILE + lane;
+                float* pg = tg + st * TILE + lane;
+                if (rows == kBT) {
+                    g = bwd_chain<CW>(pa, pg, g);
+                } else {
+                    for (int r = rows - 1; r >= 0; --r) {
+                        g = __fadd_rn(pg[r * CW], g);
+                        pg[r * CW] = g;
+                        g = __fmul_rn(g, pa[r * CW]);
+                    }
+                }
+            }
+            mbar_arrive(&done[st]);
+        }
+        if (lane < CW && d < N) ds0[(size_t)bb * N + d] = g;
+    } else {  // ------------------------------------------------------ epilogue
+        const int e = threadIdx.x - 64;
+        for (int k = 0; k < nch; ++k) {
+            const int st = k % S;
+            if (!__all_sync(~0u, mbar_wait(&done[st], (k / S) & 1, err))) break;
+            const int t0 = (nch - 1 - k) * kBT;
+            const int rows = min(kBT, T - t0);
+            const float* pa = ta + st * TILE;
+            const float* pb = tb + st * TILE;
+            const float* pp = tp + st * TILE;
+            const float* pg = tg + st * TILE;
+            if (vec) {
+                constexpr int Q = CW / 4;
+                for (int i = e; i < rows * Q; i += 64) {
+                    const int r = i / Q, q = i % Q;
+                    const int d = d0 + 4 * q;
+                    if (d >= N) continue;
+                    const int j = r * CW + 4 * q;
+                    const float4 G4 = *reinterpret_cast<const float4*>(pg + j);
+                    const float4 A4 = *reinterpret_cast<const float4*>(pa + j);
+                    const float4 B4 = *reinterpret_cast<const float4*>(pb + j);
+                    const float4 P4 = *reinterpret_cast<const float4*>(pp + j);
+                    float4 X, Y;
+                    bwd_grads(G4.x, A4.x, B4.x, P4.x, gated, &X.x, &Y.x);
+                    bwd_grads(G4.y, A4.y, B4.y, P4.y, gated, &X.y, &Y.y);
+                    bwd_grads(G4.z, A4.z, B4.z, P4.z, gated, &X.z, &Y.z);
+                    bwd_grads(G4.w, A4.w, B4.w, P4.w, gated, &X.w, &Y.w);
+                    const size_t o = base + (size_t)(t0 + r) * N + d;
+                    *reinterpret_cast<float4*>(da + o) = X;
+                    *reinterpret_cast<float4*>(db + o) = Y;
+                }
+            } else {
+                for (int i = e; i < rows * CW; i += 64) {
+                    const int r = i / CW, ch = i % CW;
+                    const int d = d0 + ch;
+                    if (d >= N) continue;
+                    float x, y;
+                    bwd_grads(pg[i], pa[i], pb[i], pp[i], gated, &x, &y);
+                    const size_t o = base + (size_t)(t0 + r) * N + d;
+                    da[o] = x;
+                    db[o] = y;
+                }
+            }
+            mbar_arrive(&empty[st]);
+        }
+    }
+}
+
+template <int CW>
+int launch_bwd_cw(const float* a, const float* b, const float* s0, const float* out,
+                  const float* dout, float* da, float* db, float* ds0, int B, int T, int N,
+                  int gated, int vec, cudaStream_t st) {
+    static const cudaError_t attr_rc = cudaFuncSetAttribute(  // the largest ring, once
+        scan_bwd_kernel<CW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        (int)BwdCfg<CW>::smem(BwdCfg<CW>::S));
+    SN_TRY(cuda_check(attr_rc, "scan bwd smem attr"));
+    const int nch = (T + kBT - 1) / kBT;
+    const size_t smem = BwdCfg<CW>::smem(nch < BwdCfg<CW>::S ? nch : BwdCfg<CW>::S);
+    dim3 grid((N + CW - 1) / CW, B);
+    scan_bwd_kernel<CW><<<grid, 128, smem, st>>>(a, b, s0, out, dout, da, db, ds0, T, N, gated,
+                                                 vec, rt().d_err);
+    return cuda_check(cudaGetLastError(), "scan bwd launch");
+}
+
 }  // namespace
 
 // Device-pointer scan used by the ABI entry points and by the model code.
@@ -307,6 +555,21 @@ int launch_scan_strided(const float* a, const float* b, const float* s0, long lo
         case 32: return launch_scan_cw<32>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st);
         case 16: return launch_scan_cw<16>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st);
         default: return launch_scan_cw<8>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st);
+    }
+}
+
+// Reverse pass of the scan on device arrays (sn_recur_bwd).
+int launch_scan_bwd(const float* a, const float* b, const float* s0, const float* out,
+                    const float* dout, float* da, float* db, float* ds0, int B, int T, int N,
+                    int gated, cudaStream_t st) {
+    if (B > 65535) return fail(SN_E_INVAL, "recur_bwd: B=%d exceeds 65535", B);
+    auto al = [](const void* p) { return (uintptr_t)p % 16 == 0; };
+    const int vec = N % 4 == 0 && al(a) && al(b) && al(s0) && al(out) && al(dout) && al(da) &&
+                    al(db);
+    switch (pick_cw(B, N)) {
+        case 32: return launch_bwd_cw<32>(a, b, s0, out, dout, da, db, ds0, B, T, N, gated, vec, st);
+        case 16: return launch_bwd_cw<16>(a, b, s0, out, dout, da, db, ds0, B, T, N, gated, vec, st);
+        default: return launch_bwd_cw<8>(a, b, s0, out, dout, da, db, ds0, B, T, N, gated, vec, st);
     }
 }
 
@@ -398,6 +661,22 @@ __device__ __forceinline__ void issue_round(float* buf, const CUtensorMap* ta,
     }
 }
 
+// Wait for round k (buffer k & 1) of the two-buffer TMA pipeline. The
+// outcome is the same for every thread of the CTA: when any thread's bounded
+// wait gave up, thread 0 first waits (bounded again) for the rounds still in
+// flight into this CTA's shared memory, rounds k and k + 1, so no copy lands
+// after the CTA has left; then all threads return true together.
+__device__ __forceinline__ bool round_gave_up(uint64_t* bars, int k, int nr, int* err) {
+    const bool bad = !mbar_wait(&bars[k & 1], (uint32_t)((k >> 1) & 1), err);
+    if (!__syncthreads_or(bad)) return false;
+    if (threadIdx.x == 0) {
+        mbar_wait(&bars[k & 1], (uint32_t)((k >> 1) & 1), nullptr);
+        if (k + 1 < nr) mbar_wait(&bars[(k + 1) & 1], (uint32_t)(((k + 1) >> 1) & 1), nullptr);
+    }
+    __syncthreads();
+    return true;
+}
+
 __global__ void __launch_bounds__(256)
     scan_agg_kernel(const float* __restrict__ a, const float* __restrict__ b,
                     float2* __restrict__ agg, int T, int N, int nv, int L, int nch, int gated,
@@ -430,7 +709,10 @@ __global__ void __launch_bounds__(256)
         __syncthreads();  // barriers initialised before anyone waits
         for (int k = 0; k < nr; ++k) {
             const int j = k & 1;
-            mbar_wait(&bars[j], (uint32_t)((k >> 1) & 1), err);
+            if (round_gave_up(bars, k, nr, err)) {  // the chunk's map is unknown
+                A = Bc = __int_as_float(0x7fc00000);
+                break;
+            }
             const float* ra = stile + j * kBufF;
             const float* rb = ra + kRound * kScanTile;
             const int rs = min(kRound, rows - k * kRound);
@@ -553,7 +835,13 @@ __global__ void __launch_bounds__(256)
         s = n < N ? ld_cg(&agg[((size_t)sq * nch + c) * N + n]).x : 0.0f;
         for (int k = 0; k < nr; ++k) {
             const int j = k & 1;
-            mbar_wait(&bars[j], (uint32_t)((k >> 1) & 1), err);
+            if (round_gave_up(bars, k, nr, err)) {
+                // rows from this round on stay uncomputed: mark them NaN
+                s = __int_as_float(0x7fc00000);
+                if (n < N)
+                    for (int r = k * kRound; r < rows; ++r) out[base + (size_t)r * N + n] = s;
+                break;
+            }
             float* ra = stile + j * kBufF;
             const float* rb = ra + kRound * kScanTile;
             const int rs = min(kRound, rows - k * kRound);
@@ -638,7 +926,8 @@ long long scan_chunk_records(int B, int T, int N, int L) {
 
 int launch_scan_chunked(const float* a, const float* b, const float* s0, float* out,
                         float* send, int B, int T, int N, int gated, int L, float2* agg,
-                        cudaStream_t st, bool prof_scopes) {
+                        cudaStream_t st, bool prof_scopes, int* err) {
+    if (!err) err = rt().d_err;
     if (B > 65535) return fail(SN_E_INVAL, "recur_scan: B=%d exceeds 65535", B);
     if (L <= 0 || L > T) return fail(SN_E_INVAL, "recur_scan: bad chunk length %d", L);
     const int nch = (T + L - 1) / L;
@@ -674,7 +963,7 @@ int launch_scan_chunked(const float* a, const float* b, const float* s0, float* 
     {
         ProfScope ps(prof_scopes ? "scan_agg" : nullptr, st);
         scan_agg_kernel<<<grid, tpb, smem, st>>>(a, b, agg, T, N, nv, L, nch, gated, vec, ta, tb,
-                                                 tma, rt().d_err);
+                                                 tma, err);
         SN_TRY(cuda_check(cudaGetLastError(), "scan agg launch"));
     }
     {
@@ -687,7 +976,7 @@ int launch_scan_chunked(const float* a, const float* b, const float* s0, float* 
         ProfScope ps(prof_scopes ? "scan_apply" : nullptr, st);
         SN_TRY(cuda_check(launch_pdl(scan_apply_kernel, grid, dim3(tpb), smem, st, a, b,
                                      (const float2*)agg, out, send, T, N, nv, L, nch, gated,
-                                     vec, ta, tb, tma, rt().d_err),
+                                     vec, ta, tb, tma, err),
                           "scan apply launch"));
     }
     return SN_OK;
@@ -792,6 +1081,32 @@ int do_scan(const float* a, const float* b, const float* s0, float* out, float* 
     return finish(O.host || SE.host || A.dev != a || Bv.dev != b || S0.dev != s0);
 }
 
+int do_bwd(const float* a, const float* b, const float* s0, const float* out, const float* dout,
+           float* da, float* db, float* ds0, int B, int T, int N, int gated) {
+    if (!a || !b || !s0 || !out || !dout || !da || !db || !ds0 || B <= 0 || T <= 0 || N <= 0)
+        return fail(SN_E_INVAL, "recur_bwd: null pointer or non-positive dimension");
+    SN_TRY(ensure_init());
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    const size_t big = (size_t)B * T * N * sizeof(float), small = (size_t)B * N * sizeof(float);
+    Arr A, Bv, S0, O, DO, DA, DB, D0;
+    SN_TRY(stage_in(a, big, 0, &A));
+    SN_TRY(stage_in(b, big, 1, &Bv));
+    SN_TRY(stage_in(s0, small, 2, &S0));
+    SN_TRY(stage_in(out, big, 3, &O));
+    SN_TRY(stage_in(dout, big, 4, &DO));
+    SN_TRY(stage_out(da, big, 5, &DA));
+    SN_TRY(stage_out(db, big, 6, &DB));
+    SN_TRY(stage_out(ds0, small, 7, &D0));
+    SN_TRY(launch_scan_bwd((const float*)A.dev, (const float*)Bv.dev, (const float*)S0.dev,
+                           (const float*)O.dev, (const float*)DO.dev, (float*)DA.dev,
+                           (float*)DB.dev, (float*)D0.dev, B, T, N, gated ? 1 : 0, stream()));
+    SN_TRY(copy_back(DA));
+    SN_TRY(copy_back(DB));
+    SN_TRY(copy_back(D0));
+    return finish(DA.host || DB.host || D0.host || A.dev != a || Bv.dev != b || S0.dev != s0 ||
+                  O.dev != out || DO.dev != dout);
+}
+
 int do_step(const float* a, const float* b, float* s, int B, int N, int gated) {
     if (!a || !b || !s || B <= 0 || N <= 0)
         return fail(SN_E_INVAL, "recur_step: null pointer or non-positive dimension");
@@ -857,6 +1172,12 @@ sn_status sn_abi_recur_scan(const float* a, const float* b, const float* s0, flo
     return do_scan(a, b, s0, out, send, B, T, N, gated);
 }
 
+sn_status sn_abi_recur_bwd(const float* a, const float* b, const float* s0, const float* out,
+                           const float* dout, float* da, float* db, float* ds0, int32_t B,
+                           int32_t T, int32_t N, int32_t gated) {
+    return do_bwd(a, b, s0, out, dout, da, db, ds0, B, T, N, gated);
+}
+
 sn_status sn_abi_recur_step(const float* a, const float* b, float* s, int32_t B, int32_t N,
                             int32_t gated) {
     return do_step(a, b, s, B, N, gated);
@@ -881,6 +1202,12 @@ void sn_recur_scan(const float* a, const float* b, const float* s0, float* out, 
 
 void sn_recur_step(const float* a, const float* b, float* s, int B, int N, int gated) {
     do_step(a, b, s, B, N, gated);
+}
+
+void sn_recur_bwd(const float* a, const float* b, const float* s0, const float* out,
+                  const float* dout, float* da, float* db, float* ds0, int B, int T, int N,
+                  int gated) {
+    do_bwd(a, b, s0, out, dout, da, db, ds0, B, T, N, gated);
 }
 
 void sn_quant_i8(const float* x, signed char* q, float* scale, int B, int N, int block) {

@@ -40,6 +40,22 @@
 // the chunk, and the rows are re-run from it with the reference's per-row
 // rule. Outputs differ from the sequential (mode 0, bit-exact) scan by a few
 // ulp of the state per chunk boundary.
+//
+// Device-side failures. The kernels' waits on their shared-memory copies are
+// bounded (about a second). A wait can only give up on a GPU that stalls that
+// long, and this call has returned SN_OK by then: its status is decided when
+// the work is enqueued. So a give-up is reported in the results: the CTA
+// waits for its copies still in flight, marks what it leaves uncomputed as NaN
+// (its chunk's summary, which turns every later row and final state of those
+// channels NaN, or its chunk's remaining rows and final state) and returns.
+// It also sets a second fixed device word of this file (g_noalloc_err), never
+// the library's shared error word, so no later call of the regular entry
+// points reports a failure that was not theirs. The word is not cleared and
+// nothing reads it back: a NaN in `send` is the signal a caller checks.
+//
+// Devices. Every array must be memory of the current device (or managed
+// memory): an array of another GPU would make the kernels read that GPU's
+// memory across NVLink, or fault without peer access.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -55,9 +71,11 @@ constexpr long long kRecords = 1ll << 18;  // float2 records: 2 MiB
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float2 g_scan_records[kRecords];
+static __device__ int g_noalloc_err;
 
 struct DeviceSlot {
     float2* records = nullptr;  // device address of g_scan_records on this device
+    int* err = nullptr;         // device address of g_noalloc_err on this device
     int num_sms = 0;
 };
 DeviceSlot g_slots[kMaxDevices];
@@ -78,22 +96,29 @@ int setup_device(int dev, DeviceSlot** out) {
             return fail(SN_E_UNSUPPORTED, "recur_scan_noalloc: device %d is sm_%d0; this build "
                         "targets sm_100a", dev, major);
         void* p = nullptr;
+        void* e = nullptr;
         SN_TRY(cuda_check(cudaGetSymbolAddress(&p, g_scan_records),
                           "recur_scan_noalloc: cudaGetSymbolAddress of the fixed scratch"));
+        SN_TRY(cuda_check(cudaGetSymbolAddress(&e, g_noalloc_err),
+                          "recur_scan_noalloc: cudaGetSymbolAddress of the error word"));
         s.num_sms = sms;
+        s.err = static_cast<int*>(e);
         s.records = static_cast<float2*>(p);
     }
     *out = &s;
     return SN_OK;
 }
 
-bool on_device(const void* p) {
+// Memory the kernels on device `dev` may read and write directly: that
+// device's own allocations, or managed memory.
+bool on_device(const void* p, int dev) {
     cudaPointerAttributes at;
     if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
         cudaGetLastError();
         return false;
     }
-    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+    return at.type == cudaMemoryTypeManaged ||
+           (at.type == cudaMemoryTypeDevice && at.device == dev);
 }
 
 }  // namespace
@@ -117,12 +142,14 @@ extern "C" sn_status sn_abi_recur_scan_noalloc(const float* a, const float* b, c
         return fail(SN_E_UNSUPPORTED, "recur_scan_noalloc: device ordinal %d", dev);
     DeviceSlot* slot = nullptr;
     SN_TRY(setup_device(dev, &slot));
-    if (!on_device(a) || !on_device(b) || !on_device(s0) || !on_device(out) || !on_device(send))
-        return fail(SN_E_INVAL, "recur_scan_noalloc: every array must be device memory (host "
-                    "arrays would need staging buffers, i.e. an allocation)");
+    if (!on_device(a, dev) || !on_device(b, dev) || !on_device(s0, dev) ||
+        !on_device(out, dev) || !on_device(send, dev))
+        return fail(SN_E_INVAL, "recur_scan_noalloc: every array must be device memory of the "
+                    "current device %d (host arrays would need staging buffers, i.e. an "
+                    "allocation; another GPU's arrays would be read across NVLink)", dev);
     const int L = scan_chunk_rows(B, T, N, slot->num_sms, kRecords);
     if (L <= 0)
         return fail(SN_E_INVAL, "recur_scan_noalloc: shape does not fit the fixed scratch");
     return launch_scan_chunked(a, b, s0, out, send, B, T, N, gated ? 1 : 0, L, slot->records,
-                               static_cast<cudaStream_t>(cuda_stream), false);
+                               static_cast<cudaStream_t>(cuda_stream), false, slot->err);
 }

@@ -82,8 +82,11 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// Barrier k of this launch; false when the step is being abandoned.
-__device__ bool grid_sync(unsigned* bar, unsigned k, int* err) {
+// Barrier k of this launch; false when the step is being abandoned. A CTA
+// gives up after `limit` SM cycles (default about a second), raises the
+// abort flag so the others leave at their barrier too, and records
+// kErrWaitTimeout in the error word.
+__device__ bool grid_sync(unsigned* bar, unsigned k, int* err, long long limit = kWaitCycles) {
     __shared__ int ok;
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -98,7 +101,7 @@ __device__ bool grid_sync(unsigned* bar, unsigned k, int* err) {
                     res = 0;
                     break;
                 }
-                if (clock64() - t0 > (1ll << 31)) {
+                if (clock64() - t0 > limit) {
                     atomicExch(bar + kBarAbort, 1u);
                     atomicExch(err, kErrWaitTimeout);
                     res = 0;
@@ -942,3 +945,50 @@ int launch_sunny_fused(const FusedArgs& a, cudaStream_t st) {
 }
 
 }  // namespace sn
+
+// ------------------------------------------------- failure-path self-test
+// One CTA waits on something nothing will ever complete, through the same
+// bounded waits the step kernels use: kind 0 an mbarrier phase no thread
+// arrives on, kind 1 a grid barrier (grid_sync) whose arrival target one CTA
+// can never reach. The wait gives up after `limit` cycles, records
+// kErrWaitTimeout in the error word and the kernel returns, so the host sees
+// SN_E_DEVICE and the context stays usable. Nothing is in flight when it
+// gives up: no copies, no TMEM.
+namespace sn {
+namespace {
+
+__device__ unsigned g_selftest_bar[kBarWords];
+
+__global__ void wait_selftest_kernel(int kind, long long limit, int* err) {
+    __shared__ __align__(8) uint64_t mb;
+    if (kind == 0) {
+        if (threadIdx.x == 0) {
+            mbar_init(&mb, 1);
+            fence_mbar_init();
+        }
+        __syncthreads();
+        mbar_wait_for(&mb, 0, err, limit);  // phase 0 never completes
+    } else {
+        if (threadIdx.x == 0) {
+            g_selftest_bar[0] = 0u;
+            g_selftest_bar[kBarAbort] = 0u;
+            __threadfence();
+        }
+        // barrier 3 of a one-CTA grid wants 4 arrivals; only 1 comes
+        grid_sync(g_selftest_bar, 3u, err, limit);
+    }
+}
+
+}  // namespace
+}  // namespace sn
+
+extern "C" sn_status sn_abi_cuda_wait_selftest(int32_t kind, int64_t cycles) {
+    using namespace sn;
+    if (kind != 0 && kind != 1) return fail(SN_E_INVAL, "wait_selftest: kind must be 0 or 1");
+    if (cycles < 1 || cycles > kWaitCycles)
+        return fail(SN_E_INVAL, "wait_selftest: cycles must be in [1, 2^31]");
+    SN_TRY(ensure_init());
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    wait_selftest_kernel<<<1, 32, 0, stream()>>>(kind, (long long)cycles, rt().d_err);
+    return finish(true);
+}

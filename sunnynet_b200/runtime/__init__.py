@@ -17,7 +17,8 @@ import numpy as np
 from .. import _lib
 from .._lib import check, ptr
 
-__all__ = ["runtime_available", "load_runtime", "FMA", "GATED", "scan", "step", "quant_i8",
+__all__ = ["runtime_available", "load_runtime", "FMA", "GATED", "scan", "scan_bwd", "step",
+           "quant_i8",
            "dequant_i8", "quant_i4", "dequant_i4", "gemv_i4", "gemm_i4", "gemv_f32",
            "bind_stream", "set_scan_mode"]
 
@@ -81,6 +82,21 @@ def scan(a, b, s0, gated=False):
     check(lib.sn_abi_recur_scan(ptr(a), ptr(b), ptr(s0), ptr(out), ptr(send), B, T, N,
                                 GATED if gated else FMA), "recur_scan")
     return out, send
+
+
+def scan_bwd(a, b, s0, out, dout, gated=False):
+    """Reverse pass over ``scan``'s outputs -> (da, db, ds0) (reference
+    runtime/__init__.py ``scan_bwd``, recur.c:51-107); gated: b holds u and
+    (da, db) are the gradients w.r.t. a and u. Bit-identical to the reference."""
+    lib = load_runtime()
+    B, T, N = a.shape
+    da = _empty(a, (B, T, N), np.float32)
+    db = _empty(a, (B, T, N), np.float32)
+    ds0 = _empty(a, (B, N), np.float32)
+    bind_stream(a, b, s0, out, dout)
+    check(lib.sn_abi_recur_bwd(ptr(a), ptr(b), ptr(s0), ptr(out), ptr(dout), ptr(da), ptr(db),
+                               ptr(ds0), B, T, N, GATED if gated else FMA), "recur_bwd")
+    return da, db, ds0
 
 
 def step(a, b, s, gated=False):

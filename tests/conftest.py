@@ -1,6 +1,7 @@
 """Shared test setup: markers, paths, golden fixtures."""
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -9,6 +10,9 @@ import pytest
 
 REPO = Path(__file__).resolve().parents[1]
 GOLDEN = REPO / "tests" / "golden"
+# The reference checkout; present on the build host only. Tests that use it
+# skip when it is absent (GPU hosts get committed fixtures instead).
+REFERENCE_ROOT = Path(os.environ.get("SN_REFERENCE_ROOT", "/root/reference"))
 if str(REPO) not in sys.path:
     sys.path.insert(0, str(REPO))
 

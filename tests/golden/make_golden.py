@@ -8,7 +8,7 @@ neither the reference tree nor oracle/_ref.
     python tests/golden/make_golden.py --ref <reference checkout>
 
 What is pinned:
-* prims.npz      -- sn_recur_scan/step, sn_quant_i8/dequant_i8, sn_quant_i4/
+* prims.npz      -- sn_recur_scan/step/bwd, sn_quant_i8/dequant_i8, sn_quant_i4/
                     dequant_i4, sn_gemv_i4, sn_gemv_f32 outputs of the reference C
                     on seeded inputs (ragged sizes included).
 * sunny_tiny.*   -- a tiny SunnyNet built by the reference's torch code
@@ -17,6 +17,9 @@ What is pinned:
                     reference C runtime (sn_step) and of SunnyNet.forward_step,
                     batched forward_step, chunked forward (prefill) final state,
                     and an sn_dbg_layer dump.
+* ref_bindings.json -- every symbol the reference's ctypes loaders bind, with
+                    the argtypes/restype they set, and the functions its
+                    runtime headers declare (the drop-in boundary).
 * rwkv_tiny.npz  -- a tiny RWKV-7 drawn by sunnynet_b200.formats.random_rwkv,
                     written to GGUF, run through the reference numpy RWKV7.step,
                     exported by the reference's _export_rwkv7.py (fp32 and INT4)
@@ -96,6 +99,25 @@ def make_prims(out: Path):
     yf = np.empty(48, np.float32)
     R.sn_gemv_f32(P(yf), P(xv), P(W), 256, 48)
     d["q4_W"], d["q4_x"], d["gemv_f32_y"] = W, xv, yf
+    # sn_recur_bwd (recur.c:51-107): reverse pass over the forward scan's
+    # outputs, both forms, ragged N (the AVX2 lanes and the scalar tail)
+    for tag, (B, T, N) in {"a": (2, 37, 13), "b": (1, 64, 40)}.items():
+        a = rng.uniform(0.3, 1.0, (B, T, N)).astype(np.float32)
+        u = rng.standard_normal((B, T, N)).astype(np.float32)
+        s0 = rng.standard_normal((B, N)).astype(np.float32)
+        dout = rng.standard_normal((B, T, N)).astype(np.float32)
+        d[f"bwd_{tag}_a"], d[f"bwd_{tag}_u"], d[f"bwd_{tag}_s0"] = a, u, s0
+        d[f"bwd_{tag}_dout"] = dout
+        for g in (0, 1):
+            o = np.empty_like(a)
+            se = np.empty((B, N), np.float32)
+            R.sn_recur_scan(P(a), P(u), P(s0), P(o), P(se), B, T, N, g)
+            da, db = np.empty_like(a), np.empty_like(a)
+            ds0 = np.empty((B, N), np.float32)
+            R.sn_recur_bwd(P(a), P(u), P(s0), P(o), P(dout), P(da), P(db), P(ds0), B, T, N, g)
+            d[f"bwd_{tag}_g{g}_out"] = o
+            d[f"bwd_{tag}_g{g}_da"], d[f"bwd_{tag}_g{g}_db"] = da, db
+            d[f"bwd_{tag}_g{g}_ds0"] = ds0
     np.savez_compressed(out / "prims.npz", **d)
 
 
@@ -316,16 +338,90 @@ def make_rwkv(out: Path, ref_root: Path):
     np.savez_compressed(out / "rwkv_tiny.npz", **res)
 
 
+# ------------------------------------------- the reference's ctypes bindings
+def _ctype_name(t) -> str:
+    if t is None:
+        return "void"
+    if getattr(t, "_type_", None) is ctypes.c_float and issubclass(t, ctypes._Pointer):
+        return "float_p"
+    return {ctypes.c_void_p: "void_p", ctypes.c_char_p: "char_p", ctypes.c_int: "int",
+            ctypes.c_uint32: "uint32", ctypes.c_int32: "int", ctypes.c_float: "float",
+            ctypes.c_int64: "int64"}[t]
+
+
+class _Recorder:
+    """Stands in for the CDLL a reference loader opens: records every
+    restype/argtypes assignment the loader makes."""
+
+    def __init__(self):
+        object.__setattr__(self, "fns", {})
+
+    def __getattr__(self, name):
+        fns = object.__getattribute__(self, "fns")
+        if name not in fns:
+            fns[name] = _RecFn()
+        return fns[name]
+
+
+class _RecFn:
+    def __init__(self):
+        self.restype = ctypes.c_int  # ctypes' default
+        self.argtypes = None
+
+
+def make_ref_bindings(out: Path, ref_root: Path):
+    """Every symbol the reference's ctypes loaders bind (runtime/__init__.py
+    load_runtime, model.py _load, abi.py load_abi, quant.py load_quant,
+    rwkv7_c.py _load) with the argtypes/restype they set, and every function
+    the reference's runtime headers declare."""
+    import importlib
+    import json
+    import re
+    sys.path.insert(0, str(ref_root))
+    loaders = {"__init__": "load_runtime", "model": "_load", "abi": "load_abi",
+               "quant": "load_quant", "rwkv7_c": "_load"}
+    real_cdll = ctypes.CDLL
+    res = {"loaders": {}, "headers": {}}
+    try:
+        for modname, fn in loaders.items():
+            full = "sunnynet.runtime" + ("" if modname == "__init__" else "." + modname)
+            mod = importlib.import_module(full)
+            rec = _Recorder()
+            ctypes.CDLL = lambda *a, **k: rec
+            for attr, val in (("_find_gcc", lambda: "gcc"), ("_needs_rebuild", lambda: False),
+                              ("_lib", None)):
+                if hasattr(mod, attr):
+                    setattr(mod, attr, val)
+            getattr(mod, fn)()
+            res["loaders"][f"runtime/{modname}.py:{fn}"] = {
+                name: {"restype": _ctype_name(f.restype),
+                       "argtypes": [_ctype_name(t) for t in (f.argtypes or [])]}
+                for name, f in sorted(object.__getattribute__(rec, "fns").items())}
+            if hasattr(mod, "_lib"):
+                mod._lib = None
+    finally:
+        ctypes.CDLL = real_cdll
+    for h in ("sn_abi.h", "recur.h", "quant.h", "sunnynet.h", "rwkv7.h"):
+        txt = (ref_root / "sunnynet" / "runtime" / h).read_text(encoding="utf-8")
+        txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+        txt = re.sub(r"//.*", "", txt)
+        txt = re.sub(r"#.*", "", txt)
+        names = sorted({m.group(1) for m in re.finditer(r"\b(sn_[A-Za-z0-9_]*)\s*\(", txt)})
+        res["headers"][h] = names
+    (out / "ref_bindings.json").write_text(json.dumps(res, indent=1, sort_keys=True) + "\n")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="root of the reference checkout")
     args = ap.parse_args()
-    oracle.build()
+    oracle.build(ref_root=args.ref)
     if not oracle.ref_available():
         raise SystemExit("oracle/_ref not built (reference tree missing?)")
     make_prims(HERE)
     make_sunny(HERE, Path(args.ref))
     make_rwkv(HERE, Path(args.ref))
+    make_ref_bindings(HERE, Path(args.ref))
     for f in sorted(HERE.glob("*")):
         if f.suffix in (".npz", ".usnn"):
             print(f"{f.name}: {f.stat().st_size} bytes")

@@ -108,3 +108,86 @@ def test_loaders_reject_bad_files_on_host(lib, tmp_path):
     short = tmp_path / "short.bin"
     short.write_bytes(b"USNN")
     assert lib.sn_abi_sunny_load(str(short).encode(), 1) is None
+
+
+# ------------------------------------------- the reference's own ctypes loaders
+def _ref_bindings():
+    import json
+    from conftest import GOLDEN
+    return json.loads((GOLDEN / "ref_bindings.json").read_text())
+
+
+def test_reference_header_symbols_are_exported(lib):
+    """Every function the reference's runtime headers declare (sn_abi.h,
+    recur.h, quant.h, sunnynet.h, rwkv7.h), as recorded from the reference
+    tree, is exported by this library."""
+    heads = _ref_bindings()["headers"]
+    want = sorted({n for names in heads.values() for n in names})
+    assert "sn_recur_bwd" in want and len(want) >= 40
+    missing = [n for n in want if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+_KIND = {"void_p": "ptr", "float_p": "ptr", "char_p": "str", "int": "int", "uint32": "int",
+         "int64": "int64", "void": "void"}
+
+
+def _kind(t):
+    if t is None:
+        return "void"
+    if t is ctypes.c_char_p:
+        return "str"
+    if t in (ctypes.c_void_p,) or (isinstance(t, type) and issubclass(t, ctypes._Pointer)):
+        return "ptr"
+    if t in (ctypes.c_int, ctypes.c_int32, ctypes.c_uint32):
+        return "int"
+    if t is ctypes.c_int64:
+        return "int64"
+    raise AssertionError(t)
+
+
+def test_reference_loader_bindings_match_this_library(lib):
+    """Each symbol the reference's loaders bind (runtime/__init__.py:135 binds
+    sn_recur_bwd) exists here with the same number and kinds of arguments."""
+    for loader, fns in _ref_bindings()["loaders"].items():
+        for name, sig in fns.items():
+            assert hasattr(lib, name), f"{loader} binds {name}, not exported"
+            if name not in _lib.SIGNATURES:
+                continue
+            _, args = _lib.SIGNATURES[name]
+            assert [_kind(t) for t in args] == [_KIND[t] for t in sig["argtypes"]], (loader, name)
+
+
+def test_reference_loaders_run_against_this_library(monkeypatch):
+    """The reference's own loader functions, with only the CDLL they open
+    redirected to libsunnynet_cuda.so (the one-line change of the integration
+    notes), set all their argtypes without an AttributeError."""
+    import importlib
+    import sys
+    from conftest import REFERENCE_ROOT
+    if not (REFERENCE_ROOT / "sunnynet" / "runtime" / "__init__.py").exists():
+        pytest.skip("reference checkout not present")
+    if not _lib.LIB_PATH.exists():
+        from sunnynet_b200 import build
+        build.build()
+    monkeypatch.syspath_prepend(str(REFERENCE_ROOT))
+    real = ctypes.CDLL
+    monkeypatch.setattr(ctypes, "CDLL", lambda *a, **k: real(str(_lib.LIB_PATH)))
+    loaders = {"__init__": "load_runtime", "model": "_load", "abi": "load_abi",
+               "quant": "load_quant", "rwkv7_c": "_load"}
+    try:
+        for modname, fn in loaders.items():
+            full = "sunnynet.runtime" + ("" if modname == "__init__" else "." + modname)
+            mod = importlib.import_module(full)
+            for attr, val in (("_find_gcc", lambda: "gcc"), ("_needs_rebuild", lambda: False),
+                              ("_lib", None)):
+                if hasattr(mod, attr):
+                    monkeypatch.setattr(mod, attr, val)
+            handle = getattr(mod, fn)()
+            assert handle is not None
+            if modname == "__init__":
+                assert handle.sn_recur_bwd.argtypes is not None
+    finally:
+        for name in list(sys.modules):
+            if name == "sunnynet" or name.startswith("sunnynet."):
+                sys.modules.pop(name)

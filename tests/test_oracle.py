@@ -30,6 +30,20 @@ def test_scan_and_step_bit_exact_vs_golden(golden, tag, gated):
     assert np.array_equal(s, g[f"step_{tag}_g{gated}"])
 
 
+@pytest.mark.parametrize("tag", ["a", "b"])
+@pytest.mark.parametrize("gated", [0, 1])
+def test_scan_bwd_bit_exact_vs_golden(golden, tag, gated):
+    """sn_recur_bwd (recur.c:51-107) as the reference C computed it."""
+    g = golden("prims.npz")
+    a, u, s0 = g[f"bwd_{tag}_a"], g[f"bwd_{tag}_u"], g[f"bwd_{tag}_s0"]
+    out, _ = oracle.recur_scan(a, u, s0, gated)
+    assert np.array_equal(out, g[f"bwd_{tag}_g{gated}_out"])
+    da, db, ds0 = oracle.recur_bwd(a, u, s0, out, g[f"bwd_{tag}_dout"], gated)
+    assert np.array_equal(da, g[f"bwd_{tag}_g{gated}_da"])
+    assert np.array_equal(db, g[f"bwd_{tag}_g{gated}_db"])
+    assert np.array_equal(ds0, g[f"bwd_{tag}_g{gated}_ds0"])
+
+
 @pytest.mark.parametrize("blk", [16, 0])
 def test_quant_i8_bit_exact_vs_golden(golden, blk):
     g = golden("prims.npz")
@@ -243,6 +257,25 @@ def test_scan_bit_exact_vs_ref_random(B, T, N):
         R.sn_recur_scan(P(a), P(u), P(s0), P(o), P(se), B, T, N, gated)
         oo, ss = oracle.recur_scan(a, u, s0, gated)
         assert np.array_equal(o, oo) and np.array_equal(se, ss)
+
+
+@needs_ref
+@pytest.mark.parametrize("B,T,N", [(1, 512, 1024), (3, 70, 13)])
+def test_scan_bwd_bit_exact_vs_ref_random(B, T, N):
+    R = oracle.ref_abi()
+    rng = np.random.default_rng(7 * B + N)
+    H = np.exp(np.linspace(np.log(2), np.log(8192), N))
+    a = rng.uniform(1 - 1 / H, 1.0, (B, T, N)).astype(np.float32)
+    u = rng.standard_normal((B, T, N)).astype(np.float32)
+    s0 = rng.standard_normal((B, N)).astype(np.float32)
+    dout = rng.standard_normal((B, T, N)).astype(np.float32)
+    for gated in (0, 1):
+        out, _ = oracle.recur_scan(a, u, s0, gated)
+        da, db = np.empty_like(a), np.empty_like(a)
+        ds0 = np.empty((B, N), np.float32)
+        R.sn_recur_bwd(P(a), P(u), P(s0), P(out), P(dout), P(da), P(db), P(ds0), B, T, N, gated)
+        oa, ob, o0 = oracle.recur_bwd(a, u, s0, out, dout, gated)
+        assert np.array_equal(da, oa) and np.array_equal(db, ob) and np.array_equal(ds0, o0)
 
 
 @needs_ref

@@ -124,3 +124,70 @@ def test_rejects_host_arrays(env):
                                               None)
     assert rc == -1
     assert "device memory" in lib.last_error()
+
+
+_FRESH = r"""
+import ctypes, sys
+import numpy as np
+import torch
+sys.path.insert(0, {repo!r})
+import oracle
+from sunnynet_b200 import _lib
+L = _lib.load()  # only the no-allocation entry point is called below
+rng = np.random.default_rng(5)
+B, T, N = 2, 600, 256
+H = np.exp(np.linspace(np.log(2.0), np.log(8192.0), N))
+a = rng.uniform(1.0 - 1.0 / H, 1.0, (B, T, N)).astype(np.float32)
+u = rng.standard_normal((B, T, N)).astype(np.float32)
+s0 = rng.standard_normal((B, N)).astype(np.float32)
+da, du, ds = (torch.from_numpy(x).cuda() for x in (a, u, s0))
+for call in range(2):
+    out = torch.full_like(da, float("nan"))
+    send = torch.full_like(ds, float("nan"))
+    rc = L.sn_abi_recur_scan_noalloc(_lib.ptr(da), _lib.ptr(du), _lib.ptr(ds), _lib.ptr(out),
+                                     _lib.ptr(send), B, T, N, 1, None)
+    assert rc == 0, (rc, _lib.last_error())
+    torch.cuda.synchronize()
+    ro, rs = oracle.recur_scan(a, u, s0, 1)
+    o, s = out.cpu().numpy().astype(np.float64), send.cpu().numpy().astype(np.float64)
+    scale = np.maximum(np.abs(ro.astype(np.float64)).max(axis=1, keepdims=True), 1e-30)
+    err = float((np.abs(o - ro) / scale).max())
+    assert err < {tol}, err
+    assert np.array_equal(send.cpu().numpy(), out.cpu().numpy()[:, -1])
+print("fresh-process no-alloc scan ok")
+"""
+
+
+def test_fresh_process_calls_only_the_no_alloc_entry_point():
+    """The intended use: a process that never lets the library initialise its
+    runtime (no stream, no mapped error word, no scratch) and calls only this
+    entry point, twice, on torch-allocated device arrays; checked against the
+    CPU oracle's recurrence (the reference's per-row rule)."""
+    import subprocess
+    import sys
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from conftest import REPO
+    code = _FRESH.format(repo=str(REPO), tol=TOL)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                       timeout=600, cwd=str(REPO))
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert "fresh-process no-alloc scan ok" in r.stdout
+
+
+def test_rejects_arrays_of_another_device(env):
+    """Arrays must live on the current device: another GPU's arrays would be
+    read across NVLink (or fault without peer access), so they are refused
+    before anything is launched."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    _, lib = env
+    from sunnynet_b200._lib import ptr
+    other = torch.zeros(64, device="cuda:1")
+    mine = torch.zeros(64, device="cuda:0")
+    with torch.cuda.device(0):
+        rc = lib.load().sn_abi_recur_scan_noalloc(ptr(other), ptr(mine), ptr(mine), ptr(mine),
+                                                  ptr(mine), 1, 8, 8, 1, None)
+    assert rc == -1
+    assert "current device" in lib.last_error()
