@@ -184,6 +184,13 @@ sn_status   sn_abi_rwkv7_step_batch(SnAbiRwkv7* m, const int32_t* tokens, int32_
                                     float* logits);
 sn_status   sn_abi_rwkv7_step_argmax(SnAbiRwkv7* m, const int32_t* tokens, int32_t B,
                                      int32_t* next);
+/* No reference counterpart: a debugging view of one batched step. The same
+ * kernels run (without the step's CUDA graph) and the residual stream is
+ * copied out as it enters each layer and leaves the last one: xs (B, L+1, D),
+ * host or device. logits (B, vocab) may be NULL. Lets a checker run any
+ * single layer from exactly this step's input. */
+sn_status   sn_abi_rwkv7_step_trace(SnAbiRwkv7* m, const int32_t* tokens, int32_t B,
+                                    float* logits, float* xs);
 /* S (B,L,NH,HS,HS), shift (B,L,2,D) */
 sn_status   sn_abi_rwkv7_get_state(SnAbiRwkv7* m, int32_t B, float* S, float* shift);
 int32_t     sn_abi_rwkv7_dims(const SnAbiRwkv7* m, int32_t* dims8); /* vocab,D,HS,NH,F,L,q4,group */

@@ -91,6 +91,8 @@ def lib():
     L.or_rk_step.argtypes = [_V, _V, _V]
     L.or_rk_dbg.argtypes = [_V, _I, _I, _V]
     L.or_rk_get_state.argtypes = [_V, _I, _V, _V]
+    L.or_rk_set_state.argtypes = [_V, _I, _V, _V]
+    L.or_rk_step_forced.argtypes = [_V, _V, _V, _V, _V]
     _lib = L
     return L
 
@@ -295,6 +297,21 @@ class Rwkv:
         out = np.empty(9 * D, np.float32)
         self.L.or_rk_dbg(self.h, int(token), int(layer), ptr(out))
         return out
+
+    def set_state(self, seq, S, shift):
+        S = np.ascontiguousarray(S, np.float32)
+        shift = np.ascontiguousarray(shift, np.float32)
+        self.L.or_rk_set_state(self.h, seq, ptr(S), ptr(shift))
+
+    def step_forced(self, tokens, xs_in):
+        """Each layer of each sequence run from xs_in (nseq, L+1, D), the input
+        another implementation gave it -> (xs_out (nseq, L+1, D), logits)."""
+        t = np.ascontiguousarray(np.asarray(tokens, np.int32).reshape(self.nseq))
+        xs_in = np.ascontiguousarray(xs_in, np.float32)
+        xs_out = np.empty_like(xs_in)
+        lg = np.empty((self.nseq, self.vocab), np.float32)
+        self.L.or_rk_step_forced(self.h, ptr(t), ptr(xs_in), ptr(xs_out), ptr(lg))
+        return xs_out, lg
 
     def get_state(self, seq, L, NH, HS, D):
         S = np.empty((L, NH, HS, HS), np.float32)

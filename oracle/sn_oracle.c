@@ -11,6 +11,7 @@
 #include "sn_oracle.h"
 
 #include <math.h>
+#include <omp.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -75,9 +76,15 @@ static float dot_sunny(const float* w, const float* x, int n) {
     return s;
 }
 
-/* y[out] = W(out,in) x, SunnyNet order. */
-static void gemv_sunny(float* y, const float* x, const float* W, int in, int out) {
+/* y[out] = W(out,in) x, SunnyNet order. `par`: rows spread over the OpenMP
+ * threads (each row's sum is unchanged, so the result is the same). */
+static void gemv_sunny_p(float* y, const float* x, const float* W, int in, int out, int par) {
+#pragma omp parallel for schedule(static) if (par)
     for (int j = 0; j < out; ++j) y[j] = dot_sunny(W + (size_t)j * in, x, in);
+}
+
+static void gemv_sunny(float* y, const float* x, const float* W, int in, int out) {
+    gemv_sunny_p(y, x, W, in, out, 0);
 }
 
 /* Two-pass layernorm with sequential sums (sunnynet.c:198-210, rwkv7.c:128-140). */
@@ -345,6 +352,7 @@ struct OrSunny {
     float* hist;                       /* (nseq,L,KH,D), KH = max(K-1,1) */
     float** blocks;
     int nblocks;
+    int row_par; /* GEMV rows over threads (set while sequences run one at a time) */
 };
 
 static float* sn_alloc(OrSunny* m, size_t n) {
@@ -489,24 +497,25 @@ static void sn_layer(const OrSunny* m, const OrLayer* L, float* s, float* hist,
     } else {
         memcpy(at, raw, sizeof(float) * D);
     }
-    gemv_sunny(v, at, L->V, D, R);
-    gemv_sunny(q, v, L->U, R, 2 * D);
+    const int par = m->row_par;
+    gemv_sunny_p(v, at, L->V, D, R, par);
+    gemv_sunny_p(q, v, L->U, R, 2 * D, par);
     memcpy(gate, q + D, sizeof(float) * D);
     for (int i = 0; i < D; ++i) {
         const int base = (i / G) * G, off = i - base;
         u[i] = q[i] * (sig(gate[i] - gate[base + (off + 1) % G]) *
                        sig(gate[i] - gate[base + (off + 2) % G]));
     }
-    gemv_sunny(sfb, s, L->Ws, D, D); /* feedback reads the previous state */
+    gemv_sunny_p(sfb, s, L->Ws, D, D, par); /* feedback reads the previous state */
     for (int i = 0; i < D; ++i) {
         float p = 1.0f - L->delta[i] * (1.0f - sig(gate[i]));
         if (m->clamp && p < m->p_floor) p = m->p_floor;
         s[i] = p * s[i] + (1.0f - p) * u[i];
     }
-    gemv_sunny(zn, u, L->Wz, D, I);
+    gemv_sunny_p(zn, u, L->Wz, D, I, par);
     for (int i = 0; i < I; ++i) zn[i] = zn[i] * (1.0f + 0.5f * L->a_tanh / (1.0f + fabsf(zn[i])));
     layernorm(yn, zn, L->nm_g, L->nm_c, I, m->eps);
-    gemv_sunny(out, yn, L->Wc, I, D);
+    gemv_sunny_p(out, yn, L->Wc, I, D, par);
     for (int i = 0; i < D; ++i) out[i] = out[i] + (L->b_gain * s[i] + sfb[i] + x[i]);
     if (dbg) {
         float* t = dbg;
@@ -542,16 +551,28 @@ static void sn_seq(OrSunny* m, int seq, int token, float* logits, int last_layer
     }
     if (last_layer >= 0 || !logits) return;
     layernorm(nrm, x, m->no_g, m->no_c, D, m->eps);
-    gemv_sunny(logits, nrm, m->head, D, m->vocab);
+    gemv_sunny_p(logits, nrm, m->head, D, m->vocab, m->row_par);
 }
 
+/* Sequences in parallel when there are at least as many as threads; else one
+ * at a time with each GEMV's rows spread over the threads. Either way every
+ * value is computed by the same sequence of operations. */
 void or_sn_step(OrSunny* m, const int32_t* tokens, float* logits) {
+    if (m->nseq >= omp_get_max_threads()) {
 #pragma omp parallel for schedule(static)
-    for (int i = 0; i < m->nseq; ++i) {
-        float* sc = (float*)malloc(sizeof(float) * sn_scratch(m));
-        sn_seq(m, i, tokens[i], logits ? logits + (size_t)i * m->vocab : NULL, -1, NULL, sc);
-        free(sc);
+        for (int i = 0; i < m->nseq; ++i) {
+            float* sc = (float*)malloc(sizeof(float) * sn_scratch(m));
+            sn_seq(m, i, tokens[i], logits ? logits + (size_t)i * m->vocab : NULL, -1, NULL, sc);
+            free(sc);
+        }
+        return;
     }
+    float* sc = (float*)malloc(sizeof(float) * sn_scratch(m));
+    m->row_par = 1;
+    for (int i = 0; i < m->nseq; ++i)
+        sn_seq(m, i, tokens[i], logits ? logits + (size_t)i * m->vocab : NULL, -1, NULL, sc);
+    m->row_par = 0;
+    free(sc);
 }
 
 void or_sn_dbg_layer(OrSunny* m, int token, int layer, float* dbg) {
@@ -926,6 +947,44 @@ void or_rk_dbg(OrRwkv* m, int token, int layer, float* out) {
     float* sc = (float*)malloc(sizeof(float) * rk_scratch(m));
     rk_seq(m, 0, token, NULL, layer, out, sc);
     free(sc);
+}
+
+void or_rk_set_state(OrRwkv* m, int seq, const float* S, const float* shift) {
+    const size_t sz = (size_t)m->L * m->NH * m->HS * m->HS;
+    memcpy(m->S + (size_t)seq * sz, S, sizeof(float) * sz);
+    memcpy(m->shift + (size_t)seq * m->L * 2 * m->D, shift, sizeof(float) * (size_t)m->L * 2 * m->D);
+}
+
+/* One step in which layer l of sequence i starts from xs_in[i][l] (the input
+ * another implementation fed that layer) instead of this oracle's own layer
+ * l-1 output: xs_out[i][0] = the embedding row after its norm, xs_out[i][l+1]
+ * = layer l applied to xs_in[i][l] (states updated as in a normal step; the
+ * v-first vector comes from layer 0 applied to xs_in[i][0]); logits from the
+ * final norm and head applied to xs_in[i][L]. xs_* are (nseq, L+1, D). */
+void or_rk_step_forced(OrRwkv* m, const int32_t* tokens, const float* xs_in, float* xs_out,
+                       float* logits) {
+    const int D = m->D, L = m->L;
+    const size_t sz = (size_t)m->NH * m->HS * m->HS;
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < m->nseq; ++i) {
+        float* sc = (float*)malloc(sizeof(float) * rk_scratch(m));
+        float *x = sc + rk_scratch(m) - 3 * (size_t)D, *nrm = x + D, *vfirst = nrm + D;
+        const float* in = xs_in + (size_t)i * (L + 1) * D;
+        float* out = xs_out + (size_t)i * (L + 1) * D;
+        memcpy(x, m->embed + (size_t)tokens[i] * D, sizeof(float) * D);
+        layernorm(out, x, m->en_w, m->en_b, D, m->eps);
+        for (int l = 0; l < L; ++l) {
+            memcpy(x, in + (size_t)l * D, sizeof(float) * D);
+            rk_layer(m, &m->ly[l], l == 0, m->S + ((size_t)i * L + l) * sz,
+                     m->shift + ((size_t)i * L + l) * 2 * D, x, vfirst, sc, NULL);
+            memcpy(out + (size_t)(l + 1) * D, x, sizeof(float) * D);
+        }
+        if (logits) {
+            layernorm(nrm, in + (size_t)L * D, m->on_w, m->on_b, D, m->eps);
+            mat_mul(logits + (size_t)i * m->vocab, nrm, &m->head);
+        }
+        free(sc);
+    }
 }
 
 void or_rk_get_state(const OrRwkv* m, int seq, float* S, float* shift) {

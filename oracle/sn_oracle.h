@@ -65,6 +65,10 @@ void or_rk_step(OrRwkv* m, const int32_t* tokens, float* logits);
 void or_rk_dbg(OrRwkv* m, int token, int layer, float* out);
 /* state of sequence i: S (L,NH,HS,HS), shift (L,2,D). */
 void or_rk_get_state(const OrRwkv* m, int seq, float* S, float* shift);
+void or_rk_set_state(OrRwkv* m, int seq, const float* S, const float* shift);
+/* one step with every layer fed the given input: xs_in, xs_out (nseq, L+1, D) */
+void or_rk_step_forced(OrRwkv* m, const int32_t* tokens, const float* xs_in, float* xs_out,
+                       float* logits);
 
 #ifdef __cplusplus
 }

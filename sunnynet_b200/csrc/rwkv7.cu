@@ -620,12 +620,23 @@ int mat_mul(const RkMat& M, float* y, const float* x, int B, int epi, cudaStream
 
 enum { E_STORE = 0, E_ADD = 1, E_RELU2 = 2, E_TANH = 3, E_SIG = 4 };
 
-int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer = -1) {
+// trace (device, (B, L+1, D)) or nullptr: the residual stream entering each
+// layer and leaving the last one, copied out after the embedding and after
+// every layer (a debugging view of the same kernels, used without a graph).
+int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer = -1,
+               float* trace = nullptr) {
     const int D = m->D;
     const size_t plane = (size_t)B * D;
     const long long sh_stride = (long long)m->L * 2 * D;
+    auto trace_x = [&](int j) {
+        return cuda_check(cudaMemcpy2DAsync(trace + (size_t)j * D, (size_t)(m->L + 1) * D * 4,
+                                            m->x, (size_t)D * 4, (size_t)D * 4, (size_t)B,
+                                            cudaMemcpyDeviceToDevice, st),
+                          "trace copy");
+    };
     rk_embed_kernel<<<B, 256, 0, st>>>(D, m->tok, m->vocab, rt().d_err, m->embed, m->en_w,
                                        m->en_b, m->x, m->eps);
+    if (trace) SN_TRY(trace_x(0));
     const int nl = last_layer >= 0 ? last_layer + 1 : m->L;
     const unsigned ew = (unsigned)((plane + 255) / 256);
     for (int l = 0; l < nl; ++l) {
@@ -731,6 +742,7 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
                           "cmix launch"));
         SN_TRY(mat_mul(A.cmk, m->ck, m->xk2, B, E_RELU2, st));
         SN_TRY(mat_mul(A.cmv, m->x, m->ck, B, E_ADD, st));
+        if (trace) SN_TRY(trace_x(l + 1));
     }
     if (last_layer < 0 && head) {
         SN_TRY(cuda_check(launch_pdl(rk_ln_kernel, dim3(B), dim3(256), 0, st, D, (const float*)m->x,
@@ -741,8 +753,9 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
     return cuda_check(cudaGetLastError(), "rwkv step launch");
 }
 
-int rk_run(RwkvModel* m, int B, bool head) {
-    if (prof_on()) return enqueue_rk(m, B, head, stream());  // bracket kernels, no graph
+int rk_run(RwkvModel* m, int B, bool head, float* trace = nullptr) {
+    if (prof_on() || trace)  // bracket kernels / copy out the trace: no graph
+        return enqueue_rk(m, B, head, stream(), -1, trace);
     auto key = std::make_pair(B, head ? 1 : 0);
     auto it = m->graphs.find(key);
     if (it == m->graphs.end()) {
@@ -765,7 +778,8 @@ int rk_run(RwkvModel* m, int B, bool head) {
     return cuda_check(cudaGraphLaunch(it->second, stream()), "graph launch");
 }
 
-int rk_step(RwkvModel* m, const int32_t* tokens, int B, float* logits, int32_t* next) {
+int rk_step(RwkvModel* m, const int32_t* tokens, int B, float* logits, int32_t* next,
+            float* xs = nullptr) {
     if (!m || !m->ready || !tokens || B <= 0 || B > m->nseq)
         return fail(SN_E_INVAL, "rwkv7_step: bad handle, tokens or B");
     std::lock_guard<std::recursive_mutex> lk(rt().mu);
@@ -774,8 +788,14 @@ int rk_step(RwkvModel* m, const int32_t* tokens, int B, float* logits, int32_t* 
     SN_TRY(cuda_check(cudaMemcpyAsync(m->tok, tokens, (size_t)B * 4,
                                       tdev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st),
                       "tokens"));
-    SN_TRY(rk_run(m, B, logits || next));
+    Arr XS;
+    if (xs) SN_TRY(stage_out(xs, (size_t)B * (m->L + 1) * m->D * 4, 11, &XS));
+    SN_TRY(rk_run(m, B, logits || next, xs ? (float*)XS.dev : nullptr));
     bool host = !tdev;
+    if (xs) {
+        SN_TRY(copy_back(XS));
+        host |= XS.host != nullptr;
+    }
     if (logits) {
         const bool dev = is_device_ptr(logits);
         host |= !dev;
@@ -878,6 +898,12 @@ sn_status sn_abi_rwkv7_step_argmax(SnAbiRwkv7* m, const int32_t* tokens, int32_t
                                    int32_t* next) {
     if (!m || !next) return SN_E_INVAL;
     return rk_step(m->m.get(), tokens, B, nullptr, next);
+}
+
+sn_status sn_abi_rwkv7_step_trace(SnAbiRwkv7* m, const int32_t* tokens, int32_t B,
+                                  float* logits, float* xs) {
+    if (!m || !xs) return fail(SN_E_INVAL, "rwkv7_step_trace: null handle or trace");
+    return rk_step(m->m.get(), tokens, B, logits, nullptr, xs);
 }
 
 sn_status sn_abi_rwkv7_get_state(SnAbiRwkv7* m, int32_t B, float* S, float* shift) {

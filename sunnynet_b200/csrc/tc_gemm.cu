@@ -930,6 +930,18 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
             }
         }
     }
+    // SN_TC_FORCE_BN (32/64/128/192/256): a test hook that overrides the
+    // model's width, unsplit, wherever that width is allowed for the shape
+    if (const char* fb = getenv("SN_TC_FORCE_BN")) {
+        const int b = atoi(fb);
+        const bool ok = (b == 32 || b == 64 || b == 128 || b == 192 || b == 256) &&
+                        (!ld || (ring ? b <= 128 : b == bld)) &&
+                        !(b == 192 && (ld || a.Ch != nullptr || tw.int8));
+        if (ok) {
+            bn = b;
+            ks = 1;
+        }
+    }
 #define SN_TC_BN(I8, LD)                                                                  \
     return bn == 256   ? launch_bn<256, I8, LD>(a, tw, tah, tal, st, pdl, ks)              \
            : bn == 192 ? launch_bn<192, I8, LD>(a, tw, tah, tal, st, pdl, ks)              \

@@ -44,6 +44,17 @@ class Rwkv7Batch:
         check(self._lib.sn_abi_rwkv7_step_argmax(self._h, ptr(t), B, ptr(out)), "rwkv7_argmax")
         return out
 
+    def step_trace(self, tokens):
+        """One step that also returns the residual stream entering each layer
+        and leaving the last: (logits (B, vocab), xs (B, L+1, D)), host arrays."""
+        t = np.ascontiguousarray(np.asarray(tokens, np.int32))
+        B = int(t.shape[0])
+        logits = np.empty((B, self.vocab), np.float32)
+        xs = np.empty((B, self.layers + 1, self.dim), np.float32)
+        check(self._lib.sn_abi_rwkv7_step_trace(self._h, ptr(t), B, ptr(logits), ptr(xs)),
+              "rwkv7_step_trace")
+        return logits, xs
+
     def reset(self):
         check(self._lib.sn_abi_rwkv7_reset(self._h), "rwkv7_reset")
 

@@ -313,3 +313,52 @@ def test_sunny_random_preset_shape_bit_exact_vs_ref():
             R.sn_step(h, int(t), P(a))
             assert np.array_equal(m.step([t])[0], a)
         R.sn_free(h)
+
+
+def test_rwkv_forced_step_fed_its_own_trace_equals_a_normal_step(golden):
+    """The layer-by-layer checker: fed the residual stream a normal step
+    produces, or_rk_step_forced reproduces that step bit for bit (logits and
+    states). The trace is found by iterating the forced step from the same
+    starting state until it is a fixed point: round k gets entries 0..k-1
+    right, and the logits read entry L, so L+2 rounds."""
+    g = golden("rwkv_tiny.npz")
+    Lr, D, HS, F, V, *ranks = (int(v) for v in g["shape"])
+    shape = formats.RwkvShape(Lr, D, HS, F, V, tuple(ranks))
+    w = formats.random_rwkv(shape, int(g["seed"]))
+    with tempfile.TemporaryDirectory() as td:
+        for kind in ("fp32", "q4g"):
+            p = Path(td) / f"{kind}.bin"
+            formats.write_krwk(p, w, quant=kind)
+            a, b = oracle.Rwkv(p, 3), oracle.Rwkv(p, 3)
+            warm = np.array([5, 77, 300], np.int32)
+            a.step(warm), b.step(warm)
+            NH = D // HS
+            st = [a.get_state(i, Lr, NH, HS, D) for i in range(3)]
+            toks = np.array([9, 123, 400], np.int32)
+            ref = a.step(toks)
+            xs = np.zeros((3, Lr + 1, D), np.float32)
+            for _ in range(Lr + 2):
+                for i in range(3):
+                    b.set_state(i, *st[i])
+                xs, lg = b.step_forced(toks, xs)
+            assert np.array_equal(lg, ref)
+            for i in range(3):
+                sa, ha = a.get_state(i, Lr, NH, HS, D)
+                sb, hb = b.get_state(i, Lr, NH, HS, D)
+                assert np.array_equal(sa, sb) and np.array_equal(ha, hb)
+
+
+def test_sunny_row_parallel_equals_sequence_parallel():
+    """With fewer sequences than threads the oracle runs them one at a time
+    and spreads each GEMV's rows over the threads; the numbers must not move."""
+    shape = formats.SunnyShape(700, 72, 100, 36, 4, 2)
+    rng = np.random.default_rng(4)
+    with tempfile.TemporaryDirectory() as td:
+        p = Path(td) / "m.usnn"
+        formats.write_usnn(p, formats.random_sunny(shape, seed=4, perturb=True))
+        few, many = oracle.Sunny(p, 2), oracle.Sunny(p, 64)
+        for _ in range(3):
+            t = rng.integers(0, 700, 64).astype(np.int32)
+            lm = many.step(t)
+            lf = few.step(t[:2])
+            assert np.array_equal(lf, lm[:2])
