@@ -1,13 +1,16 @@
 """Benchmark of the SunnyNet token loop on B200s (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl ours|reference]
 
 Workloads (synthetic seeded inputs, random-init weights):
   c1   gated scan, B=1 T=4096 C=1024 (one step = one full scan)
   c2   SunnyNet small decode (L4 d512 i896 r320 V16384, fp32), B=256 per GPU
   c2b1 the same model at B=1
-  c3   SunnyNet 100M-class (L12 d768 i1344 r480 V32000), INT8 per-row weights,
-       B=1024 split over the GPUs
+  c3   (default) SunnyNet 100M-class (L12 d768 i1344 r480 V32000), INT8
+       per-row weights, a global batch of 1024 split over the GPUs
+       (1024/512/256/128 per GPU at 1/2/4/8: strong scaling), after a
+       2048-token chunked prefill. On one GPU the line also carries the
+       metric's other batch sizes as sub-records: c2 at B=256 and at B=1.
   c4   RWKV-7 191M shape, INT4 group-128 fp16 scales, B=64 per GPU (c4b1, c4b512)
   c5   chunked prefill, SunnyNet 0.5B shape (L24 d1536 i2688 r960 V32000) fp32,
        T=32768 in chunks of 256, 8 sequences per GPU
@@ -114,34 +117,63 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def shard(total: int, world: int, rank: int):
+    """Sequences [start, start + count) that `rank` owns when `total`
+    independent sequences are split over `world` ranks: contiguous ranges whose
+    sizes differ by at most one, covering every sequence exactly once."""
+    base, extra = divmod(total, world)
+    count = base + (1 if rank < extra else 0)
+    return rank * base + min(rank, extra), count
+
+
 class Dist:
-    def __init__(self):
+    """One process per GPU (torchrun's RANK / LOCAL_RANK / WORLD_SIZE). The
+    data path has no collective (sequences are independent); the process
+    group only lines the ranks up around the timed region and takes the max
+    of their times. backend="gloo", cuda=False runs the same logic on CPU."""
+
+    def __init__(self, backend: str = "nccl", cuda: bool = True):
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.rank = int(os.environ.get("RANK", "0"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend, self.cuda = backend, cuda
         self.pg = None
 
     def init(self, torch):
-        torch.cuda.set_device(self.local)
+        if self.cuda:
+            torch.cuda.set_device(self.local)
         if self.world > 1:
             import datetime
             import torch.distributed as dist
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", self.local))
+            kw = {"device_id": torch.device("cuda", self.local)} if self.cuda else {}
+            dist.init_process_group(self.backend, timeout=datetime.timedelta(seconds=120), **kw)
             self.pg = dist
 
     def barrier(self, torch):
-        torch.cuda.synchronize()
+        if self.cuda:
+            torch.cuda.synchronize()
         if self.pg:
             self.pg.barrier()
-        torch.cuda.synchronize()
+        if self.cuda:
+            torch.cuda.synchronize()
 
     def max(self, torch, v: float) -> float:
         if not self.pg:
             return v
-        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        t = torch.tensor([v], device="cuda" if self.cuda else "cpu", dtype=torch.float64)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
+
+    def gather(self, torch, values) -> list:
+        """Every rank's equal-length list of numbers, in rank order (host-side
+        collection of per-rank results such as token counts or checksums)."""
+        t = torch.tensor(list(values), device="cuda" if self.cuda else "cpu",
+                         dtype=torch.float64)
+        if not self.pg:
+            return [t.tolist()]
+        out = [torch.empty_like(t) for _ in range(self.world)]
+        self.pg.all_gather(out, t)
+        return [o.tolist() for o in out]
 
     def close(self):
         if self.pg:
@@ -326,14 +358,19 @@ def family_cost(S, B, fam, wbytes):
 def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
     from sunnynet_b200 import formats
     S = formats.SUNNY_PRESETS[preset]
-    B = B_total // dist.world if split else B_total
+    B = shard(B_total, dist.world, dist.rank)[1] if split else B_total
+    seqs = B_total if split else B * dist.world  # sequences all ranks step together
     wbytes = 1 if quant else 4
     step_bytes, step_flops = sunny_step_cost(S, B, wbytes)
     res = {"metric": "decode tokens/s", "unit": "tokens/s", "higher_is_better": True,
-           "dtype": "i8w-f32" if quant else "f32",
+           "dtype": (("i8w-f32 (INT8 weights exact in bf16; fp32 activations as bf16 hi+lo, "
+                      "2 tcgen05 MMAs, fp32 accumulate)" if quant else
+                      "f32 (bf16x3 tcgen05 split: hi*hi + hi*lo + lo*hi, fp32 accumulate)")
+                     if B >= 16 else ("i8w-f32 (INT8 weights, fp32 FMA)" if quant
+                                      else "f32 (fp32 FMA)")),
            "config": {"workload": f"{preset} SunnyNet decode L{S.layers} d{S.dim} i{S.inner} "
                                   f"r{S.rank} V{S.vocab} {'INT8 per-row' if quant else 'fp32'}",
-                      "batch_per_gpu": B, "global_batch": B * dist.world,
+                      "batch_per_gpu": B, "global_batch": seqs,
                       "prefill_tokens": prefill_T, "decode": "greedy, teacher-free",
                       "l2": "flushed between steps" if step_bytes < 2 * (126 << 20) else
                             "working set > L2"}}
@@ -358,8 +395,11 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
     check(lib.sn_abi_cuda_set_async(1))
     prompt = torch.randint(0, S.vocab, (B, prefill_T), generator=g, device="cuda",
                            dtype=torch.int32)
-    for t in range(prefill_T):
-        m.step(prompt[:, t].contiguous(), logits=logits)
+    if prefill_T >= 256:  # the chunked prefill path (256-token chunks, state carried)
+        m.prefill(prompt, chunk=256, logits=logits)
+    else:
+        for t in range(prefill_T):
+            m.step(prompt[:, t].contiguous(), logits=logits)
     cur = torch.argmax(logits, dim=1).to(torch.int32).contiguous()
 
     def step():
@@ -374,8 +414,13 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
             for _ in range(20):
                 step()
             torch.cuda.synchronize()
-    # live per-kernel timing (CUDA events around each kernel family, same step)
-    check(lib.sn_abi_cuda_profile(1))
+    # host-side collection of every rank's greedy tokens (a checksum per rank)
+    toks = cur.to(torch.int64)
+    res["tokens_per_rank"] = [int(v[0]) for v in dist.gather(torch, [int(toks.numel())])]
+    res["token_checksums"] = [int(v[0]) for v in dist.gather(torch, [int(toks.sum().item())])]
+    # live per-kernel timing: the step's own graph replayed with CUDA event
+    # nodes around each kernel family (same nodes, streams and dependencies)
+    check(lib.sn_abi_cuda_profile(2))
     for _ in range(3):
         if flush:
             flush()
@@ -402,7 +447,10 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
                "step_alg_bytes": step_bytes, "step_alg_flops": step_flops,
                "step_hbm_gbs": step_bytes / (ms * 1e-3) / 1e9,
                "step_tflops": step_flops / (ms * 1e-3) / 1e12,
-               "families_ms_per_step": {k: v[1] / 3 for k, v in fams.items()}})
+               "timing": "in-graph: CUDA event nodes around each family in a replay of "
+                         "the step's graph",
+               "families_ms_per_step": {k: v[1] / 3 for k, v in fams.items()},
+               "share_of_step": {k: v[1] / 3 / ms for k, v in fams.items()}})
     # end to end: the public call with pinned host tokens in, host logits out
     ht = torch.randint(0, S.vocab, (B,), dtype=torch.int32).pin_memory()
     hl = torch.empty(B, S.vocab).pin_memory()
@@ -422,8 +470,8 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
         launches = 8 * S.layers + 3
     res.update({
         "ms_per_step": ms,
-        "value": B * dist.world / (ms * 1e-3),
-        "e2e": {"value": B * dist.world / e2e_s, "unit": "tokens/s",
+        "value": seqs / (ms * 1e-3),
+        "e2e": {"value": seqs / e2e_s, "unit": "tokens/s",
                 "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * S.vocab * 4,
                 "call": "sn_abi_sunny_step (host tokens, host logits)"},
         "gpu_launches": launches * args.steps,
@@ -526,7 +574,16 @@ def wl_c2b1(args, torch, dist, ours):
 
 
 def wl_c3(args, torch, dist, ours):
-    res, base = wl_sunny(args, torch, dist, ours, "c3", 1024, True, 64, split=True)
+    res, base = wl_sunny(args, torch, dist, ours, "c3", 1024, True, 2048, split=True)
+    if ours and dist.world == 1 and not args.no_sub_records:
+        # the metric's other batch sizes, on the same GPU in the same run
+        subs = {}
+        for name, fn in (("c2_b256", wl_c2), ("c2_b1", wl_c2b1)):
+            r, _ = fn(args, torch, dist, True)
+            subs[name] = {k: r[k] for k in ("config", "dtype", "value", "unit", "ms_per_step",
+                                            "e2e", "roofline", "clocks", "gpu_launches",
+                                            "cpu_baseline") if k in r}
+        res["sub_records"] = subs
     return res, base
 
 
@@ -568,7 +625,7 @@ def wl_c5(args, torch, dist, ours):
 
     with ClockSampler(dist.local) as clk:
         ms = timed_steps(torch, dist, step, args.steps, args.warmup)
-    check(lib.sn_abi_cuda_profile(1))
+    check(lib.sn_abi_cuda_profile(2))  # in-graph event timing
     for _ in range(2):
         step()
     torch.cuda.synchronize()
@@ -591,7 +648,10 @@ def wl_c5(args, torch, dist, ours):
           "note": "achieved counts the fp32 product once; the bf16x3 split issues 3 MMAs",
           "traffic": profile_traffic(f"{dom}/c5"),
           "step_tflops": flops / (ms * 1e-3) / 1e12,
-          "families_ms_per_step": {k: v[1] / 2 for k, v in fams.items()}}
+          "timing": "in-graph: CUDA event nodes around each family in a replay of "
+                    "the step's graph",
+          "families_ms_per_step": {k: v[1] / 2 for k, v in fams.items()},
+          "share_of_step": {k: v[1] / 2 / ms for k, v in fams.items()}}
     # end to end: host token ids in (pinned), host logits of the last position out
     ht = toks.cpu().pin_memory()
     hl = torch.empty(B, S.vocab).pin_memory()
@@ -721,7 +781,7 @@ def wl_rwkv(args, torch, dist, ours, B):
     flush = flushbuf.zero_ if step_bytes < 2 * (126 << 20) else None
     with ClockSampler(dist.local) as clk:
         ms = timed_steps(torch, dist, step, args.steps, args.warmup, flush=flush)
-    check(lib.sn_abi_cuda_profile(1))
+    check(lib.sn_abi_cuda_profile(2))  # in-graph event timing
     for _ in range(3):
         if flush:
             flush()
@@ -745,7 +805,10 @@ def wl_rwkv(args, torch, dist, ours, B):
           "achieved_is": "dominant kernel" if ach else "whole step (dominant is a GEMV family)",
           "traffic": profile_traffic(f"{dom}/c4/B{B}"), "step_alg_bytes": step_bytes,
           "step_alg_flops": step_flops, "step_hbm_gbs": step_gbs,
-          "families_ms_per_step": {k: v[1] / 3 for k, v in fams.items()}}
+          "timing": "in-graph: CUDA event nodes around each family in a replay of "
+                    "the step's graph",
+          "families_ms_per_step": {k: v[1] / 3 for k, v in fams.items()},
+          "share_of_step": {k: v[1] / 3 / ms for k, v in fams.items()}}
     rl["frac"] = rl["achieved"] / rl["peak"]
     ht = torch.randint(0, S.vocab, (B,), dtype=torch.int32).pin_memory()
     hl = torch.empty(B, S.vocab).pin_memory()
@@ -813,6 +876,7 @@ WORKLOADS = {"c1": wl_c1, "c2": wl_c2, "c2b1": wl_c2b1, "c3": wl_c3, "c5": wl_c5
              "c4b1": lambda a, t, d, ours: wl_rwkv(a, t, d, ours, 1),
              "c4b512": lambda a, t, d, ours: wl_rwkv(a, t, d, ours, 512)}
 SCALING = {"c3": "strong"}
+DEFAULT_CONFIG = "c3"
 
 
 def main():
@@ -821,8 +885,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub-records", action="store_true",
+                    help="default config only: skip the c2 B=256 / B=1 sub-records")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -153,9 +153,11 @@ namespace {
 struct ProfRec {
     std::string family;
     cudaEvent_t a, b;
+    bool graph;  // recorded by a graph's event nodes: read per replay, not here
 };
 struct Prof {
-    bool on = false;
+    int mode = 0;
+    unsigned epoch = 0;  // bumped when a session starts: instrumented graphs recapture
     std::vector<ProfRec> recs;
     std::vector<cudaEvent_t> pool;
     std::string open;
@@ -179,25 +181,84 @@ cudaEvent_t take_event() {
 }
 }  // namespace
 
-bool prof_on() {
-    if (!prof().on) return false;
+namespace {
+bool capturing(cudaStream_t st) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    cudaStreamIsCapturing(stream(), &cs);
-    return cs == cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return cs == cudaStreamCaptureStatusActive;
 }
+// inside a capture the record becomes an event-record node of the graph
+void record(cudaEvent_t e, cudaStream_t st) {
+    if (capturing(st))
+        cudaEventRecordWithFlags(e, st, cudaEventRecordExternal);
+    else
+        cudaEventRecord(e, st);
+}
+}  // namespace
+
+bool prof_on() {
+    const Prof& p = prof();
+    if (p.mode == 2) return true;
+    if (p.mode != 1) return false;
+    return !capturing(stream());
+}
+
+bool prof_graph() { return prof().mode == 2; }
 
 void prof_begin(const char* family, cudaStream_t st) {
     Prof& p = prof();
     p.open = family;
     p.open_ev = take_event();
-    cudaEventRecord(p.open_ev, st);
+    record(p.open_ev, st);
 }
 
 void prof_end(cudaStream_t st) {
     Prof& p = prof();
     cudaEvent_t e = take_event();
-    cudaEventRecord(e, st);
-    p.recs.push_back({p.open, p.open_ev, e});
+    record(e, st);
+    p.recs.push_back({p.open, p.open_ev, e, capturing(st)});
+}
+
+int prof_graph_run(ProfGraph* pg, cudaStream_t cap, cudaStream_t st,
+                   const std::function<int(cudaStream_t)>& enqueue) {
+    Prof& p = prof();
+    if (!pg->ex || pg->epoch != p.epoch) {
+        if (pg->ex) cudaGraphExecDestroy(pg->ex);
+        pg->ex = nullptr;
+        cudaGraph_t g = nullptr;
+        SN_TRY(cuda_check(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal),
+                          "begin capture (profiled)"));
+        const size_t i0 = p.recs.size();
+        const int rc = enqueue(cap);
+        const cudaError_t e = cudaStreamEndCapture(cap, &g);
+        if (rc != SN_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        SN_TRY(cuda_check(e, "end capture (profiled)"));
+        const cudaError_t e2 = cudaGraphInstantiate(&pg->ex, g, 0);
+        cudaGraphDestroy(g);
+        SN_TRY(cuda_check(e2, "graph instantiate (profiled)"));
+        pg->i0 = i0;
+        pg->i1 = p.recs.size();
+        pg->epoch = p.epoch;
+    }
+    SN_TRY(cuda_check(cudaGraphLaunch(pg->ex, st), "graph launch (profiled)"));
+    SN_TRY(cuda_check(cudaStreamSynchronize(st), "profiled replay"));
+    for (size_t i = pg->i0; i < pg->i1 && i < p.recs.size(); ++i) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, p.recs[i].a, p.recs[i].b) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        auto& a = p.extra[p.recs[i].family];
+        a.first += 1;
+        a.second += ms;
+    }
+    return SN_OK;
 }
 
 void prof_add(const char* family, int launches, double ms) {
@@ -212,19 +273,23 @@ using namespace sn;
 
 extern "C" {
 
-// Start (1) / stop (0) kernel-family timing. Starting clears earlier records.
+// Start (1: ungraphed, 2: instrumented graphs) / stop (0) kernel-family
+// timing. Starting clears earlier records.
 sn_status sn_abi_cuda_profile(int32_t on) {
     SN_TRY(ensure_init());
+    if (on < 0 || on > 2) return fail(SN_E_INVAL, "cuda_profile: mode must be 0, 1 or 2");
     Prof& p = prof();
     if (on) {
+        cudaStreamSynchronize(stream());
         for (auto& r : p.recs) {
             p.pool.push_back(r.a);
             p.pool.push_back(r.b);
         }
         p.recs.clear();
         p.extra.clear();
+        ++p.epoch;
     }
-    p.on = on != 0;
+    p.mode = on;
     return SN_OK;
 }
 
@@ -234,6 +299,7 @@ int32_t sn_abi_cuda_profile_report(char* buf, int32_t buflen) {
     cudaStreamSynchronize(stream());
     std::map<std::string, std::pair<int, double>> agg;
     for (auto& r : p.recs) {
+        if (r.graph) continue;  // read per replay into `extra`
         float ms = 0.0f;
         if (cudaEventElapsedTime(&ms, r.a, r.b) != cudaSuccess) cudaGetLastError();
         auto& a = agg[r.family];

@@ -5,6 +5,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 #include <mutex>
 
 #include "sn_abi.h"
@@ -57,12 +58,37 @@ inline int grid_blocks(long long total, int threads = 256, int per_sm = 8) {
     return (int)(b < 1 ? 1 : (b < cap ? b : cap));
 }
 
-// Kernel-family timing with CUDA events on the launching stream. Active only
-// between sn_abi_cuda_profile(1) and sn_abi_cuda_profile(0), and only for work
-// enqueued directly (model steps are then run without their CUDA graph).
-bool prof_on();
+// Kernel-family timing with CUDA events on the launching stream, between
+// sn_abi_cuda_profile(1 or 2) and sn_abi_cuda_profile(0).
+//   mode 1: model steps run without their CUDA graph, every kernel family
+//           bracketed by events (serialised: each launch waits for the last)
+//   mode 2: model steps replay an instrumented copy of their graph: the same
+//           nodes, streams and dependencies plus event-record nodes around
+//           each family, read after every replay (in-graph durations)
+// Work that is not graphed is bracketed directly in both modes.
+bool prof_on();      // ProfScopes record (mode 1 outside captures; mode 2 always)
+bool prof_graph();   // mode 2
 void prof_begin(const char* family, cudaStream_t st);
 void prof_end(cudaStream_t st);
+
+// Mode 2: an instrumented graph of one step shape, captured on first use in a
+// profiling session (and again after the session restarts), replayed, its
+// family events read once the replay is done.
+struct ProfGraph {
+    cudaGraphExec_t ex = nullptr;
+    size_t i0 = 0, i1 = 0;  // its records in the session's list
+    unsigned epoch = 0;
+    ProfGraph() = default;
+    ProfGraph(const ProfGraph&) = delete;
+    ProfGraph& operator=(const ProfGraph&) = delete;
+    ~ProfGraph() {
+        if (ex) cudaGraphExecDestroy(ex);
+    }
+};
+// Capture `enqueue(cap)` when needed, replay on `st`, wait, add the families'
+// in-graph times to the report.
+int prof_graph_run(ProfGraph* pg, cudaStream_t cap, cudaStream_t st,
+                   const std::function<int(cudaStream_t)>& enqueue);
 // Add a family measured another way (e.g. device timestamps) to the report.
 void prof_add(const char* family, int launches, double ms);
 

@@ -388,6 +388,7 @@ struct RwkvModel {
     float2* apart = nullptr;  // argmax partials (B x kArgChunks)
     std::vector<void*> allocs;
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+    std::map<std::pair<int, int>, ProfGraph> pgraphs;  // instrumented (profile mode 2)
     cudaStream_t cap = nullptr;
     bool ready = false;
 
@@ -754,9 +755,12 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
 }
 
 int rk_run(RwkvModel* m, int B, bool head, float* trace = nullptr) {
+    auto key = std::make_pair(B, head ? 1 : 0);
+    if (prof_graph() && !trace)  // the step's graph with event nodes around each family
+        return prof_graph_run(&m->pgraphs[key], m->cap, stream(),
+                              [&](cudaStream_t cs) { return enqueue_rk(m, B, head, cs); });
     if (prof_on() || trace)  // bracket kernels / copy out the trace: no graph
         return enqueue_rk(m, B, head, stream(), -1, trace);
-    auto key = std::make_pair(B, head ? 1 : 0);
     auto it = m->graphs.find(key);
     if (it == m->graphs.end()) {
         cudaGraph_t g = nullptr;

@@ -532,6 +532,7 @@ struct SunnyModel {
     bool c_tc = false;
     TcAct c_at, c_v, c_u, c_prev, c_z;
     std::map<std::pair<long long, int>, cudaGraphExec_t> cgraphs;  // (B*65536+Tc, head)
+    std::map<std::pair<long long, int>, ProfGraph> pgraphs;  // instrumented (profile mode 2)
     cudaStream_t cap = nullptr;
     // fused small-batch step (sunny_fused.cu): per-layer descriptors on the
     // device, barrier words, and the arguments common to every launch
@@ -1114,6 +1115,12 @@ int fused_trace_report(SunnyModel* m, const FusedArgs& fa, cudaStream_t st) {
 int run_step(SunnyModel* m, int B, bool with_head) {
     cudaStream_t st = stream();
     const bool tc = m->tc_step && B >= 16;
+    if (prof_graph())  // the step's graph with event nodes around each family
+        return prof_graph_run(&m->pgraphs[std::make_pair((long long)B, with_head ? 1 : 0)],
+                              m->cap, st, [&](cudaStream_t cs) {
+                                  return tc ? enqueue_step_tc(m, B, with_head, cs, m->side)
+                                            : enqueue_step(m, B, with_head, cs);
+                              });
     if (prof_on())  // bracket kernels, no graph
         return tc ? enqueue_step_tc(m, B, with_head, st, st) : enqueue_step(m, B, with_head, st);
     auto key = std::make_pair(B, with_head ? 1 : 0);
@@ -1186,6 +1193,7 @@ int ensure_chunk_bufs(SunnyModel* m, int B, int Tc) {
     m->cseqs = B;
     for (auto& kv : m->cgraphs) cudaGraphExecDestroy(kv.second);  // captured old pointers
     m->cgraphs.clear();
+    m->pgraphs.clear();
     return SN_OK;
 }
 
@@ -1337,8 +1345,11 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
 
 int run_chunk(SunnyModel* m, int B, int Tc, bool head) {
     cudaStream_t st = stream();
-    if (prof_on()) return enqueue_chunk(m, B, Tc, head, st);
     auto key = std::make_pair((long long)B * 65536 + Tc, head ? 1 : 0);
+    if (prof_graph())
+        return prof_graph_run(&m->pgraphs[std::make_pair(-key.first, key.second)], m->cap, st,
+                              [&](cudaStream_t cs) { return enqueue_chunk(m, B, Tc, head, cs); });
+    if (prof_on()) return enqueue_chunk(m, B, Tc, head, st);
     auto it = m->cgraphs.find(key);
     if (it == m->cgraphs.end()) {
         cudaGraph_t g = nullptr;
