@@ -142,6 +142,8 @@ def ref_model():
         L = ctypes.CDLL(str(REF_MODEL_SO))
         L.sn_load.restype = _V
         L.sn_load.argtypes = [_P, _I, _I, _I, _I, _I, _I, _I, _I]
+        L.sn_load_h.restype = _V
+        L.sn_load_h.argtypes = [_P, _I, _I, _I, _I, _I, _I, _I, _I]
         L.sn_free.argtypes = [_V]
         L.sn_reset.argtypes = [_V]
         L.sn_step.argtypes = [_V, _I, _V]

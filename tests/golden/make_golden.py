@@ -200,6 +200,16 @@ def make_sunny(out: Path, ref_root: Path):
     dbg = np.zeros(ndbg, np.float32)
     RM.sn_dbg_layer(h, int(toks[0]), 1, P(dbg))
     RM.sn_free(h)
+    # the reference's fp16-weight runtime (sn_load_h / gemv_h, sunnynet.c:142-167,
+    # 459-578) on the same blob and tokens; every row length here is a
+    # multiple of 16, so gemv_h never reaches its scalar tail
+    hh = RM.sn_load_h(str(blob).encode(), V, cfg.dim, cfg.inner, cfg.rank, cfg.taps,
+                      cfg.layers, 8, 1)
+    assert hh, "reference sn_load_h failed"
+    lch = np.empty((24, V), np.float32)
+    for t in range(24):
+        RM.sn_step(hh, int(toks[t]), P(lch[t]))
+    RM.sn_free(hh)
 
     with torch.no_grad():
         st = m.init_state(1)
@@ -227,6 +237,7 @@ def make_sunny(out: Path, ref_root: Path):
         out / "sunny_tiny.npz",
         dims=np.array([V, cfg.dim, cfg.inner, cfg.rank, cfg.taps, cfg.layers], np.int32),
         tokens=toks.numpy().astype(np.int32), logits_c=lc, logits_torch=lt,
+        logits_c_half=lch,
         prefill_logits_c=lp, dbg_tok=np.int32(toks[0]), dbg_layer1=dbg,
         state_s=s1, state_hist=h1,
         tokens_b=tb.numpy().astype(np.int32), logits_torch_b=lb,

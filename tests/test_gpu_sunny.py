@@ -263,6 +263,20 @@ def test_argmax_and_device_io():
             assert np.array_equal(nx.cpu().numpy(), lg.argmax(1).astype(np.int32))
 
 
+def test_half_weights_match_reference_half_runtime(golden):
+    """sn_load_h against the reference's own fp16-weight runtime (sunnynet.c
+    sn_load_h 459-578, gemv_h 142-167) on the same blob and tokens: the same
+    five layer matrices and head rounded to fp16 (round to nearest even), so
+    only the fp32 summation order differs: 1e-4 of max|ref| per step, while
+    the half path itself sits ~7e-4 away from the fp32 runtime here."""
+    from sunnynet_b200.runtime.model import SnModel
+    g = golden("sunny_tiny.npz")
+    V, D, I, R, K, L = _golden_dims(g)
+    m = SnModel(GOLDEN / "sunny_tiny.usnn", V, D, I, R, K, L, 8, 1, half=True)
+    for t, tok in enumerate(g["tokens"]):
+        check_logits(np.array(m.step(int(tok)), np.float32), g["logits_c_half"][t])
+
+
 def test_half_weights_track_fp32(golden):
     """sn_load_h (reference tests/test_runtime_model.py:123-167): bounded drift."""
     from sunnynet_b200.runtime.model import SnModel
