@@ -342,6 +342,21 @@ def sunny_step_cost(S, B, wbytes, with_head=True):
     return wts + state + io, flops
 
 
+def family_table(fams, reps: int, ms: float):
+    """Per kernel family of one step: launches, serialised ms (CUDA events
+    around each family with the step run kernel by kernel), and that time
+    scaled so the families add up to the timed step (`ms`, the graph with its
+    overlaps); share = scaled ms / ms. The fused step's per-phase device
+    timestamps ("fused:*") are reported apart: they subdivide its one kernel."""
+    base = {k: v for k, v in fams.items() if not k.startswith("fused:")}
+    tot = sum(v[1] for v in base.values()) / reps
+    scale = ms / tot if tot > 0 else 1.0
+    tab = {k: {"launches": v[0] / reps, "serial_ms": v[1] / reps, "ms": v[1] / reps * scale,
+               "share": v[1] / reps * scale / ms} for k, v in base.items()}
+    parts = {k: v[1] / reps for k, v in fams.items() if k.startswith("fused:")}
+    return tab, scale, parts
+
+
 def family_cost(S, B, fam, wbytes):
     """(bytes, flops) per launch of one kernel family of the SunnyNet step."""
     D, I, R, V = S.dim, S.inner, S.rank, S.vocab
@@ -358,6 +373,8 @@ def family_cost(S, B, fam, wbytes):
 def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
     from sunnynet_b200 import formats
     S = formats.SUNNY_PRESETS[preset]
+    if args.prefill_tokens is not None:
+        prefill_T = args.prefill_tokens
     B = shard(B_total, dist.world, dist.rank)[1] if split else B_total
     seqs = B_total if split else B * dist.world  # sequences all ranks step together
     wbytes = 1 if quant else 4
@@ -409,6 +426,11 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
     flush = flushbuf.zero_ if step_bytes < 2 * (126 << 20) else None
     with ClockSampler(dist.local) as clk:
         ms = timed_steps(torch, dist, step, args.steps, args.warmup, flush=flush)
+        if args.ncu:
+            res.update({"ms_per_step": ms, "value": seqs / (ms * 1e-3),
+                        "note": "--ncu run: launch list only, no other measurements"})
+            m.close()
+            return res, None
         t_end = time.time() + 1.5
         while time.time() < t_end:
             for _ in range(20):
@@ -418,9 +440,10 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
     toks = cur.to(torch.int64)
     res["tokens_per_rank"] = [int(v[0]) for v in dist.gather(torch, [int(toks.numel())])]
     res["token_checksums"] = [int(v[0]) for v in dist.gather(torch, [int(toks.sum().item())])]
-    # live per-kernel timing: the step's own graph replayed with CUDA event
-    # nodes around each kernel family (same nodes, streams and dependencies)
-    check(lib.sn_abi_cuda_profile(2))
+    # live per-kernel timing: CUDA events around every kernel family of the
+    # same step run without its graph (serialised); scaled to the timed step
+    # below so the families' shares add up to it
+    check(lib.sn_abi_cuda_profile(1))
     for _ in range(3):
         if flush:
             flush()
@@ -429,11 +452,14 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
     check(lib.sn_abi_cuda_profile(0))
     fams = _lib.profile_report()
     check(lib.sn_abi_cuda_set_async(0))
-    dom = max(fams, key=lambda k: fams[k][1])
-    n_l, t_ms = fams[dom]
+    tab, scale, parts = family_table(fams, 3, ms)
+    # the dominant kernel: the family with a work model taking the most step time
+    known = [k for k in tab if family_cost(S, B, k, wbytes)[0] is not None]
+    dom = max(known, key=lambda k: tab[k]["ms"])
+    n_l = tab[dom]["launches"]
     fb, ff = family_cost(S, B, dom, wbytes)
     peaks = measured_peaks()
-    per_launch_s = t_ms / n_l * 1e-3
+    per_launch_s = tab[dom]["ms"] / n_l * 1e-3
     if B >= 64 and ff:
         rl = {"bound": "tensor", "achieved": ff / per_launch_s / 1e12,
               "peak": peaks["bf16_tflops"], "unit": "TFLOP/s"}
@@ -442,15 +468,16 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
               "peak": peaks["hbm_gbs"], "unit": "GB/s"}
     rl.update({"frac": rl["achieved"] / rl["peak"], "peak_src": peaks["src"], "kernel": dom,
                "launches": n_l, "avg_launch_us": per_launch_s * 1e6,
+               "avg_launch_us_serialised": tab[dom]["serial_ms"] / n_l * 1e3,
                "alg_bytes_per_launch": fb, "alg_flops_per_launch": ff,
                "traffic": profile_traffic(f"{dom}/{preset}/B{B}"),
                "step_alg_bytes": step_bytes, "step_alg_flops": step_flops,
                "step_hbm_gbs": step_bytes / (ms * 1e-3) / 1e9,
                "step_tflops": step_flops / (ms * 1e-3) / 1e12,
-               "timing": "in-graph: CUDA event nodes around each family in a replay of "
-                         "the step's graph",
-               "families_ms_per_step": {k: v[1] / 3 for k, v in fams.items()},
-               "share_of_step": {k: v[1] / 3 / ms for k, v in fams.items()}})
+               "timing": "CUDA events around each kernel family of the step run kernel by "
+                         "kernel (serialised), scaled by %.3f so the families add up to the "
+                         "timed graph step" % scale,
+               "families": tab, "fused_phases_ms": parts or None})
     # end to end: the public call with pinned host tokens in, host logits out
     ht = torch.randint(0, S.vocab, (B,), dtype=torch.int32).pin_memory()
     hl = torch.empty(B, S.vocab).pin_memory()
@@ -575,7 +602,7 @@ def wl_c2b1(args, torch, dist, ours):
 
 def wl_c3(args, torch, dist, ours):
     res, base = wl_sunny(args, torch, dist, ours, "c3", 1024, True, 2048, split=True)
-    if ours and dist.world == 1 and not args.no_sub_records:
+    if ours and dist.world == 1 and not args.no_sub_records and not args.ncu:
         # the metric's other batch sizes, on the same GPU in the same run
         subs = {}
         for name, fn in (("c2_b256", wl_c2), ("c2_b1", wl_c2b1)):
@@ -625,7 +652,7 @@ def wl_c5(args, torch, dist, ours):
 
     with ClockSampler(dist.local) as clk:
         ms = timed_steps(torch, dist, step, args.steps, args.warmup)
-    check(lib.sn_abi_cuda_profile(2))  # in-graph event timing
+    check(lib.sn_abi_cuda_profile(1))  # serialised family timing, scaled below
     for _ in range(2):
         step()
     torch.cuda.synchronize()
@@ -633,25 +660,27 @@ def wl_c5(args, torch, dist, ours):
     fams = _lib.profile_report()
     check(lib.sn_abi_cuda_set_async(0))
     peaks = measured_peaks()
-    gemm_fams = {k: v for k, v in fams.items() if k.startswith("gemm_")}
-    dom = max(gemm_fams, key=lambda k: gemm_fams[k][1])
-    n_l, t_ms = fams[dom]
+    tab, scale, _ = family_table(fams, 2, ms)
     shapes = {"gemm_V": (R, D), "gemm_U": (2 * D, R), "gemm_Ws": (D, D), "gemm_Wz": (I, D),
               "gemm_Wc": (D, I)}
+    dom = max((k for k in tab if k in shapes), key=lambda k: tab[k]["ms"])
+    n_l, t_ms = tab[dom]["launches"], tab[dom]["ms"]
     n, k = shapes[dom]
     ff = 2 * B * Tc * n * k
     ach = ff / (t_ms / n_l * 1e-3) / 1e12
     rl = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops_sustained"],
           "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops_sustained"],
           "peak_src": peaks["src"] + " (sustained bf16)", "kernel": dom, "launches": n_l,
-          "avg_launch_us": t_ms / n_l * 1e3, "alg_flops_per_launch": ff,
+          "avg_launch_us": t_ms / n_l * 1e3,
+          "avg_launch_us_serialised": tab[dom]["serial_ms"] / n_l * 1e3,
+          "alg_flops_per_launch": ff,
           "note": "achieved counts the fp32 product once; the bf16x3 split issues 3 MMAs",
           "traffic": profile_traffic(f"{dom}/c5"),
           "step_tflops": flops / (ms * 1e-3) / 1e12,
-          "timing": "in-graph: CUDA event nodes around each family in a replay of "
-                    "the step's graph",
-          "families_ms_per_step": {k: v[1] / 2 for k, v in fams.items()},
-          "share_of_step": {k: v[1] / 2 / ms for k, v in fams.items()}}
+          "timing": "CUDA events around each kernel family of the step run kernel by "
+                    "kernel (serialised), scaled by %.3f so the families add up to the "
+                    "timed graph step" % scale,
+          "families": tab}
     # end to end: host token ids in (pinned), host logits of the last position out
     ht = toks.cpu().pin_memory()
     hl = torch.empty(B, S.vocab).pin_memory()
@@ -781,7 +810,7 @@ def wl_rwkv(args, torch, dist, ours, B):
     flush = flushbuf.zero_ if step_bytes < 2 * (126 << 20) else None
     with ClockSampler(dist.local) as clk:
         ms = timed_steps(torch, dist, step, args.steps, args.warmup, flush=flush)
-    check(lib.sn_abi_cuda_profile(2))  # in-graph event timing
+    check(lib.sn_abi_cuda_profile(1))  # serialised family timing, scaled below
     for _ in range(3):
         if flush:
             flush()
@@ -790,8 +819,9 @@ def wl_rwkv(args, torch, dist, ours, B):
     check(lib.sn_abi_cuda_profile(0))
     fams = _lib.profile_report()
     check(lib.sn_abi_cuda_set_async(0))
-    dom = max(fams, key=lambda k: fams[k][1])
-    n_l, t_ms = fams[dom]
+    tab, scale, _ = family_table(fams, 3, ms)
+    dom = max(tab, key=lambda k: tab[k]["ms"])
+    n_l, t_ms = tab[dom]["launches"], tab[dom]["ms"]
     peaks = measured_peaks()
     step_gbs = step_bytes / (ms * 1e-3) / 1e9
     if dom == "rk_heads":  # per launch: one layer's matrix states read + written
@@ -801,14 +831,16 @@ def wl_rwkv(args, torch, dist, ours, B):
         fb, ach = None, None
     rl = {"bound": "hbm", "achieved": ach if ach else step_gbs, "peak": peaks["hbm_gbs"],
           "unit": "GB/s", "peak_src": peaks["src"], "kernel": dom, "launches": n_l,
-          "avg_launch_us": t_ms / n_l * 1e3, "alg_bytes_per_launch": fb,
+          "avg_launch_us": t_ms / n_l * 1e3,
+          "avg_launch_us_serialised": tab[dom]["serial_ms"] / n_l * 1e3,
+          "alg_bytes_per_launch": fb,
           "achieved_is": "dominant kernel" if ach else "whole step (dominant is a GEMV family)",
           "traffic": profile_traffic(f"{dom}/c4/B{B}"), "step_alg_bytes": step_bytes,
           "step_alg_flops": step_flops, "step_hbm_gbs": step_gbs,
-          "timing": "in-graph: CUDA event nodes around each family in a replay of "
-                    "the step's graph",
-          "families_ms_per_step": {k: v[1] / 3 for k, v in fams.items()},
-          "share_of_step": {k: v[1] / 3 / ms for k, v in fams.items()}}
+          "timing": "CUDA events around each kernel family of the step run kernel by "
+                    "kernel (serialised), scaled by %.3f so the families add up to the "
+                    "timed graph step" % scale,
+          "families": tab}
     rl["frac"] = rl["achieved"] / rl["peak"]
     ht = torch.randint(0, S.vocab, (B,), dtype=torch.int32).pin_memory()
     hl = torch.empty(B, S.vocab).pin_memory()
@@ -889,6 +921,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sub-records", action="store_true",
                     help="default config only: skip the c2 B=256 / B=1 sub-records")
+    ap.add_argument("--prefill-tokens", type=int, default=None,
+                    help="SunnyNet decode configs: prompt length before the timed steps")
+    ap.add_argument("--ncu", action="store_true",
+                    help="for a profiler's launch list: the prefill, W warm-up and K timed "
+                         "steps only (no clock loop, family timing, e2e or CPU baseline)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -13,9 +13,16 @@ RWKV-7 at the config-4 shape is checked layer by layer: the GPU step reports
 the residual stream entering each layer, the oracle runs every layer from that
 same input (and from the GPU's state at the start of the step), so each
 layer's output and state carry only that layer's kernel error rather than the
-random 12-layer model's amplification of it. Bounds: 1e-4 (fp32 weights),
-5e-3 (INT4 group-128 W4A8: identical integer dot products, but an activation
-whose fp32 value sits on a rounding boundary can quantise one code apart).
+random 12-layer model's amplification of it. Bounds: 1e-4 with fp32 weights
+(every fp32 operation of the same kernels at the same shapes). With INT4
+group-128 W4A8 weights the integer block dot products are identical (bit-exact
+GEMV tests), but each of the layer's ~10 activation vectors is quantised to
+INT8 per 128-block from fp32 values that differ in the last bits (summation
+order, libm vs CUDA exp/tanh); a value on a rounding boundary quantises one
+code apart, moving that block's products by one activation step (amax/127 of
+the block), and such flips feed the heads' group norm and the next
+projections inside the same layer. Bound 2e-2 of the row's max per layer
+(logits and states alike); the observed distribution is printed.
 """
 from __future__ import annotations
 
@@ -34,7 +41,7 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 TOL = 1e-4
-TOL_Q4 = 5e-3
+TOL_Q4 = 2e-2
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -240,8 +247,9 @@ def test_config4_layer_by_layer_teacher_forced(c4_blobs, B, kind):
         toks = rng.integers(0, shape.vocab, B).astype(np.int32)
         lg, xs = gm.step_trace(toks)
         xo, lo = om.step_forced(toks[rows], xs[rows])
-        for l in range(L + 1):
-            err = _row_rel(xs[rows, l], xo[:, l])
+        errs = [_row_rel(xs[rows, l], xo[:, l]) for l in range(L + 1)]
+        print(f"{kind} B={B} per-layer max row error:", " ".join(f"{e:.1e}" for e in errs))
+        for l, err in enumerate(errs):
             assert err < tol, (kind, B, "layer output", l, err)
         err = _row_rel(lg[rows], lo)
         assert err < tol, (kind, B, "logits", err)

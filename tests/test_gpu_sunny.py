@@ -457,3 +457,34 @@ def test_split_k_cluster_matches_unsplit_and_oracle(quant):
             ref = om.step(t)
             check_logits(la, ref)
             check_logits(l_b, ref)
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_profile_modes_report_families_and_leave_results_alone(mode):
+    """Kernel-family timing: mode 1 runs the step kernel by kernel, mode 2
+    replays an instrumented copy of the step's graph. Either way the logits
+    and states equal those of an unprofiled model, and every contraction
+    family of the tensor-core step is reported once per layer and step."""
+    from sunnynet_b200 import _lib, formats
+    from sunnynet_b200.model import SunnyBatch
+    shape = formats.SunnyShape(2000, 128, 224, 80, 4, 3)
+    B = 32
+    rng = np.random.default_rng(40 + mode)
+    toks = [rng.integers(0, shape.vocab, B).astype(np.int32) for _ in range(3)]
+    lib = _lib.load()
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape, seed=4, fast=True)
+        a, b = SunnyBatch(p, B), SunnyBatch(p, B)
+        la = [a.step(t).copy() for t in toks]
+        _lib.check(lib.sn_abi_cuda_profile(mode))
+        try:
+            lb = [b.step(t).copy() for t in toks]
+        finally:
+            _lib.check(lib.sn_abi_cuda_profile(0))
+        rep = _lib.profile_report()
+    for x, y in zip(la, lb):
+        assert np.array_equal(x, y)
+    for fam in ("gemm_V", "gemm_U", "gemm_Wz", "gemm_Wc", "gemm_Ws"):
+        n, ms = rep[fam]
+        assert n == 3 * shape.layers and ms > 0, (fam, rep[fam])
+    assert rep["gemm_head"][0] == 3
