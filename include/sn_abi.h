@@ -124,6 +124,7 @@ sn_status sn_abi_cuda_set_stream(void* cuda_stream);
 sn_status sn_abi_cuda_set_async(int32_t on);          /* device-pointer calls only enqueue */
 sn_status sn_abi_cuda_synchronize(void);              /* waits; reports deferred errors */
 int32_t   sn_abi_last_error(char* buf, int32_t buflen); /* message of the last failure */
+void      sn_abi_clear_error(void);                    /* empties it (this thread) */
 int32_t   sn_abi_cuda_scan_mode(int32_t mode);        /* 0 exact (default), 1 chunked; returns old */
 /* Kernel-family timing with CUDA events (1 = start and clear, 0 = stop). While
  * on, model steps run without their CUDA graph so each kernel can be bracketed. */

@@ -24,6 +24,7 @@ HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "_build" / "liboracle.so"
 REF_ABI_SO = HERE / "_ref" / "libsnref_abi.so"
 REF_MODEL_SO = HERE / "_ref" / "libsnref_model.so"
+REF_KERNELS_SO = HERE / "_ref" / "libsnref_kernels.so"
 
 _F = ctypes.POINTER(ctypes.c_float)
 _V, _I, _P = ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p
@@ -52,6 +53,7 @@ def _stale(so: Path, srcs) -> bool:
 _lib = None
 _ref_abi = None
 _ref_model = None
+_ref_kernels = None
 
 
 def lib():
@@ -91,6 +93,11 @@ def lib():
     L.or_rk_step.argtypes = [_V, _V, _V]
     L.or_rk_dbg.argtypes = [_V, _I, _I, _V]
     L.or_rk_get_state.argtypes = [_V, _I, _V, _V]
+    L.or_core_fwd.argtypes = [_V] * 6 + [_I] * 3
+    L.or_core_bwd.argtypes = [_V] * 11 + [_I] * 3
+    L.or_step_core.argtypes = [_V] * 5 + [_I] * 2
+    L.or_dw_step.argtypes = [_V] * 4 + [_I] * 3
+    L.or_scan_f32.argtypes = [_V] * 5 + [_I] * 3
     L.or_rk_set_state.argtypes = [_V, _I, _V, _V]
     L.or_rk_step_forced.argtypes = [_V, _V, _V, _V, _V]
     _lib = L
@@ -158,6 +165,26 @@ def ref_model():
     return _ref_model
 
 
+def ref_kernels():
+    """The reference's kernels module (scan_avx2.c, core_avx2.c, step_avx2.c)
+    built with its own flags into oracle/_ref, bound as kernels/__init__.py
+    binds it."""
+    global _ref_kernels
+    if _ref_kernels is None:
+        if not REF_KERNELS_SO.exists():
+            raise FileNotFoundError(REF_KERNELS_SO)
+        L = ctypes.CDLL(str(REF_KERNELS_SO))
+        L.scan_f32.argtypes = [_V] * 5 + [_I] * 3
+        L.scan_bwd_f32.argtypes = [_V] * 8 + [_I] * 3
+        L.core_fwd_f32.argtypes = [_V] * 6 + [_I] * 3
+        L.core_bwd_f32.argtypes = [_V] * 11 + [_I] * 3
+        L.dw_step_f32.argtypes = [_V] * 4 + [_I] * 3
+        L.step_core_f32.argtypes = [_V] * 5 + [_I] * 2
+        L.sn_set_threads.argtypes = [_I]
+        _ref_kernels = L
+    return _ref_kernels
+
+
 def ptr(a: np.ndarray):
     assert a.flags["C_CONTIGUOUS"]
     return ctypes.c_void_p(a.ctypes.data)
@@ -181,6 +208,54 @@ def recur_bwd(a, b, s0, out, dout, gated):
     lib().or_recur_bwd(ptr(a), ptr(b), ptr(s0), ptr(out), ptr(dout), ptr(da), ptr(db), ptr(ds0),
                        B, T, N, int(gated))
     return da, db, ds0
+
+
+def core_fwd(q, delta, s0):
+    """core_avx2.c core_fwd_f32: q (B,T,2D), delta (D), s0 (B,D) -> states, u, p."""
+    B, T, D2 = q.shape
+    D = D2 // 2
+    st, u, p = (np.zeros((B, T, D), np.float32) for _ in range(3))
+    lib().or_core_fwd(ptr(q), ptr(delta), ptr(s0), ptr(st), ptr(u), ptr(p), B, T, D)
+    return st, u, p
+
+
+def core_bwd(q, delta, s0, states, u, p, dstate, du):
+    """core_avx2.c core_bwd_f32 -> (dq, ddelta, ds0)."""
+    B, T, D2 = q.shape
+    D = D2 // 2
+    dq = np.zeros_like(q)
+    dd = np.zeros(D, np.float32)
+    ds0 = np.zeros((B, D), np.float32)
+    lib().or_core_bwd(ptr(q), ptr(delta), ptr(s0), ptr(states), ptr(u), ptr(p), ptr(dstate),
+                      ptr(du), ptr(dq), ptr(dd), ptr(ds0), B, T, D)
+    return dq, dd, ds0
+
+
+def step_core(q, delta, s):
+    """step_avx2.c step_core_f32: q (B,2D), s (B,D) -> (u, s_new)."""
+    B, D2 = q.shape
+    D = D2 // 2
+    sn = np.zeros((B, D), np.float32)
+    u = np.zeros((B, D), np.float32)
+    lib().or_step_core(ptr(q), ptr(delta), ptr(s), ptr(sn), ptr(u), B, D)
+    return u, sn
+
+
+def scan_f32(p, nu, s0):
+    """scan_avx2.c scan_f32: s = p*s + (1-p)*nu, lane rule on every channel."""
+    B, T, N = p.shape
+    out = np.empty_like(p)
+    send = np.empty((B, N), np.float32)
+    lib().or_scan_f32(ptr(p), ptr(nu), ptr(s0), ptr(out), ptr(send), B, T, N)
+    return out, send
+
+
+def dw_step(x, hist, w):
+    """step_avx2.c dw_step_f32: x (B,D), hist (B,K-1,D), w (K,D) -> acc (B,D)."""
+    B, D = x.shape
+    acc = np.empty((B, D), np.float32)
+    lib().or_dw_step(ptr(x), ptr(hist), ptr(w), ptr(acc), B, D, w.shape[0])
+    return acc
 
 
 def recur_step(a, b, s, gated):

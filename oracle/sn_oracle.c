@@ -992,3 +992,166 @@ void or_rk_get_state(const OrRwkv* m, int seq, float* S, float* shift) {
     memcpy(S, m->S + (size_t)seq * sz, sizeof(float) * sz);
     memcpy(shift, m->shift + (size_t)seq * m->L * 2 * m->D, sizeof(float) * (size_t)m->L * 2 * m->D);
 }
+
+/* ------------------------------------------- kernels module (sunnynet/kernels)
+ * Restatements of the reference's AVX2 training/step kernels, one lane at a
+ * time in the same operation order. These files are compiled as GNU C (no
+ * -std=c11, kernels/__init__.py:24-36), which would allow the compiler to
+ * contract the N % 8 scalar tails into FMAs; the reference build leaves them
+ * as separate multiply and add, which these restatements follow and the
+ * tests check against the reference library built with its own flags. */
+
+/* core_avx2.c:17-18 lane rolls within a group of 8: v[i+1], v[i+2], v[i-1], v[i-2] */
+#define GRP(i, k) (((i) & ~7) + ((((i) & 7) + (k) + 8) & 7))
+
+/* core_avx2.c:34-79: q (B,T,2D) = [u_raw | gate], delta (D), s0 (B,D) ->
+ * states, u, p (B,T,D). Groups of 8 channels (D % 8 channels are not written). */
+void or_core_fwd(const float* q, const float* delta, const float* s0, float* states, float* uo,
+                 float* po, int B, int T, int D) {
+    const int DV = D & ~7;
+#pragma omp parallel for schedule(static)
+    for (int b = 0; b < B; ++b) {
+        float* s = (float*)malloc(sizeof(float) * (DV > 0 ? DV : 1));
+        float* e = (float*)malloc(sizeof(float) * (DV > 0 ? DV : 1));
+        for (int d = 0; d < DV; ++d) s[d] = s0[(size_t)b * D + d];
+        for (int t = 0; t < T; ++t) {
+            const float* qt = q + ((size_t)b * T + t) * 2 * D;
+            const size_t o = ((size_t)b * T + t) * D;
+            for (int d = 0; d < DV; ++d) e[d] = expf(0.0f - qt[D + d]);
+            for (int d = 0; d < DV; ++d) {
+                const float sig = 1.0f / (1.0f + e[d]);
+                const float s1 = 1.0f / (1.0f + e[d] / e[GRP(d, 1)]);
+                const float s2 = 1.0f / (1.0f + e[d] / e[GRP(d, 2)]);
+                const float w = s1 * s2;
+                const float u = qt[d] * w;
+                const float p = fmaf(delta[d], sig, 1.0f - delta[d]);
+                s[d] = fmaf(p, s[d], (1.0f - p) * u);
+                states[o + d] = s[d];
+                uo[o + d] = u;
+                po[o + d] = p;
+            }
+        }
+        free(s);
+        free(e);
+    }
+}
+
+/* core_avx2.c:84-148: reverse pass. ddelta is accumulated (+=) over the
+ * sequences in order b = 0, 1, ... (the reference adds them with OpenMP
+ * atomics in whatever order its threads finish). */
+void or_core_bwd(const float* q, const float* delta, const float* s0, const float* states,
+                 const float* uo, const float* po, const float* dstate, const float* du_in,
+                 float* dq, float* ddelta, float* ds0, int B, int T, int D) {
+    const int DV = D & ~7;
+    float* acc = (float*)calloc((size_t)B * (DV > 0 ? DV : 1), sizeof(float));
+#pragma omp parallel for schedule(static)
+    for (int b = 0; b < B; ++b) {
+        const size_t n = DV > 0 ? DV : 1;
+        float* ds = (float*)calloc(n, sizeof(float));
+        float* e = (float*)malloc(sizeof(float) * n);
+        float* a1 = (float*)malloc(sizeof(float) * n);
+        float* a2 = (float*)malloc(sizeof(float) * n);
+        float* dp = (float*)malloc(sizeof(float) * n);
+        float* sg = (float*)malloc(sizeof(float) * n);
+        float* dacc = acc + (size_t)b * n;
+        for (int t = T - 1; t >= 0; --t) {
+            const size_t qo = ((size_t)b * T + t) * 2 * D;
+            const size_t o = ((size_t)b * T + t) * D;
+            for (int d = 0; d < DV; ++d) e[d] = expf(0.0f - q[qo + D + d]);
+            for (int d = 0; d < DV; ++d) {
+                ds[d] = ds[d] + dstate[o + d];
+                const float u = uo[o + d], p = po[o + d];
+                const float sprev = t > 0 ? states[o - D + d] : s0[(size_t)b * D + d];
+                dp[d] = ds[d] * (sprev - u);
+                const float du = fmaf(ds[d], 1.0f - p, du_in[o + d]);
+                ds[d] = ds[d] * p;
+                const float ur = q[qo + d];
+                const float sig = 1.0f / (1.0f + e[d]);
+                const float s1 = 1.0f / (1.0f + e[d] / e[GRP(d, 1)]);
+                const float s2 = 1.0f / (1.0f + e[d] / e[GRP(d, 2)]);
+                const float w = s1 * s2;
+                dq[qo + d] = du * w;
+                const float dw = du * ur;
+                const float ds1 = dw * s2, ds2 = dw * s1;
+                a1[d] = ds1 * (s1 * (1.0f - s1));
+                a2[d] = ds2 * (s2 * (1.0f - s2));
+                sg[d] = sig;
+            }
+            for (int d = 0; d < DV; ++d) {
+                float dg = a1[d] + a2[d];
+                dg = dg - a1[GRP(d, -1)];
+                dg = dg - a2[GRP(d, -2)];
+                dg = fmaf(dp[d] * delta[d], sg[d] * (1.0f - sg[d]), dg);
+                dacc[d] = fmaf(dp[d], sg[d] - 1.0f, dacc[d]);
+                dq[qo + D + d] = dg;
+            }
+        }
+        for (int d = 0; d < DV; ++d) ds0[(size_t)b * D + d] = ds[d];
+        free(ds); free(e); free(a1); free(a2); free(dp); free(sg);
+    }
+    for (int b = 0; b < B; ++b)
+        for (int d = 0; d < DV; ++d) ddelta[d] = ddelta[d] + acc[(size_t)b * DV + d];
+    free(acc);
+}
+
+/* step_avx2.c:54-86: one step of core_fwd: q (B,2D), s (B,D) -> s_new, u (B,D). */
+void or_step_core(const float* q, const float* delta, const float* s, float* s_new, float* uo,
+                  int B, int D) {
+    const int DV = D & ~7;
+    float* e = (float*)malloc(sizeof(float) * (DV > 0 ? DV : 1));
+    for (int b = 0; b < B; ++b) {
+        const float* qb = q + (size_t)b * 2 * D;
+        for (int d = 0; d < DV; ++d) e[d] = expf(0.0f - qb[D + d]);
+        for (int d = 0; d < DV; ++d) {
+            const float sig = 1.0f / (1.0f + e[d]);
+            const float s1 = 1.0f / (1.0f + e[d] / e[GRP(d, 1)]);
+            const float s2 = 1.0f / (1.0f + e[d] / e[GRP(d, 2)]);
+            const float u = qb[d] * (s1 * s2);
+            const float p = fmaf(delta[d], sig, 1.0f - delta[d]);
+            uo[(size_t)b * D + d] = u;
+            s_new[(size_t)b * D + d] = fmaf(p, s[(size_t)b * D + d], (1.0f - p) * u);
+        }
+    }
+    free(e);
+}
+
+/* step_avx2.c:24-50: acc = w[K-1]*x + sum_j w[K-2-j]*hist[j]: an FMA chain
+ * on the 8-wide lanes, separate multiply and add on the D % 8 tail (the
+ * reference build leaves that scalar loop uncontracted; pinned by test). */
+void or_dw_step(const float* x, const float* hist, const float* w, float* acc, int B, int D,
+                int taps) {
+    const int k = taps - 1, DV = D & ~7;
+    for (int b = 0; b < B; ++b)
+        for (int d = 0; d < D; ++d) {
+            float a = x[(size_t)b * D + d] * w[(size_t)(taps - 1) * D + d];
+            for (int j = 0; j < k; ++j) {
+                const float hv = hist[((size_t)b * k + j) * D + d];
+                const float wv = w[(size_t)(taps - 2 - j) * D + d];
+                if (d < DV) {
+                    a = fmaf(hv, wv, a);
+                } else {
+                    const float m = hv * wv;
+                    a = a + m;
+                }
+            }
+            acc[(size_t)b * D + d] = a;
+        }
+}
+/* scan_avx2.c:12-45 scan_f32: the gated scan with (a, u) = (p, nu); the
+ * reference build contracts its N % 8 tail to fma(p, s, (1-p)*nu), the lane
+ * rule, so every channel follows it. */
+void or_scan_f32(const float* p, const float* nu, const float* s0, float* out, float* send,
+                 int B, int T, int N) {
+#pragma omp parallel for schedule(static)
+    for (int bb = 0; bb < B; ++bb)
+        for (int d = 0; d < N; ++d) {
+            float s = s0[(size_t)bb * N + d];
+            for (int t = 0; t < T; ++t) {
+                const size_t o = ((size_t)bb * T + t) * N + d;
+                s = fmaf(p[o], s, (1.0f - p[o]) * nu[o]);
+                out[o] = s;
+            }
+            send[(size_t)bb * N + d] = s;
+        }
+}
+#undef GRP

@@ -70,6 +70,19 @@ void or_rk_set_state(OrRwkv* m, int seq, const float* S, const float* shift);
 void or_rk_step_forced(OrRwkv* m, const int32_t* tokens, const float* xs_in, float* xs_out,
                        float* logits);
 
+/* ---- kernels module (reference sunnynet/kernels/{core,step}_avx2.c) ---- */
+void or_core_fwd(const float* q, const float* delta, const float* s0, float* states, float* u,
+                 float* p, int B, int T, int D);
+void or_core_bwd(const float* q, const float* delta, const float* s0, const float* states,
+                 const float* u, const float* p, const float* dstate, const float* du_in,
+                 float* dq, float* ddelta, float* ds0, int B, int T, int D);
+void or_step_core(const float* q, const float* delta, const float* s, float* s_new, float* u,
+                  int B, int D);
+void or_dw_step(const float* x, const float* hist, const float* w, float* acc, int B, int D,
+                int taps);
+void or_scan_f32(const float* p, const float* nu, const float* s0, float* out, float* send,
+                 int B, int T, int N);
+
 #ifdef __cplusplus
 }
 #endif

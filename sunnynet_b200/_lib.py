@@ -41,6 +41,7 @@ SIGNATURES = {
     "sn_abi_cuda_set_async": (I32, [I32]),
     "sn_abi_cuda_synchronize": (I32, []),
     "sn_abi_last_error": (I32, [P, I32]),
+    "sn_abi_clear_error": (None, []),
     "sn_abi_cuda_scan_mode": (I32, [I32]),
     "sn_abi_cuda_profile": (I32, [I32]),
     "sn_abi_cuda_profile_report": (I32, [P, I32]),
@@ -91,6 +92,13 @@ SIGNATURES = {
     "sn_get_threads": (CI, []),
     "sn_recommended_threads": (CI, []),
     "sn_dbg_layer": (None, [V, CI, CI, V]),
+    # sn_kernels.h (the reference's kernels module)
+    "scan_f32": (None, [V, V, V, V, V, CI, CI, CI]),
+    "scan_bwd_f32": (None, [V, V, V, V, V, V, V, V, CI, CI, CI]),
+    "core_fwd_f32": (None, [V, V, V, V, V, V, CI, CI, CI]),
+    "core_bwd_f32": (None, [V, V, V, V, V, V, V, V, V, V, V, CI, CI, CI]),
+    "step_core_f32": (None, [V, V, V, V, V, CI, CI]),
+    "dw_step_f32": (None, [V, V, V, V, CI, CI, CI]),
     # rwkv7.h
     "sn_rk_load": (V, [P]),
     "sn_rk_free": (None, [V]),

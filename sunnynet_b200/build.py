@@ -23,7 +23,8 @@ BUILD = PKG / "_build"
 LIB = PKG / "libsunnynet_cuda.so"
 
 SOURCES = ["runtime.cu", "abi.cu", "recur.cu", "quant4.cu", "gemm.cu", "tc_gemm.cu", "sunny.cu",
-           "rwkv7.cu", "scan_noalloc.cu", "sunny_fused.cu", "w4a8_tc.cu", "argmax.cu"]
+           "rwkv7.cu", "scan_noalloc.cu", "sunny_fused.cu", "w4a8_tc.cu", "argmax.cu",
+           "train.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
          "-I", str(INCLUDE), "-I", str(CSRC)]

@@ -17,9 +17,16 @@ int launch_scan(const float* a, const float* b, const float* s0, float* out, flo
 // send_ld (a layer's rows of a [seq][layer][N] state array), optionally also
 // writing the state entering each position as bf16 planes ph / pl (row t:
 // s0 for t = 0, out row t - 1 after), the input of a following contraction.
+// nv: channels [0, nv) use the reference's 8-lane FMA rule, [nv, N) its
+// scalar rule (separate multiply and add); < 0 = N - N % 8, as recur.c.
 int launch_scan_strided(const float* a, const float* b, const float* s0, long long s0_ld,
                         float* out, float* send, long long send_ld, int B, int T, int N,
-                        int gated, __nv_bfloat16* ph, __nv_bfloat16* pl, cudaStream_t st);
+                        int gated, __nv_bfloat16* ph, __nv_bfloat16* pl, cudaStream_t st,
+                        int nv = -1);
+// Reverse pass of the scan (sn_recur_bwd) on device arrays.
+int launch_scan_bwd(const float* a, const float* b, const float* s0, const float* out,
+                    const float* dout, float* da, float* db, float* ds0, int B, int T, int N,
+                    int gated, cudaStream_t st);
 int launch_step(const float* a, const float* b, float* s, int B, int N, int gated,
                 cudaStream_t st);
 // Scan mode 1 (chunked in T): chunk length for the shape (0 when even one

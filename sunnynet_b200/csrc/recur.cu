@@ -258,7 +258,7 @@ __global__ void __launch_bounds__(128)
 template <int CW>
 int launch_scan_cw(const float* a, const float* b, const float* s0, float* out, float* send,
                    int B, int T, int N, int gated, int vec, long long s0_ld, long long send_ld,
-                   __nv_bfloat16* ph, __nv_bfloat16* pl, cudaStream_t st) {
+                   __nv_bfloat16* ph, __nv_bfloat16* pl, cudaStream_t st, int nv) {
     static bool attr = false;
     const int nch = (T + kTC - 1) / kTC;
     const size_t smem = ScanCfg<CW>::smem(nch < ScanCfg<CW>::S ? nch : ScanCfg<CW>::S);
@@ -270,7 +270,7 @@ int launch_scan_cw(const float* a, const float* b, const float* s0, float* out, 
         attr = true;
     }
     dim3 grid((N + CW - 1) / CW, B);
-    scan_exact_kernel<CW><<<grid, 128, smem, st>>>(a, b, s0, out, send, T, N, N - N % 8, gated,
+    scan_exact_kernel<CW><<<grid, 128, smem, st>>>(a, b, s0, out, send, T, N, nv, gated,
                                                    vec, s0_ld, send_ld, ph, pl, rt().d_err);
     return cuda_check(cudaGetLastError(), "scan launch");
 }
@@ -545,16 +545,18 @@ int launch_scan(const float* a, const float* b, const float* s0, float* out, flo
 
 int launch_scan_strided(const float* a, const float* b, const float* s0, long long s0_ld,
                         float* out, float* send, long long send_ld, int B, int T, int N,
-                        int gated, __nv_bfloat16* ph, __nv_bfloat16* pl, cudaStream_t st) {
+                        int gated, __nv_bfloat16* ph, __nv_bfloat16* pl, cudaStream_t st,
+                        int nv) {
     if (B > 65535) return fail(SN_E_INVAL, "recur_scan: B=%d exceeds 65535", B);
+    if (nv < 0) nv = N - N % 8;
     // (plane stores are 8-byte vectors of four channels on the vector path)
     const bool vec = N % 4 == 0 && ((uintptr_t)a % 16 == 0) && ((uintptr_t)b % 16 == 0) &&
                      ((uintptr_t)out % 16 == 0) &&
                      (!ph || ((uintptr_t)ph % 8 == 0 && (uintptr_t)pl % 8 == 0));
     switch (pick_cw(B, N)) {
-        case 32: return launch_scan_cw<32>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st);
-        case 16: return launch_scan_cw<16>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st);
-        default: return launch_scan_cw<8>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st);
+        case 32: return launch_scan_cw<32>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st, nv);
+        case 16: return launch_scan_cw<16>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st, nv);
+        default: return launch_scan_cw<8>(a, b, s0, out, send, B, T, N, gated, vec, s0_ld, send_ld, ph, pl, st, nv);
     }
 }
 

@@ -324,6 +324,8 @@ int32_t sn_abi_cuda_profile_report(char* buf, int32_t buflen) {
     return need;
 }
 
+void sn_abi_clear_error(void) { g_last_err[0] = '\0'; }
+
 int32_t sn_abi_last_error(char* buf, int32_t buflen) {
     int32_t need = (int32_t)strlen(g_last_err) + 1;
     if (buf && buflen >= need) memcpy(buf, g_last_err, (size_t)need);

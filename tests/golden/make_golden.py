@@ -383,19 +383,21 @@ class _RecFn:
 def make_ref_bindings(out: Path, ref_root: Path):
     """Every symbol the reference's ctypes loaders bind (runtime/__init__.py
     load_runtime, model.py _load, abi.py load_abi, quant.py load_quant,
-    rwkv7_c.py _load) with the argtypes/restype they set, and every function
-    the reference's runtime headers declare."""
+    rwkv7_c.py _load, kernels/__init__.py load_kernel) with the argtypes/
+    restype they set, and every function the reference's runtime headers
+    declare."""
     import importlib
     import json
     import re
     sys.path.insert(0, str(ref_root))
     loaders = {"__init__": "load_runtime", "model": "_load", "abi": "load_abi",
-               "quant": "load_quant", "rwkv7_c": "_load"}
+               "quant": "load_quant", "rwkv7_c": "_load", "kernels": "load_kernel"}
     real_cdll = ctypes.CDLL
     res = {"loaders": {}, "headers": {}}
     try:
         for modname, fn in loaders.items():
-            full = "sunnynet.runtime" + ("" if modname == "__init__" else "." + modname)
+            full = ("sunnynet.kernels" if modname == "kernels" else
+                    "sunnynet.runtime" + ("" if modname == "__init__" else "." + modname))
             mod = importlib.import_module(full)
             rec = _Recorder()
             ctypes.CDLL = lambda *a, **k: rec
@@ -404,7 +406,9 @@ def make_ref_bindings(out: Path, ref_root: Path):
                 if hasattr(mod, attr):
                     setattr(mod, attr, val)
             getattr(mod, fn)()
-            res["loaders"][f"runtime/{modname}.py:{fn}"] = {
+            where = ("kernels/__init__.py" if modname == "kernels" else
+                     f"runtime/{modname}.py")
+            res["loaders"][f"{where}:{fn}"] = {
                 name: {"restype": _ctype_name(f.restype),
                        "argtypes": [_ctype_name(t) for t in (f.argtypes or [])]}
                 for name, f in sorted(object.__getattribute__(rec, "fns").items())}

@@ -28,7 +28,7 @@ def _declared_functions():
         txt = re.sub(r"#.*", "", txt)
         for m in re.finditer(r"\b([A-Za-z_][A-Za-z0-9_]*)\s*\(", txt):
             n = m.group(1)
-            if n.startswith("sn_"):
+            if n.startswith("sn_") or n.endswith("_f32"):
                 names.add(n)
     return names
 
@@ -174,10 +174,11 @@ def test_reference_loaders_run_against_this_library(monkeypatch):
     real = ctypes.CDLL
     monkeypatch.setattr(ctypes, "CDLL", lambda *a, **k: real(str(_lib.LIB_PATH)))
     loaders = {"__init__": "load_runtime", "model": "_load", "abi": "load_abi",
-               "quant": "load_quant", "rwkv7_c": "_load"}
+               "quant": "load_quant", "rwkv7_c": "_load", "kernels": "load_kernel"}
     try:
         for modname, fn in loaders.items():
-            full = "sunnynet.runtime" + ("" if modname == "__init__" else "." + modname)
+            full = ("sunnynet.kernels" if modname == "kernels" else
+                    "sunnynet.runtime" + ("" if modname == "__init__" else "." + modname))
             mod = importlib.import_module(full)
             for attr, val in (("_find_gcc", lambda: "gcc"), ("_needs_rebuild", lambda: False),
                               ("_lib", None)):

@@ -362,3 +362,90 @@ def test_sunny_row_parallel_equals_sequence_parallel():
             lm = many.step(t)
             lf = few.step(t[:2])
             assert np.array_equal(lf, lm[:2])
+
+
+# ------------------------------------------ kernels module (sunnynet/kernels)
+def _core_inputs(B, T, D, seed):
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((B, T, 2 * D)).astype(np.float32)
+    H = np.exp(np.linspace(np.log(2.0), np.log(8192.0), D))
+    delta = (1.0 / H).astype(np.float32)
+    s0 = rng.standard_normal((B, D)).astype(np.float32)
+    dstate = rng.standard_normal((B, T, D)).astype(np.float32)
+    du = rng.standard_normal((B, T, D)).astype(np.float32)
+    return q, delta, s0, dstate, du
+
+
+needs_ref_kernels = pytest.mark.skipif(not oracle.REF_KERNELS_SO.exists(),
+                                       reason="oracle/_ref kernels module not built")
+
+
+@needs_ref_kernels
+@pytest.mark.parametrize("B,T,D", [(1, 50, 16), (3, 33, 64), (2, 7, 40)])
+def test_core_fwd_bwd_bit_exact_vs_reference_kernels(B, T, D):
+    """core_fwd_f32 / core_bwd_f32 (core_avx2.c:34-148) and step_core_f32
+    (step_avx2.c:54-86): the restatement is bit-identical (ddelta too: with
+    one OpenMP thread the reference adds the sequences in order)."""
+    R = oracle.ref_kernels()
+    R.sn_set_threads(1)
+    q, delta, s0, dstate, du = _core_inputs(B, T, D, B * 100 + D)
+    st, u, p = (np.zeros((B, T, D), np.float32) for _ in range(3))
+    R.core_fwd_f32(P(q), P(delta), P(s0), P(st), P(u), P(p), B, T, D)
+    ost, ou, op = oracle.core_fwd(q, delta, s0)
+    assert np.array_equal(st, ost) and np.array_equal(u, ou) and np.array_equal(p, op)
+    dq = np.zeros_like(q)
+    dd = np.zeros(D, np.float32)
+    ds0 = np.zeros((B, D), np.float32)
+    R.core_bwd_f32(P(q), P(delta), P(s0), P(st), P(u), P(p), P(dstate), P(du), P(dq), P(dd),
+                   P(ds0), B, T, D)
+    odq, odd, ods0 = oracle.core_bwd(q, delta, s0, st, u, p, dstate, du)
+    assert np.array_equal(dq, odq) and np.array_equal(ds0, ods0) and np.array_equal(dd, odd)
+    q1 = np.ascontiguousarray(q[:, 0])
+    sn = np.zeros((B, D), np.float32)
+    u1 = np.zeros((B, D), np.float32)
+    R.step_core_f32(P(q1), P(delta), P(s0), P(sn), P(u1), B, D)
+    ou1, osn = oracle.step_core(q1, delta, s0)
+    assert np.array_equal(u1, ou1) and np.array_equal(sn, osn)
+    assert np.array_equal(osn, ost[:, 0]) and np.array_equal(ou1, ou[:, 0])
+
+
+@needs_ref_kernels
+@pytest.mark.parametrize("B,D,taps", [(2, 64, 4), (3, 13, 4), (1, 40, 3)])
+def test_dw_step_bit_exact_vs_reference_kernels(B, D, taps):
+    R = oracle.ref_kernels()
+    rng = np.random.default_rng(D)
+    x = rng.standard_normal((B, D)).astype(np.float32)
+    h = rng.standard_normal((B, taps - 1, D)).astype(np.float32)
+    w = rng.standard_normal((taps, D)).astype(np.float32)
+    acc = np.zeros((B, D), np.float32)
+    R.dw_step_f32(P(x), P(h), P(w), P(acc), B, D, taps)
+    assert np.array_equal(acc, oracle.dw_step(x, h, w))
+
+
+@needs_ref_kernels
+@pytest.mark.parametrize("B,T,N", [(2, 37, 13), (1, 300, 1024), (3, 20, 7)])
+def test_kernels_scan_matches_recur_forms(B, T, N):
+    """scan_f32 / scan_bwd_f32 (scan_avx2.c) are the gated recur_scan /
+    recur_bwd with (a, u) = (p, nu); the module is GNU C, whose scalar tail
+    (N % 8 channels) the compiler may contract: the oracle's gated scan must
+    equal it on the vector channels, and its bwd everywhere."""
+    R = oracle.ref_kernels()
+    rng = np.random.default_rng(N)
+    p = rng.uniform(0.3, 1.0, (B, T, N)).astype(np.float32)
+    nu = rng.standard_normal((B, T, N)).astype(np.float32)
+    s0 = rng.standard_normal((B, N)).astype(np.float32)
+    out = np.zeros_like(p)
+    se = np.zeros((B, N), np.float32)
+    R.scan_f32(P(p), P(nu), P(s0), P(out), P(se), B, T, N)
+    ro, rs = oracle.recur_scan(p, nu, s0, 1)
+    nv = N - N % 8
+    assert np.array_equal(out[..., :nv], ro[..., :nv])
+    dout = rng.standard_normal((B, T, N)).astype(np.float32)
+    dp, dn = np.zeros_like(p), np.zeros_like(p)
+    d0 = np.zeros((B, N), np.float32)
+    R.scan_bwd_f32(P(p), P(nu), P(s0), P(out), P(dout), P(dp), P(dn), P(d0), B, T, N)
+    ra, rb, r0 = oracle.recur_bwd(p, nu, s0, out, dout, 1)
+    assert np.array_equal(dp, ra) and np.array_equal(dn, rb) and np.array_equal(d0, r0)
+    # every channel, the scalar tail included, follows the lane rule
+    fo, fs = oracle.scan_f32(p, nu, s0)
+    assert np.array_equal(out, fo) and np.array_equal(se, fs)
