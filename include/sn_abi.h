@@ -178,6 +178,13 @@ sn_status   sn_abi_sunny_prefill_chunked(SnAbiSunny* m, const int32_t* tokens, i
 /* state of sequences [0,B): s (B,L,D), hist (B,L,K-1,D), hist[.,.,0] newest */
 sn_status   sn_abi_sunny_get_state(SnAbiSunny* m, int32_t B, float* s, float* hist);
 sn_status   sn_abi_sunny_set_state(SnAbiSunny* m, int32_t B, const float* s, const float* hist);
+/* No reference counterpart (serving with continuous batching): the same for
+ * sequences [seq0, seq0 + n) of the handle, and a reset of just those. */
+sn_status   sn_abi_sunny_get_state_at(SnAbiSunny* m, int32_t seq0, int32_t n, float* s,
+                                      float* hist);
+sn_status   sn_abi_sunny_set_state_at(SnAbiSunny* m, int32_t seq0, int32_t n, const float* s,
+                                      const float* hist);
+sn_status   sn_abi_sunny_reset_at(SnAbiSunny* m, int32_t seq0, int32_t n);
 
 /* RWKV-7 batched (SN_CAP_BATCH): a handle owning nseq sequences. */
 SnAbiRwkv7* sn_abi_rwkv7_load_batch(const char* blob_path, int32_t nseq);

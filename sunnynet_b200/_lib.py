@@ -61,6 +61,9 @@ SIGNATURES = {
     "sn_abi_sunny_prefill_chunked": (I32, [V, V, I32, I32, I32, V]),
     "sn_abi_sunny_get_state": (I32, [V, I32, V, V]),
     "sn_abi_sunny_set_state": (I32, [V, I32, V, V]),
+    "sn_abi_sunny_get_state_at": (I32, [V, I32, I32, V, V]),
+    "sn_abi_sunny_set_state_at": (I32, [V, I32, I32, V, V]),
+    "sn_abi_sunny_reset_at": (I32, [V, I32, I32]),
     "sn_abi_rwkv7_load_batch": (V, [P, I32]),
     "sn_abi_rwkv7_step_batch": (I32, [V, V, I32, V]),
     "sn_abi_rwkv7_step_argmax": (I32, [V, V, I32, V]),

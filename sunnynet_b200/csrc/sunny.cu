@@ -189,6 +189,328 @@ __global__ void ln_split_kernel(int n, const float* __restrict__ X, long long ld
         store_split(hi, lo, o + i, __fmul_rn(__fmul_rn(xr[i] - mean, r), g[i]) + c[i]);
 }
 
+
+// --------------------------------------------- row kernels: one warp per row
+// Rows of up to 128 * NV floats (n % 4 == 0, 16-byte aligned rows) are held in
+// registers as float4 (lane j covers columns 4 * (lane + 32 k)); the LN
+// statistics are warp sums (no block barriers), every load is 16 bytes. Eight
+// rows per 256-thread CTA. The launchers below pick these whenever the shape
+// allows, for every path alike (the step, the split-launch step, the fused
+// B <= 8 step's fallback, prefill), so paths that must agree bit for bit
+// compute their statistics the same way.
+constexpr int kRowsPerCta = 8;
+
+__device__ __forceinline__ float warp_allsum(float v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
+// mean and 1/sqrt(var + eps) of the row held in v[0..NV) (n valid floats)
+template <int NV>
+__device__ __forceinline__ void warp_row_stats(const float4 (&v)[NV], int n, int lane, float eps,
+                                               float* mean, float* rstd) {
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+        if (4 * (lane + 32 * k) < n) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    const float mu = warp_allsum(s) / (float)n;
+    float q = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+        if (4 * (lane + 32 * k) < n) {
+            const float a = v[k].x - mu, b = v[k].y - mu, c = v[k].z - mu, d = v[k].w - mu;
+            q += (a * a + b * b) + (c * c + d * d);
+        }
+    *mean = mu;
+    *rstd = 1.0f / sqrtf(warp_allsum(q) / (float)n + eps);
+}
+
+// prep_kernel's work, one warp per sequence
+template <int NV>
+__global__ void __launch_bounds__(256)
+    prep_rows_kernel(int B, int D, int K, int KH, int layer, int L,
+                     const int32_t* __restrict__ tok, int vocab, int* __restrict__ err,
+                     const float* __restrict__ embed, float* __restrict__ x,
+                     float* __restrict__ raw_out, float* __restrict__ at,
+                     float* __restrict__ hist, int32_t* __restrict__ pos,
+                     const float* __restrict__ g, const float* __restrict__ c,
+                     const float* __restrict__ dw, float eps, __nv_bfloat16* __restrict__ ath,
+                     __nv_bfloat16* __restrict__ atl) {
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int b = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+    if (b >= B) return;
+    const int p = pos[b * L + layer];
+    float* xr = x + (size_t)b * D;
+    const float* src = xr;
+    if (layer == 0) {
+        int t = tok[b];
+        if (t < 0 || t >= vocab) {  // never read outside the table; report instead
+            if (lane == 0) atomicExch(err, kErrBadIndex);
+            t = 0;
+        }
+        src = embed + (size_t)t * D;
+    }
+    float4 v[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int col = 4 * (lane + 32 * k);
+        if (col < D) {
+            v[k] = ld4(src + col);
+            if (layer == 0) st4(xr + col, v[k]);
+        }
+    }
+    float mean, rstd;
+    warp_row_stats<NV>(v, D, lane, eps, &mean, &rstd);
+    float* hb = hist + ((size_t)b * L + layer) * KH * D;
+    const int wslot = ((p % KH) + KH) % KH;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int col = 4 * (lane + 32 * k);
+        if (col >= D) continue;
+        const float4 gg = ld4(g + col), cc = ld4(c + col);
+        float r[4] = {(v[k].x - mean) * rstd * gg.x + cc.x, (v[k].y - mean) * rstd * gg.y + cc.y,
+                      (v[k].z - mean) * rstd * gg.z + cc.z, (v[k].w - mean) * rstd * gg.w + cc.w};
+        float a[4] = {r[0], r[1], r[2], r[3]};
+        if (K > 1) {
+            const float4 wl = ld4(dw + (size_t)(K - 1) * D + col);
+            float acc[4] = {r[0] * wl.x, r[1] * wl.y, r[2] * wl.z, r[3] * wl.w};
+            for (int j = 0; j < K - 1; ++j) {
+                const int slot = ((p - 1 - j) % KH + KH) % KH;
+                const float4 h = ld4(hb + (size_t)slot * D + col);
+                const float4 w = ld4(dw + (size_t)(K - 2 - j) * D + col);
+                acc[0] += h.x * w.x;
+                acc[1] += h.y * w.y;
+                acc[2] += h.z * w.z;
+                acc[3] += h.w * w.w;
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) a[e] = r[e] + acc[e];
+            st4(hb + (size_t)wslot * D + col, make_float4(r[0], r[1], r[2], r[3]));
+        }
+        const float4 av = make_float4(a[0], a[1], a[2], a[3]);
+        st4(at + (size_t)b * D + col, av);
+        if (ath) store_split4(ath, atl, (long long)b * D + col, av);
+        if (raw_out) st4(raw_out + (size_t)b * D + col, make_float4(r[0], r[1], r[2], r[3]));
+    }
+    if (lane == 0) pos[b * L + layer] = p + 1;
+}
+
+// rowstats_kernel's work, one warp per row
+template <int NV>
+__global__ void __launch_bounds__(256)
+    rowstats_rows_kernel(int rows, int n, const float* __restrict__ X, long long ldx,
+                         float* __restrict__ mu, float* __restrict__ rs, float eps) {
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float* xr = X + (size_t)row * ldx;
+    float4 v[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+        if (4 * (lane + 32 * k) < n) v[k] = ld4(xr + 4 * (lane + 32 * k));
+    float mean, rstd;
+    warp_row_stats<NV>(v, n, lane, eps, &mean, &rstd);
+    if (lane == 0) {
+        mu[row] = mean;
+        rs[row] = rstd;
+    }
+}
+
+// ln_split_kernel's work, one warp per row: the same statistics as
+// rowstats_rows_kernel, then ((x - mu) * rs) * g + c per element
+template <int NV>
+__global__ void __launch_bounds__(256)
+    ln_split_rows_kernel(int rows, int n, const float* __restrict__ X, long long ldx,
+                         const float* __restrict__ g, const float* __restrict__ c,
+                         __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo,
+                         float eps) {
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const float* xr = X + (size_t)row * ldx;
+    float4 v[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+        if (4 * (lane + 32 * k) < n) v[k] = ld4(xr + 4 * (lane + 32 * k));
+    float mean, rstd;
+    warp_row_stats<NV>(v, n, lane, eps, &mean, &rstd);
+    const long long o = (long long)row * n;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int col = 4 * (lane + 32 * k);
+        if (col >= n) continue;
+        const float4 gg = ld4(g + col), cc = ld4(c + col);
+        const float4 y = make_float4(__fmul_rn(__fmul_rn(v[k].x - mean, rstd), gg.x) + cc.x,
+                                     __fmul_rn(__fmul_rn(v[k].y - mean, rstd), gg.y) + cc.y,
+                                     __fmul_rn(__fmul_rn(v[k].z - mean, rstd), gg.z) + cc.z,
+                                     __fmul_rn(__fmul_rn(v[k].w - mean, rstd), gg.w) + cc.w);
+        store_split4(hi, lo, o + col, y);
+    }
+}
+
+// gate_kernel's work for groups of 8 channels, one thread per (sequence,
+// group): every element's arithmetic exactly as gate_kernel writes it
+__global__ void __launch_bounds__(256)
+    gate8_kernel(int B, int D, int L, int layer, const float* __restrict__ q,
+                 const float* __restrict__ delta, float* __restrict__ s, float* __restrict__ u,
+                 float* __restrict__ gate_out, int clamp, float p_floor,
+                 __nv_bfloat16* __restrict__ uh, __nv_bfloat16* __restrict__ ul) {
+    pdl_trigger();
+    pdl_wait();
+    const int ng = D >> 3;
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= (long long)B * ng) return;
+    const int b = (int)(i / ng), d0 = (int)(i - (long long)b * ng) * 8;
+    const float* qb = q + (size_t)b * 2 * D;
+    float ur[8], gt[8], dl[8], sv[8];
+    {
+        const float4 a0 = ld4(qb + d0), a1 = ld4(qb + d0 + 4);
+        const float4 g0 = ld4(qb + D + d0), g1 = ld4(qb + D + d0 + 4);
+        const float4 e0 = ld4(delta + d0), e1 = ld4(delta + d0 + 4);
+        ur[0] = a0.x; ur[1] = a0.y; ur[2] = a0.z; ur[3] = a0.w;
+        ur[4] = a1.x; ur[5] = a1.y; ur[6] = a1.z; ur[7] = a1.w;
+        gt[0] = g0.x; gt[1] = g0.y; gt[2] = g0.z; gt[3] = g0.w;
+        gt[4] = g1.x; gt[5] = g1.y; gt[6] = g1.z; gt[7] = g1.w;
+        dl[0] = e0.x; dl[1] = e0.y; dl[2] = e0.z; dl[3] = e0.w;
+        dl[4] = e1.x; dl[5] = e1.y; dl[6] = e1.z; dl[7] = e1.w;
+    }
+    float* sp = s + ((size_t)b * L + layer) * D + d0;
+    {
+        const float4 s0 = ld4(sp), s1 = ld4(sp + 4);
+        sv[0] = s0.x; sv[1] = s0.y; sv[2] = s0.z; sv[3] = s0.w;
+        sv[4] = s1.x; sv[5] = s1.y; sv[6] = s1.z; sv[7] = s1.w;
+    }
+    float uo[8], so[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float g0 = gt[k], g1 = gt[(k + 1) & 7], g2 = gt[(k + 2) & 7];
+        const float uu = ur[k] * (sigm(g0 - g1) * sigm(g0 - g2));
+        float p = 1.0f - dl[k] * (1.0f - sigm(g0));
+        if (clamp && p < p_floor) p = p_floor;
+        so[k] = p * sv[k] + (1.0f - p) * uu;
+        uo[k] = uu;
+    }
+    st4(sp, make_float4(so[0], so[1], so[2], so[3]));
+    st4(sp + 4, make_float4(so[4], so[5], so[6], so[7]));
+    const size_t o = (size_t)b * D + d0;
+    st4(u + o, make_float4(uo[0], uo[1], uo[2], uo[3]));
+    st4(u + o + 4, make_float4(uo[4], uo[5], uo[6], uo[7]));
+    if (uh) {
+        store_split4(uh, ul, (long long)o, make_float4(uo[0], uo[1], uo[2], uo[3]));
+        store_split4(uh, ul, (long long)o + 4, make_float4(uo[4], uo[5], uo[6], uo[7]));
+    }
+    if (gate_out) {
+        st4(gate_out + o, make_float4(gt[0], gt[1], gt[2], gt[3]));
+        st4(gate_out + o + 4, make_float4(gt[4], gt[5], gt[6], gt[7]));
+    }
+}
+
+bool al16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+bool al8(const void* p) { return ((uintptr_t)p & 7) == 0; }
+
+// float4 chunks per lane for a row of n floats (0: the warp kernels do not apply)
+int row_nv(int n) {
+    if (n <= 0 || n % 4) return 0;
+    const int need = (n + 127) / 128;
+    for (int nv : {2, 4, 6, 8, 12, 16, 24})
+        if (need <= nv) return nv;
+    return 0;
+}
+
+#define SN_ROWS_KERNELS(K) K<2>, K<4>, K<6>, K<8>, K<12>, K<16>, K<24>
+
+
+template <typename... KA, typename... Args>
+cudaError_t launch_rows(int nv, bool pdl, dim3 grid, cudaStream_t st, void (*k2)(KA...),
+                        void (*k4)(KA...), void (*k6)(KA...), void (*k8)(KA...),
+                        void (*k12)(KA...), void (*k16)(KA...), void (*k24)(KA...),
+                        Args... args) {
+    void (*k)(KA...) = nv == 2 ? k2 : nv == 4 ? k4 : nv == 6 ? k6 : nv == 8 ? k8
+                     : nv == 12 ? k12 : nv == 16 ? k16 : k24;
+    return launch_pdl_if(pdl, k, grid, dim3(256), 0, st, args...);
+}
+
+// LN + causal taps + ring write of layer `layer` for B sequences (`pdl`:
+// launched with programmatic serialization after the previous kernel).
+int launch_prep(bool pdl, cudaStream_t st, int B, int D, int K, int KH, int layer, int L,
+                const int32_t* tok, int vocab, const float* embed, float* x, float* raw_out,
+                float* at, float* hist, int32_t* pos, const float* g, const float* c,
+                const float* dw, float eps, __nv_bfloat16* ath, __nv_bfloat16* atl) {
+    const int nv = row_nv(D);
+    const bool rows = nv && al16(x) && al16(at) && al16(hist) && al16(embed) && al16(g) &&
+                      al16(c) && al16(dw) && (!raw_out || al16(raw_out)) &&
+                      (!ath || (al8(ath) && al8(atl)));
+    if (rows)
+        return cuda_check(launch_rows(nv, pdl, dim3((unsigned)((B + kRowsPerCta - 1) / kRowsPerCta)),
+                                      st, SN_ROWS_KERNELS(prep_rows_kernel), B, D, K, KH, layer, L,
+                                      tok, vocab, rt().d_err, embed, x, raw_out, at, hist, pos, g,
+                                      c, dw, eps, ath, atl),
+                          "prep launch");
+    return cuda_check(launch_pdl_if(pdl, prep_kernel, dim3(B), dim3(256), 0, st, D, K, KH, layer,
+                                    L, tok, vocab, rt().d_err, embed, x, raw_out, at, hist, pos,
+                                    g, c, dw, eps, ath, atl),
+                      "prep launch");
+}
+
+// competition gate + decay gate + state update of layer `layer`
+int launch_gate(bool pdl, cudaStream_t st, int B, int D, int G, int L, int layer, const float* q,
+                const float* delta, float* s, float* u, float* gate_out, int clamp, float p_floor,
+                __nv_bfloat16* uh, __nv_bfloat16* ul) {
+    const bool g8 = G == 8 && D % 8 == 0 && al16(q) && al16(delta) && al16(s) && al16(u) &&
+                    (!gate_out || al16(gate_out)) && (!uh || (al8(uh) && al8(ul)));
+    if (g8)
+        return cuda_check(launch_pdl_if(pdl, gate8_kernel,
+                                        dim3((unsigned)(((long long)B * (D / 8) + 255) / 256)),
+                                        dim3(256), 0, st, B, D, L, layer, q, delta, s, u, gate_out,
+                                        clamp, p_floor, uh, ul),
+                          "gate launch");
+    return cuda_check(launch_pdl_if(pdl, gate_kernel,
+                                    dim3((unsigned)(((long long)B * D + 255) / 256)), dim3(256), 0,
+                                    st, B, D, G, L, layer, q, delta, s, u, gate_out, clamp,
+                                    p_floor, uh, ul),
+                      "gate launch");
+}
+
+bool rows_ok(int n, const float* X, long long ldx) { return row_nv(n) && al16(X) && ldx % 4 == 0; }
+
+// row mean / rstd of `rows` rows of n floats, ldx apart
+int launch_rowstats(bool pdl, cudaStream_t st, int rows, int n, const float* X, long long ldx,
+                    float* mu, float* rs, float eps) {
+    if (rows_ok(n, X, ldx))
+        return cuda_check(launch_rows(row_nv(n), pdl,
+                                      dim3((unsigned)((rows + kRowsPerCta - 1) / kRowsPerCta)), st,
+                                      SN_ROWS_KERNELS(rowstats_rows_kernel), rows, n, X, ldx, mu,
+                                      rs, eps),
+                          "rowstats launch");
+    return cuda_check(launch_pdl_if(pdl, rowstats_kernel, dim3((unsigned)rows), dim3(256), 0, st,
+                                    n, X, ldx, mu, rs, eps),
+                      "rowstats launch");
+}
+
+// row LN written as the bf16 planes of the next contraction's input
+int launch_ln_split(bool pdl, cudaStream_t st, int rows, int n, const float* X, long long ldx,
+                    const float* g, const float* c, __nv_bfloat16* hi, __nv_bfloat16* lo,
+                    float eps) {
+    if (rows_ok(n, X, ldx) && al16(g) && al16(c) && al8(hi) && al8(lo))
+        return cuda_check(launch_rows(row_nv(n), pdl,
+                                      dim3((unsigned)((rows + kRowsPerCta - 1) / kRowsPerCta)), st,
+                                      SN_ROWS_KERNELS(ln_split_rows_kernel), rows, n, X, ldx, g, c,
+                                      hi, lo, eps),
+                          "ln_split launch");
+    return cuda_check(launch_pdl_if(pdl, ln_split_kernel, dim3((unsigned)rows), dim3(256), 0, st,
+                                    n, X, ldx, g, c, hi, lo, eps),
+                      "ln_split launch");
+}
+
 // y = LN(z) materialised (debug dumps only).
 __global__ void apply_ln_kernel(int n, const float* __restrict__ z, const float* __restrict__ mu,
                                 const float* __restrict__ rs, const float* __restrict__ g,
@@ -856,9 +1178,9 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
         const bool this_dbg = dbg && l == last_layer;
         {
             ProfScope ps("prep_ln_taps", st);
-            prep_kernel<<<B, 256, 0, st>>>(D, m->K, m->KH, l, m->L, m->tok, m->vocab, rt().d_err,
-                                           m->embed, m->x, this_dbg ? m->raw : nullptr, m->at,
-                                           m->hist, m->pos, y.ni_g, y.ni_c, y.dw, m->eps);
+            SN_TRY(launch_prep(false, st, B, D, m->K, m->KH, l, m->L, m->tok, m->vocab, m->embed,
+                               m->x, this_dbg ? m->raw : nullptr, m->at, m->hist, m->pos,
+                               y.ni_g, y.ni_c, y.dw, m->eps, nullptr, nullptr));
         }
         // feedback reads the previous state: before the gate kernel updates it
         GemmArgs gs = gemm(B, D, D, m->s + (size_t)l * D, y.Ws, y.sWs, m->sfb);
@@ -877,9 +1199,9 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
         }
         {
             ProfScope ps("gate_state", st);
-            gate_kernel<<<(unsigned)(((long long)B * D + 255) / 256), 256, 0, st>>>(
-                B, D, m->G, m->L, l, m->q, y.delta, m->s, m->u, this_dbg ? m->gate : nullptr,
-                m->clamp, m->p_floor);
+            SN_TRY(launch_gate(false, st, B, D, m->G, m->L, l, m->q, y.delta, m->s, m->u,
+                               this_dbg ? m->gate : nullptr, m->clamp, m->p_floor, nullptr,
+                               nullptr));
         }
         GemmArgs gz = gemm(B, I, D, m->u, y.Wz, y.sWz, m->z);
         gz.epi = kEpiWedge;
@@ -892,7 +1214,7 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
         const bool inline_ln = B <= 8 && !this_dbg;
         if (!inline_ln) {
             ProfScope ps("rowstats", st);
-            rowstats_kernel<<<B, 256, 0, st>>>(I, m->z, I, m->mu, m->rs, m->eps);
+            SN_TRY(launch_rowstats(false, st, B, I, m->z, I, m->mu, m->rs, m->eps));
         }
         if (this_dbg)
             apply_ln_kernel<<<B, 256, 0, st>>>(I, m->z, m->mu, m->rs, y.nm_g, y.nm_c, m->yn);
@@ -919,7 +1241,7 @@ int enqueue_step(SunnyModel* m, int B, bool with_head, cudaStream_t st, int last
     if (with_head) {
         if (B > 8) {
             ProfScope ps("rowstats", st);
-            rowstats_kernel<<<B, 256, 0, st>>>(D, m->x, D, m->mu, m->rs, m->eps);
+            SN_TRY(launch_rowstats(false, st, B, D, m->x, D, m->mu, m->rs, m->eps));
         }
         GemmArgs gh = gemm(B, m->vocab, D, m->x, m->head, m->shead, m->logits);
         gh.g = m->no_g; gh.c = m->no_c;
@@ -972,20 +1294,10 @@ int enqueue_step_tc(SunnyModel* m, int B, bool with_head, cudaStream_t st, cudaS
         const SunnyLayer& y = m->ly[l];
         {
             ProfScope ps("prep_ln_taps", st);
-            const dim3 g1(B), t256(256);
-            if (l > 0)  // follows Wc of the previous layer on this stream
-                SN_TRY(cuda_check(
-                    launch_pdl(prep_kernel, g1, t256, 0, st, D, m->K, m->KH, l, L,
-                               (const int32_t*)m->tok, m->vocab, rt().d_err,
-                               (const float*)m->embed, m->x, (float*)nullptr, m->at, m->hist,
-                               m->pos, (const float*)y.ni_g, (const float*)y.ni_c,
-                               (const float*)y.dw, m->eps, m->p_at.hi, m->p_at.lo),
-                    "prep launch"));
-            else
-                prep_kernel<<<g1, t256, 0, st>>>(D, m->K, m->KH, l, L, m->tok, m->vocab,
-                                                 rt().d_err, m->embed, m->x, nullptr, m->at,
-                                                 m->hist, m->pos, y.ni_g, y.ni_c, y.dw, m->eps,
-                                                 m->p_at.hi, m->p_at.lo);
+            // layers > 0 follow Wc of the previous layer on this stream
+            SN_TRY(launch_prep(l > 0, st, B, D, m->K, m->KH, l, L, m->tok, m->vocab, m->embed,
+                               m->x, nullptr, m->at, m->hist, m->pos, y.ni_g, y.ni_c, y.dw,
+                               m->eps, m->p_at.hi, m->p_at.lo));
         }
         {
             GemmArgs gv = gemm(B, R, D, m->at, y.V, y.sV, m->v);
@@ -1003,12 +1315,8 @@ int enqueue_step_tc(SunnyModel* m, int B, bool with_head, cudaStream_t st, cudaS
         {
             ProfScope ps("gate_state", st);
             // after the join (layer 0) a plain launch; later layers follow U directly
-            SN_TRY(cuda_check(
-                launch_pdl_if(l > 0 || !fork, gate_kernel,
-                              dim3((unsigned)(((long long)B * D + 255) / 256)), dim3(256), 0, st,
-                              B, D, m->G, L, l, (const float*)m->q, (const float*)y.delta, m->s,
-                              m->u, (float*)nullptr, m->clamp, m->p_floor, m->p_u.hi, m->p_u.lo),
-                "gate launch"));
+            SN_TRY(launch_gate(l > 0 || !fork, st, B, D, m->G, L, l, m->q, y.delta, m->s, m->u,
+                               nullptr, m->clamp, m->p_floor, m->p_u.hi, m->p_u.lo));
         }
         {
             GemmArgs gz = gemm(B, I, D, m->u, y.Wz, y.sWz, m->z);
@@ -1019,10 +1327,8 @@ int enqueue_step_tc(SunnyModel* m, int B, bool with_head, cudaStream_t st, cudaS
         }
         {
             ProfScope ps("rowstats", st);
-            SN_TRY(cuda_check(launch_pdl(ln_split_kernel, dim3(B), dim3(256), 0, st, I,
-                                         (const float*)m->z, (long long)I, (const float*)y.nm_g,
-                                         (const float*)y.nm_c, m->p_z.hi, m->p_z.lo, m->eps),
-                              "ln_split launch"));
+            SN_TRY(launch_ln_split(true, st, B, I, m->z, I, y.nm_g, y.nm_c, m->p_z.hi, m->p_z.lo,
+                                   m->eps));
         }
         if (fork) SN_TRY(cuda_check(cudaStreamWaitEvent(st, m->ev_ws[l], 0), "join"));
         GemmArgs gc = gemm(B, D, I, m->z, y.Wc, y.sWc, m->x);
@@ -1042,10 +1348,8 @@ int enqueue_step_tc(SunnyModel* m, int B, bool with_head, cudaStream_t st, cudaS
     if (with_head) {
         {
             ProfScope ps("rowstats", st);
-            SN_TRY(cuda_check(launch_pdl(ln_split_kernel, dim3(B), dim3(256), 0, st, D,
-                                         (const float*)m->x, (long long)D, (const float*)m->no_g,
-                                         (const float*)m->no_c, m->p_x.hi, m->p_x.lo, m->eps),
-                              "ln_split launch"));
+            SN_TRY(launch_ln_split(true, st, B, D, m->x, D, m->no_g, m->no_c, m->p_x.hi,
+                                   m->p_x.lo, m->eps));
         }
         ProfScope ps("gemm_head", st);
         SN_TRY(launch_tc_gemm_act(gemm(B, m->vocab, D, m->x, m->head, m->shead, m->logits),
@@ -1310,11 +1614,11 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
         }
         if (ctc) {  // LN(z) straight into Wc's input planes
             ProfScope ps("rowstats", st);
-            ln_split_kernel<<<(unsigned)M, 256, 0, st>>>(I, m->cz, I, y.nm_g, y.nm_c, m->c_z.hi,
-                                                         m->c_z.lo, m->eps);
+            SN_TRY(launch_ln_split(false, st, (int)M, I, m->cz, I, y.nm_g, y.nm_c, m->c_z.hi,
+                                   m->c_z.lo, m->eps));
         } else {
             ProfScope ps("rowstats", st);
-            rowstats_kernel<<<(unsigned)M, 256, 0, st>>>(I, m->cz, I, m->cmu, m->crs, m->eps);
+            SN_TRY(launch_rowstats(false, st, (int)M, I, m->cz, I, m->cmu, m->crs, m->eps));
         }
         GemmArgs gc = gemm((int)M, D, I, m->cz, y.Wc, y.sWc, m->cx);
         if (!ctc) {
@@ -1333,7 +1637,7 @@ int enqueue_chunk(SunnyModel* m, int B, int Tc, bool head, cudaStream_t st) {
     }
     if (head) {  // logits of each sequence's last position only
         const float* last = m->cx + (size_t)(Tc - 1) * D;
-        rowstats_kernel<<<B, 256, 0, st>>>(D, last, (long long)Tc * D, m->cmu, m->crs, m->eps);
+        SN_TRY(launch_rowstats(false, st, B, D, last, (long long)Tc * D, m->cmu, m->crs, m->eps));
         GemmArgs gh = gemm(B, m->vocab, D, last, m->head, m->shead, m->logits);
         gh.lda = (long long)Tc * D;
         gh.mu = m->cmu; gh.rs = m->crs; gh.g = m->no_g; gh.c = m->no_c;
@@ -1474,37 +1778,47 @@ int sunny_step(SunnyModel* m, const int32_t* tokens, int B, float* logits, int32
     return finish(host);
 }
 
-int sunny_reset(SunnyModel* m) {
+// Zero the state of sequences [seq0, seq0 + n) (all of them by default).
+int sunny_reset(SunnyModel* m, int seq0 = 0, int n = -1) {
     if (!m || !m->ready) return fail(SN_E_INVAL, "sunny_reset: bad handle");
+    if (n < 0) n = m->nseq - seq0;
+    if (seq0 < 0 || n <= 0 || seq0 + n > m->nseq)
+        return fail(SN_E_INVAL, "sunny_reset: sequences [%d, %d) outside [0, %d)", seq0,
+                    seq0 + n, m->nseq);
     std::lock_guard<std::recursive_mutex> lk(rt().mu);
     cudaStream_t st = stream();
-    const size_t n = (size_t)m->nseq;
-    cudaMemsetAsync(m->s, 0, n * m->L * m->D * 4, st);
-    cudaMemsetAsync(m->hist, 0, n * m->L * m->KH * m->D * 4, st);
-    cudaMemsetAsync(m->pos, 0, n * m->L * 4, st);
+    const size_t a = (size_t)seq0, k = (size_t)n;
+    cudaMemsetAsync(m->s + a * m->L * m->D, 0, k * m->L * m->D * 4, st);
+    cudaMemsetAsync(m->hist + a * m->L * m->KH * m->D, 0, k * m->L * m->KH * m->D * 4, st);
+    cudaMemsetAsync(m->pos + a * m->L, 0, k * m->L * 4, st);
     return finish(false);
 }
 
-int sunny_state_io(SunnyModel* m, int B, float* s, float* hist, bool get) {
-    if (!m || !m->ready || B <= 0 || B > m->nseq || !s || !hist)
+// State of sequences [seq0, seq0 + B): s (B,L,D) and hist (B,L,K-1,D), newest
+// history row first, out of (get) or into the handle's ring buffers.
+int sunny_state_io(SunnyModel* m, int seq0, int B, float* s, float* hist, bool get) {
+    if (!m || !m->ready || seq0 < 0 || B <= 0 || seq0 + B > m->nseq || !s || !hist)
         return fail(SN_E_INVAL, "sunny state: bad arguments");
     std::lock_guard<std::recursive_mutex> lk(rt().mu);
     cudaStream_t st = stream();
     const size_t ns = (size_t)B * m->L * m->D * 4, nh = (size_t)B * m->L * m->KH * m->D * 4;
+    float* ms = m->s + (size_t)seq0 * m->L * m->D;
+    float* mh = m->hist + (size_t)seq0 * m->L * m->KH * m->D;
+    int32_t* mp = m->pos + (size_t)seq0 * m->L;
     Arr S, H;
     if (get) {
         SN_TRY(stage_out(s, ns, 5, &S));
         SN_TRY(stage_out(hist, nh, 6, &H));
-        SN_TRY(cuda_check(cudaMemcpyAsync(S.dev, m->s, ns, cudaMemcpyDeviceToDevice, st), "s"));
+        SN_TRY(cuda_check(cudaMemcpyAsync(S.dev, ms, ns, cudaMemcpyDeviceToDevice, st), "s"));
     } else {
         SN_TRY(stage_in(s, ns, 5, &S));
         SN_TRY(stage_in(hist, nh, 6, &H));
-        SN_TRY(cuda_check(cudaMemcpyAsync(m->s, S.dev, ns, cudaMemcpyDeviceToDevice, st), "s"));
-        cudaMemsetAsync(m->pos, 0, (size_t)B * m->L * 4, st);
+        SN_TRY(cuda_check(cudaMemcpyAsync(ms, S.dev, ns, cudaMemcpyDeviceToDevice, st), "s"));
+        cudaMemsetAsync(mp, 0, (size_t)B * m->L * 4, st);
     }
     const long long total = (long long)B * m->L * m->KH * m->D;
     hist_io_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
-        B, m->L, m->KH, m->D, m->hist, (float*)H.dev, m->pos, get ? 1 : 0);
+        B, m->L, m->KH, m->D, mh, (float*)H.dev, mp, get ? 1 : 0);
     SN_TRY(cuda_check(cudaGetLastError(), "hist io"));
     if (get) {
         SN_TRY(copy_back(S));
@@ -1590,11 +1904,25 @@ sn_status sn_abi_sunny_prefill_chunked(SnAbiSunny* m, const int32_t* tokens, int
 }
 
 sn_status sn_abi_sunny_get_state(SnAbiSunny* m, int32_t B, float* s, float* hist) {
-    return m ? sunny_state_io(m->m.get(), B, s, hist, true) : SN_E_INVAL;
+    return m ? sunny_state_io(m->m.get(), 0, B, s, hist, true) : SN_E_INVAL;
+}
+
+sn_status sn_abi_sunny_get_state_at(SnAbiSunny* m, int32_t seq0, int32_t n, float* s,
+                                    float* hist) {
+    return m ? sunny_state_io(m->m.get(), seq0, n, s, hist, true) : SN_E_INVAL;
+}
+
+sn_status sn_abi_sunny_set_state_at(SnAbiSunny* m, int32_t seq0, int32_t n, const float* s,
+                                    const float* hist) {
+    return m ? sunny_state_io(m->m.get(), seq0, n, (float*)s, (float*)hist, false) : SN_E_INVAL;
+}
+
+sn_status sn_abi_sunny_reset_at(SnAbiSunny* m, int32_t seq0, int32_t n) {
+    return m ? sunny_reset(m->m.get(), seq0, n) : SN_E_INVAL;
 }
 
 sn_status sn_abi_sunny_set_state(SnAbiSunny* m, int32_t B, const float* s, const float* hist) {
-    return m ? sunny_state_io(m->m.get(), B, (float*)s, (float*)hist, false) : SN_E_INVAL;
+    return m ? sunny_state_io(m->m.get(), 0, B, (float*)s, (float*)hist, false) : SN_E_INVAL;
 }
 
 // ---------------------------------------------- reference sunnynet.h symbol set

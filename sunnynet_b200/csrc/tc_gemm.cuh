@@ -80,4 +80,19 @@ __device__ __forceinline__ void store_split(__nv_bfloat16* hi, __nv_bfloat16* lo
     lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
 }
 
+// The same split for four consecutive elements (i a multiple of 4, planes
+// 8-byte aligned): one 8-byte store per plane.
+__device__ __forceinline__ void store_split4(__nv_bfloat16* hi, __nv_bfloat16* lo, long long i,
+                                             float4 v) {
+    const float x[4] = {v.x, v.y, v.z, v.w};
+    __align__(8) __nv_bfloat16 h[4], l[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        h[k] = __float2bfloat16_rn(x[k]);
+        l[k] = __float2bfloat16_rn(x[k] - __bfloat162float(h[k]));
+    }
+    *reinterpret_cast<uint2*>(hi + i) = *reinterpret_cast<const uint2*>(h);
+    *reinterpret_cast<uint2*>(lo + i) = *reinterpret_cast<const uint2*>(l);
+}
+
 }  // namespace sn

@@ -94,6 +94,28 @@ class SunnyBatch:
         h = np.ascontiguousarray(h, np.float32)
         check(self._lib.sn_abi_sunny_set_state(self._h, s.shape[0], ptr(s), ptr(h)), "set_state")
 
+    def get_state_at(self, seq0: int, n: int, s=None, h=None):
+        """State of sequences [seq0, seq0+n) into s (n,L,D), h (n,L,K-1,D):
+        numpy arrays, or CUDA tensors (then copied device to device)."""
+        kh = max(self.taps - 1, 1)
+        if s is None:
+            s = np.empty((n, self.layers, self.dim), np.float32)
+            h = np.empty((n, self.layers, kh, self.dim), np.float32)
+        check(self._lib.sn_abi_sunny_get_state_at(self._h, int(seq0), int(n), ptr(s), ptr(h)),
+              "get_state_at")
+        return s, h
+
+    def set_state_at(self, seq0: int, s, h):
+        """Overwrite the state of sequences [seq0, seq0 + len(s))."""
+        if not hasattr(s, "data_ptr"):
+            s = np.ascontiguousarray(s, np.float32)
+            h = np.ascontiguousarray(h, np.float32)
+        check(self._lib.sn_abi_sunny_set_state_at(self._h, int(seq0), int(s.shape[0]), ptr(s),
+                                                  ptr(h)), "set_state_at")
+
+    def reset_at(self, seq0: int, n: int = 1):
+        check(self._lib.sn_abi_sunny_reset_at(self._h, int(seq0), int(n)), "reset_at")
+
     def close(self):
         if getattr(self, "_h", None):
             self._lib.sn_abi_sunny_free(self._h)
