@@ -488,3 +488,43 @@ def test_profile_modes_report_families_and_leave_results_alone(mode):
         n, ms = rep[fam]
         assert n == 3 * shape.layers and ms > 0, (fam, rep[fam])
     assert rep["gemm_head"][0] == 3
+
+
+def test_batch_engine_matches_requests_served_alone():
+    """Continuous batching on the GPU: 7 requests of different prompt lengths
+    and budgets through 3 slots (admission, slot reuse, state hand-off from
+    the prefill handle) against each request decoded alone on a one-sequence
+    handle, teacher-forced with the engine's own tokens: every logits row
+    within the fp32 tolerance."""
+    from sunnynet_b200 import formats
+    from sunnynet_b200.model import SunnyBatch
+    from sunnynet_b200.serve import BatchEngine
+    shape = formats.SunnyShape(1500, 128, 224, 80, 4, 3)
+    rng = np.random.default_rng(21)
+    specs = [(5, 6), (9, 4), (9, 8), (17, 5), (3, 10), (30, 3), (9, 7)]
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape, seed=21)
+        eng = BatchEngine(p, slots=3, prefill_chunk=8)
+        reqs = [eng.submit(list(rng.integers(0, shape.vocab, n)), m, record_logits=True)
+                for n, m in specs]
+        eng.run()
+        alone = SunnyBatch(p, 1)
+        for r in reqs:
+            assert r.done and len(r.tokens) == r.max_tokens
+            alone.reset()
+            ref = alone.prefill(np.array([r.prompt], np.int32), chunk=8)
+            for k, tok in enumerate(r.tokens):
+                check_logits(r.logits[k], ref)
+                assert tok == int(np.argmax(r.logits[k]))
+                if k + 1 < len(r.tokens):
+                    ref = alone.step(np.array([tok], np.int32))
+    # greedy requests without recorded logits take the device argmax path
+    with tempfile.TemporaryDirectory() as td:
+        p = _blob(td, shape, seed=21)
+        a, b = BatchEngine(p, slots=3, prefill_chunk=8), BatchEngine(p, slots=3, prefill_chunk=8)
+        prompts = [list(rng.integers(0, shape.vocab, n)) for n in (4, 7, 7, 12)]
+        ra = [a.submit(q, 6) for q in prompts]
+        rb = [b.submit(q, 6, record_logits=True) for q in prompts]
+        a.run(), b.run()
+        for x, y in zip(ra, rb):
+            assert x.tokens == y.tokens
