@@ -199,6 +199,13 @@ sn_status   sn_abi_rwkv7_step_argmax(SnAbiRwkv7* m, const int32_t* tokens, int32
  * single layer from exactly this step's input. */
 sn_status   sn_abi_rwkv7_step_trace(SnAbiRwkv7* m, const int32_t* tokens, int32_t B,
                                     float* logits, float* xs);
+/* Prompt of T tokens for each of the first B sequences (tokens (B,T) row-major)
+ * -> logits (B, vocab) of each sequence's last token (NULL: state only). The
+ * reference feeds a prompt token by token (rwkv7.c:362-364); here each layer
+ * runs over all prompt rows at once and only the matrix-state recurrence
+ * walks the tokens in order; results match stepping within fp32 rounding. */
+sn_status   sn_abi_rwkv7_prefill_batch(SnAbiRwkv7* m, const int32_t* tokens, int32_t B,
+                                       int32_t T, float* logits);
 /* S (B,L,NH,HS,HS), shift (B,L,2,D) */
 sn_status   sn_abi_rwkv7_get_state(SnAbiRwkv7* m, int32_t B, float* S, float* shift);
 int32_t     sn_abi_rwkv7_dims(const SnAbiRwkv7* m, int32_t* dims8); /* vocab,D,HS,NH,F,L,q4,group */

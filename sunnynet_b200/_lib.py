@@ -68,6 +68,7 @@ SIGNATURES = {
     "sn_abi_rwkv7_step_batch": (I32, [V, V, I32, V]),
     "sn_abi_rwkv7_step_argmax": (I32, [V, V, I32, V]),
     "sn_abi_rwkv7_step_trace": (I32, [V, V, I32, V, V]),
+    "sn_abi_rwkv7_prefill_batch": (I32, [V, V, I32, I32, V]),
     "sn_abi_rwkv7_get_state": (I32, [V, I32, V, V]),
     "sn_abi_rwkv7_dims": (I32, [V, V]),
     # recur.h

@@ -93,28 +93,36 @@ __global__ void rk_embed_kernel(int D, const int32_t* __restrict__ tok, int voca
         x[(size_t)blockIdx.x * D + i] = (e[i] - mean) * rstd * w[i] + b[i];
 }
 
-// time-mix prologue (rwkv7.c:213-226); lerps written as 6 (B,D) planes
+// time-mix prologue (rwkv7.c:213-226); lerps written as 6 (rows,D) planes.
+// Rows are T consecutive tokens of each sequence (T = 1 for a decode step).
+// The token before row t is row t-1 of the same sequence, whose normalised
+// input is recomputed here (the same arithmetic that row computes for
+// itself), or the shift state for t = 0. With T = 1 the shift state is
+// updated in place; with T > 1 the caller copies the last row's xn into it
+// after this kernel (other rows still read the old value here).
 __global__ void rk_tmix_prep_kernel(int D, int B, const float* __restrict__ x,
                                     float* __restrict__ shift, long long shift_stride,
                                     const float* __restrict__ w, const float* __restrict__ b,
                                     const float* __restrict__ lerp, float* __restrict__ xn_out,
-                                    float* __restrict__ planes, float eps) {
+                                    float* __restrict__ planes, float eps, int T) {
     __shared__ float red[32];
     pdl_trigger();
     pdl_wait();  // no-op unless launched with programmatic serialization
-    const int s = blockIdx.x;
+    const int s = blockIdx.x, seq = s / T, t = s - seq * T;
     const float* xr = x + (size_t)s * D;
-    float* sh = shift + s * shift_stride;
-    float mean, rstd;
+    float* sh = shift + seq * shift_stride;
+    float mean, rstd, pmean = 0.0f, prstd = 0.0f;
     row_stats(xr, D, eps, red, &mean, &rstd);
+    if (t > 0) row_stats(xr - D, D, eps, red, &pmean, &prstd);
     const size_t plane = (size_t)B * D;
     for (int i = threadIdx.x; i < D; i += blockDim.x) {
         const float xn = (xr[i] - mean) * rstd * w[i] + b[i];
-        const float d = sh[i] - xn;
+        const float prev = t > 0 ? (xr[i - D] - pmean) * prstd * w[i] + b[i] : sh[i];
+        const float d = prev - xn;
         float* o = planes + (size_t)s * D + i;
 #pragma unroll
         for (int j = 0; j < 6; ++j) o[j * plane] = xn + lerp[j * D + i] * d;
-        sh[i] = xn;
+        if (T == 1) sh[i] = xn;
         xn_out[(size_t)s * D + i] = xn;
     }
 }
@@ -216,6 +224,9 @@ __global__ void __launch_bounds__(256)
 // One CTA (8 warps) per (sequence, head): the matrix-state update of
 // rwkv7.c:143-189 followed by group norm + bonus + gate (rwkv7.c:268-289).
 // A warp owns state rows i = warp, warp+8, ...; a lane owns VPL columns.
+// One CTA per (sequence, head) walks that sequence's T consecutive rows in
+// order (T = 1 for a decode step, the prompt chunk in a prefill); heads up to
+// 128 wide keep the state in registers across the rows.
 template <int VPL>
 __global__ void __launch_bounds__(256)
     rk_heads_kernel(int NH, int L, int layer, int D, float* __restrict__ S,
@@ -224,7 +235,7 @@ __global__ void __launch_bounds__(256)
                     const float* __restrict__ kk, const float* __restrict__ r,
                     const float* __restrict__ g, const float* __restrict__ rk,
                     const float* __restrict__ lnw, const float* __restrict__ lnb,
-                    float* __restrict__ y) {
+                    float* __restrict__ y, int T) {
     constexpr int HS = VPL * 32;
     // warp w owns state rows w, w+8, ...; for heads up to 128 wide all of
     // them are loaded at once, before anything else, so the state costs one
@@ -236,7 +247,6 @@ __global__ void __launch_bounds__(256)
     pdl_wait();  // no-op unless launched with programmatic serialization
     const int h = blockIdx.x % NH, b = blockIdx.x / NH;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t o = (size_t)b * D + (size_t)h * HS;
     float* Sh = S + (((size_t)b * L + layer) * NH + h) * HS * HS;
     float spre[PRE ? RPW : 1][VPL];
     if (PRE) {
@@ -245,94 +255,114 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
             for (int t = 0; t < VPL; ++t) spre[q][t] = Sh[(size_t)(warp + 8 * q) * HS + lane + 32 * t];
     }
-    // kk normalised with floor 1e-12 (rwkv7.c:162-165)
-    float ss = 0.0f;
-    for (int j = threadIdx.x; j < HS; j += blockDim.x) ss += kk[o + j] * kk[o + j];
-    float nrm = sqrtf(block_sum(ss, red));
-    if (!(nrm > 1e-12f)) nrm = 1e-12f;
-    const float inv = 1.0f / nrm;
-    for (int j = threadIdx.x; j < HS; j += blockDim.x) kn[j] = kk[o + j] * inv;
-    __syncthreads();
-    float wj[VPL], kj[VPL], rj[VPL], knj[VPL], kaj[VPL];
+    for (int step = 0; step < T; ++step) {
+        const size_t o = ((size_t)b * T + step) * D + (size_t)h * HS;
+        // kk normalised with floor 1e-12 (rwkv7.c:162-165)
+        float ss = 0.0f;
+        for (int j = threadIdx.x; j < HS; j += blockDim.x) ss += kk[o + j] * kk[o + j];
+        float nrm = sqrtf(block_sum(ss, red));
+        if (!(nrm > 1e-12f)) nrm = 1e-12f;
+        const float inv = 1.0f / nrm;
+        for (int j = threadIdx.x; j < HS; j += blockDim.x) kn[j] = kk[o + j] * inv;
+        __syncthreads();
+        float wj[VPL], kj[VPL], rj[VPL], knj[VPL], kaj[VPL];
 #pragma unroll
-    for (int t = 0; t < VPL; ++t) {
-        const int j = lane + 32 * t;
-        wj[t] = ww[o + j];
-        kj[t] = k[o + j];
-        rj[t] = r[o + j];
-        knj[t] = kn[j];
-        kaj[t] = __fmul_rn(kn[j], a[o + j]);
-    }
+        for (int t = 0; t < VPL; ++t) {
+            const int j = lane + 32 * t;
+            wj[t] = ww[o + j];
+            kj[t] = k[o + j];
+            rj[t] = r[o + j];
+            knj[t] = kn[j];
+            kaj[t] = __fmul_rn(kn[j], a[o + j]);
+        }
 #pragma unroll(PRE ? RPW : 1)
-    for (int q = 0; q < RPW; ++q) {
-        const int i = warp + 8 * q;
-        float* row = Sh + (size_t)i * HS;
-        float sv[VPL];
-        float p = 0.0f;
+        for (int q = 0; q < RPW; ++q) {
+            const int i = warp + 8 * q;
+            float* row = Sh + (size_t)i * HS;
+            float sv[VPL];
+            float p = 0.0f;
 #pragma unroll
-        for (int t = 0; t < VPL; ++t) {
-            sv[t] = PRE ? spre[PRE ? q : 0][t] : row[lane + 32 * t];
-            p = fmaf(sv[t], knj[t], p);
-        }
-        for (int off = 16; off; off >>= 1) p += __shfl_xor_sync(0xffffffffu, p, off);
-        const float vi = v[o + i];
-        float yacc = 0.0f;
+            for (int t = 0; t < VPL; ++t) {
+                sv[t] = PRE ? spre[PRE ? q : 0][t] : row[lane + 32 * t];
+                p = fmaf(sv[t], knj[t], p);
+            }
+            for (int off = 16; off; off >>= 1) p += __shfl_xor_sync(0xffffffffu, p, off);
+            const float vi = v[o + i];
+            float yacc = 0.0f;
 #pragma unroll
-        for (int t = 0; t < VPL; ++t) {
-            const float ns =
-                __fmaf_rn(sv[t], wj[t], __fsub_rn(__fmul_rn(vi, kj[t]), __fmul_rn(p, kaj[t])));
-            row[lane + 32 * t] = ns;
-            yacc = fmaf(ns, rj[t], yacc);
+            for (int t = 0; t < VPL; ++t) {
+                const float ns =
+                    __fmaf_rn(sv[t], wj[t], __fsub_rn(__fmul_rn(vi, kj[t]), __fmul_rn(p, kaj[t])));
+                if (PRE)
+                    spre[PRE ? q : 0][t] = ns;
+                else
+                    row[lane + 32 * t] = ns;
+                yacc = fmaf(ns, rj[t], yacc);
+            }
+            for (int off = 16; off; off >>= 1) yacc += __shfl_xor_sync(0xffffffffu, yacc, off);
+            if (lane == 0) yv[i] = yacc;
         }
-        for (int off = 16; off; off >>= 1) yacc += __shfl_xor_sync(0xffffffffu, yacc, off);
-        if (lane == 0) yv[i] = yacc;
+        __syncthreads();
+        // group norm over the head, r.k bonus, gate
+        float m = 0.0f;
+        for (int j = threadIdx.x; j < HS; j += blockDim.x) m += yv[j];
+        const float mean = block_sum(m, red) / (float)HS;
+        float var = 0.0f, dot = 0.0f;
+        for (int j = threadIdx.x; j < HS; j += blockDim.x) {
+            const float t = yv[j] - mean;
+            var += t * t;
+            dot += r[o + j] * k[o + j] * rk[h * HS + j];
+        }
+        const float rstd = 1.0f / sqrtf(block_sum(var, red) / (float)HS + kEpsGroup);
+        dot = block_sum(dot, red);
+        for (int j = threadIdx.x; j < HS; j += blockDim.x) {
+            const float nv = (yv[j] - mean) * rstd * lnw[h * HS + j] + lnb[h * HS + j];
+            y[o + j] = (nv + dot * v[o + j]) * g[o + j];
+        }
+        __syncthreads();  // kn and yv are rewritten by the next row
     }
-    __syncthreads();
-    // group norm over the head, r.k bonus, gate
-    float m = 0.0f;
-    for (int j = threadIdx.x; j < HS; j += blockDim.x) m += yv[j];
-    const float mean = block_sum(m, red) / (float)HS;
-    float var = 0.0f, dot = 0.0f;
-    for (int j = threadIdx.x; j < HS; j += blockDim.x) {
-        const float t = yv[j] - mean;
-        var += t * t;
-        dot += r[o + j] * k[o + j] * rk[h * HS + j];
-    }
-    const float rstd = 1.0f / sqrtf(block_sum(var, red) / (float)HS + kEpsGroup);
-    dot = block_sum(dot, red);
-    for (int j = threadIdx.x; j < HS; j += blockDim.x) {
-        const float nv = (yv[j] - mean) * rstd * lnw[h * HS + j] + lnb[h * HS + j];
-        y[o + j] = (nv + dot * v[o + j]) * g[o + j];
+    if (PRE) {
+#pragma unroll
+        for (int q = 0; q < (PRE ? RPW : 1); ++q)
+#pragma unroll
+            for (int t = 0; t < VPL; ++t) Sh[(size_t)(warp + 8 * q) * HS + lane + 32 * t] = spre[q][t];
     }
 }
 
-// channel-mix prologue (rwkv7.c:295-297)
+// channel-mix prologue (rwkv7.c:295-297); rows and the shift state as in
+// rk_tmix_prep_kernel (xn2_out: every row's normalised input, for the
+// caller's copy of the last row into the shift state when T > 1).
 __global__ void rk_cmix_prep_kernel(int D, const float* __restrict__ x, float* __restrict__ shift,
                                     long long shift_stride, const float* __restrict__ w,
                                     const float* __restrict__ b, const float* __restrict__ lerp,
-                                    float* __restrict__ xk, float eps) {
+                                    float* __restrict__ xk, float eps, int T,
+                                    float* __restrict__ xn2_out) {
     __shared__ float red[32];
     pdl_trigger();
     pdl_wait();  // no-op unless launched with programmatic serialization
-    const int s = blockIdx.x;
+    const int s = blockIdx.x, seq = s / T, t = s - seq * T;
     const float* xr = x + (size_t)s * D;
-    float* sh = shift + s * shift_stride + D;
-    float mean, rstd;
+    float* sh = shift + seq * shift_stride + D;
+    float mean, rstd, pmean = 0.0f, prstd = 0.0f;
     row_stats(xr, D, eps, red, &mean, &rstd);
+    if (t > 0) row_stats(xr - D, D, eps, red, &pmean, &prstd);
     for (int i = threadIdx.x; i < D; i += blockDim.x) {
         const float xn2 = (xr[i] - mean) * rstd * w[i] + b[i];
-        xk[(size_t)s * D + i] = xn2 + lerp[i] * (sh[i] - xn2);
-        sh[i] = xn2;
+        const float prev = t > 0 ? (xr[i - D] - pmean) * prstd * w[i] + b[i] : sh[i];
+        xk[(size_t)s * D + i] = xn2 + lerp[i] * (prev - xn2);
+        if (T == 1) sh[i] = xn2;
+        if (xn2_out) xn2_out[(size_t)s * D + i] = xn2;
     }
 }
 
-// y = LN(x) per row (final norm)
+// y = LN(x) per row (final norm); input rows ldx floats apart
 __global__ void rk_ln_kernel(int D, const float* __restrict__ x, const float* __restrict__ w,
-                             const float* __restrict__ b, float* __restrict__ y, float eps) {
+                             const float* __restrict__ b, float* __restrict__ y, float eps,
+                             long long ldx) {
     __shared__ float red[32];
     pdl_trigger();
     pdl_wait();  // no-op unless launched with programmatic serialization
-    const float* xr = x + (size_t)blockIdx.x * D;
+    const float* xr = x + (size_t)blockIdx.x * ldx;
     float mean, rstd;
     row_stats(xr, D, eps, red, &mean, &rstd);
     for (int i = threadIdx.x; i < D; i += blockDim.x)
@@ -372,6 +402,18 @@ struct RkLayer {
     int Rw, Ra, Rv, Rg;
 };
 
+// Row buffers of one pass over the layers: a decode step's B rows, or a
+// prefill chunk's B sequences x T tokens.
+struct RkBufs {
+    int rows = 0;
+    int32_t* tok = nullptr;
+    float *x = nullptr, *xn = nullptr, *planes = nullptr, *r = nullptr, *k = nullptr,
+          *v = nullptr, *a = nullptr, *g = nullptr, *kk = nullptr, *ww = nullptr, *y = nullptr,
+          *xk2 = nullptr, *lo_w = nullptr, *lo_a = nullptr, *lo_v = nullptr, *lo_g = nullptr,
+          *dw = nullptr, *da = nullptr, *dv = nullptr, *ck = nullptr, *vfirst = nullptr,
+          *xf = nullptr, *logits = nullptr;
+};
+
 struct RwkvModel {
     int vocab = 0, D = 0, HS = 0, NH = 0, F = 0, L = 0, nseq = 0, q4 = 0, group = 64;
     float eps = 1e-5f;
@@ -386,6 +428,9 @@ struct RwkvModel {
     float *dw = nullptr, *da = nullptr, *dv = nullptr, *ck = nullptr, *vfirst = nullptr;
     float *logits = nullptr, *xf = nullptr;
     float2* apart = nullptr;  // argmax partials (B x kArgChunks)
+    RkBufs pre;                // prefill workspace (allocated on first use)
+    std::vector<void*> pre_allocs;
+    int rmax = 0;              // widest LoRA rank
     std::vector<void*> allocs;
     std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
     std::map<std::pair<int, int>, ProfGraph> pgraphs;  // instrumented (profile mode 2)
@@ -396,6 +441,7 @@ struct RwkvModel {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
         if (cap) cudaStreamDestroy(cap);
         for (void* p : allocs) cudaFree(p);
+        for (void* p : pre_allocs) cudaFree(p);
     }
     template <class T>
     T* dalloc(size_t n) {
@@ -498,6 +544,74 @@ struct RkParser {
     }
 };
 
+// Activation workspace of the tensor-core W4A8 path for contractions of
+// `rows` rows (allocates: call outside any stream capture).
+int reserve_tc(RwkvModel* m, int rows) {
+    auto reserve = [&](const RkMat& M) -> int {
+        if (!M.q4 || !w4a8_tc_ok(rows, M.in, M.out, M.block, M.q)) return SN_OK;
+        return w4a8_tc_reserve(rows, M.in, M.block);
+    };
+    for (const RkLayer& y : m->ly)
+        for (const RkMat* M : {&y.rw, &y.kw, &y.vw, &y.ow, &y.w1, &y.w2, &y.a1, &y.a2, &y.v1,
+                               &y.v2, &y.g1, &y.g2, &y.cmk, &y.cmv})
+            SN_TRY(reserve(*M));
+    SN_TRY(reserve(m->head));
+    if (!m->ly.empty()) {  // the grouped first-stage projections: six input planes
+        const RkMat& r0 = m->ly[0].rw;
+        if (r0.q4 && w4a8_tc_ok(rows, r0.in, r0.out, r0.block, r0.q))
+            SN_TRY(w4a8_tc_reserve(rows, r0.in, r0.block, 6));
+    }
+    return SN_OK;
+}
+
+// The decode step's row buffers (nseq rows).
+RkBufs step_bufs(RwkvModel* m) {
+    RkBufs w;
+    w.rows = m->nseq;
+    w.tok = m->tok; w.x = m->x; w.xn = m->xn; w.planes = m->planes;
+    w.r = m->r; w.k = m->k; w.v = m->v; w.a = m->a; w.g = m->g; w.kk = m->kk; w.ww = m->ww;
+    w.y = m->y; w.xk2 = m->xk2; w.lo_w = m->lo_w; w.lo_a = m->lo_a; w.lo_v = m->lo_v;
+    w.lo_g = m->lo_g; w.dw = m->dw; w.da = m->da; w.dv = m->dv; w.ck = m->ck;
+    w.vfirst = m->vfirst; w.xf = m->xf; w.logits = m->logits;
+    return w;
+}
+
+// Prefill workspace of at least `rows` rows (prompt chunks of all sequences
+// at once); the final norm and the head only ever see nseq rows.
+int ensure_pre(RwkvModel* m, int rows) {
+    if (m->pre.rows >= rows) return SN_OK;
+    cudaStreamSynchronize(stream());
+    for (void* p : m->pre_allocs) cudaFree(p);
+    m->pre_allocs.clear();
+    m->pre = RkBufs{};
+    bool ok = true;
+    auto al = [&](size_t n) -> float* {
+        void* p = nullptr;
+        if (cudaMalloc(&p, (n ? n : 1) * sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+            return nullptr;
+        }
+        m->pre_allocs.push_back(p);
+        return (float*)p;
+    };
+    const size_t R = (size_t)rows, D = m->D, S = m->nseq;
+    RkBufs w;
+    w.rows = rows;
+    w.tok = (int32_t*)al(R);
+    w.x = al(R * D); w.xn = al(R * D); w.planes = al(6 * R * D);
+    w.r = al(R * D); w.k = al(R * D); w.v = al(R * D); w.a = al(R * D); w.g = al(R * D);
+    w.kk = al(R * D); w.ww = al(R * D); w.y = al(R * D); w.xk2 = al(R * D);
+    w.lo_w = al(R * m->rmax); w.lo_a = al(R * m->rmax); w.lo_v = al(R * m->rmax);
+    w.lo_g = al(R * m->rmax); w.dw = al(R * D); w.da = al(R * D); w.dv = al(R * D);
+    w.ck = al(R * m->F); w.vfirst = al(R * D);
+    w.xf = al(S * D); w.logits = al(S * m->vocab);
+    if (!ok) return fail(SN_E_NOMEM, "rwkv7 prefill workspace of %d rows", rows);
+    SN_TRY(reserve_tc(m, rows));
+    m->pre = w;
+    return SN_OK;
+}
+
 int load_rwkv(RwkvModel* m, const char* path, int nseq) {
     FILE* f = fopen(path, "rb");
     if (!f) return fail(SN_E_IO, "cannot open %s", path);
@@ -535,6 +649,7 @@ int load_rwkv(RwkvModel* m, const char* path, int nseq) {
         A.Rw = P.i32(); A.Ra = P.i32(); A.Rv = P.i32(); A.Rg = P.i32();
         rmax = std::max(std::max(rmax, std::max(A.Rw, A.Ra)), std::max(A.Rv, A.Rg));
     }
+    m->rmax = rmax;
     for (int l = 0; l < L && P.ok; ++l) {
         RkLayer& A = m->ly[l];
         A.ln1w = P.vec(D); A.ln1b = P.vec(D); A.ln2w = P.vec(D); A.ln2b = P.vec(D);
@@ -578,22 +693,7 @@ int load_rwkv(RwkvModel* m, const char* path, int nseq) {
     cudaMemset(m->S, 0, B * L * m->NH * m->HS * m->HS * 4);
     cudaMemset(m->shift, 0, B * L * 2 * D * 4);
     SN_TRY(cuda_check(cudaStreamCreateWithFlags(&m->cap, cudaStreamNonBlocking), "stream"));
-    {   // activation workspace of the tensor-core W4A8 path, before any capture
-        auto reserve = [&](const RkMat& M) -> int {
-            if (!M.q4 || !w4a8_tc_ok(nseq, M.in, M.out, M.block, M.q)) return SN_OK;
-            return w4a8_tc_reserve(nseq, M.in, M.block);
-        };
-        for (const RkLayer& y : m->ly)
-            for (const RkMat* M : {&y.rw, &y.kw, &y.vw, &y.ow, &y.w1, &y.w2, &y.a1, &y.a2, &y.v1,
-                                   &y.v2, &y.g1, &y.g2, &y.cmk, &y.cmv})
-                SN_TRY(reserve(*M));
-        SN_TRY(reserve(m->head));
-        if (!m->ly.empty()) {  // the grouped first-stage projections: six input planes
-            const RkMat& r0 = m->ly[0].rw;
-            if (r0.q4 && w4a8_tc_ok(nseq, r0.in, r0.out, r0.block, r0.q))
-                SN_TRY(w4a8_tc_reserve(nseq, r0.in, r0.block, 6));
-        }
-    }
+    SN_TRY(reserve_tc(m, nseq));  // before any capture
     SN_TRY(cuda_check(cudaDeviceSynchronize(), "rwkv load"));
     m->ready = true;
     return SN_OK;
@@ -624,19 +724,35 @@ enum { E_STORE = 0, E_ADD = 1, E_RELU2 = 2, E_TANH = 3, E_SIG = 4 };
 // trace (device, (B, L+1, D)) or nullptr: the residual stream entering each
 // layer and leaving the last one, copied out after the embedding and after
 // every layer (a debugging view of the same kernels, used without a graph).
-int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer = -1,
-               float* trace = nullptr) {
+// A pass over `nb` sequences of T tokens each (rows = nb * T, sequence-major;
+// T = 1 is a decode step): every contraction and elementwise kernel runs over
+// all rows at once, the token shift reads the previous row of the same
+// sequence, the matrix-state recurrence walks each sequence's rows in order.
+// With T > 1 the shift states are set from each sequence's last row after
+// the kernels that read them, and the head (when asked) runs on the last row
+// of each sequence only.
+int enqueue_rk(RwkvModel* m, const RkBufs& w, int nb, int T, bool head, cudaStream_t st,
+               int last_layer = -1, float* trace = nullptr) {
     const int D = m->D;
+    const int B = nb * T;  // rows
     const size_t plane = (size_t)B * D;
+    // the shift state of layer l, slot j, from the last row of each sequence
+    auto shift_from_last = [&](int l, int j, const float* src) {
+        return cuda_check(cudaMemcpy2DAsync(m->shift + ((size_t)l * 2 + j) * D,
+                                            (size_t)m->L * 2 * D * 4, src + (size_t)(T - 1) * D,
+                                            (size_t)T * D * 4, (size_t)D * 4, (size_t)nb,
+                                            cudaMemcpyDeviceToDevice, st),
+                          "shift update");
+    };
     const long long sh_stride = (long long)m->L * 2 * D;
     auto trace_x = [&](int j) {
         return cuda_check(cudaMemcpy2DAsync(trace + (size_t)j * D, (size_t)(m->L + 1) * D * 4,
-                                            m->x, (size_t)D * 4, (size_t)D * 4, (size_t)B,
+                                            w.x, (size_t)D * 4, (size_t)D * 4, (size_t)B,
                                             cudaMemcpyDeviceToDevice, st),
                           "trace copy");
     };
-    rk_embed_kernel<<<B, 256, 0, st>>>(D, m->tok, m->vocab, rt().d_err, m->embed, m->en_w,
-                                       m->en_b, m->x, m->eps);
+    rk_embed_kernel<<<B, 256, 0, st>>>(D, w.tok, m->vocab, rt().d_err, m->embed, m->en_w,
+                                       m->en_b, w.x, m->eps);
     if (trace) SN_TRY(trace_x(0));
     const int nl = last_layer >= 0 ? last_layer + 1 : m->L;
     const unsigned ew = (unsigned)((plane + 255) / 256);
@@ -646,16 +762,17 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
         // every kernel after the embedding follows another one on this stream:
         // programmatic launches (each waits before touching its inputs)
         SN_TRY(cuda_check(launch_pdl(rk_tmix_prep_kernel, dim3(B), dim3(256), 0, st, D, B,
-                                     (const float*)m->x, sh, sh_stride, (const float*)A.ln1w,
-                                     (const float*)A.ln1b, (const float*)A.lerp, m->xn, m->planes,
-                                     m->eps),
+                                     (const float*)w.x, sh, sh_stride, (const float*)A.ln1w,
+                                     (const float*)A.ln1b, (const float*)A.lerp, w.xn, w.planes,
+                                     m->eps, T),
                           "tmix launch"));
-        const float *xr = m->planes, *xw = xr + plane, *xk = xw + plane, *xv = xk + plane,
+        if (T > 1) SN_TRY(shift_from_last(l, 0, w.xn));
+        const float *xr = w.planes, *xw = xr + plane, *xk = xw + plane, *xv = xk + plane,
                     *xa = xv + plane, *xg = xa + plane;
         {   // first-stage projections of the input mixes (v1 from layer 1 on):
             // one grouped tensor-core launch when every matrix qualifies
             const RkMat* gm[7] = {&A.rw, &A.kw, &A.vw, &A.w1, &A.a1, &A.g1, &A.v1};
-            float* gy[7] = {m->r, m->k, m->v, m->lo_w, m->lo_a, m->lo_g, m->lo_v};
+            float* gy[7] = {w.r, w.k, w.v, w.lo_w, w.lo_a, w.lo_g, w.lo_v};
             const float* gx[7] = {xr, xk, xv, xw, xa, xg, xv};
             const int ge[7] = {E_STORE, E_STORE, E_STORE, E_TANH, E_STORE, E_SIG, E_STORE};
             const int ng = l > 0 ? 7 : 6;
@@ -686,7 +803,7 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
                 for (int i = 0; i < ng; ++i) SN_TRY(mat_mul(*gm[i], gy[i], gx[i], B, ge[i], st));
             }
         }
-        SN_TRY(mat_mul(A.g2, m->g, m->lo_g, B, E_STORE, st));
+        SN_TRY(mat_mul(A.g2, w.g, w.lo_g, B, E_STORE, st));
         // fp32 LoRA second stages (ranks below a quantisation block stay fp32)
         // are folded into the mix kernel
         const int R = A.w2.in + A.a2.in + (l > 0 ? A.v2.in : 0);
@@ -699,33 +816,33 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
                 launch_pdl(rk_lora_mix_kernel, dim3((unsigned)((D + 31) / 32), (unsigned)((B + 7) / 8)),
                            dim3(256), smem, st, B, D, l == 0 ? 1 : 0, A.w2.in, A.a2.in, A.v2.in,
                            (const float*)A.w2.w, (const float*)A.a2.w, (const float*)A.v2.w,
-                           (const float*)m->lo_w, (const float*)m->lo_a, (const float*)m->lo_v,
+                           (const float*)w.lo_w, (const float*)w.lo_a, (const float*)w.lo_v,
                            (const float*)A.w0, (const float*)A.v0, (const float*)A.a0,
-                           (const float*)A.kkw, (const float*)A.kaw, m->ww, m->v, m->vfirst, m->a,
-                           m->k, m->kk),
+                           (const float*)A.kkw, (const float*)A.kaw, w.ww, w.v, w.vfirst, w.a,
+                           w.k, w.kk),
                 "lora mix launch"));
         } else {
-            SN_TRY(mat_mul(A.w2, m->dw, m->lo_w, B, E_STORE, st));
-            if (l > 0) SN_TRY(mat_mul(A.v2, m->dv, m->lo_v, B, E_STORE, st));
-            SN_TRY(mat_mul(A.a2, m->da, m->lo_a, B, E_STORE, st));
+            SN_TRY(mat_mul(A.w2, w.dw, w.lo_w, B, E_STORE, st));
+            if (l > 0) SN_TRY(mat_mul(A.v2, w.dv, w.lo_v, B, E_STORE, st));
+            SN_TRY(mat_mul(A.a2, w.da, w.lo_a, B, E_STORE, st));
             SN_TRY(cuda_check(launch_pdl(rk_mix_kernel, dim3(ew), dim3(256), 0, st, B, D,
-                                         l == 0 ? 1 : 0, (const float*)m->dw, (const float*)A.w0,
-                                         (const float*)m->dv, (const float*)A.v0,
-                                         (const float*)m->da, (const float*)A.a0,
-                                         (const float*)A.kkw, (const float*)A.kaw, m->ww, m->v,
-                                         m->vfirst, m->a, m->k, m->kk),
+                                         l == 0 ? 1 : 0, (const float*)w.dw, (const float*)A.w0,
+                                         (const float*)w.dv, (const float*)A.v0,
+                                         (const float*)w.da, (const float*)A.a0,
+                                         (const float*)A.kkw, (const float*)A.kaw, w.ww, w.v,
+                                         w.vfirst, w.a, w.k, w.kk),
                               "mix launch"));
         }
         {
-            const dim3 grid((unsigned)(B * m->NH));
+            const dim3 grid((unsigned)(nb * m->NH));
             ProfScope ps_heads("rk_heads", st);
             cudaError_t e;
             switch (m->HS) {
 #define RK_HEADS(V)                                                                                \
     e = launch_pdl(rk_heads_kernel<V>, grid, dim3(256), 0, st, m->NH, m->L, l, D, m->S,            \
-                   (const float*)m->ww, (const float*)m->k, (const float*)m->v, (const float*)m->a, \
-                   (const float*)m->kk, (const float*)m->r, (const float*)m->g,                    \
-                   (const float*)A.rkw, (const float*)A.lnxw, (const float*)A.lnxb, m->y);         \
+                   (const float*)w.ww, (const float*)w.k, (const float*)w.v, (const float*)w.a, \
+                   (const float*)w.kk, (const float*)w.r, (const float*)w.g,                    \
+                   (const float*)A.rkw, (const float*)A.lnxw, (const float*)A.lnxb, w.y, T);      \
     break;
                 case 32: RK_HEADS(1)
                 case 64: RK_HEADS(2)
@@ -735,21 +852,24 @@ int enqueue_rk(RwkvModel* m, int B, bool head, cudaStream_t st, int last_layer =
             }
             SN_TRY(cuda_check(e, "heads launch"));
         }
-        SN_TRY(mat_mul(A.ow, m->x, m->y, B, E_ADD, st));
+        SN_TRY(mat_mul(A.ow, w.x, w.y, B, E_ADD, st));
         SN_TRY(cuda_check(launch_pdl(rk_cmix_prep_kernel, dim3(B), dim3(256), 0, st, D,
-                                     (const float*)m->x, sh, sh_stride, (const float*)A.ln2w,
-                                     (const float*)A.ln2b, (const float*)A.cmk_lerp, m->xk2,
-                                     m->eps),
+                                     (const float*)w.x, sh, sh_stride, (const float*)A.ln2w,
+                                     (const float*)A.ln2b, (const float*)A.cmk_lerp, w.xk2,
+                                     m->eps, T, T > 1 ? w.xn : (float*)nullptr),
                           "cmix launch"));
-        SN_TRY(mat_mul(A.cmk, m->ck, m->xk2, B, E_RELU2, st));
-        SN_TRY(mat_mul(A.cmv, m->x, m->ck, B, E_ADD, st));
+        if (T > 1) SN_TRY(shift_from_last(l, 1, w.xn));
+        SN_TRY(mat_mul(A.cmk, w.ck, w.xk2, B, E_RELU2, st));
+        SN_TRY(mat_mul(A.cmv, w.x, w.ck, B, E_ADD, st));
         if (trace) SN_TRY(trace_x(l + 1));
     }
-    if (last_layer < 0 && head) {
-        SN_TRY(cuda_check(launch_pdl(rk_ln_kernel, dim3(B), dim3(256), 0, st, D, (const float*)m->x,
-                                     (const float*)m->on_w, (const float*)m->on_b, m->xf, m->eps),
+    if (last_layer < 0 && head) {  // the last row of each sequence
+        SN_TRY(cuda_check(launch_pdl(rk_ln_kernel, dim3(nb), dim3(256), 0, st, D,
+                                     (const float*)(w.x + (size_t)(T - 1) * D),
+                                     (const float*)m->on_w, (const float*)m->on_b, w.xf, m->eps,
+                                     (long long)T * D),
                           "ln launch"));
-        SN_TRY(mat_mul(m->head, m->logits, m->xf, B, E_STORE, st));
+        SN_TRY(mat_mul(m->head, w.logits, w.xf, nb, E_STORE, st));
     }
     return cuda_check(cudaGetLastError(), "rwkv step launch");
 }
@@ -758,15 +878,17 @@ int rk_run(RwkvModel* m, int B, bool head, float* trace = nullptr) {
     auto key = std::make_pair(B, head ? 1 : 0);
     if (prof_graph() && !trace)  // the step's graph with event nodes around each family
         return prof_graph_run(&m->pgraphs[key], m->cap, stream(),
-                              [&](cudaStream_t cs) { return enqueue_rk(m, B, head, cs); });
+                              [&](cudaStream_t cs) {
+                                  return enqueue_rk(m, step_bufs(m), B, 1, head, cs);
+                              });
     if (prof_on() || trace)  // bracket kernels / copy out the trace: no graph
-        return enqueue_rk(m, B, head, stream(), -1, trace);
+        return enqueue_rk(m, step_bufs(m), B, 1, head, stream(), -1, trace);
     auto it = m->graphs.find(key);
     if (it == m->graphs.end()) {
         cudaGraph_t g = nullptr;
         SN_TRY(cuda_check(cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeThreadLocal),
                           "begin capture"));
-        const int rc = enqueue_rk(m, B, head, m->cap);
+        const int rc = enqueue_rk(m, step_bufs(m), B, 1, head, m->cap);
         const cudaError_t e = cudaStreamEndCapture(m->cap, &g);
         if (rc != SN_OK) {
             if (g) cudaGraphDestroy(g);
@@ -816,6 +938,47 @@ int rk_step(RwkvModel* m, const int32_t* tokens, int B, float* logits, int32_t* 
                                           dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
                                           st),
                           "next"));
+    }
+    return finish(host);
+}
+
+// Prompt of T tokens for each of nb sequences (tokens (nb, T) row-major, host
+// or device) -> logits (nb, vocab) of each sequence's last token (NULL: state
+// only). Replaces the reference's token-by-token loop (rwkv7.c:362-364) with
+// layer-major passes over chunks of the prompt: every contraction over all
+// nb x Tc rows of a chunk at once, the recurrence T-serial per (sequence,
+// head), the state carried from chunk to chunk.
+constexpr int kPrefillRows = 8192;  // rows per pass (bounds the workspace)
+
+int rk_prefill(RwkvModel* m, const int32_t* tokens, int nb, int T, float* logits) {
+    if (!m || !m->ready || !tokens || nb <= 0 || T <= 0 || nb > m->nseq)
+        return fail(SN_E_INVAL, "rwkv7_prefill: bad handle, tokens or shape");
+    std::lock_guard<std::recursive_mutex> lk(rt().mu);
+    cudaStream_t st = stream();
+    int cap = std::max(kPrefillRows, m->nseq);
+    if (const char* e = getenv("SN_RK_PREFILL_ROWS"))  // test hook: smaller passes
+        cap = std::max(1, atoi(e));
+    const int Tc = std::max(1, std::min(T, cap / nb));
+    SN_TRY(ensure_pre(m, nb * Tc));
+    const bool tdev = is_device_ptr(tokens);
+    for (int t0 = 0; t0 < T; t0 += Tc) {
+        const int tc = std::min(Tc, T - t0);
+        SN_TRY(cuda_check(cudaMemcpy2DAsync(m->pre.tok, (size_t)tc * 4, tokens + t0,
+                                            (size_t)T * 4, (size_t)tc * 4, (size_t)nb,
+                                            tdev ? cudaMemcpyDeviceToDevice
+                                                 : cudaMemcpyHostToDevice,
+                                            st),
+                          "prefill tokens"));
+        SN_TRY(enqueue_rk(m, m->pre, nb, tc, logits != nullptr && t0 + tc >= T, st));
+    }
+    bool host = !tdev;
+    if (logits) {
+        const bool dev = is_device_ptr(logits);
+        host |= !dev;
+        SN_TRY(cuda_check(cudaMemcpyAsync(logits, m->pre.logits, (size_t)nb * m->vocab * 4,
+                                          dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                                          st),
+                          "logits"));
     }
     return finish(host);
 }
@@ -877,11 +1040,16 @@ sn_status sn_abi_rwkv7_step(SnAbiRwkv7* m, int32_t token, float* logits) {
 
 sn_status sn_abi_rwkv7_prefill(SnAbiRwkv7* m, const int32_t* tokens, int32_t n, float* logits) {
     if (!m || !tokens || !logits || n <= 0) return SN_E_INVAL;
-    for (int i = 0; i < n; ++i) {
-        if (tokens[i] < 0 || tokens[i] >= m->m->vocab) return SN_E_INVAL;
-        SN_TRY(rk_step(m->m.get(), tokens + i, 1, i == n - 1 ? logits : nullptr, nullptr));
-    }
-    return SN_OK;
+    if (!is_device_ptr(tokens))  // host ids are checked here (device ids on the device)
+        for (int i = 0; i < n; ++i)
+            if (tokens[i] < 0 || tokens[i] >= m->m->vocab) return SN_E_INVAL;
+    return rk_prefill(m->m.get(), tokens, 1, n, logits);
+}
+
+sn_status sn_abi_rwkv7_prefill_batch(SnAbiRwkv7* m, const int32_t* tokens, int32_t B, int32_t T,
+                                     float* logits) {
+    if (!m) return SN_E_INVAL;
+    return rk_prefill(m->m.get(), tokens, B, T, logits);
 }
 
 sn_status sn_abi_rwkv7_reset(SnAbiRwkv7* m) { return m ? rk_reset(m->m.get()) : SN_E_INVAL; }
@@ -956,10 +1124,7 @@ void sn_rk_step(SnRWKV7* m, int token, float* logits) {
 
 void sn_rk_prefill(SnRWKV7* m, const int* tokens, int n, float* logits) {
     if (!m || !tokens || n <= 0) return;
-    for (int i = 0; i < n; ++i) {
-        const int32_t t = tokens[i];
-        if (rk_step(m->m.get(), &t, 1, i == n - 1 ? logits : nullptr, nullptr) != SN_OK) return;
-    }
+    rk_prefill(m->m.get(), (const int32_t*)tokens, 1, n, logits);
 }
 
 void sn_rk_dbg(SnRWKV7* m, int token, int layer, float* out) {
@@ -969,7 +1134,7 @@ void sn_rk_dbg(SnRWKV7* m, int token, int layer, float* out) {
     cudaStream_t st = stream();
     const int32_t t = token;
     cudaMemcpyAsync(r->tok, &t, 4, cudaMemcpyHostToDevice, st);
-    if (enqueue_rk(r, 1, false, st, layer) != SN_OK) return;
+    if (enqueue_rk(r, step_bufs(r), 1, 1, false, st, layer) != SN_OK) return;
     // xn, r, k, v, a, g, ww, y, x (rwkv7.c:322-333)
     const float* parts[9] = {r->xn, r->r, r->k, r->v, r->a, r->g, r->ww, r->y, r->x};
     Arr o;

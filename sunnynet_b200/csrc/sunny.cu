@@ -190,15 +190,16 @@ __global__ void ln_split_kernel(int n, const float* __restrict__ X, long long ld
 }
 
 
-// --------------------------------------------- row kernels: one warp per row
-// Rows of up to 128 * NV floats (n % 4 == 0, 16-byte aligned rows) are held in
-// registers as float4 (lane j covers columns 4 * (lane + 32 k)); the LN
-// statistics are warp sums (no block barriers), every load is 16 bytes. Eight
-// rows per 256-thread CTA. The launchers below pick these whenever the shape
-// allows, for every path alike (the step, the split-launch step, the fused
-// B <= 8 step's fallback, prefill), so paths that must agree bit for bit
-// compute their statistics the same way.
-constexpr int kRowsPerCta = 8;
+// ------------------------------------- row kernels: one float4 per thread
+// One CTA per row of n floats (n % 4 == 0, 16-byte aligned rows), n / 4
+// threads rounded up to whole warps, each thread holding one float4 of the
+// row in registers: every load of a row is issued at once, the statistics
+// are warp sums combined through shared memory, and B rows give B CTAs. The
+// launchers below pick these whenever the shape allows, for every path alike
+// (the step, the split-launch step, the fused B <= 8 step's fallback,
+// prefill), so paths that must agree bit for bit compute their statistics the
+// same way.
+constexpr int kRowMaxThreads = 1024;  // rows up to 4096 floats
 
 __device__ __forceinline__ float warp_allsum(float v) {
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -208,153 +209,155 @@ __device__ __forceinline__ float warp_allsum(float v) {
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 
-// mean and 1/sqrt(var + eps) of the row held in v[0..NV) (n valid floats)
-template <int NV>
-__device__ __forceinline__ void warp_row_stats(const float4 (&v)[NV], int n, int lane, float eps,
-                                               float* mean, float* rstd) {
-    float s = 0.0f;
-#pragma unroll
-    for (int k = 0; k < NV; ++k)
-        if (4 * (lane + 32 * k) < n) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
-    const float mu = warp_allsum(s) / (float)n;
-    float q = 0.0f;
-#pragma unroll
-    for (int k = 0; k < NV; ++k)
-        if (4 * (lane + 32 * k) < n) {
-            const float a = v[k].x - mu, b = v[k].y - mu, c = v[k].z - mu, d = v[k].w - mu;
-            q += (a * a + b * b) + (c * c + d * d);
-        }
-    *mean = mu;
-    *rstd = 1.0f / sqrtf(warp_allsum(q) / (float)n + eps);
+// sum over the CTA (whole warps), returned to every thread
+__device__ __forceinline__ float cta_allsum(float v, float* red) {
+    v = warp_allsum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();  // red is free (a previous reduction has been read)
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = l < nw ? red[l] : 0.0f;
+    return warp_allsum(t);
 }
 
-// prep_kernel's work, one warp per sequence
-template <int NV>
-__global__ void __launch_bounds__(256)
-    prep_rows_kernel(int B, int D, int K, int KH, int layer, int L,
-                     const int32_t* __restrict__ tok, int vocab, int* __restrict__ err,
-                     const float* __restrict__ embed, float* __restrict__ x,
-                     float* __restrict__ raw_out, float* __restrict__ at,
-                     float* __restrict__ hist, int32_t* __restrict__ pos,
-                     const float* __restrict__ g, const float* __restrict__ c,
-                     const float* __restrict__ dw, float eps, __nv_bfloat16* __restrict__ ath,
-                     __nv_bfloat16* __restrict__ atl) {
+// mean and 1/sqrt(var + eps) of the row whose float4 `v` this thread holds
+// (`live`: the thread's columns are inside the row)
+__device__ __forceinline__ void cta_row_stats(float4 v, bool live, int n, float eps, float* red,
+                                              float* mean, float* rstd) {
+    const float s = live ? (v.x + v.y) + (v.z + v.w) : 0.0f;
+    const float mu = cta_allsum(s, red) / (float)n;
+    float q = 0.0f;
+    if (live) {
+        const float a = v.x - mu, b = v.y - mu, c = v.z - mu, d = v.w - mu;
+        q = (a * a + b * b) + (c * c + d * d);
+    }
+    *mean = mu;
+    *rstd = 1.0f / sqrtf(cta_allsum(q, red) / (float)n + eps);
+}
+
+// prep_kernel's work (LN, causal taps, ring write), one float4 per thread
+__global__ void __launch_bounds__(kRowMaxThreads)
+    prep_vec_kernel(int D, int K, int KH, int layer, int L, const int32_t* __restrict__ tok,
+                    int vocab, int* __restrict__ err, const float* __restrict__ embed,
+                    float* __restrict__ x, float* __restrict__ raw_out, float* __restrict__ at,
+                    float* __restrict__ hist, int32_t* __restrict__ pos,
+                    const float* __restrict__ g, const float* __restrict__ c,
+                    const float* __restrict__ dw, float eps, __nv_bfloat16* __restrict__ ath,
+                    __nv_bfloat16* __restrict__ atl) {
+    __shared__ float red[32];
     pdl_trigger();
     pdl_wait();
-    const int lane = threadIdx.x & 31;
-    const int b = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
-    if (b >= B) return;
+    const int b = blockIdx.x;
+    const int col = 4 * threadIdx.x;
+    const bool live = col < D;
     const int p = pos[b * L + layer];
     float* xr = x + (size_t)b * D;
     const float* src = xr;
     if (layer == 0) {
         int t = tok[b];
         if (t < 0 || t >= vocab) {  // never read outside the table; report instead
-            if (lane == 0) atomicExch(err, kErrBadIndex);
+            if (threadIdx.x == 0) atomicExch(err, kErrBadIndex);
             t = 0;
         }
         src = embed + (size_t)t * D;
     }
-    float4 v[NV];
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-        const int col = 4 * (lane + 32 * k);
-        if (col < D) {
-            v[k] = ld4(src + col);
-            if (layer == 0) st4(xr + col, v[k]);
-        }
-    }
-    float mean, rstd;
-    warp_row_stats<NV>(v, D, lane, eps, &mean, &rstd);
     float* hb = hist + ((size_t)b * L + layer) * KH * D;
-    const int wslot = ((p % KH) + KH) % KH;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f), gg = v, cc = v, wl = v;
+    float4 hv[3], wv[3];
+    const int kk = K - 1 < 3 ? K - 1 : 3;  // history rows held in registers
+    if (live) {  // every load of this thread's columns, issued together
+        v = ld4(src + col);
+        gg = ld4(g + col);
+        cc = ld4(c + col);
+        if (K > 1) wl = ld4(dw + (size_t)(K - 1) * D + col);
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-        const int col = 4 * (lane + 32 * k);
-        if (col >= D) continue;
-        const float4 gg = ld4(g + col), cc = ld4(c + col);
-        float r[4] = {(v[k].x - mean) * rstd * gg.x + cc.x, (v[k].y - mean) * rstd * gg.y + cc.y,
-                      (v[k].z - mean) * rstd * gg.z + cc.z, (v[k].w - mean) * rstd * gg.w + cc.w};
-        float a[4] = {r[0], r[1], r[2], r[3]};
-        if (K > 1) {
-            const float4 wl = ld4(dw + (size_t)(K - 1) * D + col);
-            float acc[4] = {r[0] * wl.x, r[1] * wl.y, r[2] * wl.z, r[3] * wl.w};
-            for (int j = 0; j < K - 1; ++j) {
+        for (int j = 0; j < 3; ++j)
+            if (j < kk) {
                 const int slot = ((p - 1 - j) % KH + KH) % KH;
-                const float4 h = ld4(hb + (size_t)slot * D + col);
-                const float4 w = ld4(dw + (size_t)(K - 2 - j) * D + col);
-                acc[0] += h.x * w.x;
-                acc[1] += h.y * w.y;
-                acc[2] += h.z * w.z;
-                acc[3] += h.w * w.w;
+                hv[j] = ld4(hb + (size_t)slot * D + col);
+                wv[j] = ld4(dw + (size_t)(K - 2 - j) * D + col);
             }
-#pragma unroll
-            for (int e = 0; e < 4; ++e) a[e] = r[e] + acc[e];
-            st4(hb + (size_t)wslot * D + col, make_float4(r[0], r[1], r[2], r[3]));
+        if (layer == 0) st4(xr + col, v);
+    }
+    float mean, rstd;
+    cta_row_stats(v, live, D, eps, red, &mean, &rstd);
+    if (!live) return;
+    const float r[4] = {(v.x - mean) * rstd * gg.x + cc.x, (v.y - mean) * rstd * gg.y + cc.y,
+                        (v.z - mean) * rstd * gg.z + cc.z, (v.w - mean) * rstd * gg.w + cc.w};
+    float a[4] = {r[0], r[1], r[2], r[3]};
+    if (K > 1) {
+        float acc[4] = {r[0] * wl.x, r[1] * wl.y, r[2] * wl.z, r[3] * wl.w};
+        for (int j = 0; j < K - 1; ++j) {
+            float4 h, w;
+            if (j < 3) {
+                h = hv[j < 3 ? j : 0];
+                w = wv[j < 3 ? j : 0];
+            } else {  // taps beyond the registers: load in order
+                const int slot = ((p - 1 - j) % KH + KH) % KH;
+                h = ld4(hb + (size_t)slot * D + col);
+                w = ld4(dw + (size_t)(K - 2 - j) * D + col);
+            }
+            acc[0] += h.x * w.x;
+            acc[1] += h.y * w.y;
+            acc[2] += h.z * w.z;
+            acc[3] += h.w * w.w;
         }
-        const float4 av = make_float4(a[0], a[1], a[2], a[3]);
-        st4(at + (size_t)b * D + col, av);
-        if (ath) store_split4(ath, atl, (long long)b * D + col, av);
-        if (raw_out) st4(raw_out + (size_t)b * D + col, make_float4(r[0], r[1], r[2], r[3]));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) a[e] = r[e] + acc[e];
+        st4(hb + (size_t)(((p % KH) + KH) % KH) * D + col, make_float4(r[0], r[1], r[2], r[3]));
     }
-    if (lane == 0) pos[b * L + layer] = p + 1;
+    const float4 av = make_float4(a[0], a[1], a[2], a[3]);
+    st4(at + (size_t)b * D + col, av);
+    if (ath) store_split4(ath, atl, (long long)b * D + col, av);
+    if (raw_out) st4(raw_out + (size_t)b * D + col, make_float4(r[0], r[1], r[2], r[3]));
+    if (threadIdx.x == 0) pos[b * L + layer] = p + 1;
 }
 
-// rowstats_kernel's work, one warp per row
-template <int NV>
-__global__ void __launch_bounds__(256)
-    rowstats_rows_kernel(int rows, int n, const float* __restrict__ X, long long ldx,
-                         float* __restrict__ mu, float* __restrict__ rs, float eps) {
+// rowstats_kernel's work, one float4 per thread
+__global__ void __launch_bounds__(kRowMaxThreads)
+    rowstats_vec_kernel(int n, const float* __restrict__ X, long long ldx,
+                        float* __restrict__ mu, float* __restrict__ rs, float eps) {
+    __shared__ float red[32];
     pdl_trigger();
     pdl_wait();
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
-    if (row >= rows) return;
-    const float* xr = X + (size_t)row * ldx;
-    float4 v[NV];
-#pragma unroll
-    for (int k = 0; k < NV; ++k)
-        if (4 * (lane + 32 * k) < n) v[k] = ld4(xr + 4 * (lane + 32 * k));
+    const int col = 4 * threadIdx.x;
+    const bool live = col < n;
+    const float4 v = live ? ld4(X + (size_t)blockIdx.x * ldx + col)
+                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float mean, rstd;
-    warp_row_stats<NV>(v, n, lane, eps, &mean, &rstd);
-    if (lane == 0) {
-        mu[row] = mean;
-        rs[row] = rstd;
+    cta_row_stats(v, live, n, eps, red, &mean, &rstd);
+    if (threadIdx.x == 0) {
+        mu[blockIdx.x] = mean;
+        rs[blockIdx.x] = rstd;
     }
 }
 
-// ln_split_kernel's work, one warp per row: the same statistics as
-// rowstats_rows_kernel, then ((x - mu) * rs) * g + c per element
-template <int NV>
-__global__ void __launch_bounds__(256)
-    ln_split_rows_kernel(int rows, int n, const float* __restrict__ X, long long ldx,
-                         const float* __restrict__ g, const float* __restrict__ c,
-                         __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo,
-                         float eps) {
+// ln_split_kernel's work, one float4 per thread: the statistics as
+// rowstats_vec_kernel, then ((x - mu) * rs) * g + c per element
+__global__ void __launch_bounds__(kRowMaxThreads)
+    ln_split_vec_kernel(int n, const float* __restrict__ X, long long ldx,
+                        const float* __restrict__ g, const float* __restrict__ c,
+                        __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo,
+                        float eps) {
+    __shared__ float red[32];
     pdl_trigger();
     pdl_wait();
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
-    if (row >= rows) return;
-    const float* xr = X + (size_t)row * ldx;
-    float4 v[NV];
-#pragma unroll
-    for (int k = 0; k < NV; ++k)
-        if (4 * (lane + 32 * k) < n) v[k] = ld4(xr + 4 * (lane + 32 * k));
-    float mean, rstd;
-    warp_row_stats<NV>(v, n, lane, eps, &mean, &rstd);
-    const long long o = (long long)row * n;
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-        const int col = 4 * (lane + 32 * k);
-        if (col >= n) continue;
-        const float4 gg = ld4(g + col), cc = ld4(c + col);
-        const float4 y = make_float4(__fmul_rn(__fmul_rn(v[k].x - mean, rstd), gg.x) + cc.x,
-                                     __fmul_rn(__fmul_rn(v[k].y - mean, rstd), gg.y) + cc.y,
-                                     __fmul_rn(__fmul_rn(v[k].z - mean, rstd), gg.z) + cc.z,
-                                     __fmul_rn(__fmul_rn(v[k].w - mean, rstd), gg.w) + cc.w);
-        store_split4(hi, lo, o + col, y);
+    const int col = 4 * threadIdx.x;
+    const bool live = col < n;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f), gg = v, cc = v;
+    if (live) {
+        v = ld4(X + (size_t)blockIdx.x * ldx + col);
+        gg = ld4(g + col);
+        cc = ld4(c + col);
     }
+    float mean, rstd;
+    cta_row_stats(v, live, n, eps, red, &mean, &rstd);
+    if (!live) return;
+    const float4 y = make_float4(__fmul_rn(__fmul_rn(v.x - mean, rstd), gg.x) + cc.x,
+                                 __fmul_rn(__fmul_rn(v.y - mean, rstd), gg.y) + cc.y,
+                                 __fmul_rn(__fmul_rn(v.z - mean, rstd), gg.z) + cc.z,
+                                 __fmul_rn(__fmul_rn(v.w - mean, rstd), gg.w) + cc.w);
+    store_split4(hi, lo, (long long)blockIdx.x * n + col, y);
 }
 
 // gate_kernel's work for groups of 8 channels, one thread per (sequence,
@@ -371,30 +374,21 @@ __global__ void __launch_bounds__(256)
     if (i >= (long long)B * ng) return;
     const int b = (int)(i / ng), d0 = (int)(i - (long long)b * ng) * 8;
     const float* qb = q + (size_t)b * 2 * D;
-    float ur[8], gt[8], dl[8], sv[8];
-    {
-        const float4 a0 = ld4(qb + d0), a1 = ld4(qb + d0 + 4);
-        const float4 g0 = ld4(qb + D + d0), g1 = ld4(qb + D + d0 + 4);
-        const float4 e0 = ld4(delta + d0), e1 = ld4(delta + d0 + 4);
-        ur[0] = a0.x; ur[1] = a0.y; ur[2] = a0.z; ur[3] = a0.w;
-        ur[4] = a1.x; ur[5] = a1.y; ur[6] = a1.z; ur[7] = a1.w;
-        gt[0] = g0.x; gt[1] = g0.y; gt[2] = g0.z; gt[3] = g0.w;
-        gt[4] = g1.x; gt[5] = g1.y; gt[6] = g1.z; gt[7] = g1.w;
-        dl[0] = e0.x; dl[1] = e0.y; dl[2] = e0.z; dl[3] = e0.w;
-        dl[4] = e1.x; dl[5] = e1.y; dl[6] = e1.z; dl[7] = e1.w;
-    }
     float* sp = s + ((size_t)b * L + layer) * D + d0;
-    {
-        const float4 s0 = ld4(sp), s1 = ld4(sp + 4);
-        sv[0] = s0.x; sv[1] = s0.y; sv[2] = s0.z; sv[3] = s0.w;
-        sv[4] = s1.x; sv[5] = s1.y; sv[6] = s1.z; sv[7] = s1.w;
-    }
+    const float4 a0 = ld4(qb + d0), a1 = ld4(qb + d0 + 4);
+    const float4 g0 = ld4(qb + D + d0), g1 = ld4(qb + D + d0 + 4);
+    const float4 e0 = ld4(delta + d0), e1 = ld4(delta + d0 + 4);
+    const float4 s0 = ld4(sp), s1 = ld4(sp + 4);
+    const float ur[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const float gt[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float dl[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
     float uo[8], so[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        const float g0 = gt[k], g1 = gt[(k + 1) & 7], g2 = gt[(k + 2) & 7];
-        const float uu = ur[k] * (sigm(g0 - g1) * sigm(g0 - g2));
-        float p = 1.0f - dl[k] * (1.0f - sigm(g0));
+        const float gk = gt[k], gk1 = gt[(k + 1) & 7], gk2 = gt[(k + 2) & 7];
+        const float uu = ur[k] * (sigm(gk - gk1) * sigm(gk - gk2));
+        float p = 1.0f - dl[k] * (1.0f - sigm(gk));
         if (clamp && p < p_floor) p = p_floor;
         so[k] = p * sv[k] + (1.0f - p) * uu;
         uo[k] = uu;
@@ -402,41 +396,27 @@ __global__ void __launch_bounds__(256)
     st4(sp, make_float4(so[0], so[1], so[2], so[3]));
     st4(sp + 4, make_float4(so[4], so[5], so[6], so[7]));
     const size_t o = (size_t)b * D + d0;
-    st4(u + o, make_float4(uo[0], uo[1], uo[2], uo[3]));
-    st4(u + o + 4, make_float4(uo[4], uo[5], uo[6], uo[7]));
+    const float4 u0 = make_float4(uo[0], uo[1], uo[2], uo[3]);
+    const float4 u1 = make_float4(uo[4], uo[5], uo[6], uo[7]);
+    st4(u + o, u0);
+    st4(u + o + 4, u1);
     if (uh) {
-        store_split4(uh, ul, (long long)o, make_float4(uo[0], uo[1], uo[2], uo[3]));
-        store_split4(uh, ul, (long long)o + 4, make_float4(uo[4], uo[5], uo[6], uo[7]));
+        store_split4(uh, ul, (long long)o, u0);
+        store_split4(uh, ul, (long long)o + 4, u1);
     }
     if (gate_out) {
-        st4(gate_out + o, make_float4(gt[0], gt[1], gt[2], gt[3]));
-        st4(gate_out + o + 4, make_float4(gt[4], gt[5], gt[6], gt[7]));
+        st4(gate_out + o, g0);
+        st4(gate_out + o + 4, g1);
     }
 }
 
 bool al16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 bool al8(const void* p) { return ((uintptr_t)p & 7) == 0; }
 
-// float4 chunks per lane for a row of n floats (0: the warp kernels do not apply)
-int row_nv(int n) {
-    if (n <= 0 || n % 4) return 0;
-    const int need = (n + 127) / 128;
-    for (int nv : {2, 4, 6, 8, 12, 16, 24})
-        if (need <= nv) return nv;
-    return 0;
-}
-
-#define SN_ROWS_KERNELS(K) K<2>, K<4>, K<6>, K<8>, K<12>, K<16>, K<24>
-
-
-template <typename... KA, typename... Args>
-cudaError_t launch_rows(int nv, bool pdl, dim3 grid, cudaStream_t st, void (*k2)(KA...),
-                        void (*k4)(KA...), void (*k6)(KA...), void (*k8)(KA...),
-                        void (*k12)(KA...), void (*k16)(KA...), void (*k24)(KA...),
-                        Args... args) {
-    void (*k)(KA...) = nv == 2 ? k2 : nv == 4 ? k4 : nv == 6 ? k6 : nv == 8 ? k8
-                     : nv == 12 ? k12 : nv == 16 ? k16 : k24;
-    return launch_pdl_if(pdl, k, grid, dim3(256), 0, st, args...);
+// threads of a row kernel for a row of n floats (0: the float4 kernels do not apply)
+int row_threads(int n) {
+    if (n <= 0 || n % 4 || n / 4 > kRowMaxThreads) return 0;
+    return (n / 4 + 31) / 32 * 32;
 }
 
 // LN + causal taps + ring write of layer `layer` for B sequences (`pdl`:
@@ -445,15 +425,14 @@ int launch_prep(bool pdl, cudaStream_t st, int B, int D, int K, int KH, int laye
                 const int32_t* tok, int vocab, const float* embed, float* x, float* raw_out,
                 float* at, float* hist, int32_t* pos, const float* g, const float* c,
                 const float* dw, float eps, __nv_bfloat16* ath, __nv_bfloat16* atl) {
-    const int nv = row_nv(D);
-    const bool rows = nv && al16(x) && al16(at) && al16(hist) && al16(embed) && al16(g) &&
-                      al16(c) && al16(dw) && (!raw_out || al16(raw_out)) &&
-                      (!ath || (al8(ath) && al8(atl)));
-    if (rows)
-        return cuda_check(launch_rows(nv, pdl, dim3((unsigned)((B + kRowsPerCta - 1) / kRowsPerCta)),
-                                      st, SN_ROWS_KERNELS(prep_rows_kernel), B, D, K, KH, layer, L,
-                                      tok, vocab, rt().d_err, embed, x, raw_out, at, hist, pos, g,
-                                      c, dw, eps, ath, atl),
+    const int nt = row_threads(D);
+    const bool vec = nt && al16(x) && al16(at) && al16(hist) && al16(embed) && al16(g) &&
+                     al16(c) && al16(dw) && (!raw_out || al16(raw_out)) &&
+                     (!ath || (al8(ath) && al8(atl)));
+    if (vec)
+        return cuda_check(launch_pdl_if(pdl, prep_vec_kernel, dim3(B), dim3(nt), 0, st, D, K, KH,
+                                        layer, L, tok, vocab, rt().d_err, embed, x, raw_out, at,
+                                        hist, pos, g, c, dw, eps, ath, atl),
                           "prep launch");
     return cuda_check(launch_pdl_if(pdl, prep_kernel, dim3(B), dim3(256), 0, st, D, K, KH, layer,
                                     L, tok, vocab, rt().d_err, embed, x, raw_out, at, hist, pos,
@@ -480,16 +459,14 @@ int launch_gate(bool pdl, cudaStream_t st, int B, int D, int G, int L, int layer
                       "gate launch");
 }
 
-bool rows_ok(int n, const float* X, long long ldx) { return row_nv(n) && al16(X) && ldx % 4 == 0; }
+bool rows_ok(int n, const float* X, long long ldx) { return row_threads(n) && al16(X) && ldx % 4 == 0; }
 
 // row mean / rstd of `rows` rows of n floats, ldx apart
 int launch_rowstats(bool pdl, cudaStream_t st, int rows, int n, const float* X, long long ldx,
                     float* mu, float* rs, float eps) {
     if (rows_ok(n, X, ldx))
-        return cuda_check(launch_rows(row_nv(n), pdl,
-                                      dim3((unsigned)((rows + kRowsPerCta - 1) / kRowsPerCta)), st,
-                                      SN_ROWS_KERNELS(rowstats_rows_kernel), rows, n, X, ldx, mu,
-                                      rs, eps),
+        return cuda_check(launch_pdl_if(pdl, rowstats_vec_kernel, dim3((unsigned)rows),
+                                        dim3(row_threads(n)), 0, st, n, X, ldx, mu, rs, eps),
                           "rowstats launch");
     return cuda_check(launch_pdl_if(pdl, rowstats_kernel, dim3((unsigned)rows), dim3(256), 0, st,
                                     n, X, ldx, mu, rs, eps),
@@ -501,10 +478,8 @@ int launch_ln_split(bool pdl, cudaStream_t st, int rows, int n, const float* X, 
                     const float* g, const float* c, __nv_bfloat16* hi, __nv_bfloat16* lo,
                     float eps) {
     if (rows_ok(n, X, ldx) && al16(g) && al16(c) && al8(hi) && al8(lo))
-        return cuda_check(launch_rows(row_nv(n), pdl,
-                                      dim3((unsigned)((rows + kRowsPerCta - 1) / kRowsPerCta)), st,
-                                      SN_ROWS_KERNELS(ln_split_rows_kernel), rows, n, X, ldx, g, c,
-                                      hi, lo, eps),
+        return cuda_check(launch_pdl_if(pdl, ln_split_vec_kernel, dim3((unsigned)rows),
+                                        dim3(row_threads(n)), 0, st, n, X, ldx, g, c, hi, lo, eps),
                           "ln_split launch");
     return cuda_check(launch_pdl_if(pdl, ln_split_kernel, dim3((unsigned)rows), dim3(256), 0, st,
                                     n, X, ldx, g, c, hi, lo, eps),

@@ -277,10 +277,13 @@ void core_fwd_f32(const float* q, const float* delta, const float* s0, float* st
     if (ensure_init() != SN_OK) return;
     std::lock_guard<std::recursive_mutex> lk(rt().mu);
     const size_t bq = (size_t)B * T * 2 * D * 4, bo = (size_t)B * T * D * 4;
+    // with a partial group the untouched channels of host outputs keep the
+    // caller's values: stage those outputs in as well as out
+    auto out = D % 8 ? stage_inout : stage_out;
     Arr Q, DL, S0, ST, UO, PO;
     if (stage_in(q, bq, 0, &Q) || stage_in(delta, (size_t)D * 4, 1, &DL) ||
-        stage_in(s0, (size_t)B * D * 4, 2, &S0) || stage_out(states, bo, 3, &ST) ||
-        stage_out(uo, bo, 4, &UO) || stage_out(po, bo, 5, &PO))
+        stage_in(s0, (size_t)B * D * 4, 2, &S0) || out(states, bo, 3, &ST) ||
+        out(uo, bo, 4, &UO) || out(po, bo, 5, &PO))
         return;
     const int DV = D & ~7;
     if (DV > 0) {
@@ -309,8 +312,9 @@ void core_bwd_f32(const float* q, const float* delta, const float* s0, const flo
     if (stage_in(q, bq, 0, &Q) || stage_in(delta, (size_t)D * 4, 1, &DL) ||
         stage_in(s0, (size_t)B * D * 4, 2, &S0) || stage_in(states, bo, 3, &ST) ||
         stage_in(uo, bo, 4, &UO) || stage_in(po, bo, 5, &PO) || stage_in(dstate, bo, 6, &DS) ||
-        stage_in(du_in, bo, 7, &DU) || stage_out(dq, bq, 8, &DQ) ||
-        stage_inout(ddelta, (size_t)D * 4, 9, &DD) || stage_out(ds0, (size_t)B * D * 4, 10, &D0))
+        stage_in(du_in, bo, 7, &DU) || (D % 8 ? stage_inout : stage_out)(dq, bq, 8, &DQ) ||
+        stage_inout(ddelta, (size_t)D * 4, 9, &DD) ||
+        (D % 8 ? stage_inout : stage_out)(ds0, (size_t)B * D * 4, 10, &D0))
         return;
     const int DV = D & ~7;
     if (DV > 0) {
@@ -335,9 +339,10 @@ void step_core_f32(const float* q, const float* delta, const float* s, float* s_
     if (ensure_init() != SN_OK) return;
     std::lock_guard<std::recursive_mutex> lk(rt().mu);
     const size_t bs = (size_t)B * D * 4;
+    auto out = D % 8 ? stage_inout : stage_out;  // keep untouched channels of host outputs
     Arr Q, DL, S, SN_, UO;
     if (stage_in(q, 2 * bs, 0, &Q) || stage_in(delta, (size_t)D * 4, 1, &DL) ||
-        stage_in(s, bs, 2, &S) || stage_out(s_new, bs, 3, &SN_) || stage_out(uo, bs, 4, &UO))
+        stage_in(s, bs, 2, &S) || out(s_new, bs, 3, &SN_) || out(uo, bs, 4, &UO))
         return;
     const int DV = D & ~7;
     if (DV > 0) {

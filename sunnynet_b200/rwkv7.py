@@ -44,6 +44,23 @@ class Rwkv7Batch:
         check(self._lib.sn_abi_rwkv7_step_argmax(self._h, ptr(t), B, ptr(out)), "rwkv7_argmax")
         return out
 
+    def prefill(self, tokens, logits=None, want_logits: bool = True):
+        """tokens (B, T) -> logits (B, vocab) of each sequence's last token:
+        every layer over all prompt rows at once, the recurrence in order."""
+        if hasattr(tokens, "data_ptr"):
+            import torch
+            t = tokens.to(torch.int32).contiguous()
+        else:
+            t = np.ascontiguousarray(np.asarray(tokens, np.int32))
+        B, T = t.shape
+        if want_logits and logits is None:
+            logits = _out_like(t, (B, self.vocab), np.float32)
+        bind_stream(t, logits)
+        check(self._lib.sn_abi_rwkv7_prefill_batch(self._h, ptr(t), B, T,
+                                                   ptr(logits) if want_logits else None),
+              "rwkv7_prefill")
+        return logits
+
     def step_trace(self, tokens):
         """One step that also returns the residual stream entering each layer
         and leaving the last: (logits (B, vocab), xs (B, L+1, D)), host arrays."""
