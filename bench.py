@@ -203,6 +203,17 @@ def timed_steps(torch, dist, step, K: int, W: int, flush=None):
     return dist.max(torch, ms)
 
 
+def keep_busy(torch, step, seconds: float = 1.5, inner: int = 20):
+    """Run the same step for `seconds` more (untimed) so the clock sampler,
+    which polls every 200 ms, sees the GPU under this load even when the K
+    timed steps take only a few milliseconds."""
+    t_end = time.time() + seconds
+    while time.time() < t_end:
+        for _ in range(inner):
+            step()
+        torch.cuda.synchronize()
+
+
 # ---------------------------------------------------------------- workloads
 def wl_c1(args, torch, dist, ours: bool):
     """Gated scan, BASELINE config 1. One step = one scan of B*T*C elements.
@@ -242,12 +253,7 @@ def wl_c1(args, torch, dist, ours: bool):
     lib.sn_abi_cuda_scan_mode(1)
     with ClockSampler(dist.local) as clk:
         ms = timed_steps(torch, dist, step, args.steps, args.warmup, flush=flushbuf.zero_)
-        # keep the clock sampler busy on a longer loop of the same step
-        t_end = time.time() + 1.5
-        while time.time() < t_end:
-            for _ in range(200):
-                step()
-            torch.cuda.synchronize()
+        keep_busy(torch, step, inner=200)
     # per-kernel device time of the mode-1 scan (CUDA events around each kernel)
     check(lib.sn_abi_cuda_profile(1))
     for _ in range(5):
@@ -431,11 +437,7 @@ def wl_sunny(args, torch, dist, ours, preset, B_total, quant, prefill_T, split):
                         "note": "--ncu run: launch list only, no other measurements"})
             m.close()
             return res, None
-        t_end = time.time() + 1.5
-        while time.time() < t_end:
-            for _ in range(20):
-                step()
-            torch.cuda.synchronize()
+        keep_busy(torch, step)
     # host-side collection of every rank's greedy tokens (a checksum per rank)
     toks = cur.to(torch.int64)
     res["tokens_per_rank"] = [int(v[0]) for v in dist.gather(torch, [int(toks.numel())])]
@@ -652,6 +654,7 @@ def wl_c5(args, torch, dist, ours):
 
     with ClockSampler(dist.local) as clk:
         ms = timed_steps(torch, dist, step, args.steps, args.warmup)
+        keep_busy(torch, step, inner=4)
     check(lib.sn_abi_cuda_profile(1))  # serialised family timing, scaled below
     for _ in range(2):
         step()
@@ -810,6 +813,7 @@ def wl_rwkv(args, torch, dist, ours, B):
     flush = flushbuf.zero_ if step_bytes < 2 * (126 << 20) else None
     with ClockSampler(dist.local) as clk:
         ms = timed_steps(torch, dist, step, args.steps, args.warmup, flush=flush)
+        keep_busy(torch, step)
     check(lib.sn_abi_cuda_profile(1))  # serialised family timing, scaled below
     for _ in range(3):
         if flush:
