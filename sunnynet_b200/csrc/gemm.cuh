@@ -61,6 +61,10 @@ struct GemmArgs {
     // (ld = ldc), the input format of a following tensor-core contraction
     void* Ch = nullptr;
     void* Cl = nullptr;
+    // tensor-core path only: > 0 keeps the grid within this many CTAs where a
+    // tile width allows it (a contraction that runs beside another stream's
+    // kernels leaves them the rest of the SMs)
+    int max_ctas = 0;
 };
 
 struct TcWeights;

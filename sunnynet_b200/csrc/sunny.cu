@@ -1086,7 +1086,17 @@ int load_model(SunnyModel* m, const char* path, int nseq, bool half, const int* 
             SN_TRY(tc_act_view(&m->p_sl[l], m->p_s, (long long)l * D, nseq, (long long)L * D, D));
         m->sfb_all = m->dalloc<float>(n * L * D);
         if (!m->sfb_all) return fail(SN_E_NOMEM, "device allocation failed");
-        SN_TRY(cuda_check(cudaStreamCreateWithFlags(&m->side, cudaStreamNonBlocking), "stream"));
+        // the feedback contractions' side stream at the lowest priority, the
+        // captured layer chain at the highest: where both have CTAs waiting,
+        // the chain's go first
+        int lo = 0, hi = 0;
+        SN_TRY(cuda_check(cudaDeviceGetStreamPriorityRange(&lo, &hi), "priorities"));
+        SN_TRY(cuda_check(cudaStreamCreateWithPriority(&m->side, cudaStreamNonBlocking, lo),
+                          "stream"));
+        SN_TRY(cuda_check(cudaStreamDestroy(m->cap), "stream"));
+        m->cap = nullptr;
+        SN_TRY(cuda_check(cudaStreamCreateWithPriority(&m->cap, cudaStreamNonBlocking, hi),
+                          "stream"));
         SN_TRY(cuda_check(cudaEventCreateWithFlags(&m->ev_fork, cudaEventDisableTiming), "event"));
         SN_TRY(cuda_check(cudaEventCreateWithFlags(&m->ev_split, cudaEventDisableTiming), "event"));
         m->ev_ws.assign(L, nullptr);
@@ -1259,6 +1269,8 @@ int enqueue_step_tc(SunnyModel* m, int B, bool with_head, cudaStream_t st, cudaS
         const SunnyLayer& y = m->ly[l];
         GemmArgs gs = gemm(B, D, D, m->s + (size_t)l * D, y.Ws, y.sWs, m->sfb_all + l * n * D);
         gs.lda = (long long)L * D;
+        // a sixth of the SMs: the layer chain's contractions keep the rest
+        gs.max_ctas = rt().num_sms / 6;
         {
             ProfScope ps("gemm_Ws", side);
             SN_TRY(launch_tc_gemm_act(gs, y.tWs, m->p_sl[l], side));

@@ -14,11 +14,12 @@
 //             frees the stage / signals the accumulator
 //     warps 2.. epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes of
 //             quarter w%4), each thread finishing its own output row (wide
-//             tiles: four warp groups share the 32-column blocks): rows
-//             staged in the drained ring (residual operands fetched there by
-//             bulk copies) and stored by one bulk copy per row; unaligned
-//             shapes stage 32x32 blocks so each global access is one 128-byte
-//             row segment; same arithmetic as gemm_epilogue
+//             tiles: four warp groups share the 32-column blocks) in a staged
+//             tile (residual operands loaded into it under the main loop),
+//             which all epilogue threads then store with coalesced 16-byte
+//             stores; unaligned shapes stage 32x32 blocks so each global
+//             access is one 128-byte row segment; same arithmetic as
+//             gemm_epilogue
 // Every mbarrier wait is bounded; a role that gives up records the error,
 // drains its own in-flight TMA/MMA work, and the CTA frees its TMEM.
 #include <cuda.h>
@@ -51,18 +52,29 @@ struct TcEpi {
     static constexpr int THREADS = 64 + 128 * GROUPS;
 };
 
-template <int BN, bool I8>
+// Residual / accumulate tiles of 64 or 128 columns stage their whole operand
+// tile under the main loop ([BM][BN + 4] fp32 next to the ring).
+template <int BN, bool LOADS>
+struct TcStage {
+    static constexpr bool ON = LOADS && BN > 32 && BN <= 128;
+};
+
+template <int BN, bool I8, bool LOADS = false>
 struct TcCfg {
     static constexpr int A_BYTES = BM * 128;
     static constexpr int W_BYTES = BN * 128;
     // a stage: the A hi / lo slabs and the weight hi (and, bf16 weights, lo) slab
     static constexpr int STAGE = 2 * A_BYTES + (I8 ? 1 : 2) * W_BYTES;
     // epilogue operands loaded under the main loop: [4 warps][32][33] floats
-    static constexpr int PRE = 4 * 32 * 33 * 4;
+    // (32x32 blocks), or the staged operand tile
+    static constexpr int PRE_BLOCKS = 4 * 32 * 33 * 4;
+    static constexpr int PRE_TILE = TcStage<BN, LOADS>::ON ? BM * (BN + 4) * 4 : 0;
+    static constexpr int PRE = PRE_TILE > PRE_BLOCKS ? PRE_TILE : PRE_BLOCKS;
     // as many stages as fit the 227 KB of shared memory next to the operand
     // area, 1 KB of alignment slack, 256 B of barriers and BN column scales
     static constexpr int S_FIT = (227 * 1024 - PRE - 1024 - 256 - BN * 4) / STAGE;
     static constexpr int S = S_FIT > 6 ? 6 : S_FIT;
+    static_assert(S >= 2, "two ring stages at least");
     // after the 256 bytes of barriers: the tile's per-column weight scales
     static constexpr int SMEM = S * STAGE + PRE + 1024 + 256 + BN * 4;
 };
@@ -206,6 +218,86 @@ __device__ __forceinline__ bool tc_rows_aligned(const GemmArgs& a) {
     return a.epi == kEpiResid ? al(a.S, a.lds) && al(a.F, a.ldf) && al(a.X, a.ldx) : al(a.C, a.ldc);
 }
 
+// The operand tile of a residual (p*S + F + X) or accumulate (C) epilogue:
+// rows [0, nr) x columns [0, nc) of the tile at (m0, n0) into `ra` as
+// [BM][BN + 4] fp32, run under the main loop. 16-byte loads spread over all
+// nt epilogue threads (consecutive threads on consecutive 16 bytes of a row),
+// four per thread in flight before their shared-memory stores. Same
+// arithmetic as tc_operand; nc % 4 == 0 and 16-byte aligned rows.
+template <int BN>
+__device__ __forceinline__ void tc_stage_operands(const GemmArgs& a, int m0, int n0, int nr,
+                                                  int nc, float* ra, int et, int nt) {
+    constexpr int RS = BN + 4, U = 4;
+    const int c4 = nc >> 2, total = nr * c4;
+    const bool resid = a.epi == kEpiResid;
+#pragma unroll 1
+    for (int i0 = et; i0 < total; i0 += U * nt) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = i0 + u * nt;
+            v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (i < total) {
+                const int r = nc == BN ? i / (BN / 4) : i / c4;
+                const long long mm = m0 + r;
+                const int n = n0 + ((i - r * c4) << 2);
+                if (resid) {
+                    const float4 sv = *reinterpret_cast<const float4*>(a.S + mm * a.lds + n);
+                    const float4 fv = *reinterpret_cast<const float4*>(a.F + mm * a.ldf + n);
+                    const float4 xv = *reinterpret_cast<const float4*>(a.X + mm * a.ldx + n);
+                    v[u] = make_float4(a.p * sv.x + fv.x + xv.x, a.p * sv.y + fv.y + xv.y,
+                                       a.p * sv.z + fv.z + xv.z, a.p * sv.w + fv.w + xv.w);
+                } else {
+                    v[u] = *reinterpret_cast<const float4*>(a.C + mm * a.ldc + n);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = i0 + u * nt;
+            if (i < total) {
+                const int r = nc == BN ? i / (BN / 4) : i / c4;
+                *reinterpret_cast<float4*>(ra + r * RS + ((i - r * c4) << 2)) = v[u];
+            }
+        }
+    }
+}
+
+// Rows [0, nr) x columns [0, nc) of a finished tile, staged in shared memory
+// as [BM][BN + 4] fp32 at `src`, to C[m0 + r][n0 + c]: 16-byte stores over
+// all nt epilogue threads, consecutive threads on consecutive 16 bytes of a
+// row (nc % 4 == 0, C rows 16-byte aligned).
+template <int BN>
+__device__ __forceinline__ void tc_store_tile(float* C, long long ldc, int m0, int n0, int nr,
+                                              int nc, const float* src, int et, int nt) {
+    constexpr int RS = BN + 4;
+    const int c4 = nc >> 2, total = nr * c4;
+#pragma unroll 4
+    for (int i = et; i < total; i += nt) {
+        const int r = nc == BN ? i / (BN / 4) : i / c4;
+        const int c = (i - r * c4) << 2;
+        *reinterpret_cast<float4*>(C + (long long)(m0 + r) * ldc + n0 + c) =
+            *reinterpret_cast<const float4*>(src + r * RS + c);
+    }
+}
+
+// The same for one bf16 plane of the result, staged as [BM][BN + 8] at `src`:
+// 16-byte stores of 8 elements (nc % 8 == 0, plane rows 16-byte aligned).
+template <int BN>
+__device__ __forceinline__ void tc_store_plane(__nv_bfloat16* P, long long ldc, int m0, int n0,
+                                               int nr, int nc, const __nv_bfloat16* src, int et,
+                                               int nt) {
+    constexpr int RSH = BN + 8;
+    const int c8 = nc >> 3, total = nr * c8;
+#pragma unroll 4
+    for (int i = et; i < total; i += nt) {
+        const int r = nc == BN ? i / (BN / 8) : i / c8;
+        const int c = (i - r * c8) << 3;
+        *reinterpret_cast<uint4*>(P + (long long)(m0 + r) * ldc + n0 + c) =
+            *reinterpret_cast<const uint4*>(src + r * RSH + c);
+    }
+}
+
 // Thread-per-row epilogue of the accumulator-only kinds, one 32-column
 // block: v = 32 accumulator columns of this thread's row (as tcgen05.ld
 // hands them), ws = their weight scales (shared memory), the result into the
@@ -334,7 +426,7 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
                    const __grid_constant__ CUtensorMap twh, const __grid_constant__ CUtensorMap twl,
                    GemmArgs a, int* err) {
-    using C = TcCfg<BN, I8>;
+    using C = TcCfg<BN, I8, LOADS>;
     constexpr int S = C::S;
     constexpr int kEpiGroups = TcEpi<BN>::GROUPS;
     // TMEM is allocated in powers of two columns (a 192-wide tile takes 256)
@@ -348,8 +440,6 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
     uint64_t* acc_full = empty + S;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(acc_full + 1);
     volatile int* give_up = reinterpret_cast<volatile int*>(acc_full + 2);
-    uint64_t* op_full = acc_full + 3;  // [4]: a warp's epilogue operands landed
-    uint64_t* row_done = op_full + 4;  // [4]: the other groups' columns of a quarter's rows
     float* wsc = reinterpret_cast<float*>(sb + S * C::STAGE + C::PRE + 256);  // [BN]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -371,10 +461,6 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
             mbar_init(&empty[s], 1);
         }
         mbar_init(acc_full, 1);
-        for (int q = 0; q < 4; ++q) {
-            mbar_init(&op_full[q], 1);
-            if (kEpiGroups > 1) mbar_init(&row_done[q], 32 * (kEpiGroups - 1));
-        }
         *give_up = 0;
         fence_mbar_init();
     }
@@ -491,22 +577,20 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
             // this warp's operands of a 32x32 block, [row][33] in shared memory
             // (group 0)
             float* pre_w = pre_all + ((warp - 2) & 3) * (32 * 33);
-            // Wide residual / accumulate tiles whose operand rows fit the drained
-            // ring (plus the operand area after it) go through it whole: rows
-            // [array][row][BN + 4] floats, fetched by bulk copies once the last
-            // MMA has completed; each thread then finishes its own row (the 32
-            // accumulator columns tcgen05.ld hands it) with conflict-free float4
-            // accesses and stores the row back by one bulk copy.
+            // Wide residual / accumulate tiles with 16-byte aligned rows stage
+            // their operand tile (p*S + F + X, or C) in its own area `ra` under
+            // the main loop, 16-byte loads spread over every epilogue thread;
+            // each thread then finishes its own row in place (the 32
+            // accumulator columns tcgen05.ld hands it, conflict-free float4
+            // accesses) and all of them store the tile with coalesced 16-byte
+            // stores. Wide accumulator-only tiles do the same with their rows
+            // staged in the drained ring (and the bf16 planes after them).
             constexpr int RS = BN + 4;  // padded row stride: 16-byte bank groups differ per row
-            constexpr bool kRing = LOADS && BN > 32 && 3 * BM * RS * 4 <= S * C::STAGE + C::PRE;
+            constexpr bool kStage = TcStage<BN, LOADS>::ON;
+            constexpr int kEt = 128 * kEpiGroups;  // epilogue threads
             const bool out_al = (reinterpret_cast<uintptr_t>(a.C) & 15) == 0 && (a.ldc & 3) == 0 &&
                                 (a.N & 3) == 0;
-            const bool ring = kRing && tc_rows_aligned(a) && a.Ch == nullptr && out_al;
-            // Other wide tiles finish rows the same way when their results can
-            // leave by bulk copies: fp32 rows [128][RS] at the ring start, the
-            // bf16 planes' rows [2][128][RSH] after them. 32-column tiles keep
-            // the staged blocks: rows of 128 bytes (64 for a plane) are too short
-            // for one bulk copy each to beat coalesced warp stores.
+            const bool staged = kStage && tc_rows_aligned(a) && a.Ch == nullptr && out_al;
             constexpr int RSH = BN + 8;
             constexpr bool kPlanesFit = BM * RS * 4 + 2 * BM * RSH * 2 <= S * C::STAGE;
             const bool planes_al = a.Ch != nullptr && kPlanesFit &&
@@ -514,87 +598,46 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
                                    (reinterpret_cast<uintptr_t>(a.Cl) & 15) == 0 &&
                                    (a.ldc & 7) == 0 && (a.N & 7) == 0;
             const bool rows = !LOADS && BN > 32 && out_al && (a.Ch == nullptr || planes_al);
+            const int nc = a.N - n0 < BN ? a.N - n0 : BN;  // this tile's columns
+            const int nr = a.M - m0 < BM ? a.M - m0 : BM;  // and rows inside the matrix
+            float* ra = pre_all;  // [BM][RS]: the staged operand tile, then the results
             if (LOADS && BN == 32 && g == 0)  // the only block's operands, under the main loop
                 tc_block_operands(a, m0 + q * 32, n0 + lane, pre_w, lane);
-            if (LOADS && BN > 32 && g == 0)  // the other blocks' operands into L2 meanwhile
-                tc_prefetch_row<BN>(a, m0 + et, n0, ring);
-            if (a.wscale) {  // the tile's column scales, read from shared memory below
-                for (int c = et; c < BN; c += 128 * kEpiGroups)
-                    wsc[c] = n0 + c < a.N ? a.wscale[n0 + c] : 1.0f;
-                named_bar_sync(1, 128 * kEpiGroups);  // every epilogue warp
-            }
+            if (kStage && !staged && g == 0)  // the other blocks' operands into L2 meanwhile
+                tc_prefetch_row<BN>(a, m0 + et, n0, false);
+            if (staged) tc_stage_operands<BN>(a, m0, n0, nr, nc, ra, et, kEt);
+            if (a.wscale)  // the tile's column scales, read from shared memory below
+                for (int c = et; c < BN; c += kEt) wsc[c] = n0 + c < a.N ? a.wscale[n0 + c] : 1.0f;
+            named_bar_sync(1, kEt);  // every epilogue warp: ra and wsc complete
             bool ok = mbar_wait(acc_full, 0, err);
             tc_fence_after();
             const int row = q * 32 + lane;  // TMEM lane = tile row of this thread
-            const long long mm = m0 + row;
-            const int nc = a.N - n0 < BN ? a.N - n0 : BN;
-            float* orow = reinterpret_cast<float*>(sb) + row * RS;
-            // Rows are finished by all groups, one 32-column block in kEpiGroups
-            // each; group 0 then stores them once every group has arrived on
-            // the quarter's row_done barrier (after its proxy fence).
-            auto rows_finished = [&]() -> bool {
-                fence_proxy_async_smem();
-                if (kEpiGroups == 1) return true;
-                if (g > 0) {
-                    mbar_arrive(&row_done[q]);
-                    return false;
-                }
-                return mbar_wait(&row_done[q], 0, err);
-            };
-            if (kRing && ring) {
+            if (staged) {
                 const bool resid = a.epi == kEpiResid;
-                if (g == 0 && ok && !*give_up) {
-                    // every MMA has completed, so no stage of the ring is still read
-                    const int left = a.M - (m0 + q * 32);  // this warp's rows inside the matrix
-                    const int nr = left < 0 ? 0 : (left < 32 ? left : 32);
-                    if (lane == 0)
-                        mbar_expect_tx(&op_full[q], (uint32_t)(nr * nc * 4 * (resid ? 3 : 1)));
-                    __syncwarp();
-                    if (mm < a.M) {
-                        if (resid) {
-                            bulk_g2s(orow, a.S + mm * a.lds + n0, nc * 4, &op_full[q]);
-                            bulk_g2s(orow + BM * RS, a.F + mm * a.ldf + n0, nc * 4, &op_full[q]);
-                            bulk_g2s(orow + 2 * BM * RS, a.X + mm * a.ldx + n0, nc * 4, &op_full[q]);
-                        } else {
-                            bulk_g2s(orow, a.C + mm * a.ldc + n0, nc * 4, &op_full[q]);
-                        }
-                    }
-                }
-                if (ok && !*give_up) ok = mbar_wait(&op_full[q], 0, err);
-                if (ok && !*give_up) {
+                float* orow = ra + row * RS;
 #pragma unroll 1
-                    for (int j0 = g * 32; j0 < BN; j0 += 32 * kEpiGroups) {
-                        float v[32];
-                        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)j0, v);
+                for (int j0 = g * 32; ok && !*give_up && j0 < BN; j0 += 32 * kEpiGroups) {
+                    float v[32];
+                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)j0, v);
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4* o = reinterpret_cast<float4*>(orow + j0 + j);
-                            const float4 s4 = o[0];
-                            float y[4] = {v[j], v[j + 1], v[j + 2], v[j + 3]};
-                            float sv[4] = {s4.x, s4.y, s4.z, s4.w};
-                            float fv[4] = {0.0f, 0.0f, 0.0f, 0.0f}, xv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                            if (resid) {
-                                const float4 f4 = o[BM * RS / 4], x4 = o[2 * BM * RS / 4];
-                                fv[0] = f4.x, fv[1] = f4.y, fv[2] = f4.z, fv[3] = f4.w;
-                                xv[0] = x4.x, xv[1] = x4.y, xv[2] = x4.z, xv[3] = x4.w;
-                            }
+                    for (int j = 0; j < 32; j += 4) {
+                        float4* o = reinterpret_cast<float4*>(orow + j0 + j);
+                        const float4 r4 = o[0];
+                        float y[4] = {v[j], v[j + 1], v[j + 2], v[j + 3]};
+                        const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                if (a.wscale) y[i] = y[i] * wsc[j0 + j + i];
-                                // same arithmetic as tc_operand and the staged path
-                                if (resid) y[i] = y[i] + (a.p * sv[i] + fv[i] + xv[i]);
-                                else y[i] = sv[i] + y[i];
-                            }
-                            o[0] = make_float4(y[0], y[1], y[2], y[3]);
+                        for (int i = 0; i < 4; ++i) {
+                            if (a.wscale) y[i] = y[i] * wsc[j0 + j + i];
+                            // same arithmetic as tc_operand and the staged block path
+                            y[i] = resid ? y[i] + rv[i] : rv[i] + y[i];
                         }
+                        o[0] = make_float4(y[0], y[1], y[2], y[3]);
                     }
                 }
-                if (rows_finished() && ok && !*give_up && mm < a.M) {
-                    bulk_s2g(a.C + mm * a.ldc + n0, orow, nc * 4);  // the finished row
-                    bulk_commit();
-                    bulk_wait_read_all();  // the ring stays valid until read
-                }
+                named_bar_sync(1, kEt);  // every row finished
+                if (ok && !*give_up) tc_store_tile<BN>(a.C, a.ldc, m0, n0, nr, nc, ra, et, kEt);
             } else if (rows) {
+                float* orow = reinterpret_cast<float*>(sb) + row * RS;
                 __nv_bfloat16* hrow =
                     a.Ch ? reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<float*>(sb) + BM * RS) +
                                row * RSH
@@ -615,14 +658,17 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
                         default: tc_row_block<kEpiNone>(a, v, wsc + j0, out, h, l);
                     }
                 }
-                if (rows_finished() && ok && !*give_up && mm < a.M) {  // the finished row
-                    bulk_s2g(a.C + mm * a.ldc + n0, orow, nc * 4);
+                named_bar_sync(1, kEt);  // every row finished
+                if (ok && !*give_up) {
+                    tc_store_tile<BN>(a.C, a.ldc, m0, n0, nr, nc, reinterpret_cast<float*>(sb), et, kEt);
                     if (a.Ch) {
-                        bulk_s2g(reinterpret_cast<__nv_bfloat16*>(a.Ch) + mm * a.ldc + n0, hrow, nc * 2);
-                        bulk_s2g(reinterpret_cast<__nv_bfloat16*>(a.Cl) + mm * a.ldc + n0, lrow, nc * 2);
+                        const __nv_bfloat16* hs =
+                            reinterpret_cast<const __nv_bfloat16*>(reinterpret_cast<float*>(sb) + BM * RS);
+                        tc_store_plane<BN>(reinterpret_cast<__nv_bfloat16*>(a.Ch), a.ldc, m0, n0, nr, nc, hs,
+                                           et, kEt);
+                        tc_store_plane<BN>(reinterpret_cast<__nv_bfloat16*>(a.Cl), a.ldc, m0, n0, nr, nc,
+                                           hs + BM * RSH, et, kEt);
                     }
-                    bulk_commit();
-                    bulk_wait_read_all();  // the ring stays valid until read
                 }
             } else if (g == 0 && ok && !*give_up) {
                 // 32x32 blocks go through shared memory (the drained ring) so that a
@@ -761,7 +807,7 @@ std::map<int, ActPlanes>& act_cache() {
 template <int BN, bool I8, bool LOADS>
 int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
               const CUtensorMap& tal, cudaStream_t st, bool pdl, int ks) {
-    using C = TcCfg<BN, I8>;
+    using C = TcCfg<BN, I8, LOADS>;
     static bool attr = false;
     auto k = tc_gemm_kernel<BN, I8, LOADS>;
     if (!attr) {
@@ -878,11 +924,11 @@ namespace {
 
 // Tile width BN and K split ks from a cost model of this kernel, per CTA in
 // SM cycles (measured on B200 decode and prefill shapes): ~2400 to the first
-// K slab, then the slab bytes at ~45 B/cycle (the TMA rate of one SM:
-// 2 x 128 x 128 B of A planes + 128 B per weight row and plane), ~900 per 32
-// output columns of epilogue, ~4000 for a split's cluster reduction; times
-// the number of waves. Split K needs a 16-byte-friendly epilogue, BN <= 64
-// and >= 8 K slabs (two per CTA at least).
+// K slab, then the slab bytes at ~45 B/cycle (2 x 128 x 128 B of A planes +
+// 128 B per weight row and plane), ~900 per 32 output columns of epilogue,
+// ~4000 for a split's cluster reduction; times the number of waves. Split K
+// needs a 16-byte-friendly epilogue, BN <= 64 and >= 8 K slabs (two per CTA
+// at least).
 int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
                  const CUtensorMap& tal, cudaStream_t st, bool pdl) {
     const long long mt = (a.M + BM - 1) / BM;
@@ -896,33 +942,32 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
     if (a.epi == kEpiResid) vec = vec && al16(a.S, a.lds) && al16(a.F, a.ldf) && al16(a.X, a.ldx);
     const bool may_split = vec && nkt >= 8 && !getenv("SN_TC_NO_SPLITK");
     const bool ld = a.epi == kEpiResid || a.epi == kEpiAdd;
-    // residual / accumulate tiles of 64 or 128 columns fetch their operand
-    // rows into the drained ring by bulk copies (all of a tile's at once,
-    // ~48 B/cycle) when rows are 16-byte aligned and no bf16 planes are
-    // written; otherwise wide tiles load them block by block after the main
-    // loop, which the model does not see: those keep BN = 32 unless that
-    // leaves most SMs idle
-    const bool ring = ld && vec && a.Ch == nullptr;
-    const int narr = a.epi == kEpiResid ? 3 : 1;
+    // residual / accumulate tiles of 64 or 128 columns stage their operand
+    // tile under the main loop when rows are 16-byte aligned and no bf16
+    // planes are written; otherwise wide tiles load them block by block after
+    // the main loop, which the model does not see: those keep BN = 32 unless
+    // that leaves most SMs idle
+    const bool staged = ld && vec && a.Ch == nullptr;
     const int bld = mt * ((a.N + 255) / 256) >= sms * 3 / 4   ? 256
                     : mt * ((a.N + 127) / 128) >= sms * 3 / 4 ? 128
                     : mt * ((a.N + 63) / 64) >= sms * 3 / 4   ? 64
                                                               : 32;
     int bn = 32, ks = 1;
     double best = 1e300;
+    for (int pass = a.max_ctas > 0 ? 0 : 1; pass < 2 && best == 1e300; ++pass)
     for (int b : {32, 64, 128, 192, 256}) {
-        if (ld && (ring ? b > 128 : b != bld)) continue;
+        if (ld && (staged ? b > 128 : b != bld)) continue;
         // 192-wide tiles: two ring stages, and neither residual operands nor
         // the bf16 planes of the result fit the drained ring for their epilogue
         if (b == 192 && (ld || a.Ch != nullptr || tw.int8)) continue;
         const long long tiles = mt * ((a.N + b - 1) / b);
         const double slab = 2.0 * BM * 128 + (tw.int8 ? 1.0 : 2.0) * b * 128;
-        const double fetch = ring && b > 32 ? narr * BM * b * 4.0 / 48.0 : 0.0;
         for (int k = 1; k <= 8; k *= 2) {
             if (k > 1 && (!may_split || b > 64 || nkt < 2 * k || tiles * k > sms)) continue;
+            if (pass == 0 && tiles * k > a.max_ctas) continue;  // within the CTA cap first
             const long long waves = (tiles * k + sms - 1) / sms;
             const double t = (double)waves * (2400.0 + ((nkt + k - 1) / k) * slab / 45.0 +
-                                              900.0 * b / 32 + (k > 1 ? 4000.0 : fetch));
+                                              900.0 * b / 32 + (k > 1 ? 4000.0 : 0.0));
             if (t < best * 0.98) {  // a wider or more split choice must win clearly
                 best = t;
                 bn = b;
@@ -935,7 +980,7 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
     if (const char* fb = getenv("SN_TC_FORCE_BN")) {
         const int b = atoi(fb);
         const bool ok = (b == 32 || b == 64 || b == 128 || b == 192 || b == 256) &&
-                        (!ld || (ring ? b <= 128 : b == bld)) &&
+                        (!ld || (staged ? b <= 128 : b == bld)) &&
                         !(b == 192 && (ld || a.Ch != nullptr || tw.int8));
         if (ok) {
             bn = b;
