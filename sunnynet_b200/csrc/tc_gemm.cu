@@ -53,7 +53,8 @@ struct TcEpi {
 };
 
 // Residual / accumulate tiles of 64 or 128 columns stage their whole operand
-// tile under the main loop ([BM][BN + 4] fp32 next to the ring).
+// tile ([BM][BN + 4] fp32): under the main loop, next to the ring, where that
+// leaves the ring three stages at least; else in the drained ring after it.
 template <int BN, bool LOADS>
 struct TcStage {
     static constexpr bool ON = LOADS && BN > 32 && BN <= 128;
@@ -68,13 +69,21 @@ struct TcCfg {
     // epilogue operands loaded under the main loop: [4 warps][32][33] floats
     // (32x32 blocks), or the staged operand tile
     static constexpr int PRE_BLOCKS = 4 * 32 * 33 * 4;
-    static constexpr int PRE_TILE = TcStage<BN, LOADS>::ON ? BM * (BN + 4) * 4 : 0;
-    static constexpr int PRE = PRE_TILE > PRE_BLOCKS ? PRE_TILE : PRE_BLOCKS;
+    static constexpr int TILE = BM * (BN + 4) * 4;
+    static constexpr int FIXED = 1024 + 256 + BN * 4;  // alignment slack, barriers, scales
+    static constexpr bool EARLY =
+        TcStage<BN, LOADS>::ON &&
+        (227 * 1024 - (TILE > PRE_BLOCKS ? TILE : PRE_BLOCKS) - FIXED) / STAGE >= 3;
+    static constexpr int PRE = EARLY && TILE > PRE_BLOCKS ? TILE : PRE_BLOCKS;
     // as many stages as fit the 227 KB of shared memory next to the operand
     // area, 1 KB of alignment slack, 256 B of barriers and BN column scales
-    static constexpr int S_FIT = (227 * 1024 - PRE - 1024 - 256 - BN * 4) / STAGE;
+    static constexpr int S_FIT = (227 * 1024 - PRE - FIXED) / STAGE;
     static constexpr int S = S_FIT > 6 ? 6 : S_FIT;
     static_assert(S >= 2, "two ring stages at least");
+    // late staging fetches the S, F and X rows into the drained ring and the
+    // operand area that follows it
+    static_assert(EARLY || !TcStage<BN, LOADS>::ON || 3 * TILE <= S * STAGE + PRE,
+                  "late-staged operand rows fit");
     // after the 256 bytes of barriers: the tile's per-column weight scales
     static constexpr int SMEM = S * STAGE + PRE + 1024 + 256 + BN * 4;
 };
@@ -440,6 +449,7 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
     uint64_t* acc_full = empty + S;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(acc_full + 1);
     volatile int* give_up = reinterpret_cast<volatile int*>(acc_full + 2);
+    uint64_t* op_full = acc_full + 3;  // [4]: a quarter's operand rows landed (late staging)
     float* wsc = reinterpret_cast<float*>(sb + S * C::STAGE + C::PRE + 256);  // [BN]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -461,6 +471,7 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
             mbar_init(&empty[s], 1);
         }
         mbar_init(acc_full, 1);
+        for (int q = 0; q < 4; ++q) mbar_init(&op_full[q], 1);
         *give_up = 0;
         fence_mbar_init();
     }
@@ -600,20 +611,76 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
             const bool rows = !LOADS && BN > 32 && out_al && (a.Ch == nullptr || planes_al);
             const int nc = a.N - n0 < BN ? a.N - n0 : BN;  // this tile's columns
             const int nr = a.M - m0 < BM ? a.M - m0 : BM;  // and rows inside the matrix
-            float* ra = pre_all;  // [BM][RS]: the staged operand tile, then the results
+            // [BM][RS]: the staged operand tile, then the results (late
+            // staging: in the drained ring, loaded once the accumulator is ready)
+            constexpr bool kEarly = C::EARLY;
+            float* ra = kEarly ? pre_all : reinterpret_cast<float*>(sb);
             if (LOADS && BN == 32 && g == 0)  // the only block's operands, under the main loop
                 tc_block_operands(a, m0 + q * 32, n0 + lane, pre_w, lane);
-            if (kStage && !staged && g == 0)  // the other blocks' operands into L2 meanwhile
-                tc_prefetch_row<BN>(a, m0 + et, n0, false);
-            if (staged) tc_stage_operands<BN>(a, m0, n0, nr, nc, ra, et, kEt);
+            if (kStage && (!staged || !kEarly) && g == 0)  // operands into L2 meanwhile
+                tc_prefetch_row<BN>(a, m0 + et, n0, staged);
+            if (staged && kEarly) tc_stage_operands<BN>(a, m0, n0, nr, nc, ra, et, kEt);
             if (a.wscale)  // the tile's column scales, read from shared memory below
                 for (int c = et; c < BN; c += kEt) wsc[c] = n0 + c < a.N ? a.wscale[n0 + c] : 1.0f;
             named_bar_sync(1, kEt);  // every epilogue warp: ra and wsc complete
             bool ok = mbar_wait(acc_full, 0, err);
             tc_fence_after();
             const int row = q * 32 + lane;  // TMEM lane = tile row of this thread
+            // a quarter's 32 rows are stored by its four warps (one per group,
+            // named barrier 2 + q) as soon as they are finished
+            const int eq = g * 32 + lane, nq = nr - q * 32 < 0 ? 0 : (nr - q * 32 < 32 ? nr - q * 32 : 32);
+            // Rows of 128 columns and more leave by one bulk copy per row (the
+            // copy engine moves them faster than the warps' stores); narrower
+            // ones by the quarter's coalesced stores.
+            constexpr bool kBulkRows = BN >= 128;
+            auto store_rows = [&](const float* fq, const __nv_bfloat16* hq, const __nv_bfloat16* lq) {
+                if (kBulkRows) fence_proxy_async_smem();  // the rows, for the copy engine
+                named_bar_sync(2 + q, 128);  // this quarter's rows finished
+                if (!ok || *give_up) return;
+                if (kBulkRows) {
+                    if (g == 0 && lane < nq) {
+                        const long long o = (long long)(m0 + row) * a.ldc + n0;
+                        bulk_s2g(a.C + o, fq + lane * RS, nc * 4);
+                        if (hq) {
+                            bulk_s2g(reinterpret_cast<__nv_bfloat16*>(a.Ch) + o, hq + lane * RSH, nc * 2);
+                            bulk_s2g(reinterpret_cast<__nv_bfloat16*>(a.Cl) + o, lq + lane * RSH, nc * 2);
+                        }
+                        bulk_commit();
+                        bulk_wait_read_all();  // the rows stay valid until read
+                    }
+                } else {
+                    tc_store_tile<BN>(a.C, a.ldc, m0 + q * 32, n0, nq, nc, fq, eq, 128);
+                    if (hq) {
+                        tc_store_plane<BN>(reinterpret_cast<__nv_bfloat16*>(a.Ch), a.ldc, m0 + q * 32, n0,
+                                           nq, nc, hq, eq, 128);
+                        tc_store_plane<BN>(reinterpret_cast<__nv_bfloat16*>(a.Cl), a.ldc, m0 + q * 32, n0,
+                                           nq, nc, lq, eq, 128);
+                    }
+                }
+            };
             if (staged) {
                 const bool resid = a.epi == kEpiResid;
+                if (!kEarly) {
+                    // every MMA has completed, so the ring is free: the quarter's
+                    // operand rows by bulk copies (group 0, a row per thread)
+                    if (g == 0 && ok && !*give_up) {
+                        if (lane == 0)
+                            mbar_expect_tx(&op_full[q], (uint32_t)(nq * nc * 4 * (resid ? 3 : 1)));
+                        __syncwarp();
+                        if (lane < nq) {
+                            float* orow = ra + row * RS;
+                            const long long mm = m0 + row;
+                            if (resid) {
+                                bulk_g2s(orow, a.S + mm * a.lds + n0, nc * 4, &op_full[q]);
+                                bulk_g2s(orow + BM * RS, a.F + mm * a.ldf + n0, nc * 4, &op_full[q]);
+                                bulk_g2s(orow + 2 * BM * RS, a.X + mm * a.ldx + n0, nc * 4, &op_full[q]);
+                            } else {
+                                bulk_g2s(orow, a.C + mm * a.ldc + n0, nc * 4, &op_full[q]);
+                            }
+                        }
+                    }
+                    if (ok && !*give_up) ok = mbar_wait(&op_full[q], 0, err);
+                }
                 float* orow = ra + row * RS;
 #pragma unroll 1
                 for (int j0 = g * 32; ok && !*give_up && j0 < BN; j0 += 32 * kEpiGroups) {
@@ -622,9 +689,18 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
                         float4* o = reinterpret_cast<float4*>(orow + j0 + j);
-                        const float4 r4 = o[0];
                         float y[4] = {v[j], v[j + 1], v[j + 2], v[j + 3]};
-                        const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+                        float rv[4];
+                        if (kEarly || !resid) {  // the staged operand (p*S + F + X, or C)
+                            const float4 r4 = o[0];
+                            rv[0] = r4.x, rv[1] = r4.y, rv[2] = r4.z, rv[3] = r4.w;
+                        } else {  // late staging: S, F and X rows as fetched
+                            const float4 s4 = o[0], f4 = o[BM * RS / 4], x4 = o[2 * BM * RS / 4];
+                            rv[0] = a.p * s4.x + f4.x + x4.x;
+                            rv[1] = a.p * s4.y + f4.y + x4.y;
+                            rv[2] = a.p * s4.z + f4.z + x4.z;
+                            rv[3] = a.p * s4.w + f4.w + x4.w;
+                        }
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             if (a.wscale) y[i] = y[i] * wsc[j0 + j + i];
@@ -634,8 +710,7 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
                         o[0] = make_float4(y[0], y[1], y[2], y[3]);
                     }
                 }
-                named_bar_sync(1, kEt);  // every row finished
-                if (ok && !*give_up) tc_store_tile<BN>(a.C, a.ldc, m0, n0, nr, nc, ra, et, kEt);
+                store_rows(ra + q * 32 * RS, nullptr, nullptr);
             } else if (rows) {
                 float* orow = reinterpret_cast<float*>(sb) + row * RS;
                 __nv_bfloat16* hrow =
@@ -658,18 +733,11 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
                         default: tc_row_block<kEpiNone>(a, v, wsc + j0, out, h, l);
                     }
                 }
-                named_bar_sync(1, kEt);  // every row finished
-                if (ok && !*give_up) {
-                    tc_store_tile<BN>(a.C, a.ldc, m0, n0, nr, nc, reinterpret_cast<float*>(sb), et, kEt);
-                    if (a.Ch) {
-                        const __nv_bfloat16* hs =
-                            reinterpret_cast<const __nv_bfloat16*>(reinterpret_cast<float*>(sb) + BM * RS);
-                        tc_store_plane<BN>(reinterpret_cast<__nv_bfloat16*>(a.Ch), a.ldc, m0, n0, nr, nc, hs,
-                                           et, kEt);
-                        tc_store_plane<BN>(reinterpret_cast<__nv_bfloat16*>(a.Cl), a.ldc, m0, n0, nr, nc,
-                                           hs + BM * RSH, et, kEt);
-                    }
-                }
+                const __nv_bfloat16* hs =
+                    reinterpret_cast<const __nv_bfloat16*>(reinterpret_cast<float*>(sb) + BM * RS) +
+                    q * 32 * RSH;
+                store_rows(reinterpret_cast<float*>(sb) + q * 32 * RS, a.Ch ? hs : nullptr,
+                           a.Ch ? hs + BM * RSH : nullptr);
             } else if (g == 0 && ok && !*give_up) {
                 // 32x32 blocks go through shared memory (the drained ring) so that a
                 // warp touches one 128-byte row segment per global access
