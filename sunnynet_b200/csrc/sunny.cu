@@ -246,10 +246,13 @@ __global__ void __launch_bounds__(kRowMaxThreads)
                     __nv_bfloat16* __restrict__ atl) {
     __shared__ float red[32];
     pdl_trigger();
-    pdl_wait();
     const int b = blockIdx.x;
     const int col = 4 * threadIdx.x;
     const bool live = col < D;
+    // Before waiting for the previous kernel: everything this kernel reads
+    // that no kernel of the current step writes before it (the ring position
+    // and history rows of this layer, written only by this layer's prep of
+    // earlier steps; the parameters; the token and its embedding row).
     const int p = pos[b * L + layer];
     float* xr = x + (size_t)b * D;
     const float* src = xr;
@@ -266,7 +269,6 @@ __global__ void __launch_bounds__(kRowMaxThreads)
     float4 hv[3], wv[3];
     const int kk = K - 1 < 3 ? K - 1 : 3;  // history rows held in registers
     if (live) {  // every load of this thread's columns, issued together
-        v = ld4(src + col);
         gg = ld4(g + col);
         cc = ld4(c + col);
         if (K > 1) wl = ld4(dw + (size_t)(K - 1) * D + col);
@@ -277,7 +279,12 @@ __global__ void __launch_bounds__(kRowMaxThreads)
                 hv[j] = ld4(hb + (size_t)slot * D + col);
                 wv[j] = ld4(dw + (size_t)(K - 2 - j) * D + col);
             }
-        if (layer == 0) st4(xr + col, v);
+        if (layer == 0) v = ld4(src + col);
+    }
+    pdl_wait();  // x: the previous layer's output
+    if (live) {
+        if (layer > 0) v = ld4(src + col);
+        else st4(xr + col, v);
     }
     float mean, rstd;
     cta_row_stats(v, live, D, eps, red, &mean, &rstd);
@@ -341,15 +348,15 @@ __global__ void __launch_bounds__(kRowMaxThreads)
                         float eps) {
     __shared__ float red[32];
     pdl_trigger();
-    pdl_wait();
     const int col = 4 * threadIdx.x;
     const bool live = col < n;
     float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f), gg = v, cc = v;
-    if (live) {
-        v = ld4(X + (size_t)blockIdx.x * ldx + col);
+    if (live) {  // the parameters before waiting for X's producer
         gg = ld4(g + col);
         cc = ld4(c + col);
     }
+    pdl_wait();
+    if (live) v = ld4(X + (size_t)blockIdx.x * ldx + col);
     float mean, rstd;
     cta_row_stats(v, live, n, eps, red, &mean, &rstd);
     if (!live) return;
@@ -368,17 +375,23 @@ __global__ void __launch_bounds__(256)
                  float* __restrict__ gate_out, int clamp, float p_floor,
                  __nv_bfloat16* __restrict__ uh, __nv_bfloat16* __restrict__ ul) {
     pdl_trigger();
-    pdl_wait();
     const int ng = D >> 3;
     const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    if (i >= (long long)B * ng) return;
-    const int b = (int)(i / ng), d0 = (int)(i - (long long)b * ng) * 8;
+    const bool live = i < (long long)B * ng;
+    const int b = live ? (int)(i / ng) : 0, d0 = live ? (int)(i - (long long)b * ng) * 8 : 0;
     const float* qb = q + (size_t)b * 2 * D;
     float* sp = s + ((size_t)b * L + layer) * D + d0;
+    // before waiting for U: delta, and this layer's state (written only by
+    // this layer's gate, in earlier steps)
+    float4 e0, e1, s0, s1;
+    if (live) {
+        e0 = ld4(delta + d0), e1 = ld4(delta + d0 + 4);
+        s0 = ld4(sp), s1 = ld4(sp + 4);
+    }
+    pdl_wait();
+    if (!live) return;
     const float4 a0 = ld4(qb + d0), a1 = ld4(qb + d0 + 4);
     const float4 g0 = ld4(qb + D + d0), g1 = ld4(qb + D + d0 + 4);
-    const float4 e0 = ld4(delta + d0), e1 = ld4(delta + d0 + 4);
-    const float4 s0 = ld4(sp), s1 = ld4(sp + 4);
     const float ur[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
     const float gt[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
     const float dl[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
