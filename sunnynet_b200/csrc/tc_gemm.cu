@@ -355,21 +355,20 @@ __device__ __forceinline__ void tc_row_block(const GemmArgs& a, const float* v, 
 //
 // Split K, owner side, in groups of 4 consecutive outputs of a row (16-byte
 // loads and stores; the host splits K only when every operand allows that).
-// The owner's ng = rows * BN / 4 groups are spread over the 128 epilogue
-// threads: group g = u * 128 + et, row-major. tc_own_operands stages each
-// group's residual / accumulate operands in shared memory before the
-// accumulator is ready; tc_reduce sums the ks partial rows of the cluster in
-// rank order (partials at [row][BN+4] in each CTA), then applies the epilogue.
+// The owner's ng = rows * BN / 4 groups are spread over the nt epilogue
+// threads (et = 0..nt-1), row-major. tc_own_operands stages each group's
+// residual / accumulate operands in shared memory before the accumulator is
+// ready; tc_reduce sums the ks partial rows of the cluster in rank order
+// (partials at [row][BN+4] in each CTA), then applies the epilogue.
 template <int BN>
 __device__ __forceinline__ void tc_own_operands(const GemmArgs& a, int mr0, int n0, int ng, int et,
-                                                float4* pre) {
+                                                int nt, float4* pre) {
 #pragma unroll 2
-    for (int u = 0; u * 128 < ng; ++u) {
-        const int g = u * 128 + et;
+    for (int g = et; g < ng; g += nt) {
         float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         const long long mm = mr0 + (4 * g) / BN;
         const int n = n0 + (4 * g) % BN;
-        if (g < ng && mm < a.M && n < a.N) {
+        if (mm < a.M && n < a.N) {
             if (a.epi == kEpiResid) {
                 const float4 sv = *reinterpret_cast<const float4*>(a.S + mm * a.lds + n);
                 const float4 fv = *reinterpret_cast<const float4*>(a.F + mm * a.ldf + n);
@@ -386,12 +385,11 @@ __device__ __forceinline__ void tc_own_operands(const GemmArgs& a, int mr0, int 
 
 template <int EPI, int BN>
 __device__ __forceinline__ void tc_reduce(const GemmArgs& a, const float* part, int ks, int rows,
-                                          int r0, int m0, int n0, int et, const float4* pre) {
+                                          int r0, int m0, int n0, int et, int nt,
+                                          const float4* pre) {
     const int ng = rows * BN / 4;
 #pragma unroll 2
-    for (int u = 0; u * 128 < ng; ++u) {
-        const int g = u * 128 + et;
-        if (g >= ng) continue;
+    for (int g = et; g < ng; g += nt) {
         const int r = (4 * g) / BN, c = (4 * g) % BN;
         const float* src = part + (r0 + r) * (BN + 4) + c;
         float4 x = ld_dsmem_f32x4(src, 0);
@@ -559,24 +557,24 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
         const int g = (warp - 2) >> 2;  // column group
         const int et = threadIdx.x - 64;
         pdl_wait();  // the epilogue reads (and overwrites) the previous kernels' outputs
-        if (ks > 1 && g > 0) {
-            // split K: group 0 alone
-        } else if (ks > 1) {
+        if (ks > 1) {
             // split K: CTA kz owns rows [kz*rows, (kz+1)*rows) of the tile; its
             // residual / accumulate operands are loaded now, under the main loop
+            // (every epilogue thread)
             const int rows = BM / ks;
             if (LOADS)
-                tc_own_operands<BN>(a, m0 + kz * rows, n0, rows * BN / 4, et,
+                tc_own_operands<BN>(a, m0 + kz * rows, n0, rows * BN / 4, et, 128 * kEpiGroups,
                                     reinterpret_cast<float4*>(pre_all));
             const bool ok = mbar_wait(acc_full, 0, err);
             tc_fence_after();
             if (ok && !*give_up) {
                 // this CTA's partial rows into its own shared memory (the
-                // drained ring), [128][BN+4]; the owners read them below
+                // drained ring), [128][BN+4]; the owners read them below. The
+                // groups share the 32-column blocks.
                 float4* part = reinterpret_cast<float4*>(reinterpret_cast<float*>(sb) +
                                                          (q * 32 + lane) * (BN + 4));
 #pragma unroll 1
-                for (int j0 = 0; j0 < BN; j0 += 32) {
+                for (int j0 = g * 32; j0 < BN; j0 += 32 * kEpiGroups) {
                     float v[32];
                     tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)j0, v);
 #pragma unroll
@@ -800,17 +798,17 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
         // tile, summing the cluster's partials in rank order (results do not
         // depend on timing); no CTA leaves while its partials may be read.
         cluster_sync();
-        if (warp >= 2 && warp < 6) {  // epilogue group 0
-            const int et = threadIdx.x - 64, rows = BM / ks, r0 = kz * rows;
+        if (warp >= 2) {  // every epilogue thread
+            const int et = threadIdx.x - 64, nt = 128 * kEpiGroups, rows = BM / ks, r0 = kz * rows;
             const float* part = reinterpret_cast<const float*>(sb);
             switch (a.epi) {
-                case kEpiWedge: tc_reduce<kEpiWedge, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
-                case kEpiResid: tc_reduce<kEpiResid, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
-                case kEpiAdd: tc_reduce<kEpiAdd, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
-                case kEpiRelu2: tc_reduce<kEpiRelu2, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
-                case kEpiTanh: tc_reduce<kEpiTanh, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
-                case kEpiSigmoid: tc_reduce<kEpiSigmoid, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all)); break;
-                default: tc_reduce<kEpiNone, BN>(a, part, ks, rows, r0, m0, n0, et, reinterpret_cast<const float4*>(pre_all));
+                case kEpiWedge: tc_reduce<kEpiWedge, BN>(a, part, ks, rows, r0, m0, n0, et, nt, reinterpret_cast<const float4*>(pre_all)); break;
+                case kEpiResid: tc_reduce<kEpiResid, BN>(a, part, ks, rows, r0, m0, n0, et, nt, reinterpret_cast<const float4*>(pre_all)); break;
+                case kEpiAdd: tc_reduce<kEpiAdd, BN>(a, part, ks, rows, r0, m0, n0, et, nt, reinterpret_cast<const float4*>(pre_all)); break;
+                case kEpiRelu2: tc_reduce<kEpiRelu2, BN>(a, part, ks, rows, r0, m0, n0, et, nt, reinterpret_cast<const float4*>(pre_all)); break;
+                case kEpiTanh: tc_reduce<kEpiTanh, BN>(a, part, ks, rows, r0, m0, n0, et, nt, reinterpret_cast<const float4*>(pre_all)); break;
+                case kEpiSigmoid: tc_reduce<kEpiSigmoid, BN>(a, part, ks, rows, r0, m0, n0, et, nt, reinterpret_cast<const float4*>(pre_all)); break;
+                default: tc_reduce<kEpiNone, BN>(a, part, ks, rows, r0, m0, n0, et, nt, reinterpret_cast<const float4*>(pre_all));
             }
         }
         cluster_sync();
@@ -990,13 +988,41 @@ bool tc_usable(const GemmArgs& a, const TcWeights* tw) {
 
 namespace {
 
+// Whether K may split ks ways for a tile width (host side): each CTA's
+// partial tile [BM][BN + 4] fp32 must fit its drained ring and, for residual /
+// accumulate kinds, the owner's operand rows ([BM / ks][BN] fp32) the operand
+// area next to it.
+template <int B, bool I, bool L>
+bool split_fits_cfg(int ks) {
+    using C = TcCfg<B, I, L>;
+    return BM % ks == 0 && BM * (B + 4) * 4 <= C::S * C::STAGE && (!L || (BM / ks) * B * 4 <= C::PRE);
+}
+bool split_fits(int b, bool i8, bool ld, int ks) {
+#define SN_FIT(B)                                                                        \
+    if (b == B)                                                                          \
+        return i8 ? (ld ? split_fits_cfg<B, true, true>(ks) : split_fits_cfg<B, true, false>(ks)) \
+                  : (ld ? split_fits_cfg<B, false, true>(ks) : split_fits_cfg<B, false, false>(ks));
+    SN_FIT(32)
+    SN_FIT(64)
+    SN_FIT(128)
+    SN_FIT(192)
+    SN_FIT(256)
+#undef SN_FIT
+    return false;
+}
+
 // Tile width BN and K split ks from a cost model of this kernel, per CTA in
-// SM cycles (measured on B200 decode and prefill shapes): ~2400 to the first
-// K slab, then the slab bytes at ~45 B/cycle (2 x 128 x 128 B of A planes +
-// 128 B per weight row and plane), ~900 per 32 output columns of epilogue,
-// ~4000 for a split's cluster reduction; times the number of waves. Split K
-// needs a 16-byte-friendly epilogue, BN <= 64 and >= 8 K slabs (two per CTA
-// at least).
+// SM cycles, fitted to launches timed back to back on B200 decode and prefill
+// shapes: ~10400 of launch, first-slab latency and epilogue, then per K slab
+// the slower of its TMA bytes at ~92 B/cycle (2 x 128 x 128 B of A planes +
+// 128 B per weight row and plane) and its MMAs (two or three per 16-wide K
+// step; one M=128 tcgen05.mma of N columns takes max(90, 0.63 N) cycles, so
+// narrow tiles are issue-bound), and 4500 + 22 per column for a split's
+// cluster reduction and co-scheduling (a cluster waits for SMs of one GPC to
+// be free together, which the step's overlapping kernels make costly); times
+// the number of waves. Split K needs a
+// 16-byte-friendly epilogue, partial and operand tiles that fit shared memory
+// (split_fits) and >= 8 K slabs (two per CTA at least).
 int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
                  const CUtensorMap& tal, cudaStream_t st, bool pdl) {
     const long long mt = (a.M + BM - 1) / BM;
@@ -1029,13 +1055,18 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
         // the bf16 planes of the result fit the drained ring for their epilogue
         if (b == 192 && (ld || a.Ch != nullptr || tw.int8)) continue;
         const long long tiles = mt * ((a.N + b - 1) / b);
-        const double slab = 2.0 * BM * 128 + (tw.int8 ? 1.0 : 2.0) * b * 128;
+        const double bytes = 2.0 * BM * 128 + (tw.int8 ? 1.0 : 2.0) * b * 128;
+        const double mma = 0.63 * b > 90.0 ? 0.63 * b : 90.0;
+        const double slab = bytes / 92.0 > (tw.int8 ? 8 : 12) * mma ? bytes / 92.0
+                                                                    : (tw.int8 ? 8 : 12) * mma;
         for (int k = 1; k <= 8; k *= 2) {
-            if (k > 1 && (!may_split || b > 64 || nkt < 2 * k || tiles * k > sms)) continue;
+            if (k > 1 && (!may_split || !split_fits(b, tw.int8, ld, k) || nkt < 2 * k ||
+                          tiles * k > sms))
+                continue;
             if (pass == 0 && tiles * k > a.max_ctas) continue;  // within the CTA cap first
             const long long waves = (tiles * k + sms - 1) / sms;
-            const double t = (double)waves * (2400.0 + ((nkt + k - 1) / k) * slab / 45.0 +
-                                              900.0 * b / 32 + (k > 1 ? 4000.0 : 0.0));
+            const double t = (double)waves * (10400.0 + ((nkt + k - 1) / k) * slab +
+                                              (k > 1 ? 4500.0 + 22.0 * b : 0.0));
             if (t < best * 0.98) {  // a wider or more split choice must win clearly
                 best = t;
                 bn = b;
@@ -1053,6 +1084,13 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
         if (ok) {
             bn = b;
             ks = 1;
+            // SN_TC_FORCE_KS (2/4/8) with it: that K split where it is allowed
+            if (const char* fk = getenv("SN_TC_FORCE_KS")) {
+                const int k = atoi(fk);
+                if ((k == 2 || k == 4 || k == 8) && may_split && split_fits(b, tw.int8, ld, k) &&
+                    nkt >= 2 * k)
+                    ks = k;
+            }
         }
     }
 #define SN_TC_BN(I8, LD)                                                                  \
