@@ -582,8 +582,8 @@ int launch_scan_bwd(const float* a, const float* b, const float* s0, const float
 //   agg    thread per (seq, chunk, channel): the chunk's composed map (A, B),
 //          B chained from 0 with the reference's per-row rule
 //   carry  per (seq, channel), over chunks: carry_c = A_c*carry_{c-1} + B_c,
-//          a two-level pass (8 warps split the chunks, a short serial combine
-//          of the 8 warp totals, then each warp re-applies its chunks); the
+//          a two-level pass (32 warps split the chunks, a shuffle scan of
+//          the 32 warp totals, then each warp re-applies its chunks); the
 //          state entering chunk c replaces A_c in the record
 //   apply  same threads as agg: re-run the chunk's rows from its carry with
 //          the reference rule, write every row; the last chunk writes send
@@ -746,16 +746,25 @@ __global__ void __launch_bounds__(256)
     if (n < N) agg[((size_t)sq * nch + c) * N + n] = make_float2(A, Bc);
 }
 
-// Block: 32 channels x kCarryWarps warps; warp w owns chunks
-// [w*per, (w+1)*per). Records are read kCarryBatch at a time into registers
-// before any of them is used or overwritten, so each batch costs one L2
-// round trip rather than one per chunk.
+// Block: 32 channels x kCarryWarps (= 32) warps; warp w owns chunks
+// [w*per, (w+1)*per). Each warp composes its chunks' maps (records read
+// kCarryBatch at a time into registers, one L2 round trip per batch, and kept
+// there when per <= kCarryBatch); the 32 warp totals of a channel are then
+// scanned by one warp with shuffles (log2(32) compositions instead of a
+// serial walk), and each warp re-applies its chunks from the carry entering
+// them.
 constexpr int kCarryWarps = 32;
 constexpr int kCarryBatch = 8;
 
+// (A1, B1) then (A2, B2): s -> A2*(A1*s + B1) + B2
+__device__ __forceinline__ float2 compose(float2 first, float2 then) {
+    return make_float2(__fmul_rn(then.x, first.x), __fmaf_rn(then.x, first.y, then.y));
+}
+
 __global__ void __launch_bounds__(kCarryWarps * 32)
     scan_carry_kernel(const float* __restrict__ s0, float2* __restrict__ agg, int N, int nch) {
-    __shared__ float2 wtot[kCarryWarps][32];
+    static_assert(kCarryWarps == 32, "one warp scans the warp totals");
+    __shared__ float2 wtot[kCarryWarps][33];  // [warp][channel]: totals, then carries in
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -764,9 +773,10 @@ __global__ void __launch_bounds__(kCarryWarps * 32)
     const int per = (nch + kCarryWarps - 1) / kCarryWarps;
     const int c0 = min(nch, w * per), c1 = min(nch, c0 + per);
     float2* rec = agg + (size_t)sq * nch * N + n;
+    const bool keep = per <= kCarryBatch;  // one batch: the records stay in registers
+    float2 m[kCarryBatch];
     float A = 1.0f, Bc = 0.0f;  // composition of this warp's chunks
     for (int cb = c0; cb < c1; cb += kCarryBatch) {
-        float2 m[kCarryBatch];
 #pragma unroll
         for (int j = 0; j < kCarryBatch; ++j)
             if (live && cb + j < c1) m[j] = ld_cg(rec + (size_t)(cb + j) * N);
@@ -780,13 +790,28 @@ __global__ void __launch_bounds__(kCarryWarps * 32)
     }
     wtot[w][lane] = make_float2(A, Bc);
     __syncthreads();
-    float s = live ? s0[(size_t)sq * N + n] : 0.0f;
-    for (int v = 0; v < w; ++v) s = __fmaf_rn(wtot[v][lane].x, s, wtot[v][lane].y);
-    for (int cb = c0; cb < c1; cb += kCarryBatch) {
-        float2 m[kCarryBatch];
+    {   // warp v: exclusive scan over the warps' totals of channel v (lane = warp)
+        const int v = w;
+        float2 t = wtot[lane][v];
 #pragma unroll
-        for (int j = 0; j < kCarryBatch; ++j)
-            if (live && cb + j < c1) m[j] = ld_cg(rec + (size_t)(cb + j) * N);
+        for (int off = 1; off < 32; off <<= 1) {
+            const float2 e = make_float2(__shfl_up_sync(~0u, t.x, off), __shfl_up_sync(~0u, t.y, off));
+            if (lane >= off) t = compose(e, t);
+        }
+        float2 ex = make_float2(__shfl_up_sync(~0u, t.x, 1), __shfl_up_sync(~0u, t.y, 1));
+        if (lane == 0) ex = make_float2(1.0f, 0.0f);
+        __syncthreads();  // every total read before the carries overwrite them
+        wtot[lane][v] = ex;
+    }
+    __syncthreads();
+    const float2 ex = wtot[w][lane];
+    float s = live ? __fmaf_rn(ex.x, s0[(size_t)sq * N + n], ex.y) : 0.0f;
+    for (int cb = c0; cb < c1; cb += kCarryBatch) {
+        if (!keep) {
+#pragma unroll
+            for (int j = 0; j < kCarryBatch; ++j)
+                if (live && cb + j < c1) m[j] = ld_cg(rec + (size_t)(cb + j) * N);
+        }
 #pragma unroll
         for (int j = 0; j < kCarryBatch; ++j) {
             if (live && cb + j < c1) {
