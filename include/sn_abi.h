@@ -126,6 +126,12 @@ sn_status sn_abi_cuda_synchronize(void);              /* waits; reports deferred
 int32_t   sn_abi_last_error(char* buf, int32_t buflen); /* message of the last failure */
 void      sn_abi_clear_error(void);                    /* empties it (this thread) */
 int32_t   sn_abi_cuda_scan_mode(int32_t mode);        /* 0 exact (default), 1 chunked; returns old */
+/* INT8 weights of models loaded afterwards, batched (tensor-core) path: 1 keeps
+ * the codes (1 byte per weight) and converts each K slab to bf16 inside the
+ * contraction's main loop; 0 (default) expands them once at load to bf16 code
+ * planes (2 bytes per weight, faster on this build's B200 measurements).
+ * Results are identical. Returns the old setting. */
+int32_t   sn_abi_cuda_int8_mainloop(int32_t on);
 /* Kernel-family timing with CUDA events (1 = start and clear, 0 = stop). While
  * on, model steps run without their CUDA graph so each kernel can be bracketed. */
 sn_status sn_abi_cuda_profile(int32_t on);

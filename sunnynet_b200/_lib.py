@@ -43,6 +43,7 @@ SIGNATURES = {
     "sn_abi_last_error": (I32, [P, I32]),
     "sn_abi_clear_error": (None, []),
     "sn_abi_cuda_scan_mode": (I32, [I32]),
+    "sn_abi_cuda_int8_mainloop": (I32, [I32]),
     "sn_abi_cuda_profile": (I32, [I32]),
     "sn_abi_cuda_profile_report": (I32, [P, I32]),
     "sn_abi_cuda_wait_selftest": (I32, [I32, ctypes.c_int64]),

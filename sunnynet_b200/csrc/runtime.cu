@@ -356,4 +356,10 @@ int32_t sn_abi_cuda_scan_mode(int32_t mode) {
     return old;
 }
 
+int32_t sn_abi_cuda_int8_mainloop(int32_t on) {
+    int32_t old = rt().int8_mainloop;
+    if (on == 0 || on == 1) rt().int8_mainloop = on;
+    return old;
+}
+
 }  // extern "C"

@@ -23,6 +23,7 @@ struct Runtime {
     bool async = false;
     int threads = 1;
     int scan_mode = 0;
+    int int8_mainloop = 0;  // INT8 contractions convert codes in the main loop
     volatile int* h_err = nullptr;  // mapped pinned word written by device waits
     int* d_err = nullptr;           // device alias of h_err
     void* slot[12] = {};

@@ -51,6 +51,13 @@ struct TcEpi {
     static constexpr int GROUPS = BN > 32 ? 4 : 1;
     static constexpr int THREADS = 64 + 128 * GROUPS;
 };
+// INT8 codes converted in the main loop (CV) add converter warps after the
+// epilogue warps: one warp group, two for tiles of 128 columns and more
+template <int BN, bool CV>
+struct TcThreads {
+    static constexpr int CONV = CV ? (BN >= 128 ? 256 : 128) : 0;
+    static constexpr int N = TcEpi<BN>::THREADS + CONV;
+};
 
 // Residual / accumulate tiles of 64 or 128 columns stage their whole operand
 // tile ([BM][BN + 4] fp32): under the main loop, next to the ring, where that
@@ -64,7 +71,8 @@ template <int BN, bool I8, bool LOADS = false>
 struct TcCfg {
     static constexpr int A_BYTES = BM * 128;
     static constexpr int W_BYTES = BN * 128;
-    // a stage: the A hi / lo slabs and the weight hi (and, bf16 weights, lo) slab
+    // a stage: the A hi / lo slabs and the weight slab, bf16 hi and lo (INT8
+    // weights: the one bf16 slab the converter warps write)
     static constexpr int STAGE = 2 * A_BYTES + (I8 ? 1 : 2) * W_BYTES;
     // epilogue operands loaded under the main loop: [4 warps][32][33] floats
     // (32x32 blocks), or the staged operand tile
@@ -80,10 +88,11 @@ struct TcCfg {
     static constexpr int S_FIT = (227 * 1024 - PRE - FIXED) / STAGE;
     static constexpr int S = S_FIT > 6 ? 6 : S_FIT;
     static_assert(S >= 2, "two ring stages at least");
-    // late staging fetches the S, F and X rows into the drained ring and the
-    // operand area that follows it
-    static_assert(EARLY || !TcStage<BN, LOADS>::ON || 3 * TILE <= S * STAGE + PRE,
-                  "late-staged operand rows fit");
+    // late staging fetches the S, F and X rows by bulk copies into the
+    // drained ring and the operand area that follows it where the three fit
+    // (LATE3), else p*S + F + X into the ring with 16-byte loads
+    static constexpr bool LATE3 = 3 * TILE <= S * STAGE + PRE;
+    static_assert(EARLY || !TcStage<BN, LOADS>::ON || TILE <= S * STAGE, "late operand tile fits");
     // after the 256 bytes of barriers: the tile's per-column weight scales
     static constexpr int SMEM = S * STAGE + PRE + 1024 + 256 + BN * 4;
 };
@@ -428,8 +437,8 @@ __device__ __forceinline__ void tc_reduce(const GemmArgs& a, const float* part, 
 
 // LOADS: the epilogue reads more than the accumulator (residual / accumulate
 // kinds); those operands are then all loaded before any result is stored.
-template <int BN, bool I8, bool LOADS>
-__global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
+template <int BN, bool I8, bool LOADS, bool CV>
+__global__ void __launch_bounds__(TcThreads<BN, CV>::N, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
                    const __grid_constant__ CUtensorMap twh, const __grid_constant__ CUtensorMap twl,
                    GemmArgs a, int* err) {
@@ -444,7 +453,8 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
     float* pre_all = reinterpret_cast<float*>(sb + S * C::STAGE);
     uint64_t* full = reinterpret_cast<uint64_t*>(sb + S * C::STAGE + C::PRE);
     uint64_t* empty = full + S;
-    uint64_t* acc_full = empty + S;
+    uint64_t* conv = empty + S;  // INT8: a stage's weight slab converted to bf16
+    uint64_t* acc_full = conv + S;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(acc_full + 1);
     volatile int* give_up = reinterpret_cast<volatile int*>(acc_full + 2);
     uint64_t* op_full = acc_full + 3;  // [4]: a quarter's operand rows landed (late staging)
@@ -457,6 +467,9 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
     const int m0 = blockIdx.y * BM, n0 = (blockIdx.x / ks) * BN;
     const int nkt = (a.K + BK - 1) / BK;
     const int k0 = kz * nkt / ks, nk = (kz + 1) * nkt / ks - k0;
+    // INT8 weights: codes converted to bf16 in the main loop by the converter
+    // warps (CV), or bf16 code planes loaded by TMA like other weights
+    constexpr bool cv = I8 && CV;
     pdl_trigger();  // the next kernel may start its own prologue
     auto stage_ptr = [&](int s, int part) -> uint8_t* {  // 0 Ah, 1 Al, 2 Wh, 3 Wl
         return sb + s * C::STAGE +
@@ -467,6 +480,7 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+            mbar_init(&conv[s], TcThreads<BN, CV>::CONV > 0 ? TcThreads<BN, CV>::CONV : 1);
         }
         mbar_init(acc_full, 1);
         for (int q = 0; q < 4; ++q) mbar_init(&op_full[q], 1);
@@ -491,17 +505,25 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
             // first use comes after the wait for the previous kernel)
             prefetch_tmap(&tah);
             prefetch_tmap(&tal);
-            prefetch_tmap(&twh);
-            if (!I8) prefetch_tmap(&twl);
-            const uint32_t bytes = 2 * C::A_BYTES + (I8 ? 1 : 2) * C::W_BYTES;
+            // INT8 codes converted in the main loop (cv) are not loaded by TMA:
+            // the converter warps write the weight slab
+            auto load_w = [&](int s, int kt) {
+                if (cv) return;
+                tma_load_2d(stage_ptr(s, 2), &twh, (k0 + kt) * BK, n0, &full[s]);
+                if (!I8) tma_load_2d(stage_ptr(s, 3), &twl, (k0 + kt) * BK, n0, &full[s]);
+            };
+            if (!cv) {
+                prefetch_tmap(&twh);
+                if (!I8) prefetch_tmap(&twl);
+            }
+            const uint32_t bytes = 2 * C::A_BYTES + (cv ? 0 : (I8 ? 1 : 2) * C::W_BYTES);
             // the weight tiles of the first S stages do not depend on the
             // previous kernel: in flight before waiting for it (programmatic
             // launch; pdl_wait is a no-op otherwise)
             const int pre = nk < S ? nk : S;
             for (int kt = 0; kt < pre; ++kt) {
                 mbar_expect_tx(&full[kt], bytes);
-                tma_load_2d(stage_ptr(kt, 2), &twh, (k0 + kt) * BK, n0, &full[kt]);
-                if (!I8) tma_load_2d(stage_ptr(kt, 3), &twl, (k0 + kt) * BK, n0, &full[kt]);
+                load_w(kt, kt);
             }
             pdl_wait();
             int issued = 0;
@@ -514,8 +536,7 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
                         break;
                     }
                     mbar_expect_tx(&full[s], bytes);
-                    tma_load_2d(stage_ptr(s, 2), &twh, (k0 + kt) * BK, n0, &full[s]);
-                    if (!I8) tma_load_2d(stage_ptr(s, 3), &twl, (k0 + kt) * BK, n0, &full[s]);
+                    load_w(s, kt);
                 }
                 tma_load_2d(stage_ptr(s, 0), &tah, (k0 + kt) * BK, m0, &full[s]);
                 tma_load_2d(stage_ptr(s, 1), &tal, (k0 + kt) * BK, m0, &full[s]);
@@ -533,7 +554,8 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
                                    | ((uint32_t)(BM >> 4) << 24); // M
             for (int kt = 0; kt < nk; ++kt) {
                 const int s = kt % S;
-                if (!mbar_wait(&full[s], (kt / S) & 1, err)) {
+                if (!mbar_wait(&full[s], (kt / S) & 1, err) ||
+                    (cv && !mbar_wait(&conv[s], (kt / S) & 1, err))) {
                     *give_up = 1;
                     break;
                 }
@@ -551,6 +573,84 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
                 tc_commit(&empty[s]);  // stage reusable once these MMAs have read it
             }
             tc_commit(acc_full);  // accumulator complete (or: nothing left in flight)
+        }
+    } else if (cv && warp >= 2 + 4 * kEpiGroups) {  // ------------- INT8 converter
+        if (!cv) {
+            // bf16 code planes: nothing to convert
+        } else {
+        // Each K slab's BN x 64 weight codes, read from global memory (L2) a
+        // few slabs ahead into registers, become the stage's bf16 slab the
+        // MMAs read, in the layout a SWIZZLE_128B load would write: row n in
+        // 8-row atoms of 1024 B, its 16-byte chunk c at position c ^ (n % 8).
+        // A code q is exact in bf16: the fp32 bit pattern 0x4B0000(q ^ 0x80)
+        // is 2^23 + 128 + q, so one subtraction gives q and its upper 16 bits
+        // are bf16(q). A thread takes 32 codes (row i / 2, half i % 2) per
+        // pass; codes past N or K read as zero. The weights do not depend on
+        // the previous kernel: no wait for it.
+        constexpr int NC = TcThreads<BN, CV>::CONV > 0 ? TcThreads<BN, CV>::CONV : 128;
+        constexpr int PER = (2 * BN + NC - 1) / NC;  // row halves per thread per slab
+        constexpr int DEPTH = 3;                      // slabs in flight per thread
+        const int ct = threadIdx.x - (64 + 128 * kEpiGroups);
+        const int8_t* q8 = reinterpret_cast<const int8_t*>(a.W);
+        uint4 buf[DEPTH][PER][2];
+        auto load = [&](int kt, uint4 (&b)[PER][2]) {
+#pragma unroll
+            for (int p = 0; p < PER; ++p) {
+                const int i = ct + p * NC, n = i >> 1, h = i & 1;
+                const int row = n0 + n, k = (k0 + kt) * BK + h * 32;
+                const int8_t* src = q8 + (long long)row * a.ldw + k;
+                const bool rok = i < 2 * BN && row < a.N && kt < nk;
+                b[p][0] = rok && k < a.K ? __ldg(reinterpret_cast<const uint4*>(src))
+                                         : make_uint4(0, 0, 0, 0);
+                b[p][1] = rok && k + 16 < a.K ? __ldg(reinterpret_cast<const uint4*>(src + 16))
+                                              : make_uint4(0, 0, 0, 0);
+            }
+        };
+#pragma unroll
+        for (int d = 0; d < DEPTH; ++d) load(d, buf[d]);
+        bool stop = false;
+        for (int kt0 = 0; kt0 < nk && !stop; kt0 += DEPTH) {
+#pragma unroll
+            for (int d = 0; d < DEPTH; ++d) {
+                const int kt = kt0 + d, s = kt % S;
+                if (kt >= nk || stop) break;
+                if (*give_up ||
+                    (kt >= S && !mbar_wait(&empty[s], ((kt / S) - 1) & 1, err))) {
+                    *give_up = 1;
+                    stop = true;
+                    break;
+                }
+                uint8_t* dst = stage_ptr(s, 2);
+#pragma unroll
+                for (int p = 0; p < PER; ++p) {
+                    const int i = ct + p * NC, n = i >> 1, h = i & 1;
+                    if (i >= 2 * BN) continue;
+                    const uint32_t* qw = reinterpret_cast<const uint32_t*>(buf[d][p]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {  // chunk 4h + j: codes 8j .. 8j + 7 of the half
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const uint32_t u = qw[2 * j + (e >> 1)] ^ 0x80808080u;  // q + 128
+                            const int b0 = (e & 1) * 2;  // bytes b0, b0 + 1 of the word
+                            const float f0 =
+                                __int_as_float((int)__byte_perm(u, 0x4B000000u, 0x7540u + b0)) -
+                                8388736.0f;
+                            const float f1 =
+                                __int_as_float((int)__byte_perm(u, 0x4B000000u, 0x7541u + b0)) -
+                                8388736.0f;
+                            o[e] = __byte_perm(__float_as_uint(f0), __float_as_uint(f1), 0x7632u);
+                        }
+                        *reinterpret_cast<uint4*>(dst + (n >> 3) * 1024 + (n & 7) * 128 +
+                                                  ((((4 * h + j) ^ (n & 7))) << 4)) =
+                            make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+                fence_proxy_async_smem();  // the slab, for the tensor cores
+                mbar_arrive(&conv[s]);
+                load(kt + DEPTH, buf[d]);
+            }
+        }
         }
     } else {  // ------------------------------------------------ epilogue (warps 2..)
         const int q = warp & 3;         // TMEM lane quarter this warp may read
@@ -658,7 +758,12 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
             };
             if (staged) {
                 const bool resid = a.epi == kEpiResid;
-                if (!kEarly) {
+                if (!kEarly && !C::LATE3) {
+                    // every MMA has completed, so the ring is free: the operand
+                    // tile p*S + F + X (or C) by every epilogue thread
+                    if (ok && !*give_up) tc_stage_operands<BN>(a, m0, n0, nr, nc, ra, et, kEt);
+                    named_bar_sync(1, kEt);
+                } else if (!kEarly) {
                     // every MMA has completed, so the ring is free: the quarter's
                     // operand rows by bulk copies (group 0, a row per thread)
                     if (g == 0 && ok && !*give_up) {
@@ -689,7 +794,7 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
                         float4* o = reinterpret_cast<float4*>(orow + j0 + j);
                         float y[4] = {v[j], v[j + 1], v[j + 2], v[j + 3]};
                         float rv[4];
-                        if (kEarly || !resid) {  // the staged operand (p*S + F + X, or C)
+                        if (kEarly || !C::LATE3 || !resid) {  // the staged operand (p*S + F + X, or C)
                             const float4 r4 = o[0];
                             rv[0] = r4.x, rv[1] = r4.y, rv[2] = r4.z, rv[3] = r4.w;
                         } else {  // late staging: S, F and X rows as fetched
@@ -798,7 +903,7 @@ __global__ void __launch_bounds__(TcEpi<BN>::THREADS, 1)
         // tile, summing the cluster's partials in rank order (results do not
         // depend on timing); no CTA leaves while its partials may be read.
         cluster_sync();
-        if (warp >= 2) {  // every epilogue thread
+        if (warp >= 2 && warp < 2 + 4 * kEpiGroups) {  // every epilogue thread
             const int et = threadIdx.x - 64, nt = 128 * kEpiGroups, rows = BM / ks, r0 = kz * rows;
             const float* part = reinterpret_cast<const float*>(sb);
             switch (a.epi) {
@@ -870,12 +975,12 @@ std::map<int, ActPlanes>& act_cache() {
     return c;
 }
 
-template <int BN, bool I8, bool LOADS>
+template <int BN, bool I8, bool LOADS, bool CV = false>
 int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
               const CUtensorMap& tal, cudaStream_t st, bool pdl, int ks) {
     using C = TcCfg<BN, I8, LOADS>;
     static bool attr = false;
-    auto k = tc_gemm_kernel<BN, I8, LOADS>;
+    auto k = tc_gemm_kernel<BN, I8, LOADS, CV>;
     if (!attr) {
         SN_TRY(cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                C::SMEM),
@@ -885,7 +990,7 @@ int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
     const int bi = BN == 32 ? 0 : (BN == 64 ? 1 : (BN == 128 ? 2 : (BN == 256 ? 3 : 4)));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(((a.N + BN - 1) / BN) * ks), (unsigned)((a.M + BM - 1) / BM));
-    cfg.blockDim = dim3(TcEpi<BN>::THREADS);
+    cfg.blockDim = dim3(TcThreads<BN, CV>::N);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute la[2];
@@ -904,7 +1009,12 @@ int launch_bn(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
     }
     cfg.attrs = la;
     cfg.numAttrs = na;
-    return cuda_check(cudaLaunchKernelEx(&cfg, k, tah, tal, tw.tm_hi[bi], tw.tm_lo[bi], a,
+    GemmArgs ka = a;
+    if (CV) {  // the converter warps read the (16-byte aligned) codes
+        ka.W = tw.q8;
+        ka.ldw = tw.K;
+    }
+    return cuda_check(cudaLaunchKernelEx(&cfg, k, tah, tal, tw.tm_hi[bi], tw.tm_lo[bi], ka,
                                          rt().d_err),
                       "tc_gemm launch");
 }
@@ -957,17 +1067,55 @@ int tc_prepare(TcWeights* tw, const void* W, int wtype, int N, int K,
     tw->K = K;
     tw->int8 = wtype == kWI8;
     tw->ready = false;
+    const int rows[5] = {32, 64, 128, 256, 192};  // weight tile heights (BN)
+    if (tw->int8 && rt().int8_mainloop) {
+        // the codes stay as they are: the contraction's converter warps read
+        // each K slab's codes and write its bf16 slab (rows of K bytes, 16-byte
+        // aligned: K % 16 == 0)
+        if (K % 16 != 0) return SN_OK;
+        const int8_t* q = reinterpret_cast<const int8_t*>(W);
+        if ((uintptr_t)q % 16 != 0) {  // a 16-byte aligned copy
+            int8_t* c = (int8_t*)alloc((size_t)N * K, owner);
+            if (!c) return fail(SN_E_NOMEM, "tc int8 weights");
+            SN_TRY(cuda_check(cudaMemcpy(c, q, (size_t)N * K, cudaMemcpyDeviceToDevice),
+                              "tc int8 copy"));
+            q = c;
+        }
+        tw->q8 = q;
+        // valid maps for the kernel's parameters (not used for the weights)
+        for (int i = 0; i < 5; ++i) {
+            SN_TRY(encode_tiled(&tw->tm_lo[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, q, K, N, K, BK,
+                                rows[i], CU_TENSOR_MAP_SWIZZLE_NONE));
+            tw->tm_hi[i] = tw->tm_lo[i];
+        }
+        tw->ready = true;
+        return SN_OK;
+    }
+    if (tw->int8) {  // bf16 code planes (exact), loaded by TMA; no lo plane
+        if (K % 8 != 0) return SN_OK;
+        const size_t n = (size_t)N * K;
+        tw->hi = (__nv_bfloat16*)alloc(n * 2, owner);
+        if (!tw->hi) return fail(SN_E_NOMEM, "tc weight planes");
+        split_bf16_kernel<<<grid_blocks((long long)n), 256>>>(W, wtype, (long long)n, tw->hi,
+                                                              nullptr);
+        SN_TRY(cuda_check(cudaGetLastError(), "split launch"));
+        for (int i = 0; i < 5; ++i) {
+            SN_TRY(encode_map(&tw->tm_hi[i], tw->hi, N, K, rows[i]));
+            tw->tm_lo[i] = tw->tm_hi[i];
+        }
+        tw->ready = true;
+        return SN_OK;
+    }
     if (K % 8 != 0) return SN_OK;  // TMA row stride must be a multiple of 16 bytes
     const size_t n = (size_t)N * K;
     tw->hi = (__nv_bfloat16*)alloc(n * 2, owner);
-    tw->lo = tw->int8 ? nullptr : (__nv_bfloat16*)alloc(n * 2, owner);
-    if (!tw->hi || (!tw->int8 && !tw->lo)) return fail(SN_E_NOMEM, "tc weight planes");
+    tw->lo = (__nv_bfloat16*)alloc(n * 2, owner);
+    if (!tw->hi || !tw->lo) return fail(SN_E_NOMEM, "tc weight planes");
     split_bf16_kernel<<<grid_blocks((long long)n), 256>>>(W, wtype, (long long)n, tw->hi, tw->lo);
     SN_TRY(cuda_check(cudaGetLastError(), "split launch"));
-    const int rows[5] = {32, 64, 128, 256, 192};  // weight tile heights (BN)
     for (int i = 0; i < 5; ++i) {
         SN_TRY(encode_map(&tw->tm_hi[i], tw->hi, N, K, rows[i]));
-        SN_TRY(encode_map(&tw->tm_lo[i], tw->int8 ? tw->hi : tw->lo, N, K, rows[i]));
+        SN_TRY(encode_map(&tw->tm_lo[i], tw->lo, N, K, rows[i]));
     }
     tw->ready = true;
     return SN_OK;
@@ -1055,7 +1203,7 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
         // the bf16 planes of the result fit the drained ring for their epilogue
         if (b == 192 && (ld || a.Ch != nullptr || tw.int8)) continue;
         const long long tiles = mt * ((a.N + b - 1) / b);
-        const double bytes = 2.0 * BM * 128 + (tw.int8 ? 1.0 : 2.0) * b * 128;
+        const double bytes = 2.0 * BM * 128 + (tw.q8 ? 0.5 : (tw.int8 ? 1.0 : 2.0)) * b * 128;
         const double mma = 0.63 * b > 90.0 ? 0.63 * b : 90.0;
         const double slab = bytes / 92.0 > (tw.int8 ? 8 : 12) * mma ? bytes / 92.0
                                                                     : (tw.int8 ? 8 : 12) * mma;
@@ -1093,18 +1241,22 @@ int launch_tiles(const GemmArgs& a, const TcWeights& tw, const CUtensorMap& tah,
             }
         }
     }
-#define SN_TC_BN(I8, LD)                                                                  \
-    return bn == 256   ? launch_bn<256, I8, LD>(a, tw, tah, tal, st, pdl, ks)              \
-           : bn == 192 ? launch_bn<192, I8, LD>(a, tw, tah, tal, st, pdl, ks)              \
-           : bn == 128 ? launch_bn<128, I8, LD>(a, tw, tah, tal, st, pdl, ks)              \
-                       : (bn == 64 ? launch_bn<64, I8, LD>(a, tw, tah, tal, st, pdl, ks)   \
-                                   : launch_bn<32, I8, LD>(a, tw, tah, tal, st, pdl, ks))
-    if (tw.int8) {
-        if (ld) SN_TC_BN(true, true);
-        SN_TC_BN(true, false);
+#define SN_TC_BN(I8, LD, CV)                                                                  \
+    return bn == 256   ? launch_bn<256, I8, LD, CV>(a, tw, tah, tal, st, pdl, ks)              \
+           : bn == 192 ? launch_bn<192, I8, LD, CV>(a, tw, tah, tal, st, pdl, ks)              \
+           : bn == 128 ? launch_bn<128, I8, LD, CV>(a, tw, tah, tal, st, pdl, ks)              \
+                       : (bn == 64 ? launch_bn<64, I8, LD, CV>(a, tw, tah, tal, st, pdl, ks)   \
+                                   : launch_bn<32, I8, LD, CV>(a, tw, tah, tal, st, pdl, ks))
+    if (tw.int8 && tw.q8) {  // codes converted in the main loop
+        if (ld) SN_TC_BN(true, true, true);
+        SN_TC_BN(true, false, true);
     }
-    if (ld) SN_TC_BN(false, true);
-    SN_TC_BN(false, false);
+    if (tw.int8) {
+        if (ld) SN_TC_BN(true, true, false);
+        SN_TC_BN(true, false, false);
+    }
+    if (ld) SN_TC_BN(false, true, false);
+    SN_TC_BN(false, false, false);
 #undef SN_TC_BN
 }
 

@@ -19,7 +19,12 @@ namespace sn {
 // one TMA descriptor per plane and tile width.
 struct TcWeights {
     int N = 0, K = 0;
-    bool int8 = false;                 // hi holds the exact int8 codes; no lo plane
+    // INT8: bf16 planes of the codes (hi, exact; no lo), or, with the
+    // runtime's int8_mainloop setting at preparation, the codes themselves
+    // (q8, (N,K) bytes, 16-byte aligned), converted to bf16 in the
+    // contraction's main loop
+    bool int8 = false;
+    const int8_t* q8 = nullptr;
     __nv_bfloat16* hi = nullptr;
     __nv_bfloat16* lo = nullptr;
     CUtensorMap tm_hi[5];              // box rows 32 / 64 / 128 / 256 / 192
@@ -27,9 +32,10 @@ struct TcWeights {
     bool ready = false;
 };
 
-// Split device weights (fp32 / fp16 (out,in) or int8 codes) into bf16 planes
-// (allocated with cudaMalloc into *allocs owner) and build the TMA maps.
-// wtype: kWF32, kWF16, kWI8.
+// Split device weights (fp32 / fp16 (out,in); INT8 codes into one exact
+// plane) into bf16 planes (allocated through `alloc` for `owner`) and build
+// the TMA maps; with the int8_mainloop setting INT8 codes are used in place
+// (copied only to reach 16-byte alignment). wtype: kWF32, kWF16, kWI8.
 int tc_prepare(TcWeights* tw, const void* W, int wtype, int N, int K, void* (*alloc)(size_t, void*),
                void* owner);
 

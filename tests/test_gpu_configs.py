@@ -91,6 +91,40 @@ def test_config3_b1024_int8_from_warm_states():
         _check_states(gs, gh, om, range(B), shape)
 
 
+def test_config3_int8_codes_converted_in_mainloop_match_planes():
+    """INT8 dequant inside the contraction's main loop (converter warps turn
+    each K slab of 1-byte codes into the bf16 slab the MMAs read) against the
+    default load-time bf16 code planes: the tensor cores see the same operand
+    values, so logits and states are bit-identical. Config-3 shape at
+    B=1024 (the benchmarked tile widths and K splits)."""
+    from sunnynet_b200 import _lib, formats
+    from sunnynet_b200.model import SunnyBatch
+    lib = _lib.load()
+    shape = formats.SUNNY_PRESETS["c3"]
+    B = 1024
+    rng = np.random.default_rng(33)
+    s0 = (0.5 * rng.standard_normal((B, shape.layers, shape.dim))).astype(np.float32)
+    h0 = rng.standard_normal((B, shape.layers, shape.kh, shape.dim)).astype(np.float32)
+    toks = [rng.integers(0, shape.vocab, B).astype(np.int32) for _ in range(3)]
+    out = []
+    with tempfile.TemporaryDirectory() as td:
+        p = _sunny_blob(td, shape, quant=True, seed=5)
+        for mode in (0, 1):
+            old = lib.sn_abi_cuda_int8_mainloop(mode)
+            try:
+                gm = SunnyBatch(p, B)  # weights prepared under this setting
+            finally:
+                lib.sn_abi_cuda_int8_mainloop(old)
+            gm.set_state(s0, h0)
+            logits = [gm.step(t).copy() for t in toks]
+            out.append((logits, gm.get_state()))
+            gm.close()
+    (la, (sa, ha)), (lb, (sb, hb)) = out
+    for x, y in zip(la, lb):
+        assert np.array_equal(x, y)
+    assert np.array_equal(sa, sb) and np.array_equal(ha, hb)
+
+
 # ---------------------------------------------------------------- config 2
 def test_config2_b256_prefill_then_256_decode_steps():
     """Config 2 (L4 d512 V16384, fp32 weights on the bf16x3 tensor-core path)
