@@ -769,6 +769,8 @@ def rwkv_launches(S, B, block=128):
     first-stage projections of a layer share one such pair when all suit."""
     D, F = S.dim, S.ffn
     Rw, Ra, Rv, Rg = S.ranks
+    if B == 1:  # one sequence: the fused persistent step kernel, then the two argmax kernels
+        return 3
 
     def tc(K, N):
         return B >= 16 and N >= 32 and K % 128 == 0 and block in (32, 64, 128)
@@ -856,7 +858,9 @@ def wl_rwkv(args, torch, dist, ours, B):
           "avg_launch_us": t_ms / n_l * 1e3,
           "avg_launch_us_serialised": tab[dom]["serial_ms"] / n_l * 1e3,
           "alg_bytes_per_launch": fb,
-          "achieved_is": "dominant kernel" if ach else "whole step (dominant is a GEMV family)",
+          "achieved_is": "dominant kernel" if ach else (
+              "whole step (one fused kernel)" if dom == "rk_fused"
+              else "whole step (dominant is a GEMV family)"),
           "traffic": profile_traffic(f"{dom}/c4/B{B}"), "step_alg_bytes": step_bytes,
           "step_alg_flops": step_flops, "step_hbm_gbs": step_gbs,
           "timing": "CUDA events around each kernel family of the step run kernel by "

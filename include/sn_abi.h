@@ -140,7 +140,8 @@ int32_t   sn_abi_cuda_profile_report(char* buf, int32_t buflen);
 /* Failure-path test hook (no reference counterpart). Runs one CTA that waits,
  * through the library's bounded device waits, on something that never
  * completes: kind 0 an mbarrier phase, kind 1 a grid barrier like the fused
- * decode step's. After `cycles` SM cycles (1 .. 2^31; the step kernels use
+ * decode step's, kind 2 the same barrier split into its arrive and wait
+ * halves (the fused RWKV-7 step's form). After `cycles` SM cycles (1 .. 2^31; the step kernels use
  * 2^31) the wait gives up and the kernel returns. Returns SN_E_DEVICE when
  * the give-up was reported, as every model call does after a device wait
  * times out; the library stays usable afterwards. */

@@ -23,14 +23,10 @@
 #include "ptx.cuh"
 #include "quant.h"
 #include "runtime.cuh"
+#include "w4a8_rows.cuh"
 
 namespace sn {
 namespace {
-
-__device__ __forceinline__ float load_scale(const void* s, size_t i, bool fp16) {
-    return fp16 ? __half2float(reinterpret_cast<const __half*>(s)[i])
-                : reinterpret_cast<const float*>(s)[i];
-}
 
 // ------------------------------------------------------------ quantisers
 // One warp per (row, group).
@@ -79,160 +75,6 @@ __global__ void dequant_i4_kernel(const uint8_t* __restrict__ q, const void* __r
         float* xr = x + (size_t)r * N + (size_t)b * block;
         xr[k] = __fmul_rn((float)((int)(v & 0x0F) - 8), sc);
         xr[half + k] = __fmul_rn((float)((int)(v >> 4) - 8), sc);
-    }
-}
-
-// ------------------------------------------------------- activation quant
-// Quantise NB activation rows (in floats each) into shared memory:
-// xq[NB][in] int8, xs[NB][nb] scale, xsum[NB][nb] integer sums. Warp per block.
-__device__ void quant_act_smem(const float* __restrict__ X, int nseq, int in, int block, int nb,
-                               int8_t* xq, float* xs, int* xsum) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int w = warp; w < nseq * nb; w += nw) {
-        const int s = w / nb, b = w % nb;
-        const float* xb = X + (size_t)s * in + (size_t)b * block;
-        float m = 0.0f;
-        for (int i = lane; i < block; i += 32) m = fmaxf(m, fabsf(xb[i]));
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const float sc = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
-        const float inv = __fdiv_rn(1.0f, sc);
-        int sum = 0;
-        for (int i = lane; i < block; i += 32) {
-            int t = __float2int_rn(__fmul_rn(xb[i], inv));
-            t = min(max(t, -127), 127);
-            xq[(size_t)s * in + (size_t)b * block + i] = (int8_t)t;
-            sum += t;
-        }
-        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) {
-            xs[s * nb + b] = sc;
-            xsum[s * nb + b] = sum;
-        }
-    }
-}
-
-__device__ __forceinline__ int dot16(uint4 w, const int8_t* xlo, const int8_t* xhi) {
-    const int4 a = *reinterpret_cast<const int4*>(xlo);
-    const int4 c = *reinterpret_cast<const int4*>(xhi);
-    int d = 0;
-    d = __dp4a((int)(w.x & 0x0F0F0F0Fu), a.x, d);
-    d = __dp4a((int)((w.x >> 4) & 0x0F0F0F0Fu), c.x, d);
-    d = __dp4a((int)(w.y & 0x0F0F0F0Fu), a.y, d);
-    d = __dp4a((int)((w.y >> 4) & 0x0F0F0F0Fu), c.y, d);
-    d = __dp4a((int)(w.z & 0x0F0F0F0Fu), a.z, d);
-    d = __dp4a((int)((w.z >> 4) & 0x0F0F0F0Fu), c.z, d);
-    d = __dp4a((int)(w.w & 0x0F0F0F0Fu), a.w, d);
-    d = __dp4a((int)((w.w >> 4) & 0x0F0F0F0Fu), c.w, d);
-    return d;
-}
-
-constexpr int kMaxSeqTile = 8;
-
-// Output epilogues (the RWKV-7 layer fuses these into its GEMVs):
-// store | accumulate into Y (x += W y, rwkv7.c:292,306) | relu^2 | tanh | sigmoid
-__device__ __forceinline__ void w4_store(float* y, float v, int epi) {
-    switch (epi) {
-        case kW4Add: *y = *y + v; break;
-        case kW4Relu2: {
-            const float t = v > 0.0f ? v : 0.0f;
-            *y = t * t;
-        } break;
-        case kW4Tanh: *y = tanhf(v); break;
-        case kW4Sigmoid: *y = 1.0f / (1.0f + expf(-v)); break;
-        default: *y = v;
-    }
-}
-
-// Fast path: block % 32 == 0 (whole 16-byte chunks per block half), in % 32 == 0,
-// in <= 1024 * NCH (a 16-byte chunk holds 32 codes; NCH chunk passes of 32
-// lanes per row). A warp takes kW4Rows output rows at a time
-// (rows gw, gw + nw, ...): the 16-byte weight chunks and block scales of all
-// of them are loaded before any is used, and the first group's before the
-// activations are quantised (they do not depend on the previous kernel), so
-// the weight stream has several rows in flight per warp. NS sequences share
-// each weight load. The per-row arithmetic is the reference's, in its order.
-constexpr int kW4Rows = 4;
-constexpr int kW4MaxProblems = 8;
-template <bool FP16S, int NCH>
-__device__ __forceinline__ void w4a8_rows(float* __restrict__ Y, const float* __restrict__ X,
-                                          const uint8_t* __restrict__ Wq,
-                                          const void* __restrict__ scale, int nseq, int in,
-                                          int out, int block, int epi, int gw, int nw) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    const int nb = in / block, half = block / 2, cpb = half / 16, cpr = in / 32;
-    const int nch = (cpr + 31) / 32;  // chunk passes per row (<= NCH)
-    const int seq0 = blockIdx.y * kMaxSeqTile;
-    const int ns = min(kMaxSeqTile, nseq - seq0);
-    int8_t* xq = reinterpret_cast<int8_t*>(smem);
-    float* xs = reinterpret_cast<float*>(smem + (size_t)kMaxSeqTile * in);
-    int* xsum = reinterpret_cast<int*>(xs + kMaxSeqTile * nb);
-    const int lane = threadIdx.x & 31;
-    uint4 wr[kW4Rows][NCH];
-    float sw[kW4Rows][NCH];
-    auto load_rows = [&](int row0) {  // rows row0 + i*nw, i < kW4Rows
-#pragma unroll
-        for (int i = 0; i < kW4Rows; ++i) {
-            const int row = row0 + i * nw;
-#pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-                const int ci = c * 32 + lane;
-                const bool live = c < nch && ci < cpr && row < out;
-                wr[i][c] = live ? __ldg(reinterpret_cast<const uint4*>(Wq + (size_t)row * (in / 2)) + ci)
-                                : make_uint4(0, 0, 0, 0);
-                sw[i][c] = live ? load_scale(scale, (size_t)row * nb + ci / cpb, FP16S) : 0.0f;
-            }
-        }
-    };
-    pdl_trigger();
-    load_rows(gw);
-    pdl_wait();  // no-op unless launched with programmatic serialization
-    quant_act_smem(X + (size_t)seq0 * in, ns, in, block, nb, xq, xs, xsum);
-    __syncthreads();
-
-    for (int row0 = gw; row0 < out; row0 += kW4Rows * nw) {
-#pragma unroll
-        for (int i = 0; i < kW4Rows; ++i) {
-            const int row = row0 + i * nw;
-            if (row >= out) break;
-            float acc[kMaxSeqTile];
-#pragma unroll
-            for (int s = 0; s < kMaxSeqTile; ++s) acc[s] = 0.0f;
-#pragma unroll
-            for (int c = 0; c < NCH; ++c) {
-                if (c >= nch) break;
-                const int c0 = c * 32, ci = c0 + lane;
-                const bool live = ci < cpr;
-                const uint4 w = wr[i][c];
-                const int b = live ? ci / cpb : 0;
-                const int j = (ci % cpb) * 16;
-                const int nblk = min(32, cpr - c0) / cpb;  // whole blocks in this pass
-                const int bfirst = c0 / cpb;
-#pragma unroll
-                for (int s = 0; s < kMaxSeqTile; ++s) {
-                    if (s >= ns) break;
-                    int d = live ? dot16(w, xq + (size_t)s * in + b * block + j,
-                                         xq + (size_t)s * in + b * block + half + j)
-                                 : 0;
-                    for (int o = 1; o < cpb; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                    // sequential block-order accumulation (same value in every lane)
-                    for (int k = 0; k < nblk; ++k) {
-                        const int dk = __shfl_sync(0xffffffffu, d, k * cpb);
-                        const float swk = __shfl_sync(0xffffffffu, sw[i][c], k * cpb);
-                        const int bk = bfirst + k;
-                        const float f = (float)(dk - 8 * xsum[s * nb + bk]);
-                        acc[s] = __fadd_rn(acc[s], __fmul_rn(__fmul_rn(swk, xs[s * nb + bk]), f));
-                    }
-                }
-            }
-            if (lane < ns) {
-                float v = acc[0];
-#pragma unroll
-                for (int s = 1; s < kMaxSeqTile; ++s)
-                    if (lane == s) v = acc[s];
-                w4_store(Y + (size_t)(seq0 + lane) * out + row, v, epi);
-            }
-        }
-        if (row0 + kW4Rows * nw < out) load_rows(row0 + kW4Rows * nw);
     }
 }
 

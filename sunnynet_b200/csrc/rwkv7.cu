@@ -33,11 +33,13 @@
 #include <vector>
 
 #include "gemm.cuh"
+#include "grid_sync.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
 #include "runtime.cuh"
 #include "rwkv7.h"
 #include "sn_abi.h"
+#include "w4a8_rows.cuh"
 
 namespace sn {
 namespace {
@@ -227,25 +229,32 @@ __global__ void __launch_bounds__(256)
 // One CTA per (sequence, head) walks that sequence's T consecutive rows in
 // order (T = 1 for a decode step, the prompt chunk in a prefill); heads up to
 // 128 wide keep the state in registers across the rows.
-template <int VPL>
-__global__ void __launch_bounds__(256)
-    rk_heads_kernel(int NH, int L, int layer, int D, float* __restrict__ S,
-                    const float* __restrict__ ww, const float* __restrict__ k,
-                    const float* __restrict__ v, const float* __restrict__ a,
-                    const float* __restrict__ kk, const float* __restrict__ r,
-                    const float* __restrict__ g, const float* __restrict__ rk,
-                    const float* __restrict__ lnw, const float* __restrict__ lnb,
-                    float* __restrict__ y, int T) {
+// CG: the step's vectors are read through L2 (ld.global.cg), for a caller in
+// which other CTAs of the same launch wrote them (the fused decode step).
+struct RkNoPre {
+    __device__ bool operator()() const { return true; }
+};
+
+// NOG: y is left ungated (the caller multiplies by g, the same single
+// rounding); pre() runs after the state rows are requested and before the
+// head's vectors are read (the fused step computes them there), and returns
+// false, the same in every thread, to leave the state untouched.
+template <int VPL, bool CG, bool NOG = false, class Pre = RkNoPre>
+__device__ __forceinline__ void rk_heads_body(int h, int b, int NH, int L, int layer, int D,
+                                              float* __restrict__ S, const float* ww,
+                                              const float* k, const float* v, const float* a,
+                                              const float* kk, const float* r, const float* g,
+                                              const float* __restrict__ rk,
+                                              const float* __restrict__ lnw,
+                                              const float* __restrict__ lnb, float* y, int T,
+                                              float* kn, float* yv, float* red, Pre pre = Pre()) {
+    auto ld = [](const float* p) { return CG ? __ldcg(p) : *p; };
     constexpr int HS = VPL * 32;
     // warp w owns state rows w, w+8, ...; for heads up to 128 wide all of
     // them are loaded at once, before anything else, so the state costs one
     // memory round trip per warp instead of one per row
     constexpr int RPW = HS / 8;
     constexpr bool PRE = VPL <= 4;
-    __shared__ float kn[HS], yv[HS], red[32];
-    pdl_trigger();
-    pdl_wait();  // no-op unless launched with programmatic serialization
-    const int h = blockIdx.x % NH, b = blockIdx.x / NH;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float* Sh = S + (((size_t)b * L + layer) * NH + h) * HS * HS;
     float spre[PRE ? RPW : 1][VPL];
@@ -255,25 +264,26 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
             for (int t = 0; t < VPL; ++t) spre[q][t] = Sh[(size_t)(warp + 8 * q) * HS + lane + 32 * t];
     }
+    if (!pre()) return;
     for (int step = 0; step < T; ++step) {
         const size_t o = ((size_t)b * T + step) * D + (size_t)h * HS;
         // kk normalised with floor 1e-12 (rwkv7.c:162-165)
         float ss = 0.0f;
-        for (int j = threadIdx.x; j < HS; j += blockDim.x) ss += kk[o + j] * kk[o + j];
+        for (int j = threadIdx.x; j < HS; j += blockDim.x) ss += ld(&kk[o + j]) * ld(&kk[o + j]);
         float nrm = sqrtf(block_sum(ss, red));
         if (!(nrm > 1e-12f)) nrm = 1e-12f;
         const float inv = 1.0f / nrm;
-        for (int j = threadIdx.x; j < HS; j += blockDim.x) kn[j] = kk[o + j] * inv;
+        for (int j = threadIdx.x; j < HS; j += blockDim.x) kn[j] = ld(&kk[o + j]) * inv;
         __syncthreads();
         float wj[VPL], kj[VPL], rj[VPL], knj[VPL], kaj[VPL];
 #pragma unroll
         for (int t = 0; t < VPL; ++t) {
             const int j = lane + 32 * t;
-            wj[t] = ww[o + j];
-            kj[t] = k[o + j];
-            rj[t] = r[o + j];
+            wj[t] = ld(&ww[o + j]);
+            kj[t] = ld(&k[o + j]);
+            rj[t] = ld(&r[o + j]);
             knj[t] = kn[j];
-            kaj[t] = __fmul_rn(kn[j], a[o + j]);
+            kaj[t] = __fmul_rn(kn[j], ld(&a[o + j]));
         }
 #pragma unroll(PRE ? RPW : 1)
         for (int q = 0; q < RPW; ++q) {
@@ -287,7 +297,7 @@ __global__ void __launch_bounds__(256)
                 p = fmaf(sv[t], knj[t], p);
             }
             for (int off = 16; off; off >>= 1) p += __shfl_xor_sync(0xffffffffu, p, off);
-            const float vi = v[o + i];
+            const float vi = ld(&v[o + i]);
             float yacc = 0.0f;
 #pragma unroll
             for (int t = 0; t < VPL; ++t) {
@@ -311,13 +321,16 @@ __global__ void __launch_bounds__(256)
         for (int j = threadIdx.x; j < HS; j += blockDim.x) {
             const float t = yv[j] - mean;
             var += t * t;
-            dot += r[o + j] * k[o + j] * rk[h * HS + j];
+            dot += ld(&r[o + j]) * ld(&k[o + j]) * rk[h * HS + j];
         }
         const float rstd = 1.0f / sqrtf(block_sum(var, red) / (float)HS + kEpsGroup);
         dot = block_sum(dot, red);
         for (int j = threadIdx.x; j < HS; j += blockDim.x) {
             const float nv = (yv[j] - mean) * rstd * lnw[h * HS + j] + lnb[h * HS + j];
-            y[o + j] = (nv + dot * v[o + j]) * g[o + j];
+            if (NOG)
+                y[o + j] = nv + dot * ld(&v[o + j]);
+            else
+                y[o + j] = (nv + dot * ld(&v[o + j])) * ld(&g[o + j]);
         }
         __syncthreads();  // kn and yv are rewritten by the next row
     }
@@ -327,6 +340,23 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
             for (int t = 0; t < VPL; ++t) Sh[(size_t)(warp + 8 * q) * HS + lane + 32 * t] = spre[q][t];
     }
+}
+
+
+template <int VPL>
+__global__ void __launch_bounds__(256)
+    rk_heads_kernel(int NH, int L, int layer, int D, float* __restrict__ S,
+                    const float* __restrict__ ww, const float* __restrict__ k,
+                    const float* __restrict__ v, const float* __restrict__ a,
+                    const float* __restrict__ kk, const float* __restrict__ r,
+                    const float* __restrict__ g, const float* __restrict__ rk,
+                    const float* __restrict__ lnw, const float* __restrict__ lnb,
+                    float* __restrict__ y, int T) {
+    __shared__ float kn[VPL * 32], yv[VPL * 32], red[32];
+    pdl_trigger();
+    pdl_wait();  // no-op unless launched with programmatic serialization
+    rk_heads_body<VPL, false>((int)blockIdx.x % NH, (int)blockIdx.x / NH, NH, L, layer, D, S, ww,
+                              k, v, a, kk, r, g, rk, lnw, lnb, y, T, kn, yv, red);
 }
 
 // channel-mix prologue (rwkv7.c:295-297); rows and the shift state as in
@@ -414,6 +444,39 @@ struct RkBufs {
           *xf = nullptr, *logits = nullptr;
 };
 
+// The fused B = 1 decode step's tables (its kernel is below).
+struct RkFMat {
+    const uint8_t* q;
+    const void* scale;
+    int in, out;
+};
+
+struct RkFLayer {
+    const float *ln1w, *ln1b, *ln2w, *ln2b, *lerp, *cmk_lerp;
+    RkFMat rw, kw, vw, w1, a1, g1, v1, g2, ow, cmk, cmv;
+    const float *w2, *a2, *v2;  // fp32 LoRA second stages (D, rank)
+    int Rw, Ra, Rv;
+    const float *w0, *a0, *v0, *kkw, *kaw, *rkw, *lnxw, *lnxb;
+};
+
+struct RkFArgs {
+    const RkFLayer* layers;
+    int L, D, NH, F, block, with_head;
+    float eps;
+    const int32_t* tok;
+    int vocab;
+    int* err;
+    const float *embed, *en_w, *en_b, *on_w, *on_b;
+    RkFMat head;
+    float *S, *shift;  // sequence 0's state and shift rows
+    float *x, *r, *k, *v, *a, *g, *kk, *ww, *y, *ck, *lo_w, *lo_a, *lo_v, *lo_g, *vfirst;
+    float *logits, *xn, *xn2;
+    unsigned* bar;
+    int part0[8], part1[8];  // phase A: first CTA of each problem (layer 0: 6, later: 7), then the grid size
+    size_t qbytes;           // W4A8 quantisation area at the start of shared memory
+};
+
+
 struct RwkvModel {
     int vocab = 0, D = 0, HS = 0, NH = 0, F = 0, L = 0, nseq = 0, q4 = 0, group = 64;
     float eps = 1e-5f;
@@ -436,6 +499,11 @@ struct RwkvModel {
     std::map<std::pair<int, int>, ProfGraph> pgraphs;  // instrumented (profile mode 2)
     cudaStream_t cap = nullptr;
     bool ready = false;
+    // fused B = 1 decode step: -1 not tried yet, 0 not applicable, 1 set up
+    int fused = -1, fctas = 0;
+    RkFLayer* flayers = nullptr;
+    unsigned* fbar = nullptr;
+    float* xn2 = nullptr;
 
     ~RwkvModel() {
         for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
@@ -721,6 +789,474 @@ int mat_mul(const RkMat& M, float* y, const float* x, int B, int epi, cudaStream
 
 enum { E_STORE = 0, E_ADD = 1, E_RELU2 = 2, E_TANH = 3, E_SIG = 4 };
 
+// ------------------------------------------------- fused decode step (B = 1)
+// One sequence's decode step in one cooperative launch (one CTA of 256
+// threads per SM) instead of ~110 dependent launches of small kernels. Each
+// layer is five phases separated by grid barriers (grid_sync.cuh):
+//   A  every CTA: x (the embedding, or the residual stream through L2),
+//      LN1 and the time-mix lerp of its problem's plane; its share of the
+//      rows of one first-stage projection (r, k, v, w1, a1, g1, v1: the CTAs
+//      are partitioned over the problems in proportion to their rows)
+//   BC CTA h < NH, for head h's 64 channels: the LoRA second stages and the
+//      mix (the w, a and v sums on three thread groups, each the same
+//      sequential fmaf over its rank as rk_lora_mix_kernel; the rows staged
+//      by cp.async during A), then the head's matrix-state step
+//      (rk_heads_body, output left ungated); the other CTAs meanwhile take
+//      the g2 rows, and the last one writes A's normalised input into the
+//      time-mix shift state (every CTA read the old one in A)
+//   D  ow rows over every warp (x += Wo (y g), the gate applied as the rows'
+//      input is staged: the heads kernel's one rounding of the product)
+//   E  every CTA: LN2 and the channel-mix lerp; its share of the cmk rows
+//   F  cmv rows (x += Wv relu(.)^2); CTA 0 updates the channel-mix shift
+// then the final LN and the head rows over every warp. Every per-element
+// formula, reduction partition (256-thread CTAs) and W4A8 row is the
+// multi-kernel path's, so the two produce identical results. Vectors other
+// CTAs wrote in this launch are read through L2 (ld.global.cg). Each phase's
+// input row is staged after its first weight rows are requested.
+constexpr int kRkFusedThreads = 256;
+
+// dst[0, n) = src[0, n) (times gate[0, n) when given, one rounding) through
+// L2: another CTA wrote it in this launch. A thread's 16-byte loads are all
+// issued before its stores. src, gate and dst are 16-byte aligned.
+__device__ __forceinline__ const float* rk_stage(float* dst, const float* src, int n,
+                                                 const float* gate = nullptr) {
+    const int n4 = n >> 2, nt = blockDim.x;
+    const float4* s4 = reinterpret_cast<const float4*>(src);
+    const float4* g4 = reinterpret_cast<const float4*>(gate);
+    float4* d4 = reinterpret_cast<float4*>(dst);
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * nt) {
+        float4 t[4], u[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = i0 + k * nt;
+            if (i < n4) {
+                t[k] = __ldcg(s4 + i);
+                if (gate) u[k] = __ldcg(g4 + i);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = i0 + k * nt;
+            if (i < n4) {
+                if (gate) {
+                    t[k].x = __fmul_rn(t[k].x, u[k].x);
+                    t[k].y = __fmul_rn(t[k].y, u[k].y);
+                    t[k].z = __fmul_rn(t[k].z, u[k].z);
+                    t[k].w = __fmul_rn(t[k].w, u[k].w);
+                }
+                d4[i] = t[k];
+            }
+        }
+    }
+    for (int i = 4 * n4 + threadIdx.x; i < n; i += nt)
+        dst[i] = gate ? __fmul_rn(__ldcg(src + i), __ldcg(gate + i)) : __ldcg(src + i);
+    __syncthreads();
+    return dst;
+}
+
+// Rows gw, gw + nw, ... of one W4A8 contraction of a single activation row;
+// pro() stages the row once the first weight rows are in flight.
+template <bool FP16S, int NCH, class Pro>
+__device__ __forceinline__ void rk_rows(const RkFMat& M, float* Y, int epi, int block, int gw,
+                                        int nw, unsigned char* sm, Pro pro) {
+    w4a8_rows_p<FP16S, NCH>(Y, M.q, M.scale, 1, 0, M.in, M.out, block, epi, gw, nw, sm, pro);
+    __syncthreads();  // the quantisation area is reused by the next contraction
+}
+
+template <bool FP16S, int NCHD, int NCHF>
+__global__ void __launch_bounds__(kRkFusedThreads, 1) rk_fused_kernel(const __grid_constant__ RkFArgs a) {
+    extern __shared__ __align__(16) unsigned char rk_sm[];
+    unsigned char* sm = rk_sm;
+    __shared__ float red[32], kn[64], yv[64];
+    __shared__ float dlo[3][64];  // the head's LoRA second-stage sums (w, a, v)
+    const int cta = blockIdx.x, nct = gridDim.x, tid = threadIdx.x, warp = tid >> 5;
+    const int D = a.D, gw = cta * (kRkFusedThreads / 32) + warp, nw = nct * (kRkFusedThreads / 32);
+    float* xr = reinterpret_cast<float*>(sm + a.qbytes);  // [max(D, F)]: the phase's input row
+    float* mix = xr + (a.F > D ? a.F : D);                // [D]: a lerped plane
+    float* lov = mix + D;                                 // LoRA vectors (Rw + Ra + Rv, rg)
+    float* lrows = lov + 3 * kLoraMax + D;                // [64][Rw + Ra + Rv + 4]: BC rows
+    float* cst = lrows + 64 * (3 * kLoraMax + 4);         // [4][D]: A's or E's constants
+    __shared__ __align__(16) float hc[5][64];             // the head's w0, a0, v0, kkw, kaw
+    unsigned nbar = 0;
+    // the embedding row, LN'd (every CTA; CTA 0 also stores the residual stream)
+    {
+        int t = a.tok[0];
+        if (t < 0 || t >= a.vocab) {  // never read outside the table; report instead
+            if (tid == 0 && cta == 0) atomicExch(a.err, kErrBadIndex);
+            t = 0;
+        }
+        const float* e = a.embed + (size_t)t * D;
+        float mean, rstd;
+        row_stats(e, D, a.eps, red, &mean, &rstd);
+        for (int i = tid; i < D; i += kRkFusedThreads) {
+            const float xv = (e[i] - mean) * rstd * a.en_w[i] + a.en_b[i];
+            xr[i] = xv;
+            if (cta == 0) a.x[i] = xv;
+        }
+        __syncthreads();
+    }
+    // A CTA arrives at the grid barrier that opens a phase as soon as its
+    // part of the previous one is written, then requests the phase's weight
+    // rows (rk_rows calls its prologue, which waits at the barrier, once they
+    // are in flight) and copies the per-channel constants it needs to shared
+    // memory: after the barrier, only the vectors other CTAs just wrote cost
+    // a round trip. When a barrier gives up (an error is recorded), the phase
+    // under way finishes its in-bounds arithmetic on whatever it reads,
+    // writes no recurrent state, and the kernel returns.
+    bool ok = true;
+    auto arrive = [&] { grid_arrive(a.bar); };
+    auto sync = [&] { ok = ok && grid_wait(a.bar, nbar++, a.err); };
+    auto consts = [&](const float* c0, const float* c1, const float* c2, const float* c3) {
+        const float* src[4] = {c0, c1, c2, c3};
+        const int n4 = D / 4;
+        for (int e = tid; e < 4 * n4; e += kRkFusedThreads) {
+            const int v = e / n4, q = (e - v * n4) * 4;
+            cp_async16(cst + v * D + q, src[v] + q, 16u);
+        }
+    };
+    for (int l = 0; l < a.L; ++l) {
+        const RkFLayer& Y = a.layers[l];
+        float* sh = a.shift + (size_t)l * 2 * D;
+        const int Rw = Y.Rw, Ra = Y.Ra, Rv = l > 0 ? Y.Rv : 0, R = Rw + Ra + Rv;
+        // ------------------------------------------------------------- A
+        if (l > 0) arrive();
+        if (cta < a.NH) {  // head h's 64 channels' LoRA rows (w2, a2, v2) and constants
+            // rows of R + 4 floats: 16-byte aligned (ranks % 4 == 0), and
+            // consecutive channels' float4 reads fall on different bank groups
+            const int c0 = cta * 64, RS = R + 4, R4 = R / 4;
+            for (int e = tid; e < 64 * R4; e += kRkFusedThreads) {
+                const int t = e / R4, q = (e - t * R4) * 4, i = c0 + t;
+                const float* src = q < Rw        ? Y.w2 + (size_t)i * Rw + q
+                                   : q < Rw + Ra ? Y.a2 + (size_t)i * Ra + (q - Rw)
+                                                 : Y.v2 + (size_t)i * Y.Rv + (q - Rw - Ra);
+                cp_async16(lrows + t * RS + q, src, 16u);
+            }
+            if (tid < 80) {
+                const float* hsrc[5] = {Y.w0, Y.a0, Y.v0, Y.kkw, Y.kaw};
+                cp_async16(&hc[tid >> 4][(tid & 15) * 4], hsrc[tid >> 4] + c0 + (tid & 15) * 4,
+                           16u);
+            }
+        }
+        {
+            const int* part = l == 0 ? a.part0 : a.part1;
+            const int np = l == 0 ? 6 : 7;
+            int p = 0;
+            while (p + 1 < np && cta >= part[p + 1]) ++p;
+            const RkFMat* mats[7] = {&Y.rw, &Y.kw, &Y.vw, &Y.w1, &Y.a1, &Y.g1, &Y.v1};
+            float* outs[7] = {a.r, a.k, a.v, a.lo_w, a.lo_a, a.lo_g, a.lo_v};
+            const int plane[7] = {0, 2, 3, 1, 4, 5, 3};  // r, k, v <- xr, xk, xv; w1, a1, g1, v1
+            const int epis[7] = {kW4Store, kW4Store, kW4Store, kW4Tanh, kW4Store, kW4Sigmoid,
+                                 kW4Store};
+            // the time-mix shift row: this layer's BC phase rewrites it, after this read
+            consts(sh, Y.ln1w, Y.ln1b, Y.lerp + (size_t)plane[p] * D);
+            const int c0 = part[p], c1 = part[p + 1];
+            rk_rows<FP16S, NCHD>(
+                *mats[p], outs[p], epis[p], a.block, (cta - c0) * (kRkFusedThreads / 32) + warp,
+                (c1 - c0) * (kRkFusedThreads / 32), sm, [&] {
+                    if (l > 0) {
+                        sync();
+                        rk_stage(xr, a.x, D);
+                    }
+                    cp_async_wait_all();  // the constants (and a head's LoRA rows)
+                    __syncthreads();
+                    float mean, rstd;
+                    row_stats(xr, D, a.eps, red, &mean, &rstd);
+                    for (int i = tid; i < D; i += kRkFusedThreads) {
+                        const float xn = (xr[i] - mean) * rstd * cst[D + i] + cst[2 * D + i];
+                        const float d = cst[i] - xn;
+                        mix[i] = xn + cst[3 * D + i] * d;
+                        if (cta == 0) a.xn[i] = xn;
+                    }
+                    __syncthreads();
+                    return static_cast<const float*>(mix);
+                });
+        }
+        if (!ok) return;
+        // ------------------------------------------------------------ BC
+        arrive();
+        if (cta < a.NH) {
+            const int c0 = cta * 64;
+            rk_heads_body<2, true, true>(
+                cta, 0, a.NH, a.L, l, D, a.S, a.ww, a.k, a.v, a.a, a.kk, a.r, a.g, Y.rkw, Y.lnxw,
+                Y.lnxb, a.y, 1, kn, yv, red, [&] {  // once the state rows are requested
+                    sync();
+                    float* lw = lov;
+                    float* la = lw + Rw;
+                    float* lv = la + Ra;
+                    for (int i = tid; i < Rw; i += kRkFusedThreads) lw[i] = __ldcg(a.lo_w + i);
+                    for (int i = tid; i < Ra; i += kRkFusedThreads) la[i] = __ldcg(a.lo_a + i);
+                    for (int i = tid; i < Rv; i += kRkFusedThreads) lv[i] = __ldcg(a.lo_v + i);
+                    __syncthreads();
+                    if (tid < 192) {  // w, a, v sums of channel c0 + t on three groups
+                        const int t = tid & 63, which = tid >> 6;
+                        const int q0 = which == 0 ? 0 : which == 1 ? Rw : Rw + Ra;
+                        const int n = which == 0 ? Rw : which == 1 ? Ra : Rv;
+                        const float* lo = lw + q0;
+                        const float* wr = lrows + t * (R + 4) + q0;
+                        float acc = 0.0f;
+                        for (int q = 0; q < n; q += 4) {  // sequential in q, four per load
+                            const float4 w4 = *reinterpret_cast<const float4*>(wr + q);
+                            acc = fmaf(lo[q], w4.x, acc);
+                            acc = fmaf(lo[q + 1], w4.y, acc);
+                            acc = fmaf(lo[q + 2], w4.z, acc);
+                            acc = fmaf(lo[q + 3], w4.w, acc);
+                        }
+                        dlo[which][t] = acc;
+                    }
+                    __syncthreads();
+                    if (tid < 64) {  // the LoRA mix of channel c0 + tid
+                        const int i = c0 + tid;
+                        a.ww[i] = expf(-sigm(dlo[0][tid] + hc[0][tid]) * kInvSqrtE);
+                        if (l == 0) {
+                            a.vfirst[i] = __ldcg(a.v + i);
+                        } else {
+                            const float vv = __ldcg(a.v + i);
+                            a.v[i] = vv + (__ldcg(a.vfirst + i) - vv) * sigm(dlo[2][tid] + hc[2][tid]);
+                        }
+                        const float aa = sigm(dlo[1][tid] + hc[1][tid]);
+                        a.a[i] = aa;
+                        const float kv = __ldcg(a.k + i);
+                        a.kk[i] = kv * hc[3][tid];
+                        a.k[i] = kv + kv * (aa - 1.0f) * hc[4][tid];
+                    }
+                    __syncthreads();  // the head's vectors are written (read back through L2)
+                    return ok;
+                });
+        } else {
+            rk_rows<FP16S, NCHD>(Y.g2, a.g, kW4Store, a.block,
+                                 (cta - a.NH) * (kRkFusedThreads / 32) + warp,
+                                 (nct - a.NH) * (kRkFusedThreads / 32), sm, [&] {
+                                     sync();
+                                     if (ok && cta == nct - 1)  // the time-mix shift: A read the old one
+                                         for (int i = tid; i < D; i += kRkFusedThreads)
+                                             sh[i] = __ldcg(a.xn + i);
+                                     return rk_stage(lov, a.lo_g, Y.g2.in);
+                                 });
+        }
+        if (!ok) return;
+        // ------------------------------------------------------------- D
+        arrive();
+        rk_rows<FP16S, NCHD>(Y.ow, a.x, kW4Add, a.block, gw, nw, sm, [&] {
+            sync();
+            return rk_stage(mix, a.y, D, a.g);
+        });
+        if (!ok) return;
+        // ------------------------------------------------------------- E
+        arrive();
+        // the channel-mix shift row: F rewrites it, after this read
+        consts(sh + D, Y.ln2w, Y.ln2b, Y.cmk_lerp);
+        rk_rows<FP16S, NCHD>(Y.cmk, a.ck, kW4Relu2, a.block, gw, nw, sm, [&] {
+            sync();
+            rk_stage(xr, a.x, D);
+            cp_async_wait_all();
+            __syncthreads();
+            float mean, rstd;
+            row_stats(xr, D, a.eps, red, &mean, &rstd);
+            for (int i = tid; i < D; i += kRkFusedThreads) {
+                const float xn2 = (xr[i] - mean) * rstd * cst[D + i] + cst[2 * D + i];
+                mix[i] = xn2 + cst[3 * D + i] * (cst[i] - xn2);
+                if (cta == 0) a.xn2[i] = xn2;
+            }
+            __syncthreads();
+            return static_cast<const float*>(mix);
+        });
+        if (!ok) return;
+        // ------------------------------------------------------------- F
+        arrive();
+        rk_rows<FP16S, NCHF>(Y.cmv, a.x, kW4Add, a.block, gw, nw, sm, [&] {
+            sync();
+            if (ok && cta == 0)  // the channel-mix shift: E read the old one
+                for (int i = tid; i < D; i += kRkFusedThreads) sh[D + i] = __ldcg(a.xn2 + i);
+            return rk_stage(xr, a.ck, a.F);
+        });
+        if (!ok) return;
+    }
+    if (a.with_head) {  // final LN (rk_ln_kernel's arithmetic), then the head rows
+        arrive();
+        rk_rows<FP16S, NCHD>(a.head, a.logits, kW4Store, a.block, gw, nw, sm, [&] {
+            sync();
+            rk_stage(xr, a.x, D);
+            float mean, rstd;
+            row_stats(xr, D, a.eps, red, &mean, &rstd);
+            for (int i = tid; i < D; i += kRkFusedThreads)
+                mix[i] = (xr[i] - mean) * rstd * a.on_w[i] + a.on_b[i];
+            __syncthreads();
+            return static_cast<const float*>(mix);
+        });
+    }
+}
+
+// The fused step applies to one sequence of a model whose every contraction
+// is W4A8 (one block size and scale type), with fp32 LoRA second stages of
+// rank <= kLoraMax, 64-wide heads, and widths the SIMT rows take.
+bool rk_fused_shape_ok(const RwkvModel* m) {
+    if (!m->q4 || m->HS != 64 || m->D % 32 || m->D > 2048 || m->F % 32 || m->F > 4096)
+        return false;
+    const int blk = m->head.block;
+    const bool f16 = m->head.fp16;
+    if (!(blk == 32 || blk == 64 || blk == 128 || blk == 256)) return false;
+    auto q4 = [&](const RkMat& M, int in) {
+        return M.q4 && M.block == blk && M.fp16 == f16 && M.in == in && M.in % 32 == 0 &&
+               M.in % blk == 0 && (uintptr_t)M.q % 16 == 0;
+    };
+    if (!q4(m->head, m->D) || m->head.out != m->vocab) return false;
+    for (int l = 0; l < m->L; ++l) {
+        const RkLayer& A = m->ly[l];
+        if (!q4(A.rw, m->D) || !q4(A.kw, m->D) || !q4(A.vw, m->D) || !q4(A.w1, m->D) ||
+            !q4(A.a1, m->D) || !q4(A.g1, m->D) || (l > 0 && !q4(A.v1, m->D)) ||
+            !q4(A.g2, A.g2.in) || A.g2.in > m->D || A.g2.out != m->D || !q4(A.ow, m->D) ||
+            !q4(A.cmk, m->D) || !q4(A.cmv, m->F))
+            return false;
+        if (A.w2.q4 || A.a2.q4 || (l > 0 && A.v2.q4) || A.w2.in > kLoraMax ||
+            A.a2.in > kLoraMax || A.v2.in > kLoraMax || A.w2.in % 4 || A.a2.in % 4 ||
+            A.v2.in % 4 || (uintptr_t)A.w2.w % 16 || (uintptr_t)A.a2.w % 16 ||
+            (l > 0 && (uintptr_t)A.v2.w % 16))
+            return false;
+    }
+    return true;
+}
+
+RkFMat fmat(const RkMat& M) { return RkFMat{M.q, M.scale, M.in, M.out}; }
+
+// First CTA of each of np problems (np + 1 entries, the last = ctas): CTAs
+// first .. ctas - 1 in proportion to the problems' rows, at least one each.
+void rk_partition(const int* rows, int np, int first, int ctas, int* part) {
+    const int avail = ctas - first;
+    long long tot = 0;
+    for (int p = 0; p < np; ++p) tot += rows[p];
+    int n[8], used = 0;
+    for (int p = 0; p < np; ++p) {
+        n[p] = std::max(1, (int)((long long)avail * rows[p] / tot));
+        used += n[p];
+    }
+    while (used > avail) {  // take back from the largest
+        int b = 0;
+        for (int p = 1; p < np; ++p) if (n[p] > n[b]) b = p;
+        --n[b];
+        --used;
+    }
+    for (int p = 0; used < avail; p = (p + 1) % np, ++used) ++n[p];
+    part[0] = first;
+    for (int p = 0; p < np; ++p) part[p + 1] = part[p] + n[p];
+}
+
+// The fused step's kernel instance, shared-memory size and W4A8 area.
+struct RkFusedCfg {
+    void (*kern)(RkFArgs) = nullptr;
+    size_t smem = 0, qbytes = 0;
+};
+RkFusedCfg rk_fused_cfg(const RwkvModel* m) {
+    const int D = m->D;
+    const int nchd = D <= 1024 ? 1 : 2, nchf = m->F <= 1024 ? 1 : (m->F <= 2048 ? 2 : 4);
+    const bool f16 = m->head.fp16;
+    auto kern = [&]() -> void (*)(RkFArgs) {
+#define RKF(F16, A, B) if (f16 == F16 && nchd == A && nchf == B) return rk_fused_kernel<F16, A, B>;
+        RKF(false, 1, 1) RKF(false, 1, 2) RKF(false, 1, 4) RKF(false, 2, 2) RKF(false, 2, 4)
+        RKF(true, 1, 1) RKF(true, 1, 2) RKF(true, 1, 4) RKF(true, 2, 2) RKF(true, 2, 4)
+#undef RKF
+        return nullptr;
+    }();
+    RkFusedCfg c;
+    c.kern = kern;
+    const int maxin = std::max(D, m->F);
+    const int blk = m->head.block > 0 ? m->head.block : 32;
+    c.qbytes = ((size_t)kMaxSeqTile * maxin + (size_t)kMaxSeqTile * (maxin / blk) * 8 + 15) / 16 * 16;
+    c.smem = c.qbytes + ((size_t)maxin + D + 3 * kLoraMax + D + (size_t)64 * (3 * kLoraMax + 4) + (size_t)4 * D) *
+                            sizeof(float);
+    return c;
+}
+
+// Check the model and build the fused step's device tables, once per model
+// and outside any stream capture (it allocates and copies): m->fused becomes
+// 1, or 0 when the model or the device does not take the fused step.
+int rk_fused_setup(RwkvModel* m) {
+    if (m->fused >= 0) return SN_OK;
+    m->fused = 0;
+    const RkFusedCfg c = rk_fused_cfg(m);
+    auto kern = c.kern;
+    const size_t smem = c.smem;
+    {
+        // the heads' CTAs and at least as many again for the g2 rows
+        if (!kern || !rk_fused_shape_ok(m) || smem > 200 * 1024 || rt().num_sms < 2 * m->NH)
+            return SN_OK;
+        SN_TRY(cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem),
+                          "rwkv fused smem"));
+        int per_sm = 0;
+        SN_TRY(cuda_check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                              &per_sm, kern, kRkFusedThreads, smem),
+                          "rwkv fused occupancy"));
+        if (per_sm < 1) return SN_OK;
+        std::vector<RkFLayer> h(m->L);
+        for (int l = 0; l < m->L; ++l) {
+            const RkLayer& A = m->ly[l];
+            RkFLayer& f = h[l];
+            f.ln1w = A.ln1w; f.ln1b = A.ln1b; f.ln2w = A.ln2w; f.ln2b = A.ln2b;
+            f.lerp = A.lerp; f.cmk_lerp = A.cmk_lerp;
+            f.rw = fmat(A.rw); f.kw = fmat(A.kw); f.vw = fmat(A.vw); f.w1 = fmat(A.w1);
+            f.a1 = fmat(A.a1); f.g1 = fmat(A.g1); f.v1 = fmat(A.v1); f.g2 = fmat(A.g2);
+            f.ow = fmat(A.ow); f.cmk = fmat(A.cmk); f.cmv = fmat(A.cmv);
+            f.w2 = A.w2.w; f.a2 = A.a2.w; f.v2 = A.v2.w;
+            f.Rw = A.w2.in; f.Ra = A.a2.in; f.Rv = A.v2.in;
+            f.w0 = A.w0; f.a0 = A.a0; f.v0 = A.v0; f.kkw = A.kkw; f.kaw = A.kaw;
+            f.rkw = A.rkw; f.lnxw = A.lnxw; f.lnxb = A.lnxb;
+        }
+        m->flayers = m->dalloc<RkFLayer>(m->L);
+        m->fbar = m->dalloc<unsigned>(64);
+        m->xn2 = m->dalloc<float>(m->D);
+        if (!m->flayers || !m->fbar || !m->xn2) return fail(SN_E_NOMEM, "rwkv fused tables");
+        SN_TRY(cuda_check(cudaMemcpy(m->flayers, h.data(), h.size() * sizeof(RkFLayer),
+                                     cudaMemcpyHostToDevice),
+                          "rwkv fused tables"));
+        m->fctas = rt().num_sms;
+        m->fused = 1;
+    }
+    return SN_OK;
+}
+
+// Launch the fused step (set up first: rk_fused_setup); SN_E_UNSUPPORTED when
+// the model or the device does not take it (the caller then runs the chain).
+int rk_fused_launch(RwkvModel* m, const RkBufs& w, bool head, cudaStream_t st) {
+    SN_TRY(rk_fused_setup(m));
+    if (m->fused != 1) return SN_E_UNSUPPORTED;
+    const RkFusedCfg c = rk_fused_cfg(m);
+    auto kern = c.kern;
+    const size_t smem = c.smem, qbytes = c.qbytes;
+    const int D = m->D;
+    RkFArgs a{};
+    a.layers = m->flayers;
+    a.L = m->L; a.D = D; a.NH = m->NH; a.F = m->F; a.block = m->head.block;
+    a.with_head = head ? 1 : 0;
+    a.eps = m->eps;
+    a.tok = w.tok; a.vocab = m->vocab; a.err = rt().d_err;
+    a.embed = m->embed; a.en_w = m->en_w; a.en_b = m->en_b; a.on_w = m->on_w; a.on_b = m->on_b;
+    a.head = fmat(m->head);
+    a.S = m->S; a.shift = m->shift;
+    a.x = w.x; a.r = w.r; a.k = w.k; a.v = w.v; a.a = w.a; a.g = w.g; a.kk = w.kk; a.ww = w.ww;
+    a.y = w.y; a.ck = w.ck; a.lo_w = w.lo_w; a.lo_a = w.lo_a; a.lo_v = w.lo_v; a.lo_g = w.lo_g;
+    a.vfirst = w.vfirst; a.logits = w.logits; a.xn = w.xn; a.xn2 = m->xn2;
+    a.bar = m->fbar;
+    {
+        const RkLayer& A = m->ly[m->L > 1 ? 1 : 0];
+        const int rows[7] = {A.rw.out, A.kw.out, A.vw.out, A.w1.out, A.a1.out, A.g1.out, A.v1.out};
+        rk_partition(rows, 6, 0, m->fctas, a.part0);
+        rk_partition(rows, 7, 0, m->fctas, a.part1);
+    }
+    a.qbytes = qbytes;
+    SN_TRY(cuda_check(cudaMemsetAsync(m->fbar, 0, 64 * sizeof(unsigned), st), "rwkv fused reset"));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)m->fctas);
+    cfg.blockDim = dim3(kRkFusedThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_check(cudaLaunchKernelEx(&cfg, kern, a), "rwkv fused step launch");
+}
+
 // trace (device, (B, L+1, D)) or nullptr: the residual stream entering each
 // layer and leaving the last one, copied out after the embedding and after
 // every layer (a debugging view of the same kernels, used without a graph).
@@ -734,6 +1270,13 @@ enum { E_STORE = 0, E_ADD = 1, E_RELU2 = 2, E_TANH = 3, E_SIG = 4 };
 int enqueue_rk(RwkvModel* m, const RkBufs& w, int nb, int T, bool head, cudaStream_t st,
                int last_layer = -1, float* trace = nullptr) {
     const int D = m->D;
+    // one sequence's decode step: the fused persistent kernel where it applies
+    // (SN_RK_UNFUSED=1 keeps the kernel chain, for comparisons)
+    if (nb == 1 && T == 1 && last_layer < 0 && !trace && !getenv("SN_RK_UNFUSED")) {
+        ProfScope ps("rk_fused", st);
+        const int rc = rk_fused_launch(m, w, head, st);
+        if (rc != SN_E_UNSUPPORTED) return rc;
+    }
     const int B = nb * T;  // rows
     const size_t plane = (size_t)B * D;
     // the shift state of layer l, slot j, from the last row of each sequence
@@ -876,6 +1419,7 @@ int enqueue_rk(RwkvModel* m, const RkBufs& w, int nb, int T, bool head, cudaStre
 
 int rk_run(RwkvModel* m, int B, bool head, float* trace = nullptr) {
     auto key = std::make_pair(B, head ? 1 : 0);
+    if (B == 1) SN_TRY(rk_fused_setup(m));  // allocates: before any capture
     if (prof_graph() && !trace)  // the step's graph with event nodes around each family
         return prof_graph_run(&m->pgraphs[key], m->cap, stream(),
                               [&](cudaStream_t cs) {

@@ -52,6 +52,7 @@
 #include "ptx.cuh"
 #include "runtime.cuh"
 #include "sunny_fused.cuh"
+#include "grid_sync.cuh"
 
 namespace sn {
 namespace {
@@ -63,57 +64,11 @@ constexpr unsigned kPrefetchChunk = 1u << 16;
 __device__ __forceinline__ void bulk_prefetch_l2(const void* p, unsigned bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void fence_acq_rel_gpu() {
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-}
-
 __device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 __device__ __forceinline__ float warp_sum(float v) {
     for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
-}
-
-// Barrier k of this launch; false when the step is being abandoned. A CTA
-// gives up after `limit` SM cycles (default about a second), raises the
-// abort flag so the others leave at their barrier too, and records
-// kErrWaitTimeout in the error word.
-__device__ bool grid_sync(unsigned* bar, unsigned k, int* err, long long limit = kWaitCycles) {
-    __shared__ int ok;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int res = 1;
-        const unsigned target = (k + 1) * gridDim.x;
-        red_release_add(bar, 1u);
-        const long long t0 = clock64();
-        unsigned it = 0;
-        while (ld_relaxed_u32(bar) < target) {
-            if ((++it & 63u) == 0) {
-                if (ld_relaxed_u32(bar + kBarAbort)) {
-                    res = 0;
-                    break;
-                }
-                if (clock64() - t0 > limit) {
-                    atomicExch(bar + kBarAbort, 1u);
-                    atomicExch(err, kErrWaitTimeout);
-                    res = 0;
-                    break;
-                }
-            }
-        }
-        fence_acq_rel_gpu();
-        ok = res;
-    }
-    __syncthreads();
-    return ok != 0;
 }
 
 // Profile mode: %globaltimer (shared time base, ~1 us ticks) and clock64
@@ -950,7 +905,8 @@ int launch_sunny_fused(const FusedArgs& a, cudaStream_t st) {
 // One CTA waits on something nothing will ever complete, through the same
 // bounded waits the step kernels use: kind 0 an mbarrier phase no thread
 // arrives on, kind 1 a grid barrier (grid_sync) whose arrival target one CTA
-// can never reach. The wait gives up after `limit` cycles, records
+// can never reach, kind 2 the same barrier in its two halves (grid_arrive,
+// then grid_wait, as the fused RWKV-7 step uses it). The wait gives up after `limit` cycles, records
 // kErrWaitTimeout in the error word and the kernel returns, so the host sees
 // SN_E_DEVICE and the context stays usable. Nothing is in flight when it
 // gives up: no copies, no TMEM.
@@ -975,7 +931,12 @@ __global__ void wait_selftest_kernel(int kind, long long limit, int* err) {
             __threadfence();
         }
         // barrier 3 of a one-CTA grid wants 4 arrivals; only 1 comes
-        grid_sync(g_selftest_bar, 3u, err, limit);
+        if (kind == 1) {
+            grid_sync(g_selftest_bar, 3u, err, limit);
+        } else {
+            grid_arrive(g_selftest_bar);
+            grid_wait(g_selftest_bar, 3u, err, limit);
+        }
     }
 }
 
@@ -984,7 +945,7 @@ __global__ void wait_selftest_kernel(int kind, long long limit, int* err) {
 
 extern "C" sn_status sn_abi_cuda_wait_selftest(int32_t kind, int64_t cycles) {
     using namespace sn;
-    if (kind != 0 && kind != 1) return fail(SN_E_INVAL, "wait_selftest: kind must be 0 or 1");
+    if (kind < 0 || kind > 2) return fail(SN_E_INVAL, "wait_selftest: kind must be 0, 1 or 2");
     if (cycles < 1 || cycles > kWaitCycles)
         return fail(SN_E_INVAL, "wait_selftest: cycles must be in [1, 2^31]");
     SN_TRY(ensure_init());

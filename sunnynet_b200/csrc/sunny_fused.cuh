@@ -64,6 +64,7 @@ struct FusedArgs {
 };
 
 constexpr int kBarAbort = 32, kBarDone = 64, kBarAmax = 96, kBarWords = 128;
+static_assert(kBarAbort == 32, "the abort word grid_sync.cuh polls (kGridAbortWord)");
 
 // Dynamic shared memory the fused step needs (0 when the shapes do not fit).
 size_t fused_smem_bytes(const FusedArgs& a);

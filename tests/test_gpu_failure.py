@@ -27,7 +27,7 @@ def lib():
     return _lib
 
 
-@pytest.mark.parametrize("kind", [0, 1])
+@pytest.mark.parametrize("kind", [0, 1, 2])
 def test_bounded_wait_gives_up_and_reports(lib, kind):
     L = lib.load()
     rc = L.sn_abi_cuda_wait_selftest(kind, 1 << 20)  # ~0.5 ms at 1.9 GHz
@@ -47,6 +47,7 @@ def test_bounded_wait_gives_up_and_reports(lib, kind):
 
 def test_selftest_rejects_bad_arguments(lib):
     L = lib.load()
-    assert L.sn_abi_cuda_wait_selftest(2, 100) == -1
+    assert L.sn_abi_cuda_wait_selftest(3, 100) == -1
+    assert L.sn_abi_cuda_wait_selftest(-1, 100) == -1
     assert L.sn_abi_cuda_wait_selftest(0, 0) == -1
     assert L.sn_abi_cuda_wait_selftest(0, (1 << 31) + 1) == -1

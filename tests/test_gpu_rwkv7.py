@@ -231,6 +231,26 @@ def c4_blobs():
     return shape, p32, p4
 
 
+def test_config4_fused_single_sequence_step_equals_kernel_chain(c4_blobs):
+    """One sequence's INT4 decode step runs as one persistent kernel (six
+    grid-barrier phases per layer); the same step of a 2-sequence handle runs
+    the kernel chain. Every formula, reduction partition and W4A8 row is the
+    same, so with the same tokens sequence 0's logits, matrix state and shift
+    state are bit-identical, step after step."""
+    from sunnynet_b200.rwkv7 import Rwkv7Batch
+    shape, _, p4 = c4_blobs
+    one, two = Rwkv7Batch(p4, 1), Rwkv7Batch(p4, 2)
+    rng = np.random.default_rng(44)
+    for _ in range(4):
+        t = rng.integers(0, shape.vocab, 2).astype(np.int32)
+        l1 = one.step(t[:1]).copy()
+        l2 = two.step(t).copy()
+        assert np.array_equal(l1[0], l2[0])
+    S1, sh1 = one.get_state()
+    S2, sh2 = two.get_state()
+    assert np.array_equal(S1[0], S2[0]) and np.array_equal(sh1[0], sh2[0])
+
+
 @pytest.mark.parametrize("B", [1, 4])
 def test_config4_shape_fp32_vs_oracle(c4_blobs, B):
     """Every kernel of the full-shape model in fp32. Layer-0 intermediates at
