@@ -112,8 +112,11 @@ __device__ __forceinline__ void w4a8_rows_p(float* __restrict__ Y, const uint8_t
     float* xs = reinterpret_cast<float*>(smem + (size_t)kMaxSeqTile * in);
     int* xsum = reinterpret_cast<int*>(xs + kMaxSeqTile * nb);
     const int lane = threadIdx.x & 31;
+    // Weight chunks and the raw bits of their block scales: predicated loads
+    // into zeroed registers, nothing that waits for the data until it is used,
+    // so a warp's requests all leave before its first use.
     uint4 wr[kW4Rows][NCH];
-    float sw[kW4Rows][NCH];
+    unsigned swr[kW4Rows][NCH];
     auto load_rows = [&](int row0) {  // rows row0 + i*nw, i < kW4Rows
 #pragma unroll
         for (int i = 0; i < kW4Rows; ++i) {
@@ -122,11 +125,19 @@ __device__ __forceinline__ void w4a8_rows_p(float* __restrict__ Y, const uint8_t
             for (int c = 0; c < NCH; ++c) {
                 const int ci = c * 32 + lane;
                 const bool live = c < nch && ci < cpr && row < out;
-                wr[i][c] = live ? __ldg(reinterpret_cast<const uint4*>(Wq + (size_t)row * (in / 2)) + ci)
-                                : make_uint4(0, 0, 0, 0);
-                sw[i][c] = live ? load_scale(scale, (size_t)row * nb + ci / cpb, FP16S) : 0.0f;
+                wr[i][c] = make_uint4(0, 0, 0, 0);
+                swr[i][c] = 0u;
+                if (live) {
+                    wr[i][c] = __ldg(reinterpret_cast<const uint4*>(Wq + (size_t)row * (in / 2)) + ci);
+                    const size_t si = (size_t)row * nb + ci / cpb;
+                    swr[i][c] = FP16S ? (unsigned)__ldg(reinterpret_cast<const unsigned short*>(scale) + si)
+                                      : __ldg(reinterpret_cast<const unsigned*>(scale) + si);
+                }
             }
         }
+    };
+    auto scale_of = [](unsigned raw) {
+        return FP16S ? __half2float(__ushort_as_half((unsigned short)raw)) : __uint_as_float(raw);
     };
     load_rows(gw);
     const float* X = pro();
@@ -161,7 +172,7 @@ __device__ __forceinline__ void w4a8_rows_p(float* __restrict__ Y, const uint8_t
                     // sequential block-order accumulation (same value in every lane)
                     for (int k = 0; k < nblk; ++k) {
                         const int dk = __shfl_sync(0xffffffffu, d, k * cpb);
-                        const float swk = __shfl_sync(0xffffffffu, sw[i][c], k * cpb);
+                        const float swk = scale_of(__shfl_sync(0xffffffffu, swr[i][c], k * cpb));
                         const int bk = bfirst + k;
                         const float f = (float)(dk - 8 * xsum[s * nb + bk]);
                         acc[s] = __fadd_rn(acc[s], __fmul_rn(__fmul_rn(swk, xs[s * nb + bk]), f));
