@@ -876,8 +876,18 @@ __global__ void __launch_bounds__(kRkFusedThreads, 1) rk_fused_kernel(const __gr
     float* lov = mix + D;                                 // LoRA vectors (Rw + Ra + Rv, rg)
     float* lrows = lov + 3 * kLoraMax + D;                // [64][Rw + Ra + Rv + 4]: BC rows
     float* cst = lrows + 64 * (3 * kLoraMax + 4);         // [4][D]: A's or E's constants
+    // the layer tables (weight and vector addresses), copied once: every phase
+    // starts by reading them, and from shared memory that costs no round trip
+    RkFLayer* ltab = reinterpret_cast<RkFLayer*>(cst + 4 * D);
     __shared__ __align__(16) float hc[5][64];             // the head's w0, a0, v0, kkw, kaw
     unsigned nbar = 0;
+    {
+        static_assert(sizeof(RkFLayer) % 8 == 0, "layer table rows are copied in 8-byte words");
+        const int nwd = a.L * (int)(sizeof(RkFLayer) / 8);
+        const unsigned long long* src = reinterpret_cast<const unsigned long long*>(a.layers);
+        unsigned long long* dst = reinterpret_cast<unsigned long long*>(ltab);
+        for (int i = tid; i < nwd; i += kRkFusedThreads) dst[i] = src[i];
+    }
     // the embedding row, LN'd (every CTA; CTA 0 also stores the residual stream)
     {
         int t = a.tok[0];
@@ -915,7 +925,7 @@ __global__ void __launch_bounds__(kRkFusedThreads, 1) rk_fused_kernel(const __gr
         }
     };
     for (int l = 0; l < a.L; ++l) {
-        const RkFLayer& Y = a.layers[l];
+        const RkFLayer& Y = ltab[l];
         float* sh = a.shift + (size_t)l * 2 * D;
         const int Rw = Y.Rw, Ra = Y.Ra, Rv = l > 0 ? Y.Rv : 0, R = Rw + Ra + Rv;
         // ------------------------------------------------------------- A
@@ -1162,7 +1172,8 @@ RkFusedCfg rk_fused_cfg(const RwkvModel* m) {
     const int blk = m->head.block > 0 ? m->head.block : 32;
     c.qbytes = ((size_t)kMaxSeqTile * maxin + (size_t)kMaxSeqTile * (maxin / blk) * 8 + 15) / 16 * 16;
     c.smem = c.qbytes + ((size_t)maxin + D + 3 * kLoraMax + D + (size_t)64 * (3 * kLoraMax + 4) + (size_t)4 * D) *
-                            sizeof(float);
+                            sizeof(float) +
+             (size_t)m->L * sizeof(RkFLayer);
     return c;
 }
 
