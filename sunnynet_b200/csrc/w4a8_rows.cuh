@@ -216,7 +216,6 @@ __device__ __forceinline__ void w4a8_rows_p(float* __restrict__ Y, const uint8_t
                 const int b = live ? ci / cpb : 0;
                 const int j = (ci % cpb) * 16;
                 const int nblk = min(32, cpr - c0) / cpb;  // whole blocks in this pass
-                const int bfirst = c0 / cpb;
 #pragma unroll
                 for (int s = 0; s < kMaxSeqTile; ++s) {
                     if (s >= ns) break;
@@ -224,14 +223,15 @@ __device__ __forceinline__ void w4a8_rows_p(float* __restrict__ Y, const uint8_t
                                          xq + (size_t)s * in + b * block + half + j)
                                  : 0;
                     for (int o = 1; o < cpb; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                    // sequential block-order accumulation (same value in every lane)
-                    for (int k = 0; k < nblk; ++k) {
-                        const int dk = __shfl_sync(0xffffffffu, d, k * cpb);
-                        const float swk = scale_of(__shfl_sync(0xffffffffu, swr[i][c], k * cpb));
-                        const int bk = bfirst + k;
-                        const float f = (float)(dk - 8 * xsum[s * nb + bk]);
-                        acc[s] = __fadd_rn(acc[s], __fmul_rn(__fmul_rn(swk, xs[s * nb + bk]), f));
-                    }
+                    // every lane of block b's group forms the block's term; the
+                    // terms are then added in block order (same value in every lane)
+                    const float fb =
+                        live ? __fmul_rn(__fmul_rn(scale_of(swr[i][c]), xs[s * nb + b]),
+                                         (float)(d - 8 * xsum[s * nb + b]))
+                             : 0.0f;
+#pragma unroll 4
+                    for (int k = 0; k < nblk; ++k)
+                        acc[s] = __fadd_rn(acc[s], __shfl_sync(0xffffffffu, fb, k * cpb));
                 }
             }
             if (lane < ns) {
