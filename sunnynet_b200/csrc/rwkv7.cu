@@ -859,7 +859,7 @@ __device__ __forceinline__ const float* rk_stage(float* dst, const float* src, i
 template <bool FP16S, int NCH, class Pro>
 __device__ __forceinline__ void rk_rows(const RkFMat& M, float* Y, int epi, int block, int gw,
                                         int nw, unsigned char* sm, Pro pro) {
-    w4a8_rows_p<FP16S, NCH>(Y, M.q, M.scale, 1, 0, M.in, M.out, block, epi, gw, nw, sm, pro);
+    w4a8_rows_p<FP16S, NCH, 1>(Y, M.q, M.scale, 1, 0, M.in, M.out, block, epi, gw, nw, sm, pro);
     __syncthreads();  // the quantisation area is reused by the next contraction
 }
 

@@ -148,12 +148,16 @@ __device__ __forceinline__ void w4_store(float* y, float v, int epi) {
 // each weight load. The per-row arithmetic is the reference's, in its order.
 constexpr int kW4Rows = 4;
 //
-// w4a8_rows_p: rows gw, gw + nw, ... of the contraction for the ns <= 8
-// activation rows from seq0 on, with the quantised activations in `smem`
-// ([kMaxSeqTile][in] codes, then scales and code sums). `pro` runs after the
-// first rows' weights are requested and returns the activation rows (ns x
-// in floats, global or shared memory): it performs whatever wait they need.
-template <bool FP16S, int NCH, class Pro>
+// w4a8_rows_p: rows gw, gw + nw, ... of the contraction for the ns <= NSX
+// (<= 8) activation rows from seq0 on, with the quantised activations in
+// `smem` ([kMaxSeqTile][in] codes, then scales and code sums). `pro` runs
+// after the first rows' weights are requested and returns the activation rows
+// (ns x in floats, global or shared memory): it performs whatever wait they
+// need. With NSX == 1 each lane keeps its row-invariant operands (its 32
+// activation codes, the block's scale and 8 x code sum) in registers, so a
+// row costs its weight chunk's dot products, the block combination and one
+// store: the same operations on the same values, in the same order.
+template <bool FP16S, int NCH, int NSX = kMaxSeqTile, class Pro>
 __device__ __forceinline__ void w4a8_rows_p(float* __restrict__ Y, const uint8_t* __restrict__ Wq,
                                             const void* __restrict__ scale, int ns, int seq0,
                                             int in, int out, int block, int epi, int gw, int nw,
@@ -198,6 +202,64 @@ __device__ __forceinline__ void w4a8_rows_p(float* __restrict__ Y, const uint8_t
     else
         quant_act_smem(X, ns, in, block, nb, xq, xs, xsum);
     __syncthreads();
+
+    if constexpr (NSX == 1) {
+        int4 xlo[NCH], xhi[NCH];
+        float xsc[NCH];
+        int xs8[NCH], nbk[NCH];
+        bool lv[NCH];
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
+            const int ci = c * 32 + lane;
+            lv[c] = c < nch && ci < cpr;
+            const int b = lv[c] ? ci / cpb : 0;
+            const int j = (ci % cpb) * 16;
+            xlo[c] = make_int4(0, 0, 0, 0);
+            xhi[c] = make_int4(0, 0, 0, 0);
+            xsc[c] = 0.0f;
+            xs8[c] = 0;
+            if (lv[c]) {
+                xlo[c] = *reinterpret_cast<const int4*>(xq + b * block + j);
+                xhi[c] = *reinterpret_cast<const int4*>(xq + b * block + half + j);
+                xsc[c] = xs[b];
+                xs8[c] = 8 * xsum[b];
+            }
+            nbk[c] = c < nch ? min(32, cpr - c * 32) / cpb : 0;  // whole blocks in the pass
+        }
+        for (int row0 = gw; row0 < out; row0 += kW4Rows * nw) {
+#pragma unroll
+            for (int i = 0; i < kW4Rows; ++i) {
+                const int row = row0 + i * nw;
+                if (row >= out) break;
+                float acc = 0.0f;
+#pragma unroll
+                for (int c = 0; c < NCH; ++c) {
+                    if (c >= nch) break;
+                    const uint4 w = wr[i][c];
+                    int d = 0;  // dot16's order: (low, high) nibbles of each word
+                    d = __dp4a((int)(w.x & 0x0F0F0F0Fu), xlo[c].x, d);
+                    d = __dp4a((int)((w.x >> 4) & 0x0F0F0F0Fu), xhi[c].x, d);
+                    d = __dp4a((int)(w.y & 0x0F0F0F0Fu), xlo[c].y, d);
+                    d = __dp4a((int)((w.y >> 4) & 0x0F0F0F0Fu), xhi[c].y, d);
+                    d = __dp4a((int)(w.z & 0x0F0F0F0Fu), xlo[c].z, d);
+                    d = __dp4a((int)((w.z >> 4) & 0x0F0F0F0Fu), xhi[c].z, d);
+                    d = __dp4a((int)(w.w & 0x0F0F0F0Fu), xlo[c].w, d);
+                    d = __dp4a((int)((w.w >> 4) & 0x0F0F0F0Fu), xhi[c].w, d);
+                    if (!lv[c]) d = 0;
+                    for (int o = 1; o < cpb; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                    const float fb =
+                        lv[c] ? __fmul_rn(__fmul_rn(scale_of(swr[i][c]), xsc[c]), (float)(d - xs8[c]))
+                              : 0.0f;
+#pragma unroll 4
+                    for (int k = 0; k < nbk[c]; ++k)
+                        acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, fb, k * cpb));
+                }
+                if (lane == 0 && ns > 0) w4_store(Y + (size_t)seq0 * out + row, acc, epi);
+            }
+            if (row0 + kW4Rows * nw < out) load_rows(row0 + kW4Rows * nw);
+        }
+        return;
+    }
 
     for (int row0 = gw; row0 < out; row0 += kW4Rows * nw) {
 #pragma unroll
