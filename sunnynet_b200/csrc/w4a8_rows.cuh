@@ -226,35 +226,67 @@ __device__ __forceinline__ void w4a8_rows_p(float* __restrict__ Y, const uint8_t
             }
             nbk[c] = c < nch ? min(32, cpr - c * 32) / cpb : 0;  // whole blocks in the pass
         }
+        // A row's block sum for chunk pass c: integer dot products over the
+        // block's cpb (1, 2, 4 or 8) lanes, then the block term.
+        auto term = [&](const uint4& w, unsigned sraw, int c) {
+            int d = 0;  // dot16's order: (low, high) nibbles of each word
+            d = __dp4a((int)(w.x & 0x0F0F0F0Fu), xlo[c].x, d);
+            d = __dp4a((int)((w.x >> 4) & 0x0F0F0F0Fu), xhi[c].x, d);
+            d = __dp4a((int)(w.y & 0x0F0F0F0Fu), xlo[c].y, d);
+            d = __dp4a((int)((w.y >> 4) & 0x0F0F0F0Fu), xhi[c].y, d);
+            d = __dp4a((int)(w.z & 0x0F0F0F0Fu), xlo[c].z, d);
+            d = __dp4a((int)((w.z >> 4) & 0x0F0F0F0Fu), xhi[c].z, d);
+            d = __dp4a((int)(w.w & 0x0F0F0F0Fu), xlo[c].w, d);
+            d = __dp4a((int)((w.w >> 4) & 0x0F0F0F0Fu), xhi[c].w, d);
+            if (!lv[c]) d = 0;
+            int t = __shfl_xor_sync(0xffffffffu, d, 1);
+            d += cpb > 1 ? t : 0;
+            t = __shfl_xor_sync(0xffffffffu, d, 2);
+            d += cpb > 2 ? t : 0;
+            t = __shfl_xor_sync(0xffffffffu, d, 4);
+            d += cpb > 4 ? t : 0;
+            return lv[c] ? __fmul_rn(__fmul_rn(scale_of(sraw), xsc[c]), (float)(d - xs8[c])) : 0.0f;
+        };
         for (int row0 = gw; row0 < out; row0 += kW4Rows * nw) {
+            if (row0 + (kW4Rows - 1) * nw < out) {
+                // a full group: its rows side by side, so their dot products,
+                // block terms and in-order block sums interleave
+                float acc[kW4Rows];
 #pragma unroll
-            for (int i = 0; i < kW4Rows; ++i) {
-                const int row = row0 + i * nw;
-                if (row >= out) break;
-                float acc = 0.0f;
+                for (int i = 0; i < kW4Rows; ++i) acc[i] = 0.0f;
 #pragma unroll
                 for (int c = 0; c < NCH; ++c) {
                     if (c >= nch) break;
-                    const uint4 w = wr[i][c];
-                    int d = 0;  // dot16's order: (low, high) nibbles of each word
-                    d = __dp4a((int)(w.x & 0x0F0F0F0Fu), xlo[c].x, d);
-                    d = __dp4a((int)((w.x >> 4) & 0x0F0F0F0Fu), xhi[c].x, d);
-                    d = __dp4a((int)(w.y & 0x0F0F0F0Fu), xlo[c].y, d);
-                    d = __dp4a((int)((w.y >> 4) & 0x0F0F0F0Fu), xhi[c].y, d);
-                    d = __dp4a((int)(w.z & 0x0F0F0F0Fu), xlo[c].z, d);
-                    d = __dp4a((int)((w.z >> 4) & 0x0F0F0F0Fu), xhi[c].z, d);
-                    d = __dp4a((int)(w.w & 0x0F0F0F0Fu), xlo[c].w, d);
-                    d = __dp4a((int)((w.w >> 4) & 0x0F0F0F0Fu), xhi[c].w, d);
-                    if (!lv[c]) d = 0;
-                    for (int o = 1; o < cpb; o <<= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                    const float fb =
-                        lv[c] ? __fmul_rn(__fmul_rn(scale_of(swr[i][c]), xsc[c]), (float)(d - xs8[c]))
-                              : 0.0f;
-#pragma unroll 4
-                    for (int k = 0; k < nbk[c]; ++k)
-                        acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, fb, k * cpb));
+                    float fb[kW4Rows];
+#pragma unroll
+                    for (int i = 0; i < kW4Rows; ++i) fb[i] = term(wr[i][c], swr[i][c], c);
+                    for (int k = 0; k < nbk[c]; ++k) {
+#pragma unroll
+                        for (int i = 0; i < kW4Rows; ++i)
+                            acc[i] = __fadd_rn(acc[i], __shfl_sync(0xffffffffu, fb[i], k * cpb));
+                    }
                 }
-                if (lane == 0 && ns > 0) w4_store(Y + (size_t)seq0 * out + row, acc, epi);
+                if (lane == 0 && ns > 0) {
+#pragma unroll
+                    for (int i = 0; i < kW4Rows; ++i)
+                        w4_store(Y + (size_t)seq0 * out + row0 + i * nw, acc[i], epi);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < kW4Rows; ++i) {  // the last, partial group: row by row
+                    const int row = row0 + i * nw;
+                    if (row >= out) break;
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < NCH; ++c) {
+                        if (c >= nch) break;
+                        const float fb = term(wr[i][c], swr[i][c], c);
+#pragma unroll 4
+                        for (int k = 0; k < nbk[c]; ++k)
+                            acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, fb, k * cpb));
+                    }
+                    if (lane == 0 && ns > 0) w4_store(Y + (size_t)seq0 * out + row, acc, epi);
+                }
             }
             if (row0 + kW4Rows * nw < out) load_rows(row0 + kW4Rows * nw);
         }
