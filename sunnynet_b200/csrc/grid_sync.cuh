@@ -1,8 +1,8 @@
 // Grid-wide barrier of a cooperative launch (every CTA co-resident): a
 // monotonic arrival counter in global memory, zeroed before each launch.
 // Barrier k: thread 0 adds 1 with red.release (after bar.sync, so the release
-// covers the whole CTA's writes) and polls, relaxed, until the counter reaches
-// (k+1)*CTAs, then fences (acquire). Word kGridAbortWord of the same array is
+// covers the whole CTA's writes) and polls with acquire loads until the
+// counter reaches (k+1)*CTAs (the passing read synchronizes with every add). Word kGridAbortWord of the same array is
 // the abort flag. Data other CTAs wrote is read through L2 (ld.global.cg),
 // never through L1 or the read-only path.
 #pragma once
@@ -22,11 +22,13 @@ __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void fence_acq_rel_gpu() {
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
 // Barrier k of this launch; false when the step is being abandoned. A CTA
@@ -42,7 +44,7 @@ __device__ bool grid_sync(unsigned* bar, unsigned k, int* err, long long limit =
         red_release_add(bar, 1u);
         const long long t0 = clock64();
         unsigned it = 0;
-        while (ld_relaxed_u32(bar) < target) {
+        while (ld_acquire_u32(bar) < target) {  // the read that passes is the acquire
             if ((++it & 63u) == 0) {
                 if (ld_relaxed_u32(bar + kGridAbortWord)) {
                     res = 0;
@@ -56,7 +58,6 @@ __device__ bool grid_sync(unsigned* bar, unsigned k, int* err, long long limit =
                 }
             }
         }
-        fence_acq_rel_gpu();
         ok = res;
     }
     __syncthreads();
@@ -70,11 +71,6 @@ __device__ bool grid_sync(unsigned* bar, unsigned k, int* err, long long limit =
 // writes before it), and the release does not wait for them. The wait ends
 // with an acquire load of the counter, which synchronizes with every CTA's
 // release add.
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 __device__ __forceinline__ void grid_arrive(unsigned* bar) {
     __syncthreads();
     if (threadIdx.x == 0) red_release_add(bar, 1u);

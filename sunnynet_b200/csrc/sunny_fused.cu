@@ -36,8 +36,8 @@
 //
 // Barriers. The launch is cooperative (all CTAs co-resident). Barrier k of a
 // launch: thread 0 adds 1 to a monotonic counter with red.release (after
-// bar.sync, so the release covers the whole CTA's writes) and polls it,
-// relaxed, until it reaches (k+1)*CTAs, then fences (acquire). The counter
+// bar.sync, so the release covers the whole CTA's writes) and polls it with
+// acquire loads until it reaches (k+1)*CTAs. The counter
 // is zeroed before each launch. Data written by other CTAs is read with
 // ld.global.cg (L2), never through L1 or the read-only path. Every wait is
 // bounded (~2^31 cycles): on give-up the CTA sets the abort word and the
