@@ -791,7 +791,7 @@ enum { E_STORE = 0, E_ADD = 1, E_RELU2 = 2, E_TANH = 3, E_SIG = 4 };
 
 // ------------------------------------------------- fused decode step (B = 1)
 // One sequence's decode step in one cooperative launch (one CTA of 256
-// threads per SM) instead of ~110 dependent launches of small kernels. Each
+// threads per SM) instead of ~90 dependent launches of small kernels. Each
 // layer is five phases separated by grid barriers (grid_sync.cuh):
 //   A  every CTA: x (the embedding, or the residual stream through L2),
 //      LN1 and the time-mix lerp of its problem's plane; its share of the
